@@ -1,0 +1,370 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 NVFP4 MoE layer (one JSON line on rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (N = 1): the benchmark's configs[1], the decode batch --
+H2048, 64 routed experts top-4 (scale 2.5), expert intermediate 1536, one
+BF16 shared expert of 1536, 64 tokens -- with seeded synthetic weights and
+activations.  A step is one forward of the layer over the 64 tokens, inputs
+resident in HBM (the 340 MB of weights exceed the 126 MB L2, so no flush is
+needed between steps).  `value` is tokens/s of the whole job; the line also
+carries us/layer, the per-stage device times, the HBM roofline of the
+dominant kernel (the grouped gate/up GEMM), the end-to-end number through
+the host-buffer C-ABI call, the reference CPU path timed on this host, and a
+secondary prefill measurement (configs[2], 8192 tokens, tensor roofline).
+
+With N > 1 (torchrun), every rank runs the same decode batch on its own GPU
+("replicas": no cross-rank exchange in this build); value sums the tokens of
+all ranks over the max-over-ranks device time.
+
+--impl reference times the reference's own CPU implementation (its sources
+compiled under oracle/_ref, else the C restatement) on this host's cores over
+the same workload: each step is a bounded 16-token sample of the decode
+batch.  Under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+# The CPU legs use every host core; OpenMP reads this when the oracle loads.
+os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "tests"))
+from helpers import load_module  # noqa: E402  (module loader by path)
+
+PKG = REPO / "ninfer_nvfp4_glm-5.3_flash_2x_dgxspark_b200"
+wl = load_module("nf_workload", PKG / "workload.py")
+
+METRIC = "MoE layer tokens/s (decode c1, T=64) + % HBM BW; prefill c2 tokens/s + % NVFP4 TC peak"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def peaks() -> tuple[float, float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, f[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def decode_bytes(lay, active: int, tokens: int) -> dict:
+    """Algorithmic HBM bytes of one decode step and of the gate/up kernel."""
+    H, I, Is, E = lay.hidden, lay.inter, lay.shared_inter, lay.experts
+    gu_w = active * (2 * I * H // 2 + 2 * I * H // 16)
+    dn_w = active * (H * I // 2 + H * I // 16)
+    pairs = tokens * lay.top_k
+    act_gu = pairs * (H // 2 + H // 16)      # quantised dispatch rows read
+    h_out = pairs * (I // 2 + I // 16)       # down-input codes written
+    shared = 3 * Is * H * 2
+    router = E * H * 2 + E * 4
+    io = tokens * H * 2 + tokens * H * 4     # x in, y out
+    return {"gate_up": gu_w + act_gu + h_out, "layer": gu_w + dn_w + shared + router + io}
+
+
+def prefill_flops(lay, tokens: int) -> dict:
+    H, I, Is, E, k = lay.hidden, lay.inter, lay.shared_inter, lay.experts, lay.top_k
+    return {"fp4": tokens * k * (2 * H * 2 * I + 2 * I * H), "fp4_gate_up": tokens * k * 2 * H * 2 * I,
+            "bf16_shared": tokens * 3 * 2 * Is * H, "router": 2 * tokens * E * H}
+
+
+def cpu_reference_rate(lay, x_bits, tokens: int) -> tuple[float, dict]:
+    """Tokens/s of the reference CPU path on `tokens` tokens of the batch."""
+    orc = load_module("nf_oracle_py", REPO / "oracle" / "oracle.py")
+    lib = orc.ref()
+    kind = "reference"
+    if lib is None:
+        lib, kind = orc.port(), "port"
+    x = wl.bf16_bits_to_f32(x_bits[:tokens])
+    t0 = time.perf_counter()
+    orc.moe_layer(lib, lay, x)
+    dt = time.perf_counter() - t0
+    info = {"kind": kind, "cores": int(os.environ["OMP_NUM_THREADS"]),
+            "sample": f"{tokens} of the {x_bits.shape[0]} decode tokens, one token at a time with OpenMP GEMV rows "
+                      "(the reference's own schedule)"}
+    return tokens / dt, info
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    lay, x_bits = wl.config_layer("c1")
+    sample = 16
+    for i in range(args.warmup):
+        cpu_reference_rate(lay, x_bits[16 * (i % 4):], sample)
+    rates = []
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        r, info = cpu_reference_rate(lay, x_bits[16 * (i % 4):], sample)
+        rates.append(r)
+    total = time.perf_counter() - t0
+    value = sample * args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (NVFP4 fake-quant)",
+        "data": "synthetic", "config": {"workload": "c1 decode: H2048 E64 k4 I1536 Is1536 T64 (configs[1])"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", **info},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank: int, world: int, local: int) -> None:
+    import torch
+
+    m = load_module("nf_moe", PKG / "nf_moe.py")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    hbm_peak, bf16_peak, peak_src = peaks()
+    fp4_peak = 4 * bf16_peak  # dense FP4 is 4x dense BF16 on this part
+
+    lay, x_bits = wl.config_layer("c1")
+    T, H, K = x_bits.shape[0], lay.hidden, lay.top_k
+    layer = m.MoeLayer(H, lay.experts, K, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                       swiglu_limit=lay.swiglu_limit, max_tokens=T, device=local)
+    layer.bind_layer(lay)
+    x = torch.from_numpy(x_bits.view(np.int16)).cuda()
+    y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    idx = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step():
+        layer.forward(x, y, T, None, idx, w, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    layer.sync(stream)
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_end = time.perf_counter() + 0.6  # settle clocks under the same load before timing
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    layer.profile(True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    stages, nfw = layer.stage_times()
+    layer.profile(False)
+    t_end = time.perf_counter() + 0.3
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+    clk = clocks.stop()
+    layer.sync(stream)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    stage_ms = {k: v / max(nfw, 1) for k, v in stages.items()}
+    idx_h = idx.cpu().numpy()
+    active = int(np.unique(idx_h).size)
+    nbytes = decode_bytes(lay, active, T)
+
+    # end to end through the host-buffer C-ABI call (pinned host memory)
+    xh = torch.from_numpy(wl.bf16_bits_to_f32(x_bits)).pin_memory().numpy()
+    for _ in range(args.warmup):
+        layer.forward_host(xh)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        layer.forward_host(xh, with_routes=True)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    line = None
+    if rank == 0:
+        gu_ms = stage_ms["gate_up"]
+        achieved = nbytes["gate_up"] / (gu_ms * 1e-3) / 1e9
+        traffic = None
+        tf = REPO / "profiles" / "ncu_traffic.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get("gate_up_decode_bytes_per_launch")
+        launches_per_step = 10 if lay.shared_inter > 0 else 8
+        line = {
+            "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "nvfp4 (E2M1 x UE4M3/16, fp32 accumulate); bf16 shared expert", "data": "synthetic",
+            "config": {"workload": "c1 decode: H2048 E64 k4 I1536 Is1536 T64 scale2.5 (configs[1])",
+                       "tokens_per_gpu": T, "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "no flush: the 340 MB of weights streamed per step exceed the 126 MB L2",
+                       "active_experts": active},
+            "stages_us": {k: 1e3 * v for k, v in stage_ms.items()},
+            "roofline": {"bound": "hbm", "kernel": "grouped NVFP4 gate/up GEMM (SwiGLU + quant fused)",
+                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                         "peak_source": peak_src, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": nbytes["gate_up"],
+                         "layer_achieved_gbs": nbytes["layer"] / (ms * 1e-3) / 1e9,
+                         "layer_frac": nbytes["layer"] / (ms * 1e-3) / 1e9 / hbm_peak,
+                         "layer_algorithmic_bytes": nbytes["layer"]},
+            "e2e": {"value": world * T / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
+                    "d2h_bytes_per_step": T * H * 4 + T * K * 8, "ms_per_step": 1e3 * e2e_s},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+        }
+    if world == 1 and not args.no_prefill:
+        line["prefill"] = run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src)
+    if rank == 0 and world == 1:
+        rate, info = cpu_reference_rate(lay, x_bits, T)
+        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", **info}
+    layer.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src) -> dict:
+    lay, x_bits = wl.config_layer("c2")
+    T, H, K = x_bits.shape[0], lay.hidden, lay.top_k
+    layer = m.MoeLayer(H, lay.experts, K, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                       swiglu_limit=lay.swiglu_limit, max_tokens=T)
+    layer.bind_layer(lay)
+    x = torch.from_numpy(x_bits.view(np.int16)).cuda()
+    y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    idx = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(args.warmup):
+        layer.forward(x, y, T, None, idx, w, stream=stream)
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 20))
+    layer.profile(True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        layer.forward(x, y, T, None, idx, w, stream=stream)
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    stages, nfw = layer.stage_times()
+    layer.profile(False)
+    layer.sync(stream)
+    counts = np.bincount(idx.cpu().numpy().ravel(), minlength=lay.experts)
+    fl = prefill_flops(lay, T)
+    gu_ms = stages["gate_up"] / max(nfw, 1)
+    dn_ms = stages["down"] / max(nfw, 1)
+    t_ideal = fl["fp4"] / (fp4_peak * 1e12) + (fl["bf16_shared"] + fl["router"]) / (bf16_peak * 1e12)
+    layer.close()
+    return {
+        "workload": "c2 prefill: c1 shapes, T8192, bias tuned to 512 +- 10% tokens per expert (configs[2])",
+        "tokens_per_s": T / (ms * 1e-3), "ms_per_step": ms, "steps": steps,
+        "stages_us": {k: 1e3 * v / max(nfw, 1) for k, v in stages.items()},
+        "expert_tokens_min_max": [int(counts.min()), int(counts.max())],
+        "fp4_tflops_layer": fl["fp4"] / (ms * 1e-3) / 1e12,
+        "fp4_frac_layer": fl["fp4"] / (ms * 1e-3) / 1e12 / fp4_peak,
+        "mixed_roofline_frac": t_ideal / (ms * 1e-3),
+        "roofline": {"bound": "tensor", "kernel": "grouped NVFP4 gate/up GEMM",
+                     "achieved": fl["fp4_gate_up"] / (gu_ms * 1e-3) / 1e12, "peak": fp4_peak, "unit": "TFLOP/s",
+                     "frac": fl["fp4_gate_up"] / (gu_ms * 1e-3) / 1e12 / fp4_peak,
+                     "peak_source": f"4 x {peak_src} dense BF16 ({bf16_peak:.0f} TFLOP/s); nominal dense FP4 9000",
+                     "down_tflops": (fl["fp4"] - fl["fp4_gate_up"]) / (dn_ms * 1e-3) / 1e12},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the secondary prefill measurement")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,217 @@
+/*
+ * nf_moe.h -- C ABI of the B200 (sm_100a) NVFP4 routed-expert MoE layer.
+ *
+ * This library replaces the CPU path of GLM-5.3-Flash's MoE feed-forward in
+ * alan70435-vibe/Ninfer_Nvfp4_Glm-5.3_Flash_2x_DgxSpark.  Every entry point
+ * cites the reference interface it stands in for (file:line inside that
+ * project).  The reference has no plugin or FFI layer: its MoE path is the
+ * private member TextModel::moe, so the entry points below are the ones a
+ * maintainer binds from the reference's C++ host (see INTEGRATION.md for the
+ * binding).  Conventions:
+ *   - every call returns an int status (NF_OK == 0); no exception or C++
+ *     type crosses the ABI; nf_moe_last_error() gives the message, worded
+ *     like the reference's std::runtime_error messages;
+ *   - pointers named *_dev are device pointers on the handle's device,
+ *     *_host are host pointers; sizes are element counts;
+ *   - bind calls copy host data into device memory owned by the handle (the
+ *     caller's checkpoint mmaps only need to live during the call) and
+ *     validate before any device write;
+ *   - one handle per (device, stream); a handle is not thread-safe;
+ *   - nf_moe_forward allocates nothing: every workspace is sized at create
+ *     time from nf_moe_desc.max_tokens.
+ */
+#ifndef NF_MOE_H
+#define NF_MOE_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NF_API __attribute__((visibility("default")))
+#else
+#define NF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+enum {
+    NF_OK = 0,
+    NF_ERR_INVALID = 1,     /* bad argument (null pointer, out-of-range id) */
+    NF_ERR_SHAPE = 2,       /* "NVFP4 shape <name>" / "BF16 linear layout <name>" */
+    NF_ERR_LAYOUT = 3,      /* "NVFP4 layout <name>" */
+    NF_ERR_SCALE = 4,       /* "NVFP4 input scale", bad block / global scale */
+    NF_ERR_STATE = 5,       /* weights missing, not finalized, already finalized */
+    NF_ERR_CUDA = 6,        /* a CUDA runtime call failed */
+    NF_ERR_TIMEOUT = 7,     /* a device-side bounded wait gave up */
+    NF_ERR_UNSUPPORTED = 8, /* a descriptor this build does not implement */
+    NF_ERR_NOMEM = 9,       /* device allocation failed at create/bind time */
+    NF_ERR_CAPACITY = 10    /* tokens > max_tokens */
+};
+
+/* NVFP4 projection ids (parameter_schema add_nvfp4 prefixes,
+ * src/parameter_schema.cpp:93-95). */
+enum { NF_PROJ_GATE = 0, NF_PROJ_UP = 1, NF_PROJ_DOWN = 2 };
+
+/* BF16 tensor ids (src/parameter_schema.cpp:76-82 and the BF16 MTP experts
+ * :87-91). */
+enum {
+    NF_BF16_ROUTER = 0,      /* mlp.gate.weight                  [E, H]  */
+    NF_BF16_SHARED_GATE = 1, /* mlp.shared_experts.gate_proj     [Is, H] */
+    NF_BF16_SHARED_UP = 2,   /* mlp.shared_experts.up_proj       [Is, H] */
+    NF_BF16_SHARED_DOWN = 3, /* mlp.shared_experts.down_proj     [H, Is] */
+    NF_BF16_EXPERT_GATE = 4, /* mlp.experts.<e>.gate_proj.weight [I, H]  (layer-45 BF16 experts) */
+    NF_BF16_EXPERT_UP = 5,   /* mlp.experts.<e>.up_proj.weight   [I, H]  */
+    NF_BF16_EXPERT_DOWN = 6  /* mlp.experts.<e>.down_proj.weight [H, I]  */
+};
+
+/* F32 tensor ids. */
+enum { NF_F32_ROUTER_BIAS = 0 /* mlp.gate.e_score_correction_bias [E] (src/parameter_schema.cpp:78-79) */ };
+
+/* Routed expert storage. */
+enum { NF_EXPERTS_NVFP4 = 0, NF_EXPERTS_BF16 = 1 };
+
+/* Layer descriptor.  Filled from ModelSpec (include/ninfer_glm53/model_spec.hpp:
+ * hidden_size, routed_experts, experts_per_token, moe_intermediate_size,
+ * routed_scaling_factor, swiglu_limit) or from a synthetic configuration.
+ * Limits of this build: hidden % 256 == 0, inter % 128 == 0,
+ * shared_inter % 128 == 0 (or 0 for no shared expert), 1 <= top_k <= 32,
+ * top_k <= experts <= 1024. */
+typedef struct nf_moe_desc {
+    int32_t hidden;         /* H */
+    int32_t experts;        /* E, routed experts (global, before EP sharding) */
+    int32_t top_k;          /* experts per token */
+    int32_t inter;          /* I, routed expert intermediate size */
+    int32_t shared_inter;   /* shared expert intermediate size, 0 = none */
+    int32_t n_group;        /* group-limited routing: expert groups (1 = off) */
+    int32_t topk_group;     /* groups kept when n_group > 1 */
+    int32_t normalize;      /* renormalise top-k weights (router_select normalize) */
+    float routed_scaling;   /* routed_scaling_factor */
+    float swiglu_limit;     /* swiglu_limit */
+    int32_t expert_kind;    /* NF_EXPERTS_NVFP4 or NF_EXPERTS_BF16 */
+    int32_t max_tokens;     /* workspace capacity per forward */
+} nf_moe_desc;
+
+typedef struct nf_moe nf_moe;
+
+/* Creates a handle on `device` (which becomes current for the call) and
+ * allocates the device weights and workspace.  Replaces TextModel's
+ * construction of the MoE state (src/text_forward.cpp:580-623). */
+NF_API int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out);
+NF_API void nf_moe_destroy(nf_moe* handle);
+/* Message of the handle's last failure ("" when none).  With a NULL handle,
+ * the message of the last failed nf_moe_create on this thread. */
+NF_API const char* nf_moe_last_error(const nf_moe* handle);
+NF_API const char* nf_status_string(int status);
+
+/* Binds one NVFP4 expert projection: packed U8 [rows, cols/2] (low nibble =
+ * even column), F8_E4M3 block scales [rows, cols/16], rank-0 F32
+ * weight_scale_2 and input_scale, all in checkpoint order.  Validates what
+ * linear_nvfp4 (src/text_forward.cpp:832-843) and Nvfp4MatrixView
+ * (src/nvfp4_decode.cpp:56-79) validate: rows/cols match the descriptor
+ * ("NVFP4 shape"), cols % 16, finite positive input_scale ("NVFP4 input
+ * scale"), finite weight_scale_2 >= FLT_MIN, block scales finite and
+ * non-negative.  gate and up of one expert must carry the same input_scale
+ * in this build (ModelOpt calibrates both on the same input). */
+NF_API int nf_moe_bind_nvfp4(nf_moe* handle, int expert, int proj, const uint8_t* packed_host, const uint8_t* scales_host,
+                      float weight_scale_2, float input_scale, int64_t rows, int64_t cols);
+/* Binds a BF16 matrix (see the NF_BF16_* ids; `expert` is ignored for the
+ * router and shared tensors).  Checks the shape like linear_bf16
+ * (src/text_forward.cpp:821-825, "BF16 linear layout <name>"). */
+NF_API int nf_moe_bind_bf16(nf_moe* handle, int which, int expert, const uint16_t* data_host, int64_t rows, int64_t cols);
+/* Binds an F32 vector (router correction bias, Store::load
+ * src/text_forward.cpp:478-491, "vector length mismatch"). */
+NF_API int nf_moe_bind_f32(nf_moe* handle, int which, const float* data_host, int64_t n);
+/* Checks that every tensor the descriptor needs is bound and builds the
+ * device layouts (block-scale atoms, gate/up interleave).  Required once
+ * before the first forward. */
+NF_API int nf_moe_finalize(nf_moe* handle);
+
+/* The MoE layer for `tokens` tokens, enqueued on `stream` (cudaStream_t,
+ * NULL = legacy default stream).  Replaces TextModel::moe
+ * (src/text_forward.cpp:924-963) stepped over each token, plus the hc = 1
+ * residual form of mhc_combine (src/text_forward.cpp:906, 1646-1657):
+ *   x_dev        BF16 [tokens, H] (the rmsnorm_stash output, BF16-valued)
+ *   residual_dev F32 [tokens, H] or NULL (NULL: y is the FFN branch alone)
+ *   y_dev        F32 [tokens, H]
+ *   topk_idx_dev INT32 [tokens, top_k] or NULL (router_select indices)
+ *   topk_w_dev   F32 [tokens, top_k] or NULL (router_select weights)
+ * Asynchronous: a device-side failure (bounded wait timeout) is reported by
+ * the next call that synchronises (nf_moe_sync or nf_moe_forward_host). */
+NF_API int nf_moe_forward(nf_moe* handle, const uint16_t* x_dev, const float* residual_dev, int tokens, float* y_dev,
+                   int32_t* topk_idx_dev, float* topk_w_dev, void* stream);
+/* Host-buffer form with the reference's own contract (fp32 in, fp32 out;
+ * moe(prefix, x, y) src/text_forward.cpp:924): copies x (BF16-valued F32,
+ * rounded to BF16 on the device) and residual to the device, runs the layer
+ * on the handle's internal stream, copies y (and the routes when the
+ * pointers are not NULL) back and synchronises. */
+NF_API int nf_moe_forward_host(nf_moe* handle, const float* x_host, const float* residual_host, int tokens, float* y_host,
+                        int32_t* topk_idx_host, float* topk_w_host);
+/* Waits for the handle's work on `stream` and reports a device-side error. */
+NF_API int nf_moe_sync(nf_moe* handle, void* stream);
+
+/* ---- stage-level entry points (parity tests and profiling) ---------------
+ * Router only: logits (optional, F32 [tokens, E]), indices and weights.
+ * gemv_bf16 + router_select (src/text_forward.cpp:926-931, 497-508,
+ * 1447-1471), bit-exact. */
+NF_API int nf_moe_route(nf_moe* handle, const uint16_t* x_dev, int tokens, float* logits_dev, int32_t* topk_idx_dev,
+                 float* topk_w_dev, void* stream);
+
+/* Internal buffers of the last forward, for parity tests.  Returns the
+ * device pointer and its size in bytes. */
+enum {
+    NF_DBG_COUNTS = 0,      /* INT32 [E]          tokens routed to each expert          */
+    NF_DBG_SEG_OFFSET = 1,  /* INT32 [E + 1]      first permuted row of each expert      */
+    NF_DBG_PAIR_ROW = 2,    /* INT32 [T, top_k]   permuted row of each (token, pick)     */
+    NF_DBG_ROW_TOKEN = 3,   /* INT32 [rows]       token of each permuted row, -1 = pad   */
+    NF_DBG_ACT_CODES = 4,   /* U8    [rows, H/2]  E2M1 codes of the gate/up input        */
+    NF_DBG_ACT_SF = 5,      /* U8    E4M3 block scales of the gate/up input (atom layout) */
+    NF_DBG_H_CODES = 6,     /* U8    [rows, I/2]  E2M1 codes of the down input           */
+    NF_DBG_H_SF = 7,        /* U8    E4M3 block scales of the down input (atom layout)   */
+    NF_DBG_DOWN = 8,        /* BF16 [rows, H] (NVFP4) or F32 (BF16 experts): down output */
+    NF_DBG_SHARED = 9,      /* F32   [T, H]       shared expert output                   */
+    NF_DBG_ROWS = 10        /* INT32 [1]          permuted rows in use (incl. padding)   */
+};
+NF_API int nf_moe_debug_tensor(nf_moe* handle, int which, void** dev_ptr, int64_t* bytes);
+/* Copies the first `bytes` bytes of a debug tensor to host memory
+ * (synchronous; waits for the handle's device work first). */
+NF_API int nf_moe_debug_read(nf_moe* handle, int which, void* host_dst, int64_t bytes);
+
+/* Per-stage timing with CUDA events recorded on the forward's stream.
+ * enable != 0 starts recording (and clears the totals); every forward then
+ * adds the device time of each stage.  nf_moe_stage_times synchronises and
+ * returns the accumulated milliseconds per stage (NF_STAGE_COUNT values)
+ * and the number of forwards recorded. */
+enum {
+    NF_STAGE_ROUTER = 0,
+    NF_STAGE_PERMUTE = 1,
+    NF_STAGE_GATE_UP = 2,
+    NF_STAGE_DOWN = 3,
+    NF_STAGE_SHARED = 4,
+    NF_STAGE_COMBINE = 5,
+    NF_STAGE_COUNT = 6
+};
+NF_API int nf_moe_profile(nf_moe* handle, int enable);
+NF_API int nf_moe_stage_times(nf_moe* handle, float* ms_out, int* forwards);
+
+/* NVFP4 dequantisation: out[r, c] = e2m1 * e4m3(scale) * global_scale with
+ * one rounding (Nvfp4MatrixView::at, src/nvfp4_decode.cpp:88-97), after the
+ * view constructor's validation (src/nvfp4_decode.cpp:56-79), which reads the
+ * scales back to the host.  Synchronous. */
+NF_API int nf_nvfp4_dequantize(const uint8_t* packed_dev, const uint8_t* scales_dev, float global_scale, int64_t rows,
+                        int64_t cols, float* out_dev, void* stream);
+/* NVFP4 activation quantiser (quant_dequant_nvfp4_activation,
+ * src/text_forward.cpp:527-550) on F32 rows: codes [rows, cols/2], E4M3
+ * scales [rows, cols/16] in plain row-major order, optional fake-quant
+ * values [rows, cols] (e2m1 * scale, the reference's output vector). */
+NF_API int nf_nvfp4_quantize(const float* x_dev, int64_t rows, int64_t cols, float input_scale, uint8_t* codes_dev,
+                      uint8_t* scales_dev, float* fake_dev, void* stream);
+/* Sigmoid exactly as the reference computes it (src/text_forward.cpp:42-49,
+ * libm expf), element-wise over n floats. */
+NF_API int nf_sigmoid_ref(const float* x_dev, int64_t n, float* y_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,97 @@
+// nf_internal.h -- declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace nf {
+
+// One GEMM work tile: 128 permuted rows of one expert x one 256-wide block
+// of output columns.
+struct NfTile {
+    int32_t expert;
+    int32_t row0;     // first permuted row (a multiple of 128)
+    int32_t n_block;  // 256-column output block
+    int32_t m_valid;  // rows of the tile that belong to the expert
+};
+
+// Device buffers the permutation kernels write.
+struct PermuteBuffers {
+    int32_t* chunk_counts;  // [nchunks, E]
+    int32_t* chunk_base;    // [nchunks, E]
+    int32_t* counts;        // [E]
+    int32_t* seg_off;       // [E + 1]
+    int32_t* pair_row;      // [T, K]
+    int32_t* row_token;     // [rows_cap]
+    NfTile* tiles_gu;       // gate/up tile list
+    NfTile* tiles_down;     // down tile list
+    int32_t* meta;          // [0] rows in use, [1] gate/up tiles, [2] down tiles, [3] m-tiles
+    uint8_t* a_codes;       // NVFP4 dispatch: [rows_cap, H/2]
+    uint8_t* a_sf;          //                 scale atoms
+    uint16_t* a_bf16;       // BF16 dispatch:  [rows_cap, H]
+};
+
+// Epilogue kinds of the tcgen05 GEMM.
+enum GemmEpi : int {
+    EPI_SWIGLU_QUANT = 0,  // NVFP4 gate/up: alpha, BF16 round, clamped SwiGLU, NVFP4 quantise for down
+    EPI_STORE_BF16 = 1,    // NVFP4 down: alpha, BF16 round, store BF16
+    EPI_SWIGLU_BF16 = 2,   // BF16 gate/up: clamped SwiGLU in fp32, store BF16 h
+    EPI_STORE_F32 = 3      // BF16 down: store F32
+};
+
+// Operand kinds.
+enum GemmKind : int { KIND_NVFP4 = 0, KIND_BF16 = 1 };
+
+struct GemmArgs {
+    int kind;            // GemmKind
+    int epi;             // GemmEpi
+    int K;               // reduction length in elements
+    int b_rows_per_expert;  // B rows per expert (0 for a dense GEMM)
+    // tile source: grouped (tiles + device tile count) or dense
+    const NfTile* tiles;
+    const int32_t* num_tiles_dev;
+    int dense_rows;      // > 0: dense GEMM over this many A rows
+    int n_blocks;        // 256-wide output blocks
+    // NVFP4 scale-factor atoms
+    const uint8_t* sfa;
+    const uint8_t* sfb;
+    // epilogue
+    const float* alpha0;       // [E] gate alpha (SwiGLU) or down alpha
+    const float* alpha1;       // [E] up alpha (SwiGLU)
+    const float* gscale_next;  // [E] 1 / input_scale of the down projection
+    float limit;               // swiglu_limit
+    const int32_t* row_token;  // permuted row -> token (-1 = padding), NULL for dense
+    void* out;                 // output rows
+    int64_t out_ld;            // output row stride in elements of the output type
+    uint8_t* out_sf;           // EPI_SWIGLU_QUANT: down-input scale atoms
+    int out_kgroups;           // EPI_SWIGLU_QUANT: 16-groups per output row
+    int* err;                  // device error word
+};
+
+// Host helpers (nf_gemm.cu).
+bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner_elems, uint64_t rows,
+                  uint32_t box_inner, uint32_t box_rows);
+cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tmb, const GemmArgs& args, int grid,
+                        cudaStream_t st);
+int gemm_grid_size(int device);
+
+// Launchers (nf_kernels.cu).
+cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H, int E, int K,
+                          float scaling, int normalize, int n_group, int topk_group, float* logits, int32_t* idx,
+                          float* wts, cudaStream_t st);
+cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
+                           const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st);
+cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair_row, const float* topk_w,
+                           const float* shared, const float* residual, int T, int K, int H, float* y,
+                           cudaStream_t st);
+cudaError_t launch_dequant(const uint8_t* packed, const uint8_t* scales, float gscale, int64_t rows, int64_t cols,
+                           float* out, cudaStream_t st);
+cudaError_t launch_quantize(const float* x, int64_t rows, int64_t cols, float gscale, uint8_t* codes,
+                            uint8_t* scales, float* fake, cudaStream_t st);
+cudaError_t launch_sigmoid_ref(const float* x, int64_t n, float* y, cudaStream_t st);
+cudaError_t launch_f32_to_bf16(const float* x, int64_t n, uint16_t* y, cudaStream_t st);
+
+constexpr int kChunkTokHost = 128;  // tokens per permutation chunk (nf_kernels.cu kChunkTok)
+
+}  // namespace nf

@@ -1,0 +1,783 @@
+// nf_moe.cu -- the C ABI (include/nf_moe.h): handle, weight binding with the
+// reference's validation, device layouts, and the forward pass that chains
+// router -> permutation/dispatch -> grouped gate/up GEMM (SwiGLU + NVFP4
+// quantisation fused) -> grouped down GEMM -> shared expert -> combine.
+#include "nf_moe.h"
+
+#include "nf_common.cuh"
+#include "nf_internal.h"
+
+#include <cfloat>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+using namespace nf;
+
+namespace {
+
+thread_local std::string g_create_error;
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+};
+
+}  // namespace
+
+struct nf_moe {
+    nf_moe_desc d{};
+    int device = 0;
+    int grid = 148;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    bool finalized = false;
+    std::vector<DevBuf> allocs;
+
+    // sizes
+    int rows_cap = 0, nchunks_cap = 0, mtiles_cap = 0;
+
+    // weights
+    uint16_t* router_w = nullptr;   // [E, H]
+    float* router_bias = nullptr;   // [E]
+    uint8_t* w_gu = nullptr;        // NVFP4 [E * 2I, H/2], 128-row gate/up interleave
+    uint8_t* w_gu_sf = nullptr;     // atoms
+    uint8_t* w_dn = nullptr;        // NVFP4 [E * H, I/2]
+    uint8_t* w_dn_sf = nullptr;
+    uint16_t* wb_gu = nullptr;      // BF16 experts [E * 2I, H]
+    uint16_t* wb_dn = nullptr;      // BF16 experts [E * H, I]
+    uint16_t* ws_gu = nullptr;      // shared [2 Is, H]
+    uint16_t* ws_dn = nullptr;      // shared [H, Is]
+    float* alpha_g = nullptr;       // [E] weight_scale_2 * input_scale
+    float* alpha_u = nullptr;
+    float* alpha_d = nullptr;
+    float* gs_g = nullptr;          // [E] 1 / input_scale
+    float* gs_d = nullptr;
+    std::vector<float> h_alpha_g, h_alpha_u, h_alpha_d, h_in_g, h_in_u, h_in_d;
+    std::vector<uint8_t> bound;     // [E * 3] expert projection bound flags
+    bool router_bound = false, bias_bound = false, sg_bound = false, su_bound = false, sd_bound = false;
+
+    // workspace
+    float* logits = nullptr;
+    int32_t* topk_idx = nullptr;
+    float* topk_w = nullptr;
+    PermuteBuffers pb{};
+    uint8_t* h_codes = nullptr;
+    uint8_t* h_sf = nullptr;
+    uint16_t* h_bf16 = nullptr;
+    void* down = nullptr;           // BF16 (NVFP4 experts) or F32 (BF16 experts)
+    uint16_t* sh_h = nullptr;       // [Tm, Is]
+    float* sh_out = nullptr;        // [Tm, H]
+    float* x_f32 = nullptr;         // host-path staging
+    uint16_t* x_bf16 = nullptr;
+    float* res_f32 = nullptr;
+    float* y_f32 = nullptr;
+    int* dev_err = nullptr;
+
+    // tensor maps built at finalize
+    CUtensorMap tm_a{}, tm_bgu{}, tm_h{}, tm_bdn{}, tm_sgu{}, tm_shh{}, tm_sdn{};
+    int last_tokens = 0;
+
+    // per-stage event profile: a ring of event sets, folded into stage_ms
+    static constexpr int kProfSets = 64;
+    bool profiling = false;
+    std::vector<cudaEvent_t> prof_ev;   // kProfSets * (NF_STAGE_COUNT + 1)
+    std::vector<uint8_t> prof_used;     // set holds an unfolded forward
+    int prof_next = 0, prof_forwards = 0;
+    double stage_ms[NF_STAGE_COUNT] = {};
+
+    void fold(int set) {
+        cudaEvent_t* ev = &prof_ev[static_cast<size_t>(set) * (NF_STAGE_COUNT + 1)];
+        cudaEventSynchronize(ev[NF_STAGE_COUNT]);
+        for (int s = 0; s < NF_STAGE_COUNT; ++s) {
+            float ms = 0.f;
+            if (cudaEventElapsedTime(&ms, ev[s], ev[s + 1]) == cudaSuccess) stage_ms[s] += ms;
+        }
+        prof_used[static_cast<size_t>(set)] = 0;
+        ++prof_forwards;
+    }
+    // events of the set recording the current forward (nullptr when off)
+    cudaEvent_t* prof_begin() {
+        if (!profiling) return nullptr;
+        const int set = prof_next;
+        prof_next = (prof_next + 1) % kProfSets;
+        if (prof_used[static_cast<size_t>(set)]) fold(set);
+        prof_used[static_cast<size_t>(set)] = 1;
+        return &prof_ev[static_cast<size_t>(set) * (NF_STAGE_COUNT + 1)];
+    }
+
+    int fail(int status, const char* fmt, ...) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof(buf), fmt, ap);
+        va_end(ap);
+        err = buf;
+        return status;
+    }
+    int cuda_fail(cudaError_t e, const char* what) {
+        return fail(NF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    }
+    template <typename T>
+    bool alloc(T** p, size_t count) {
+        void* q = nullptr;
+        const size_t bytes = count * sizeof(T) > 0 ? count * sizeof(T) : 16;
+        if (cudaMalloc(&q, bytes) != cudaSuccess) return false;
+        allocs.push_back({q, bytes});
+        *p = static_cast<T*>(q);
+        return true;
+    }
+    size_t bytes_of(const void* p) const {
+        for (const auto& a : allocs)
+            if (a.p == p) return a.bytes;
+        return 0;
+    }
+};
+
+namespace {
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+float e4m3_host(uint8_t bits) {
+    const int exponent = (bits >> 3) & 0xf;
+    const int mantissa = bits & 0x7;
+    float magnitude;
+    if (exponent == 0) magnitude = std::ldexp(static_cast<float>(mantissa), -9);
+    else if (exponent == 15 && mantissa == 7) magnitude = NAN;
+    else magnitude = std::ldexp(1.f + static_cast<float>(mantissa) / 8.f, exponent - 7);
+    return (bits & 0x80u) ? -magnitude : magnitude;
+}
+
+int64_t sf_off_host(int64_t row, int64_t kg, int64_t kgroups) {
+    const int64_t atom = (row >> 7) * (kgroups >> 2) + (kg >> 2);
+    return atom * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4 + (kg & 3);
+}
+
+// Validates block scales like Nvfp4MatrixView (src/nvfp4_decode.cpp:70-79)
+// and converts row-major [rows, kgroups] E4M3 scales into 128x4 atoms
+// (rows % 128 == 0).  -0 (0x80) is canonicalised to +0: both are the value 0
+// and the tensor core reads the scale as unsigned.
+bool scales_to_atoms(const uint8_t* scales, int64_t rows, int64_t kgroups, float gscale, std::vector<uint8_t>& out) {
+    out.assign(static_cast<size_t>(rows * kgroups), 0);
+    for (int64_t r = 0; r < rows; ++r) {
+        for (int64_t k = 0; k < kgroups; ++k) {
+            uint8_t b = scales[r * kgroups + k];
+            const float s = e4m3_host(b);
+            if (!std::isfinite(s) || s < 0.f) return false;
+            if (6.0 * static_cast<double>(s) * static_cast<double>(gscale) > static_cast<double>(FLT_MAX)) return false;
+            if (b == 0x80) b = 0;
+            out[static_cast<size_t>(sf_off_host(r, k, kgroups))] = b;
+        }
+    }
+    return true;
+}
+
+const char* proj_name(int proj) { return proj == NF_PROJ_GATE ? "gate_proj" : proj == NF_PROJ_UP ? "up_proj" : "down_proj"; }
+
+}  // namespace
+
+extern "C" {
+
+const char* nf_status_string(int s) {
+    switch (s) {
+        case NF_OK: return "ok";
+        case NF_ERR_INVALID: return "invalid argument";
+        case NF_ERR_SHAPE: return "shape mismatch";
+        case NF_ERR_LAYOUT: return "layout mismatch";
+        case NF_ERR_SCALE: return "bad scale";
+        case NF_ERR_STATE: return "bad state";
+        case NF_ERR_CUDA: return "CUDA error";
+        case NF_ERR_TIMEOUT: return "device wait timed out";
+        case NF_ERR_UNSUPPORTED: return "unsupported";
+        case NF_ERR_NOMEM: return "out of device memory";
+        case NF_ERR_CAPACITY: return "token capacity exceeded";
+        default: return "unknown status";
+    }
+}
+
+const char* nf_moe_last_error(const nf_moe* h) { return h ? h->err.c_str() : g_create_error.c_str(); }
+
+void nf_moe_destroy(nf_moe* h) {
+    if (!h) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    if (h->stream) {
+        cudaStreamSynchronize(h->stream);
+        cudaStreamDestroy(h->stream);
+    }
+    for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
+    for (auto& a : h->allocs) cudaFree(a.p);
+    cudaSetDevice(prev);
+    delete h;
+}
+
+int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
+    g_create_error.clear();
+    auto reject = [](int st, const char* msg) {
+        g_create_error = msg;
+        return st;
+    };
+    if (!desc || !out) return reject(NF_ERR_INVALID, "null descriptor or output");
+    *out = nullptr;
+    const nf_moe_desc& d = *desc;
+    if (d.hidden <= 0 || d.hidden % 256 != 0) return reject(NF_ERR_UNSUPPORTED, "hidden must be a positive multiple of 256");
+    if (d.inter <= 0 || d.inter % 128 != 0) return reject(NF_ERR_UNSUPPORTED, "inter must be a positive multiple of 128");
+    if (d.shared_inter < 0 || d.shared_inter % 128 != 0)
+        return reject(NF_ERR_UNSUPPORTED, "shared_inter must be 0 or a multiple of 128");
+    if (d.experts < 1 || d.experts > 1024) return reject(NF_ERR_UNSUPPORTED, "experts must be in [1, 1024]");
+    if (d.top_k < 1 || d.top_k > 32 || d.top_k > d.experts) return reject(NF_ERR_UNSUPPORTED, "top_k must be in [1, min(32, experts)]");
+    if (d.max_tokens < 1) return reject(NF_ERR_INVALID, "max_tokens must be positive");
+    if (d.n_group < 1) return reject(NF_ERR_INVALID, "n_group must be >= 1");
+    if (d.n_group > 1 && (d.n_group > 32 || d.experts % d.n_group != 0 || d.topk_group < 1 ||
+                          d.topk_group > d.n_group || d.top_k > d.topk_group * (d.experts / d.n_group)))
+        return reject(NF_ERR_UNSUPPORTED, "group-limited routing needs n_group <= 32 dividing experts and enough eligible experts");
+    if (d.expert_kind != NF_EXPERTS_NVFP4 && d.expert_kind != NF_EXPERTS_BF16)
+        return reject(NF_ERR_INVALID, "expert_kind must be NF_EXPERTS_NVFP4 or NF_EXPERTS_BF16");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+        return reject(NF_ERR_CUDA, "no such CUDA device");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) return reject(NF_ERR_CUDA, "cudaSetDevice failed");
+    cudaDeviceProp prop{};
+    cudaGetDeviceProperties(&prop, device);
+    if (prop.major != 10) {
+        cudaSetDevice(prev);
+        return reject(NF_ERR_UNSUPPORTED, "this library is built for sm_100a (B200)");
+    }
+
+    nf_moe* h = new nf_moe();
+    h->d = d;
+    h->device = device;
+    h->grid = gemm_grid_size(device);
+    const int64_t H = d.hidden, E = d.experts, K = d.top_k, I = d.inter, Is = d.shared_inter, Tm = d.max_tokens;
+    const int64_t pairs = Tm * K;
+    h->rows_cap = static_cast<int>(round_up(pairs + 127 * E, 128));
+    h->nchunks_cap = static_cast<int>((Tm + kChunkTokHost - 1) / kChunkTokHost);
+    h->mtiles_cap = h->rows_cap / 128;
+    const int64_t R = h->rows_cap;
+    const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
+    bool ok = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && h->alloc(&h->router_w, E * H) && h->alloc(&h->router_bias, E);
+    if (fp4) {
+        ok = ok && h->alloc(&h->w_gu, E * 2 * I * H / 2) && h->alloc(&h->w_gu_sf, E * 2 * I * H / 16) &&
+             h->alloc(&h->w_dn, E * H * I / 2) && h->alloc(&h->w_dn_sf, E * H * I / 16);
+    } else {
+        ok = ok && h->alloc(&h->wb_gu, E * 2 * I * H) && h->alloc(&h->wb_dn, E * H * I);
+    }
+    if (Is > 0) ok = ok && h->alloc(&h->ws_gu, 2 * Is * H) && h->alloc(&h->ws_dn, H * Is);
+    ok = ok && h->alloc(&h->alpha_g, E) && h->alloc(&h->alpha_u, E) && h->alloc(&h->alpha_d, E) &&
+         h->alloc(&h->gs_g, E) && h->alloc(&h->gs_d, E);
+    ok = ok && h->alloc(&h->logits, Tm * E) && h->alloc(&h->topk_idx, Tm * K) && h->alloc(&h->topk_w, Tm * K);
+    PermuteBuffers& b = h->pb;
+    ok = ok && h->alloc(&b.chunk_counts, static_cast<int64_t>(h->nchunks_cap) * E) &&
+         h->alloc(&b.chunk_base, static_cast<int64_t>(h->nchunks_cap) * E) && h->alloc(&b.counts, E) &&
+         h->alloc(&b.seg_off, E + 1) && h->alloc(&b.pair_row, pairs) && h->alloc(&b.row_token, R) &&
+         h->alloc(&b.tiles_gu, static_cast<int64_t>(h->mtiles_cap) * (I / 128)) &&
+         h->alloc(&b.tiles_down, static_cast<int64_t>(h->mtiles_cap) * (H / 256)) && h->alloc(&b.meta, 4);
+    if (fp4) {
+        ok = ok && h->alloc(&b.a_codes, R * H / 2) && h->alloc(&b.a_sf, R * H / 16) && h->alloc(&h->h_codes, R * I / 2) &&
+             h->alloc(&h->h_sf, R * I / 16);
+        uint16_t* dn = nullptr;
+        ok = ok && h->alloc(&dn, R * H);
+        h->down = dn;
+    } else {
+        ok = ok && h->alloc(&b.a_bf16, R * H) && h->alloc(&h->h_bf16, R * I);
+        float* dn = nullptr;
+        ok = ok && h->alloc(&dn, R * H);
+        h->down = dn;
+    }
+    if (Is > 0) ok = ok && h->alloc(&h->sh_h, Tm * Is) && h->alloc(&h->sh_out, Tm * H);
+    ok = ok && h->alloc(&h->x_f32, Tm * H) && h->alloc(&h->x_bf16, Tm * H) && h->alloc(&h->res_f32, Tm * H) &&
+         h->alloc(&h->y_f32, Tm * H) && h->alloc(&h->dev_err, 1);
+    if (!ok) {
+        cudaGetLastError();
+        nf_moe_destroy(h);
+        cudaSetDevice(prev);
+        return reject(NF_ERR_NOMEM, "device allocation failed");
+    }
+    cudaMemset(h->dev_err, 0, sizeof(int));
+    cudaMemset(b.row_token, 0xff, R * sizeof(int32_t));
+    h->bound.assign(static_cast<size_t>(E * 3), 0);
+    h->h_alpha_g.assign(E, 0.f);
+    h->h_alpha_u.assign(E, 0.f);
+    h->h_alpha_d.assign(E, 0.f);
+    h->h_in_g.assign(E, 0.f);
+    h->h_in_u.assign(E, 0.f);
+    h->h_in_d.assign(E, 0.f);
+    cudaSetDevice(prev);
+    *out = h;
+    return NF_OK;
+}
+
+int nf_moe_bind_nvfp4(nf_moe* h, int expert, int proj, const uint8_t* packed, const uint8_t* scales, float ws2,
+                      float in_scale, int64_t rows, int64_t cols) {
+    if (!h) return NF_ERR_INVALID;
+    const nf_moe_desc& d = h->d;
+    if (d.expert_kind != NF_EXPERTS_NVFP4) return h->fail(NF_ERR_STATE, "handle holds BF16 experts");
+    if (h->finalized) return h->fail(NF_ERR_STATE, "weights are already finalized");
+    if (expert < 0 || expert >= d.experts || proj < 0 || proj > 2) return h->fail(NF_ERR_INVALID, "bad expert or projection id");
+    if (!packed || !scales) return h->fail(NF_ERR_LAYOUT, "NVFP4 layout mlp.experts.%d.%s", expert, proj_name(proj));
+    const int64_t H = d.hidden, I = d.inter;
+    const int64_t want_rows = proj == NF_PROJ_DOWN ? H : I, want_cols = proj == NF_PROJ_DOWN ? I : H;
+    if (rows != want_rows || cols != want_cols || cols % 16 != 0)
+        return h->fail(NF_ERR_SHAPE, "NVFP4 shape mlp.experts.%d.%s", expert, proj_name(proj));
+    if (!(in_scale > 0.f) || !std::isfinite(in_scale)) return h->fail(NF_ERR_SCALE, "NVFP4 input scale");
+    if (!std::isfinite(ws2) || ws2 < FLT_MIN)
+        return h->fail(NF_ERR_SCALE, "NVFP4 global scale must be finite and at least the minimum normal float");
+    std::vector<uint8_t> atoms;
+    if (!scales_to_atoms(scales, rows, cols / 16, ws2, atoms))
+        return h->fail(NF_ERR_SCALE, "NVFP4 block scales must be finite and nonnegative");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    cudaError_t e = cudaSuccess;
+    const int64_t kbytes = cols / 2;
+    const int64_t slab = (cols / 64) * 512;  // one 128-row block of atoms
+    if (proj == NF_PROJ_DOWN) {
+        e = cudaMemcpy(h->w_dn + expert * H * kbytes, packed, static_cast<size_t>(H * kbytes), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(h->w_dn_sf + expert * H * (cols / 16), atoms.data(), atoms.size(), cudaMemcpyHostToDevice);
+    } else {
+        // gate rows j -> interleaved row (j / 128) * 256 + j % 128, up rows +128
+        const int64_t off = proj == NF_PROJ_UP ? 128 : 0;
+        uint8_t* base = h->w_gu + (expert * 2 * I + off) * kbytes;
+        e = cudaMemcpy2D(base, static_cast<size_t>(256 * kbytes), packed, static_cast<size_t>(128 * kbytes),
+                         static_cast<size_t>(128 * kbytes), static_cast<size_t>(I / 128), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) {
+            uint8_t* sbase = h->w_gu_sf + (expert * 2 * I / 128 + (proj == NF_PROJ_UP ? 1 : 0)) * slab;
+            e = cudaMemcpy2D(sbase, static_cast<size_t>(2 * slab), atoms.data(), static_cast<size_t>(slab),
+                             static_cast<size_t>(slab), static_cast<size_t>(I / 128), cudaMemcpyHostToDevice);
+        }
+    }
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return h->cuda_fail(e, "bind copy");
+    const float alpha = ws2 * in_scale;  // gemv_nvfp4_rows: alpha = scale2 * input_scale
+    if (proj == NF_PROJ_GATE) h->h_alpha_g[expert] = alpha, h->h_in_g[expert] = in_scale;
+    else if (proj == NF_PROJ_UP) h->h_alpha_u[expert] = alpha, h->h_in_u[expert] = in_scale;
+    else h->h_alpha_d[expert] = alpha, h->h_in_d[expert] = in_scale;
+    h->bound[static_cast<size_t>(expert * 3 + proj)] = 1;
+    return NF_OK;
+}
+
+int nf_moe_bind_bf16(nf_moe* h, int which, int expert, const uint16_t* data, int64_t rows, int64_t cols) {
+    if (!h) return NF_ERR_INVALID;
+    if (h->finalized) return h->fail(NF_ERR_STATE, "weights are already finalized");
+    const nf_moe_desc& d = h->d;
+    const int64_t H = d.hidden, E = d.experts, I = d.inter, Is = d.shared_inter;
+    int64_t wr = 0, wc = 0;
+    const char* name = "";
+    switch (which) {
+        case NF_BF16_ROUTER: wr = E, wc = H, name = "mlp.gate.weight"; break;
+        case NF_BF16_SHARED_GATE: wr = Is, wc = H, name = "mlp.shared_experts.gate_proj.weight"; break;
+        case NF_BF16_SHARED_UP: wr = Is, wc = H, name = "mlp.shared_experts.up_proj.weight"; break;
+        case NF_BF16_SHARED_DOWN: wr = H, wc = Is, name = "mlp.shared_experts.down_proj.weight"; break;
+        case NF_BF16_EXPERT_GATE: wr = I, wc = H, name = "mlp.experts.<e>.gate_proj.weight"; break;
+        case NF_BF16_EXPERT_UP: wr = I, wc = H, name = "mlp.experts.<e>.up_proj.weight"; break;
+        case NF_BF16_EXPERT_DOWN: wr = H, wc = I, name = "mlp.experts.<e>.down_proj.weight"; break;
+        default: return h->fail(NF_ERR_INVALID, "bad BF16 tensor id %d", which);
+    }
+    const bool is_expert = which >= NF_BF16_EXPERT_GATE;
+    if (is_expert && d.expert_kind != NF_EXPERTS_BF16) return h->fail(NF_ERR_STATE, "handle holds NVFP4 experts");
+    if (is_expert && (expert < 0 || expert >= E)) return h->fail(NF_ERR_INVALID, "bad expert id");
+    if ((which >= NF_BF16_SHARED_GATE && which <= NF_BF16_SHARED_DOWN) && Is == 0)
+        return h->fail(NF_ERR_STATE, "descriptor has no shared expert");
+    if (!data || rows != wr || cols != wc) return h->fail(NF_ERR_SHAPE, "BF16 linear layout %s", name);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    cudaError_t e = cudaSuccess;
+    const size_t rb = static_cast<size_t>(cols) * 2;
+    switch (which) {
+        case NF_BF16_ROUTER: e = cudaMemcpy(h->router_w, data, rows * rb, cudaMemcpyHostToDevice); h->router_bound = e == cudaSuccess; break;
+        case NF_BF16_SHARED_GATE:
+        case NF_BF16_SHARED_UP: {
+            uint16_t* base = h->ws_gu + (which == NF_BF16_SHARED_UP ? 128 : 0) * H;
+            e = cudaMemcpy2D(base, 256 * rb, data, 128 * rb, 128 * rb, static_cast<size_t>(Is / 128), cudaMemcpyHostToDevice);
+            if (which == NF_BF16_SHARED_GATE) h->sg_bound = e == cudaSuccess;
+            else h->su_bound = e == cudaSuccess;
+            break;
+        }
+        case NF_BF16_SHARED_DOWN: e = cudaMemcpy(h->ws_dn, data, rows * rb, cudaMemcpyHostToDevice); h->sd_bound = e == cudaSuccess; break;
+        case NF_BF16_EXPERT_GATE:
+        case NF_BF16_EXPERT_UP: {
+            uint16_t* base = h->wb_gu + (expert * 2 * I + (which == NF_BF16_EXPERT_UP ? 128 : 0)) * H;
+            e = cudaMemcpy2D(base, 256 * rb, data, 128 * rb, 128 * rb, static_cast<size_t>(I / 128), cudaMemcpyHostToDevice);
+            if (e == cudaSuccess) h->bound[static_cast<size_t>(expert * 3 + (which - NF_BF16_EXPERT_GATE))] = 1;
+            break;
+        }
+        case NF_BF16_EXPERT_DOWN:
+            e = cudaMemcpy(h->wb_dn + expert * H * I, data, rows * rb, cudaMemcpyHostToDevice);
+            if (e == cudaSuccess) h->bound[static_cast<size_t>(expert * 3 + 2)] = 1;
+            break;
+    }
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return h->cuda_fail(e, "bind copy");
+    return NF_OK;
+}
+
+int nf_moe_bind_f32(nf_moe* h, int which, const float* data, int64_t n) {
+    if (!h) return NF_ERR_INVALID;
+    if (h->finalized) return h->fail(NF_ERR_STATE, "weights are already finalized");
+    if (which != NF_F32_ROUTER_BIAS) return h->fail(NF_ERR_INVALID, "bad F32 tensor id %d", which);
+    if (!data || n != h->d.experts) return h->fail(NF_ERR_SHAPE, "vector length mismatch for mlp.gate.e_score_correction_bias");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    const cudaError_t e = cudaMemcpy(h->router_bias, data, static_cast<size_t>(n) * sizeof(float), cudaMemcpyHostToDevice);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return h->cuda_fail(e, "bind copy");
+    h->bias_bound = true;
+    return NF_OK;
+}
+
+int nf_moe_finalize(nf_moe* h) {
+    if (!h) return NF_ERR_INVALID;
+    if (h->finalized) return NF_OK;
+    const nf_moe_desc& d = h->d;
+    const int64_t H = d.hidden, E = d.experts, I = d.inter, Is = d.shared_inter;
+    if (!h->router_bound) return h->fail(NF_ERR_STATE, "missing tensor mlp.gate.weight");
+    if (!h->bias_bound) return h->fail(NF_ERR_STATE, "missing tensor mlp.gate.e_score_correction_bias");
+    if (Is > 0 && !(h->sg_bound && h->su_bound && h->sd_bound)) return h->fail(NF_ERR_STATE, "missing tensor mlp.shared_experts");
+    for (int64_t e = 0; e < E; ++e)
+        for (int p = 0; p < 3; ++p)
+            if (!h->bound[static_cast<size_t>(e * 3 + p)])
+                return h->fail(NF_ERR_STATE, "missing tensor mlp.experts.%lld.%s", static_cast<long long>(e), proj_name(p));
+    const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
+    std::vector<float> gs_g(E, 1.f), gs_d(E, 1.f);
+    if (fp4) {
+        for (int64_t e = 0; e < E; ++e) {
+            if (h->h_in_g[e] != h->h_in_u[e])
+                return h->fail(NF_ERR_UNSUPPORTED,
+                               "mlp.experts.%lld gate_proj and up_proj input_scale differ; this build needs one gate/up input scale",
+                               static_cast<long long>(e));
+            gs_g[e] = 1.f / h->h_in_g[e];  // quant_dequant_nvfp4_activation: global_scale = 1 / input_scale
+            gs_d[e] = 1.f / h->h_in_d[e];
+        }
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    cudaError_t e = cudaMemcpy(h->alpha_g, h->h_alpha_g.data(), E * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(h->alpha_u, h->h_alpha_u.data(), E * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(h->alpha_d, h->h_alpha_d.data(), E * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(h->gs_g, gs_g.data(), E * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(h->gs_d, gs_d.data(), E * 4, cudaMemcpyHostToDevice);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return h->cuda_fail(e, "finalize copy");
+    const int64_t R = h->rows_cap, Tm = d.max_tokens;
+    bool ok = true;
+    if (fp4) {
+        ok = ok && make_tmap_2d(&h->tm_a, h->pb.a_codes, false, H / 2, R, 128, 128);
+        ok = ok && make_tmap_2d(&h->tm_bgu, h->w_gu, false, H / 2, E * 2 * I, 128, 256);
+        ok = ok && make_tmap_2d(&h->tm_h, h->h_codes, false, I / 2, R, 128, 128);
+        ok = ok && make_tmap_2d(&h->tm_bdn, h->w_dn, false, I / 2, E * H, 128, 256);
+    } else {
+        ok = ok && make_tmap_2d(&h->tm_a, h->pb.a_bf16, true, H, R, 64, 128);
+        ok = ok && make_tmap_2d(&h->tm_bgu, h->wb_gu, true, H, E * 2 * I, 64, 256);
+        ok = ok && make_tmap_2d(&h->tm_h, h->h_bf16, true, I, R, 64, 128);
+        ok = ok && make_tmap_2d(&h->tm_bdn, h->wb_dn, true, I, E * H, 64, 256);
+    }
+    if (Is > 0) {
+        ok = ok && make_tmap_2d(&h->tm_sgu, h->ws_gu, true, H, 2 * Is, 64, 256);
+        ok = ok && make_tmap_2d(&h->tm_shh, h->sh_h, true, Is, Tm, 64, 128);
+        ok = ok && make_tmap_2d(&h->tm_sdn, h->ws_dn, true, Is, H, 64, 256);
+    }
+    if (!ok) return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    h->finalized = true;
+    return NF_OK;
+}
+
+static int check_forward_args(nf_moe* h, const void* x, int tokens) {
+    if (!h) return NF_ERR_INVALID;
+    if (!h->finalized) return h->fail(NF_ERR_STATE, "nf_moe_finalize has not run");
+    if (!x) return h->fail(NF_ERR_INVALID, "null input");
+    if (tokens < 0) return h->fail(NF_ERR_INVALID, "negative token count");
+    if (tokens > h->d.max_tokens) return h->fail(NF_ERR_CAPACITY, "tokens %d exceed max_tokens %d", tokens, h->d.max_tokens);
+    return NF_OK;
+}
+
+int nf_moe_route(nf_moe* h, const uint16_t* x, int tokens, float* logits, int32_t* idx, float* w, void* stream) {
+    int st = check_forward_args(h, x, tokens);
+    if (st != NF_OK) return st;
+    if (tokens == 0) return NF_OK;
+    const nf_moe_desc& d = h->d;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    const cudaError_t e = launch_router(x, h->router_w, h->router_bias, tokens, d.hidden, d.experts, d.top_k,
+                                        d.routed_scaling, d.normalize, d.n_group, d.topk_group,
+                                        logits ? logits : h->logits, idx ? idx : h->topk_idx, w ? w : h->topk_w, s);
+    cudaSetDevice(prev);
+    return e == cudaSuccess ? NF_OK : h->cuda_fail(e, "router launch");
+}
+
+static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx_user,
+                        float* w_user, cudaStream_t s) {
+    const nf_moe_desc& d = h->d;
+    const int H = d.hidden, E = d.experts, K = d.top_k, I = d.inter, Is = d.shared_inter;
+    const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
+    int32_t* idx = idx_user ? idx_user : h->topk_idx;
+    float* w = w_user ? w_user : h->topk_w;
+    h->last_tokens = T;
+    cudaEvent_t* ev = h->prof_begin();
+    auto mark = [&](int stage) {
+        if (ev) cudaEventRecord(ev[stage], s);
+    };
+    mark(NF_STAGE_ROUTER);
+    cudaError_t e = launch_router(x, h->router_w, h->router_bias, T, H, E, K, d.routed_scaling, d.normalize, d.n_group,
+                                  d.topk_group, h->logits, idx, w, s);
+    if (e != cudaSuccess) return h->cuda_fail(e, "router launch");
+    mark(NF_STAGE_PERMUTE);
+    e = launch_permute(idx, x, T, K, E, H, I / 128, H / 256, h->gs_g, fp4 ? 0 : 1, h->pb, s);
+    if (e != cudaSuccess) return h->cuda_fail(e, "permute launch");
+    mark(NF_STAGE_GATE_UP);
+
+    GemmArgs g{};
+    g.err = h->dev_err;
+    g.limit = d.swiglu_limit;
+    // gate/up
+    g.kind = fp4 ? KIND_NVFP4 : KIND_BF16;
+    g.epi = fp4 ? EPI_SWIGLU_QUANT : EPI_SWIGLU_BF16;
+    g.K = H;
+    g.b_rows_per_expert = 2 * I;
+    g.tiles = h->pb.tiles_gu;
+    g.num_tiles_dev = h->pb.meta + 1;
+    g.dense_rows = 0;
+    g.n_blocks = I / 128;
+    g.sfa = h->pb.a_sf;
+    g.sfb = h->w_gu_sf;
+    g.alpha0 = h->alpha_g;
+    g.alpha1 = h->alpha_u;
+    g.gscale_next = h->gs_d;
+    g.row_token = h->pb.row_token;
+    g.out = fp4 ? static_cast<void*>(h->h_codes) : static_cast<void*>(h->h_bf16);
+    g.out_ld = fp4 ? I / 2 : I;
+    g.out_sf = h->h_sf;
+    g.out_kgroups = I / 16;
+    e = launch_gemm(h->tm_a, h->tm_bgu, g, h->grid, s);
+    if (e != cudaSuccess) return h->cuda_fail(e, "gate/up GEMM launch");
+    mark(NF_STAGE_DOWN);
+    // down
+    g.epi = fp4 ? EPI_STORE_BF16 : EPI_STORE_F32;
+    g.K = I;
+    g.b_rows_per_expert = H;
+    g.tiles = h->pb.tiles_down;
+    g.num_tiles_dev = h->pb.meta + 2;
+    g.n_blocks = H / 256;
+    g.sfa = h->h_sf;
+    g.sfb = h->w_dn_sf;
+    g.alpha0 = h->alpha_d;
+    g.out = h->down;
+    g.out_ld = H;
+    e = launch_gemm(h->tm_h, h->tm_bdn, g, h->grid, s);
+    if (e != cudaSuccess) return h->cuda_fail(e, "down GEMM launch");
+    mark(NF_STAGE_SHARED);
+    // shared expert (dense BF16)
+    if (Is > 0) {
+        CUtensorMap tm_x;
+        if (!make_tmap_2d(&tm_x, x, true, H, T, 64, 128)) return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+        GemmArgs sg{};
+        sg.err = h->dev_err;
+        sg.limit = d.swiglu_limit;
+        sg.kind = KIND_BF16;
+        sg.epi = EPI_SWIGLU_BF16;
+        sg.K = H;
+        sg.dense_rows = T;
+        sg.n_blocks = Is / 128;
+        sg.out = h->sh_h;
+        sg.out_ld = Is;
+        e = launch_gemm(tm_x, h->tm_sgu, sg, h->grid, s);
+        if (e != cudaSuccess) return h->cuda_fail(e, "shared gate/up GEMM launch");
+        sg.epi = EPI_STORE_F32;
+        sg.K = Is;
+        sg.n_blocks = H / 256;
+        sg.out = h->sh_out;
+        sg.out_ld = H;
+        e = launch_gemm(h->tm_shh, h->tm_sdn, sg, h->grid, s);
+        if (e != cudaSuccess) return h->cuda_fail(e, "shared down GEMM launch");
+    }
+    mark(NF_STAGE_COMBINE);
+    e = launch_combine(h->down, fp4, h->pb.pair_row, w, Is > 0 ? h->sh_out : nullptr, residual, T, K, H, y, s);
+    if (e != cudaSuccess) return h->cuda_fail(e, "combine launch");
+    mark(NF_STAGE_COUNT);
+    return NF_OK;
+}
+
+int nf_moe_profile(nf_moe* h, int enable) {
+    if (!h) return NF_ERR_INVALID;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    if (h->prof_ev.empty()) {
+        h->prof_ev.resize(static_cast<size_t>(nf_moe::kProfSets) * (NF_STAGE_COUNT + 1));
+        for (auto& ev : h->prof_ev) {
+            if (cudaEventCreate(&ev) != cudaSuccess) {
+                cudaSetDevice(prev);
+                return h->fail(NF_ERR_CUDA, "cudaEventCreate failed");
+            }
+        }
+        h->prof_used.assign(nf_moe::kProfSets, 0);
+    }
+    for (int set = 0; set < nf_moe::kProfSets; ++set) h->prof_used[static_cast<size_t>(set)] = 0;
+    for (double& v : h->stage_ms) v = 0.0;
+    h->prof_forwards = 0;
+    h->prof_next = 0;
+    h->profiling = enable != 0;
+    cudaSetDevice(prev);
+    return NF_OK;
+}
+
+int nf_moe_stage_times(nf_moe* h, float* ms_out, int* forwards) {
+    if (!h || !ms_out) return NF_ERR_INVALID;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    for (int set = 0; set < static_cast<int>(h->prof_used.size()); ++set)
+        if (h->prof_used[static_cast<size_t>(set)]) h->fold(set);
+    cudaSetDevice(prev);
+    for (int s = 0; s < NF_STAGE_COUNT; ++s) ms_out[s] = static_cast<float>(h->stage_ms[s]);
+    if (forwards) *forwards = h->prof_forwards;
+    return NF_OK;
+}
+
+int nf_moe_forward(nf_moe* h, const uint16_t* x, const float* residual, int tokens, float* y, int32_t* idx, float* w,
+                   void* stream) {
+    int st = check_forward_args(h, x, tokens);
+    if (st != NF_OK) return st;
+    if (!y) return h->fail(NF_ERR_INVALID, "null output");
+    if (tokens == 0) return NF_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    st = forward_impl(h, x, residual, tokens, y, idx, w, static_cast<cudaStream_t>(stream));
+    cudaSetDevice(prev);
+    return st;
+}
+
+int nf_moe_sync(nf_moe* h, void* stream) {
+    if (!h) return NF_ERR_INVALID;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    int derr = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&derr, h->dev_err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && derr != 0) cudaMemset(h->dev_err, 0, sizeof(int));
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return h->cuda_fail(e, "synchronise");
+    if (derr != 0) return h->fail(NF_ERR_TIMEOUT, "device-side wait gave up (code %d)", derr);
+    return NF_OK;
+}
+
+int nf_moe_forward_host(nf_moe* h, const float* x_host, const float* res_host, int tokens, float* y_host,
+                        int32_t* idx_host, float* w_host) {
+    int st = check_forward_args(h, x_host, tokens);
+    if (st != NF_OK) return st;
+    if (!y_host) return h->fail(NF_ERR_INVALID, "null output");
+    if (tokens == 0) return NF_OK;
+    const int64_t n = static_cast<int64_t>(tokens) * h->d.hidden;
+    const int64_t nk = static_cast<int64_t>(tokens) * h->d.top_k;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    cudaStream_t s = h->stream;
+    cudaError_t e = cudaMemcpyAsync(h->x_f32, x_host, n * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && res_host) e = cudaMemcpyAsync(h->res_f32, res_host, n * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = launch_f32_to_bf16(h->x_f32, n, h->x_bf16, s);
+    if (e != cudaSuccess) {
+        cudaSetDevice(prev);
+        return h->cuda_fail(e, "host input copy");
+    }
+    st = forward_impl(h, h->x_bf16, res_host ? h->res_f32 : nullptr, tokens, h->y_f32, nullptr, nullptr, s);
+    if (st == NF_OK) {
+        e = cudaMemcpyAsync(y_host, h->y_f32, n * 4, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess && idx_host) e = cudaMemcpyAsync(idx_host, h->topk_idx, nk * 4, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess && w_host) e = cudaMemcpyAsync(w_host, h->topk_w, nk * 4, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) st = h->cuda_fail(e, "host output copy");
+    }
+    cudaSetDevice(prev);
+    if (st != NF_OK) return st;
+    return nf_moe_sync(h, s);
+}
+
+int nf_moe_debug_tensor(nf_moe* h, int which, void** ptr, int64_t* bytes) {
+    if (!h || !ptr || !bytes) return NF_ERR_INVALID;
+    void* p = nullptr;
+    switch (which) {
+        case NF_DBG_COUNTS: p = h->pb.counts; break;
+        case NF_DBG_SEG_OFFSET: p = h->pb.seg_off; break;
+        case NF_DBG_PAIR_ROW: p = h->pb.pair_row; break;
+        case NF_DBG_ROW_TOKEN: p = h->pb.row_token; break;
+        case NF_DBG_ACT_CODES: p = h->pb.a_codes; break;
+        case NF_DBG_ACT_SF: p = h->pb.a_sf; break;
+        case NF_DBG_H_CODES: p = h->h_codes; break;
+        case NF_DBG_H_SF: p = h->h_sf; break;
+        case NF_DBG_DOWN: p = h->down; break;
+        case NF_DBG_SHARED: p = h->sh_out; break;
+        case NF_DBG_ROWS: p = h->pb.meta; break;
+        default: return h->fail(NF_ERR_INVALID, "bad debug tensor id %d", which);
+    }
+    if (!p) return h->fail(NF_ERR_STATE, "debug tensor %d does not exist for this descriptor", which);
+    *ptr = p;
+    *bytes = static_cast<int64_t>(h->bytes_of(p));
+    return NF_OK;
+}
+
+int nf_moe_debug_read(nf_moe* h, int which, void* host, int64_t bytes) {
+    void* p = nullptr;
+    int64_t n = 0;
+    const int st = nf_moe_debug_tensor(h, which, &p, &n);
+    if (st != NF_OK) return st;
+    if (!host || bytes < 0 || bytes > n) return h->fail(NF_ERR_INVALID, "debug read of %lld bytes from a %lld-byte tensor",
+                                                       static_cast<long long>(bytes), static_cast<long long>(n));
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(host, p, static_cast<size_t>(bytes), cudaMemcpyDeviceToHost);
+    cudaSetDevice(prev);
+    return e == cudaSuccess ? NF_OK : h->cuda_fail(e, "debug read");
+}
+
+int nf_nvfp4_dequantize(const uint8_t* packed, const uint8_t* scales, float gscale, int64_t rows, int64_t cols,
+                        float* out, void* stream) {
+    if (rows <= 0 || cols <= 0 || cols % 16 != 0 || !packed || !scales || !out) return NF_ERR_SHAPE;
+    if (!std::isfinite(gscale) || gscale < FLT_MIN) return NF_ERR_SCALE;
+    std::vector<uint8_t> hs(static_cast<size_t>(rows * (cols / 16)));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(hs.data(), scales, hs.size(), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return NF_ERR_CUDA;
+    for (uint8_t b : hs) {
+        const float v = e4m3_host(b);
+        if (!std::isfinite(v) || v < 0.f) return NF_ERR_SCALE;
+        if (6.0 * static_cast<double>(v) * static_cast<double>(gscale) > static_cast<double>(FLT_MAX)) return NF_ERR_SCALE;
+    }
+    if (launch_dequant(packed, scales, gscale, rows, cols, out, s) != cudaSuccess) return NF_ERR_CUDA;
+    return cudaStreamSynchronize(s) == cudaSuccess ? NF_OK : NF_ERR_CUDA;
+}
+
+int nf_nvfp4_quantize(const float* x, int64_t rows, int64_t cols, float in_scale, uint8_t* codes, uint8_t* scales,
+                      float* fake, void* stream) {
+    if (!(in_scale > 0.f) || !std::isfinite(in_scale) || cols % 16 != 0) return NF_ERR_SCALE;  // "NVFP4 input scale"
+    if (rows < 0 || cols <= 0 || !x || !codes || !scales) return NF_ERR_INVALID;
+    if (rows == 0) return NF_OK;
+    return launch_quantize(x, rows, cols, 1.f / in_scale, codes, scales, fake, static_cast<cudaStream_t>(stream)) ==
+                   cudaSuccess
+               ? NF_OK
+               : NF_ERR_CUDA;
+}
+
+int nf_sigmoid_ref(const float* x, int64_t n, float* y, void* stream) {
+    if (n < 0 || (n > 0 && (!x || !y))) return NF_ERR_INVALID;
+    if (n == 0) return NF_OK;
+    return launch_sigmoid_ref(x, n, y, static_cast<cudaStream_t>(stream)) == cudaSuccess ? NF_OK : NF_ERR_CUDA;
+}
+
+}  // extern "C"

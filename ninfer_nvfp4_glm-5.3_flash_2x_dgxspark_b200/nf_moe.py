@@ -1,0 +1,290 @@
+"""Python host binding of libnf_moe.so (include/nf_moe.h) through ctypes.
+
+`MoeLayer` mirrors the reference's MoE contract: weights are bound by their
+checkpoint names (parameter_schema, src/parameter_schema.cpp:53-98) from a
+name -> array mapping (the role of the reference's safetensors Store,
+src/text_forward.cpp:328-495), and `forward` runs TextModel::moe
+(src/text_forward.cpp:924-963) for a batch of tokens.  Failures raise
+RuntimeError carrying the library's message, the way the reference's
+fail() throws std::runtime_error (src/text_forward.cpp:40).
+
+There is no fallback: if the CUDA library is missing or cannot load, this
+module raises.  Device buffers are passed as raw pointers (torch tensors'
+data_ptr() or integers); torch is only used by callers for device memory.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Mapping
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libnf_moe.so"
+
+NF_OK = 0
+NF_ERR = {1: "INVALID", 2: "SHAPE", 3: "LAYOUT", 4: "SCALE", 5: "STATE", 6: "CUDA", 7: "TIMEOUT",
+          8: "UNSUPPORTED", 9: "NOMEM", 10: "CAPACITY"}
+PROJ_GATE, PROJ_UP, PROJ_DOWN = 0, 1, 2
+BF16_ROUTER, BF16_SHARED_GATE, BF16_SHARED_UP, BF16_SHARED_DOWN = 0, 1, 2, 3
+BF16_EXPERT_GATE, BF16_EXPERT_UP, BF16_EXPERT_DOWN = 4, 5, 6
+F32_ROUTER_BIAS = 0
+EXPERTS_NVFP4, EXPERTS_BF16 = 0, 1
+DBG = dict(counts=0, seg_offset=1, pair_row=2, row_token=3, act_codes=4, act_sf=5, h_codes=6, h_sf=7, down=8,
+           shared=9, rows=10)
+
+EXPORTED = [
+    "nf_moe_create", "nf_moe_destroy", "nf_moe_last_error", "nf_status_string", "nf_moe_bind_nvfp4",
+    "nf_moe_bind_bf16", "nf_moe_bind_f32", "nf_moe_finalize", "nf_moe_forward", "nf_moe_forward_host",
+    "nf_moe_sync", "nf_moe_route", "nf_moe_debug_tensor", "nf_moe_debug_read", "nf_nvfp4_dequantize", "nf_nvfp4_quantize",
+    "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times",
+]
+STAGES = ["router", "permute", "gate_up", "down", "shared", "combine"]
+
+
+class Desc(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_int32), ("experts", ctypes.c_int32), ("top_k", ctypes.c_int32),
+        ("inter", ctypes.c_int32), ("shared_inter", ctypes.c_int32), ("n_group", ctypes.c_int32),
+        ("topk_group", ctypes.c_int32), ("normalize", ctypes.c_int32), ("routed_scaling", ctypes.c_float),
+        ("swiglu_limit", ctypes.c_float), ("expert_kind", ctypes.c_int32), ("max_tokens", ctypes.c_int32),
+    ]
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads the library (raises when it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with python build.py")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    P, I32, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+    sig = {
+        "nf_moe_create": ([ctypes.POINTER(Desc), I32, ctypes.POINTER(P)], I32),
+        "nf_moe_destroy": ([P], None),
+        "nf_moe_last_error": ([P], ctypes.c_char_p),
+        "nf_status_string": ([I32], ctypes.c_char_p),
+        "nf_moe_bind_nvfp4": ([P, I32, I32, P, P, F, F, I64, I64], I32),
+        "nf_moe_bind_bf16": ([P, I32, I32, P, I64, I64], I32),
+        "nf_moe_bind_f32": ([P, I32, P, I64], I32),
+        "nf_moe_finalize": ([P], I32),
+        "nf_moe_forward": ([P, P, P, I32, P, P, P, P], I32),
+        "nf_moe_forward_host": ([P, P, P, I32, P, P, P], I32),
+        "nf_moe_sync": ([P, P], I32),
+        "nf_moe_route": ([P, P, I32, P, P, P, P], I32),
+        "nf_moe_debug_tensor": ([P, I32, ctypes.POINTER(P), ctypes.POINTER(I64)], I32),
+        "nf_moe_debug_read": ([P, I32, P, I64], I32),
+        "nf_nvfp4_dequantize": ([P, P, F, I64, I64, P, P], I32),
+        "nf_nvfp4_quantize": ([P, I64, I64, F, P, P, P, P], I32),
+        "nf_sigmoid_ref": ([P, I64, P, P], I32),
+        "nf_moe_profile": ([P, I32], I32),
+        "nf_moe_stage_times": ([P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(I32)], I32),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = lib
+    return lib
+
+
+def _ptr(a) -> int | None:
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if isinstance(a, np.ndarray):
+        assert a.flags["C_CONTIGUOUS"]
+        return a.ctypes.data
+    return a.data_ptr()  # torch tensor
+
+
+class NfError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{message} [{NF_ERR.get(status, status)}]")
+        self.status = status
+
+
+class MoeLayer:
+    """One MoE layer resident on one GPU."""
+
+    def __init__(self, hidden: int, experts: int, top_k: int, inter: int, shared_inter: int, *,
+                 routed_scaling: float = 1.0, swiglu_limit: float = 10.0, n_group: int = 1, topk_group: int = 1,
+                 normalize: bool = True, bf16_experts: bool = False, max_tokens: int = 64, device: int = 0):
+        self.lib = load()
+        self.desc = Desc(hidden, experts, top_k, inter, shared_inter, n_group, topk_group, int(normalize),
+                         routed_scaling, swiglu_limit, EXPERTS_BF16 if bf16_experts else EXPERTS_NVFP4, max_tokens)
+        h = ctypes.c_void_p()
+        st = self.lib.nf_moe_create(ctypes.byref(self.desc), device, ctypes.byref(h))
+        if st != NF_OK:
+            raise NfError(st, self.lib.nf_moe_last_error(None).decode())
+        self.h = h
+        self.device = device
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.nf_moe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, st: int) -> None:
+        if st != NF_OK:
+            raise NfError(st, self.lib.nf_moe_last_error(self.h).decode())
+
+    # ---- binding -----------------------------------------------------------
+    def bind_nvfp4(self, expert: int, proj: int, packed: np.ndarray, scales: np.ndarray, weight_scale_2: float,
+                   input_scale: float) -> None:
+        packed = np.ascontiguousarray(packed, dtype=np.uint8)
+        scales = np.ascontiguousarray(scales, dtype=np.uint8)
+        rows, half = packed.shape
+        self._check(self.lib.nf_moe_bind_nvfp4(self.h, expert, proj, _ptr(packed), _ptr(scales),
+                                               float(weight_scale_2), float(input_scale), rows, 2 * half))
+
+    def bind_bf16(self, which: int, data: np.ndarray, expert: int = 0) -> None:
+        data = np.ascontiguousarray(data, dtype=np.uint16)
+        rows, cols = data.shape
+        self._check(self.lib.nf_moe_bind_bf16(self.h, which, expert, _ptr(data), rows, cols))
+
+    def bind_f32(self, which: int, data: np.ndarray) -> None:
+        data = np.ascontiguousarray(data, dtype=np.float32)
+        self._check(self.lib.nf_moe_bind_f32(self.h, which, _ptr(data), data.size))
+
+    def finalize(self) -> None:
+        self._check(self.lib.nf_moe_finalize(self.h))
+
+    def bind_layer(self, lay) -> None:
+        """Binds a workload.Layer and finalizes."""
+        self.bind_bf16(BF16_ROUTER, lay.router_w)
+        self.bind_f32(F32_ROUTER_BIAS, lay.bias)
+        if lay.shared_inter > 0:
+            self.bind_bf16(BF16_SHARED_GATE, lay.shared_gate)
+            self.bind_bf16(BF16_SHARED_UP, lay.shared_up)
+            self.bind_bf16(BF16_SHARED_DOWN, lay.shared_down)
+        for e in range(lay.experts):
+            if lay.bf16_experts:
+                self.bind_bf16(BF16_EXPERT_GATE, lay.gate_bf16[e], e)
+                self.bind_bf16(BF16_EXPERT_UP, lay.up_bf16[e], e)
+                self.bind_bf16(BF16_EXPERT_DOWN, lay.down_bf16[e], e)
+            else:
+                self.bind_nvfp4(e, PROJ_GATE, lay.gate_packed[e], lay.gate_scales[e], lay.gate_ws2[e], lay.gate_in[e])
+                self.bind_nvfp4(e, PROJ_UP, lay.up_packed[e], lay.up_scales[e], lay.up_ws2[e], lay.up_in[e])
+                self.bind_nvfp4(e, PROJ_DOWN, lay.down_packed[e], lay.down_scales[e], lay.down_ws2[e], lay.down_in[e])
+        self.finalize()
+
+    def bind_from_store(self, store: Mapping[str, np.ndarray], prefix: str) -> None:
+        """Binds every tensor of one MoE layer by checkpoint name, e.g.
+        prefix = "model.language_model.layers.3." (names as in
+        parameter_schema add_moe, src/parameter_schema.cpp:72-98).  A missing
+        name raises "missing tensor <name>" like Store::get
+        (src/text_forward.cpp:462-466)."""
+
+        def get(name: str) -> np.ndarray:
+            if name not in store:
+                raise NfError(5, f"missing tensor {name}")
+            return np.asarray(store[name])
+
+        self.bind_bf16(BF16_ROUTER, get(prefix + "mlp.gate.weight"))
+        self.bind_f32(F32_ROUTER_BIAS, get(prefix + "mlp.gate.e_score_correction_bias"))
+        if self.desc.shared_inter > 0:
+            self.bind_bf16(BF16_SHARED_GATE, get(prefix + "mlp.shared_experts.gate_proj.weight"))
+            self.bind_bf16(BF16_SHARED_UP, get(prefix + "mlp.shared_experts.up_proj.weight"))
+            self.bind_bf16(BF16_SHARED_DOWN, get(prefix + "mlp.shared_experts.down_proj.weight"))
+        for e in range(self.desc.experts):
+            base = f"{prefix}mlp.experts.{e}."
+            for proj, name in ((PROJ_GATE, "gate_proj"), (PROJ_UP, "up_proj"), (PROJ_DOWN, "down_proj")):
+                if self.desc.expert_kind == EXPERTS_BF16:
+                    self.bind_bf16(BF16_EXPERT_GATE + proj, get(base + name + ".weight"), e)
+                else:
+                    ws2 = get(base + name + ".weight_scale_2")
+                    ins = get(base + name + ".input_scale")
+                    if ws2.ndim != 0 or ins.ndim != 0:
+                        raise NfError(3, f"expected rank-0 F32 for {base + name}.weight_scale_2")
+                    self.bind_nvfp4(e, proj, get(base + name + ".weight"), get(base + name + ".weight_scale"),
+                                    float(ws2), float(ins))
+        self.finalize()
+
+    # ---- execution ---------------------------------------------------------
+    def forward(self, x_dev, y_dev, tokens: int, residual_dev=None, idx_dev=None, w_dev=None, stream=0) -> None:
+        """Device-buffer forward (asynchronous on `stream`)."""
+        self._check(self.lib.nf_moe_forward(self.h, _ptr(x_dev), _ptr(residual_dev), tokens, _ptr(y_dev),
+                                            _ptr(idx_dev), _ptr(w_dev), stream or None))
+
+    def forward_host(self, x: np.ndarray, residual: np.ndarray | None = None, with_routes: bool = False):
+        """Host fp32 in / fp32 out, the reference's own moe() contract."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T = x.shape[0]
+        y = np.empty_like(x)
+        idx = np.empty((T, self.desc.top_k), np.int32) if with_routes else None
+        w = np.empty((T, self.desc.top_k), np.float32) if with_routes else None
+        res = None if residual is None else np.ascontiguousarray(residual, dtype=np.float32)
+        self._check(self.lib.nf_moe_forward_host(self.h, _ptr(x), _ptr(res), T, _ptr(y), _ptr(idx), _ptr(w)))
+        return (y, idx, w) if with_routes else y
+
+    def route(self, x_dev, tokens: int, logits_dev=None, idx_dev=None, w_dev=None, stream=0) -> None:
+        self._check(self.lib.nf_moe_route(self.h, _ptr(x_dev), tokens, _ptr(logits_dev), _ptr(idx_dev),
+                                          _ptr(w_dev), stream or None))
+
+    def sync(self, stream=0) -> None:
+        self._check(self.lib.nf_moe_sync(self.h, stream or None))
+
+    def debug_tensor(self, which: str) -> tuple[int, int]:
+        p = ctypes.c_void_p()
+        n = ctypes.c_int64()
+        self._check(self.lib.nf_moe_debug_tensor(self.h, DBG[which], ctypes.byref(p), ctypes.byref(n)))
+        return p.value, n.value
+
+    def profile(self, enable: bool) -> None:
+        """Start (and clear) or stop per-stage CUDA-event timing."""
+        self._check(self.lib.nf_moe_profile(self.h, int(enable)))
+
+    def stage_times(self) -> tuple[dict, int]:
+        """Accumulated device milliseconds per stage and the forwards counted."""
+        ms = (ctypes.c_float * len(STAGES))()
+        n = ctypes.c_int()
+        self._check(self.lib.nf_moe_stage_times(self.h, ms, ctypes.byref(n)))
+        return {name: float(ms[i]) for i, name in enumerate(STAGES)}, n.value
+
+    def debug_read(self, which: str, dtype, count: int) -> np.ndarray:
+        """Host copy of the first `count` elements of an internal buffer."""
+        out = np.empty(count, dtype)
+        self._check(self.lib.nf_moe_debug_read(self.h, DBG[which], _ptr(out), out.nbytes))
+        return out
+
+
+def dequantize(packed_dev, scales_dev, global_scale: float, rows: int, cols: int, out_dev, stream=0) -> int:
+    return load().nf_nvfp4_dequantize(_ptr(packed_dev), _ptr(scales_dev), global_scale, rows, cols, _ptr(out_dev),
+                                      stream or None)
+
+
+def quantize(x_dev, rows: int, cols: int, input_scale: float, codes_dev, scales_dev, fake_dev=None, stream=0) -> int:
+    return load().nf_nvfp4_quantize(_ptr(x_dev), rows, cols, input_scale, _ptr(codes_dev), _ptr(scales_dev),
+                                    _ptr(fake_dev), stream or None)
+
+
+def sigmoid_ref(x_dev, n: int, y_dev, stream=0) -> int:
+    return load().nf_sigmoid_ref(_ptr(x_dev), n, _ptr(y_dev), stream or None)
+
+
+def sf_atom_offset(row: np.ndarray, kgroup: np.ndarray, kgroups_total: int) -> np.ndarray:
+    """Byte offset of block scale (row, kgroup) in the tcgen05 atom layout."""
+    row = np.asarray(row, dtype=np.int64)
+    kgroup = np.asarray(kgroup, dtype=np.int64)
+    atom = (row >> 7) * (kgroups_total >> 2) + (kgroup >> 2)
+    return atom * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4 + (kgroup & 3)
+
+
+def sf_from_atoms(atoms: np.ndarray, rows: int, kgroups: int) -> np.ndarray:
+    """Row-major [rows, kgroups] scales from the atom layout."""
+    r = np.arange(rows)[:, None]
+    k = np.arange(kgroups)[None, :]
+    return np.asarray(atoms)[sf_atom_offset(r, k, kgroups)]

@@ -1,0 +1,70 @@
+"""The C-ABI library loads, exports every entry point include/nf_moe.h
+declares, and rejects bad descriptors before touching a device.  No compute
+call runs here (there is no GPU in the CPU suite)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from helpers import REPO, nfm
+
+HEADER = REPO / "include" / "nf_moe.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"NF_API\s+[\w\s\*]+?\b(nf_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert "nf_moe_forward" in syms and "nf_moe_bind_nvfp4" in syms and len(syms) >= 16
+
+
+def test_library_exports_every_declared_symbol():
+    m = nfm()
+    lib = m.load()
+    for s in declared_symbols():
+        assert hasattr(lib, s), f"{s} declared in nf_moe.h but not exported"
+    assert set(m.EXPORTED) <= set(declared_symbols())
+
+
+def test_status_strings():
+    lib = nfm().load()
+    assert lib.nf_status_string(0) == b"ok"
+    assert lib.nf_status_string(10) == b"token capacity exceeded"
+    assert lib.nf_status_string(999) == b"unknown status"
+
+
+def test_create_rejects_bad_descriptors_without_gpu():
+    m = nfm()
+    lib = m.load()
+    cases = [
+        dict(hidden=100),          # not a multiple of 256
+        dict(inter=96),            # not a multiple of 128
+        dict(top_k=0),
+        dict(top_k=9, experts=8),
+        dict(experts=2000),
+        dict(max_tokens=0),
+        dict(n_group=3),           # does not divide the experts
+        dict(expert_kind=7),
+    ]
+    base = dict(hidden=256, experts=8, top_k=2, inter=128, shared_inter=128, n_group=1, topk_group=1, normalize=1,
+                routed_scaling=1.0, swiglu_limit=10.0, expert_kind=0, max_tokens=16)
+    for c in cases:
+        d = m.Desc(**{**base, **c})
+        h = ctypes.c_void_p()
+        st = lib.nf_moe_create(ctypes.byref(d), 0, ctypes.byref(h))
+        assert st != 0 and not h.value
+        assert lib.nf_moe_last_error(None)
+    # null arguments
+    assert lib.nf_moe_create(None, 0, None) == 1
+    assert lib.nf_moe_forward(None, None, None, 0, None, None, None, None) == 1
+    assert lib.nf_moe_bind_nvfp4(None, 0, 0, None, None, 1.0, 1.0, 1, 16) == 1
+
+
+def test_python_layer_raises_with_message_without_gpu():
+    m = nfm()
+    with pytest.raises(RuntimeError):
+        m.MoeLayer(hidden=100, experts=8, top_k=2, inter=128, shared_inter=128)
