@@ -138,6 +138,58 @@ NF_DEV uint32_t quantize_group16(const float (&x)[16], float global_scale, uint3
     return scode;
 }
 
+// Two E2M1 codes from the hardware conversion (round to nearest even on the
+// E2M1 grid, saturating at +-6): low nibble = `even`, high nibble = `odd`.
+// On finite inputs this is cast_to_e2m1 (the reference's ties -- 0.25, 2.5
+// and 5 down, 0.75, 1.25, 1.75 and 3.5 up -- are exactly round-half-even on
+// that grid); NaN is not handled here.
+NF_DEV uint32_t e2m1x2_hw(float even, float odd) {
+    uint16_t r;
+    asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u16.u8 %0, t;\n\t}"
+        : "=h"(r)
+        : "f"(odd), "f"(even));
+    return r;
+}
+
+// E4M3 code from the hardware conversion (round to nearest even, saturating
+// at 448).  Matches f32_to_e4m3 for v in [2^-6, inf); below 2^-6 the
+// reference's subnormal rule differs, so callers route that band elsewhere.
+NF_DEV uint32_t e4m3_hw(float v) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.f), "f"(v));
+    return r & 0xffu;
+}
+
+// quantize_group16 with the hardware conversions: identical results (NaN
+// groups and scales below 2^-6 take the reference-rule path).  kBf16Input:
+// the inputs are BF16 values already, so the BF16 rounding is skipped.
+template <bool kBf16Input>
+NF_DEV uint32_t quantize_group16_fast(const float (&x)[16], float global_scale, uint32_t (&codes)[2]) {
+    float r[16];
+    float peak = 0.f;
+    bool nan = false;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        r[i] = kBf16Input ? x[i] : bf16_round(x[i]);
+        nan |= isnan(r[i]);
+        const float a = fabsf(r[i]);
+        peak = (peak < a) ? a : peak;
+    }
+    if (nan) return quantize_group16(x, global_scale, codes);
+    float scale = __fmul_rn(global_scale, __fdiv_rn(peak, 6.f));
+    scale = scale > 448.f ? 448.f : scale;
+    const uint32_t scode = scale >= 0.015625f ? e4m3_hw(scale) : f32_to_e4m3(scale);
+    scale = e4m3_to_f32(scode);
+    const float reduced = __fdiv_rn(scale, global_scale);
+    const float output_scale = __fdiv_rn(1.f, __fadd_rn(reduced, reduced == 0.f ? 1.0e8f : 0.f));
+    uint32_t b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b[i] = e2m1x2_hw(__fmul_rn(r[2 * i], output_scale), __fmul_rn(r[2 * i + 1], output_scale));
+    codes[0] = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
+    codes[1] = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
+    return scode;
+}
+
 // Offset of block scale (row, kgroup) inside the tcgen05 scale-factor atom
 // layout: 128 rows x 4 scales per 512-byte atom, atoms ordered row-block
 // major then K-block; inside an atom byte (row % 32) * 16 + ((row % 128) / 32)

@@ -13,8 +13,9 @@
 // elements) loaded by TMA with 128-byte swizzle; block-scale atoms arrive by
 // 1-D bulk copy and move to TMEM with tcgen05.cp; one elected thread issues
 // the MMAs and commits stage release / accumulator-ready to mbarriers.
-// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
-// issuer, warps 2-5 epilogue (TMEM lane quadrant = warp % 4).
+// Warp roles (576 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
+// issuer, warps 2-17 epilogue (TMEM lane quadrant = warp % 4, four column
+// slices per quadrant).
 // The persistent grid walks a device-side tile list, so the launch needs no
 // host synchronisation after routing.
 // Every wait is bounded (nf_common.cuh mbar_wait); on a timeout the kernel
@@ -27,6 +28,8 @@
 namespace nf {
 
 constexpr int BM = 128, BN = 256, STAGES = 4;
+constexpr int kEpiWarps = 16;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int A_STAGE_BYTES = BM * 128;
 constexpr int B_STAGE_BYTES = BN * 128;
 constexpr int SFA_STAGE_BYTES = 4 * 512;   // [k-step][512]
@@ -60,26 +63,16 @@ __device__ __forceinline__ TileInfo get_tile(const GemmArgs& a, int i) {
     return t;
 }
 
-// Reference sigmoid / SiLU shape (src/text_forward.cpp:42-51) with the CUDA
-// expf; the SwiGLU output feeds a 4-bit quantiser, so the last-bit agreement
-// the router needs is not required here.
-__device__ __forceinline__ float silu_dev(float x) {
-    float s;
-    if (x >= 0.f) s = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-x)));
-    else {
-        const float z = expf(x);
-        s = __fdiv_rn(z, __fadd_rn(1.f, z));
-    }
-    return __fmul_rn(x, s);
-}
-
 // swiglu_clamp element (src/text_forward.cpp:1439-1445): min(g, L) into SiLU,
-// up clamped to [-L, L] with std::min/std::max semantics.
-__device__ __forceinline__ float swiglu_dev(float g, float u, float L) {
+// up clamped to [-L, L] with std::min / std::max semantics, with a fast SiLU
+// (x / (1 + e^-x), hardware exp2 and divide).  Used
+// where the result feeds a 4-bit quantiser or a BF16 store, so agreement to
+// a few ulp with the reference's libm SiLU is all that matters.
+__device__ __forceinline__ float swiglu_fast(float g, float u, float L) {
     const float cg = (L < g) ? L : g;
     const float lo = (-L < u) ? u : -L;
     const float cu = (lo < L) ? lo : L;
-    return __fmul_rn(silu_dev(cg), cu);
+    return __fmul_rn(__fdividef(cg, 1.f + __expf(-cg)), cu);
 }
 
 __device__ __forceinline__ void set_abort(volatile int* cta_abort, int* dev_err, int code) {
@@ -88,7 +81,7 @@ __device__ __forceinline__ void set_abort(volatile int* cta_abort, int* dev_err,
 }
 
 template <int KIND, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, const GemmArgs args) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -112,7 +105,7 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(&empty[s], 1);
         }
         mbar_init(acc_full, 1);
-        mbar_init(acc_empty, 4);
+        mbar_init(acc_empty, kEpiWarps);
         mbar_init(drain, 1);
         *cta_abort = 0;
         fence_barrier_init();
@@ -254,7 +247,13 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else {
         // ------------------------------ epilogue ----------------------------
-        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        // kEpiWarps warps: a warp may only touch the TMEM lane quadrant
+        // warp % 4, and the 4 warps of one quadrant split the tile's columns
+        // into slices.  Each warp copies its slice of the accumulator into
+        // registers, hands the accumulator back to the MMA warp at once, then
+        // does the math and the stores while the next tile's MMAs run.
+        const int q = warp & 3;
+        const int cs = (warp - 2) >> 2;
         const int r = q * 32 + lane;
         const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16);
         uint32_t acc_phase = 0;
@@ -270,108 +269,90 @@ __global__ void __launch_bounds__(192, 1)
             tc_fence_after();
             const int row = t.row0 + r;
             const bool valid = r < t.m_valid;
-            if (EPI == EPI_SWIGLU_QUANT) {
-                const float ag = args.alpha0[t.expert], au = args.alpha1[t.expert];
-                const float gsd = args.gscale_next[t.expert], L = args.limit;
-                uint32_t codes[16];
-                uint32_t sfw0 = 0u, sfw1 = 0u;
-#pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t g[16], u[16];
-                    tmem_ld16(tbase + 16 * c, g);
-                    tmem_ld16(tbase + 128 + 16 * c, u);
-                    tmem_wait_ld();
-                    float h[16];
+            const bool warp_live = q * 32 < t.m_valid;  // some row of this warp belongs to the expert
+            uint32_t v[64];
+            if (warp_live) {
+                if (EPI == EPI_SWIGLU_QUANT || EPI == EPI_SWIGLU_BF16) {
+                    // gate columns [32cs, 32cs+32), up columns 128 further
+                    tmem_ld16(tbase + 32 * cs, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                    tmem_ld16(tbase + 32 * cs + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+                    tmem_ld16(tbase + 128 + 32 * cs, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
+                    tmem_ld16(tbase + 128 + 32 * cs + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
+                } else {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float gv = bf16_round(__fmul_rn(__uint_as_float(g[j]), ag));
-                        const float uv = bf16_round(__fmul_rn(__uint_as_float(u[j]), au));
-                        h[j] = swiglu_dev(gv, uv, L);
-                    }
-                    uint32_t cc[2];
-                    const uint32_t sc = quantize_group16(h, gsd, cc);
-                    codes[2 * c] = cc[0];
-                    codes[2 * c + 1] = cc[1];
-                    if (c < 4) sfw0 |= sc << (8 * c);
-                    else sfw1 |= sc << (8 * (c - 4));
+                    for (int c = 0; c < 4; ++c)
+                        tmem_ld16(tbase + 64 * cs + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&v[16 * c]));
                 }
-                if (valid) {
-                    uint8_t* o = static_cast<uint8_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld + t.n_block * 64;
-                    uint4* d = reinterpret_cast<uint4*>(o);
-                    d[0] = make_uint4(codes[0], codes[1], codes[2], codes[3]);
-                    d[1] = make_uint4(codes[4], codes[5], codes[6], codes[7]);
-                    d[2] = make_uint4(codes[8], codes[9], codes[10], codes[11]);
-                    d[3] = make_uint4(codes[12], codes[13], codes[14], codes[15]);
-                    *reinterpret_cast<uint32_t*>(args.out_sf + sf_atom_offset(row, t.n_block * 8, args.out_kgroups)) = sfw0;
-                    *reinterpret_cast<uint32_t*>(args.out_sf + sf_atom_offset(row, t.n_block * 8 + 4, args.out_kgroups)) = sfw1;
-                }
-            } else if (EPI == EPI_STORE_BF16) {
-                const float a = args.alpha0[t.expert];
-#pragma unroll 1
-                for (int c = 0; c < 16; ++c) {
-                    uint32_t v[16];
-                    tmem_ld16(tbase + 16 * c, v);
-                    tmem_wait_ld();
-                    uint32_t p[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t lo = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[2 * j]), a));
-                        const uint32_t hi = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[2 * j + 1]), a));
-                        p[j] = lo | (hi << 16);
-                    }
-                    if (valid) {
-                        uint16_t* o = static_cast<uint16_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
-                                      t.n_block * BN + 16 * c;
-                        uint4* d = reinterpret_cast<uint4*>(o);
-                        d[0] = make_uint4(p[0], p[1], p[2], p[3]);
-                        d[1] = make_uint4(p[4], p[5], p[6], p[7]);
-                    }
-                }
-            } else if (EPI == EPI_SWIGLU_BF16) {
-                const float L = args.limit;
-#pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t g[16], u[16];
-                    tmem_ld16(tbase + 16 * c, g);
-                    tmem_ld16(tbase + 128 + 16 * c, u);
-                    tmem_wait_ld();
-                    uint32_t p[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t lo = f32_to_bf16_bits(swiglu_dev(__uint_as_float(g[2 * j]), __uint_as_float(u[2 * j]), L));
-                        const uint32_t hi =
-                            f32_to_bf16_bits(swiglu_dev(__uint_as_float(g[2 * j + 1]), __uint_as_float(u[2 * j + 1]), L));
-                        p[j] = lo | (hi << 16);
-                    }
-                    if (valid) {
-                        uint16_t* o = static_cast<uint16_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
-                                      t.n_block * 128 + 16 * c;
-                        uint4* d = reinterpret_cast<uint4*>(o);
-                        d[0] = make_uint4(p[0], p[1], p[2], p[3]);
-                        d[1] = make_uint4(p[4], p[5], p[6], p[7]);
-                    }
-                }
-            } else {  // EPI_STORE_F32
-#pragma unroll 1
-                for (int c = 0; c < 16; ++c) {
-                    uint32_t v[16];
-                    tmem_ld16(tbase + 16 * c, v);
-                    tmem_wait_ld();
-                    if (valid) {
-                        float* o = static_cast<float*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
-                                   t.n_block * BN + 16 * c;
-                        uint4* d = reinterpret_cast<uint4*>(o);
-                        d[0] = make_uint4(v[0], v[1], v[2], v[3]);
-                        d[1] = make_uint4(v[4], v[5], v[6], v[7]);
-                        d[2] = make_uint4(v[8], v[9], v[10], v[11]);
-                        d[3] = make_uint4(v[12], v[13], v[14], v[15]);
-                    }
-                }
+                tmem_wait_ld();
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty);
             acc_phase ^= 1u;
+            if (!warp_live) continue;
+
+            if (EPI == EPI_SWIGLU_QUANT) {
+                const float ag = args.alpha0[t.expert], au = args.alpha1[t.expert];
+                const float gsd = args.gscale_next[t.expert], L = args.limit;
+                uint32_t cc[2][2];
+                uint32_t sc[2];
+#pragma unroll
+                for (int g = 0; g < 2; ++g) {
+                    float h[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float gv = bf16_round(__fmul_rn(__uint_as_float(v[16 * g + j]), ag));
+                        const float uv = bf16_round(__fmul_rn(__uint_as_float(v[32 + 16 * g + j]), au));
+                        h[j] = swiglu_fast(gv, uv, L);
+                    }
+                    sc[g] = quantize_group16_fast<false>(h, gsd, cc[g]);
+                }
+                if (valid) {
+                    uint8_t* o = static_cast<uint8_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
+                                 t.n_block * 64 + cs * 16;
+                    *reinterpret_cast<uint4*>(o) = make_uint4(cc[0][0], cc[0][1], cc[1][0], cc[1][1]);
+                    *reinterpret_cast<uint16_t*>(args.out_sf + sf_atom_offset(row, t.n_block * 8 + cs * 2, args.out_kgroups)) =
+                        static_cast<uint16_t>(sc[0] | (sc[1] << 8));
+                }
+            } else if (EPI == EPI_STORE_BF16) {
+                const float a = args.alpha0[t.expert];
+                uint32_t p[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const uint32_t lo = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[2 * j]), a));
+                    const uint32_t hi = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[2 * j + 1]), a));
+                    p[j] = lo | (hi << 16);
+                }
+                if (valid) {
+                    uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) +
+                                                        static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + 64 * cs);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) d[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                }
+            } else if (EPI == EPI_SWIGLU_BF16) {
+                const float L = args.limit;
+                uint32_t p[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const uint32_t lo = f32_to_bf16_bits(swiglu_fast(__uint_as_float(v[2 * j]), __uint_as_float(v[32 + 2 * j]), L));
+                    const uint32_t hi =
+                        f32_to_bf16_bits(swiglu_fast(__uint_as_float(v[2 * j + 1]), __uint_as_float(v[32 + 2 * j + 1]), L));
+                    p[j] = lo | (hi << 16);
+                }
+                if (valid) {
+                    uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) +
+                                                        static_cast<int64_t>(row) * args.out_ld + t.n_block * 128 + 32 * cs);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) d[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                }
+            } else {  // EPI_STORE_F32
+                if (valid) {
+                    uint4* d = reinterpret_cast<uint4*>(static_cast<float*>(args.out) +
+                                                        static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + 64 * cs);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) d[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                }
+            }
         }
     }
 
@@ -435,7 +416,7 @@ static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tmb, co
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    gemm_kernel<KIND, EPI><<<grid, 192, SMEM_BYTES, st>>>(tma, tmb, args);
+    gemm_kernel<KIND, EPI><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tmb, args);
     return cudaGetLastError();
 }
 

@@ -91,6 +91,10 @@ cudaError_t launch_quantize(const float* x, int64_t rows, int64_t cols, float gs
                             uint8_t* scales, float* fake, cudaStream_t st);
 cudaError_t launch_sigmoid_ref(const float* x, int64_t n, float* y, cudaStream_t st);
 cudaError_t launch_f32_to_bf16(const float* x, int64_t n, uint16_t* y, cudaStream_t st);
+cudaError_t launch_format_selfcheck(unsigned long long* mismatches_dev, cudaStream_t st);
+// Builds the per-device lookup index of the router's sigmoid exception table
+// (once per device; the calling thread's current device).
+cudaError_t prepare_device_tables();
 
 constexpr int kChunkTokHost = 128;  // tokens per permutation chunk (nf_kernels.cu kChunkTok)
 

@@ -16,8 +16,29 @@ namespace nf {
 // Sigmoid exactly as the reference computes it (src/text_forward.cpp:42-49).
 // exp is evaluated in double and rounded once (a correctly rounded expf);
 // the arguments where libm's expf gives a different sigmoid come from the
-// build-time exception table.
+// build-time exception table, found through a 2^20-bucket index over the
+// key bits (bucket = bits >> 12; at most a few dozen keys, one or two cache
+// lines, per bucket).
 // ---------------------------------------------------------------------------
+constexpr int kSigBucketShift = 12;
+constexpr int kSigBuckets = 1 << (32 - kSigBucketShift);
+__device__ uint32_t g_sig_index[kSigBuckets + 1];
+
+__global__ void sig_index_kernel() {
+    for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b <= kSigBuckets;
+         b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        // first key >= b << shift (lower bound)
+        const uint64_t target = static_cast<uint64_t>(b) << kSigBucketShift;
+        int lo = 0, hi = NF_SIG_TABLE_N;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (static_cast<uint64_t>(g_sig_keys[mid]) < target) lo = mid + 1;
+            else hi = mid;
+        }
+        g_sig_index[b] = static_cast<uint32_t>(lo);
+    }
+}
+
 __device__ __forceinline__ float sigmoid_ref(float x) {
     float r;
     if (x >= 0.f) {
@@ -28,14 +49,10 @@ __device__ __forceinline__ float sigmoid_ref(float x) {
         r = __fdiv_rn(z, __fadd_rn(1.f, z));
     }
     const uint32_t key = __float_as_uint(x);
-    int lo = 0, hi = NF_SIG_TABLE_N - 1;
-    while (lo <= hi) {
-        const int mid = (lo + hi) >> 1;
-        const uint32_t k = g_sig_keys[mid];
-        if (k == key) return __uint_as_float(g_sig_vals[mid]);
-        if (k < key) lo = mid + 1;
-        else hi = mid - 1;
-    }
+    const uint32_t b = key >> kSigBucketShift;
+    const uint32_t hi = g_sig_index[b + 1];
+    for (uint32_t j = g_sig_index[b]; j < hi; ++j)
+        if (g_sig_keys[j] == key) return __uint_as_float(g_sig_vals[j]);
     return r;
 }
 
@@ -45,66 +62,55 @@ __global__ void sigmoid_ref_kernel(const float* __restrict__ x, int64_t n, float
         y[i] = sigmoid_ref(x[i]);
 }
 
+cudaError_t prepare_device_tables() {
+    static int ready[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (ready[dev]) return cudaSuccess;
+    sig_index_kernel<<<1024, 256>>>();
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) ready[dev] = 1;
+    return e;
+}
+
 // ---------------------------------------------------------------------------
 // Router logits: gemv_bf16 (src/text_forward.cpp:497-508) for every token:
 // logits[t, e] = sum_c bf16(W[e, c]) * x[t, c], accumulated sequentially in
-// fp32 with separate multiply and add (no fused multiply-add), which is what
-// makes the result bit-identical to the reference.  A CTA stages
-// kRouterTok tokens of x in shared memory; each thread runs 4 independent
-// chains (4 tokens of one expert) for instruction-level parallelism.
+// fp32 with a separately rounded multiply and add in column order, which is
+// what makes the result bit-identical to the reference.  One thread runs the
+// chains of one expert for two tokens with paired f32x2 instructions; the
+// chain length (H dependent adds) is the kernel's latency floor, so the
+// work is spread one chain pair per thread over as many SMs as possible.
 // ---------------------------------------------------------------------------
-constexpr int kRouterTok = 16;
+__device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
 
-__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
-                                                            const uint16_t* __restrict__ w, int T, int H, int E,
-                                                            float* __restrict__ logits) {
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    uint16_t* xs = reinterpret_cast<uint16_t*>(smem_raw);  // [kRouterTok][H]
-    const int t0 = blockIdx.x * kRouterTok;
-    const int nt = min(kRouterTok, T - t0);
-    // stage x rows (16-byte vectors; H % 8 == 0)
-    const int vec_per_row = H / 8;
-    for (int i = threadIdx.x; i < kRouterTok * vec_per_row; i += blockDim.x) {
-        const int r = i / vec_per_row, c = i % vec_per_row;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < nt) v = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0 + r) * H)[c];
-        reinterpret_cast<uint4*>(xs + static_cast<int64_t>(r) * H)[c] = v;
-    }
-    __syncthreads();
-    const int items = E * (kRouterTok / 4);
-    for (int item = threadIdx.x; item < items; item += blockDim.x) {
-        const int e = item % E, tq = item / E;
-        const uint16_t* wr = w + static_cast<int64_t>(e) * H;
-        const uint16_t* x0 = xs + static_cast<int64_t>(tq * 4) * H;
-        float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-        for (int c = 0; c < H; c += 8) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(wr + c);
-            const uint4 a = *reinterpret_cast<const uint4*>(x0 + c);
-            const uint4 b = *reinterpret_cast<const uint4*>(x0 + H + c);
-            const uint4 d = *reinterpret_cast<const uint4*>(x0 + 2 * H + c);
-            const uint4 f = *reinterpret_cast<const uint4*>(x0 + 3 * H + c);
-            const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-            const uint32_t aa[4] = {a.x, a.y, a.z, a.w}, bb[4] = {b.x, b.y, b.z, b.w};
-            const uint32_t dd[4] = {d.x, d.y, d.z, d.w}, ff[4] = {f.x, f.y, f.z, f.w};
+__global__ void router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, int T, int H,
+                                     int E, float* __restrict__ logits) {
+    const int64_t item = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    const int pairs = (T + 1) / 2;
+    if (item >= static_cast<int64_t>(pairs) * E) return;
+    const int tp = static_cast<int>(item / E), e = static_cast<int>(item % E);
+    const int t0 = 2 * tp, t1 = min(2 * tp + 1, T - 1);
+    const uint4* wr = reinterpret_cast<const uint4*>(w + static_cast<int64_t>(e) * H);
+    const uint4* xa = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0) * H);
+    const uint4* xb = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t1) * H);
+    float2 acc = make_float2(0.f, 0.f);
+    for (int c = 0; c < H / 8; ++c) {
+        const uint4 wv = __ldg(wr + c), av = __ldg(xa + c), bv = __ldg(xb + c);
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        const uint32_t aa[4] = {av.x, av.y, av.z, av.w}, bb[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int sh = 16 * h;
-                    const float wf = __uint_as_float(((ww[j] >> sh) & 0xffffu) << 16);
-                    acc0 = __fadd_rn(acc0, __fmul_rn(wf, __uint_as_float(((aa[j] >> sh) & 0xffffu) << 16)));
-                    acc1 = __fadd_rn(acc1, __fmul_rn(wf, __uint_as_float(((bb[j] >> sh) & 0xffffu) << 16)));
-                    acc2 = __fadd_rn(acc2, __fmul_rn(wf, __uint_as_float(((dd[j] >> sh) & 0xffffu) << 16)));
-                    acc3 = __fadd_rn(acc3, __fmul_rn(wf, __uint_as_float(((ff[j] >> sh) & 0xffffu) << 16)));
-                }
-            }
+        for (int j = 0; j < 4; ++j) {
+            const float w0 = bf16_lo(ww[j]), w1 = bf16_hi(ww[j]);
+            acc = __fadd2_rn(acc, __fmul2_rn(make_float2(w0, w0), make_float2(bf16_lo(aa[j]), bf16_lo(bb[j]))));
+            acc = __fadd2_rn(acc, __fmul2_rn(make_float2(w1, w1), make_float2(bf16_hi(aa[j]), bf16_hi(bb[j]))));
         }
-        const int tb = t0 + tq * 4;
-        if (tb + 0 < T) logits[static_cast<int64_t>(tb + 0) * E + e] = acc0;
-        if (tb + 1 < T) logits[static_cast<int64_t>(tb + 1) * E + e] = acc1;
-        if (tb + 2 < T) logits[static_cast<int64_t>(tb + 2) * E + e] = acc2;
-        if (tb + 3 < T) logits[static_cast<int64_t>(tb + 3) * E + e] = acc3;
     }
+    logits[static_cast<int64_t>(t0) * E + e] = acc.x;
+    if (2 * tp + 1 < T) logits[static_cast<int64_t>(t1) * E + e] = acc.y;
 }
 
 // ---------------------------------------------------------------------------
@@ -194,16 +200,120 @@ __global__ void __launch_bounds__(kSelectWarps * 32) router_select_kernel(
 // ---------------------------------------------------------------------------
 // Permutation.  Output order is (expert, token): each expert owns a
 // contiguous segment of permuted rows that starts on a multiple of 128 (the
-// GEMM tile height and the scale-factor atom height), and within a segment
-// rows follow token order.  The order is fully deterministic.
-//   hist    : per chunk of kChunkTok tokens, tokens routed to each expert
-//   scan    : per-expert totals, chunk bases, 128-aligned segment offsets,
-//             padding rows marked -1, GEMM tile lists
-//   scatter : row of every (token, pick), token of every row, and the
-//             dispatch of x into the permuted activation buffer (NVFP4
-//             quantised with the expert's gate input_scale, or BF16 copied)
+// GEMM tile height and the scale-factor atom height); inside a segment rows
+// follow token order.  The order is fully deterministic.
+// Small batches (T * K <= kSmallPairs) run in one CTA; large batches use
+// per-chunk histograms, a scan and a per-chunk scatter.
 // ---------------------------------------------------------------------------
 constexpr int kChunkTok = 128;
+constexpr int kSmallPairs = 2048;
+
+// Segment offsets, padding rows, GEMM tile lists and meta from per-expert
+// counts in shared memory (s_cnt [E]); s_off and s_mt get [E + 1] entries.
+// Whole CTA; ends with the CTA synchronised.
+__device__ void build_segments(const int32_t* s_cnt, int32_t* s_off, int32_t* s_mt, int E, int nb_gu, int nb_down,
+                               int32_t* __restrict__ counts, int32_t* __restrict__ seg_off,
+                               int32_t* __restrict__ row_token, NfTile* __restrict__ tiles_gu,
+                               NfTile* __restrict__ tiles_down, int32_t* __restrict__ meta) {
+    // exclusive scans of padded rows and m-tiles (warp 0, 32 experts a pass)
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        int32_t base_off = 0, base_mt = 0;
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            const int32_t m = e < E ? (s_cnt[e] + 127) / 128 : 0;
+            int32_t inc = m;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int32_t v = __shfl_up_sync(0xffffffffu, inc, d);
+                if (lane >= d) inc += v;
+            }
+            if (e < E) {
+                s_mt[e] = base_mt + inc - m;
+                s_off[e] = (base_mt + inc - m) * 128;
+            }
+            base_mt += __shfl_sync(0xffffffffu, inc, 31);
+        }
+        base_off = base_mt * 128;
+        if (lane == 0) {
+            s_mt[E] = base_mt;
+            s_off[E] = base_off;
+            meta[0] = base_off;
+            meta[1] = base_mt * nb_gu;
+            meta[2] = base_mt * nb_down;
+            meta[3] = base_mt;
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) {
+        seg_off[e] = s_off[e];
+        if (e < E) counts[e] = s_cnt[e];
+    }
+    // padding rows (at most 127 per expert)
+    for (int i = threadIdx.x; i < E * 128; i += blockDim.x) {
+        const int e = i >> 7, j = i & 127;
+        const int32_t r = s_off[e] + s_cnt[e] + j;
+        if (r < s_off[e + 1]) row_token[r] = -1;
+    }
+    // tile lists, ordered (expert, n_block, m_tile): CTAs that run at the same
+    // time share the weight block through L2
+    const int32_t mt_total = s_mt[E];
+    for (int pass = 0; pass < 2; ++pass) {
+        const int nb = pass == 0 ? nb_gu : nb_down;
+        NfTile* tiles = pass == 0 ? tiles_gu : tiles_down;
+        for (int32_t i = threadIdx.x; i < mt_total * nb; i += blockDim.x) {
+            const int32_t mi = i / nb;  // any tile of m-tile group mi's expert
+            int lo = 0, hi = E - 1;     // expert e with s_mt[e] <= mi < s_mt[e + 1]
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (s_mt[mid] <= mi) lo = mid;
+                else hi = mid - 1;
+            }
+            const int e = lo;
+            const int32_t mtiles = s_mt[e + 1] - s_mt[e];
+            const int32_t local = i - s_mt[e] * nb;
+            const int n = local / mtiles, m = local % mtiles;
+            NfTile t;
+            t.expert = e;
+            t.row0 = s_off[e] + m * 128;
+            t.n_block = n;
+            t.m_valid = min(128, s_cnt[e] - m * 128);
+            tiles[i] = t;
+        }
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
+                                                             int nb_gu, int nb_down, int32_t* __restrict__ counts,
+                                                             int32_t* __restrict__ seg_off,
+                                                             int32_t* __restrict__ pair_row,
+                                                             int32_t* __restrict__ row_token,
+                                                             NfTile* __restrict__ tiles_gu,
+                                                             NfTile* __restrict__ tiles_down,
+                                                             int32_t* __restrict__ meta) {
+    extern __shared__ int32_t sh[];
+    int32_t* s_cnt = sh;
+    int32_t* s_off = s_cnt + E;
+    int32_t* s_mt = s_off + E + 1;
+    int32_t* s_idx = s_mt + E + 1;  // [T * K]
+    const int n = T * K;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s_idx[i] = idx[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&s_cnt[s_idx[i]], 1);
+    __syncthreads();
+    build_segments(s_cnt, s_off, s_mt, E, nb_gu, nb_down, counts, seg_off, row_token, tiles_gu, tiles_down, meta);
+    // rank of (t, p) in its expert = picks of that expert by earlier tokens
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = s_idx[i], t = i / K;
+        int rank = 0;
+        for (int j = 0; j < t * K; ++j) rank += s_idx[j] == e ? 1 : 0;
+        const int32_t row = s_off[e] + rank;
+        pair_row[i] = row;
+        row_token[row] = t;
+    }
+}
 
 __global__ void permute_hist_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
                                     int32_t* __restrict__ chunk_counts) {
@@ -222,13 +332,14 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __res
                                                             int32_t* __restrict__ chunk_base,
                                                             int32_t* __restrict__ counts,
                                                             int32_t* __restrict__ seg_off,
-                                                            int32_t* __restrict__ row_token, NfTile* __restrict__ tiles_gu,
+                                                            int32_t* __restrict__ row_token,
+                                                            NfTile* __restrict__ tiles_gu,
                                                             NfTile* __restrict__ tiles_down,
                                                             int32_t* __restrict__ meta) {
     extern __shared__ int32_t sh[];
-    int32_t* s_cnt = sh;             // [E]
-    int32_t* s_off = sh + E;         // [E + 1]
-    int32_t* s_mt = sh + 2 * E + 1;  // [E + 1] m-tile prefix
+    int32_t* s_cnt = sh;
+    int32_t* s_off = s_cnt + E;
+    int32_t* s_mt = s_off + E + 1;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         int32_t run = 0;
         for (int c = 0; c < nchunks; ++c) {
@@ -236,83 +347,33 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __res
             run += chunk_counts[static_cast<int64_t>(c) * E + e];
         }
         s_cnt[e] = run;
-        counts[e] = run;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int32_t off = 0, mt = 0;
-        for (int e = 0; e < E; ++e) {
-            s_off[e] = off;
-            s_mt[e] = mt;
-            const int32_t m = (s_cnt[e] + 127) / 128;
-            off += m * 128;
-            mt += m;
-        }
-        s_off[E] = off;
-        s_mt[E] = mt;
-        meta[0] = off;             // rows in use
-        meta[1] = mt * nb_gu;      // gate/up tiles
-        meta[2] = mt * nb_down;    // down tiles
-        meta[3] = mt;              // m-tiles
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e <= E; e += blockDim.x) seg_off[e] = s_off[e];
-    // padding rows of every segment
-    for (int e = 0; e < E; ++e) {
-        const int32_t beg = s_off[e] + s_cnt[e], end = s_off[e + 1];
-        for (int r = beg + threadIdx.x; r < end; r += blockDim.x) row_token[r] = -1;
-    }
-    // tile lists, ordered (expert, n_block, m_tile) so that CTAs working at
-    // the same time share the weight block through L2
-    for (int e = 0; e < E; ++e) {
-        const int32_t mtiles = s_mt[e + 1] - s_mt[e];
-        if (mtiles == 0) continue;
-        const int32_t base_gu = s_mt[e] * nb_gu, base_dn = s_mt[e] * nb_down;
-        for (int i = threadIdx.x; i < mtiles * nb_gu; i += blockDim.x) {
-            const int n = i / mtiles, m = i % mtiles;
-            NfTile t;
-            t.expert = e;
-            t.row0 = s_off[e] + m * 128;
-            t.n_block = n;
-            t.m_valid = min(128, s_cnt[e] - m * 128);
-            tiles_gu[base_gu + i] = t;
-        }
-        for (int i = threadIdx.x; i < mtiles * nb_down; i += blockDim.x) {
-            const int n = i / mtiles, m = i % mtiles;
-            NfTile t;
-            t.expert = e;
-            t.row0 = s_off[e] + m * 128;
-            t.n_block = n;
-            t.m_valid = min(128, s_cnt[e] - m * 128);
-            tiles_down[base_dn + i] = t;
-        }
-    }
+    build_segments(s_cnt, s_off, s_mt, E, nb_gu, nb_down, counts, seg_off, row_token, tiles_gu, tiles_down, meta);
 }
 
-// One CTA per chunk of kChunkTok tokens, 256 threads.
-__global__ void __launch_bounds__(256) permute_scatter_kernel(
-    const int32_t* __restrict__ idx, const uint16_t* __restrict__ x, int T, int K, int E, int H,
-    const int32_t* __restrict__ chunk_base, const int32_t* __restrict__ seg_off,
-    const float* __restrict__ gscale,  // [E] 1 / gate input_scale (NVFP4 mode)
-    int bf16_mode, int32_t* __restrict__ pair_row, int32_t* __restrict__ row_token, uint8_t* __restrict__ a_codes,
-    uint8_t* __restrict__ a_sf, uint16_t* __restrict__ a_bf16) {
+// Rows of a chunk of kChunkTok tokens: one warp ranks the picks in token
+// order (rounds of 32 tokens), then the CTA writes pair_row / row_token.
+__global__ void __launch_bounds__(256) permute_rows_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
+                                                           const int32_t* __restrict__ chunk_base,
+                                                           const int32_t* __restrict__ seg_off,
+                                                           int32_t* __restrict__ pair_row,
+                                                           int32_t* __restrict__ row_token) {
     extern __shared__ int32_t sh[];
-    int32_t* s_run = sh;                        // [E] running count inside the chunk
-    int32_t* s_rows = sh + E;                   // [kChunkTok * K] permuted row of each pick
-    int32_t* s_pe = s_rows + kChunkTok * K;     // [kChunkTok * K] expert of each pick
+    int32_t* s_run = sh;                     // [E]
+    int32_t* s_rows = sh + E;                // [kChunkTok * K]
+    int32_t* s_pe = s_rows + kChunkTok * K;  // [kChunkTok * K]
     const int t0 = blockIdx.x * kChunkTok;
     const int nt = min(kChunkTok, T - t0);
     for (int e = threadIdx.x; e < E; e += blockDim.x) s_run[e] = 0;
     for (int i = threadIdx.x; i < nt * K; i += blockDim.x) s_pe[i] = idx[static_cast<int64_t>(t0) * K + i];
     __syncthreads();
-    // ranks inside the chunk, in token order (one warp, rounds of 32 tokens)
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         for (int r0 = 0; r0 < nt; r0 += 32) {
             const int tl = r0 + lane;
-            const bool valid = tl < nt;
             const int lanes = min(32, nt - r0);
-            if (valid) {
+            if (tl < nt) {
                 for (int p = 0; p < K; ++p) {
                     const int e = s_pe[tl * K + p];
                     int rank = 0;
@@ -334,58 +395,93 @@ __global__ void __launch_bounds__(256) permute_scatter_kernel(
         pair_row[static_cast<int64_t>(t0) * K + i] = row;
         row_token[row] = t0 + i / K;
     }
-    // dispatch: one warp per token
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int groups = H / 16;
-    for (int tl = warp; tl < nt; tl += 8) {
-        const int t = t0 + tl;
-        const uint16_t* xr = x + static_cast<int64_t>(t) * H;
-        if (bf16_mode) {
-            for (int p = 0; p < K; ++p) {
-                const int row = s_rows[tl * K + p];
-                const uint4* src = reinterpret_cast<const uint4*>(xr);
-                uint4* dst = reinterpret_cast<uint4*>(a_bf16 + static_cast<int64_t>(row) * H);
-                for (int v = lane; v < H / 8; v += 32) dst[v] = src[v];
-            }
-            continue;
+}
+
+// ---------------------------------------------------------------------------
+// Dispatch: x rows into the permuted activation buffer.  NVFP4 experts: the
+// row of pick (t, p) is x[t] quantised with the gate input_scale of expert
+// idx[t, p] (quant_dequant_nvfp4_activation, src/text_forward.cpp:527-550),
+// stored as E2M1 codes plus E4M3 scales in the tcgen05 atom layout; one
+// quantisation serves every pick whose expert has the same scale.  BF16
+// experts: plain row copies.  One thread per (token, 64 columns): the 32
+// lanes of a warp write 1 KB of contiguous codes.
+// ---------------------------------------------------------------------------
+__global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ idx,
+                                const int32_t* __restrict__ pair_row, const float* __restrict__ gscale, int T, int K,
+                                int H, int bf16_mode, uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
+                                uint16_t* __restrict__ a_bf16) {
+    const int gq = H / 64;
+    const int64_t item = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (item >= static_cast<int64_t>(T) * gq) return;
+    const int t = static_cast<int>(item / gq), q = static_cast<int>(item % gq);
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * H + q * 64);
+    uint4 raw[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) raw[i] = __ldg(src + i);
+    if (bf16_mode) {
+        for (int p = 0; p < K; ++p) {
+            const int row = pair_row[static_cast<int64_t>(t) * K + p];
+            uint4* dst = reinterpret_cast<uint4*>(a_bf16 + static_cast<int64_t>(row) * H + q * 64);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = raw[i];
         }
-        // each lane quantises 4 consecutive groups (64 elements) per pass;
-        // one quantisation serves every pick whose expert shares the scale
-        for (int g0 = lane * 4; g0 < groups; g0 += 128) {
-            float v[4][16];
+        return;
+    }
+    float v[4][16];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint4* src = reinterpret_cast<const uint4*>(xr + (g0 + j) * 16);
-                const uint4 q0 = src[0], q1 = src[1];
-                const uint32_t u[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t u[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    v[j][2 * i] = __uint_as_float((u[i] & 0xffffu) << 16);
-                    v[j][2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
-                }
-            }
-            float cur_gs = 0.f;
-            bool have = false;
-            uint32_t codes[4][2];
-            uint32_t sfw = 0u;
-            for (int p = 0; p < K; ++p) {
-                const int e = s_pe[tl * K + p];
-                const int row = s_rows[tl * K + p];
-                const float gs = gscale[e];
-                if (!have || gs != cur_gs) {
-                    sfw = 0u;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) sfw |= quantize_group16(v[j], gs, codes[j]) << (8 * j);
-                    cur_gs = gs;
-                    have = true;
-                }
-                uint4* dst = reinterpret_cast<uint4*>(a_codes + static_cast<int64_t>(row) * (H / 2) + g0 * 8);
-                dst[0] = make_uint4(codes[0][0], codes[0][1], codes[1][0], codes[1][1]);
-                dst[1] = make_uint4(codes[2][0], codes[2][1], codes[3][0], codes[3][1]);
-                *reinterpret_cast<uint32_t*>(a_sf + sf_atom_offset(row, g0, groups)) = sfw;
-            }
+        for (int j = 0; j < 4; ++j) {
+            v[i >> 1][(i & 1) * 8 + 2 * j] = bf16_lo(u[j]);
+            v[i >> 1][(i & 1) * 8 + 2 * j + 1] = bf16_hi(u[j]);
         }
     }
+    float cur_gs = 0.f;
+    bool have = false;
+    uint32_t codes[4][2];
+    uint32_t sfw = 0u;
+    for (int p = 0; p < K; ++p) {
+        const int e = idx[static_cast<int64_t>(t) * K + p];
+        const int row = pair_row[static_cast<int64_t>(t) * K + p];
+        const float gs = gscale[e];
+        if (!have || gs != cur_gs) {
+            sfw = 0u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sfw |= quantize_group16_fast<true>(v[j], gs, codes[j]) << (8 * j);
+            cur_gs = gs;
+            have = true;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(a_codes + static_cast<int64_t>(row) * (H / 2) + q * 32);
+        dst[0] = make_uint4(codes[0][0], codes[0][1], codes[1][0], codes[1][1]);
+        dst[1] = make_uint4(codes[2][0], codes[2][1], codes[3][0], codes[3][1]);
+        *reinterpret_cast<uint32_t*>(a_sf + sf_atom_offset(row, q * 4, H / 16)) = sfw;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Self-check of the hardware format conversions against the reference's
+// rules over every 32-bit pattern: E2M1 (cast_to_e2m1 after the +-6 clamp)
+// and E4M3 on [2^-6, inf) (f32_to_e4m3 after the 448 clamp).
+// ---------------------------------------------------------------------------
+__global__ void format_selfcheck_kernel(unsigned long long* __restrict__ mismatches) {
+    unsigned long long bad_e2m1 = 0, bad_e4m3 = 0;
+    for (uint64_t b = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; b < (1ull << 32);
+         b += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const float x = __uint_as_float(static_cast<uint32_t>(b));
+        if (isnan(x)) continue;
+        const float c = x > 6.f ? 6.f : (x < -6.f ? -6.f : x);
+        const uint32_t want = e2m1_code(c);
+        if ((e2m1x2_hw(c, 0.f) & 0xfu) != want || (e2m1x2_hw(x, 0.f) & 0xfu) != want) ++bad_e2m1;
+        if ((e2m1x2_hw(0.f, c) >> 4) != want) ++bad_e2m1;
+        if (x >= 0.015625f) {
+            const float m = x > 448.f ? 448.f : x;
+            const uint32_t w8 = f32_to_e4m3(m);
+            if (e4m3_hw(m) != w8 || e4m3_hw(x) != w8) ++bad_e4m3;
+        }
+    }
+    atomicAdd(&mismatches[0], bad_e2m1);
+    atomicAdd(&mismatches[1], bad_e4m3);
 }
 
 // ---------------------------------------------------------------------------
@@ -477,7 +573,7 @@ __global__ void quantize_kernel(const float* __restrict__ x, int64_t rows, int64
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = x[g * 16 + i];
         uint32_t c[2];
-        const uint32_t sc = quantize_group16(v, gscale, c);
+        const uint32_t sc = quantize_group16_fast<false>(v, gscale, c);
         reinterpret_cast<uint2*>(codes)[g] = make_uint2(c[0], c[1]);
         scales[g] = static_cast<uint8_t>(sc);
         if (fake) {
@@ -498,15 +594,12 @@ __global__ void quantize_kernel(const float* __restrict__ x, int64_t rows, int64
 cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H, int E, int K,
                           float scaling, int normalize, int n_group, int topk_group, float* logits, int32_t* idx,
                           float* wts, cudaStream_t st) {
-    const size_t smem = static_cast<size_t>(kRouterTok) * H * sizeof(uint16_t);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(200 * 1024));
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
-    router_logits_kernel<<<(T + kRouterTok - 1) / kRouterTok, 256, smem, st>>>(x, w, T, H, E, logits);
+    const int64_t items = static_cast<int64_t>((T + 1) / 2) * E;
+    // small batches: one warp per CTA, spread over every SM (the chain
+    // latency is the bound); large batches: 128 threads per CTA
+    const int threads = items <= 148 * 64 ? 32 : 128;
+    router_logits_kernel<<<static_cast<unsigned>((items + threads - 1) / threads), threads, 0, st>>>(x, w, T, H, E,
+                                                                                                     logits);
     router_select_kernel<<<(T + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32,
                            kSelectWarps * 2 * E * sizeof(float), st>>>(logits, bias, T, E, K, scaling, normalize,
                                                                       n_group, topk_group, idx, wts);
@@ -515,15 +608,28 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* bia
 
 cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
                            const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st) {
-    const int nchunks = (T + kChunkTok - 1) / kChunkTok;
-    permute_hist_kernel<<<nchunks, 256, E * sizeof(int32_t), st>>>(idx, T, K, E, b.chunk_counts);
-    permute_scan_kernel<<<1, 1024, (3 * E + 2) * sizeof(int32_t), st>>>(b.chunk_counts, nchunks, E, nb_gu, nb_down,
-                                                                       b.chunk_base, b.counts, b.seg_off, b.row_token,
-                                                                       b.tiles_gu, b.tiles_down, b.meta);
-    const size_t smem = (E + 2 * kChunkTok * K) * sizeof(int32_t);
-    permute_scatter_kernel<<<nchunks, 256, smem, st>>>(idx, x, T, K, E, H, b.chunk_base, b.seg_off, gscale,
-                                                       bf16_mode, b.pair_row, b.row_token, b.a_codes, b.a_sf,
-                                                       b.a_bf16);
+    if (T * K <= kSmallPairs) {
+        const size_t smem = (3 * E + 2 + T * K) * sizeof(int32_t);
+        permute_small_kernel<<<1, 1024, smem, st>>>(idx, T, K, E, nb_gu, nb_down, b.counts, b.seg_off, b.pair_row,
+                                                    b.row_token, b.tiles_gu, b.tiles_down, b.meta);
+    } else {
+        const int nchunks = (T + kChunkTok - 1) / kChunkTok;
+        permute_hist_kernel<<<nchunks, 256, E * sizeof(int32_t), st>>>(idx, T, K, E, b.chunk_counts);
+        permute_scan_kernel<<<1, 1024, (3 * E + 2) * sizeof(int32_t), st>>>(b.chunk_counts, nchunks, E, nb_gu, nb_down,
+                                                                           b.chunk_base, b.counts, b.seg_off,
+                                                                           b.row_token, b.tiles_gu, b.tiles_down,
+                                                                           b.meta);
+        permute_rows_kernel<<<nchunks, 256, (E + 2 * kChunkTok * K) * sizeof(int32_t), st>>>(
+            idx, T, K, E, b.chunk_base, b.seg_off, b.pair_row, b.row_token);
+    }
+    const int64_t items = static_cast<int64_t>(T) * (H / 64);
+    dispatch_kernel<<<static_cast<unsigned>((items + 127) / 128), 128, 0, st>>>(
+        x, idx, b.pair_row, gscale, T, K, H, bf16_mode, b.a_codes, b.a_sf, b.a_bf16);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_format_selfcheck(unsigned long long* mismatches_dev, cudaStream_t st) {
+    format_selfcheck_kernel<<<148 * 8, 256, 0, st>>>(mismatches_dev);
     return cudaGetLastError();
 }
 

@@ -250,6 +250,10 @@ int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
         return reject(NF_ERR_UNSUPPORTED, "this library is built for sm_100a (B200)");
     }
 
+    if (prepare_device_tables() != cudaSuccess) {
+        cudaSetDevice(prev);
+        return reject(NF_ERR_CUDA, "could not build the router's device tables");
+    }
     nf_moe* h = new nf_moe();
     h->d = d;
     h->device = device;
@@ -777,7 +781,23 @@ int nf_nvfp4_quantize(const float* x, int64_t rows, int64_t cols, float in_scale
 int nf_sigmoid_ref(const float* x, int64_t n, float* y, void* stream) {
     if (n < 0 || (n > 0 && (!x || !y))) return NF_ERR_INVALID;
     if (n == 0) return NF_OK;
+    if (prepare_device_tables() != cudaSuccess) return NF_ERR_CUDA;
     return launch_sigmoid_ref(x, n, y, static_cast<cudaStream_t>(stream)) == cudaSuccess ? NF_OK : NF_ERR_CUDA;
+}
+
+int nf_format_selfcheck(int64_t* e2m1_mismatches, int64_t* e4m3_mismatches) {
+    if (!e2m1_mismatches || !e4m3_mismatches) return NF_ERR_INVALID;
+    unsigned long long* d = nullptr;
+    if (cudaMalloc(&d, 2 * sizeof(unsigned long long)) != cudaSuccess) return NF_ERR_NOMEM;
+    unsigned long long h[2] = {0, 0};
+    cudaError_t e = cudaMemset(d, 0, sizeof(h));
+    if (e == cudaSuccess) e = launch_format_selfcheck(d, nullptr);
+    if (e == cudaSuccess) e = cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (e != cudaSuccess) return NF_ERR_CUDA;
+    *e2m1_mismatches = static_cast<int64_t>(h[0]);
+    *e4m3_mismatches = static_cast<int64_t>(h[1]);
+    return NF_OK;
 }
 
 }  // extern "C"

@@ -38,7 +38,7 @@ EXPORTED = [
     "nf_moe_create", "nf_moe_destroy", "nf_moe_last_error", "nf_status_string", "nf_moe_bind_nvfp4",
     "nf_moe_bind_bf16", "nf_moe_bind_f32", "nf_moe_finalize", "nf_moe_forward", "nf_moe_forward_host",
     "nf_moe_sync", "nf_moe_route", "nf_moe_debug_tensor", "nf_moe_debug_read", "nf_nvfp4_dequantize", "nf_nvfp4_quantize",
-    "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times",
+    "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck",
 ]
 STAGES = ["router", "permute", "gate_up", "down", "shared", "combine"]
 
@@ -83,6 +83,7 @@ def load() -> ctypes.CDLL:
         "nf_nvfp4_quantize": ([P, I64, I64, F, P, P, P, P], I32),
         "nf_sigmoid_ref": ([P, I64, P, P], I32),
         "nf_moe_profile": ([P, I32], I32),
+        "nf_format_selfcheck": ([ctypes.POINTER(I64), ctypes.POINTER(I64)], I32),
         "nf_moe_stage_times": ([P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(I32)], I32),
     }
     for name, (args, res) in sig.items():
@@ -273,6 +274,16 @@ def quantize(x_dev, rows: int, cols: int, input_scale: float, codes_dev, scales_
 
 def sigmoid_ref(x_dev, n: int, y_dev, stream=0) -> int:
     return load().nf_sigmoid_ref(_ptr(x_dev), n, _ptr(y_dev), stream or None)
+
+
+def format_selfcheck() -> tuple[int, int]:
+    """(E2M1, E4M3) mismatch counts of the hardware conversions against the
+    reference encoders over every 32-bit pattern (current device)."""
+    a, b = ctypes.c_int64(), ctypes.c_int64()
+    st = load().nf_format_selfcheck(ctypes.byref(a), ctypes.byref(b))
+    if st != NF_OK:
+        raise NfError(st, "format self-check failed to run")
+    return a.value, b.value
 
 
 def sf_atom_offset(row: np.ndarray, kgroup: np.ndarray, kgroups_total: int) -> np.ndarray:
