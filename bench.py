@@ -350,6 +350,35 @@ def run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src) -> dict:
     }
 
 
+def run_decode_only(args, m, torch) -> dict:
+    """The decode batch alone: warm-up, `steps` timed forwards, stage times."""
+    lay, x_bits = wl.config_layer("c1")
+    T, H, K = x_bits.shape[0], lay.hidden, lay.top_k
+    layer = m.MoeLayer(H, lay.experts, K, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                       swiglu_limit=lay.swiglu_limit, max_tokens=T)
+    layer.bind_layer(lay)
+    x = torch.from_numpy(x_bits.view(np.int16)).cuda()
+    y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(args.warmup):
+        layer.forward(x, y, T, stream=stream)
+    torch.cuda.synchronize()
+    layer.profile(True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        layer.forward(x, y, T, stream=stream)
+    ev1.record()
+    torch.cuda.synchronize()
+    stages, nfw = layer.stage_times()
+    layer.profile(False)
+    layer.sync(stream)
+    layer.close()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    return {"workload": "c1 decode", "ms_per_step": ms, "tokens_per_s": T / (ms * 1e-3),
+            "stages_us": {k: 1e3 * v / max(nfw, 1) for k, v in stages.items()}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -357,9 +386,23 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true", help="skip the secondary prefill measurement")
+    ap.add_argument("--only", choices=["decode", "prefill"],
+                    help="time one workload alone (no e2e, CPU baseline or clock sampling); for profilers")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_env()
+    if args.only:
+        import torch
+
+        m = load_module("nf_moe", PKG / "nf_moe.py")
+        torch.cuda.set_device(local)
+        if args.only == "decode":
+            out = run_decode_only(args, m, torch)
+        else:
+            _, bf16_peak, peak_src = peaks()
+            out = run_prefill(args, m, torch, 4 * bf16_peak, bf16_peak, peak_src)
+        print(json.dumps(out), flush=True)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
     else:

@@ -211,11 +211,12 @@ NF_API int nf_nvfp4_quantize(const float* x_dev, int64_t rows, int64_t cols, flo
  * libm expf), element-wise over n floats. */
 NF_API int nf_sigmoid_ref(const float* x_dev, int64_t n, float* y_dev, void* stream);
 /* Checks, on the current device and over every 32-bit pattern, that the
- * hardware E2M1 and E4M3 conversions the quantisers use agree with the
+ * hardware E2M1, E4M3 and BF16 conversions the kernels use agree with the
  * reference's encoders (cast_to_e2m1, src/text_forward.cpp:510-522, after
- * the +-6 clamp; f32_to_e4m3, :60-85, on [2^-6, inf) after the 448 clamp).
- * Returns the mismatch counts (both 0 on a correct build).  Synchronous. */
-NF_API int nf_format_selfcheck(int64_t* e2m1_mismatches, int64_t* e4m3_mismatches);
+ * the +-6 clamp; f32_to_e4m3, :60-85, on [2^-6, inf) after the 448 clamp;
+ * f32_to_bf16, :87-95, on every non-NaN input).  Returns the mismatch
+ * counts (all 0 on a correct build).  Synchronous. */
+NF_API int nf_format_selfcheck(int64_t* e2m1_mismatches, int64_t* e4m3_mismatches, int64_t* bf16_mismatches);
 
 #ifdef __cplusplus
 }

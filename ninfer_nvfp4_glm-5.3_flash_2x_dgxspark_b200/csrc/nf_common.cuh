@@ -44,6 +44,21 @@ NF_DEV float bf16_round(float v) {
     return __uint_as_float(b & 0xffff0000u);
 }
 NF_DEV float bf16_bits_to_f32(uint16_t bits) { return __uint_as_float(static_cast<uint32_t>(bits) << 16); }
+
+// f32 -> bf16 -> f32 by the hardware conversion (round to nearest even).
+// Same as bf16_round for every non-NaN input (checked over all 2^32 inputs
+// by nf_format_selfcheck); NaN inputs give the canonical NaN.
+NF_DEV float bf16_round_hw(float v) {
+    uint16_t b;
+    asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(b) : "f"(v));
+    return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+// Two values at once, packed (low half = `lo`).
+NF_DEV uint32_t bf16x2_hw(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
 NF_DEV uint16_t f32_to_bf16_bits(float v) { return static_cast<uint16_t>(__float_as_uint(bf16_round(v)) >> 16); }
 
 // E4M3FN decode (src/nvfp4_decode.cpp:42-54); exact.
@@ -170,7 +185,9 @@ NF_DEV uint32_t quantize_group16_fast(const float (&x)[16], float global_scale, 
     bool nan = false;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-        r[i] = kBf16Input ? x[i] : bf16_round(x[i]);
+        // the hardware rounding equals bf16_round for every non-NaN input,
+        // and a NaN sends the whole group to the reference-rule path
+        r[i] = kBf16Input ? x[i] : bf16_round_hw(x[i]);
         nan |= isnan(r[i]);
         const float a = fabsf(r[i]);
         peak = (peak < a) ? a : peak;
@@ -228,19 +245,38 @@ NF_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that may suspend the thread until the phase completes, for at
+// most `hint_ns` (the hardware wakes it earlier when the phase completes),
+// so a waiting warp does not spin on issue slots the working warps need.
+NF_DEV bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with `parity`.  Gives up (returns false) when
 // the budget runs out or when another role of the CTA (abort flag in shared
 // memory) or another CTA (error word in global memory) has given up.
 NF_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* cta_abort, volatile int* dev_err) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = globaltimer_ns();
-    for (uint32_t spin = 1;; ++spin) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((spin & 63u) == 0u) {
-            if (*cta_abort != 0 || *dev_err != 0) return false;
-            if (globaltimer_ns() - start > NF_WAIT_BUDGET_NS) return false;
-        }
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+        if (*cta_abort != 0 || *dev_err != 0) return false;
+        if (globaltimer_ns() - start > NF_WAIT_BUDGET_NS) return false;
     }
+}
+
+// Named barrier over `threads` threads (a multiple of 32) with id `id` (1-15;
+// id 0 is __syncthreads).
+NF_DEV void named_bar_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // ---------------------------------------------------------------------------

@@ -17,7 +17,10 @@
 // issuer, warps 2-17 epilogue (TMEM lane quadrant = warp % 4, four column
 // slices per quadrant).
 // The persistent grid walks a device-side tile list, so the launch needs no
-// host synchronisation after routing.
+// host synchronisation after routing: the producer claims tiles in list
+// order with an atomic counter and publishes each to the MMA and epilogue
+// warps through a small mbarrier-guarded queue, so CTAs that start late
+// (their SM still busy with another kernel) simply take fewer tiles.
 // Every wait is bounded (nf_common.cuh mbar_wait); on a timeout the kernel
 // records an error code, stops every role, drains and frees TMEM.
 #include "nf_common.cuh"
@@ -29,6 +32,7 @@ namespace nf {
 
 constexpr int BM = 128, BN = 256, STAGES = 4;
 constexpr int kEpiWarps = 16;
+constexpr int kTileQ = 4;  // depth of the producer -> consumer tile queue
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int A_STAGE_BYTES = BM * 128;
 constexpr int B_STAGE_BYTES = BN * 128;
@@ -94,7 +98,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* acc_full = empty + STAGES;
     uint64_t* acc_empty = acc_full + 1;
     uint64_t* drain = acc_empty + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* tq_full = drain + 1;          // tile queue: slot published
+    uint64_t* tq_empty = tq_full + kTileQ;  // tile queue: slot read by every consumer
+    int* tileq = reinterpret_cast<int*>(tq_empty + kTileQ);
+    volatile int* epi_mail = tileq + kTileQ;  // [2 slots][tile, ok]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(epi_mail) + 4);
     volatile int* cta_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* dev_err = args.err;
 
@@ -103,6 +111,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < kTileQ; ++s) {
+            mbar_init(&tq_full[s], 1);
+            mbar_init(&tq_empty[s], 2);  // the MMA thread and the epilogue leader
         }
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, kEpiWarps);
@@ -134,7 +146,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool issued[STAGES];
             for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
             bool ok = true;
-            for (int i = blockIdx.x; ok && i < num_tiles; i += gridDim.x) {
+            int qslot = 0;
+            uint32_t qphase = 0;
+            while (ok) {
+                // claim the next tile of the list and publish it to the MMA
+                // and epilogue warps (-1 ends the CTA's work)
+                int i = atomicAdd(args.tile_counter, 1);
+                if (i >= num_tiles) i = -1;
+                if (!mbar_wait(&tq_empty[qslot], qphase ^ 1u, cta_abort, dev_err)) {
+                    set_abort(cta_abort, args.err, NF_DEVERR_WAIT_EMPTY);
+                    ok = false;
+                    break;
+                }
+                tileq[qslot] = i;
+                mbar_arrive(&tq_full[qslot]);
+                if (++qslot == kTileQ) qslot = 0, qphase ^= 1u;
+                if (i < 0) break;
                 const TileInfo t = get_tile(args, i);
                 const int brow0 = t.expert * args.b_rows_per_expert + t.n_block * BN;
                 for (int kt = 0; kt < k_tiles; ++kt) {
@@ -188,7 +215,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0, acc_phase = 0;
             const uint32_t idesc = KIND == KIND_NVFP4 ? idesc_nvfp4(BM, BN) : idesc_bf16(BM, BN);
             bool ok = true;
-            for (int i = blockIdx.x; ok && i < num_tiles; i += gridDim.x) {
+            int qslot = 0;
+            uint32_t qphase = 0;
+            while (ok) {
+                if (!mbar_wait(&tq_full[qslot], qphase, cta_abort, dev_err)) {
+                    set_abort(cta_abort, args.err, NF_DEVERR_WAIT_ACC);
+                    ok = false;
+                    break;
+                }
+                const int i = tileq[qslot];
+                mbar_arrive(&tq_empty[qslot]);
+                if (++qslot == kTileQ) qslot = 0, qphase ^= 1u;
+                if (i < 0) break;
                 if (!mbar_wait(acc_empty, acc_phase ^ 1u, cta_abort, dev_err)) {
                     set_abort(cta_abort, args.err, NF_DEVERR_WAIT_ACC);
                     ok = false;
@@ -256,16 +294,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int cs = (warp - 2) >> 2;
         const int r = q * 32 + lane;
         const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        // One leader thread waits for the next tile and for its accumulator;
+        // the other epilogue warps sleep on a hardware named barrier instead
+        // of polling.  The leader's verdict travels through a two-slot
+        // shared-memory mailbox (a slot is rewritten only after every warp
+        // has passed the next barrier, i.e. read it).
+        const bool leader = warp == 2 && lane == 0;
         uint32_t acc_phase = 0;
-        for (int i = blockIdx.x; i < num_tiles; i += gridDim.x) {
-            const TileInfo t = get_tile(args, i);
-            int ok = 1;
-            if (lane == 0) ok = mbar_wait(acc_full, acc_phase, cta_abort, dev_err) ? 1 : 0;
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) {
-                if (lane == 0) set_abort(cta_abort, args.err, NF_DEVERR_WAIT_ACC);
-                break;
+        int qslot = 0;
+        uint32_t qphase = 0;
+        for (int iter = 0;; ++iter) {
+            if (leader) {
+                int ok = mbar_wait(&tq_full[qslot], qphase, cta_abort, dev_err) ? 1 : 0;
+                const int tile = ok ? tileq[qslot] : -1;
+                if (ok) mbar_arrive(&tq_empty[qslot]);
+                if (ok && tile >= 0) ok = mbar_wait(acc_full, acc_phase, cta_abort, dev_err) ? 1 : 0;
+                if (!ok) set_abort(cta_abort, args.err, NF_DEVERR_WAIT_ACC);
+                epi_mail[2 * (iter & 1)] = tile;
+                epi_mail[2 * (iter & 1) + 1] = ok;
             }
+            named_bar_sync(1, 32 * kEpiWarps);
+            const int tile = epi_mail[2 * (iter & 1)];
+            const int ok = epi_mail[2 * (iter & 1) + 1];
+            if (++qslot == kTileQ) qslot = 0, qphase ^= 1u;
+            if (!ok || tile < 0) break;
+            const TileInfo t = get_tile(args, tile);
             tc_fence_after();
             const int row = t.row0 + r;
             const bool valid = r < t.m_valid;
@@ -278,6 +331,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld16(tbase + 32 * cs + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
                     tmem_ld16(tbase + 128 + 32 * cs, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
                     tmem_ld16(tbase + 128 + 32 * cs + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
+                } else if (EPI == EPI_STORE_F32) {
+                    // no math: stream 16 columns at a time straight to memory
+                    uint4* d = reinterpret_cast<uint4*>(static_cast<float*>(args.out) +
+                                                        static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + 64 * cs);
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        tmem_ld16(tbase + 64 * cs + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                        tmem_wait_ld();
+                        if (valid) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) d[4 * c + j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                        }
+                    }
                 } else {
 #pragma unroll
                     for (int c = 0; c < 4; ++c)
@@ -300,10 +366,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int g = 0; g < 2; ++g) {
                     float h[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float gv = bf16_round(__fmul_rn(__uint_as_float(v[16 * g + j]), ag));
-                        const float uv = bf16_round(__fmul_rn(__uint_as_float(v[32 + 16 * g + j]), au));
-                        h[j] = swiglu_fast(gv, uv, L);
+                    for (int j = 0; j < 16; j += 2) {
+                        // linear_nvfp4 output: acc * alpha rounded to BF16 (src/text_forward.cpp:852-855)
+                        const uint32_t g2 = bf16x2_hw(__fmul_rn(__uint_as_float(v[16 * g + j]), ag),
+                                                      __fmul_rn(__uint_as_float(v[16 * g + j + 1]), ag));
+                        const uint32_t u2 = bf16x2_hw(__fmul_rn(__uint_as_float(v[32 + 16 * g + j]), au),
+                                                      __fmul_rn(__uint_as_float(v[32 + 16 * g + j + 1]), au));
+                        h[j] = swiglu_fast(__uint_as_float(g2 << 16), __uint_as_float(u2 << 16), L);
+                        h[j + 1] = swiglu_fast(__uint_as_float(g2 & 0xffff0000u), __uint_as_float(u2 & 0xffff0000u), L);
                     }
                     sc[g] = quantize_group16_fast<false>(h, gsd, cc[g]);
                 }
@@ -318,11 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float a = args.alpha0[t.expert];
                 uint32_t p[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const uint32_t lo = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[2 * j]), a));
-                    const uint32_t hi = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[2 * j + 1]), a));
-                    p[j] = lo | (hi << 16);
-                }
+                for (int j = 0; j < 32; ++j)
+                    p[j] = bf16x2_hw(__fmul_rn(__uint_as_float(v[2 * j]), a), __fmul_rn(__uint_as_float(v[2 * j + 1]), a));
                 if (valid) {
                     uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) +
                                                         static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + 64 * cs);
@@ -333,26 +400,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float L = args.limit;
                 uint32_t p[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const uint32_t lo = f32_to_bf16_bits(swiglu_fast(__uint_as_float(v[2 * j]), __uint_as_float(v[32 + 2 * j]), L));
-                    const uint32_t hi =
-                        f32_to_bf16_bits(swiglu_fast(__uint_as_float(v[2 * j + 1]), __uint_as_float(v[32 + 2 * j + 1]), L));
-                    p[j] = lo | (hi << 16);
-                }
+                for (int j = 0; j < 16; ++j)
+                    p[j] = bf16x2_hw(swiglu_fast(__uint_as_float(v[2 * j]), __uint_as_float(v[32 + 2 * j]), L),
+                                     swiglu_fast(__uint_as_float(v[2 * j + 1]), __uint_as_float(v[32 + 2 * j + 1]), L));
                 if (valid) {
                     uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) +
                                                         static_cast<int64_t>(row) * args.out_ld + t.n_block * 128 + 32 * cs);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) d[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
                 }
-            } else {  // EPI_STORE_F32
-                if (valid) {
-                    uint4* d = reinterpret_cast<uint4*>(static_cast<float*>(args.out) +
-                                                        static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + 64 * cs);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) d[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                }
-            }
+            }  // EPI_STORE_F32 stored while reading the accumulator
         }
     }
 

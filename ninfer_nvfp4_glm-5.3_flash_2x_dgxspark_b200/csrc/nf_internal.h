@@ -26,7 +26,8 @@ struct PermuteBuffers {
     int32_t* row_token;     // [rows_cap]
     NfTile* tiles_gu;       // gate/up tile list
     NfTile* tiles_down;     // down tile list
-    int32_t* meta;          // [0] rows in use, [1] gate/up tiles, [2] down tiles, [3] m-tiles
+    int32_t* meta;          // [0] rows in use, [1] gate/up tiles, [2] down tiles, [3] m-tiles,
+                            // [4] / [5] gate/up / down tile counters (reset here)
     uint8_t* a_codes;       // NVFP4 dispatch: [rows_cap, H/2]
     uint8_t* a_sf;          //                 scale atoms
     uint16_t* a_bf16;       // BF16 dispatch:  [rows_cap, H]
@@ -67,6 +68,7 @@ struct GemmArgs {
     uint8_t* out_sf;           // EPI_SWIGLU_QUANT: down-input scale atoms
     int out_kgroups;           // EPI_SWIGLU_QUANT: 16-groups per output row
     int* err;                  // device error word
+    int* tile_counter;         // tiles claimed so far (zero before the launch)
 };
 
 // Host helpers (nf_gemm.cu).
@@ -77,9 +79,11 @@ cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tmb, const Ge
 int gemm_grid_size(int device);
 
 // Launchers (nf_kernels.cu).
+// w_safe: every nonzero router weight has |w| in [2^-67, 2^63) (checked at
+// bind), which lets the exact logit chains use fused multiply-add.
 cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H, int E, int K,
-                          float scaling, int normalize, int n_group, int topk_group, float* logits, int32_t* idx,
-                          float* wts, cudaStream_t st);
+                          float scaling, int normalize, int n_group, int topk_group, int w_safe, float* logits,
+                          int32_t* idx, float* wts, int* err, cudaStream_t st);
 cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
                            const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st);
 cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair_row, const float* topk_w,

@@ -78,39 +78,132 @@ cudaError_t prepare_device_tables() {
 // ---------------------------------------------------------------------------
 // Router logits: gemv_bf16 (src/text_forward.cpp:497-508) for every token:
 // logits[t, e] = sum_c bf16(W[e, c]) * x[t, c], accumulated sequentially in
-// fp32 with a separately rounded multiply and add in column order, which is
-// what makes the result bit-identical to the reference.  One thread runs the
-// chains of one expert for two tokens with paired f32x2 instructions; the
-// chain length (H dependent adds) is the kernel's latency floor, so the
-// work is spread one chain pair per thread over as many SMs as possible.
+// fp32 in column order with the product rounded before the add, which is
+// what makes the result bit-identical to the reference.
+//
+// A CTA owns kRtExp experts x kRtTok tokens: it stages those router rows and
+// token rows in shared memory with 1-D bulk copies (row pitch padded by 16
+// bytes so the 8 rows a warp reads fall in distinct banks), then each thread
+// runs the chains of one expert for two tokens with paired f32x2
+// instructions.  A product of two BF16 values has at most 16 significant
+// bits, so it is exact in fp32 unless it leaves fp32's range; when every
+// nonzero |w| and |x| lies in [2^-67, 2^63) (router weights checked at bind,
+// token rows checked here in shared memory) the product is exact and
+// fma(w, x, acc) equals the reference's round(acc + round(w * x)).  Otherwise
+// the CTA runs the separately rounded multiply and add.  The chain of H
+// dependent adds is the latency floor.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
 
-__global__ void router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, int T, int H,
-                                     int E, float* __restrict__ logits) {
-    const int64_t item = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-    const int pairs = (T + 1) / 2;
-    if (item >= static_cast<int64_t>(pairs) * E) return;
-    const int tp = static_cast<int>(item / E), e = static_cast<int>(item % E);
-    const int t0 = 2 * tp, t1 = min(2 * tp + 1, T - 1);
-    const uint4* wr = reinterpret_cast<const uint4*>(w + static_cast<int64_t>(e) * H);
-    const uint4* xa = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0) * H);
-    const uint4* xb = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t1) * H);
-    float2 acc = make_float2(0.f, 0.f);
-    for (int c = 0; c < H / 8; ++c) {
-        const uint4 wv = __ldg(wr + c), av = __ldg(xa + c), bv = __ldg(xb + c);
-        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-        const uint32_t aa[4] = {av.x, av.y, av.z, av.w}, bb[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float w0 = bf16_lo(ww[j]), w1 = bf16_hi(ww[j]);
-            acc = __fadd2_rn(acc, __fmul2_rn(make_float2(w0, w0), make_float2(bf16_lo(aa[j]), bf16_lo(bb[j]))));
-            acc = __fadd2_rn(acc, __fmul2_rn(make_float2(w1, w1), make_float2(bf16_hi(aa[j]), bf16_hi(bb[j]))));
-        }
+constexpr int kRtExp = 8;    // experts per CTA
+constexpr int kRtTok = 16;   // tokens per CTA
+constexpr int kRtThreads = kRtExp * kRtTok / 2;
+constexpr int kRtMaxChunk = 4096;  // K elements staged at a time
+
+// true when a BF16 pair holds a value whose product with another in-range
+// BF16 value could leave fp32's exact range (nonzero |v| outside
+// [2^-67, 2^63), inf or NaN)
+__device__ __forceinline__ bool bf16x2_unsafe(uint32_t u) {
+    const uint32_t e0 = (u >> 7) & 0xffu, e1 = (u >> 23) & 0xffu;
+    const bool nz0 = (u & 0x7fffu) != 0u, nz1 = (u & 0x7fff0000u) != 0u;
+    return (nz0 && (e0 < 60u || e0 > 189u)) || (nz1 && (e1 < 60u || e1 > 189u));
+}
+
+template <bool kFma>
+__device__ __forceinline__ float2 chain_step2(uint32_t wv, uint32_t av, uint32_t bv, float2 acc) {
+    const float2 w0 = make_float2(bf16_lo(wv), bf16_lo(wv)), w1 = make_float2(bf16_hi(wv), bf16_hi(wv));
+    const float2 x0 = make_float2(bf16_lo(av), bf16_lo(bv)), x1 = make_float2(bf16_hi(av), bf16_hi(bv));
+    if (kFma) {
+        acc = __ffma2_rn(w0, x0, acc);
+        acc = __ffma2_rn(w1, x1, acc);
+    } else {
+        acc = __fadd2_rn(acc, __fmul2_rn(w0, x0));
+        acc = __fadd2_rn(acc, __fmul2_rn(w1, x1));
     }
-    logits[static_cast<int64_t>(t0) * E + e] = acc.x;
-    if (2 * tp + 1 < T) logits[static_cast<int64_t>(t1) * E + e] = acc.y;
+    return acc;
+}
+
+// Chains over n8 groups of 8 elements from shared memory; the next group's
+// three 16-byte loads are issued before the current group's 8 dependent
+// steps, so the load latency hides behind the chain.
+template <bool kFma>
+__device__ __forceinline__ float2 chain_pair(const uint4* __restrict__ wr, const uint4* __restrict__ xa,
+                                             const uint4* __restrict__ xb, int n8, float2 acc) {
+    uint4 w = wr[0], a = xa[0], b = xb[0];
+    for (int c = 0; c < n8; ++c) {
+        const int nx = c + 1 < n8 ? c + 1 : c;
+        const uint4 wn = wr[nx], an = xa[nx], bn = xb[nx];
+        acc = chain_step2<kFma>(w.x, a.x, b.x, acc);
+        acc = chain_step2<kFma>(w.y, a.y, b.y, acc);
+        acc = chain_step2<kFma>(w.z, a.z, b.z, acc);
+        acc = chain_step2<kFma>(w.w, a.w, b.w, acc);
+        w = wn;
+        a = an;
+        b = bn;
+    }
+    return acc;
+}
+
+__global__ void __launch_bounds__(kRtThreads) router_logits_kernel(const uint16_t* __restrict__ x,
+                                                                   const uint16_t* __restrict__ w, int T, int H, int E,
+                                                                   int w_safe, float* __restrict__ logits,
+                                                                   int* __restrict__ err) {
+    extern __shared__ __align__(128) uint8_t rt_smem[];
+    __shared__ uint64_t bar;
+    const int chunk = min(H, kRtMaxChunk);
+    const int pitch = chunk * 2 + 16;  // bytes
+    uint8_t* ws = rt_smem;
+    uint8_t* xs = rt_smem + kRtExp * pitch;
+    const int t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp;
+    const int nt = min(kRtTok, T - t0), ne = min(kRtExp, E - e0);
+    const int el = threadIdx.x % kRtExp, tp = threadIdx.x / kRtExp;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    float2 acc = make_float2(0.f, 0.f);
+    int ok = 1;
+    for (int k0 = 0, phase = 0; k0 < H; k0 += chunk, phase ^= 1) {
+        const int kc = min(chunk, H - k0);
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(&bar, static_cast<uint32_t>((ne + nt) * kc * 2));
+            for (int r = 0; r < ne; ++r)
+                bulk_load(ws + r * pitch, w + static_cast<int64_t>(e0 + r) * H + k0, kc * 2, &bar);
+            for (int r = 0; r < nt; ++r)
+                bulk_load(xs + r * pitch, x + static_cast<int64_t>(t0 + r) * H + k0, kc * 2, &bar);
+        }
+        // bounded wait; every thread polls the same barrier
+        const uint64_t start = globaltimer_ns();
+        while (!mbar_try_wait(&bar, static_cast<uint32_t>(phase))) {
+            if (globaltimer_ns() - start > NF_WAIT_BUDGET_NS) {
+                ok = 0;
+                break;
+            }
+        }
+        if (!__syncthreads_and(ok)) {
+            if (threadIdx.x == 0) atomicCAS(err, 0, NF_DEVERR_WAIT_FULL);
+            return;
+        }
+        // range check of the staged token rows
+        int unsafe = 0;
+        for (int i = threadIdx.x; i < nt * (kc / 2); i += blockDim.x) {
+            const int r = i / (kc / 2), c = i % (kc / 2);
+            unsafe |= bf16x2_unsafe(reinterpret_cast<const uint32_t*>(xs + r * pitch)[c]) ? 1 : 0;
+        }
+        const bool use_fma = w_safe && !__syncthreads_or(unsafe);
+        const int ta = min(2 * tp, kRtTok - 1), tb = min(2 * tp + 1, kRtTok - 1);
+        const uint4* wr = reinterpret_cast<const uint4*>(ws + el * pitch);
+        const uint4* xa = reinterpret_cast<const uint4*>(xs + ta * pitch);
+        const uint4* xb = reinterpret_cast<const uint4*>(xs + tb * pitch);
+        acc = use_fma ? chain_pair<true>(wr, xa, xb, kc / 8, acc) : chain_pair<false>(wr, xa, xb, kc / 8, acc);
+        __syncthreads();  // the next chunk overwrites the staged rows
+    }
+    if (el < ne) {
+        if (2 * tp < nt) logits[static_cast<int64_t>(t0 + 2 * tp) * E + e0 + el] = acc.x;
+        if (2 * tp + 1 < nt) logits[static_cast<int64_t>(t0 + 2 * tp + 1) * E + e0 + el] = acc.y;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -140,52 +233,86 @@ __global__ void __launch_bounds__(kSelectWarps * 32) router_select_kernel(
         score[e] = s;
         choice[e] = __fadd_rn(s, bias[e]);
     }
+    // experts excluded by the group limit (computed by lane 0, rare path)
+    __shared__ uint32_t s_excl[kSelectWarps][32];  // E <= 1024 bits
+    uint32_t* excl = s_excl[warp];
+    excl[lane] = 0u;
     __syncwarp();
-    if (lane != 0) return;
-    uint32_t used[32];  // E <= 1024
-    for (int i = 0; i < 32; ++i) used[i] = 0u;
     if (n_group > 1 && topk_group < n_group) {
-        const int per = E / n_group;
-        uint32_t keep = 0u;  // n_group <= 32
-        for (int r = 0; r < topk_group; ++r) {
-            int best = -1;
-            float best_score = 0.f;
-            for (int g = 0; g < n_group; ++g) {
-                if (keep & (1u << g)) continue;
-                float b1 = -INFINITY, b2 = -INFINITY;
-                for (int j = 0; j < per; ++j) {
-                    const float c = choice[g * per + j];
-                    if (c > b1) {
-                        b2 = b1;
-                        b1 = c;
-                    } else if (c > b2) {
-                        b2 = c;
+        if (lane == 0) {
+            const int per = E / n_group;
+            uint32_t keep = 0u;  // n_group <= 32
+            for (int r = 0; r < topk_group; ++r) {
+                int best = -1;
+                float best_score = 0.f;
+                for (int g = 0; g < n_group; ++g) {
+                    if (keep & (1u << g)) continue;
+                    float b1 = -INFINITY, b2 = -INFINITY;
+                    for (int j = 0; j < per; ++j) {
+                        const float c = choice[g * per + j];
+                        if (c > b1) {
+                            b2 = b1;
+                            b1 = c;
+                        } else if (c > b2) {
+                            b2 = c;
+                        }
+                    }
+                    const float s = per >= 2 ? __fadd_rn(b1, b2) : b1;
+                    if (best < 0 || s > best_score) {
+                        best = g;
+                        best_score = s;
                     }
                 }
-                const float s = per >= 2 ? __fadd_rn(b1, b2) : b1;
-                if (best < 0 || s > best_score) {
-                    best = g;
-                    best_score = s;
-                }
+                keep |= 1u << best;
             }
-            keep |= 1u << best;
+            for (int e = 0; e < E; ++e)
+                if (!(keep & (1u << (e / per)))) excl[e >> 5] |= 1u << (e & 31);
         }
-        for (int e = 0; e < E; ++e)
-            if (!(keep & (1u << (e / per)))) used[e >> 5] |= 1u << (e & 31);
+        __syncwarp();
+    }
+    // The reference scans from the first unused expert and moves on a strict
+    // '>' only: so a NaN first choice is kept, NaN choices are never taken
+    // otherwise, and the pick is the largest non-NaN choice with the lowest
+    // index among equals.  Lane l owns experts l, l + 32, ... and the warp
+    // reduces (first unused, best non-NaN) per pick.
+    const int jn = (E + 31) / 32;
+    uint32_t used = 0u;  // bit j: expert lane + 32 j taken or excluded
+    for (int j = 0; j < jn; ++j) {
+        const int e = lane + 32 * j;
+        if (e >= E || ((excl[e >> 5] >> (e & 31)) & 1u)) used |= 1u << j;
     }
     int picks[32];
     float wts[32];
     for (int p = 0; p < K; ++p) {
-        int best = -1;
-        for (int e = 0; e < E; ++e) {
-            if (used[e >> 5] & (1u << (e & 31))) continue;
-            if (best < 0 || choice[e] > choice[best]) best = e;
+        int first = 0x7fffffff, best = -1;
+        float bv = 0.f;
+        for (int j = 0; j < jn; ++j) {
+            if (used & (1u << j)) continue;
+            const int e = lane + 32 * j;
+            if (e < first) first = e;
+            const float c = choice[e];
+            if (!isnan(c) && (best < 0 || c > bv)) {
+                best = e;
+                bv = c;
+            }
         }
-        if (best < 0) best = 0;
-        used[best >> 5] |= 1u << (best & 31);
-        picks[p] = best;
-        wts[p] = score[best];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            first = min(first, __shfl_xor_sync(0xffffffffu, first, off));
+            const int ob = __shfl_xor_sync(0xffffffffu, best, off);
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            if (ob >= 0 && (best < 0 || ov > bv || (ov == bv && ob < best))) {
+                best = ob;
+                bv = ov;
+            }
+        }
+        int pick = 0;
+        if (first != 0x7fffffff) pick = (isnan(choice[first]) || best < 0) ? first : best;
+        if ((pick & 31) == lane) used |= 1u << (pick >> 5);
+        picks[p] = pick;
+        wts[p] = score[pick];
     }
+    if (lane != 0) return;
     if (normalize) {
         float sum = 1e-20f;
         for (int p = 0; p < K; ++p) sum = __fadd_rn(sum, wts[p]);
@@ -242,6 +369,8 @@ __device__ void build_segments(const int32_t* s_cnt, int32_t* s_off, int32_t* s_
             meta[1] = base_mt * nb_gu;
             meta[2] = base_mt * nb_down;
             meta[3] = base_mt;
+            meta[4] = 0;  // tile counters of the two grouped GEMMs
+            meta[5] = 0;
         }
     }
     __syncthreads();
@@ -461,15 +590,20 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
 
 // ---------------------------------------------------------------------------
 // Self-check of the hardware format conversions against the reference's
-// rules over every 32-bit pattern: E2M1 (cast_to_e2m1 after the +-6 clamp)
-// and E4M3 on [2^-6, inf) (f32_to_e4m3 after the 448 clamp).
+// rules over every 32-bit pattern: E2M1 (cast_to_e2m1 after the +-6 clamp),
+// E4M3 on [2^-6, inf) (f32_to_e4m3 after the 448 clamp) and BF16 rounding
+// (f32_to_bf16 on every non-NaN input).
 // ---------------------------------------------------------------------------
 __global__ void format_selfcheck_kernel(unsigned long long* __restrict__ mismatches) {
-    unsigned long long bad_e2m1 = 0, bad_e4m3 = 0;
+    unsigned long long bad_e2m1 = 0, bad_e4m3 = 0, bad_bf16 = 0;
     for (uint64_t b = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; b < (1ull << 32);
          b += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         const float x = __uint_as_float(static_cast<uint32_t>(b));
         if (isnan(x)) continue;
+        if (__float_as_uint(bf16_round_hw(x)) != __float_as_uint(bf16_round(x))) ++bad_bf16;
+        const uint32_t pair = bf16x2_hw(x, -x);
+        if ((pair << 16) != __float_as_uint(bf16_round(x)) || (pair & 0xffff0000u) != __float_as_uint(bf16_round(-x)))
+            ++bad_bf16;
         const float c = x > 6.f ? 6.f : (x < -6.f ? -6.f : x);
         const uint32_t want = e2m1_code(c);
         if ((e2m1x2_hw(c, 0.f) & 0xfu) != want || (e2m1x2_hw(x, 0.f) & 0xfu) != want) ++bad_e2m1;
@@ -482,6 +616,7 @@ __global__ void format_selfcheck_kernel(unsigned long long* __restrict__ mismatc
     }
     atomicAdd(&mismatches[0], bad_e2m1);
     atomicAdd(&mismatches[1], bad_e4m3);
+    atomicAdd(&mismatches[2], bad_bf16);
 }
 
 // ---------------------------------------------------------------------------
@@ -592,14 +727,19 @@ __global__ void quantize_kernel(const float* __restrict__ x, int64_t rows, int64
 // Launchers
 // ---------------------------------------------------------------------------
 cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H, int E, int K,
-                          float scaling, int normalize, int n_group, int topk_group, float* logits, int32_t* idx,
-                          float* wts, cudaStream_t st) {
-    const int64_t items = static_cast<int64_t>((T + 1) / 2) * E;
-    // small batches: one warp per CTA, spread over every SM (the chain
-    // latency is the bound); large batches: 128 threads per CTA
-    const int threads = items <= 148 * 64 ? 32 : 128;
-    router_logits_kernel<<<static_cast<unsigned>((items + threads - 1) / threads), threads, 0, st>>>(x, w, T, H, E,
-                                                                                                     logits);
+                          float scaling, int normalize, int n_group, int topk_group, int w_safe, float* logits,
+                          int32_t* idx, float* wts, int* err, cudaStream_t st) {
+    const int chunk = H < kRtMaxChunk ? H : kRtMaxChunk;
+    const size_t smem = static_cast<size_t>(kRtExp + kRtTok) * (chunk * 2 + 16);
+    static bool attr = false;
+    if (!attr) {
+        const cudaError_t e = cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>((kRtExp + kRtTok) * (kRtMaxChunk * 2 + 16)));
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    const dim3 grid((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp);
+    router_logits_kernel<<<grid, kRtThreads, smem, st>>>(x, w, T, H, E, w_safe, logits, err);
     router_select_kernel<<<(T + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32,
                            kSelectWarps * 2 * E * sizeof(float), st>>>(logits, bias, T, E, K, scaling, normalize,
                                                                       n_group, topk_group, idx, wts);

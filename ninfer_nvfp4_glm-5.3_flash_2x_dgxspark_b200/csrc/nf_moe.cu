@@ -32,7 +32,10 @@ struct nf_moe {
     nf_moe_desc d{};
     int device = 0;
     int grid = 148;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr;   // internal stream of the host-buffer path
+    cudaStream_t side = nullptr;     // shared expert, forked from the caller's stream
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    int* shared_counters = nullptr;  // tile counters of the two shared-expert GEMMs
     std::string err;
     bool finalized = false;
     std::vector<DevBuf> allocs;
@@ -59,6 +62,7 @@ struct nf_moe {
     std::vector<float> h_alpha_g, h_alpha_u, h_alpha_d, h_in_g, h_in_u, h_in_d;
     std::vector<uint8_t> bound;     // [E * 3] expert projection bound flags
     bool router_bound = false, bias_bound = false, sg_bound = false, su_bound = false, sd_bound = false;
+    int router_w_safe = 0;  // every nonzero router weight has |w| in [2^-67, 2^63)
 
     // workspace
     float* logits = nullptr;
@@ -81,32 +85,40 @@ struct nf_moe {
     CUtensorMap tm_a{}, tm_bgu{}, tm_h{}, tm_bdn{}, tm_sgu{}, tm_shh{}, tm_sdn{};
     int last_tokens = 0;
 
-    // per-stage event profile: a ring of event sets, folded into stage_ms
+    // per-stage event profile: a ring of event sets (a begin and an end event
+    // per stage, recorded on the stream the stage runs on), folded into
+    // stage_ms
     static constexpr int kProfSets = 64;
+    static constexpr int kEvPerSet = 2 * NF_STAGE_COUNT;
     bool profiling = false;
-    std::vector<cudaEvent_t> prof_ev;   // kProfSets * (NF_STAGE_COUNT + 1)
+    std::vector<cudaEvent_t> prof_ev;   // kProfSets * kEvPerSet
     std::vector<uint8_t> prof_used;     // set holds an unfolded forward
+    std::vector<uint8_t> prof_mask;     // stages recorded by the set
     int prof_next = 0, prof_forwards = 0;
     double stage_ms[NF_STAGE_COUNT] = {};
 
     void fold(int set) {
-        cudaEvent_t* ev = &prof_ev[static_cast<size_t>(set) * (NF_STAGE_COUNT + 1)];
-        cudaEventSynchronize(ev[NF_STAGE_COUNT]);
+        cudaEvent_t* ev = &prof_ev[static_cast<size_t>(set) * kEvPerSet];
+        const uint8_t mask = prof_mask[static_cast<size_t>(set)];
         for (int s = 0; s < NF_STAGE_COUNT; ++s) {
+            if (!(mask & (1u << s))) continue;
+            cudaEventSynchronize(ev[2 * s + 1]);
             float ms = 0.f;
-            if (cudaEventElapsedTime(&ms, ev[s], ev[s + 1]) == cudaSuccess) stage_ms[s] += ms;
+            if (cudaEventElapsedTime(&ms, ev[2 * s], ev[2 * s + 1]) == cudaSuccess) stage_ms[s] += ms;
         }
         prof_used[static_cast<size_t>(set)] = 0;
         ++prof_forwards;
     }
     // events of the set recording the current forward (nullptr when off)
-    cudaEvent_t* prof_begin() {
+    cudaEvent_t* prof_begin(int* set_out) {
         if (!profiling) return nullptr;
         const int set = prof_next;
         prof_next = (prof_next + 1) % kProfSets;
         if (prof_used[static_cast<size_t>(set)]) fold(set);
         prof_used[static_cast<size_t>(set)] = 1;
-        return &prof_ev[static_cast<size_t>(set) * (NF_STAGE_COUNT + 1)];
+        prof_mask[static_cast<size_t>(set)] = 0;
+        *set_out = set;
+        return &prof_ev[static_cast<size_t>(set) * kEvPerSet];
     }
 
     int fail(int status, const char* fmt, ...) {
@@ -209,6 +221,12 @@ void nf_moe_destroy(nf_moe* h) {
         cudaStreamSynchronize(h->stream);
         cudaStreamDestroy(h->stream);
     }
+    if (h->side) {
+        cudaStreamSynchronize(h->side);
+        cudaStreamDestroy(h->side);
+    }
+    if (h->ev_fork) cudaEventDestroy(h->ev_fork);
+    if (h->ev_join) cudaEventDestroy(h->ev_join);
     for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
     for (auto& a : h->allocs) cudaFree(a.p);
     cudaSetDevice(prev);
@@ -282,7 +300,11 @@ int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
          h->alloc(&b.chunk_base, static_cast<int64_t>(h->nchunks_cap) * E) && h->alloc(&b.counts, E) &&
          h->alloc(&b.seg_off, E + 1) && h->alloc(&b.pair_row, pairs) && h->alloc(&b.row_token, R) &&
          h->alloc(&b.tiles_gu, static_cast<int64_t>(h->mtiles_cap) * (I / 128)) &&
-         h->alloc(&b.tiles_down, static_cast<int64_t>(h->mtiles_cap) * (H / 256)) && h->alloc(&b.meta, 4);
+         h->alloc(&b.tiles_down, static_cast<int64_t>(h->mtiles_cap) * (H / 256)) && h->alloc(&b.meta, 8) &&
+         h->alloc(&h->shared_counters, 2);
+    ok = ok && cudaStreamCreateWithFlags(&h->side, cudaStreamNonBlocking) == cudaSuccess &&
+         cudaEventCreateWithFlags(&h->ev_fork, cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&h->ev_join, cudaEventDisableTiming) == cudaSuccess;
     if (fp4) {
         ok = ok && h->alloc(&b.a_codes, R * H / 2) && h->alloc(&b.a_sf, R * H / 16) && h->alloc(&h->h_codes, R * I / 2) &&
              h->alloc(&h->h_sf, R * I / 16);
@@ -397,7 +419,19 @@ int nf_moe_bind_bf16(nf_moe* h, int which, int expert, const uint16_t* data, int
     cudaError_t e = cudaSuccess;
     const size_t rb = static_cast<size_t>(cols) * 2;
     switch (which) {
-        case NF_BF16_ROUTER: e = cudaMemcpy(h->router_w, data, rows * rb, cudaMemcpyHostToDevice); h->router_bound = e == cudaSuccess; break;
+        case NF_BF16_ROUTER: {
+            e = cudaMemcpy(h->router_w, data, rows * rb, cudaMemcpyHostToDevice);
+            h->router_bound = e == cudaSuccess;
+            // products with BF16 activations stay exact in fp32 when every
+            // nonzero weight has a biased exponent in [60, 189]
+            int safe = 1;
+            for (int64_t i = 0; i < rows * cols && safe; ++i) {
+                const uint32_t v = data[i], ex = (v >> 7) & 0xffu;
+                if ((v & 0x7fffu) != 0u && (ex < 60u || ex > 189u)) safe = 0;
+            }
+            h->router_w_safe = safe;
+            break;
+        }
         case NF_BF16_SHARED_GATE:
         case NF_BF16_SHARED_UP: {
             uint16_t* base = h->ws_gu + (which == NF_BF16_SHARED_UP ? 128 : 0) * H;
@@ -515,8 +549,9 @@ int nf_moe_route(nf_moe* h, const uint16_t* x, int tokens, float* logits, int32_
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
     const cudaError_t e = launch_router(x, h->router_w, h->router_bias, tokens, d.hidden, d.experts, d.top_k,
-                                        d.routed_scaling, d.normalize, d.n_group, d.topk_group,
-                                        logits ? logits : h->logits, idx ? idx : h->topk_idx, w ? w : h->topk_w, s);
+                                        d.routed_scaling, d.normalize, d.n_group, d.topk_group, h->router_w_safe,
+                                        logits ? logits : h->logits, idx ? idx : h->topk_idx, w ? w : h->topk_w,
+                                        h->dev_err, s);
     cudaSetDevice(prev);
     return e == cudaSuccess ? NF_OK : h->cuda_fail(e, "router launch");
 }
@@ -529,18 +564,63 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     int32_t* idx = idx_user ? idx_user : h->topk_idx;
     float* w = w_user ? w_user : h->topk_w;
     h->last_tokens = T;
-    cudaEvent_t* ev = h->prof_begin();
-    auto mark = [&](int stage) {
-        if (ev) cudaEventRecord(ev[stage], s);
+    int set = -1;
+    cudaEvent_t* ev = h->prof_begin(&set);
+    auto begin = [&](int stage, cudaStream_t st) {
+        if (!ev) return;
+        cudaEventRecord(ev[2 * stage], st);
+        h->prof_mask[static_cast<size_t>(set)] |= static_cast<uint8_t>(1u << stage);
     };
-    mark(NF_STAGE_ROUTER);
-    cudaError_t e = launch_router(x, h->router_w, h->router_bias, T, H, E, K, d.routed_scaling, d.normalize, d.n_group,
-                                  d.topk_group, h->logits, idx, w, s);
+    auto end = [&](int stage, cudaStream_t st) {
+        if (ev) cudaEventRecord(ev[2 * stage + 1], st);
+    };
+    cudaError_t e = cudaSuccess;
+    // The shared expert does not depend on routing: fork it onto the side
+    // stream so it overlaps the router, the permutation and the routed GEMMs
+    // (the GEMMs' dynamic tile scheduler absorbs the SMs it holds).
+    if (Is > 0) {
+        if ((e = cudaEventRecord(h->ev_fork, s)) != cudaSuccess ||
+            (e = cudaStreamWaitEvent(h->side, h->ev_fork, 0)) != cudaSuccess)
+            return h->cuda_fail(e, "shared expert fork");
+        CUtensorMap tm_x;
+        if (!make_tmap_2d(&tm_x, x, true, H, T, 64, 128)) return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+        begin(NF_STAGE_SHARED, h->side);
+        if ((e = cudaMemsetAsync(h->shared_counters, 0, 2 * sizeof(int), h->side)) != cudaSuccess)
+            return h->cuda_fail(e, "shared expert counters");
+        GemmArgs sg{};
+        sg.err = h->dev_err;
+        sg.limit = d.swiglu_limit;
+        sg.kind = KIND_BF16;
+        sg.epi = EPI_SWIGLU_BF16;
+        sg.K = H;
+        sg.dense_rows = T;
+        sg.n_blocks = Is / 128;
+        sg.out = h->sh_h;
+        sg.out_ld = Is;
+        sg.tile_counter = h->shared_counters;
+        e = launch_gemm(tm_x, h->tm_sgu, sg, h->grid, h->side);
+        if (e != cudaSuccess) return h->cuda_fail(e, "shared gate/up GEMM launch");
+        sg.epi = EPI_STORE_F32;
+        sg.K = Is;
+        sg.n_blocks = H / 256;
+        sg.out = h->sh_out;
+        sg.out_ld = H;
+        sg.tile_counter = h->shared_counters + 1;
+        e = launch_gemm(h->tm_shh, h->tm_sdn, sg, h->grid, h->side);
+        if (e != cudaSuccess) return h->cuda_fail(e, "shared down GEMM launch");
+        end(NF_STAGE_SHARED, h->side);
+        if ((e = cudaEventRecord(h->ev_join, h->side)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
+    }
+    begin(NF_STAGE_ROUTER, s);
+    e = launch_router(x, h->router_w, h->router_bias, T, H, E, K, d.routed_scaling, d.normalize, d.n_group,
+                      d.topk_group, h->router_w_safe, h->logits, idx, w, h->dev_err, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "router launch");
-    mark(NF_STAGE_PERMUTE);
+    end(NF_STAGE_ROUTER, s);
+    begin(NF_STAGE_PERMUTE, s);
     e = launch_permute(idx, x, T, K, E, H, I / 128, H / 256, h->gs_g, fp4 ? 0 : 1, h->pb, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "permute launch");
-    mark(NF_STAGE_GATE_UP);
+    end(NF_STAGE_PERMUTE, s);
+    begin(NF_STAGE_GATE_UP, s);
 
     GemmArgs g{};
     g.err = h->dev_err;
@@ -564,9 +644,11 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.out_ld = fp4 ? I / 2 : I;
     g.out_sf = h->h_sf;
     g.out_kgroups = I / 16;
+    g.tile_counter = h->pb.meta + 4;
     e = launch_gemm(h->tm_a, h->tm_bgu, g, h->grid, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "gate/up GEMM launch");
-    mark(NF_STAGE_DOWN);
+    end(NF_STAGE_GATE_UP, s);
+    begin(NF_STAGE_DOWN, s);
     // down
     g.epi = fp4 ? EPI_STORE_BF16 : EPI_STORE_F32;
     g.K = I;
@@ -579,37 +661,16 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.alpha0 = h->alpha_d;
     g.out = h->down;
     g.out_ld = H;
+    g.tile_counter = h->pb.meta + 5;
     e = launch_gemm(h->tm_h, h->tm_bdn, g, h->grid, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "down GEMM launch");
-    mark(NF_STAGE_SHARED);
-    // shared expert (dense BF16)
-    if (Is > 0) {
-        CUtensorMap tm_x;
-        if (!make_tmap_2d(&tm_x, x, true, H, T, 64, 128)) return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-        GemmArgs sg{};
-        sg.err = h->dev_err;
-        sg.limit = d.swiglu_limit;
-        sg.kind = KIND_BF16;
-        sg.epi = EPI_SWIGLU_BF16;
-        sg.K = H;
-        sg.dense_rows = T;
-        sg.n_blocks = Is / 128;
-        sg.out = h->sh_h;
-        sg.out_ld = Is;
-        e = launch_gemm(tm_x, h->tm_sgu, sg, h->grid, s);
-        if (e != cudaSuccess) return h->cuda_fail(e, "shared gate/up GEMM launch");
-        sg.epi = EPI_STORE_F32;
-        sg.K = Is;
-        sg.n_blocks = H / 256;
-        sg.out = h->sh_out;
-        sg.out_ld = H;
-        e = launch_gemm(h->tm_shh, h->tm_sdn, sg, h->grid, s);
-        if (e != cudaSuccess) return h->cuda_fail(e, "shared down GEMM launch");
-    }
-    mark(NF_STAGE_COMBINE);
+    end(NF_STAGE_DOWN, s);
+    if (Is > 0 && (e = cudaStreamWaitEvent(s, h->ev_join, 0)) != cudaSuccess)
+        return h->cuda_fail(e, "shared expert join");
+    begin(NF_STAGE_COMBINE, s);
     e = launch_combine(h->down, fp4, h->pb.pair_row, w, Is > 0 ? h->sh_out : nullptr, residual, T, K, H, y, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "combine launch");
-    mark(NF_STAGE_COUNT);
+    end(NF_STAGE_COMBINE, s);
     return NF_OK;
 }
 
@@ -619,7 +680,7 @@ int nf_moe_profile(nf_moe* h, int enable) {
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
     if (h->prof_ev.empty()) {
-        h->prof_ev.resize(static_cast<size_t>(nf_moe::kProfSets) * (NF_STAGE_COUNT + 1));
+        h->prof_ev.resize(static_cast<size_t>(nf_moe::kProfSets) * nf_moe::kEvPerSet);
         for (auto& ev : h->prof_ev) {
             if (cudaEventCreate(&ev) != cudaSuccess) {
                 cudaSetDevice(prev);
@@ -627,6 +688,7 @@ int nf_moe_profile(nf_moe* h, int enable) {
             }
         }
         h->prof_used.assign(nf_moe::kProfSets, 0);
+        h->prof_mask.assign(nf_moe::kProfSets, 0);
     }
     for (int set = 0; set < nf_moe::kProfSets; ++set) h->prof_used[static_cast<size_t>(set)] = 0;
     for (double& v : h->stage_ms) v = 0.0;
@@ -785,11 +847,11 @@ int nf_sigmoid_ref(const float* x, int64_t n, float* y, void* stream) {
     return launch_sigmoid_ref(x, n, y, static_cast<cudaStream_t>(stream)) == cudaSuccess ? NF_OK : NF_ERR_CUDA;
 }
 
-int nf_format_selfcheck(int64_t* e2m1_mismatches, int64_t* e4m3_mismatches) {
-    if (!e2m1_mismatches || !e4m3_mismatches) return NF_ERR_INVALID;
+int nf_format_selfcheck(int64_t* e2m1_mismatches, int64_t* e4m3_mismatches, int64_t* bf16_mismatches) {
+    if (!e2m1_mismatches || !e4m3_mismatches || !bf16_mismatches) return NF_ERR_INVALID;
     unsigned long long* d = nullptr;
-    if (cudaMalloc(&d, 2 * sizeof(unsigned long long)) != cudaSuccess) return NF_ERR_NOMEM;
-    unsigned long long h[2] = {0, 0};
+    if (cudaMalloc(&d, 3 * sizeof(unsigned long long)) != cudaSuccess) return NF_ERR_NOMEM;
+    unsigned long long h[3] = {0, 0, 0};
     cudaError_t e = cudaMemset(d, 0, sizeof(h));
     if (e == cudaSuccess) e = launch_format_selfcheck(d, nullptr);
     if (e == cudaSuccess) e = cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
@@ -797,6 +859,7 @@ int nf_format_selfcheck(int64_t* e2m1_mismatches, int64_t* e4m3_mismatches) {
     if (e != cudaSuccess) return NF_ERR_CUDA;
     *e2m1_mismatches = static_cast<int64_t>(h[0]);
     *e4m3_mismatches = static_cast<int64_t>(h[1]);
+    *bf16_mismatches = static_cast<int64_t>(h[2]);
     return NF_OK;
 }
 

@@ -83,7 +83,7 @@ def load() -> ctypes.CDLL:
         "nf_nvfp4_quantize": ([P, I64, I64, F, P, P, P, P], I32),
         "nf_sigmoid_ref": ([P, I64, P, P], I32),
         "nf_moe_profile": ([P, I32], I32),
-        "nf_format_selfcheck": ([ctypes.POINTER(I64), ctypes.POINTER(I64)], I32),
+        "nf_format_selfcheck": ([ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64)], I32),
         "nf_moe_stage_times": ([P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(I32)], I32),
     }
     for name, (args, res) in sig.items():
@@ -276,14 +276,14 @@ def sigmoid_ref(x_dev, n: int, y_dev, stream=0) -> int:
     return load().nf_sigmoid_ref(_ptr(x_dev), n, _ptr(y_dev), stream or None)
 
 
-def format_selfcheck() -> tuple[int, int]:
-    """(E2M1, E4M3) mismatch counts of the hardware conversions against the
-    reference encoders over every 32-bit pattern (current device)."""
-    a, b = ctypes.c_int64(), ctypes.c_int64()
-    st = load().nf_format_selfcheck(ctypes.byref(a), ctypes.byref(b))
+def format_selfcheck() -> tuple[int, int, int]:
+    """(E2M1, E4M3, BF16) mismatch counts of the hardware conversions against
+    the reference encoders over every 32-bit pattern (current device)."""
+    a, b, c = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+    st = load().nf_format_selfcheck(ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
     if st != NF_OK:
         raise NfError(st, "format self-check failed to run")
-    return a.value, b.value
+    return a.value, b.value, c.value
 
 
 def sf_atom_offset(row: np.ndarray, kgroup: np.ndarray, kgroups_total: int) -> np.ndarray:

@@ -118,9 +118,11 @@ def test_sigmoid_full_binades():
 
 
 def test_hardware_conversions_match_reference_encoders():
-    """The quantisers use cvt.rn.satfinite e2m1x2 / e4m3x2; over every 32-bit
-    pattern they must agree with cast_to_e2m1 (after the +-6 clamp) and with
-    f32_to_e4m3 on [2^-6, inf) (after the 448 clamp)."""
-    e2m1, e4m3 = m.format_selfcheck()
+    """The kernels use cvt.rn.satfinite e2m1x2 / e4m3x2 and cvt.rn.bf16(x2);
+    over every 32-bit pattern they must agree with cast_to_e2m1 (after the
+    +-6 clamp), f32_to_e4m3 on [2^-6, inf) (after the 448 clamp) and
+    f32_to_bf16 on every non-NaN input."""
+    e2m1, e4m3, bf16 = m.format_selfcheck()
     assert e2m1 == 0, f"{e2m1} E2M1 mismatches"
     assert e4m3 == 0, f"{e4m3} E4M3 mismatches"
+    assert bf16 == 0, f"{bf16} BF16 rounding mismatches"
