@@ -175,6 +175,12 @@ NF_DEV uint32_t e4m3_hw(float v) {
     return r & 0xffu;
 }
 
+// Out-of-line copy of quantize_group16 for the rare NaN groups, so the
+// common path keeps its registers.
+static __device__ __noinline__ uint32_t quantize_group16_cold(const float (&x)[16], float global_scale, uint32_t (&codes)[2]) {
+    return quantize_group16(x, global_scale, codes);
+}
+
 // quantize_group16 with the hardware conversions: identical results (NaN
 // groups and scales below 2^-6 take the reference-rule path).  kBf16Input:
 // the inputs are BF16 values already, so the BF16 rounding is skipped.
@@ -192,7 +198,7 @@ NF_DEV uint32_t quantize_group16_fast(const float (&x)[16], float global_scale, 
         const float a = fabsf(r[i]);
         peak = (peak < a) ? a : peak;
     }
-    if (nan) return quantize_group16(x, global_scale, codes);
+    if (nan) return quantize_group16_cold(x, global_scale, codes);
     float scale = __fmul_rn(global_scale, __fdiv_rn(peak, 6.f));
     scale = scale > 448.f ? 448.f : scale;
     const uint32_t scode = scale >= 0.015625f ? e4m3_hw(scale) : f32_to_e4m3(scale);
