@@ -33,6 +33,7 @@ namespace nf {
 constexpr int BM = 128, BN = 256, STAGES = 4;
 constexpr int kEpiWarps = 16;
 constexpr int kTileQ = 4;  // depth of the producer -> consumer tile queue
+constexpr int kSmallRows = 32;  // A box height for tiles with few rows (decode)
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int A_STAGE_BYTES = BM * 128;
 constexpr int B_STAGE_BYTES = BN * 128;
@@ -86,7 +87,8 @@ __device__ __forceinline__ void set_abort(volatile int* cta_abort, int* dev_err,
 
 template <int KIND, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, const GemmArgs args) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tma_small,
+                const __grid_constant__ CUtensorMap tmb, const GemmArgs args) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -122,6 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *cta_abort = 0;
         fence_barrier_init();
         prefetch_tensormap(&tma);
+        prefetch_tensormap(&tma_small);
         prefetch_tensormap(&tmb);
     }
     if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
@@ -172,12 +175,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const int k0 = kt * kElemsPerStage;
                     const int steps = min(4, (K - k0) / kMmaK);
-                    uint32_t bytes = A_STAGE_BYTES + B_STAGE_BYTES;
+                    // tiles with at most 32 rows of the expert load only those rows of A
+                    const bool small_a = t.m_valid <= kSmallRows;
+                    uint32_t bytes = (small_a ? kSmallRows * 128 : A_STAGE_BYTES) + B_STAGE_BYTES;
                     if (KIND == KIND_NVFP4) bytes += static_cast<uint32_t>(steps) * 512u * 3u;
                     mbar_arrive_expect_tx(&full[stage], bytes);
                     const int xc = KIND == KIND_NVFP4 ? kt * 128 : k0;
-                    tma_load_2d(sA + stage * A_STAGE_BYTES, &tma, &full[stage], xc, t.row0);
-                    tma_load_2d(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], xc, brow0);
+                    tma_load_2d(sA + stage * A_STAGE_BYTES, small_a ? &tma_small : &tma, &full[stage], xc, t.row0);
+                    // B in box order: stage kt of tile (expert, n_block) is one 32 KB block
+                    tma_load_2d(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0,
+                                ((t.expert * args.b_nb + t.n_block) * args.b_kt + kt) * BN);
                     if (KIND == KIND_NVFP4) {
                         const int64_t a_atom = static_cast<int64_t>(t.row0 / 128) * sf_atoms_per_rowblock + kt * 4;
                         bulk_load(sSFA + stage * SFA_STAGE_BYTES, args.sfa + a_atom * 512, steps * 512u, &full[stage]);
@@ -464,7 +471,7 @@ int gemm_grid_size(int device) {
 }
 
 template <int KIND, int EPI>
-static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tmb, const GemmArgs& args, int grid,
+static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb, const GemmArgs& args, int grid,
                               cudaStream_t st) {
     static bool attr = false;
     if (!attr) {
@@ -473,18 +480,18 @@ static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tmb, co
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    gemm_kernel<KIND, EPI><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tmb, args);
+    gemm_kernel<KIND, EPI><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, tmb, args);
     return cudaGetLastError();
 }
 
-cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tmb, const GemmArgs& args, int grid,
+cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb, const GemmArgs& args, int grid,
                         cudaStream_t st) {
     if (args.kind == KIND_NVFP4) {
-        if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT>(tma, tmb, args, grid, st);
-        if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16>(tma, tmb, args, grid, st);
+        if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT>(tma, tma_small, tmb, args, grid, st);
+        if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16>(tma, tma_small, tmb, args, grid, st);
     } else {
-        if (args.epi == EPI_SWIGLU_BF16) return launch_one<KIND_BF16, EPI_SWIGLU_BF16>(tma, tmb, args, grid, st);
-        if (args.epi == EPI_STORE_F32) return launch_one<KIND_BF16, EPI_STORE_F32>(tma, tmb, args, grid, st);
+        if (args.epi == EPI_SWIGLU_BF16) return launch_one<KIND_BF16, EPI_SWIGLU_BF16>(tma, tma_small, tmb, args, grid, st);
+        if (args.epi == EPI_STORE_F32) return launch_one<KIND_BF16, EPI_STORE_F32>(tma, tma_small, tmb, args, grid, st);
     }
     return cudaErrorInvalidValue;
 }

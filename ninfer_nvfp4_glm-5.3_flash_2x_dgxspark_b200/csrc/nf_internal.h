@@ -48,7 +48,9 @@ struct GemmArgs {
     int kind;            // GemmKind
     int epi;             // GemmEpi
     int K;               // reduction length in elements
-    int b_rows_per_expert;  // B rows per expert (0 for a dense GEMM)
+    int b_rows_per_expert;  // B rows per expert (0 for a dense GEMM; indexes the scale atoms)
+    int b_nb;               // B is stored in box order: 256-row blocks per expert ...
+    int b_kt;               // ... each split into b_kt blocks of 128 bytes of K
     // tile source: grouped (tiles + device tile count) or dense
     const NfTile* tiles;
     const int32_t* num_tiles_dev;
@@ -74,7 +76,8 @@ struct GemmArgs {
 // Host helpers (nf_gemm.cu).
 bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner_elems, uint64_t rows,
                   uint32_t box_inner, uint32_t box_rows);
-cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tmb, const GemmArgs& args, int grid,
+// tma_small: the same A tensor with a 32-row box, used for tiles with <= 32 rows.
+cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb, const GemmArgs& args, int grid,
                         cudaStream_t st);
 int gemm_grid_size(int device);
 

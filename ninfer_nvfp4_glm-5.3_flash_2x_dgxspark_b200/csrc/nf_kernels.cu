@@ -188,9 +188,12 @@ __global__ void __launch_bounds__(kRtThreads) router_logits_kernel(const uint16_
         }
         // range check of the staged token rows
         int unsafe = 0;
-        for (int i = threadIdx.x; i < nt * (kc / 2); i += blockDim.x) {
-            const int r = i / (kc / 2), c = i % (kc / 2);
-            unsafe |= bf16x2_unsafe(reinterpret_cast<const uint32_t*>(xs + r * pitch)[c]) ? 1 : 0;
+        for (int r = 0; r < nt; ++r) {
+            const uint4* row = reinterpret_cast<const uint4*>(xs + r * pitch);
+            for (int c = threadIdx.x; c < kc / 8; c += blockDim.x) {
+                const uint4 q = row[c];
+                unsafe |= (bf16x2_unsafe(q.x) | bf16x2_unsafe(q.y) | bf16x2_unsafe(q.z) | bf16x2_unsafe(q.w)) ? 1 : 0;
+            }
         }
         const bool use_fma = w_safe && !__syncthreads_or(unsafe);
         const int ta = min(2 * tp, kRtTok - 1), tb = min(2 * tp + 1, kRtTok - 1);

@@ -83,6 +83,7 @@ struct nf_moe {
 
     // tensor maps built at finalize
     CUtensorMap tm_a{}, tm_bgu{}, tm_h{}, tm_bdn{}, tm_sgu{}, tm_shh{}, tm_sdn{};
+    CUtensorMap tm_a_s{}, tm_h_s{}, tm_shh_s{};  // 32-row boxes of the A operands
     int last_tokens = 0;
 
     // per-stage event profile: a ring of event sets (a begin and an end event
@@ -189,6 +190,47 @@ bool scales_to_atoms(const uint8_t* scales, int64_t rows, int64_t kgroups, float
 
 const char* proj_name(int proj) { return proj == NF_PROJ_GATE ? "gate_proj" : proj == NF_PROJ_UP ? "up_proj" : "down_proj"; }
 
+// Weight matrices that the GEMMs stream (their B operands) are stored in
+// "box order": the matrix is cut into blocks of 256 rows x 128 bytes (one
+// pipeline stage of one tile; 256 FP4 or 64 BF16 K-elements), each block is
+// 32 KB contiguous with 128-byte rows (zero padded past the row end), blocks
+// ordered row-block major, K-block minor.  A stage is then one contiguous
+// 32 KB read from HBM instead of 256 strided 128-byte pieces.
+constexpr int64_t kBlockRows = 256, kBlockRowBytes = 128, kBlockBytes = kBlockRows * kBlockRowBytes;
+
+int64_t k_blocks(int64_t row_bytes) { return (row_bytes + kBlockRowBytes - 1) / kBlockRowBytes; }
+int64_t blocked_bytes(int64_t rows, int64_t row_bytes) { return (rows / kBlockRows) * k_blocks(row_bytes) * kBlockBytes; }
+
+// Copies a row-major [rows, row_bytes] matrix (rows % 256 == 0) into box order.
+cudaError_t upload_blocked(uint8_t* dst, const uint8_t* src, int64_t rows, int64_t row_bytes) {
+    const int64_t nb = rows / kBlockRows, kt = k_blocks(row_bytes);
+    std::vector<uint8_t> stage(static_cast<size_t>(nb * kt * kBlockBytes), 0);
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t k = 0; k < kt; ++k) {
+            const int64_t n = std::min(kBlockRowBytes, row_bytes - k * kBlockRowBytes);
+            std::memcpy(&stage[static_cast<size_t>(((r / kBlockRows) * kt + k) * kBlockBytes + (r % kBlockRows) * kBlockRowBytes)],
+                        src + r * row_bytes + k * kBlockRowBytes, static_cast<size_t>(n));
+        }
+    return cudaMemcpy(dst, stage.data(), stage.size(), cudaMemcpyHostToDevice);
+}
+
+// Copies one of the two halves of a gate/up pair into box order: source row
+// j lands in row (j % 128) + 128 * half of row block j / 128 (the 256-row
+// blocks hold 128 gate rows then the 128 up rows of the same intermediate
+// columns).  `dst` is the expert's first block.
+cudaError_t upload_blocked_half(uint8_t* dst, const uint8_t* src, int64_t rows, int64_t row_bytes, int half) {
+    const int64_t nb = rows / 128, kt = k_blocks(row_bytes), hb = kBlockBytes / 2;
+    std::vector<uint8_t> stage(static_cast<size_t>(nb * kt * hb), 0);
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t k = 0; k < kt; ++k) {
+            const int64_t n = std::min(kBlockRowBytes, row_bytes - k * kBlockRowBytes);
+            std::memcpy(&stage[static_cast<size_t>(((r / 128) * kt + k) * hb + (r % 128) * kBlockRowBytes)],
+                        src + r * row_bytes + k * kBlockRowBytes, static_cast<size_t>(n));
+        }
+    return cudaMemcpy2D(dst + half * hb, static_cast<size_t>(kBlockBytes), stage.data(), static_cast<size_t>(hb),
+                        static_cast<size_t>(hb), static_cast<size_t>(nb * kt), cudaMemcpyHostToDevice);
+}
+
 }  // namespace
 
 extern "C" {
@@ -286,12 +328,13 @@ int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
     bool ok = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && h->alloc(&h->router_w, E * H) && h->alloc(&h->router_bias, E);
     if (fp4) {
-        ok = ok && h->alloc(&h->w_gu, E * 2 * I * H / 2) && h->alloc(&h->w_gu_sf, E * 2 * I * H / 16) &&
-             h->alloc(&h->w_dn, E * H * I / 2) && h->alloc(&h->w_dn_sf, E * H * I / 16);
+        ok = ok && h->alloc(&h->w_gu, E * blocked_bytes(2 * I, H / 2)) && h->alloc(&h->w_gu_sf, E * 2 * I * H / 16) &&
+             h->alloc(&h->w_dn, E * blocked_bytes(H, I / 2)) && h->alloc(&h->w_dn_sf, E * H * I / 16);
     } else {
-        ok = ok && h->alloc(&h->wb_gu, E * 2 * I * H) && h->alloc(&h->wb_dn, E * H * I);
+        ok = ok && h->alloc(&h->wb_gu, E * blocked_bytes(2 * I, 2 * H) / 2) &&
+             h->alloc(&h->wb_dn, E * blocked_bytes(H, 2 * I) / 2);
     }
-    if (Is > 0) ok = ok && h->alloc(&h->ws_gu, 2 * Is * H) && h->alloc(&h->ws_dn, H * Is);
+    if (Is > 0) ok = ok && h->alloc(&h->ws_gu, blocked_bytes(2 * Is, 2 * H) / 2) && h->alloc(&h->ws_dn, blocked_bytes(H, 2 * Is) / 2);
     ok = ok && h->alloc(&h->alpha_g, E) && h->alloc(&h->alpha_u, E) && h->alloc(&h->alpha_d, E) &&
          h->alloc(&h->gs_g, E) && h->alloc(&h->gs_d, E);
     ok = ok && h->alloc(&h->logits, Tm * E) && h->alloc(&h->topk_idx, Tm * K) && h->alloc(&h->topk_w, Tm * K);
@@ -365,15 +408,13 @@ int nf_moe_bind_nvfp4(nf_moe* h, int expert, int proj, const uint8_t* packed, co
     const int64_t kbytes = cols / 2;
     const int64_t slab = (cols / 64) * 512;  // one 128-row block of atoms
     if (proj == NF_PROJ_DOWN) {
-        e = cudaMemcpy(h->w_dn + expert * H * kbytes, packed, static_cast<size_t>(H * kbytes), cudaMemcpyHostToDevice);
+        e = upload_blocked(h->w_dn + expert * blocked_bytes(H, kbytes), packed, H, kbytes);
         if (e == cudaSuccess)
             e = cudaMemcpy(h->w_dn_sf + expert * H * (cols / 16), atoms.data(), atoms.size(), cudaMemcpyHostToDevice);
     } else {
         // gate rows j -> interleaved row (j / 128) * 256 + j % 128, up rows +128
-        const int64_t off = proj == NF_PROJ_UP ? 128 : 0;
-        uint8_t* base = h->w_gu + (expert * 2 * I + off) * kbytes;
-        e = cudaMemcpy2D(base, static_cast<size_t>(256 * kbytes), packed, static_cast<size_t>(128 * kbytes),
-                         static_cast<size_t>(128 * kbytes), static_cast<size_t>(I / 128), cudaMemcpyHostToDevice);
+        e = upload_blocked_half(h->w_gu + expert * blocked_bytes(2 * I, kbytes), packed, I, kbytes,
+                                proj == NF_PROJ_UP ? 1 : 0);
         if (e == cudaSuccess) {
             uint8_t* sbase = h->w_gu_sf + (expert * 2 * I / 128 + (proj == NF_PROJ_UP ? 1 : 0)) * slab;
             e = cudaMemcpy2D(sbase, static_cast<size_t>(2 * slab), atoms.data(), static_cast<size_t>(slab),
@@ -434,22 +475,28 @@ int nf_moe_bind_bf16(nf_moe* h, int which, int expert, const uint16_t* data, int
         }
         case NF_BF16_SHARED_GATE:
         case NF_BF16_SHARED_UP: {
-            uint16_t* base = h->ws_gu + (which == NF_BF16_SHARED_UP ? 128 : 0) * H;
-            e = cudaMemcpy2D(base, 256 * rb, data, 128 * rb, 128 * rb, static_cast<size_t>(Is / 128), cudaMemcpyHostToDevice);
+            e = upload_blocked_half(reinterpret_cast<uint8_t*>(h->ws_gu), reinterpret_cast<const uint8_t*>(data), Is,
+                                    static_cast<int64_t>(rb), which == NF_BF16_SHARED_UP ? 1 : 0);
             if (which == NF_BF16_SHARED_GATE) h->sg_bound = e == cudaSuccess;
             else h->su_bound = e == cudaSuccess;
             break;
         }
-        case NF_BF16_SHARED_DOWN: e = cudaMemcpy(h->ws_dn, data, rows * rb, cudaMemcpyHostToDevice); h->sd_bound = e == cudaSuccess; break;
+        case NF_BF16_SHARED_DOWN:
+            e = upload_blocked(reinterpret_cast<uint8_t*>(h->ws_dn), reinterpret_cast<const uint8_t*>(data), H,
+                               static_cast<int64_t>(rb));
+            h->sd_bound = e == cudaSuccess;
+            break;
         case NF_BF16_EXPERT_GATE:
         case NF_BF16_EXPERT_UP: {
-            uint16_t* base = h->wb_gu + (expert * 2 * I + (which == NF_BF16_EXPERT_UP ? 128 : 0)) * H;
-            e = cudaMemcpy2D(base, 256 * rb, data, 128 * rb, 128 * rb, static_cast<size_t>(I / 128), cudaMemcpyHostToDevice);
+            uint8_t* base = reinterpret_cast<uint8_t*>(h->wb_gu) + expert * blocked_bytes(2 * I, H * 2);
+            e = upload_blocked_half(base, reinterpret_cast<const uint8_t*>(data), I, static_cast<int64_t>(rb),
+                                    which == NF_BF16_EXPERT_UP ? 1 : 0);
             if (e == cudaSuccess) h->bound[static_cast<size_t>(expert * 3 + (which - NF_BF16_EXPERT_GATE))] = 1;
             break;
         }
         case NF_BF16_EXPERT_DOWN:
-            e = cudaMemcpy(h->wb_dn + expert * H * I, data, rows * rb, cudaMemcpyHostToDevice);
+            e = upload_blocked(reinterpret_cast<uint8_t*>(h->wb_dn) + expert * blocked_bytes(H, I * 2),
+                               reinterpret_cast<const uint8_t*>(data), H, static_cast<int64_t>(rb));
             if (e == cudaSuccess) h->bound[static_cast<size_t>(expert * 3 + 2)] = 1;
             break;
     }
@@ -511,19 +558,24 @@ int nf_moe_finalize(nf_moe* h) {
     bool ok = true;
     if (fp4) {
         ok = ok && make_tmap_2d(&h->tm_a, h->pb.a_codes, false, H / 2, R, 128, 128);
-        ok = ok && make_tmap_2d(&h->tm_bgu, h->w_gu, false, H / 2, E * 2 * I, 128, 256);
+        ok = ok && make_tmap_2d(&h->tm_a_s, h->pb.a_codes, false, H / 2, R, 128, 32);
+        ok = ok && make_tmap_2d(&h->tm_h_s, h->h_codes, false, I / 2, R, 128, 32);
+        ok = ok && make_tmap_2d(&h->tm_bgu, h->w_gu, false, 128, E * blocked_bytes(2 * I, H / 2) / 128, 128, 256);
         ok = ok && make_tmap_2d(&h->tm_h, h->h_codes, false, I / 2, R, 128, 128);
-        ok = ok && make_tmap_2d(&h->tm_bdn, h->w_dn, false, I / 2, E * H, 128, 256);
+        ok = ok && make_tmap_2d(&h->tm_bdn, h->w_dn, false, 128, E * blocked_bytes(H, I / 2) / 128, 128, 256);
     } else {
         ok = ok && make_tmap_2d(&h->tm_a, h->pb.a_bf16, true, H, R, 64, 128);
-        ok = ok && make_tmap_2d(&h->tm_bgu, h->wb_gu, true, H, E * 2 * I, 64, 256);
+        ok = ok && make_tmap_2d(&h->tm_a_s, h->pb.a_bf16, true, H, R, 64, 32);
+        ok = ok && make_tmap_2d(&h->tm_h_s, h->h_bf16, true, I, R, 64, 32);
+        ok = ok && make_tmap_2d(&h->tm_bgu, h->wb_gu, true, 64, E * blocked_bytes(2 * I, 2 * H) / 128, 64, 256);
         ok = ok && make_tmap_2d(&h->tm_h, h->h_bf16, true, I, R, 64, 128);
-        ok = ok && make_tmap_2d(&h->tm_bdn, h->wb_dn, true, I, E * H, 64, 256);
+        ok = ok && make_tmap_2d(&h->tm_bdn, h->wb_dn, true, 64, E * blocked_bytes(H, 2 * I) / 128, 64, 256);
     }
     if (Is > 0) {
-        ok = ok && make_tmap_2d(&h->tm_sgu, h->ws_gu, true, H, 2 * Is, 64, 256);
+        ok = ok && make_tmap_2d(&h->tm_sgu, h->ws_gu, true, 64, blocked_bytes(2 * Is, 2 * H) / 128, 64, 256);
         ok = ok && make_tmap_2d(&h->tm_shh, h->sh_h, true, Is, Tm, 64, 128);
-        ok = ok && make_tmap_2d(&h->tm_sdn, h->ws_dn, true, Is, H, 64, 256);
+        ok = ok && make_tmap_2d(&h->tm_shh_s, h->sh_h, true, Is, Tm, 64, 32);
+        ok = ok && make_tmap_2d(&h->tm_sdn, h->ws_dn, true, 64, blocked_bytes(H, 2 * Is) / 128, 64, 256);
     }
     if (!ok) return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
     h->finalized = true;
@@ -582,8 +634,9 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
         if ((e = cudaEventRecord(h->ev_fork, s)) != cudaSuccess ||
             (e = cudaStreamWaitEvent(h->side, h->ev_fork, 0)) != cudaSuccess)
             return h->cuda_fail(e, "shared expert fork");
-        CUtensorMap tm_x;
-        if (!make_tmap_2d(&tm_x, x, true, H, T, 64, 128)) return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+        CUtensorMap tm_x, tm_x_s;
+        if (!make_tmap_2d(&tm_x, x, true, H, T, 64, 128) || !make_tmap_2d(&tm_x_s, x, true, H, T, 64, 32))
+            return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
         begin(NF_STAGE_SHARED, h->side);
         if ((e = cudaMemsetAsync(h->shared_counters, 0, 2 * sizeof(int), h->side)) != cudaSuccess)
             return h->cuda_fail(e, "shared expert counters");
@@ -595,18 +648,22 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
         sg.K = H;
         sg.dense_rows = T;
         sg.n_blocks = Is / 128;
+        sg.b_nb = 2 * Is / 256;
+        sg.b_kt = static_cast<int>(k_blocks(2 * H));
         sg.out = h->sh_h;
         sg.out_ld = Is;
         sg.tile_counter = h->shared_counters;
-        e = launch_gemm(tm_x, h->tm_sgu, sg, h->grid, h->side);
+        e = launch_gemm(tm_x, tm_x_s, h->tm_sgu, sg, h->grid, h->side);
         if (e != cudaSuccess) return h->cuda_fail(e, "shared gate/up GEMM launch");
         sg.epi = EPI_STORE_F32;
         sg.K = Is;
         sg.n_blocks = H / 256;
+        sg.b_nb = H / 256;
+        sg.b_kt = static_cast<int>(k_blocks(2 * Is));
         sg.out = h->sh_out;
         sg.out_ld = H;
         sg.tile_counter = h->shared_counters + 1;
-        e = launch_gemm(h->tm_shh, h->tm_sdn, sg, h->grid, h->side);
+        e = launch_gemm(h->tm_shh, h->tm_shh_s, h->tm_sdn, sg, h->grid, h->side);
         if (e != cudaSuccess) return h->cuda_fail(e, "shared down GEMM launch");
         end(NF_STAGE_SHARED, h->side);
         if ((e = cudaEventRecord(h->ev_join, h->side)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
@@ -630,6 +687,8 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.epi = fp4 ? EPI_SWIGLU_QUANT : EPI_SWIGLU_BF16;
     g.K = H;
     g.b_rows_per_expert = 2 * I;
+    g.b_nb = 2 * I / 256;
+    g.b_kt = static_cast<int>(k_blocks(fp4 ? H / 2 : 2 * H));
     g.tiles = h->pb.tiles_gu;
     g.num_tiles_dev = h->pb.meta + 1;
     g.dense_rows = 0;
@@ -645,7 +704,7 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.out_sf = h->h_sf;
     g.out_kgroups = I / 16;
     g.tile_counter = h->pb.meta + 4;
-    e = launch_gemm(h->tm_a, h->tm_bgu, g, h->grid, s);
+    e = launch_gemm(h->tm_a, h->tm_a_s, h->tm_bgu, g, h->grid, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "gate/up GEMM launch");
     end(NF_STAGE_GATE_UP, s);
     begin(NF_STAGE_DOWN, s);
@@ -653,6 +712,8 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.epi = fp4 ? EPI_STORE_BF16 : EPI_STORE_F32;
     g.K = I;
     g.b_rows_per_expert = H;
+    g.b_nb = H / 256;
+    g.b_kt = static_cast<int>(k_blocks(fp4 ? I / 2 : 2 * I));
     g.tiles = h->pb.tiles_down;
     g.num_tiles_dev = h->pb.meta + 2;
     g.n_blocks = H / 256;
@@ -662,7 +723,7 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.out = h->down;
     g.out_ld = H;
     g.tile_counter = h->pb.meta + 5;
-    e = launch_gemm(h->tm_h, h->tm_bdn, g, h->grid, s);
+    e = launch_gemm(h->tm_h, h->tm_h_s, h->tm_bdn, g, h->grid, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "down GEMM launch");
     end(NF_STAGE_DOWN, s);
     if (Is > 0 && (e = cudaStreamWaitEvent(s, h->ev_join, 0)) != cudaSuccess)
