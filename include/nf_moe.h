@@ -148,6 +148,13 @@ NF_API int nf_moe_forward(nf_moe* handle, const uint16_t* x_dev, const float* re
  * pointers are not NULL) back and synchronises. */
 NF_API int nf_moe_forward_host(nf_moe* handle, const float* x_host, const float* residual_host, int tokens, float* y_host,
                         int32_t* topk_idx_host, float* topk_w_host);
+/* Graph mode (off by default): nf_moe_forward captures its launches for each
+ * distinct (x, residual, y, idx, w, tokens, stream) into a CUDA graph on
+ * first use and replays the graph afterwards (the 16 most recent argument
+ * sets are kept).  Needs a non-NULL stream; forwards with per-stage
+ * profiling on, on the NULL stream, or issued while the caller is capturing
+ * run the kernels directly. */
+NF_API int nf_moe_set_graph_mode(nf_moe* handle, int enable);
 /* Waits for the handle's work on `stream` and reports a device-side error. */
 NF_API int nf_moe_sync(nf_moe* handle, void* stream);
 

@@ -86,7 +86,7 @@ int gemm_grid_size(int device);
 // bind), which lets the exact logit chains use fused multiply-add.
 cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H, int E, int K,
                           float scaling, int normalize, int n_group, int topk_group, int w_safe, float* logits,
-                          int32_t* idx, float* wts, int* err, cudaStream_t st);
+                          float* scores, float* choices, int32_t* idx, float* wts, int* err, cudaStream_t st);
 cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
                            const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st);
 cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair_row, const float* topk_w,

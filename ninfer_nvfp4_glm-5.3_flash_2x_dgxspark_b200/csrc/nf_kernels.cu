@@ -84,21 +84,22 @@ cudaError_t prepare_device_tables() {
 // A CTA owns kRtExp experts x kRtTok tokens: it stages those router rows and
 // token rows in shared memory with 1-D bulk copies (row pitch padded by 16
 // bytes so the 8 rows a warp reads fall in distinct banks), then each thread
-// runs the chains of one expert for two tokens with paired f32x2
-// instructions.  A product of two BF16 values has at most 16 significant
-// bits, so it is exact in fp32 unless it leaves fp32's range; when every
-// nonzero |w| and |x| lies in [2^-67, 2^63) (router weights checked at bind,
-// token rows checked here in shared memory) the product is exact and
-// fma(w, x, acc) equals the reference's round(acc + round(w * x)).  Otherwise
-// the CTA runs the separately rounded multiply and add.  The chain of H
-// dependent adds is the latency floor.
+// runs the chain of one (token, expert) pair: two unpack operations and one
+// fused multiply-add per step, so the warp issues fast enough for the chain
+// of H dependent adds -- the kernel's latency floor -- to be the bound.
+// A product of two BF16 values has at most 16 significant bits, so it is
+// exact in fp32 unless it leaves fp32's range; when every nonzero |w| and |x|
+// lies in [2^-67, 2^63) (router weights checked at bind, token rows checked
+// here in shared memory) the product is exact and fma(w, x, acc) equals the
+// reference's round(acc + round(w * x)).  Otherwise the CTA runs the
+// separately rounded multiply and add.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
 
 constexpr int kRtExp = 8;    // experts per CTA
-constexpr int kRtTok = 16;   // tokens per CTA
-constexpr int kRtThreads = kRtExp * kRtTok / 2;
+constexpr int kRtTok = 8;    // tokens per CTA
+constexpr int kRtThreads = kRtExp * kRtTok;
 constexpr int kRtMaxChunk = 4096;  // K elements staged at a time
 
 // true when a BF16 pair holds a value whose product with another in-range
@@ -111,43 +112,42 @@ __device__ __forceinline__ bool bf16x2_unsafe(uint32_t u) {
 }
 
 template <bool kFma>
-__device__ __forceinline__ float2 chain_step2(uint32_t wv, uint32_t av, uint32_t bv, float2 acc) {
-    const float2 w0 = make_float2(bf16_lo(wv), bf16_lo(wv)), w1 = make_float2(bf16_hi(wv), bf16_hi(wv));
-    const float2 x0 = make_float2(bf16_lo(av), bf16_lo(bv)), x1 = make_float2(bf16_hi(av), bf16_hi(bv));
+__device__ __forceinline__ float chain_step2(uint32_t wv, uint32_t xv, float acc) {
     if (kFma) {
-        acc = __ffma2_rn(w0, x0, acc);
-        acc = __ffma2_rn(w1, x1, acc);
+        acc = fmaf(bf16_lo(wv), bf16_lo(xv), acc);
+        acc = fmaf(bf16_hi(wv), bf16_hi(xv), acc);
     } else {
-        acc = __fadd2_rn(acc, __fmul2_rn(w0, x0));
-        acc = __fadd2_rn(acc, __fmul2_rn(w1, x1));
+        acc = __fadd_rn(acc, __fmul_rn(bf16_lo(wv), bf16_lo(xv)));
+        acc = __fadd_rn(acc, __fmul_rn(bf16_hi(wv), bf16_hi(xv)));
     }
     return acc;
 }
 
-// Chains over n8 groups of 8 elements from shared memory; the next group's
-// three 16-byte loads are issued before the current group's 8 dependent
-// steps, so the load latency hides behind the chain.
+// One chain over n8 groups of 8 elements from shared memory; the next
+// group's two 16-byte loads are issued before the current group's 8
+// dependent steps, so the load latency hides behind the chain.
 template <bool kFma>
-__device__ __forceinline__ float2 chain_pair(const uint4* __restrict__ wr, const uint4* __restrict__ xa,
-                                             const uint4* __restrict__ xb, int n8, float2 acc) {
-    uint4 w = wr[0], a = xa[0], b = xb[0];
+__device__ __forceinline__ float chain(const uint4* __restrict__ wr, const uint4* __restrict__ xr, int n8, float acc) {
+    uint4 w = wr[0], a = xr[0];
     for (int c = 0; c < n8; ++c) {
         const int nx = c + 1 < n8 ? c + 1 : c;
-        const uint4 wn = wr[nx], an = xa[nx], bn = xb[nx];
-        acc = chain_step2<kFma>(w.x, a.x, b.x, acc);
-        acc = chain_step2<kFma>(w.y, a.y, b.y, acc);
-        acc = chain_step2<kFma>(w.z, a.z, b.z, acc);
-        acc = chain_step2<kFma>(w.w, a.w, b.w, acc);
+        const uint4 wn = wr[nx], an = xr[nx];
+        acc = chain_step2<kFma>(w.x, a.x, acc);
+        acc = chain_step2<kFma>(w.y, a.y, acc);
+        acc = chain_step2<kFma>(w.z, a.z, acc);
+        acc = chain_step2<kFma>(w.w, a.w, acc);
         w = wn;
         a = an;
-        b = bn;
     }
     return acc;
 }
 
 __global__ void __launch_bounds__(kRtThreads) router_logits_kernel(const uint16_t* __restrict__ x,
-                                                                   const uint16_t* __restrict__ w, int T, int H, int E,
+                                                                   const uint16_t* __restrict__ w,
+                                                                   const float* __restrict__ bias, int T, int H, int E,
                                                                    int w_safe, float* __restrict__ logits,
+                                                                   float* __restrict__ scores,
+                                                                   float* __restrict__ choices,
                                                                    int* __restrict__ err) {
     extern __shared__ __align__(128) uint8_t rt_smem[];
     __shared__ uint64_t bar;
@@ -157,13 +157,13 @@ __global__ void __launch_bounds__(kRtThreads) router_logits_kernel(const uint16_
     uint8_t* xs = rt_smem + kRtExp * pitch;
     const int t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp;
     const int nt = min(kRtTok, T - t0), ne = min(kRtExp, E - e0);
-    const int el = threadIdx.x % kRtExp, tp = threadIdx.x / kRtExp;
+    const int el = threadIdx.x % kRtExp, tl = threadIdx.x / kRtExp;
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         fence_barrier_init();
     }
     __syncthreads();
-    float2 acc = make_float2(0.f, 0.f);
+    float acc = 0.f;
     int ok = 1;
     for (int k0 = 0, phase = 0; k0 < H; k0 += chunk, phase ^= 1) {
         const int kc = min(chunk, H - k0);
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(kRtThreads) router_logits_kernel(const uint16_
         }
         // bounded wait; every thread polls the same barrier
         const uint64_t start = globaltimer_ns();
-        while (!mbar_try_wait(&bar, static_cast<uint32_t>(phase))) {
+        while (!mbar_try_wait_sleep(&bar, static_cast<uint32_t>(phase), 20000u)) {
             if (globaltimer_ns() - start > NF_WAIT_BUDGET_NS) {
                 ok = 0;
                 break;
@@ -196,25 +196,25 @@ __global__ void __launch_bounds__(kRtThreads) router_logits_kernel(const uint16_
             }
         }
         const bool use_fma = w_safe && !__syncthreads_or(unsafe);
-        const int ta = min(2 * tp, kRtTok - 1), tb = min(2 * tp + 1, kRtTok - 1);
         const uint4* wr = reinterpret_cast<const uint4*>(ws + el * pitch);
-        const uint4* xa = reinterpret_cast<const uint4*>(xs + ta * pitch);
-        const uint4* xb = reinterpret_cast<const uint4*>(xs + tb * pitch);
-        acc = use_fma ? chain_pair<true>(wr, xa, xb, kc / 8, acc) : chain_pair<false>(wr, xa, xb, kc / 8, acc);
+        const uint4* xr = reinterpret_cast<const uint4*>(xs + tl * pitch);
+        acc = use_fma ? chain<true>(wr, xr, kc / 8, acc) : chain<false>(wr, xr, kc / 8, acc);
         __syncthreads();  // the next chunk overwrites the staged rows
     }
-    if (el < ne) {
-        if (2 * tp < nt) logits[static_cast<int64_t>(t0 + 2 * tp) * E + e0 + el] = acc.x;
-        if (2 * tp + 1 < nt) logits[static_cast<int64_t>(t0 + 2 * tp + 1) * E + e0 + el] = acc.y;
+    if (el < ne && tl < nt) {
+        // router_select's per-expert part (src/text_forward.cpp:1453-1456):
+        // score = sigmoid(logit), choice = score + correction bias
+        const int64_t o = static_cast<int64_t>(t0 + tl) * E + e0 + el;
+        const float sc = sigmoid_ref(acc);
+        logits[o] = acc;
+        scores[o] = sc;
+        choices[o] = __fadd_rn(sc, bias[e0 + el]);
     }
 }
 
 // ---------------------------------------------------------------------------
-// Router selection: router_select (src/text_forward.cpp:1447-1471).  One warp
-// per token: the lanes evaluate score = sigmoid(logit) and choice = score +
-// bias for every expert into shared memory, then lane 0 runs the reference's
-// sequential scan (strict '>' from the lowest unused index), so ties and NaN
-// behave exactly as in the reference.  With n_group > 1 the group-limited
+// Router selection: router_select (src/text_forward.cpp:1447-1471) on the
+// scores and choices the logits kernel wrote.  One warp per token.  With n_group > 1 the group-limited
 // form (a group scores the sum of its two best choices, topk_group groups
 // stay eligible, lower group index on ties) masks the other experts first;
 // the reference has no group limit.
@@ -222,20 +222,13 @@ __global__ void __launch_bounds__(kRtThreads) router_logits_kernel(const uint16_
 constexpr int kSelectWarps = 4;
 
 __global__ void __launch_bounds__(kSelectWarps * 32) router_select_kernel(
-    const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int K, float scaling,
+    const float* __restrict__ scores, const float* __restrict__ choices, int T, int E, int K, float scaling,
     int normalize, int n_group, int topk_group, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
-    extern __shared__ float s_sel[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* score = s_sel + static_cast<int64_t>(warp) * 2 * E;
-    float* choice = score + E;
     const int t = blockIdx.x * kSelectWarps + warp;
     if (t >= T) return;
-    const float* lg = logits + static_cast<int64_t>(t) * E;
-    for (int e = lane; e < E; e += 32) {
-        const float s = sigmoid_ref(lg[e]);
-        score[e] = s;
-        choice[e] = __fadd_rn(s, bias[e]);
-    }
+    const float* score = scores + static_cast<int64_t>(t) * E;
+    const float* choice = choices + static_cast<int64_t>(t) * E;
     // experts excluded by the group limit (computed by lane 0, rare path)
     __shared__ uint32_t s_excl[kSelectWarps][32];  // E <= 1024 bits
     uint32_t* excl = s_excl[warp];
@@ -731,7 +724,7 @@ __global__ void quantize_kernel(const float* __restrict__ x, int64_t rows, int64
 // ---------------------------------------------------------------------------
 cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H, int E, int K,
                           float scaling, int normalize, int n_group, int topk_group, int w_safe, float* logits,
-                          int32_t* idx, float* wts, int* err, cudaStream_t st) {
+                          float* scores, float* choices, int32_t* idx, float* wts, int* err, cudaStream_t st) {
     const int chunk = H < kRtMaxChunk ? H : kRtMaxChunk;
     const size_t smem = static_cast<size_t>(kRtExp + kRtTok) * (chunk * 2 + 16);
     static bool attr = false;
@@ -742,10 +735,9 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* bia
         attr = true;
     }
     const dim3 grid((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp);
-    router_logits_kernel<<<grid, kRtThreads, smem, st>>>(x, w, T, H, E, w_safe, logits, err);
-    router_select_kernel<<<(T + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32,
-                           kSelectWarps * 2 * E * sizeof(float), st>>>(logits, bias, T, E, K, scaling, normalize,
-                                                                      n_group, topk_group, idx, wts);
+    router_logits_kernel<<<grid, kRtThreads, smem, st>>>(x, w, bias, T, H, E, w_safe, logits, scores, choices, err);
+    router_select_kernel<<<(T + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, st>>>(
+        scores, choices, T, E, K, scaling, normalize, n_group, topk_group, idx, wts);
     return cudaGetLastError();
 }
 

@@ -65,7 +65,9 @@ struct nf_moe {
     int router_w_safe = 0;  // every nonzero router weight has |w| in [2^-67, 2^63)
 
     // workspace
-    float* logits = nullptr;
+    float* logits = nullptr;         // router logits, sigmoid scores and choices [Tm, E]
+    float* scores = nullptr;
+    float* choices = nullptr;
     int32_t* topk_idx = nullptr;
     float* topk_w = nullptr;
     PermuteBuffers pb{};
@@ -85,6 +87,21 @@ struct nf_moe {
     CUtensorMap tm_a{}, tm_bgu{}, tm_h{}, tm_bdn{}, tm_sgu{}, tm_shh{}, tm_sdn{};
     CUtensorMap tm_a_s{}, tm_h_s{}, tm_shh_s{};  // 32-row boxes of the A operands
     int last_tokens = 0;
+
+    // graph mode (nf_moe_set_graph_mode): captured forwards by argument set
+    struct GraphEntry {
+        const void* x;
+        const void* res;
+        void* y;
+        void* idx;
+        void* w;
+        int T;
+        cudaStream_t s;
+        cudaGraphExec_t exec;
+    };
+    static constexpr size_t kMaxGraphs = 16;
+    bool use_graphs = false;
+    std::vector<GraphEntry> graphs;
 
     // per-stage event profile: a ring of event sets (a begin and an end event
     // per stage, recorded on the stream the stage runs on), folded into
@@ -270,6 +287,7 @@ void nf_moe_destroy(nf_moe* h) {
     if (h->ev_fork) cudaEventDestroy(h->ev_fork);
     if (h->ev_join) cudaEventDestroy(h->ev_join);
     for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
+    for (auto& g : h->graphs) cudaGraphExecDestroy(g.exec);
     for (auto& a : h->allocs) cudaFree(a.p);
     cudaSetDevice(prev);
     delete h;
@@ -337,7 +355,8 @@ int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
     if (Is > 0) ok = ok && h->alloc(&h->ws_gu, blocked_bytes(2 * Is, 2 * H) / 2) && h->alloc(&h->ws_dn, blocked_bytes(H, 2 * Is) / 2);
     ok = ok && h->alloc(&h->alpha_g, E) && h->alloc(&h->alpha_u, E) && h->alloc(&h->alpha_d, E) &&
          h->alloc(&h->gs_g, E) && h->alloc(&h->gs_d, E);
-    ok = ok && h->alloc(&h->logits, Tm * E) && h->alloc(&h->topk_idx, Tm * K) && h->alloc(&h->topk_w, Tm * K);
+    ok = ok && h->alloc(&h->logits, Tm * E) && h->alloc(&h->scores, Tm * E) && h->alloc(&h->choices, Tm * E) &&
+         h->alloc(&h->topk_idx, Tm * K) && h->alloc(&h->topk_w, Tm * K);
     PermuteBuffers& b = h->pb;
     ok = ok && h->alloc(&b.chunk_counts, static_cast<int64_t>(h->nchunks_cap) * E) &&
          h->alloc(&b.chunk_base, static_cast<int64_t>(h->nchunks_cap) * E) && h->alloc(&b.counts, E) &&
@@ -602,8 +621,8 @@ int nf_moe_route(nf_moe* h, const uint16_t* x, int tokens, float* logits, int32_
     cudaSetDevice(h->device);
     const cudaError_t e = launch_router(x, h->router_w, h->router_bias, tokens, d.hidden, d.experts, d.top_k,
                                         d.routed_scaling, d.normalize, d.n_group, d.topk_group, h->router_w_safe,
-                                        logits ? logits : h->logits, idx ? idx : h->topk_idx, w ? w : h->topk_w,
-                                        h->dev_err, s);
+                                        logits ? logits : h->logits, h->scores, h->choices,
+                                        idx ? idx : h->topk_idx, w ? w : h->topk_w, h->dev_err, s);
     cudaSetDevice(prev);
     return e == cudaSuccess ? NF_OK : h->cuda_fail(e, "router launch");
 }
@@ -670,7 +689,7 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     }
     begin(NF_STAGE_ROUTER, s);
     e = launch_router(x, h->router_w, h->router_bias, T, H, E, K, d.routed_scaling, d.normalize, d.n_group,
-                      d.topk_group, h->router_w_safe, h->logits, idx, w, h->dev_err, s);
+                      d.topk_group, h->router_w_safe, h->logits, h->scores, h->choices, idx, w, h->dev_err, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "router launch");
     end(NF_STAGE_ROUTER, s);
     begin(NF_STAGE_PERMUTE, s);
@@ -773,6 +792,39 @@ int nf_moe_stage_times(nf_moe* h, float* ms_out, int* forwards) {
     return NF_OK;
 }
 
+// Graph mode: the forward's launches for one (buffers, tokens, stream)
+// combination are captured once into a CUDA graph and replayed, which
+// removes the per-kernel launch gaps that dominate small batches.
+static int forward_graph(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx, float* w,
+                         cudaStream_t s) {
+    for (auto& g : h->graphs)
+        if (g.x == x && g.res == residual && g.y == y && g.idx == idx && g.w == w && g.T == T && g.s == s) {
+            const cudaError_t e = cudaGraphLaunch(g.exec, s);
+            return e == cudaSuccess ? NF_OK : h->cuda_fail(e, "graph launch");
+        }
+    cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return h->cuda_fail(e, "stream capture");
+    const int st = forward_impl(h, x, residual, T, y, idx, w, s);
+    cudaGraph_t graph = nullptr;
+    e = cudaStreamEndCapture(s, &graph);
+    if (st != NF_OK) {
+        if (graph) cudaGraphDestroy(graph);
+        return st;
+    }
+    if (e != cudaSuccess) return h->cuda_fail(e, "stream capture");
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return h->cuda_fail(e, "graph instantiate");
+    if (h->graphs.size() >= nf_moe::kMaxGraphs) {
+        cudaGraphExecDestroy(h->graphs.front().exec);
+        h->graphs.erase(h->graphs.begin());
+    }
+    h->graphs.push_back({x, residual, y, idx, w, T, s, exec});
+    e = cudaGraphLaunch(exec, s);
+    return e == cudaSuccess ? NF_OK : h->cuda_fail(e, "graph launch");
+}
+
 int nf_moe_forward(nf_moe* h, const uint16_t* x, const float* residual, int tokens, float* y, int32_t* idx, float* w,
                    void* stream) {
     int st = check_forward_args(h, x, tokens);
@@ -782,9 +834,21 @@ int nf_moe_forward(nf_moe* h, const uint16_t* x, const float* residual, int toke
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
-    st = forward_impl(h, x, residual, tokens, y, idx, w, static_cast<cudaStream_t>(stream));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    // graphs need a capturable stream, no per-stage events, and a caller
+    // that is not capturing already
+    const bool graph = h->use_graphs && s != nullptr && !h->profiling &&
+                       cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone;
+    st = graph ? forward_graph(h, x, residual, tokens, y, idx, w, s) : forward_impl(h, x, residual, tokens, y, idx, w, s);
     cudaSetDevice(prev);
     return st;
+}
+
+int nf_moe_set_graph_mode(nf_moe* h, int enable) {
+    if (!h) return NF_ERR_INVALID;
+    h->use_graphs = enable != 0;
+    return NF_OK;
 }
 
 int nf_moe_sync(nf_moe* h, void* stream) {
@@ -821,7 +885,9 @@ int nf_moe_forward_host(nf_moe* h, const float* x_host, const float* res_host, i
         cudaSetDevice(prev);
         return h->cuda_fail(e, "host input copy");
     }
-    st = forward_impl(h, h->x_bf16, res_host ? h->res_f32 : nullptr, tokens, h->y_f32, nullptr, nullptr, s);
+    const float* res = res_host ? h->res_f32 : nullptr;
+    st = (h->use_graphs && !h->profiling) ? forward_graph(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s)
+                                          : forward_impl(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s);
     if (st == NF_OK) {
         e = cudaMemcpyAsync(y_host, h->y_f32, n * 4, cudaMemcpyDeviceToHost, s);
         if (e == cudaSuccess && idx_host) e = cudaMemcpyAsync(idx_host, h->topk_idx, nk * 4, cudaMemcpyDeviceToHost, s);

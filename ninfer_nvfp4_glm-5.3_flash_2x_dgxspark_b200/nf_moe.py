@@ -38,7 +38,7 @@ EXPORTED = [
     "nf_moe_create", "nf_moe_destroy", "nf_moe_last_error", "nf_status_string", "nf_moe_bind_nvfp4",
     "nf_moe_bind_bf16", "nf_moe_bind_f32", "nf_moe_finalize", "nf_moe_forward", "nf_moe_forward_host",
     "nf_moe_sync", "nf_moe_route", "nf_moe_debug_tensor", "nf_moe_debug_read", "nf_nvfp4_dequantize", "nf_nvfp4_quantize",
-    "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck",
+    "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck", "nf_moe_set_graph_mode",
 ]
 STAGES = ["router", "permute", "gate_up", "down", "shared", "combine"]
 
@@ -83,6 +83,7 @@ def load() -> ctypes.CDLL:
         "nf_nvfp4_quantize": ([P, I64, I64, F, P, P, P, P], I32),
         "nf_sigmoid_ref": ([P, I64, P, P], I32),
         "nf_moe_profile": ([P, I32], I32),
+        "nf_moe_set_graph_mode": ([P, I32], I32),
         "nf_format_selfcheck": ([ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64)], I32),
         "nf_moe_stage_times": ([P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(I32)], I32),
     }
@@ -243,6 +244,10 @@ class MoeLayer:
         n = ctypes.c_int64()
         self._check(self.lib.nf_moe_debug_tensor(self.h, DBG[which], ctypes.byref(p), ctypes.byref(n)))
         return p.value, n.value
+
+    def set_graph_mode(self, enable: bool) -> None:
+        """Capture forwards into CUDA graphs and replay them (needs a stream)."""
+        self._check(self.lib.nf_moe_set_graph_mode(self.h, int(enable)))
 
     def profile(self, enable: bool) -> None:
         """Start (and clear) or stop per-stage CUDA-event timing."""

@@ -164,3 +164,46 @@ def test_ragged_expert_sizes():
     assert np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
     assert_close(y, want_y, what="ragged")
     layer.close()
+
+
+def test_graph_mode_replays_bit_identical():
+    lay, x_bits = wl.config_layer("c1")
+    T, H, K = x_bits.shape[0], lay.hidden, lay.top_k
+    layer = make_layer(lay, T)
+    direct, _, _ = gpu_forward(layer, x_bits)
+    layer.set_graph_mode(True)
+    s = torch.cuda.Stream()
+    x = torch.from_numpy(x_bits.view(np.int16)).cuda()
+    y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    idx = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    outs = []
+    with torch.cuda.stream(s):
+        for _ in range(3):  # capture, then two replays
+            y.zero_()
+            layer.forward(x, y, T, None, idx, w, stream=s.cuda_stream)
+            layer.sync(s.cuda_stream)
+            outs.append(y.cpu().numpy().copy())
+    for o in outs:
+        assert np.array_equal(o.view(np.uint32), direct.view(np.uint32))
+    yh = layer.forward_host(wl.bf16_bits_to_f32(x_bits))  # host path through its own captured graph
+    assert np.array_equal(yh.view(np.uint32), direct.view(np.uint32))
+    layer.close()
+
+
+def test_nan_token_routes_like_reference():
+    """A NaN activation makes every logit NaN: the reference then keeps the
+    first unused expert at each pick (its strict '>' scan never moves)."""
+    lay, x_bits = wl.config_layer("c0")
+    x_bits = x_bits.copy()
+    x_bits[3, 17] = 0x7FC0  # BF16 NaN
+    layer = make_layer(lay, 16)
+    y, idx, w = gpu_forward(layer, x_bits)
+    _, want_idx, want_w = orc.route_tokens(lay, wl.bf16_bits_to_f32(x_bits))
+    assert np.array_equal(idx, want_idx)
+    assert list(idx[3]) == list(range(lay.top_k))
+    assert np.all(np.isnan(w[3])) and np.all(np.isnan(want_w[3]))
+    ok = np.ones(16, bool)
+    ok[3] = False
+    assert np.array_equal(w[ok].view(np.uint32), want_w[ok].view(np.uint32))
+    layer.close()
