@@ -473,12 +473,15 @@ int gemm_grid_size(int device) {
 template <int KIND, int EPI>
 static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb, const GemmArgs& args, int grid,
                               cudaStream_t st) {
-    static bool attr = false;
-    if (!attr) {
+    // the shared memory limit is an attribute of the kernel in each device's context
+    static bool attr[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (!attr[dev]) {
         const cudaError_t e =
             cudaFuncSetAttribute(gemm_kernel<KIND, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
-        attr = true;
+        attr[dev] = true;
     }
     gemm_kernel<KIND, EPI><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, tmb, args);
     return cudaGetLastError();

@@ -104,5 +104,8 @@ cudaError_t launch_format_selfcheck(unsigned long long* mismatches_dev, cudaStre
 cudaError_t prepare_device_tables();
 
 constexpr int kChunkTokHost = 128;  // tokens per permutation chunk (nf_kernels.cu kChunkTok)
+// Per-device one-time state (kernel attributes, lookup tables) is kept in
+// arrays of this many devices.
+constexpr int kMaxDevices = 64;
 
 }  // namespace nf

@@ -63,10 +63,10 @@ __global__ void sigmoid_ref_kernel(const float* __restrict__ x, int64_t n, float
 }
 
 cudaError_t prepare_device_tables() {
-    static int ready[64] = {0};
+    static int ready[kMaxDevices] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     if (ready[dev]) return cudaSuccess;
     sig_index_kernel<<<1024, 256>>>();
     cudaError_t e = cudaGetLastError();
@@ -727,12 +727,15 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* bia
                           float* scores, float* choices, int32_t* idx, float* wts, int* err, cudaStream_t st) {
     const int chunk = H < kRtMaxChunk ? H : kRtMaxChunk;
     const size_t smem = static_cast<size_t>(kRtExp + kRtTok) * (chunk * 2 + 16);
-    static bool attr = false;
-    if (!attr) {
+    // the shared memory limit is an attribute of the kernel in each device's context
+    static bool attr[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (!attr[dev]) {
         const cudaError_t e = cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    static_cast<int>((kRtExp + kRtTok) * (kRtMaxChunk * 2 + 16)));
         if (e != cudaSuccess) return e;
-        attr = true;
+        attr[dev] = true;
     }
     const dim3 grid((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp);
     router_logits_kernel<<<grid, kRtThreads, smem, st>>>(x, w, bias, T, H, E, w_safe, logits, scores, choices, err);
