@@ -225,6 +225,42 @@ NF_API int nf_sigmoid_ref(const float* x_dev, int64_t n, float* y_dev, void* str
  * counts (all 0 on a correct build).  Synchronous. */
 NF_API int nf_format_selfcheck(int64_t* e2m1_mismatches, int64_t* e4m3_mismatches, int64_t* bf16_mismatches);
 
+/* ---- router top-k without device allocation ------------------------------
+ * No counterpart in the reference: its router runs inside moe() on host
+ * buffers (src/text_forward.cpp:926-931).  This entry point is for callers
+ * that cannot allocate device memory and so cannot create an nf_moe handle
+ * (which owns weights and a workspace): a serving runtime whose memory pool
+ * reserved the device's free memory up front, a path where a cudaMalloc
+ * would synchronise the device, a process under a hard memory budget.
+ *
+ * Same routes as nf_moe_route (gemv_bf16 + router_select, bit-exact) from
+ * caller-owned device buffers; nothing is allocated: the intermediate
+ * logits, scores and choices live in a static device array compiled into
+ * the library (about 192 KB of every device the library is used on).
+ *   x_dev        BF16 [tokens, hidden], 16-byte aligned
+ *   router_w_dev BF16 [experts, hidden], 16-byte aligned (mlp.gate.weight)
+ *   bias_dev     F32  [experts] (mlp.gate.e_score_correction_bias)
+ *   topk_idx_dev INT32 [tokens, top_k];  topk_w_dev F32 [tokens, top_k]
+ *   msg, msg_len optional caller buffer that receives an error message
+ * Limits: tokens x experts <= NF_NOALLOC_MAX_SCORES (e.g. 256 tokens at 64
+ * experts); a larger call returns NF_ERR_CAPACITY before any device work.
+ * hidden a multiple of 8, experts <= 1024, top_k <= 32.
+ * The first call on a device does one-time set-up with that device current
+ * (it resolves the scratch array's address and builds the sigmoid lookup
+ * index, synchronising the device): make it before any stream capture.
+ * Later calls only enqueue work on `stream`.  Every call on a device uses
+ * the same scratch array, so calls that overlap in time (two streams, or two
+ * threads, with no ordering between them) race and give wrong routes: order
+ * them.  The chain always runs the separately rounded multiply and add (the
+ * caller's weights are not range-checked), slower than nf_moe_route on large
+ * batches.  If the logits stage gives up on its bounded wait, every
+ * topk_idx entry of the call is -1. */
+#define NF_NOALLOC_MAX_SCORES 16384
+NF_API int nf_router_topk_noalloc(const uint16_t* x_dev, const uint16_t* router_w_dev, const float* bias_dev, int tokens,
+                                  int hidden, int experts, int top_k, int n_group, int topk_group, int normalize,
+                                  float routed_scaling, int32_t* topk_idx_dev, float* topk_w_dev, char* msg,
+                                  int msg_len, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

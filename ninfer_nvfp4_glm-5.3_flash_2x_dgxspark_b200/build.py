@@ -27,7 +27,7 @@ OBJ = HERE / "_build"
 LIB = HERE / "lib" / "libnf_moe.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["nf_kernels.cu", "nf_gemm.cu", "nf_moe.cu"]
+CU_SOURCES = ["nf_kernels.cu", "nf_gemm.cu", "nf_moe.cu", "nf_noalloc.cu"]
 HEADERS = ["nf_common.cuh", "nf_internal.h"]
 
 

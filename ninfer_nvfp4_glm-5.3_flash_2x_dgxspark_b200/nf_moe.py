@@ -39,6 +39,7 @@ EXPORTED = [
     "nf_moe_bind_bf16", "nf_moe_bind_f32", "nf_moe_finalize", "nf_moe_forward", "nf_moe_forward_host",
     "nf_moe_sync", "nf_moe_route", "nf_moe_debug_tensor", "nf_moe_debug_read", "nf_nvfp4_dequantize", "nf_nvfp4_quantize",
     "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck", "nf_moe_set_graph_mode",
+    "nf_router_topk_noalloc",
 ]
 STAGES = ["router", "permute", "gate_up", "down", "shared", "combine"]
 
@@ -86,6 +87,8 @@ def load() -> ctypes.CDLL:
         "nf_moe_set_graph_mode": ([P, I32], I32),
         "nf_format_selfcheck": ([ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64)], I32),
         "nf_moe_stage_times": ([P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(I32)], I32),
+        "nf_router_topk_noalloc": ([P, P, P, I32, I32, I32, I32, I32, I32, I32, F, P, P, ctypes.c_char_p, I32, P],
+                                   I32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -279,6 +282,22 @@ def quantize(x_dev, rows: int, cols: int, input_scale: float, codes_dev, scales_
 
 def sigmoid_ref(x_dev, n: int, y_dev, stream=0) -> int:
     return load().nf_sigmoid_ref(_ptr(x_dev), n, _ptr(y_dev), stream or None)
+
+
+NOALLOC_MAX_SCORES = 16384  # tokens x experts of one nf_router_topk_noalloc call
+
+
+def router_topk_noalloc(x_dev, router_w_dev, bias_dev, tokens: int, hidden: int, experts: int, top_k: int,
+                        idx_dev, w_dev, *, n_group: int = 1, topk_group: int = 1, normalize: bool = True,
+                        routed_scaling: float = 1.0, stream=0) -> tuple[int, str]:
+    """Router top-k from caller device buffers with no device allocation
+    (the library's static scratch; calls must not overlap).  Returns
+    (status, message)."""
+    buf = ctypes.create_string_buffer(256)
+    st = load().nf_router_topk_noalloc(_ptr(x_dev), _ptr(router_w_dev), _ptr(bias_dev), tokens, hidden, experts,
+                                       top_k, n_group, topk_group, int(normalize), routed_scaling, _ptr(idx_dev),
+                                       _ptr(w_dev), buf, len(buf), stream or None)
+    return st, buf.value.decode()
 
 
 def format_selfcheck() -> tuple[int, int, int]:
