@@ -6,8 +6,9 @@
  * cites the reference interface it stands in for (file:line inside that
  * project).  The reference has no plugin or FFI layer: its MoE path is the
  * private member TextModel::moe, so the entry points below are the ones a
- * maintainer binds from the reference's C++ host (see INTEGRATION.md for the
- * binding).  Conventions:
+ * maintainer binds from the reference's C++ host (a handle per MoE layer,
+ * bound from the Store by checkpoint name, called from TextModel::moe).
+ * Conventions:
  *   - every call returns an int status (NF_OK == 0); no exception or C++
  *     type crosses the ABI; nf_moe_last_error() gives the message, worded
  *     like the reference's std::runtime_error messages;
@@ -135,6 +136,7 @@ NF_API int nf_moe_finalize(nf_moe* handle);
  *   x_dev        BF16 [tokens, H] (the rmsnorm_stash output, BF16-valued)
  *   residual_dev F32 [tokens, H] or NULL (NULL: y is the FFN branch alone)
  *   y_dev        F32 [tokens, H]
+ *   (x_dev, residual_dev and y_dev 16-byte aligned, else NF_ERR_LAYOUT)
  *   topk_idx_dev INT32 [tokens, top_k] or NULL (router_select indices)
  *   topk_w_dev   F32 [tokens, top_k] or NULL (router_select weights)
  * Asynchronous: a device-side failure (bounded wait timeout) is reported by

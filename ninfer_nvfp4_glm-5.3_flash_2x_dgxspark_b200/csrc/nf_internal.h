@@ -84,9 +84,35 @@ int gemm_grid_size(int device);
 // Launchers (nf_kernels.cu).
 // w_safe: every nonzero router weight has |w| in [2^-67, 2^63) (checked at
 // bind), which lets the exact logit chains use fused multiply-add.
-cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H, int E, int K,
-                          float scaling, int normalize, int n_group, int topk_group, int w_safe, float* logits,
-                          float* scores, float* choices, int32_t* idx, float* wts, int* err, cudaStream_t st);
+// w_chunked (may be NULL): the same weights in the fused router's chunk-major
+// layout (router_chunked_layout), which stages each K chunk of all experts
+// with one copy; NULL stages row by row from w.
+cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const uint16_t* w_chunked, const float* bias, int T,
+                          int H, int E, int K, float scaling, int normalize, int n_group, int topk_group, int w_safe,
+                          float* logits, float* scores, float* choices, int32_t* idx, float* wts, int* err,
+                          cudaStream_t st);
+
+// Fused router (E <= kRouterMaxE): K streams in chunks of kRouterKc elements;
+// a staged router row is kRouterPitch BF16 values (16 bytes of padding keep
+// the rows a warp reads in distinct shared-memory banks).
+constexpr int kRouterMaxE = 128;
+constexpr int kRouterKc = 256;
+constexpr int kRouterPitch = kRouterKc + 8;
+inline int64_t router_chunked_elems(int E, int H) {
+    return static_cast<int64_t>((H + kRouterKc - 1) / kRouterKc) * E * kRouterPitch;
+}
+// [E, H] -> [chunk][E][kRouterPitch], padding zero-filled (host side)
+inline void router_chunked_layout(const uint16_t* w, int E, int H, uint16_t* out) {
+    const int nchunks = (H + kRouterKc - 1) / kRouterKc;
+    for (int c = 0; c < nchunks; ++c)
+        for (int e = 0; e < E; ++e) {
+            uint16_t* dst = out + (static_cast<int64_t>(c) * E + e) * kRouterPitch;
+            for (int k = 0; k < kRouterPitch; ++k) {
+                const int col = c * kRouterKc + k;
+                dst[k] = (k < kRouterKc && col < H) ? w[static_cast<int64_t>(e) * H + col] : uint16_t(0);
+            }
+        }
+}
 cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
                            const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st);
 cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair_row, const float* topk_w,

@@ -221,17 +221,14 @@ __global__ void __launch_bounds__(kRtThreads) router_logits_kernel(const uint16_
 // ---------------------------------------------------------------------------
 constexpr int kSelectWarps = 4;
 
-__global__ void __launch_bounds__(kSelectWarps * 32) router_select_kernel(
-    const float* __restrict__ scores, const float* __restrict__ choices, int T, int E, int K, float scaling,
-    int normalize, int n_group, int topk_group, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * kSelectWarps + warp;
-    if (t >= T) return;
-    const float* score = scores + static_cast<int64_t>(t) * E;
-    const float* choice = choices + static_cast<int64_t>(t) * E;
+// One warp selects the top-k experts of one token from its scores and
+// choices (global or shared memory) and writes K indices and weights.
+// `excl` is a 32-word scratch of the warp (shared memory).
+__device__ __forceinline__ void warp_select(const float* score, const float* choice, int E, int K, float scaling,
+                                            int normalize, int n_group, int topk_group, uint32_t* excl,
+                                            int32_t* __restrict__ idx_row, float* __restrict__ w_row) {
+    const int lane = threadIdx.x & 31;
     // experts excluded by the group limit (computed by lane 0, rare path)
-    __shared__ uint32_t s_excl[kSelectWarps][32];  // E <= 1024 bits
-    uint32_t* excl = s_excl[warp];
     excl[lane] = 0u;
     __syncwarp();
     if (n_group > 1 && topk_group < n_group) {
@@ -315,9 +312,205 @@ __global__ void __launch_bounds__(kSelectWarps * 32) router_select_kernel(
         for (int p = 0; p < K; ++p) wts[p] = __fmul_rn(__fdiv_rn(wts[p], sum), scaling);
     }
     for (int p = 0; p < K; ++p) {
-        idx_out[static_cast<int64_t>(t) * K + p] = picks[p];
-        w_out[static_cast<int64_t>(t) * K + p] = wts[p];
+        idx_row[p] = picks[p];
+        w_row[p] = wts[p];
     }
+}
+
+__global__ void __launch_bounds__(kSelectWarps * 32) router_select_kernel(
+    const float* __restrict__ scores, const float* __restrict__ choices, int T, int E, int K, float scaling,
+    int normalize, int n_group, int topk_group, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
+    __shared__ uint32_t s_excl[kSelectWarps][32];  // E <= 1024 bits
+    const int warp = threadIdx.x >> 5;
+    const int t = blockIdx.x * kSelectWarps + warp;
+    if (t >= T) return;
+    warp_select(scores + static_cast<int64_t>(t) * E, choices + static_cast<int64_t>(t) * E, E, K, scaling, normalize,
+                n_group, topk_group, s_excl[warp], idx_out + static_cast<int64_t>(t) * K,
+                w_out + static_cast<int64_t>(t) * K);
+}
+
+// ---------------------------------------------------------------------------
+// Fused router for E <= 128 (every configuration of the benchmark): one CTA
+// owns `tc` tokens and all experts, so it runs the logits, the sigmoid, the
+// bias and the selection without a second launch or a round trip through
+// global memory.
+//
+// The K dimension streams through shared memory in chunks of kFzKc elements,
+// double-buffered with 1-D bulk copies (row pitch padded by 16 bytes: the 32
+// expert rows a warp reads fall in distinct banks).  Token rows are widened
+// to fp32 in shared memory once per chunk (with the range check that allows
+// the fused multiply-add), so a chain step is one broadcast load share, one
+// BF16 unpack of the weight and one FMA.  Thread (g, e) runs the chains of
+// expert e for the TPT tokens of group g: TPT = 1 keeps each warp on the
+// latency of its one chain (small batches: the chain of H dependent adds is
+// the floor); TPT = 4 amortises the weight unpack over four chains and keeps
+// the FP32 pipe busy (large batches: instruction issue is the bound).
+// ---------------------------------------------------------------------------
+constexpr int kFzThreads = 128;
+constexpr int kFzKc = kRouterKc;               // K elements per chunk
+constexpr int kFzPitch = kRouterPitch * 2;      // bytes per staged BF16 row
+constexpr int kFzXPitch = kFzKc * 4 + 16;       // bytes per widened fp32 token row
+constexpr int kFzMaxE = kRouterMaxE;
+constexpr int kFzXRegs = 4;                     // 16-byte token pieces a thread carries (tc <= 16)
+
+__host__ __device__ constexpr int fz_lanes(int E) { return (E + 31) & ~31; }
+__host__ __device__ constexpr int fz_tokens(int E, int tpt) { return (kFzThreads / fz_lanes(E)) * tpt; }
+__host__ __device__ constexpr size_t fz_smem(int E, int tpt) {
+    return static_cast<size_t>(2) * E * kFzPitch + static_cast<size_t>(fz_tokens(E, tpt)) * kFzXPitch;
+}
+
+template <bool kFma, int TPT>
+__device__ __forceinline__ void chain_fz(const uint4* __restrict__ wr, const float4* __restrict__ xr0, int xstride4,
+                                         int n8, float (&acc)[TPT]) {
+#pragma unroll 2
+    for (int q = 0; q < n8; ++q) {
+        const uint4 wv = wr[q];
+        const float wf[8] = {bf16_lo(wv.x), bf16_hi(wv.x), bf16_lo(wv.y), bf16_hi(wv.y),
+                             bf16_lo(wv.z), bf16_hi(wv.z), bf16_lo(wv.w), bf16_hi(wv.w)};
+#pragma unroll
+        for (int j = 0; j < TPT; ++j) {
+            const float4 a = xr0[j * xstride4 + 2 * q], b = xr0[j * xstride4 + 2 * q + 1];
+            const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                acc[j] = kFma ? fmaf(wf[i], xv[i], acc[j]) : __fadd_rn(acc[j], __fmul_rn(wf[i], xv[i]));
+        }
+    }
+}
+
+// Bounded wait of every thread on a stage barrier; false after the budget.
+__device__ __forceinline__ bool fz_wait(uint64_t* bar, uint32_t parity) {
+    const uint64_t start = globaltimer_ns();
+    while (!mbar_try_wait_sleep(bar, parity, 20000u))
+        if (globaltimer_ns() - start > NF_WAIT_BUDGET_NS) return false;
+    return true;
+}
+
+template <int TPT>
+__global__ void __launch_bounds__(kFzThreads) router_fused_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, const uint16_t* __restrict__ wz,
+    const float* __restrict__ bias, int T, int H, int E, int K, float scaling, int normalize, int n_group,
+    int topk_group, int w_safe, float* __restrict__ logits, int32_t* __restrict__ idx_out, float* __restrict__ w_out,
+    int* __restrict__ err) {
+    extern __shared__ __align__(128) uint8_t fz_smem_buf[];
+    __shared__ uint64_t full[2];
+    __shared__ uint32_t s_excl[kFzThreads / 32][32];
+    const int ew = fz_lanes(E), tg = kFzThreads / ew, tc = tg * TPT;
+    const int stage_bytes = E * kFzPitch;
+    uint8_t* xf = fz_smem_buf + 2 * stage_bytes;
+    const int t0 = blockIdx.x * tc;
+    const int nt = min(tc, T - t0);
+    const int e = threadIdx.x % ew, g = threadIdx.x / ew;
+    const bool active = e < E && g < tg;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nchunks = (H + kFzKc - 1) / kFzKc;
+    if (threadIdx.x == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    // warp 0 stages the router rows of chunk c into stage c & 1: one copy
+    // from the chunk-major layout, else one copy per row
+    auto issue_w = [&](int c) {
+        const int k0 = c * kFzKc, kc = min(kFzKc, H - k0);
+        uint8_t* st = fz_smem_buf + (c & 1) * stage_bytes;
+        if (wz) {
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[c & 1], static_cast<uint32_t>(E * kFzPitch));
+                bulk_load(st, wz + static_cast<int64_t>(c) * E * kRouterPitch, static_cast<uint32_t>(E * kFzPitch),
+                          &full[c & 1]);
+            }
+            return;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&full[c & 1], static_cast<uint32_t>(E * kc * 2));
+        __syncwarp();
+        for (int r = lane; r < E; r += 32)
+            bulk_load(st + r * kFzPitch, w + static_cast<int64_t>(r) * H + k0, static_cast<uint32_t>(kc * 2),
+                      &full[c & 1]);
+    };
+    // token rows travel through registers one chunk ahead: piece i of the
+    // chunk's tc x (kc / 8) grid of 16-byte pieces is loaded by thread
+    // i % kFzThreads (a warp reads one contiguous 512-byte row segment)
+    uint4 xv[kFzXRegs];
+    auto load_x = [&](int c) {
+        const int k0 = c * kFzKc, q8 = min(kFzKc, H - k0) / 8;
+#pragma unroll
+        for (int j = 0; j < kFzXRegs; ++j) {
+            const int i = threadIdx.x + j * kFzThreads, r = i / q8, q = i - r * q8;
+            xv[j] = make_uint4(0u, 0u, 0u, 0u);
+            if (i < tc * q8 && r < nt)
+                xv[j] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0 + r) * H + k0) + q);
+        }
+    };
+    if (warp == 0) {
+        issue_w(0);
+        if (nchunks > 1) issue_w(1);
+    }
+    load_x(0);
+    float acc[TPT];
+#pragma unroll
+    for (int j = 0; j < TPT; ++j) acc[j] = 0.f;
+    for (int c = 0; c < nchunks; ++c) {
+        const int s = c & 1, q8 = min(kFzKc, H - c * kFzKc) / 8;
+        const bool ok = fz_wait(&full[s], static_cast<uint32_t>((c >> 1) & 1));
+        if (!__syncthreads_and(ok)) {
+            // give up: record, let the copy still in flight land, leave
+            if (threadIdx.x == 0) {
+                atomicCAS(err, 0, NF_DEVERR_WAIT_FULL);
+                if (c + 1 < nchunks) fz_wait(&full[s ^ 1], static_cast<uint32_t>(((c + 1) >> 1) & 1));
+            }
+            return;
+        }
+        // widen this chunk's token rows to fp32 (rows past the batch are
+        // zero), check their range, then start loading the next chunk's
+        int unsafe = 0;
+#pragma unroll
+        for (int j = 0; j < kFzXRegs; ++j) {
+            const int i = threadIdx.x + j * kFzThreads;
+            if (i < tc * q8) {
+                const int r = i / q8, q = i - r * q8;
+                const uint4 u = xv[j];
+                unsafe |= (bf16x2_unsafe(u.x) | bf16x2_unsafe(u.y) | bf16x2_unsafe(u.z) | bf16x2_unsafe(u.w)) ? 1 : 0;
+                float4* dst = reinterpret_cast<float4*>(xf + r * kFzXPitch) + 2 * q;
+                dst[0] = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+                dst[1] = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
+            }
+        }
+        if (c + 1 < nchunks) load_x(c + 1);
+        // the barrier also publishes the widened rows: it runs whatever w_safe is
+        const int any_unsafe = __syncthreads_or(unsafe);
+        const bool use_fma = w_safe && !any_unsafe;
+        if (active) {
+            const uint4* wr = reinterpret_cast<const uint4*>(fz_smem_buf + s * stage_bytes + e * kFzPitch);
+            const float4* xr = reinterpret_cast<const float4*>(xf + g * TPT * kFzXPitch);
+            if (use_fma) chain_fz<true, TPT>(wr, xr, kFzXPitch / 16, q8, acc);
+            else chain_fz<false, TPT>(wr, xr, kFzXPitch / 16, q8, acc);
+        }
+        __syncthreads();  // stage s and the widened rows are free again
+        if (warp == 0 && c + 2 < nchunks) issue_w(c + 2);
+    }
+    // router_select's per-expert part (src/text_forward.cpp:1453-1456):
+    // score = sigmoid(logit), choice = score + correction bias
+    float* s_sc = reinterpret_cast<float*>(fz_smem_buf);  // [tc][ew]
+    float* s_ch = s_sc + tc * ew;
+    if (active) {
+        const float b = bias[e];
+#pragma unroll
+        for (int j = 0; j < TPT; ++j) {
+            const int t = g * TPT + j;
+            if (t < nt) {
+                const float sc = sigmoid_ref(acc[j]);
+                logits[static_cast<int64_t>(t0 + t) * E + e] = acc[j];
+                s_sc[t * ew + e] = sc;
+                s_ch[t * ew + e] = __fadd_rn(sc, b);
+            }
+        }
+    }
+    __syncthreads();
+    for (int t = warp; t < nt; t += kFzThreads / 32)
+        warp_select(s_sc + t * ew, s_ch + t * ew, E, K, scaling, normalize, n_group, topk_group, s_excl[warp],
+                    idx_out + static_cast<int64_t>(t0 + t) * K, w_out + static_cast<int64_t>(t0 + t) * K);
 }
 
 // ---------------------------------------------------------------------------
@@ -722,21 +915,47 @@ __global__ void quantize_kernel(const float* __restrict__ x, int64_t rows, int64
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
-cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H, int E, int K,
-                          float scaling, int normalize, int n_group, int topk_group, int w_safe, float* logits,
-                          float* scores, float* choices, int32_t* idx, float* wts, int* err, cudaStream_t st) {
-    const int chunk = H < kRtMaxChunk ? H : kRtMaxChunk;
-    const size_t smem = static_cast<size_t>(kRtExp + kRtTok) * (chunk * 2 + 16);
-    // the shared memory limit is an attribute of the kernel in each device's context
-    static bool attr[kMaxDevices] = {};
+// Sets a kernel's dynamic shared memory limit once per device.
+template <typename Kernel>
+static cudaError_t smem_attr_once(Kernel kernel, int bytes, bool (&done)[kMaxDevices]) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    if (!attr[dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   static_cast<int>((kRtExp + kRtTok) * (kRtMaxChunk * 2 + 16)));
-        if (e != cudaSuccess) return e;
-        attr[dev] = true;
+    if (done[dev]) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done[dev] = true;
+    return e;
+}
+
+cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const uint16_t* w_chunked, const float* bias, int T,
+                          int H, int E, int K, float scaling, int normalize, int n_group, int topk_group, int w_safe,
+                          float* logits, float* scores, float* choices, int32_t* idx, float* wts, int* err,
+                          cudaStream_t st) {
+    if (E <= kFzMaxE) {
+        // one chain per thread while the batch leaves SMs idle, four once
+        // there are several waves of CTAs
+        static bool attr1[kMaxDevices] = {}, attr4[kMaxDevices] = {};
+        const int ctas1 = (T + fz_tokens(E, 1) - 1) / fz_tokens(E, 1);
+        if (ctas1 < 4 * 148) {
+            const size_t smem = fz_smem(E, 1);
+            cudaError_t e = smem_attr_once(router_fused_kernel<1>, static_cast<int>(fz_smem(kFzMaxE, 1)), attr1);
+            if (e != cudaSuccess) return e;
+            router_fused_kernel<1><<<ctas1, kFzThreads, smem, st>>>(x, w, w_chunked, bias, T, H, E, K, scaling, normalize, n_group,
+                                                                    topk_group, w_safe, logits, idx, wts, err);
+        } else {
+            const size_t smem = fz_smem(E, 4);
+            cudaError_t e = smem_attr_once(router_fused_kernel<4>, static_cast<int>(fz_smem(kFzMaxE, 4)), attr4);
+            if (e != cudaSuccess) return e;
+            const int ctas = (T + fz_tokens(E, 4) - 1) / fz_tokens(E, 4);
+            router_fused_kernel<4><<<ctas, kFzThreads, smem, st>>>(x, w, w_chunked, bias, T, H, E, K, scaling, normalize, n_group,
+                                                                   topk_group, w_safe, logits, idx, wts, err);
+        }
+        return cudaGetLastError();
     }
+    const int chunk = H < kRtMaxChunk ? H : kRtMaxChunk;
+    const size_t smem = static_cast<size_t>(kRtExp + kRtTok) * (chunk * 2 + 16);
+    static bool attr[kMaxDevices] = {};
+    cudaError_t e = smem_attr_once(router_logits_kernel, static_cast<int>((kRtExp + kRtTok) * (kRtMaxChunk * 2 + 16)), attr);
+    if (e != cudaSuccess) return e;
     const dim3 grid((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp);
     router_logits_kernel<<<grid, kRtThreads, smem, st>>>(x, w, bias, T, H, E, w_safe, logits, scores, choices, err);
     router_select_kernel<<<(T + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, st>>>(

@@ -207,3 +207,20 @@ def test_nan_token_routes_like_reference():
     ok[3] = False
     assert np.array_equal(w[ok].view(np.uint32), want_w[ok].view(np.uint32))
     layer.close()
+
+
+def test_misaligned_buffers_are_rejected_before_any_launch():
+    lay, x_bits = wl.config_layer("c0")
+    T = x_bits.shape[0]
+    layer = m.MoeLayer(lay.hidden, lay.experts, lay.top_k, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                       swiglu_limit=lay.swiglu_limit, max_tokens=T)
+    layer.bind_layer(lay)
+    xbuf = torch.zeros(T * lay.hidden + 8, dtype=torch.int16, device="cuda")
+    y = torch.zeros((T, lay.hidden), dtype=torch.float32, device="cuda")
+    with pytest.raises(m.NfError, match="16-byte aligned"):
+        layer.forward(xbuf.data_ptr() + 2, y, T)   # x off by one BF16 element
+    ybuf = torch.zeros(T * lay.hidden + 4, dtype=torch.float32, device="cuda")
+    with pytest.raises(m.NfError, match="16-byte aligned"):
+        layer.forward(xbuf, ybuf.data_ptr() + 4, T)
+    layer.sync()
+    layer.close()

@@ -67,3 +67,34 @@ def test_router_group_limited():
     assert np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
     groups = idx // 8
     assert all(len(set(g)) <= 2 for g in groups)
+
+
+@pytest.mark.parametrize("experts,top_k", [(96, 6), (160, 6)])
+def test_router_wide_expert_counts(experts, top_k):
+    """96 experts: the fused kernel with three warps of expert lanes; 160: the
+    two-kernel path for more than 128 experts.  37 tokens: a ragged tail."""
+    cfg = dict(hidden=256, experts=experts, top_k=top_k, inter=128, shared_inter=128, scaling=1.5, tokens=37)
+    lay = wl.make_layer(cfg, seed=11)
+    x_bits = wl.make_tokens(cfg, seed=11)
+    lg, idx, w = run_router(lay, x_bits)
+    want_lg, want_idx, want_w = orc.route_tokens(lay, wl.bf16_bits_to_f32(x_bits))
+    assert np.array_equal(lg.view(np.uint32), want_lg.view(np.uint32))
+    assert np.array_equal(idx, want_idx)
+    assert np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
+
+
+def test_router_rows_outside_the_exact_product_range():
+    """Token values whose products with the weights leave fp32's exact range
+    (huge, tiny, infinite) take the separately rounded multiply-add; the
+    results still match the reference bit for bit."""
+    lay, x_bits = wl.config_layer("c1")
+    x_bits = x_bits.copy()
+    x_bits[3] = (x_bits[3].astype(np.uint32) + (80 << 7)).astype(np.uint16)  # x 2^80
+    x_bits[5, 10] = 0x0d00                                                      # 2^-101
+    x_bits[9, 7] = 0x7f80                                                       # +inf
+    x_bits[60, 2047] = 0x0001                                                   # BF16 subnormal
+    lg, idx, w = run_router(lay, x_bits)
+    want_lg, want_idx, want_w = orc.route_tokens(lay, wl.bf16_bits_to_f32(x_bits))
+    assert np.array_equal(lg.view(np.uint32), want_lg.view(np.uint32))
+    assert np.array_equal(idx, want_idx)
+    assert np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
