@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cstring>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -84,31 +85,46 @@ int gemm_grid_size(int device);
 // Launchers (nf_kernels.cu).
 // w_safe: every nonzero router weight has |w| in [2^-67, 2^63) (checked at
 // bind), which lets the exact logit chains use fused multiply-add.
-// w_chunked (may be NULL): the same weights in the fused router's chunk-major
-// layout (router_chunked_layout), which stages each K chunk of all experts
-// with one copy; NULL stages row by row from w.
-cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const uint16_t* w_chunked, const float* bias, int T,
-                          int H, int E, int K, float scaling, int normalize, int n_group, int topk_group, int w_safe,
-                          float* logits, float* scores, float* choices, int32_t* idx, float* wts, int* err,
-                          cudaStream_t st);
+// Router weights in the fused router's chunk-major layouts (may be NULL):
+// w_chunked32 (fp32, router_chunked_layout) for large batches, w_chunked16
+// (BF16, router_chunked_layout16) for small ones.  With NULL the general
+// two-kernel router runs on w.
+cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* w_chunked32, const uint16_t* w_chunked16,
+                          const float* bias, int T, int H, int E, int K, float scaling, int normalize, int n_group,
+                          int topk_group, int w_safe, float* logits, float* scores, float* choices, int32_t* idx,
+                          float* wts, int* err, cudaStream_t st);
 
-// Fused router (E <= kRouterMaxE): K streams in chunks of kRouterKc elements;
-// a staged router row is kRouterPitch BF16 values (16 bytes of padding keep
-// the rows a warp reads in distinct shared-memory banks).
+// Fused router (E <= kRouterMaxE, H % kRouterKc == 0): K streams in chunks of
+// kRouterKc elements; a staged router row is kRouterPitch fp32 values or
+// kRouterPitch16 BF16 values (16 bytes of padding keep the rows a warp reads
+// in distinct shared-memory banks).
 constexpr int kRouterMaxE = 128;
-constexpr int kRouterKc = 256;
-constexpr int kRouterPitch = kRouterKc + 8;
-inline int64_t router_chunked_elems(int E, int H) {
-    return static_cast<int64_t>((H + kRouterKc - 1) / kRouterKc) * E * kRouterPitch;
-}
-// [E, H] -> [chunk][E][kRouterPitch], padding zero-filled (host side)
-inline void router_chunked_layout(const uint16_t* w, int E, int H, uint16_t* out) {
-    const int nchunks = (H + kRouterKc - 1) / kRouterKc;
-    for (int c = 0; c < nchunks; ++c)
+constexpr int kRouterKc = 128;
+constexpr int kRouterPitch = kRouterKc + 4;
+constexpr int kRouterPitch16 = kRouterKc + 8;
+inline int64_t router_chunks(int H) { return (H + kRouterKc - 1) / kRouterKc; }
+inline int64_t router_chunked_elems(int E, int H) { return router_chunks(H) * E * kRouterPitch; }
+inline int64_t router_chunked_elems16(int E, int H) { return router_chunks(H) * E * kRouterPitch16; }
+// BF16 [E, H] -> fp32 [chunk][E][kRouterPitch], padding zero (host side)
+inline void router_chunked_layout(const uint16_t* w, int E, int H, float* out) {
+    for (int64_t c = 0; c < router_chunks(H); ++c)
         for (int e = 0; e < E; ++e) {
-            uint16_t* dst = out + (static_cast<int64_t>(c) * E + e) * kRouterPitch;
+            float* dst = out + (c * E + e) * kRouterPitch;
             for (int k = 0; k < kRouterPitch; ++k) {
-                const int col = c * kRouterKc + k;
+                const int64_t col = c * kRouterKc + k;
+                uint32_t bits = 0u;
+                if (k < kRouterKc && col < H) bits = static_cast<uint32_t>(w[static_cast<int64_t>(e) * H + col]) << 16;
+                std::memcpy(dst + k, &bits, sizeof(float));
+            }
+        }
+}
+// BF16 [E, H] -> BF16 [chunk][E][kRouterPitch16], padding zero (host side)
+inline void router_chunked_layout16(const uint16_t* w, int E, int H, uint16_t* out) {
+    for (int64_t c = 0; c < router_chunks(H); ++c)
+        for (int e = 0; e < E; ++e) {
+            uint16_t* dst = out + (c * E + e) * kRouterPitch16;
+            for (int k = 0; k < kRouterPitch16; ++k) {
+                const int64_t col = c * kRouterKc + k;
                 dst[k] = (k < kRouterKc && col < H) ? w[static_cast<int64_t>(e) * H + col] : uint16_t(0);
             }
         }

@@ -14,11 +14,14 @@ namespace nf {
 
 // ---------------------------------------------------------------------------
 // Sigmoid exactly as the reference computes it (src/text_forward.cpp:42-49).
-// exp is evaluated in double and rounded once (a correctly rounded expf);
-// the arguments where libm's expf gives a different sigmoid come from the
-// build-time exception table, found through a 2^20-bucket index over the
-// key bits (bucket = bits >> 12; at most a few dozen keys, one or two cache
-// lines, per bucket).
+// exp is evaluated in double and rounded once (a correctly rounded expf).
+// libm's expf can only differ from that next to a float rounding boundary,
+// so the arguments whose exp lies within a relative NF_SIG_NEAR_EPS of one
+// (checked by rounding the double value nudged both ways) look themselves up
+// in the build-time exception table, found through a 2^20-bucket index over
+// the key bits (bucket = bits >> 12; at most a few dozen keys, one or two
+// cache lines, per bucket).  The generator proves that every table entry is
+// caught by this screen.
 // ---------------------------------------------------------------------------
 constexpr int kSigBucketShift = 12;
 constexpr int kSigBuckets = 1 << (32 - kSigBucketShift);
@@ -39,21 +42,22 @@ __global__ void sig_index_kernel() {
     }
 }
 
-__device__ __forceinline__ float sigmoid_ref(float x) {
-    float r;
-    if (x >= 0.f) {
-        const float z = static_cast<float>(exp(-static_cast<double>(x)));
-        r = __fdiv_rn(1.f, __fadd_rn(1.f, z));
-    } else {
-        const float z = static_cast<float>(exp(static_cast<double>(x)));
-        r = __fdiv_rn(z, __fadd_rn(1.f, z));
-    }
+__device__ __noinline__ float sigmoid_lookup(float x, float r) {
     const uint32_t key = __float_as_uint(x);
     const uint32_t b = key >> kSigBucketShift;
     const uint32_t hi = g_sig_index[b + 1];
     for (uint32_t j = g_sig_index[b]; j < hi; ++j)
         if (g_sig_keys[j] == key) return __uint_as_float(g_sig_vals[j]);
     return r;
+}
+
+__device__ __forceinline__ float sigmoid_ref(float x) {
+    const double zd = exp(x >= 0.f ? -static_cast<double>(x) : static_cast<double>(x));
+    const float z = __double2float_rn(zd);
+    const float r = x >= 0.f ? __fdiv_rn(1.f, __fadd_rn(1.f, z)) : __fdiv_rn(z, __fadd_rn(1.f, z));
+    const bool near = !(zd > NF_SIG_TINY) || __double2float_rn(zd * (1.0 + NF_SIG_NEAR_EPS)) != z ||
+                      __double2float_rn(zd * (1.0 - NF_SIG_NEAR_EPS)) != z;
+    return near ? sigmoid_lookup(x, r) : r;
 }
 
 __global__ void sigmoid_ref_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ y) {
@@ -329,188 +333,405 @@ __global__ void __launch_bounds__(kSelectWarps * 32) router_select_kernel(
                 w_out + static_cast<int64_t>(t) * K);
 }
 
+// One thread selects the top-k experts of one token, scanning its choices
+// (shared memory) in expert order exactly as router_select does: each pick
+// starts from the first unused expert and moves on a strict '>' only (lowest
+// index wins ties, a NaN first choice is kept, later NaNs are never taken).
+// The group limit, when on, first marks the experts of the groups that lose.
+// `used` is a per-token byte scratch of E entries.
+__device__ __forceinline__ void thread_select(const float* score, const float* choice, int E, int K, float scaling,
+                                              int normalize, int n_group, int topk_group, uint8_t* used,
+                                              int32_t* __restrict__ idx_row, float* __restrict__ w_row) {
+    const bool grouped = n_group > 1 && topk_group < n_group;
+    const int per = grouped ? E / n_group : E;
+    uint32_t keep = 0xffffffffu;
+    if (grouped) {
+        keep = 0u;
+        for (int r = 0; r < topk_group; ++r) {
+            int best = -1;
+            float best_score = 0.f;
+            for (int gi = 0; gi < n_group; ++gi) {
+                if (keep & (1u << gi)) continue;
+                float b1 = -INFINITY, b2 = -INFINITY;
+                for (int j = 0; j < per; ++j) {
+                    const float c = choice[gi * per + j];
+                    if (c > b1) {
+                        b2 = b1;
+                        b1 = c;
+                    } else if (c > b2) {
+                        b2 = c;
+                    }
+                }
+                const float sg = per >= 2 ? __fadd_rn(b1, b2) : b1;
+                if (best < 0 || sg > best_score) {
+                    best = gi;
+                    best_score = sg;
+                }
+            }
+            keep |= 1u << best;
+        }
+    }
+    for (int e = 0; e < E; ++e) used[e] = grouped ? static_cast<uint8_t>(((keep >> (e / per)) & 1u) ^ 1u) : 0;
+    int picks[32];
+    float wts[32];
+    for (int p = 0; p < K; ++p) {
+        int best = -1;
+        float bc = 0.f;
+        for (int e = 0; e < E; ++e) {
+            if (used[e]) continue;
+            const float c = choice[e];
+            if (best < 0 || c > bc) {
+                best = e;
+                bc = c;
+            }
+        }
+        best = max(best, 0);
+        used[best] = 1;
+        picks[p] = best;
+        wts[p] = score[best];
+    }
+    if (normalize) {
+        float sum = 1e-20f;
+        for (int p = 0; p < K; ++p) sum = __fadd_rn(sum, wts[p]);
+        for (int p = 0; p < K; ++p) wts[p] = __fmul_rn(__fdiv_rn(wts[p], sum), scaling);
+    }
+    for (int p = 0; p < K; ++p) {
+        idx_row[p] = picks[p];
+        w_row[p] = wts[p];
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Fused router for E <= 128 (every configuration of the benchmark): one CTA
 // owns `tc` tokens and all experts, so it runs the logits, the sigmoid, the
 // bias and the selection without a second launch or a round trip through
 // global memory.
 //
-// The K dimension streams through shared memory in chunks of kFzKc elements,
-// double-buffered with 1-D bulk copies (row pitch padded by 16 bytes: the 32
-// expert rows a warp reads fall in distinct banks).  Token rows are widened
-// to fp32 in shared memory once per chunk (with the range check that allows
-// the fused multiply-add), so a chain step is one broadcast load share, one
-// BF16 unpack of the weight and one FMA.  Thread (g, e) runs the chains of
-// expert e for the TPT tokens of group g: TPT = 1 keeps each warp on the
-// latency of its one chain (small batches: the chain of H dependent adds is
-// the floor); TPT = 4 amortises the weight unpack over four chains and keeps
-// the FP32 pipe busy (large batches: instruction issue is the bound).
+// Warp-specialised.  The router rows stream through a ring of NS shared-
+// memory slots: the producer warp copies the chunk of every row with one bulk
+// copy per stage (rows laid out chunk-major at bind, 16 bytes of padding per
+// row so the rows a warp reads fall in distinct banks), and the consumer warps
+// run the chains without a CTA-wide barrier -- a slot is handed over by its
+// `full` mbarrier and handed back by `empty`.  A bulk copy costs a fixed
+// latency of several hundred cycles on top of its bytes, so each stage is one
+// large copy and token rows never travel by bulk copy:
+//   - small batches (kXRes): the CTA's few token rows are loaded once with
+//     coalesced loads by every thread, range-checked and widened to fp32 in
+//     shared memory for the whole of H; one chain per thread over BF16 router
+//     rows (half the bytes to stream; the unpack is free next to the chain of
+//     H dependent adds, which is the floor), loads four groups ahead.
+//   - large batches: the producer lanes load the next stage's token rows into
+//     registers while the consumers work, then widen them into the stage's
+//     slot; 8 tokens x 2 experts per consumer thread over fp32 router rows,
+//     64 independent FMAs per 10 loads (2 distinct rows, 8 broadcasts).
 // ---------------------------------------------------------------------------
-constexpr int kFzThreads = 128;
-constexpr int kFzKc = kRouterKc;               // K elements per chunk
-constexpr int kFzPitch = kRouterPitch * 2;      // bytes per staged BF16 row
-constexpr int kFzXPitch = kFzKc * 4 + 16;       // bytes per widened fp32 token row
+constexpr int kFzConsumers = 4;                    // consumer warps
+constexpr int kFzCThreads = kFzConsumers * 32;
+constexpr int kFzKc = kRouterKc;                   // K elements per chunk
+constexpr int kFzXPitch = kFzKc * 4 + 16;          // bytes per widened token row chunk
 constexpr int kFzMaxE = kRouterMaxE;
-constexpr int kFzXRegs = 4;                     // 16-byte token pieces a thread carries (tc <= 16)
+constexpr int kFzMaxResH = 4096;                   // resident token rows: H limit
 
-__host__ __device__ constexpr int fz_lanes(int E) { return (E + 31) & ~31; }
-__host__ __device__ constexpr int fz_tokens(int E, int tpt) { return (kFzThreads / fz_lanes(E)) * tpt; }
-__host__ __device__ constexpr size_t fz_smem(int E, int tpt) {
-    return static_cast<size_t>(2) * E * kFzPitch + static_cast<size_t>(fz_tokens(E, tpt)) * kFzXPitch;
+__host__ __device__ constexpr int fz_group_threads(int E, int ept) { return ((E + 32 * ept - 1) / (32 * ept)) * 32; }
+__host__ __device__ constexpr int fz_tokens(int E, int ept, int tpt) { return (kFzCThreads / fz_group_threads(E, ept)) * tpt; }
+__host__ __device__ constexpr int fz_wpitch(bool w16) { return w16 ? kRouterPitch16 * 2 : kRouterPitch * 4; }
+// kXRes: slot = SUB router chunks; token rows resident after the ring
+// (tc rows of H fp32, + 16 bytes).  Else: slot = router chunk + widened token chunk.
+__host__ __device__ constexpr size_t fz_slot(int E, int ept, int tpt, int sub, bool w16, bool xres) {
+    return static_cast<size_t>(sub) * E * fz_wpitch(w16) +
+           (xres ? 0 : static_cast<size_t>(fz_tokens(E, ept, tpt)) * kFzXPitch);
+}
+__host__ __device__ constexpr size_t fz_smem(int E, int ept, int tpt, int sub, int ns, bool w16, bool xres, int H) {
+    return ns * fz_slot(E, ept, tpt, sub, w16, xres) +
+           (xres ? static_cast<size_t>(fz_tokens(E, ept, tpt)) * (static_cast<size_t>(H) * 4 + 16) : 0);
 }
 
-template <bool kFma, int TPT>
-__device__ __forceinline__ void chain_fz(const uint4* __restrict__ wr, const float4* __restrict__ xr0, int xstride4,
-                                         int n8, float (&acc)[TPT]) {
-#pragma unroll 2
-    for (int q = 0; q < n8; ++q) {
-        const uint4 wv = wr[q];
-        const float wf[8] = {bf16_lo(wv.x), bf16_hi(wv.x), bf16_lo(wv.y), bf16_hi(wv.y),
-                             bf16_lo(wv.z), bf16_hi(wv.z), bf16_lo(wv.w), bf16_hi(wv.w)};
+template <bool kFma>
+__device__ __forceinline__ float fz_step(float acc, float w, float x) {
+    return kFma ? fmaf(w, x, acc) : __fadd_rn(acc, __fmul_rn(w, x));
+}
+
+// One chain over one chunk of BF16 router weights (8 per 16-byte load) and
+// widened tokens, loads kAhead groups ahead in a register ring.
+template <bool kFma>
+__device__ __forceinline__ float chain_fz16(const uint4* __restrict__ wr, const float4* __restrict__ xr, float a) {
+    constexpr int kN8 = kFzKc / 8, kAhead = 4;
+    uint4 wq[kAhead];
+    float4 xq[kAhead][2];
 #pragma unroll
-        for (int j = 0; j < TPT; ++j) {
-            const float4 a = xr0[j * xstride4 + 2 * q], b = xr0[j * xstride4 + 2 * q + 1];
-            const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    for (int i = 0; i < kAhead; ++i) {
+        wq[i] = wr[i];
+        xq[i][0] = xr[2 * i];
+        xq[i][1] = xr[2 * i + 1];
+    }
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                acc[j] = kFma ? fmaf(wf[i], xv[i], acc[j]) : __fadd_rn(acc[j], __fmul_rn(wf[i], xv[i]));
+    for (int q = 0; q < kN8; ++q) {
+        const uint4 wv = wq[q % kAhead];
+        const float4 xa = xq[q % kAhead][0], xb = xq[q % kAhead][1];
+        if (q + kAhead < kN8) {
+            wq[q % kAhead] = wr[q + kAhead];
+            xq[q % kAhead][0] = xr[2 * (q + kAhead)];
+            xq[q % kAhead][1] = xr[2 * (q + kAhead) + 1];
         }
+        a = fz_step<kFma>(a, bf16_lo(wv.x), xa.x);
+        a = fz_step<kFma>(a, bf16_hi(wv.x), xa.y);
+        a = fz_step<kFma>(a, bf16_lo(wv.y), xa.z);
+        a = fz_step<kFma>(a, bf16_hi(wv.y), xa.w);
+        a = fz_step<kFma>(a, bf16_lo(wv.z), xb.x);
+        a = fz_step<kFma>(a, bf16_hi(wv.z), xb.y);
+        a = fz_step<kFma>(a, bf16_lo(wv.w), xb.z);
+        a = fz_step<kFma>(a, bf16_hi(wv.w), xb.w);
+    }
+    return a;
+}
+
+// TPT x EPT chains over one chunk of fp32 router weights and widened tokens.
+template <bool kFma, int EPT, int TPT>
+__device__ __forceinline__ void chain_fz32(const float4* const (&wr)[EPT], const float4* __restrict__ xr,
+                                           float (&acc)[TPT][EPT]) {
+    constexpr int kN4 = kFzKc / 4, kXs = kFzXPitch / 16;
+#pragma unroll 4
+    for (int q = 0; q < kN4; ++q) {
+        float4 wv[EPT], xv[TPT];
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) wv[j] = wr[j][q];
+#pragma unroll
+        for (int t = 0; t < TPT; ++t) xv[t] = xr[t * kXs + q];
+#pragma unroll
+        for (int t = 0; t < TPT; ++t)
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) acc[t][j] = fz_step<kFma>(acc[t][j], wv[j].x, xv[t].x);
+#pragma unroll
+        for (int t = 0; t < TPT; ++t)
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) acc[t][j] = fz_step<kFma>(acc[t][j], wv[j].y, xv[t].y);
+#pragma unroll
+        for (int t = 0; t < TPT; ++t)
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) acc[t][j] = fz_step<kFma>(acc[t][j], wv[j].z, xv[t].z);
+#pragma unroll
+        for (int t = 0; t < TPT; ++t)
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) acc[t][j] = fz_step<kFma>(acc[t][j], wv[j].w, xv[t].w);
     }
 }
 
-// Bounded wait of every thread on a stage barrier; false after the budget.
-__device__ __forceinline__ bool fz_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait on a slot barrier that also gives up once the CTA aborted.
+__device__ __forceinline__ bool fz_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = globaltimer_ns();
-    while (!mbar_try_wait_sleep(bar, parity, 20000u))
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
+        if (abort && *abort) return false;
         if (globaltimer_ns() - start > NF_WAIT_BUDGET_NS) return false;
-    return true;
+    }
 }
 
-template <int TPT>
-__global__ void __launch_bounds__(kFzThreads) router_fused_kernel(
-    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, const uint16_t* __restrict__ wz,
-    const float* __restrict__ bias, int T, int H, int E, int K, float scaling, int normalize, int n_group,
-    int topk_group, int w_safe, float* __restrict__ logits, int32_t* __restrict__ idx_out, float* __restrict__ w_out,
-    int* __restrict__ err) {
+__device__ __forceinline__ int bf16x8_unsafe(uint4 u) {
+    return (bf16x2_unsafe(u.x) | bf16x2_unsafe(u.y) | bf16x2_unsafe(u.z) | bf16x2_unsafe(u.w)) ? 1 : 0;
+}
+
+template <int EPT, int TPT, int SUB, int NS, int PW, bool kW16, bool kXRes>
+__global__ void __launch_bounds__(kFzCThreads + 32 * PW, 1) router_fused_kernel(
+    const uint16_t* __restrict__ x, const void* __restrict__ wz, const float* __restrict__ bias, int T, int H, int E,
+    int K, float scaling, int normalize, int n_group, int topk_group, int w_safe, float* __restrict__ logits,
+    int32_t* __restrict__ idx_out, float* __restrict__ w_out, int* __restrict__ err) {
+    static_assert(!kW16 || (EPT == 1 && TPT == 1), "BF16 staging serves the one-chain form");
+    static_assert(!kXRes || (EPT == 1 && TPT == 1), "resident token rows serve small batches");
+    static_assert(kXRes || SUB == 1, "streamed token rows come one chunk per stage");
+    constexpr int kThreads = kFzCThreads + 32 * PW;       // consumers + PW producer warps
+    constexpr int kXRegs = 16 / PW;  // token pieces a producer thread carries per stage (tc <= 32)
     extern __shared__ __align__(128) uint8_t fz_smem_buf[];
-    __shared__ uint64_t full[2];
-    __shared__ uint32_t s_excl[kFzThreads / 32][32];
-    const int ew = fz_lanes(E), tg = kFzThreads / ew, tc = tg * TPT;
-    const int stage_bytes = E * kFzPitch;
-    uint8_t* xf = fz_smem_buf + 2 * stage_bytes;
-    const int t0 = blockIdx.x * tc;
-    const int nt = min(tc, T - t0);
-    const int e = threadIdx.x % ew, g = threadIdx.x / ew;
-    const bool active = e < E && g < tg;
+    __shared__ uint64_t full[NS], empty[NS];
+    __shared__ int s_unsafe[NS][PW];
+    __shared__ int s_abort, s_x_unsafe;
+    const int gt = fz_group_threads(E, EPT), tg = kFzCThreads / gt, tc = tg * TPT;
+    const int wchunk = E * fz_wpitch(kW16);
+    const int wbytes = SUB * wchunk;  // router bytes per stage
+    const int slot_bytes = static_cast<int>(fz_slot(E, EPT, TPT, SUB, kW16, kXRes));
+    const int t0 = blockIdx.x * tc, nt = min(tc, T - t0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nchunks = (H + kFzKc - 1) / kFzKc;
+    const int nchunks = H / kFzKc, nstages = (nchunks + SUB - 1) / SUB;
+    const int xres_pitch = H * 4 + 16;
+    uint8_t* xres = fz_smem_buf + NS * slot_bytes;
     if (threadIdx.x == 0) {
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
+#pragma unroll
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&full[i], kXRes ? 1 : 32 * PW);
+            mbar_init(&empty[i], kFzConsumers);
+        }
+        s_abort = 0;
+        s_x_unsafe = 0;
         fence_barrier_init();
     }
     __syncthreads();
-    // warp 0 stages the router rows of chunk c into stage c & 1: one copy
-    // from the chunk-major layout, else one copy per row
-    auto issue_w = [&](int c) {
-        const int k0 = c * kFzKc, kc = min(kFzKc, H - k0);
-        uint8_t* st = fz_smem_buf + (c & 1) * stage_bytes;
-        if (wz) {
-            if (lane == 0) {
-                mbar_arrive_expect_tx(&full[c & 1], static_cast<uint32_t>(E * kFzPitch));
-                bulk_load(st, wz + static_cast<int64_t>(c) * E * kRouterPitch, static_cast<uint32_t>(E * kFzPitch),
-                          &full[c & 1]);
+    if constexpr (kXRes) {
+        // the first router copies go out at once, then every thread widens
+        // the resident token rows (zero past the batch)
+        if (threadIdx.x == kFzCThreads)
+            for (int c = 0; c < NS && c < nstages; ++c) {
+                const int bytes = min(SUB, nchunks - c * SUB) * wchunk;
+                mbar_arrive_expect_tx(&full[c], static_cast<uint32_t>(bytes));
+                bulk_load(fz_smem_buf + c * slot_bytes, static_cast<const uint8_t*>(wz) + static_cast<int64_t>(c) * wbytes,
+                          static_cast<uint32_t>(bytes), &full[c]);
             }
-            return;
-        }
-        if (lane == 0) mbar_arrive_expect_tx(&full[c & 1], static_cast<uint32_t>(E * kc * 2));
-        __syncwarp();
-        for (int r = lane; r < E; r += 32)
-            bulk_load(st + r * kFzPitch, w + static_cast<int64_t>(r) * H + k0, static_cast<uint32_t>(kc * 2),
-                      &full[c & 1]);
-    };
-    // token rows travel through registers one chunk ahead: piece i of the
-    // chunk's tc x (kc / 8) grid of 16-byte pieces is loaded by thread
-    // i % kFzThreads (a warp reads one contiguous 512-byte row segment)
-    uint4 xv[kFzXRegs];
-    auto load_x = [&](int c) {
-        const int k0 = c * kFzKc, q8 = min(kFzKc, H - k0) / 8;
-#pragma unroll
-        for (int j = 0; j < kFzXRegs; ++j) {
-            const int i = threadIdx.x + j * kFzThreads, r = i / q8, q = i - r * q8;
-            xv[j] = make_uint4(0u, 0u, 0u, 0u);
-            if (i < tc * q8 && r < nt)
-                xv[j] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0 + r) * H + k0) + q);
-        }
-    };
-    if (warp == 0) {
-        issue_w(0);
-        if (nchunks > 1) issue_w(1);
-    }
-    load_x(0);
-    float acc[TPT];
-#pragma unroll
-    for (int j = 0; j < TPT; ++j) acc[j] = 0.f;
-    for (int c = 0; c < nchunks; ++c) {
-        const int s = c & 1, q8 = min(kFzKc, H - c * kFzKc) / 8;
-        const bool ok = fz_wait(&full[s], static_cast<uint32_t>((c >> 1) & 1));
-        if (!__syncthreads_and(ok)) {
-            // give up: record, let the copy still in flight land, leave
-            if (threadIdx.x == 0) {
-                atomicCAS(err, 0, NF_DEVERR_WAIT_FULL);
-                if (c + 1 < nchunks) fz_wait(&full[s ^ 1], static_cast<uint32_t>(((c + 1) >> 1) & 1));
-            }
-            return;
-        }
-        // widen this chunk's token rows to fp32 (rows past the batch are
-        // zero), check their range, then start loading the next chunk's
         int unsafe = 0;
+        const int q8 = H / 8;
+        for (int i = threadIdx.x; i < tc * q8; i += kThreads) {
+            const int r = i / q8, q = i - r * q8;
+            uint4 u = make_uint4(0u, 0u, 0u, 0u);
+            if (r < nt) u = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0 + r) * H) + q);
+            unsafe |= bf16x8_unsafe(u);
+            float4* dst = reinterpret_cast<float4*>(xres + r * xres_pitch) + 2 * q;
+            dst[0] = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+            dst[1] = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
+        }
+        if (__syncthreads_or(unsafe) && threadIdx.x == 0) s_x_unsafe = 1;
+        __syncthreads();
+    }
+    const int el = threadIdx.x % gt, g = threadIdx.x / gt;
+    const bool active = warp < kFzConsumers && g < tg;
+    float acc[TPT][EPT];
 #pragma unroll
-        for (int j = 0; j < kFzXRegs; ++j) {
-            const int i = threadIdx.x + j * kFzThreads;
-            if (i < tc * q8) {
-                const int r = i / q8, q = i - r * q8;
-                const uint4 u = xv[j];
-                unsafe |= (bf16x2_unsafe(u.x) | bf16x2_unsafe(u.y) | bf16x2_unsafe(u.z) | bf16x2_unsafe(u.w)) ? 1 : 0;
-                float4* dst = reinterpret_cast<float4*>(xf + r * kFzXPitch) + 2 * q;
-                dst[0] = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
-                dst[1] = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
+    for (int t = 0; t < TPT; ++t)
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) acc[t][j] = 0.f;
+    if (warp >= kFzConsumers) {
+        // producer warps (thread pl of 32 * PW)
+        const int pl = threadIdx.x - kFzCThreads, pw = warp - kFzConsumers;
+        uint4 xv[kXRegs];
+        auto load_x = [&](int c) {  // stage c's token chunk into registers
+#pragma unroll
+            for (int j = 0; j < kXRegs; ++j) {
+                const int i = pl + 32 * PW * j, r = i / (kFzKc / 8), q = i % (kFzKc / 8);
+                xv[j] = make_uint4(0u, 0u, 0u, 0u);
+                if (i < tc * (kFzKc / 8) && r < nt)
+                    xv[j] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0 + r) * H + c * kFzKc) + q);
+            }
+        };
+        int issued = 0;
+        bool ok = true;
+        if (!kXRes) load_x(0);
+        for (int c = kXRes ? min(NS, nstages) : 0; c < nstages; ++c) {
+            const int s = c % NS;
+            if (c >= NS && !fz_wait(&empty[s], static_cast<uint32_t>((c / NS - 1) & 1), &s_abort)) {
+                ok = false;
+                break;
+            }
+            uint8_t* slot = fz_smem_buf + s * slot_bytes;
+            const int bytes = min(SUB, nchunks - c * SUB) * wchunk;
+            if (pl == 0) {
+                if (kXRes) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(bytes));
+                else mbar_expect_tx(&full[s], static_cast<uint32_t>(bytes));
+                bulk_load(slot, static_cast<const uint8_t*>(wz) + static_cast<int64_t>(c) * wbytes,
+                          static_cast<uint32_t>(bytes), &full[s]);
+            }
+            issued = c + 1;
+            if constexpr (!kXRes) {
+                int unsafe = 0;
+#pragma unroll
+                for (int j = 0; j < kXRegs; ++j) {
+                    const int i = pl + 32 * PW * j;
+                    if (i < tc * (kFzKc / 8)) {
+                        const int r = i / (kFzKc / 8), q = i % (kFzKc / 8);
+                        const uint4 u = xv[j];
+                        unsafe |= bf16x8_unsafe(u);
+                        float4* dst = reinterpret_cast<float4*>(slot + wchunk + r * kFzXPitch) + 2 * q;
+                        dst[0] = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+                        dst[1] = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
+                    }
+                }
+                unsafe = __any_sync(0xffffffffu, unsafe);
+                if (lane == 0) s_unsafe[s][pw] = unsafe;
+                mbar_arrive(&full[s]);  // releases this thread's token stores (and its warp's flag)
+                if (c + 1 < nstages) load_x(c + 1);
             }
         }
-        if (c + 1 < nchunks) load_x(c + 1);
-        // the barrier also publishes the widened rows: it runs whatever w_safe is
-        const int any_unsafe = __syncthreads_or(unsafe);
-        const bool use_fma = w_safe && !any_unsafe;
-        if (active) {
-            const uint4* wr = reinterpret_cast<const uint4*>(fz_smem_buf + s * stage_bytes + e * kFzPitch);
-            const float4* xr = reinterpret_cast<const float4*>(xf + g * TPT * kFzXPitch);
-            if (use_fma) chain_fz<true, TPT>(wr, xr, kFzXPitch / 16, q8, acc);
-            else chain_fz<false, TPT>(wr, xr, kFzXPitch / 16, q8, acc);
-        }
-        __syncthreads();  // stage s and the widened rows are free again
-        if (warp == 0 && c + 2 < nchunks) issue_w(c + 2);
-    }
-    // router_select's per-expert part (src/text_forward.cpp:1453-1456):
-    // score = sigmoid(logit), choice = score + correction bias
-    float* s_sc = reinterpret_cast<float*>(fz_smem_buf);  // [tc][ew]
-    float* s_ch = s_sc + tc * ew;
-    if (active) {
-        const float b = bias[e];
+        if (!ok && pl == 0 && atomicExch(const_cast<int*>(&s_abort), 1) == 0) atomicCAS(err, 0, NF_DEVERR_WAIT_EMPTY);
+        // every router copy issued has to land before the CTA leaves (each
+        // issued stage already has all its arrivals: they follow the issue)
+        for (int c = max(0, issued - NS); c < issued; ++c)
+            fz_wait(&full[c % NS], static_cast<uint32_t>((c / NS) & 1), nullptr);
+    } else {
+        for (int c = 0; c < nstages; ++c) {
+            const int s = c % NS;
+            if (!fz_wait(&full[s], static_cast<uint32_t>((c / NS) & 1), &s_abort)) {
+                if (lane == 0 && atomicExch(const_cast<int*>(&s_abort), 1) == 0) atomicCAS(err, 0, NF_DEVERR_WAIT_FULL);
+                break;
+            }
+            const uint8_t* slot = fz_smem_buf + s * slot_bytes;
+            int unsafe_stage = kXRes ? s_x_unsafe : 0;
+            if constexpr (!kXRes) {
 #pragma unroll
-        for (int j = 0; j < TPT; ++j) {
-            const int t = g * TPT + j;
-            if (t < nt) {
-                const float sc = sigmoid_ref(acc[j]);
-                logits[static_cast<int64_t>(t0 + t) * E + e] = acc[j];
-                s_sc[t * ew + e] = sc;
-                s_ch[t * ew + e] = __fadd_rn(sc, b);
+                for (int i = 0; i < PW; ++i) unsafe_stage |= s_unsafe[s][i];
+            }
+            const bool use_fma = w_safe && !unsafe_stage;
+            if (active) {
+                if constexpr (kXRes) {
+#pragma unroll
+                    for (int sub = 0; sub < SUB; ++sub) {
+                        const int chunk = c * SUB + sub;
+                        if (chunk < nchunks) {
+                            const float4* xr = reinterpret_cast<const float4*>(xres + g * xres_pitch) + chunk * (kFzKc / 4);
+                            const uint4* wr = reinterpret_cast<const uint4*>(slot + sub * wchunk + el * fz_wpitch(kW16));
+                            acc[0][0] = use_fma ? chain_fz16<true>(wr, xr, acc[0][0]) : chain_fz16<false>(wr, xr, acc[0][0]);
+                        }
+                    }
+                } else {
+                    const float4* xr = reinterpret_cast<const float4*>(slot + wchunk + g * TPT * kFzXPitch);
+                    const float4* wr[EPT];
+#pragma unroll
+                    for (int j = 0; j < EPT; ++j)
+                        wr[j] = reinterpret_cast<const float4*>(slot + min(el + j * gt, E - 1) * fz_wpitch(false));
+                    if (use_fma) chain_fz32<true, EPT, TPT>(wr, xr, acc);
+                    else chain_fz32<false, EPT, TPT>(wr, xr, acc);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+    }
+    __syncthreads();
+    if (s_abort) return;
+    // router_select's per-expert part (src/text_forward.cpp:1453-1456):
+    // score = sigmoid(logit), choice = score + correction bias; rows padded
+    // to E + 1 so the per-token scans below hit distinct banks
+    const int rs = E + 1;
+    float* s_sc = reinterpret_cast<float*>(fz_smem_buf);  // [tc][E + 1]
+    float* s_ch = s_sc + tc * rs;
+    uint8_t* s_used = reinterpret_cast<uint8_t*>(s_ch + tc * rs);  // [tc][E]
+    if (active) {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) {
+            const int e = el + j * gt;
+            if (e < E) {
+                const float b = bias[e];
+#pragma unroll
+                for (int t = 0; t < TPT; ++t) {
+                    const int tok = g * TPT + t;
+                    if (tok < nt) {
+                        const float sc = sigmoid_ref(acc[t][j]);
+                        logits[static_cast<int64_t>(t0 + tok) * E + e] = acc[t][j];
+                        s_sc[tok * rs + e] = sc;
+                        s_ch[tok * rs + e] = __fadd_rn(sc, b);
+                    }
+                }
             }
         }
     }
     __syncthreads();
-    for (int t = warp; t < nt; t += kFzThreads / 32)
-        warp_select(s_sc + t * ew, s_ch + t * ew, E, K, scaling, normalize, n_group, topk_group, s_excl[warp],
-                    idx_out + static_cast<int64_t>(t0 + t) * K, w_out + static_cast<int64_t>(t0 + t) * K);
+    if constexpr (TPT == 1) {
+        // a few tokens: a warp per token, lanes split the experts
+        __shared__ uint32_t s_excl[kThreads / 32][32];
+        for (int t = warp; t < nt; t += kThreads / 32)
+            warp_select(s_sc + t * rs, s_ch + t * rs, E, K, scaling, normalize, n_group, topk_group, s_excl[warp],
+                        idx_out + static_cast<int64_t>(t0 + t) * K, w_out + static_cast<int64_t>(t0 + t) * K);
+    } else {
+        // many tokens: a thread per token
+        for (int t = threadIdx.x; t < nt; t += kThreads)
+            thread_select(s_sc + t * rs, s_ch + t * rs, E, K, scaling, normalize, n_group, topk_group, s_used + t * E,
+                          idx_out + static_cast<int64_t>(t0 + t) * K, w_out + static_cast<int64_t>(t0 + t) * K);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -615,18 +836,28 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __re
     int32_t* s_off = s_cnt + E;
     int32_t* s_mt = s_off + E + 1;
     int32_t* s_idx = s_mt + E + 1;  // [T * K]
+    // per expert, a bit per token that picked it (the picks of a token are
+    // distinct experts): the rank of pick (t, e) in expert e's segment is the
+    // popcount of e's bits below t
+    const int words = (T + 31) / 32;
+    uint32_t* s_mask = reinterpret_cast<uint32_t*>(s_idx + T * K);  // [E][words]
     const int n = T * K;
     for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+    for (int i = threadIdx.x; i < E * words; i += blockDim.x) s_mask[i] = 0u;
     for (int i = threadIdx.x; i < n; i += blockDim.x) s_idx[i] = idx[i];
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&s_cnt[s_idx[i]], 1);
-    __syncthreads();
-    build_segments(s_cnt, s_off, s_mt, E, nb_gu, nb_down, counts, seg_off, row_token, tiles_gu, tiles_down, meta);
-    // rank of (t, p) in its expert = picks of that expert by earlier tokens
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int e = s_idx[i], t = i / K;
-        int rank = 0;
-        for (int j = 0; j < t * K; ++j) rank += s_idx[j] == e ? 1 : 0;
+        atomicAdd(&s_cnt[e], 1);
+        atomicOr(&s_mask[e * words + (t >> 5)], 1u << (t & 31));
+    }
+    __syncthreads();
+    build_segments(s_cnt, s_off, s_mt, E, nb_gu, nb_down, counts, seg_off, row_token, tiles_gu, tiles_down, meta);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = s_idx[i], t = i / K;
+        const uint32_t* m = s_mask + e * words;
+        int rank = __popc(m[t >> 5] & ((1u << (t & 31)) - 1u));
+        for (int wd = 0; wd < (t >> 5); ++wd) rank += __popc(m[wd]);
         const int32_t row = s_off[e] + rank;
         pair_row[i] = row;
         row_token[row] = t;
@@ -659,10 +890,13 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __res
     int32_t* s_off = s_cnt + E;
     int32_t* s_mt = s_off + E + 1;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        // the loads are independent: unrolled, eight are in flight at a time
         int32_t run = 0;
+#pragma unroll 8
         for (int c = 0; c < nchunks; ++c) {
+            const int32_t n = chunk_counts[static_cast<int64_t>(c) * E + e];
             chunk_base[static_cast<int64_t>(c) * E + e] = run;
-            run += chunk_counts[static_cast<int64_t>(c) * E + e];
+            run += n;
         }
         s_cnt[e] = run;
     }
@@ -670,48 +904,36 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __res
     build_segments(s_cnt, s_off, s_mt, E, nb_gu, nb_down, counts, seg_off, row_token, tiles_gu, tiles_down, meta);
 }
 
-// Rows of a chunk of kChunkTok tokens: one warp ranks the picks in token
-// order (rounds of 32 tokens), then the CTA writes pair_row / row_token.
+// Rows of a chunk of kChunkTok tokens.  A token's picks are distinct experts,
+// so the rank of pick (t, e) inside expert e's share of the chunk is the
+// number of earlier tokens of the chunk that picked e: each expert keeps a
+// kChunkTok-bit mask of the tokens that picked it, and the rank is a
+// popcount of the bits below t.
+constexpr int kChunkWords = kChunkTok / 32;
+
 __global__ void __launch_bounds__(256) permute_rows_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
                                                            const int32_t* __restrict__ chunk_base,
                                                            const int32_t* __restrict__ seg_off,
                                                            int32_t* __restrict__ pair_row,
                                                            int32_t* __restrict__ row_token) {
-    extern __shared__ int32_t sh[];
-    int32_t* s_run = sh;                     // [E]
-    int32_t* s_rows = sh + E;                // [kChunkTok * K]
-    int32_t* s_pe = s_rows + kChunkTok * K;  // [kChunkTok * K]
+    extern __shared__ uint32_t s_mask[];  // [E][kChunkWords]
     const int t0 = blockIdx.x * kChunkTok;
-    const int nt = min(kChunkTok, T - t0);
-    for (int e = threadIdx.x; e < E; e += blockDim.x) s_run[e] = 0;
-    for (int i = threadIdx.x; i < nt * K; i += blockDim.x) s_pe[i] = idx[static_cast<int64_t>(t0) * K + i];
+    const int n = min(kChunkTok, T - t0) * K;
+    for (int i = threadIdx.x; i < E * kChunkWords; i += blockDim.x) s_mask[i] = 0u;
     __syncthreads();
-    if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
-        for (int r0 = 0; r0 < nt; r0 += 32) {
-            const int tl = r0 + lane;
-            const int lanes = min(32, nt - r0);
-            if (tl < nt) {
-                for (int p = 0; p < K; ++p) {
-                    const int e = s_pe[tl * K + p];
-                    int rank = 0;
-                    for (int l = 0; l < lane; ++l)
-                        for (int q = 0; q < K; ++q) rank += (s_pe[(r0 + l) * K + q] == e) ? 1 : 0;
-                    s_rows[tl * K + p] =
-                        seg_off[e] + chunk_base[static_cast<int64_t>(blockIdx.x) * E + e] + s_run[e] + rank;
-                }
-            }
-            __syncwarp();
-            if (lane == 0)
-                for (int i = 0; i < lanes * K; ++i) s_run[s_pe[r0 * K + i]] += 1;
-            __syncwarp();
-        }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = idx[static_cast<int64_t>(t0) * K + i], t = i / K;
+        atomicOr(&s_mask[e * kChunkWords + (t >> 5)], 1u << (t & 31));
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < nt * K; i += blockDim.x) {
-        const int row = s_rows[i];
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = idx[static_cast<int64_t>(t0) * K + i], t = i / K;
+        const uint32_t* m = s_mask + e * kChunkWords;
+        int rank = __popc(m[t >> 5] & ((1u << (t & 31)) - 1u));
+        for (int wd = 0; wd < (t >> 5); ++wd) rank += __popc(m[wd]);
+        const int row = seg_off[e] + chunk_base[static_cast<int64_t>(blockIdx.x) * E + e] + rank;
         pair_row[static_cast<int64_t>(t0) * K + i] = row;
-        row_token[row] = t0 + i / K;
+        row_token[row] = t0 + t;
     }
 }
 
@@ -926,30 +1148,38 @@ static cudaError_t smem_attr_once(Kernel kernel, int bytes, bool (&done)[kMaxDev
     return e;
 }
 
-cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const uint16_t* w_chunked, const float* bias, int T,
-                          int H, int E, int K, float scaling, int normalize, int n_group, int topk_group, int w_safe,
-                          float* logits, float* scores, float* choices, int32_t* idx, float* wts, int* err,
-                          cudaStream_t st) {
-    if (E <= kFzMaxE) {
-        // one chain per thread while the batch leaves SMs idle, four once
-        // there are several waves of CTAs
-        static bool attr1[kMaxDevices] = {}, attr4[kMaxDevices] = {};
-        const int ctas1 = (T + fz_tokens(E, 1) - 1) / fz_tokens(E, 1);
-        if (ctas1 < 4 * 148) {
-            const size_t smem = fz_smem(E, 1);
-            cudaError_t e = smem_attr_once(router_fused_kernel<1>, static_cast<int>(fz_smem(kFzMaxE, 1)), attr1);
-            if (e != cudaSuccess) return e;
-            router_fused_kernel<1><<<ctas1, kFzThreads, smem, st>>>(x, w, w_chunked, bias, T, H, E, K, scaling, normalize, n_group,
-                                                                    topk_group, w_safe, logits, idx, wts, err);
-        } else {
-            const size_t smem = fz_smem(E, 4);
-            cudaError_t e = smem_attr_once(router_fused_kernel<4>, static_cast<int>(fz_smem(kFzMaxE, 4)), attr4);
-            if (e != cudaSuccess) return e;
-            const int ctas = (T + fz_tokens(E, 4) - 1) / fz_tokens(E, 4);
-            router_fused_kernel<4><<<ctas, kFzThreads, smem, st>>>(x, w, w_chunked, bias, T, H, E, K, scaling, normalize, n_group,
-                                                                   topk_group, w_safe, logits, idx, wts, err);
-        }
-        return cudaGetLastError();
+template <int EPT, int TPT, int SUB, int NS, int PW, bool kW16, bool kXRes>
+static cudaError_t launch_fused(const uint16_t* x, const void* wz, const float* bias, int T, int H, int E, int K,
+                                float scaling, int normalize, int n_group, int topk_group, int w_safe, float* logits,
+                                int32_t* idx, float* wts, int* err, cudaStream_t st) {
+    static bool attr[kMaxDevices] = {};
+    const cudaError_t e = smem_attr_once(router_fused_kernel<EPT, TPT, SUB, NS, PW, kW16, kXRes>,
+                                         static_cast<int>(fz_smem(kFzMaxE, EPT, TPT, SUB, NS, kW16, kXRes, kFzMaxResH)),
+                                         attr);
+    if (e != cudaSuccess) return e;
+    const int tc = fz_tokens(E, EPT, TPT);
+    router_fused_kernel<EPT, TPT, SUB, NS, PW, kW16, kXRes>
+        <<<(T + tc - 1) / tc, kFzCThreads + 32 * PW, fz_smem(E, EPT, TPT, SUB, NS, kW16, kXRes, H), st>>>(
+            x, wz, bias, T, H, E, K, scaling, normalize, n_group, topk_group, w_safe, logits, idx, wts, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* w_chunked32, const uint16_t* w_chunked16,
+                          const float* bias, int T, int H, int E, int K, float scaling, int normalize, int n_group,
+                          int topk_group, int w_safe, float* logits, float* scores, float* choices, int32_t* idx,
+                          float* wts, int* err, cudaStream_t st) {
+    if (w_chunked32 && w_chunked16 && E <= kFzMaxE && H % kFzKc == 0) {
+        // one chain per thread over resident token rows while the batch gives
+        // each CTA a couple of tokens; 8 tokens x 2 experts per thread once it
+        // fills the GPU
+        if (T < 2048 && H <= kFzMaxResH)
+            return launch_fused<1, 1, 2, 3, 1, true, true>(x, w_chunked16, bias, T, H, E, K, scaling, normalize, n_group,
+                                                         topk_group, w_safe, logits, idx, wts, err, st);
+        if (E > 32)
+            return launch_fused<2, 8, 1, 2, 2, false, false>(x, w_chunked32, bias, T, H, E, K, scaling, normalize, n_group,
+                                                          topk_group, w_safe, logits, idx, wts, err, st);
+        return launch_fused<1, 8, 1, 2, 2, false, false>(x, w_chunked32, bias, T, H, E, K, scaling, normalize, n_group,
+                                                      topk_group, w_safe, logits, idx, wts, err, st);
     }
     const int chunk = H < kRtMaxChunk ? H : kRtMaxChunk;
     const size_t smem = static_cast<size_t>(kRtExp + kRtTok) * (chunk * 2 + 16);
@@ -965,8 +1195,9 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const uint16_t* 
 
 cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
                            const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st) {
-    if (T * K <= kSmallPairs) {
-        const size_t smem = (3 * E + 2 + T * K) * sizeof(int32_t);
+    const size_t small_smem = (3 * E + 2 + T * K + static_cast<size_t>(E) * ((T + 31) / 32)) * sizeof(int32_t);
+    if (T * K <= kSmallPairs && small_smem <= 48 * 1024) {
+        const size_t smem = small_smem;
         permute_small_kernel<<<1, 1024, smem, st>>>(idx, T, K, E, nb_gu, nb_down, b.counts, b.seg_off, b.pair_row,
                                                     b.row_token, b.tiles_gu, b.tiles_down, b.meta);
     } else {
@@ -976,7 +1207,7 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
                                                                            b.chunk_base, b.counts, b.seg_off,
                                                                            b.row_token, b.tiles_gu, b.tiles_down,
                                                                            b.meta);
-        permute_rows_kernel<<<nchunks, 256, (E + 2 * kChunkTok * K) * sizeof(int32_t), st>>>(
+        permute_rows_kernel<<<nchunks, 256, static_cast<size_t>(E) * kChunkWords * sizeof(uint32_t), st>>>(
             idx, T, K, E, b.chunk_base, b.seg_off, b.pair_row, b.row_token);
     }
     const int64_t items = static_cast<int64_t>(T) * (H / 64);

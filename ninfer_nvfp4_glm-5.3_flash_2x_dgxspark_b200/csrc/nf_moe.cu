@@ -45,7 +45,8 @@ struct nf_moe {
 
     // weights
     uint16_t* router_w = nullptr;   // [E, H]
-    uint16_t* router_wz = nullptr;  // fused router's chunk-major copy (E <= kRouterMaxE)
+    float* router_wz = nullptr;     // fused router's fp32 chunk-major copy (E <= kRouterMaxE)
+    uint16_t* router_wz16 = nullptr;  // and its BF16 chunk-major copy
     float* router_bias = nullptr;   // [E]
     uint8_t* w_gu = nullptr;        // NVFP4 [E * 2I, H/2], 128-row gate/up interleave
     uint8_t* w_gu_sf = nullptr;     // atoms
@@ -346,7 +347,9 @@ int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
     bool ok = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && h->alloc(&h->router_w, E * H) && h->alloc(&h->router_bias, E);
-    if (E <= kRouterMaxE) ok = ok && h->alloc(&h->router_wz, router_chunked_elems(E, H));
+    if (E <= kRouterMaxE)
+        ok = ok && h->alloc(&h->router_wz, router_chunked_elems(E, H)) &&
+             h->alloc(&h->router_wz16, router_chunked_elems16(E, H));
     if (fp4) {
         ok = ok && h->alloc(&h->w_gu, E * blocked_bytes(2 * I, H / 2)) && h->alloc(&h->w_gu_sf, E * 2 * I * H / 16) &&
              h->alloc(&h->w_dn, E * blocked_bytes(H, I / 2)) && h->alloc(&h->w_dn_sf, E * H * I / 16);
@@ -484,9 +487,14 @@ int nf_moe_bind_bf16(nf_moe* h, int which, int expert, const uint16_t* data, int
         case NF_BF16_ROUTER: {
             e = cudaMemcpy(h->router_w, data, rows * rb, cudaMemcpyHostToDevice);
             if (e == cudaSuccess && h->router_wz) {
-                std::vector<uint16_t> wz(static_cast<size_t>(router_chunked_elems(E, d.hidden)));
+                std::vector<float> wz(static_cast<size_t>(router_chunked_elems(E, d.hidden)));
                 router_chunked_layout(data, E, d.hidden, wz.data());
-                e = cudaMemcpy(h->router_wz, wz.data(), wz.size() * 2, cudaMemcpyHostToDevice);
+                e = cudaMemcpy(h->router_wz, wz.data(), wz.size() * sizeof(float), cudaMemcpyHostToDevice);
+                if (e == cudaSuccess) {
+                    std::vector<uint16_t> wz16(static_cast<size_t>(router_chunked_elems16(E, d.hidden)));
+                    router_chunked_layout16(data, E, d.hidden, wz16.data());
+                    e = cudaMemcpy(h->router_wz16, wz16.data(), wz16.size() * 2, cudaMemcpyHostToDevice);
+                }
             }
             h->router_bound = e == cudaSuccess;
             // products with BF16 activations stay exact in fp32 when every
@@ -628,7 +636,7 @@ int nf_moe_route(nf_moe* h, const uint16_t* x, int tokens, float* logits, int32_
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
-    const cudaError_t e = launch_router(x, h->router_w, h->router_wz, h->router_bias, tokens, d.hidden, d.experts, d.top_k,
+    const cudaError_t e = launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, tokens, d.hidden, d.experts, d.top_k,
                                         d.routed_scaling, d.normalize, d.n_group, d.topk_group, h->router_w_safe,
                                         logits ? logits : h->logits, h->scores, h->choices,
                                         idx ? idx : h->topk_idx, w ? w : h->topk_w, h->dev_err, s);
@@ -697,7 +705,7 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
         if ((e = cudaEventRecord(h->ev_join, h->side)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
     }
     begin(NF_STAGE_ROUTER, s);
-    e = launch_router(x, h->router_w, h->router_wz, h->router_bias, T, H, E, K, d.routed_scaling, d.normalize, d.n_group,
+    e = launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, T, H, E, K, d.routed_scaling, d.normalize, d.n_group,
                       d.topk_group, h->router_w_safe, h->logits, h->scores, h->choices, idx, w, h->dev_err, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "router launch");
     end(NF_STAGE_ROUTER, s);

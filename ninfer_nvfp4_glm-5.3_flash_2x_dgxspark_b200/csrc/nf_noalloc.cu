@@ -124,7 +124,7 @@ int nf_router_topk_noalloc(const uint16_t* x, const uint16_t* router_w, const fl
     // w_safe = 0: the caller's weights are not range-checked on the host, so
     // the chain always runs the separately rounded multiply and add
     if (e == cudaSuccess)
-        e = launch_router(x, router_w, /*w_chunked=*/nullptr, bias, tokens, hidden, experts, top_k, routed_scaling,
+        e = launch_router(x, router_w, /*w_chunked32=*/nullptr, /*w_chunked16=*/nullptr, bias, tokens, hidden, experts, top_k, routed_scaling,
                           normalize, n_group, topk_group, /*w_safe=*/0, scratch, scratch + kMaxScores,
                           scratch + 2 * kMaxScores, topk_idx, topk_w, err, s);
     if (e == cudaSuccess) {
