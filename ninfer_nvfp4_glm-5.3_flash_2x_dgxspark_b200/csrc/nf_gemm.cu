@@ -88,7 +88,7 @@ __device__ __forceinline__ void set_abort(volatile int* cta_abort, int* dev_err,
 template <int KIND, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tma_small,
-                const __grid_constant__ CUtensorMap tmb, const GemmArgs args) {
+                const GemmArgs args) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -125,7 +125,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_barrier_init();
         prefetch_tensormap(&tma);
         prefetch_tensormap(&tma_small);
-        prefetch_tensormap(&tmb);
     }
     if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
     tc_fence_before();
@@ -141,76 +140,108 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sf_atoms_per_rowblock = K / 64;
 
     if (warp == 0) {
-        // ------------------------------ TMA producer ------------------------
+        // ------------------------------ producer ----------------------------
+        // The whole warp runs the loop: lane 0 claims tiles, waits for free
+        // stages and sets the expected bytes; the copies of a stage then go
+        // out from separate lanes, because the copies one thread issues are
+        // carried out one after another while those of different threads
+        // overlap.  Lane 0: A (tensor map); lanes 1-4: the four 8 KB quarters
+        // of the stage's B block (stored swizzled: plain bulk copies); lanes
+        // 5-7: the scale-factor atoms of A and of the two B row blocks.
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t issued_parity[STAGES];
+        bool issued[STAGES];
+        for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
+        bool ok = true;
+        int qslot = 0;
+        uint32_t qphase = 0;
+        // The next tile is claimed three stages before the current tile's
+        // last and its descriptor read at the last, so neither the atomic nor
+        // the dependent load sits between two tiles' copies (and a CTA holds
+        // no tile long before it can start it).
+        int next = 0;
+        TileInfo next_t{};
         if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            uint32_t issued_parity[STAGES];
-            bool issued[STAGES];
-            for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
-            bool ok = true;
-            int qslot = 0;
-            uint32_t qphase = 0;
-            while (ok) {
-                // claim the next tile of the list and publish it to the MMA
-                // and epilogue warps (-1 ends the CTA's work)
-                int i = atomicAdd(args.tile_counter, 1);
-                if (i >= num_tiles) i = -1;
+            next = atomicAdd(args.tile_counter, 1);
+            if (next < num_tiles) next_t = get_tile(args, next);
+        }
+        while (ok) {
+            // publish the claimed tile to the MMA and epilogue warps (-1 ends
+            // the CTA's work)
+            int i = 0;
+            TileInfo t = next_t;
+            if (lane == 0) {
+                i = next < num_tiles ? next : -1;
                 if (!mbar_wait(&tq_empty[qslot], qphase ^ 1u, cta_abort, dev_err)) {
                     set_abort(cta_abort, args.err, NF_DEVERR_WAIT_EMPTY);
                     ok = false;
-                    break;
+                } else {
+                    tileq[qslot] = i;
+                    mbar_arrive(&tq_full[qslot]);
                 }
-                tileq[qslot] = i;
-                mbar_arrive(&tq_full[qslot]);
-                if (++qslot == kTileQ) qslot = 0, qphase ^= 1u;
-                if (i < 0) break;
-                const TileInfo t = get_tile(args, i);
-                const int brow0 = t.expert * args.b_rows_per_expert + t.n_block * BN;
-                for (int kt = 0; kt < k_tiles; ++kt) {
+            }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            i = __shfl_sync(0xffffffffu, i, 0);
+            if (!ok) break;
+            if (++qslot == kTileQ) qslot = 0, qphase ^= 1u;
+            if (i < 0) break;
+            t.expert = __shfl_sync(0xffffffffu, t.expert, 0);
+            t.row0 = __shfl_sync(0xffffffffu, t.row0, 0);
+            t.n_block = __shfl_sync(0xffffffffu, t.n_block, 0);
+            t.m_valid = __shfl_sync(0xffffffffu, t.m_valid, 0);
+            const int brow0 = t.expert * args.b_rows_per_expert + t.n_block * BN;
+            // tiles with at most 32 rows of the expert load only those rows of A
+            const bool small_a = t.m_valid <= kSmallRows;
+            for (int kt = 0; kt < k_tiles; ++kt) {
+                const int k0 = kt * kElemsPerStage;
+                const int steps = min(4, (K - k0) / kMmaK);
+                if (lane == 0) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, cta_abort, dev_err)) {
                         set_abort(cta_abort, args.err, NF_DEVERR_WAIT_EMPTY);
                         ok = false;
-                        break;
+                    } else {
+                        uint32_t bytes = (small_a ? kSmallRows * 128 : A_STAGE_BYTES) + B_STAGE_BYTES;
+                        if (KIND == KIND_NVFP4) bytes += static_cast<uint32_t>(steps) * 512u * 3u;
+                        mbar_arrive_expect_tx(&full[stage], bytes);
                     }
-                    const int k0 = kt * kElemsPerStage;
-                    const int steps = min(4, (K - k0) / kMmaK);
-                    // tiles with at most 32 rows of the expert load only those rows of A
-                    const bool small_a = t.m_valid <= kSmallRows;
-                    uint32_t bytes = (small_a ? kSmallRows * 128 : A_STAGE_BYTES) + B_STAGE_BYTES;
-                    if (KIND == KIND_NVFP4) bytes += static_cast<uint32_t>(steps) * 512u * 3u;
-                    mbar_arrive_expect_tx(&full[stage], bytes);
+                }
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) break;
+                if (lane == 0) {
                     const int xc = KIND == KIND_NVFP4 ? kt * 128 : k0;
                     tma_load_2d(sA + stage * A_STAGE_BYTES, small_a ? &tma_small : &tma, &full[stage], xc, t.row0);
+                } else if (lane <= 4) {
                     // B in box order: stage kt of tile (expert, n_block) is one 32 KB block
-                    tma_load_2d(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0,
-                                ((t.expert * args.b_nb + t.n_block) * args.b_kt + kt) * BN);
-                    if (KIND == KIND_NVFP4) {
-                        const int64_t a_atom = static_cast<int64_t>(t.row0 / 128) * sf_atoms_per_rowblock + kt * 4;
-                        bulk_load(sSFA + stage * SFA_STAGE_BYTES, args.sfa + a_atom * 512, steps * 512u, &full[stage]);
-#pragma unroll
-                        for (int b = 0; b < 2; ++b) {
-                            const int64_t b_atom =
-                                static_cast<int64_t>(brow0 / 128 + b) * sf_atoms_per_rowblock + kt * 4;
-                            bulk_load(sSFB + stage * SFB_STAGE_BYTES + b * 2048, args.sfb + b_atom * 512,
-                                      steps * 512u, &full[stage]);
-                        }
-                    }
-                    issued[stage] = true;
-                    issued_parity[stage] = phase;
-                    if (++stage == STAGES) stage = 0, phase ^= 1u;
+                    const int64_t blk = (static_cast<int64_t>(t.expert) * args.b_nb + t.n_block) * args.b_kt + kt;
+                    constexpr uint32_t kQ = B_STAGE_BYTES / 4;
+                    bulk_load(sB + stage * B_STAGE_BYTES + (lane - 1) * kQ,
+                              args.b + blk * B_STAGE_BYTES + (lane - 1) * kQ, kQ, &full[stage]);
+                } else if (KIND == KIND_NVFP4 && lane == 5) {
+                    const int64_t a_atom = static_cast<int64_t>(t.row0 / 128) * sf_atoms_per_rowblock + kt * 4;
+                    bulk_load(sSFA + stage * SFA_STAGE_BYTES, args.sfa + a_atom * 512, steps * 512u, &full[stage]);
+                } else if (KIND == KIND_NVFP4 && lane <= 7) {
+                    const int b = lane - 6;
+                    const int64_t b_atom = static_cast<int64_t>(brow0 / 128 + b) * sf_atoms_per_rowblock + kt * 4;
+                    bulk_load(sSFB + stage * SFB_STAGE_BYTES + b * 2048, args.sfb + b_atom * 512, steps * 512u,
+                              &full[stage]);
                 }
+                issued[stage] = true;
+                issued_parity[stage] = phase;
+                if (++stage == STAGES) stage = 0, phase ^= 1u;
+                if (lane == 0 && kt == max(0, k_tiles - 3)) next = atomicAdd(args.tile_counter, 1);
+                if (lane == 0 && kt == k_tiles - 1 && next < num_tiles) next_t = get_tile(args, next);
             }
-            if (!ok) {
-                // drain: every issued copy lands before the CTA may exit
-                for (int s = 0; s < STAGES; ++s) {
-                    if (!issued[s]) continue;
-                    const uint64_t t0 = globaltimer_ns();
-                    while (!mbar_try_wait(&full[s], issued_parity[s])) {
-                        if (globaltimer_ns() - t0 > NF_WAIT_BUDGET_NS) {
-                            atomicCAS(args.err, 0, NF_DEVERR_DRAIN);
-                            break;
-                        }
+        }
+        if (!ok && lane == 0) {
+            // drain: every issued copy lands before the CTA may exit
+            for (int s = 0; s < STAGES; ++s) {
+                if (!issued[s]) continue;
+                const uint64_t t0 = globaltimer_ns();
+                while (!mbar_try_wait(&full[s], issued_parity[s])) {
+                    if (globaltimer_ns() - t0 > NF_WAIT_BUDGET_NS) {
+                        atomicCAS(args.err, 0, NF_DEVERR_DRAIN);
+                        break;
                     }
                 }
             }
@@ -471,7 +502,7 @@ int gemm_grid_size(int device) {
 }
 
 template <int KIND, int EPI>
-static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb, const GemmArgs& args, int grid,
+static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_small, const GemmArgs& args, int grid,
                               cudaStream_t st) {
     // the shared memory limit is an attribute of the kernel in each device's context
     static bool attr[kMaxDevices] = {};
@@ -483,18 +514,18 @@ static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_sma
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
-    gemm_kernel<KIND, EPI><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, tmb, args);
+    gemm_kernel<KIND, EPI><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, args);
     return cudaGetLastError();
 }
 
-cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb, const GemmArgs& args, int grid,
+cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const GemmArgs& args, int grid,
                         cudaStream_t st) {
     if (args.kind == KIND_NVFP4) {
-        if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT>(tma, tma_small, tmb, args, grid, st);
-        if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16>(tma, tma_small, tmb, args, grid, st);
+        if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT>(tma, tma_small, args, grid, st);
+        if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16>(tma, tma_small, args, grid, st);
     } else {
-        if (args.epi == EPI_SWIGLU_BF16) return launch_one<KIND_BF16, EPI_SWIGLU_BF16>(tma, tma_small, tmb, args, grid, st);
-        if (args.epi == EPI_STORE_F32) return launch_one<KIND_BF16, EPI_STORE_F32>(tma, tma_small, tmb, args, grid, st);
+        if (args.epi == EPI_SWIGLU_BF16) return launch_one<KIND_BF16, EPI_SWIGLU_BF16>(tma, tma_small, args, grid, st);
+        if (args.epi == EPI_STORE_F32) return launch_one<KIND_BF16, EPI_STORE_F32>(tma, tma_small, args, grid, st);
     }
     return cudaErrorInvalidValue;
 }

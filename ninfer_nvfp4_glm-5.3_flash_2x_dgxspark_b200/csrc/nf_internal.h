@@ -52,6 +52,7 @@ struct GemmArgs {
     int b_rows_per_expert;  // B rows per expert (0 for a dense GEMM; indexes the scale atoms)
     int b_nb;               // B is stored in box order: 256-row blocks per expert ...
     int b_kt;               // ... each split into b_kt blocks of 128 bytes of K
+    const uint8_t* b;       // B in box order (32 KB blocks, rows stored swizzled)
     // tile source: grouped (tiles + device tile count) or dense
     const NfTile* tiles;
     const int32_t* num_tiles_dev;
@@ -78,7 +79,7 @@ struct GemmArgs {
 bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner_elems, uint64_t rows,
                   uint32_t box_inner, uint32_t box_rows);
 // tma_small: the same A tensor with a 32-row box, used for tiles with <= 32 rows.
-cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb, const GemmArgs& args, int grid,
+cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const GemmArgs& args, int grid,
                         cudaStream_t st);
 int gemm_grid_size(int device);
 

@@ -86,7 +86,7 @@ struct nf_moe {
     int* dev_err = nullptr;
 
     // tensor maps built at finalize
-    CUtensorMap tm_a{}, tm_bgu{}, tm_h{}, tm_bdn{}, tm_sgu{}, tm_shh{}, tm_sdn{};
+    CUtensorMap tm_a{}, tm_h{}, tm_shh{};
     CUtensorMap tm_a_s{}, tm_h_s{}, tm_shh_s{};  // 32-row boxes of the A operands
     int last_tokens = 0;
 
@@ -213,12 +213,21 @@ const char* proj_name(int proj) { return proj == NF_PROJ_GATE ? "gate_proj" : pr
 // "box order": the matrix is cut into blocks of 256 rows x 128 bytes (one
 // pipeline stage of one tile; 256 FP4 or 64 BF16 K-elements), each block is
 // 32 KB contiguous with 128-byte rows (zero padded past the row end), blocks
-// ordered row-block major, K-block minor.  A stage is then one contiguous
-// 32 KB read from HBM instead of 256 strided 128-byte pieces.
+// ordered row-block major, K-block minor.  Inside a block every row is
+// stored in the 128-byte swizzled form the MMA operand descriptors read
+// (16-byte chunk j of row r at chunk j ^ (r % 8)), so a stage is one
+// contiguous 32 KB region that plain bulk copies move into shared memory
+// ready to use, split across several issuing threads.
 constexpr int64_t kBlockRows = 256, kBlockRowBytes = 128, kBlockBytes = kBlockRows * kBlockRowBytes;
 
 int64_t k_blocks(int64_t row_bytes) { return (row_bytes + kBlockRowBytes - 1) / kBlockRowBytes; }
 int64_t blocked_bytes(int64_t rows, int64_t row_bytes) { return (rows / kBlockRows) * k_blocks(row_bytes) * kBlockBytes; }
+
+// One row piece (n bytes, a multiple of 16) into row `row` of a block, swizzled.
+void put_row_swizzled(uint8_t* block, int64_t row, const uint8_t* src, int64_t n) {
+    for (int64_t j = 0; j < n / 16; ++j)
+        std::memcpy(block + row * kBlockRowBytes + ((j ^ (row & 7)) * 16), src + j * 16, 16);
+}
 
 // Copies a row-major [rows, row_bytes] matrix (rows % 256 == 0) into box order.
 cudaError_t upload_blocked(uint8_t* dst, const uint8_t* src, int64_t rows, int64_t row_bytes) {
@@ -227,8 +236,8 @@ cudaError_t upload_blocked(uint8_t* dst, const uint8_t* src, int64_t rows, int64
     for (int64_t r = 0; r < rows; ++r)
         for (int64_t k = 0; k < kt; ++k) {
             const int64_t n = std::min(kBlockRowBytes, row_bytes - k * kBlockRowBytes);
-            std::memcpy(&stage[static_cast<size_t>(((r / kBlockRows) * kt + k) * kBlockBytes + (r % kBlockRows) * kBlockRowBytes)],
-                        src + r * row_bytes + k * kBlockRowBytes, static_cast<size_t>(n));
+            put_row_swizzled(&stage[static_cast<size_t>(((r / kBlockRows) * kt + k) * kBlockBytes)], r % kBlockRows,
+                             src + r * row_bytes + k * kBlockRowBytes, n);
         }
     return cudaMemcpy(dst, stage.data(), stage.size(), cudaMemcpyHostToDevice);
 }
@@ -243,8 +252,9 @@ cudaError_t upload_blocked_half(uint8_t* dst, const uint8_t* src, int64_t rows, 
     for (int64_t r = 0; r < rows; ++r)
         for (int64_t k = 0; k < kt; ++k) {
             const int64_t n = std::min(kBlockRowBytes, row_bytes - k * kBlockRowBytes);
-            std::memcpy(&stage[static_cast<size_t>(((r / 128) * kt + k) * hb + (r % 128) * kBlockRowBytes)],
-                        src + r * row_bytes + k * kBlockRowBytes, static_cast<size_t>(n));
+            // the half starts at row 128 * half of the block: (r % 128 + 128 * half) % 8 == r % 8
+            put_row_swizzled(&stage[static_cast<size_t>(((r / 128) * kt + k) * hb)], r % 128,
+                             src + r * row_bytes + k * kBlockRowBytes, n);
         }
     return cudaMemcpy2D(dst + half * hb, static_cast<size_t>(kBlockBytes), stage.data(), static_cast<size_t>(hb),
                         static_cast<size_t>(hb), static_cast<size_t>(nb * kt), cudaMemcpyHostToDevice);
@@ -594,22 +604,16 @@ int nf_moe_finalize(nf_moe* h) {
         ok = ok && make_tmap_2d(&h->tm_a, h->pb.a_codes, false, H / 2, R, 128, 128);
         ok = ok && make_tmap_2d(&h->tm_a_s, h->pb.a_codes, false, H / 2, R, 128, 32);
         ok = ok && make_tmap_2d(&h->tm_h_s, h->h_codes, false, I / 2, R, 128, 32);
-        ok = ok && make_tmap_2d(&h->tm_bgu, h->w_gu, false, 128, E * blocked_bytes(2 * I, H / 2) / 128, 128, 256);
         ok = ok && make_tmap_2d(&h->tm_h, h->h_codes, false, I / 2, R, 128, 128);
-        ok = ok && make_tmap_2d(&h->tm_bdn, h->w_dn, false, 128, E * blocked_bytes(H, I / 2) / 128, 128, 256);
     } else {
         ok = ok && make_tmap_2d(&h->tm_a, h->pb.a_bf16, true, H, R, 64, 128);
         ok = ok && make_tmap_2d(&h->tm_a_s, h->pb.a_bf16, true, H, R, 64, 32);
         ok = ok && make_tmap_2d(&h->tm_h_s, h->h_bf16, true, I, R, 64, 32);
-        ok = ok && make_tmap_2d(&h->tm_bgu, h->wb_gu, true, 64, E * blocked_bytes(2 * I, 2 * H) / 128, 64, 256);
         ok = ok && make_tmap_2d(&h->tm_h, h->h_bf16, true, I, R, 64, 128);
-        ok = ok && make_tmap_2d(&h->tm_bdn, h->wb_dn, true, 64, E * blocked_bytes(H, 2 * I) / 128, 64, 256);
     }
     if (Is > 0) {
-        ok = ok && make_tmap_2d(&h->tm_sgu, h->ws_gu, true, 64, blocked_bytes(2 * Is, 2 * H) / 128, 64, 256);
         ok = ok && make_tmap_2d(&h->tm_shh, h->sh_h, true, Is, Tm, 64, 128);
         ok = ok && make_tmap_2d(&h->tm_shh_s, h->sh_h, true, Is, Tm, 64, 32);
-        ok = ok && make_tmap_2d(&h->tm_sdn, h->ws_dn, true, 64, blocked_bytes(H, 2 * Is) / 128, 64, 256);
     }
     if (!ok) return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
     h->finalized = true;
@@ -685,21 +689,23 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
         sg.dense_rows = T;
         sg.n_blocks = Is / 128;
         sg.b_nb = 2 * Is / 256;
+        sg.b = reinterpret_cast<const uint8_t*>(h->ws_gu);
         sg.b_kt = static_cast<int>(k_blocks(2 * H));
         sg.out = h->sh_h;
         sg.out_ld = Is;
         sg.tile_counter = h->shared_counters;
-        e = launch_gemm(tm_x, tm_x_s, h->tm_sgu, sg, h->grid, h->side);
+        e = launch_gemm(tm_x, tm_x_s, sg, h->grid, h->side);
         if (e != cudaSuccess) return h->cuda_fail(e, "shared gate/up GEMM launch");
         sg.epi = EPI_STORE_F32;
         sg.K = Is;
         sg.n_blocks = H / 256;
         sg.b_nb = H / 256;
+        sg.b = reinterpret_cast<const uint8_t*>(h->ws_dn);
         sg.b_kt = static_cast<int>(k_blocks(2 * Is));
         sg.out = h->sh_out;
         sg.out_ld = H;
         sg.tile_counter = h->shared_counters + 1;
-        e = launch_gemm(h->tm_shh, h->tm_shh_s, h->tm_sdn, sg, h->grid, h->side);
+        e = launch_gemm(h->tm_shh, h->tm_shh_s, sg, h->grid, h->side);
         if (e != cudaSuccess) return h->cuda_fail(e, "shared down GEMM launch");
         end(NF_STAGE_SHARED, h->side);
         if ((e = cudaEventRecord(h->ev_join, h->side)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
@@ -724,6 +730,7 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.K = H;
     g.b_rows_per_expert = 2 * I;
     g.b_nb = 2 * I / 256;
+    g.b = fp4 ? h->w_gu : reinterpret_cast<const uint8_t*>(h->wb_gu);
     g.b_kt = static_cast<int>(k_blocks(fp4 ? H / 2 : 2 * H));
     g.tiles = h->pb.tiles_gu;
     g.num_tiles_dev = h->pb.meta + 1;
@@ -740,7 +747,7 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.out_sf = h->h_sf;
     g.out_kgroups = I / 16;
     g.tile_counter = h->pb.meta + 4;
-    e = launch_gemm(h->tm_a, h->tm_a_s, h->tm_bgu, g, h->grid, s);
+    e = launch_gemm(h->tm_a, h->tm_a_s, g, h->grid, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "gate/up GEMM launch");
     end(NF_STAGE_GATE_UP, s);
     begin(NF_STAGE_DOWN, s);
@@ -749,6 +756,7 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.K = I;
     g.b_rows_per_expert = H;
     g.b_nb = H / 256;
+    g.b = fp4 ? h->w_dn : reinterpret_cast<const uint8_t*>(h->wb_dn);
     g.b_kt = static_cast<int>(k_blocks(fp4 ? I / 2 : 2 * I));
     g.tiles = h->pb.tiles_down;
     g.num_tiles_dev = h->pb.meta + 2;
@@ -759,7 +767,7 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.out = h->down;
     g.out_ld = H;
     g.tile_counter = h->pb.meta + 5;
-    e = launch_gemm(h->tm_h, h->tm_h_s, h->tm_bdn, g, h->grid, s);
+    e = launch_gemm(h->tm_h, h->tm_h_s, g, h->grid, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "down GEMM launch");
     end(NF_STAGE_DOWN, s);
     if (Is > 0 && (e = cudaStreamWaitEvent(s, h->ev_join, 0)) != cudaSuccess)
