@@ -272,13 +272,16 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     if rank == 0:
         gu_ms = stage_ms["gate_up"]
         achieved = nbytes["gate_up"] / (gu_ms * 1e-3) / 1e9
+        # DRAM read + write of one gate/up launch from the committed ncu summary
         traffic = None
-        tf = REPO / "profiles" / "ncu_traffic.json"
+        tf = REPO / "profiles" / "gemm_gate_up_c1_decode.md"
         if tf.exists():
-            traffic = json.loads(tf.read_text()).get("gate_up_decode_bytes_per_launch")
-        # router logits, router select, permutation, dispatch, gate/up GEMM,
-        # down GEMM, combine; + shared gate/up and down GEMMs on the side stream
-        launches_per_step = 9 if lay.shared_inter > 0 else 7
+            for ln in tf.read_text().splitlines():
+                if ln.startswith("traffic_bytes_per_launch:"):
+                    traffic = int(ln.split(":")[1])
+        # fused router, permutation, dispatch, gate/up GEMM, down GEMM,
+        # combine; + shared gate/up and down GEMMs on the side stream
+        launches_per_step = 8 if lay.shared_inter > 0 else 6
         line = {
             "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3,
