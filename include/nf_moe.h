@@ -227,6 +227,27 @@ NF_API int nf_sigmoid_ref(const float* x_dev, int64_t n, float* y_dev, void* str
  * counts (all 0 on a correct build).  Synchronous. */
 NF_API int nf_format_selfcheck(int64_t* e2m1_mismatches, int64_t* e4m3_mismatches, int64_t* bf16_mismatches);
 
+/* ---- expert parallelism ----------------------------------------------------
+ * The layer sharded by experts over `world` GPUs of one node (1 <= world <= 8,
+ * experts % world == 0), one handle per rank and GPU; the reference runs one
+ * process per GPU with a TP split of the dense projections
+ * (src/text_forward.cpp:242-256, src/execution_plan.cpp:69-70) and has no
+ * expert parallelism.  Rank r owns experts [r E/world, (r+1) E/world); the
+ * router and the shared expert are replicated; every rank passes its own
+ * tokens (max_tokens per rank).  The host of rank 0 makes a group id with
+ * nf_ep_unique_id and hands it to every rank (by any means); each rank
+ * creates its handle with it.  Binding: pass every expert (global ids); a
+ * rank keeps the ones it owns and skips the others.  Every rank must call
+ * nf_moe_forward (or nf_moe_forward_host) for each step, also with tokens ==
+ * 0: the forward exchanges rows with the other ranks (NCCL point-to-point,
+ * loaded from libnccl.so.2 at the first EP handle) and synchronises the host
+ * once for the row counts, so EP forwards are never captured into graphs.
+ * Results are bit-identical to one GPU holding every expert. */
+#define NF_EP_ID_BYTES 128
+NF_API int nf_ep_unique_id(uint8_t* group_id_out, int len);
+NF_API int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, const uint8_t* group_id,
+                            int id_len, nf_moe** out);
+
 /* ---- router top-k without device allocation ------------------------------
  * No counterpart in the reference: its router runs inside moe() on host
  * buffers (src/text_forward.cpp:926-931).  This entry point is for callers

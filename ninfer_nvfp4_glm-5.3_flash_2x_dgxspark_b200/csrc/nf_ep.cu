@@ -1,0 +1,295 @@
+// nf_ep.cu -- expert parallelism: the MoE layer sharded by experts over the
+// GPUs of one node, one handle per rank (nf_moe_create_ep), exchanging
+// token rows with NCCL point-to-point calls on the forward's stream.
+//
+// Rank r owns experts [r E/R, (r+1) E/R); the router, its bias and the shared
+// expert are replicated; every rank routes its own tokens.  One forward:
+//   1. shared expert forked onto the side stream (as on one GPU);
+//   2. router over the rank's tokens (bit-exact, as on one GPU);
+//   3. the picks are laid out in (destination, token, pick) order and their
+//      BF16 token rows gathered into that order (ep_pack, gather_rows);
+//   4. count exchange, then one host synchronisation: NCCL needs the row
+//      counts on the host;
+//   5. rows and destination-local expert ids exchanged (ncclSend/ncclRecv);
+//   6. the rank's experts run on the received rows as top-1 picks: the same
+//      permutation, NVFP4 dispatch and grouped GEMMs as on one GPU, so every
+//      row's down output is the one a single GPU computes;
+//   7. the down rows (BF16 for NVFP4 experts, F32 for BF16 experts) go back
+//      to their source rank in receive order;
+//   8. the combine adds them in pick order with the routing weights, plus
+//      the shared expert and the residual -- the single-GPU combine, so the
+//      layer output is bit-identical to one GPU's.
+// NCCL is loaded with dlopen on the first EP handle: a process that already
+// loaded NCCL (e.g. through PyTorch) shares that copy, and processes that
+// never use EP never load it.
+#include "nf_handle.h"
+
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+
+using namespace nf;
+
+namespace {
+
+struct NcclApi {
+    bool ok = false;
+    std::string why;
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*group_start)() = nullptr;
+    ncclResult_t (*group_end)() = nullptr;
+    ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!lib) lib = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!lib) {
+            api.why = "libnccl.so.2 not found";
+            return;
+        }
+        auto sym = [&](const char* name) { return dlsym(lib, name); };
+        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
+        api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
+        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
+        api.group_start = reinterpret_cast<decltype(api.group_start)>(sym("ncclGroupStart"));
+        api.group_end = reinterpret_cast<decltype(api.group_end)>(sym("ncclGroupEnd"));
+        api.send = reinterpret_cast<decltype(api.send)>(sym("ncclSend"));
+        api.recv = reinterpret_cast<decltype(api.recv)>(sym("ncclRecv"));
+        api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
+        api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.group_start && api.group_end &&
+                 api.send && api.recv && api.error_string;
+        if (!api.ok) api.why = "libnccl.so.2 lacks the point-to-point API";
+    });
+    return api;
+}
+
+const char* nccl_str(ncclResult_t r) { return nccl().error_string ? nccl().error_string(r) : "unknown"; }
+
+}  // namespace
+
+// Rows, expert ids and outputs of one forward cross the group in three
+// grouped exchanges; `rows` are element counts per peer (host side).
+int ep_forward(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx_user,
+               float* w_user, cudaStream_t s) {
+    const nf_moe_desc& d = h->d;
+    const int H = d.hidden, E = d.experts, K = d.top_k, Is = d.shared_inter, R = h->ep_world;
+    const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
+    const int out_bytes = H * (fp4 ? 2 : 4);  // a down row: BF16 (NVFP4 experts) or F32 (BF16 experts)
+    int32_t* idx = idx_user ? idx_user : h->topk_idx;
+    float* w = w_user ? w_user : h->topk_w;
+    ncclComm_t comm = static_cast<ncclComm_t>(h->nccl);
+    NcclApi& api = nccl();
+    h->last_tokens = T;
+    StageRec rec;
+    rec.h = h;
+    rec.ev = h->prof_begin(&rec.set);
+    int st = NF_OK;
+    cudaError_t e = cudaSuccess;
+    ncclResult_t r = ncclSuccess;
+    if (T > 0 && Is > 0 && (st = launch_shared_expert(h, x, T, rec, s)) != NF_OK) return st;
+    // route, lay out, count
+    rec.begin(NF_STAGE_ROUTER, s);
+    if (T > 0) {
+        e = launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, T, H, E, K, d.routed_scaling,
+                          d.normalize, d.n_group, d.topk_group, h->router_w_safe, h->logits, h->scores, h->choices, idx,
+                          w, h->dev_err, s);
+        if (e == cudaSuccess)
+            e = launch_ep_pack(idx, T, K, h->ep_local, R, h->ep_slot, h->ep_send_tok, h->ep_send_e, h->ep_cnt, s);
+        if (e == cudaSuccess) e = launch_gather_rows(x, h->ep_send_tok, T * K, H * 2, h->ep_send, s);
+    } else {
+        e = cudaMemsetAsync(h->ep_cnt, 0, R * sizeof(int32_t), s);
+    }
+    if (e != cudaSuccess) return h->cuda_fail(e, "route and pack");
+    r = api.group_start();
+    for (int p = 0; p < R && r == ncclSuccess; ++p) {
+        r = api.send(h->ep_cnt + p, 1, ncclInt32, p, comm, s);
+        if (r == ncclSuccess) r = api.recv(h->ep_cnt + R + p, 1, ncclInt32, p, comm, s);
+    }
+    const ncclResult_t r2 = api.group_end();
+    if (r == ncclSuccess) r = r2;
+    if (r != ncclSuccess) return h->fail(NF_ERR_CUDA, "count exchange: %s", nccl_str(r));
+    if ((e = cudaMemcpyAsync(h->ep_hcnt, h->ep_cnt, 2 * R * sizeof(int32_t), cudaMemcpyDeviceToHost, s)) != cudaSuccess ||
+        (e = cudaStreamSynchronize(s)) != cudaSuccess)
+        return h->cuda_fail(e, "count exchange");
+    int64_t soff[kEpMaxRanks + 1] = {0}, roff[kEpMaxRanks + 1] = {0};
+    for (int p = 0; p < R; ++p) {
+        soff[p + 1] = soff[p] + h->ep_hcnt[p];
+        roff[p + 1] = roff[p] + h->ep_hcnt[R + p];
+    }
+    const int64_t n_recv = roff[R];
+    if (soff[R] != static_cast<int64_t>(T) * K || n_recv > static_cast<int64_t>(R) * d.max_tokens * K)
+        return h->fail(NF_ERR_CAPACITY, "expert-parallel exchange: %lld rows received, capacity %lld",
+                       static_cast<long long>(n_recv), static_cast<long long>(R) * d.max_tokens * K);
+    // rows and their destination-local experts
+    r = api.group_start();
+    for (int p = 0; p < R && r == ncclSuccess; ++p) {
+        const size_t sc = static_cast<size_t>(h->ep_hcnt[p]), rc = static_cast<size_t>(h->ep_hcnt[R + p]);
+        if (sc) {
+            r = api.send(h->ep_send + soff[p] * H, sc * H * 2, ncclUint8, p, comm, s);
+            if (r == ncclSuccess) r = api.send(h->ep_send_e + soff[p], sc, ncclInt32, p, comm, s);
+        }
+        if (rc && r == ncclSuccess) {
+            r = api.recv(h->ep_recv + roff[p] * H, rc * H * 2, ncclUint8, p, comm, s);
+            if (r == ncclSuccess) r = api.recv(h->ep_recv_e + roff[p], rc, ncclInt32, p, comm, s);
+        }
+    }
+    const ncclResult_t r3 = api.group_end();
+    if (r == ncclSuccess) r = r3;
+    if (r != ncclSuccess) return h->fail(NF_ERR_CUDA, "row exchange: %s", nccl_str(r));
+    rec.end(NF_STAGE_ROUTER, s);
+    // this rank's experts on the received rows (top-1 picks), back in receive order
+    nf_moe* in = h->inner;
+    if (n_recv > 0) {
+        if ((st = launch_routed_experts(in, h->ep_recv, h->ep_recv_e, static_cast<int>(n_recv), 1, rec, s)) != NF_OK)
+            return h->fail(st, "%s", in->err.c_str());
+        e = launch_gather_rows(in->down, in->pb.pair_row, static_cast<int>(n_recv), out_bytes, h->ep_back, s);
+        if (e != cudaSuccess) return h->cuda_fail(e, "expert output gather");
+    }
+    // outputs back to their source ranks, then the single-GPU combine
+    rec.begin(NF_STAGE_COMBINE, s);
+    r = api.group_start();
+    for (int p = 0; p < R && r == ncclSuccess; ++p) {
+        const size_t sc = static_cast<size_t>(h->ep_hcnt[p]), rc = static_cast<size_t>(h->ep_hcnt[R + p]);
+        if (rc) r = api.send(static_cast<uint8_t*>(h->ep_back) + roff[p] * out_bytes, rc * out_bytes, ncclUint8, p, comm, s);
+        if (sc && r == ncclSuccess)
+            r = api.recv(static_cast<uint8_t*>(h->ep_ret) + soff[p] * out_bytes, sc * out_bytes, ncclUint8, p, comm, s);
+    }
+    const ncclResult_t r4 = api.group_end();
+    if (r == ncclSuccess) r = r4;
+    if (r != ncclSuccess) return h->fail(NF_ERR_CUDA, "output exchange: %s", nccl_str(r));
+    if (T > 0) {
+        if (Is > 0 && (e = cudaStreamWaitEvent(s, h->ev_join, 0)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
+        e = launch_combine(h->ep_ret, fp4, h->ep_slot, w, Is > 0 ? h->sh_out : nullptr, residual, T, K, H, y, s);
+        if (e != cudaSuccess) return h->cuda_fail(e, "combine launch");
+    }
+    rec.end(NF_STAGE_COMBINE, s);
+    return NF_OK;
+}
+
+void ep_release(nf_moe* h) {
+    if (h->nccl) {
+        cudaSetDevice(h->device);
+        nccl().comm_destroy(static_cast<ncclComm_t>(h->nccl));
+        h->nccl = nullptr;
+    }
+    if (h->inner) {
+        nf_moe_destroy(h->inner);
+        h->inner = nullptr;
+    }
+    if (h->ep_hcnt) {
+        cudaFreeHost(h->ep_hcnt);
+        h->ep_hcnt = nullptr;
+    }
+}
+
+extern "C" {
+
+int nf_ep_unique_id(uint8_t* out, int len) {
+    if (!out || len < NF_EP_ID_BYTES) return NF_ERR_INVALID;
+    NcclApi& api = nccl();
+    if (!api.ok) {
+        create_error() = api.why;
+        return NF_ERR_UNSUPPORTED;
+    }
+    static_assert(sizeof(ncclUniqueId) == NF_EP_ID_BYTES, "NCCL unique id size");
+    ncclUniqueId id;
+    const ncclResult_t r = api.get_unique_id(&id);
+    if (r != ncclSuccess) {
+        create_error() = std::string("ncclGetUniqueId: ") + nccl_str(r);
+        return NF_ERR_CUDA;
+    }
+    std::memcpy(out, &id, sizeof(id));
+    return NF_OK;
+}
+
+int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, const uint8_t* group_id, int id_len,
+                     nf_moe** out) {
+    std::string& err = create_error();
+    err.clear();
+    if (!desc || !out || !group_id || id_len < NF_EP_ID_BYTES) {
+        err = "null descriptor, output or group id";
+        return NF_ERR_INVALID;
+    }
+    *out = nullptr;
+    const nf_moe_desc& d = *desc;
+    int st = validate_desc(d, &err);
+    if (st != NF_OK) return st;
+    if (world < 1 || world > kEpMaxRanks || rank < 0 || rank >= world) {
+        err = "expert parallelism needs 1 <= world <= 8 and 0 <= rank < world";
+        return NF_ERR_UNSUPPORTED;
+    }
+    if (d.experts % world != 0) {
+        err = "the experts must divide evenly over the ranks";
+        return NF_ERR_UNSUPPORTED;
+    }
+    NcclApi& api = nccl();
+    if (!api.ok) {
+        err = api.why;
+        return NF_ERR_UNSUPPORTED;
+    }
+    nf_moe* h = nullptr;
+    if ((st = create_impl(d, device, kRoleEpOuter, &h, &err)) != NF_OK) return st;
+    h->ep_rank = rank;
+    h->ep_world = world;
+    h->ep_local = d.experts / world;
+    h->ep_base = rank * h->ep_local;
+    // the rank's experts: top-1 picks over rows received from every rank
+    nf_moe_desc di = d;
+    di.experts = h->ep_local;
+    di.top_k = 1;
+    di.shared_inter = 0;
+    di.n_group = 1;
+    di.topk_group = 1;
+    di.normalize = 0;
+    di.routed_scaling = 1.f;
+    di.max_tokens = world * d.max_tokens * d.top_k;
+    if ((st = create_impl(di, device, kRoleExperts, &h->inner, &err)) != NF_OK) {
+        nf_moe_destroy(h);
+        return st;
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    const int64_t H = d.hidden, pairs = static_cast<int64_t>(d.max_tokens) * d.top_k, cap = world * pairs;
+    const int64_t ob = d.expert_kind == NF_EXPERTS_NVFP4 ? 2 : 4;
+    uint8_t* back = nullptr;
+    uint8_t* ret = nullptr;
+    bool ok = h->alloc(&h->ep_send, pairs * H) && h->alloc(&h->ep_send_e, pairs) && h->alloc(&h->ep_send_tok, pairs) &&
+              h->alloc(&h->ep_slot, pairs) && h->alloc(&h->ep_cnt, 2 * world) && h->alloc(&h->ep_recv, cap * H) &&
+              h->alloc(&h->ep_recv_e, cap) && h->alloc(&back, cap * H * ob) && h->alloc(&ret, pairs * H * ob);
+    h->ep_back = back;
+    h->ep_ret = ret;
+    ok = ok && cudaMallocHost(&h->ep_hcnt, 2 * world * sizeof(int32_t)) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        cudaSetDevice(prev);
+        nf_moe_destroy(h);
+        err = "device allocation failed";
+        return NF_ERR_NOMEM;
+    }
+    ncclUniqueId id;
+    std::memcpy(&id, group_id, sizeof(id));
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = api.comm_init_rank(&comm, world, id, rank);
+    cudaSetDevice(prev);
+    if (r != ncclSuccess) {
+        nf_moe_destroy(h);
+        err = std::string("ncclCommInitRank: ") + nccl_str(r);
+        return NF_ERR_CUDA;
+    }
+    h->nccl = comm;
+    *out = h;
+    return NF_OK;
+}
+
+}  // extern "C"

@@ -135,6 +135,12 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
 cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair_row, const float* topk_w,
                            const float* shared, const float* residual, int T, int K, int H, float* y,
                            cudaStream_t st);
+// Expert parallelism (up to kEpMaxRanks ranks): the (destination, token,
+// pick) layout of the picks, and a row gather.
+constexpr int kEpMaxRanks = 8;
+cudaError_t launch_ep_pack(const int32_t* idx, int T, int K, int e_per_rank, int world, int32_t* slot,
+                           int32_t* send_tok, int32_t* send_e, int32_t* counts, cudaStream_t st);
+cudaError_t launch_gather_rows(const void* src, const int32_t* map, int n, int row_bytes, void* dst, cudaStream_t st);
 cudaError_t launch_dequant(const uint8_t* packed, const uint8_t* scales, float gscale, int64_t rows, int64_t cols,
                            float* out, cudaStream_t st);
 cudaError_t launch_quantize(const float* x, int64_t rows, int64_t cols, float gscale, uint8_t* codes,

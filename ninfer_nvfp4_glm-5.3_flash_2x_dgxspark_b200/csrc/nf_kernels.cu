@@ -10,6 +10,8 @@
 
 #include "_gen/sigmoid_table.inc"
 
+#include <algorithm>
+
 namespace nf {
 
 // ---------------------------------------------------------------------------
@@ -1231,6 +1233,93 @@ cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair
     else
         combine_kernel<float><<<T, threads, 0, st>>>(static_cast<const float*>(down), pair_row, topk_w, shared,
                                                      residual, T, K, H, y);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Expert parallelism.  Pick (t, p) goes to rank d = idx[t, p] / e_per_rank.
+// ep_pack lays the picks out in (destination, token, pick) order -- the
+// order the exchange sends them in, fully deterministic -- and writes, per
+// pick, its send slot (the combine's pair_row at the source), per slot its
+// token and destination-local expert, and per destination its count.  One
+// CTA of 1024 threads walks the picks in chunks of 1024: per chunk, each
+// warp ballots its lanes per destination and a scan over the warps gives
+// every pick its rank.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) ep_pack_kernel(const int32_t* __restrict__ idx, int n, int K, int e_per_rank,
+                                                       int world, int32_t* __restrict__ slot,
+                                                       int32_t* __restrict__ send_tok, int32_t* __restrict__ send_e,
+                                                       int32_t* __restrict__ counts) {
+    __shared__ int32_t s_base[kEpMaxRanks];
+    __shared__ int32_t s_w[32][kEpMaxRanks];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x < kEpMaxRanks) s_base[threadIdx.x] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&s_base[idx[i] / e_per_rank], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int d = 0; d < world; ++d) {
+            const int c = s_base[d];
+            counts[d] = c;
+            s_base[d] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+    for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+        const int i = c0 + threadIdx.x;
+        const int d = i < n ? idx[i] / e_per_rank : -1;
+        int in_warp = 0;
+        for (int dd = 0; dd < world; ++dd) {
+            const uint32_t m = __ballot_sync(0xffffffffu, d == dd);
+            if (lane == 0) s_w[warp][dd] = __popc(m);
+            if (d == dd) in_warp = __popc(m & ((1u << lane) - 1u));
+        }
+        __syncthreads();
+        if (d >= 0) {
+            int r = s_base[d] + in_warp;
+            for (int w = 0; w < warp; ++w) r += s_w[w][d];
+            slot[i] = r;
+            send_tok[r] = i / K;
+            send_e[r] = idx[i] - d * e_per_rank;
+        }
+        __syncthreads();
+        if (threadIdx.x < world) {
+            int total = 0;
+            for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) total += s_w[w][threadIdx.x];
+            s_base[threadIdx.x] += total;
+        }
+        __syncthreads();
+    }
+}
+
+// dst row i = src row map[i]; rows of row_bytes (a multiple of 16) bytes.
+__global__ void gather_rows_kernel(const uint8_t* __restrict__ src, const int32_t* __restrict__ map, int n,
+                                   int row_bytes, uint8_t* __restrict__ dst) {
+    const int per_row = row_bytes / 16;
+    const int64_t total = static_cast<int64_t>(n) * per_row;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / per_row, c = i - r * per_row;
+        reinterpret_cast<uint4*>(dst + r * row_bytes)[c] =
+            __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(map[r]) * row_bytes) + c);
+    }
+}
+
+cudaError_t launch_ep_pack(const int32_t* idx, int T, int K, int e_per_rank, int world, int32_t* slot,
+                           int32_t* send_tok, int32_t* send_e, int32_t* counts, cudaStream_t st) {
+    if (world < 1 || world > kEpMaxRanks) return cudaErrorInvalidValue;
+    ep_pack_kernel<<<1, 1024, 0, st>>>(idx, T * K, K, e_per_rank, world, slot, send_tok, send_e, counts);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const void* src, const int32_t* map, int n, int row_bytes, void* dst, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const int64_t total = static_cast<int64_t>(n) * (row_bytes / 16);
+    const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+    gather_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint8_t*>(src), map, n, row_bytes,
+                                               static_cast<uint8_t*>(dst));
     return cudaGetLastError();
 }
 

@@ -2,15 +2,15 @@
 // reference's validation, device layouts, and the forward pass that chains
 // router -> permutation/dispatch -> grouped gate/up GEMM (SwiGLU + NVFP4
 // quantisation fused) -> grouped down GEMM -> shared expert -> combine.
-#include "nf_moe.h"
+#include "nf_handle.h"
 
 #include "nf_common.cuh"
-#include "nf_internal.h"
 
 #include <cfloat>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -21,153 +21,9 @@ namespace {
 
 thread_local std::string g_create_error;
 
-struct DevBuf {
-    void* p = nullptr;
-    size_t bytes = 0;
-};
-
 }  // namespace
 
-struct nf_moe {
-    nf_moe_desc d{};
-    int device = 0;
-    int grid = 148;
-    cudaStream_t stream = nullptr;   // internal stream of the host-buffer path
-    cudaStream_t side = nullptr;     // shared expert, forked from the caller's stream
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
-    int* shared_counters = nullptr;  // tile counters of the two shared-expert GEMMs
-    std::string err;
-    bool finalized = false;
-    std::vector<DevBuf> allocs;
-
-    // sizes
-    int rows_cap = 0, nchunks_cap = 0, mtiles_cap = 0;
-
-    // weights
-    uint16_t* router_w = nullptr;   // [E, H]
-    float* router_wz = nullptr;     // fused router's fp32 chunk-major copy (E <= kRouterMaxE)
-    uint16_t* router_wz16 = nullptr;  // and its BF16 chunk-major copy
-    float* router_bias = nullptr;   // [E]
-    uint8_t* w_gu = nullptr;        // NVFP4 [E * 2I, H/2], 128-row gate/up interleave
-    uint8_t* w_gu_sf = nullptr;     // atoms
-    uint8_t* w_dn = nullptr;        // NVFP4 [E * H, I/2]
-    uint8_t* w_dn_sf = nullptr;
-    uint16_t* wb_gu = nullptr;      // BF16 experts [E * 2I, H]
-    uint16_t* wb_dn = nullptr;      // BF16 experts [E * H, I]
-    uint16_t* ws_gu = nullptr;      // shared [2 Is, H]
-    uint16_t* ws_dn = nullptr;      // shared [H, Is]
-    float* alpha_g = nullptr;       // [E] weight_scale_2 * input_scale
-    float* alpha_u = nullptr;
-    float* alpha_d = nullptr;
-    float* gs_g = nullptr;          // [E] 1 / input_scale
-    float* gs_d = nullptr;
-    std::vector<float> h_alpha_g, h_alpha_u, h_alpha_d, h_in_g, h_in_u, h_in_d;
-    std::vector<uint8_t> bound;     // [E * 3] expert projection bound flags
-    bool router_bound = false, bias_bound = false, sg_bound = false, su_bound = false, sd_bound = false;
-    int router_w_safe = 0;  // every nonzero router weight has |w| in [2^-67, 2^63)
-
-    // workspace
-    float* logits = nullptr;         // router logits, sigmoid scores and choices [Tm, E]
-    float* scores = nullptr;
-    float* choices = nullptr;
-    int32_t* topk_idx = nullptr;
-    float* topk_w = nullptr;
-    PermuteBuffers pb{};
-    uint8_t* h_codes = nullptr;
-    uint8_t* h_sf = nullptr;
-    uint16_t* h_bf16 = nullptr;
-    void* down = nullptr;           // BF16 (NVFP4 experts) or F32 (BF16 experts)
-    uint16_t* sh_h = nullptr;       // [Tm, Is]
-    float* sh_out = nullptr;        // [Tm, H]
-    float* x_f32 = nullptr;         // host-path staging
-    uint16_t* x_bf16 = nullptr;
-    float* res_f32 = nullptr;
-    float* y_f32 = nullptr;
-    int* dev_err = nullptr;
-
-    // tensor maps built at finalize
-    CUtensorMap tm_a{}, tm_h{}, tm_shh{};
-    CUtensorMap tm_a_s{}, tm_h_s{}, tm_shh_s{};  // 32-row boxes of the A operands
-    int last_tokens = 0;
-
-    // graph mode (nf_moe_set_graph_mode): captured forwards by argument set
-    struct GraphEntry {
-        const void* x;
-        const void* res;
-        void* y;
-        void* idx;
-        void* w;
-        int T;
-        cudaStream_t s;
-        cudaGraphExec_t exec;
-    };
-    static constexpr size_t kMaxGraphs = 16;
-    bool use_graphs = false;
-    std::vector<GraphEntry> graphs;
-
-    // per-stage event profile: a ring of event sets (a begin and an end event
-    // per stage, recorded on the stream the stage runs on), folded into
-    // stage_ms
-    static constexpr int kProfSets = 64;
-    static constexpr int kEvPerSet = 2 * NF_STAGE_COUNT;
-    bool profiling = false;
-    std::vector<cudaEvent_t> prof_ev;   // kProfSets * kEvPerSet
-    std::vector<uint8_t> prof_used;     // set holds an unfolded forward
-    std::vector<uint8_t> prof_mask;     // stages recorded by the set
-    int prof_next = 0, prof_forwards = 0;
-    double stage_ms[NF_STAGE_COUNT] = {};
-
-    void fold(int set) {
-        cudaEvent_t* ev = &prof_ev[static_cast<size_t>(set) * kEvPerSet];
-        const uint8_t mask = prof_mask[static_cast<size_t>(set)];
-        for (int s = 0; s < NF_STAGE_COUNT; ++s) {
-            if (!(mask & (1u << s))) continue;
-            cudaEventSynchronize(ev[2 * s + 1]);
-            float ms = 0.f;
-            if (cudaEventElapsedTime(&ms, ev[2 * s], ev[2 * s + 1]) == cudaSuccess) stage_ms[s] += ms;
-        }
-        prof_used[static_cast<size_t>(set)] = 0;
-        ++prof_forwards;
-    }
-    // events of the set recording the current forward (nullptr when off)
-    cudaEvent_t* prof_begin(int* set_out) {
-        if (!profiling) return nullptr;
-        const int set = prof_next;
-        prof_next = (prof_next + 1) % kProfSets;
-        if (prof_used[static_cast<size_t>(set)]) fold(set);
-        prof_used[static_cast<size_t>(set)] = 1;
-        prof_mask[static_cast<size_t>(set)] = 0;
-        *set_out = set;
-        return &prof_ev[static_cast<size_t>(set) * kEvPerSet];
-    }
-
-    int fail(int status, const char* fmt, ...) {
-        char buf[512];
-        va_list ap;
-        va_start(ap, fmt);
-        vsnprintf(buf, sizeof(buf), fmt, ap);
-        va_end(ap);
-        err = buf;
-        return status;
-    }
-    int cuda_fail(cudaError_t e, const char* what) {
-        return fail(NF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
-    }
-    template <typename T>
-    bool alloc(T** p, size_t count) {
-        void* q = nullptr;
-        const size_t bytes = count * sizeof(T) > 0 ? count * sizeof(T) : 16;
-        if (cudaMalloc(&q, bytes) != cudaSuccess) return false;
-        allocs.push_back({q, bytes});
-        *p = static_cast<T*>(q);
-        return true;
-    }
-    size_t bytes_of(const void* p) const {
-        for (const auto& a : allocs)
-            if (a.p == p) return a.bytes;
-        return 0;
-    }
-};
+std::string& create_error() { return g_create_error; }
 
 namespace {
 
@@ -285,6 +141,7 @@ const char* nf_moe_last_error(const nf_moe* h) { return h ? h->err.c_str() : g_c
 
 void nf_moe_destroy(nf_moe* h) {
     if (!h) return;
+    if (h->ep_outer) ep_release(h);
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
@@ -305,15 +162,14 @@ void nf_moe_destroy(nf_moe* h) {
     delete h;
 }
 
-int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
-    g_create_error.clear();
-    auto reject = [](int st, const char* msg) {
-        g_create_error = msg;
+}  // extern "C"
+
+// The descriptor checks of nf_moe_create; NF_OK or a status with *err set.
+int validate_desc(const nf_moe_desc& d, std::string* err) {
+    auto reject = [&](int st, const char* msg) {
+        if (err) *err = msg;
         return st;
     };
-    if (!desc || !out) return reject(NF_ERR_INVALID, "null descriptor or output");
-    *out = nullptr;
-    const nf_moe_desc& d = *desc;
     if (d.hidden <= 0 || d.hidden % 256 != 0) return reject(NF_ERR_UNSUPPORTED, "hidden must be a positive multiple of 256");
     if (d.inter <= 0 || d.inter % 128 != 0) return reject(NF_ERR_UNSUPPORTED, "inter must be a positive multiple of 128");
     if (d.shared_inter < 0 || d.shared_inter % 128 != 0)
@@ -327,6 +183,35 @@ int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
         return reject(NF_ERR_UNSUPPORTED, "group-limited routing needs n_group <= 32 dividing experts and enough eligible experts");
     if (d.expert_kind != NF_EXPERTS_NVFP4 && d.expert_kind != NF_EXPERTS_BF16)
         return reject(NF_ERR_INVALID, "expert_kind must be NF_EXPERTS_NVFP4 or NF_EXPERTS_BF16");
+    return NF_OK;
+}
+
+extern "C" {
+
+int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
+    g_create_error.clear();
+    if (!desc || !out) {
+        g_create_error = "null descriptor or output";
+        return NF_ERR_INVALID;
+    }
+    *out = nullptr;
+    const nf_moe_desc& d = *desc;
+    const int st = validate_desc(d, &g_create_error);
+    if (st != NF_OK) return st;
+    return create_impl(d, device, kRoleFull, out, &g_create_error);
+}
+
+}  // extern "C"
+
+// Allocates a handle for a validated descriptor.  kRoleExperts (the experts
+// of an EP rank) has no router or shared expert; kRoleEpOuter has no routed
+// experts or GEMM workspace (its experts live in the inner handle).
+int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::string* err) {
+    auto reject = [&](int st, const char* msg) {
+        if (err) *err = msg;
+        return st;
+    };
+    *out = nullptr;
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
         return reject(NF_ERR_CUDA, "no such CUDA device");
@@ -348,6 +233,9 @@ int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
     h->d = d;
     h->device = device;
     h->grid = gemm_grid_size(device);
+    h->experts_only = role == kRoleExperts;
+    h->ep_outer = role == kRoleEpOuter;
+    const bool routed = role != kRoleEpOuter, router = role != kRoleExperts;
     const int64_t H = d.hidden, E = d.experts, K = d.top_k, I = d.inter, Is = d.shared_inter, Tm = d.max_tokens;
     const int64_t pairs = Tm * K;
     h->rows_cap = static_cast<int>(round_up(pairs + 127 * E, 128));
@@ -356,39 +244,45 @@ int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
     const int64_t R = h->rows_cap;
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
     bool ok = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) == cudaSuccess;
-    ok = ok && h->alloc(&h->router_w, E * H) && h->alloc(&h->router_bias, E);
-    if (E <= kRouterMaxE)
-        ok = ok && h->alloc(&h->router_wz, router_chunked_elems(E, H)) &&
-             h->alloc(&h->router_wz16, router_chunked_elems16(E, H));
-    if (fp4) {
-        ok = ok && h->alloc(&h->w_gu, E * blocked_bytes(2 * I, H / 2)) && h->alloc(&h->w_gu_sf, E * 2 * I * H / 16) &&
-             h->alloc(&h->w_dn, E * blocked_bytes(H, I / 2)) && h->alloc(&h->w_dn_sf, E * H * I / 16);
-    } else {
-        ok = ok && h->alloc(&h->wb_gu, E * blocked_bytes(2 * I, 2 * H) / 2) &&
-             h->alloc(&h->wb_dn, E * blocked_bytes(H, 2 * I) / 2);
+    if (router) {
+        ok = ok && h->alloc(&h->router_w, E * H) && h->alloc(&h->router_bias, E);
+        if (E <= kRouterMaxE)
+            ok = ok && h->alloc(&h->router_wz, router_chunked_elems(E, H)) &&
+                 h->alloc(&h->router_wz16, router_chunked_elems16(E, H));
+        ok = ok && h->alloc(&h->logits, Tm * E) && h->alloc(&h->scores, Tm * E) && h->alloc(&h->choices, Tm * E);
+    }
+    if (routed) {
+        if (fp4) {
+            ok = ok && h->alloc(&h->w_gu, E * blocked_bytes(2 * I, H / 2)) && h->alloc(&h->w_gu_sf, E * 2 * I * H / 16) &&
+                 h->alloc(&h->w_dn, E * blocked_bytes(H, I / 2)) && h->alloc(&h->w_dn_sf, E * H * I / 16);
+        } else {
+            ok = ok && h->alloc(&h->wb_gu, E * blocked_bytes(2 * I, 2 * H) / 2) &&
+                 h->alloc(&h->wb_dn, E * blocked_bytes(H, 2 * I) / 2);
+        }
     }
     if (Is > 0) ok = ok && h->alloc(&h->ws_gu, blocked_bytes(2 * Is, 2 * H) / 2) && h->alloc(&h->ws_dn, blocked_bytes(H, 2 * Is) / 2);
     ok = ok && h->alloc(&h->alpha_g, E) && h->alloc(&h->alpha_u, E) && h->alloc(&h->alpha_d, E) &&
          h->alloc(&h->gs_g, E) && h->alloc(&h->gs_d, E);
-    ok = ok && h->alloc(&h->logits, Tm * E) && h->alloc(&h->scores, Tm * E) && h->alloc(&h->choices, Tm * E) &&
-         h->alloc(&h->topk_idx, Tm * K) && h->alloc(&h->topk_w, Tm * K);
+    ok = ok && h->alloc(&h->topk_idx, Tm * K) && h->alloc(&h->topk_w, Tm * K);
     PermuteBuffers& b = h->pb;
-    ok = ok && h->alloc(&b.chunk_counts, static_cast<int64_t>(h->nchunks_cap) * E) &&
-         h->alloc(&b.chunk_base, static_cast<int64_t>(h->nchunks_cap) * E) && h->alloc(&b.counts, E) &&
-         h->alloc(&b.seg_off, E + 1) && h->alloc(&b.pair_row, pairs) && h->alloc(&b.row_token, R) &&
-         h->alloc(&b.tiles_gu, static_cast<int64_t>(h->mtiles_cap) * (I / 128)) &&
-         h->alloc(&b.tiles_down, static_cast<int64_t>(h->mtiles_cap) * (H / 256)) && h->alloc(&b.meta, 8) &&
-         h->alloc(&h->shared_counters, 2);
+    if (routed) {
+        ok = ok && h->alloc(&b.chunk_counts, static_cast<int64_t>(h->nchunks_cap) * E) &&
+             h->alloc(&b.chunk_base, static_cast<int64_t>(h->nchunks_cap) * E) && h->alloc(&b.counts, E) &&
+             h->alloc(&b.seg_off, E + 1) && h->alloc(&b.pair_row, pairs) && h->alloc(&b.row_token, R) &&
+             h->alloc(&b.tiles_gu, static_cast<int64_t>(h->mtiles_cap) * (I / 128)) &&
+             h->alloc(&b.tiles_down, static_cast<int64_t>(h->mtiles_cap) * (H / 256)) && h->alloc(&b.meta, 8);
+    }
+    ok = ok && h->alloc(&h->shared_counters, 2);
     ok = ok && cudaStreamCreateWithFlags(&h->side, cudaStreamNonBlocking) == cudaSuccess &&
          cudaEventCreateWithFlags(&h->ev_fork, cudaEventDisableTiming) == cudaSuccess &&
          cudaEventCreateWithFlags(&h->ev_join, cudaEventDisableTiming) == cudaSuccess;
-    if (fp4) {
+    if (routed && fp4) {
         ok = ok && h->alloc(&b.a_codes, R * H / 2) && h->alloc(&b.a_sf, R * H / 16) && h->alloc(&h->h_codes, R * I / 2) &&
              h->alloc(&h->h_sf, R * I / 16);
         uint16_t* dn = nullptr;
         ok = ok && h->alloc(&dn, R * H);
         h->down = dn;
-    } else {
+    } else if (routed) {
         ok = ok && h->alloc(&b.a_bf16, R * H) && h->alloc(&h->h_bf16, R * I);
         float* dn = nullptr;
         ok = ok && h->alloc(&dn, R * H);
@@ -404,7 +298,7 @@ int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
         return reject(NF_ERR_NOMEM, "device allocation failed");
     }
     cudaMemset(h->dev_err, 0, sizeof(int));
-    cudaMemset(b.row_token, 0xff, R * sizeof(int32_t));
+    if (routed) cudaMemset(b.row_token, 0xff, R * sizeof(int32_t));
     h->bound.assign(static_cast<size_t>(E * 3), 0);
     h->h_alpha_g.assign(E, 0.f);
     h->h_alpha_u.assign(E, 0.f);
@@ -417,6 +311,26 @@ int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
     return NF_OK;
 }
 
+extern "C" {
+
+// An EP rank binds only the experts it owns (into its inner handle, with
+// local ids); the others belong to other ranks and are skipped.  Inner
+// failures come back with the expert's global id.
+static int ep_relay(nf_moe* h, int st) {
+    if (st == NF_OK) return NF_OK;
+    std::string m = h->inner->err;
+    const size_t at = m.find("mlp.experts.");
+    if (at != std::string::npos) {
+        size_t end = at + 12;
+        while (end < m.size() && m[end] >= '0' && m[end] <= '9') ++end;
+        if (end > at + 12) {
+            const long long local = std::atoll(m.substr(at + 12, end - at - 12).c_str());
+            m = m.substr(0, at + 12) + std::to_string(local + h->ep_base) + m.substr(end);
+        }
+    }
+    return h->fail(st, "%s", m.c_str());
+}
+
 int nf_moe_bind_nvfp4(nf_moe* h, int expert, int proj, const uint8_t* packed, const uint8_t* scales, float ws2,
                       float in_scale, int64_t rows, int64_t cols) {
     if (!h) return NF_ERR_INVALID;
@@ -424,6 +338,10 @@ int nf_moe_bind_nvfp4(nf_moe* h, int expert, int proj, const uint8_t* packed, co
     if (d.expert_kind != NF_EXPERTS_NVFP4) return h->fail(NF_ERR_STATE, "handle holds BF16 experts");
     if (h->finalized) return h->fail(NF_ERR_STATE, "weights are already finalized");
     if (expert < 0 || expert >= d.experts || proj < 0 || proj > 2) return h->fail(NF_ERR_INVALID, "bad expert or projection id");
+    if (h->ep_outer) {
+        if (expert < h->ep_base || expert >= h->ep_base + h->ep_local) return NF_OK;
+        return ep_relay(h, nf_moe_bind_nvfp4(h->inner, expert - h->ep_base, proj, packed, scales, ws2, in_scale, rows, cols));
+    }
     if (!packed || !scales) return h->fail(NF_ERR_LAYOUT, "NVFP4 layout mlp.experts.%d.%s", expert, proj_name(proj));
     const int64_t H = d.hidden, I = d.inter;
     const int64_t want_rows = proj == NF_PROJ_DOWN ? H : I, want_cols = proj == NF_PROJ_DOWN ? I : H;
@@ -485,6 +403,11 @@ int nf_moe_bind_bf16(nf_moe* h, int which, int expert, const uint16_t* data, int
     const bool is_expert = which >= NF_BF16_EXPERT_GATE;
     if (is_expert && d.expert_kind != NF_EXPERTS_BF16) return h->fail(NF_ERR_STATE, "handle holds NVFP4 experts");
     if (is_expert && (expert < 0 || expert >= E)) return h->fail(NF_ERR_INVALID, "bad expert id");
+    if (is_expert && h->ep_outer) {
+        if (expert < h->ep_base || expert >= h->ep_base + h->ep_local) return NF_OK;
+        return ep_relay(h, nf_moe_bind_bf16(h->inner, which, expert - h->ep_base, data, rows, cols));
+    }
+    if (!is_expert && h->experts_only) return h->fail(NF_ERR_STATE, "an experts-only handle holds no %s", name);
     if ((which >= NF_BF16_SHARED_GATE && which <= NF_BF16_SHARED_DOWN) && Is == 0)
         return h->fail(NF_ERR_STATE, "descriptor has no shared expert");
     if (!data || rows != wr || cols != wc) return h->fail(NF_ERR_SHAPE, "BF16 linear layout %s", name);
@@ -569,16 +492,30 @@ int nf_moe_finalize(nf_moe* h) {
     if (h->finalized) return NF_OK;
     const nf_moe_desc& d = h->d;
     const int64_t H = d.hidden, E = d.experts, I = d.inter, Is = d.shared_inter;
-    if (!h->router_bound) return h->fail(NF_ERR_STATE, "missing tensor mlp.gate.weight");
-    if (!h->bias_bound) return h->fail(NF_ERR_STATE, "missing tensor mlp.gate.e_score_correction_bias");
+    if (!h->experts_only && !h->router_bound) return h->fail(NF_ERR_STATE, "missing tensor mlp.gate.weight");
+    if (!h->experts_only && !h->bias_bound)
+        return h->fail(NF_ERR_STATE, "missing tensor mlp.gate.e_score_correction_bias");
     if (Is > 0 && !(h->sg_bound && h->su_bound && h->sd_bound)) return h->fail(NF_ERR_STATE, "missing tensor mlp.shared_experts");
-    for (int64_t e = 0; e < E; ++e)
-        for (int p = 0; p < 3; ++p)
-            if (!h->bound[static_cast<size_t>(e * 3 + p)])
-                return h->fail(NF_ERR_STATE, "missing tensor mlp.experts.%lld.%s", static_cast<long long>(e), proj_name(p));
+    if (h->ep_outer) {
+        // the routed experts live in the inner handle (expert ids local to this rank)
+        const int st = nf_moe_finalize(h->inner);
+        if (st != NF_OK) {
+            const char* m = h->inner->err.c_str();
+            long long le = -1;
+            char proj[32] = {0};
+            if (std::sscanf(m, "missing tensor mlp.experts.%lld.%31s", &le, proj) == 2)
+                return h->fail(st, "missing tensor mlp.experts.%lld.%s", le + h->ep_base, proj);
+            return h->fail(st, "%s", m);
+        }
+    } else {
+        for (int64_t e = 0; e < E; ++e)
+            for (int p = 0; p < 3; ++p)
+                if (!h->bound[static_cast<size_t>(e * 3 + p)])
+                    return h->fail(NF_ERR_STATE, "missing tensor mlp.experts.%lld.%s", static_cast<long long>(e), proj_name(p));
+    }
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
     std::vector<float> gs_g(E, 1.f), gs_d(E, 1.f);
-    if (fp4) {
+    if (fp4 && !h->ep_outer) {
         for (int64_t e = 0; e < E; ++e) {
             if (h->h_in_g[e] != h->h_in_u[e])
                 return h->fail(NF_ERR_UNSUPPORTED,
@@ -600,7 +537,9 @@ int nf_moe_finalize(nf_moe* h) {
     if (e != cudaSuccess) return h->cuda_fail(e, "finalize copy");
     const int64_t R = h->rows_cap, Tm = d.max_tokens;
     bool ok = true;
-    if (fp4) {
+    if (h->ep_outer) {
+        // no routed workspace: only the shared expert's maps
+    } else if (fp4) {
         ok = ok && make_tmap_2d(&h->tm_a, h->pb.a_codes, false, H / 2, R, 128, 128);
         ok = ok && make_tmap_2d(&h->tm_a_s, h->pb.a_codes, false, H / 2, R, 128, 32);
         ok = ok && make_tmap_2d(&h->tm_h_s, h->h_codes, false, I / 2, R, 128, 32);
@@ -620,12 +559,12 @@ int nf_moe_finalize(nf_moe* h) {
     return NF_OK;
 }
 
-static int check_forward_args(nf_moe* h, const void* x, int tokens) {
+static int check_forward_args(nf_moe* h, const void* x, int tokens, bool device_x = true) {
     if (!h) return NF_ERR_INVALID;
     if (!h->finalized) return h->fail(NF_ERR_STATE, "nf_moe_finalize has not run");
     if (!x) return h->fail(NF_ERR_INVALID, "null input");
-    // the router copies and the combine read and write 16-byte pieces
-    if (reinterpret_cast<uintptr_t>(x) % 16 != 0) return h->fail(NF_ERR_LAYOUT, "x must be 16-byte aligned");
+    // the router copies and the combine read and write 16-byte pieces of device rows
+    if (device_x && reinterpret_cast<uintptr_t>(x) % 16 != 0) return h->fail(NF_ERR_LAYOUT, "x must be 16-byte aligned");
     if (tokens < 0) return h->fail(NF_ERR_INVALID, "negative token count");
     if (tokens > h->d.max_tokens) return h->fail(NF_ERR_CAPACITY, "tokens %d exceed max_tokens %d", tokens, h->d.max_tokens);
     return NF_OK;
@@ -648,79 +587,72 @@ int nf_moe_route(nf_moe* h, const uint16_t* x, int tokens, float* logits, int32_
     return e == cudaSuccess ? NF_OK : h->cuda_fail(e, "router launch");
 }
 
-static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx_user,
-                        float* w_user, cudaStream_t s) {
+}  // extern "C"
+
+// The shared expert (mlp_bf16, src/text_forward.cpp:917-922) on the side
+// stream: it does not depend on routing, so it is forked from `s` and
+// overlaps the router, the permutation and the routed GEMMs (the GEMMs'
+// dynamic tile scheduler absorbs the SMs it holds).  Joined by ev_join.
+int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cudaStream_t s) {
     const nf_moe_desc& d = h->d;
-    const int H = d.hidden, E = d.experts, K = d.top_k, I = d.inter, Is = d.shared_inter;
-    const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
-    int32_t* idx = idx_user ? idx_user : h->topk_idx;
-    float* w = w_user ? w_user : h->topk_w;
-    h->last_tokens = T;
-    int set = -1;
-    cudaEvent_t* ev = h->prof_begin(&set);
-    auto begin = [&](int stage, cudaStream_t st) {
-        if (!ev) return;
-        cudaEventRecord(ev[2 * stage], st);
-        h->prof_mask[static_cast<size_t>(set)] |= static_cast<uint8_t>(1u << stage);
-    };
-    auto end = [&](int stage, cudaStream_t st) {
-        if (ev) cudaEventRecord(ev[2 * stage + 1], st);
-    };
+    const int H = d.hidden, Is = d.shared_inter;
     cudaError_t e = cudaSuccess;
-    // The shared expert does not depend on routing: fork it onto the side
-    // stream so it overlaps the router, the permutation and the routed GEMMs
-    // (the GEMMs' dynamic tile scheduler absorbs the SMs it holds).
-    if (Is > 0) {
-        if ((e = cudaEventRecord(h->ev_fork, s)) != cudaSuccess ||
-            (e = cudaStreamWaitEvent(h->side, h->ev_fork, 0)) != cudaSuccess)
-            return h->cuda_fail(e, "shared expert fork");
-        CUtensorMap tm_x, tm_x_s;
-        if (!make_tmap_2d(&tm_x, x, true, H, T, 64, 128) || !make_tmap_2d(&tm_x_s, x, true, H, T, 64, 32))
-            return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-        begin(NF_STAGE_SHARED, h->side);
-        if ((e = cudaMemsetAsync(h->shared_counters, 0, 2 * sizeof(int), h->side)) != cudaSuccess)
-            return h->cuda_fail(e, "shared expert counters");
-        GemmArgs sg{};
-        sg.err = h->dev_err;
-        sg.limit = d.swiglu_limit;
-        sg.kind = KIND_BF16;
-        sg.epi = EPI_SWIGLU_BF16;
-        sg.K = H;
-        sg.dense_rows = T;
-        sg.n_blocks = Is / 128;
-        sg.b_nb = 2 * Is / 256;
-        sg.b = reinterpret_cast<const uint8_t*>(h->ws_gu);
-        sg.b_kt = static_cast<int>(k_blocks(2 * H));
-        sg.out = h->sh_h;
-        sg.out_ld = Is;
-        sg.tile_counter = h->shared_counters;
-        e = launch_gemm(tm_x, tm_x_s, sg, h->grid, h->side);
-        if (e != cudaSuccess) return h->cuda_fail(e, "shared gate/up GEMM launch");
-        sg.epi = EPI_STORE_F32;
-        sg.K = Is;
-        sg.n_blocks = H / 256;
-        sg.b_nb = H / 256;
-        sg.b = reinterpret_cast<const uint8_t*>(h->ws_dn);
-        sg.b_kt = static_cast<int>(k_blocks(2 * Is));
-        sg.out = h->sh_out;
-        sg.out_ld = H;
-        sg.tile_counter = h->shared_counters + 1;
-        e = launch_gemm(h->tm_shh, h->tm_shh_s, sg, h->grid, h->side);
-        if (e != cudaSuccess) return h->cuda_fail(e, "shared down GEMM launch");
-        end(NF_STAGE_SHARED, h->side);
-        if ((e = cudaEventRecord(h->ev_join, h->side)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
-    }
-    begin(NF_STAGE_ROUTER, s);
-    e = launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, T, H, E, K, d.routed_scaling, d.normalize, d.n_group,
-                      d.topk_group, h->router_w_safe, h->logits, h->scores, h->choices, idx, w, h->dev_err, s);
-    if (e != cudaSuccess) return h->cuda_fail(e, "router launch");
-    end(NF_STAGE_ROUTER, s);
-    begin(NF_STAGE_PERMUTE, s);
+    if ((e = cudaEventRecord(h->ev_fork, s)) != cudaSuccess || (e = cudaStreamWaitEvent(h->side, h->ev_fork, 0)) != cudaSuccess)
+        return h->cuda_fail(e, "shared expert fork");
+    CUtensorMap tm_x, tm_x_s;
+    if (!make_tmap_2d(&tm_x, x, true, H, T, 64, 128) || !make_tmap_2d(&tm_x_s, x, true, H, T, 64, 32))
+        return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    rec.begin(NF_STAGE_SHARED, h->side);
+    if ((e = cudaMemsetAsync(h->shared_counters, 0, 2 * sizeof(int), h->side)) != cudaSuccess)
+        return h->cuda_fail(e, "shared expert counters");
+    GemmArgs sg{};
+    sg.err = h->dev_err;
+    sg.limit = d.swiglu_limit;
+    sg.kind = KIND_BF16;
+    sg.epi = EPI_SWIGLU_BF16;
+    sg.K = H;
+    sg.dense_rows = T;
+    sg.n_blocks = Is / 128;
+    sg.b_nb = 2 * Is / 256;
+    sg.b = reinterpret_cast<const uint8_t*>(h->ws_gu);
+    sg.b_kt = static_cast<int>(k_blocks(2 * H));
+    sg.out = h->sh_h;
+    sg.out_ld = Is;
+    sg.tile_counter = h->shared_counters;
+    e = launch_gemm(tm_x, tm_x_s, sg, h->grid, h->side);
+    if (e != cudaSuccess) return h->cuda_fail(e, "shared gate/up GEMM launch");
+    sg.epi = EPI_STORE_F32;
+    sg.K = Is;
+    sg.n_blocks = H / 256;
+    sg.b_nb = H / 256;
+    sg.b = reinterpret_cast<const uint8_t*>(h->ws_dn);
+    sg.b_kt = static_cast<int>(k_blocks(2 * Is));
+    sg.out = h->sh_out;
+    sg.out_ld = H;
+    sg.tile_counter = h->shared_counters + 1;
+    e = launch_gemm(h->tm_shh, h->tm_shh_s, sg, h->grid, h->side);
+    if (e != cudaSuccess) return h->cuda_fail(e, "shared down GEMM launch");
+    rec.end(NF_STAGE_SHARED, h->side);
+    if ((e = cudaEventRecord(h->ev_join, h->side)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
+    return NF_OK;
+}
+
+// The routed experts for T rows of x with K expert picks each (idx, global
+// to this handle's experts): permutation + NVFP4 dispatch, grouped gate/up
+// GEMM (SwiGLU and the down input's quantisation fused), grouped down GEMM.
+// The down rows land in h->down in permuted order (h->pb.pair_row maps a
+// pick to its row).
+int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int T, int K, StageRec& rec,
+                          cudaStream_t s) {
+    const nf_moe_desc& d = h->d;
+    const int H = d.hidden, E = d.experts, I = d.inter;
+    const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
+    cudaError_t e = cudaSuccess;
+    rec.begin(NF_STAGE_PERMUTE, s);
     e = launch_permute(idx, x, T, K, E, H, I / 128, H / 256, h->gs_g, fp4 ? 0 : 1, h->pb, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "permute launch");
-    end(NF_STAGE_PERMUTE, s);
-    begin(NF_STAGE_GATE_UP, s);
-
+    rec.end(NF_STAGE_PERMUTE, s);
+    rec.begin(NF_STAGE_GATE_UP, s);
     GemmArgs g{};
     g.err = h->dev_err;
     g.limit = d.swiglu_limit;
@@ -749,8 +681,8 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.tile_counter = h->pb.meta + 4;
     e = launch_gemm(h->tm_a, h->tm_a_s, g, h->grid, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "gate/up GEMM launch");
-    end(NF_STAGE_GATE_UP, s);
-    begin(NF_STAGE_DOWN, s);
+    rec.end(NF_STAGE_GATE_UP, s);
+    rec.begin(NF_STAGE_DOWN, s);
     // down
     g.epi = fp4 ? EPI_STORE_BF16 : EPI_STORE_F32;
     g.K = I;
@@ -769,15 +701,40 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     g.tile_counter = h->pb.meta + 5;
     e = launch_gemm(h->tm_h, h->tm_h_s, g, h->grid, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "down GEMM launch");
-    end(NF_STAGE_DOWN, s);
-    if (Is > 0 && (e = cudaStreamWaitEvent(s, h->ev_join, 0)) != cudaSuccess)
-        return h->cuda_fail(e, "shared expert join");
-    begin(NF_STAGE_COMBINE, s);
-    e = launch_combine(h->down, fp4, h->pb.pair_row, w, Is > 0 ? h->sh_out : nullptr, residual, T, K, H, y, s);
-    if (e != cudaSuccess) return h->cuda_fail(e, "combine launch");
-    end(NF_STAGE_COMBINE, s);
+    rec.end(NF_STAGE_DOWN, s);
     return NF_OK;
 }
+
+static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx_user,
+                        float* w_user, cudaStream_t s) {
+    if (h->ep_outer) return ep_forward(h, x, residual, T, y, idx_user, w_user, s);
+    const nf_moe_desc& d = h->d;
+    const int H = d.hidden, E = d.experts, K = d.top_k, Is = d.shared_inter;
+    const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
+    int32_t* idx = idx_user ? idx_user : h->topk_idx;
+    float* w = w_user ? w_user : h->topk_w;
+    h->last_tokens = T;
+    StageRec rec;
+    rec.h = h;
+    rec.ev = h->prof_begin(&rec.set);
+    int st = NF_OK;
+    if (Is > 0 && (st = launch_shared_expert(h, x, T, rec, s)) != NF_OK) return st;
+    rec.begin(NF_STAGE_ROUTER, s);
+    cudaError_t e = launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, T, H, E, K,
+                                  d.routed_scaling, d.normalize, d.n_group, d.topk_group, h->router_w_safe, h->logits,
+                                  h->scores, h->choices, idx, w, h->dev_err, s);
+    if (e != cudaSuccess) return h->cuda_fail(e, "router launch");
+    rec.end(NF_STAGE_ROUTER, s);
+    if ((st = launch_routed_experts(h, x, idx, T, K, rec, s)) != NF_OK) return st;
+    if (Is > 0 && (e = cudaStreamWaitEvent(s, h->ev_join, 0)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
+    rec.begin(NF_STAGE_COMBINE, s);
+    e = launch_combine(h->down, fp4, h->pb.pair_row, w, Is > 0 ? h->sh_out : nullptr, residual, T, K, H, y, s);
+    if (e != cudaSuccess) return h->cuda_fail(e, "combine launch");
+    rec.end(NF_STAGE_COMBINE, s);
+    return NF_OK;
+}
+
+extern "C" {
 
 int nf_moe_profile(nf_moe* h, int enable) {
     if (!h) return NF_ERR_INVALID;
@@ -857,7 +814,7 @@ int nf_moe_forward(nf_moe* h, const uint16_t* x, const float* residual, int toke
     if (!y) return h->fail(NF_ERR_INVALID, "null output");
     if ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(residual)) % 16 != 0)
         return h->fail(NF_ERR_LAYOUT, "y and residual must be 16-byte aligned");
-    if (tokens == 0) return NF_OK;
+    if (tokens == 0 && !h->ep_outer) return NF_OK;  // an EP rank still takes part in the exchanges
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
@@ -865,7 +822,7 @@ int nf_moe_forward(nf_moe* h, const uint16_t* x, const float* residual, int toke
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     // graphs need a capturable stream, no per-stage events, and a caller
     // that is not capturing already
-    const bool graph = h->use_graphs && s != nullptr && !h->profiling &&
+    const bool graph = h->use_graphs && !h->ep_outer && s != nullptr && !h->profiling &&
                        cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone;
     st = graph ? forward_graph(h, x, residual, tokens, y, idx, w, s) : forward_impl(h, x, residual, tokens, y, idx, w, s);
     cudaSetDevice(prev);
@@ -887,6 +844,11 @@ int nf_moe_sync(nf_moe* h, void* stream) {
     int derr = 0;
     if (e == cudaSuccess) e = cudaMemcpy(&derr, h->dev_err, sizeof(int), cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && derr != 0) cudaMemset(h->dev_err, 0, sizeof(int));
+    if (e == cudaSuccess && derr == 0 && h->inner) {
+        // an EP rank's experts report through their own handle
+        e = cudaMemcpy(&derr, h->inner->dev_err, sizeof(int), cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess && derr != 0) cudaMemset(h->inner->dev_err, 0, sizeof(int));
+    }
     cudaSetDevice(prev);
     if (e != cudaSuccess) return h->cuda_fail(e, "synchronise");
     if (derr != 0) return h->fail(NF_ERR_TIMEOUT, "device-side wait gave up (code %d)", derr);
@@ -895,10 +857,10 @@ int nf_moe_sync(nf_moe* h, void* stream) {
 
 int nf_moe_forward_host(nf_moe* h, const float* x_host, const float* res_host, int tokens, float* y_host,
                         int32_t* idx_host, float* w_host) {
-    int st = check_forward_args(h, x_host, tokens);
+    int st = check_forward_args(h, x_host, tokens, false);
     if (st != NF_OK) return st;
     if (!y_host) return h->fail(NF_ERR_INVALID, "null output");
-    if (tokens == 0) return NF_OK;
+    if (tokens == 0 && !h->ep_outer) return NF_OK;  // an EP rank still takes part in the exchanges
     const int64_t n = static_cast<int64_t>(tokens) * h->d.hidden;
     const int64_t nk = static_cast<int64_t>(tokens) * h->d.top_k;
     int prev = 0;
@@ -913,7 +875,7 @@ int nf_moe_forward_host(nf_moe* h, const float* x_host, const float* res_host, i
         return h->cuda_fail(e, "host input copy");
     }
     const float* res = res_host ? h->res_f32 : nullptr;
-    st = (h->use_graphs && !h->profiling) ? forward_graph(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s)
+    st = (h->use_graphs && !h->ep_outer && !h->profiling) ? forward_graph(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s)
                                           : forward_impl(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s);
     if (st == NF_OK) {
         e = cudaMemcpyAsync(y_host, h->y_f32, n * 4, cudaMemcpyDeviceToHost, s);

@@ -1,0 +1,55 @@
+"""Host-side statement of the expert-parallel exchange layout (numpy).
+
+The library's EP forward (csrc/nf_ep.cu, ep_pack_kernel in csrc/nf_kernels.cu)
+sends every (token, pick) of a rank to the rank that owns the picked expert,
+in (destination, token, pick) order, and combines the returned expert outputs
+in pick order.  This module restates that layout so that a host (or a test)
+can reason about it without a GPU: which rank owns an expert, the send slot
+of every pick, the rows and destination-local experts in send order, the
+per-destination counts and the receive offsets.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+
+def owner(expert: np.ndarray, experts: int, world: int) -> np.ndarray:
+    """Rank that owns each (global) expert id: experts [r E/R, (r+1) E/R)."""
+    if experts % world:
+        raise ValueError("the experts must divide evenly over the ranks")
+    return np.asarray(expert) // (experts // world)
+
+
+@dataclass
+class SendPlan:
+    slot: np.ndarray        # [T, K] send slot of each pick (the combine's pair_row)
+    send_token: np.ndarray  # [T*K] source token of each slot
+    send_expert: np.ndarray # [T*K] destination-local expert of each slot
+    counts: np.ndarray      # [world] picks sent to each rank
+    offsets: np.ndarray     # [world + 1] first slot of each destination
+
+
+def pack(idx: np.ndarray, experts: int, world: int) -> SendPlan:
+    """The (destination, token, pick) layout of a rank's picks; idx [T, K]."""
+    idx = np.asarray(idx, dtype=np.int64)
+    T, K = idx.shape
+    per = experts // world
+    dest = owner(idx, experts, world).ravel()
+    counts = np.bincount(dest, minlength=world).astype(np.int64)
+    offsets = np.concatenate([[0], np.cumsum(counts)])
+    order = np.argsort(dest, kind="stable")  # stable: token-major, pick-minor inside a destination
+    slot = np.empty(T * K, np.int64)
+    slot[order] = np.arange(T * K)
+    flat = np.arange(T * K)
+    send_token = np.empty(T * K, np.int64)
+    send_expert = np.empty(T * K, np.int64)
+    send_token[slot] = flat // K
+    send_expert[slot] = idx.ravel() - dest * per
+    return SendPlan(slot.reshape(T, K), send_token, send_expert, counts, offsets)
+
+
+def receive_offsets(recv_counts: np.ndarray) -> np.ndarray:
+    """First received row of each source rank (rows arrive in rank order)."""
+    return np.concatenate([[0], np.cumsum(np.asarray(recv_counts, dtype=np.int64))])

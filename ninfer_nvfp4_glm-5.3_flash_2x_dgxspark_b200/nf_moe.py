@@ -39,7 +39,7 @@ EXPORTED = [
     "nf_moe_bind_bf16", "nf_moe_bind_f32", "nf_moe_finalize", "nf_moe_forward", "nf_moe_forward_host",
     "nf_moe_sync", "nf_moe_route", "nf_moe_debug_tensor", "nf_moe_debug_read", "nf_nvfp4_dequantize", "nf_nvfp4_quantize",
     "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck", "nf_moe_set_graph_mode",
-    "nf_router_topk_noalloc",
+    "nf_router_topk_noalloc", "nf_ep_unique_id", "nf_moe_create_ep",
 ]
 STAGES = ["router", "permute", "gate_up", "down", "shared", "combine"]
 
@@ -89,6 +89,8 @@ def load() -> ctypes.CDLL:
         "nf_moe_stage_times": ([P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(I32)], I32),
         "nf_router_topk_noalloc": ([P, P, P, I32, I32, I32, I32, I32, I32, I32, F, P, P, ctypes.c_char_p, I32, P],
                                    I32),
+        "nf_ep_unique_id": ([ctypes.c_char_p, I32], I32),
+        "nf_moe_create_ep": ([ctypes.POINTER(Desc), I32, I32, I32, ctypes.c_char_p, I32, ctypes.POINTER(P)], I32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -120,16 +122,26 @@ class MoeLayer:
 
     def __init__(self, hidden: int, experts: int, top_k: int, inter: int, shared_inter: int, *,
                  routed_scaling: float = 1.0, swiglu_limit: float = 10.0, n_group: int = 1, topk_group: int = 1,
-                 normalize: bool = True, bf16_experts: bool = False, max_tokens: int = 64, device: int = 0):
+                 normalize: bool = True, bf16_experts: bool = False, max_tokens: int = 64, device: int = 0,
+                 ep: tuple[int, int, bytes] | None = None):
+        """ep = (rank, world, group_id) makes this rank's handle of an expert-
+        parallel group (group_id from ep_group_id() on one rank, shared by all);
+        max_tokens is then per rank."""
         self.lib = load()
         self.desc = Desc(hidden, experts, top_k, inter, shared_inter, n_group, topk_group, int(normalize),
                          routed_scaling, swiglu_limit, EXPERTS_BF16 if bf16_experts else EXPERTS_NVFP4, max_tokens)
         h = ctypes.c_void_p()
-        st = self.lib.nf_moe_create(ctypes.byref(self.desc), device, ctypes.byref(h))
+        if ep is None:
+            st = self.lib.nf_moe_create(ctypes.byref(self.desc), device, ctypes.byref(h))
+        else:
+            rank, world, group_id = ep
+            st = self.lib.nf_moe_create_ep(ctypes.byref(self.desc), device, rank, world, group_id, len(group_id),
+                                           ctypes.byref(h))
         if st != NF_OK:
             raise NfError(st, self.lib.nf_moe_last_error(None).decode())
         self.h = h
         self.device = device
+        self.ep = ep
 
     def close(self) -> None:
         if getattr(self, "h", None):
@@ -298,6 +310,18 @@ def router_topk_noalloc(x_dev, router_w_dev, bias_dev, tokens: int, hidden: int,
                                        top_k, n_group, topk_group, int(normalize), routed_scaling, _ptr(idx_dev),
                                        _ptr(w_dev), buf, len(buf), stream or None)
     return st, buf.value.decode()
+
+
+EP_ID_BYTES = 128
+
+
+def ep_group_id() -> bytes:
+    """A new expert-parallel group id (NCCL unique id) to hand to every rank."""
+    buf = ctypes.create_string_buffer(EP_ID_BYTES)
+    st = load().nf_ep_unique_id(buf, EP_ID_BYTES)
+    if st != NF_OK:
+        raise NfError(st, load().nf_moe_last_error(None).decode())
+    return buf.raw
 
 
 def format_selfcheck() -> tuple[int, int, int]:

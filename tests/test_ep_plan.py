@@ -1,0 +1,125 @@
+"""Expert parallelism on the CPU: the (destination, token, pick) exchange
+layout, and the whole EP decomposition run by two gloo ranks -- route own
+tokens, send rows to the owners of the picked experts, run the experts there
+(the oracle's expert_forward), send the outputs back, combine in pick order --
+against the single-rank oracle layer, bit for bit."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+from helpers import PKG, REPO, load_module, oracle, workload
+
+plan = load_module("nf_ep_plan", PKG / "ep_plan.py")
+
+
+def test_owner_blocks():
+    assert list(plan.owner(np.arange(8), 8, 2)) == [0, 0, 0, 0, 1, 1, 1, 1]
+    assert list(plan.owner(np.arange(64), 64, 8)[::8]) == list(range(8))
+    with pytest.raises(ValueError):
+        plan.owner(np.arange(6), 6, 4)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_pack_is_destination_token_pick_order(world):
+    rng = np.random.default_rng(world)
+    T, K, E = 37, 4, 64
+    idx = np.stack([rng.choice(E, K, replace=False) for _ in range(T)])
+    sp = plan.pack(idx, E, world)
+    dest = plan.owner(idx, E, world)
+    # brute force: sort (dest, t, p)
+    keys = sorted((int(dest[t, p]), t, p) for t in range(T) for p in range(K))
+    for s, (d, t, p) in enumerate(keys):
+        assert sp.slot[t, p] == s
+        assert sp.send_token[s] == t
+        assert sp.send_expert[s] == idx[t, p] - d * (E // world)
+    assert list(sp.counts) == [int((dest == d).sum()) for d in range(world)]
+    assert sp.offsets[-1] == T * K
+    assert sorted(sp.slot.ravel()) == list(range(T * K))
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _exchange(dist, send: list, recv_shapes: list, dtype, rank: int, world: int) -> list:
+    """Point-to-point exchange: send[p] to rank p, receive from every rank."""
+    import torch
+
+    out = [None] * world
+    reqs = []
+    for p in range(world):
+        if p == rank:
+            out[p] = send[p].copy()
+            continue
+        buf = torch.empty(recv_shapes[p], dtype=dtype)
+        out[p] = buf
+        reqs.append(dist.isend(torch.from_numpy(np.ascontiguousarray(send[p])), p))
+        reqs.append(dist.irecv(buf, p))
+    for r in reqs:
+        r.wait()
+    return [o if isinstance(o, np.ndarray) else o.numpy() for o in out]
+
+
+def _ep_rank(rank: int, world: int, port: int, out_dir: str) -> None:
+    sys.path.insert(0, str(REPO / "tests"))
+    import torch
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    wl, orc = workload(), oracle()
+    lay, x_bits = wl.config_layer("c0")
+    x_all = wl.bf16_bits_to_f32(x_bits)
+    T_all, H, E, K = x_all.shape[0], lay.hidden, lay.experts, lay.top_k
+    per_tok = T_all // world
+    x = x_all[rank * per_tok:(rank + 1) * per_tok]
+    # 1. route own tokens; the shared expert of own tokens (tap of the port layer)
+    _, idx, w = orc.route_tokens(lay, x)
+    _, _, _, _, shared = orc.moe_layer(orc.port(), lay, x, taps=True)
+    # 2. send rows to the experts' owners in (destination, token, pick) order
+    sp = plan.pack(idx, E, world)
+    rows = x[sp.send_token]
+    counts = _exchange(dist, [np.array([c], np.int64) for c in sp.counts], [(1,)] * world, torch.int64, rank, world)
+    rc = np.array([int(c[0]) for c in counts])
+    send_rows = [rows[sp.offsets[p]:sp.offsets[p + 1]] for p in range(world)]
+    send_e = [sp.send_expert[sp.offsets[p]:sp.offsets[p + 1]] for p in range(world)]
+    recv_rows = _exchange(dist, send_rows, [(int(c), H) for c in rc], torch.float32, rank, world)
+    recv_e = _exchange(dist, send_e, [(int(c),) for c in rc], torch.int64, rank, world)
+    # 3. the owned experts on the received rows
+    base = rank * (E // world)
+    outs = []
+    for p in range(world):
+        o = np.zeros((rc[p], H), np.float32)
+        for i in range(rc[p]):
+            o[i] = orc.expert_forward(lay, base + int(recv_e[p][i]), recv_rows[p][i])[1]
+        outs.append(o)
+    # 4. outputs back to their sources, in send order
+    back = _exchange(dist, outs, [(int(c), H) for c in sp.counts], torch.float32, rank, world)
+    ret = np.concatenate(back) if back else np.zeros((0, H), np.float32)
+    # 5. combine in pick order (y = 0; y += w_p * down_p), then the shared expert
+    y = np.zeros((per_tok, H), np.float32)
+    for t in range(per_tok):
+        acc = np.zeros(H, np.float32)
+        for p in range(K):
+            acc = acc + np.float32(w[t, p]) * ret[sp.slot[t, p]]
+        y[t] = acc + shared[t]
+    np.save(os.path.join(out_dir, f"y{rank}.npy"), y)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_ep_decomposition_matches_single_rank(tmp_path, world):
+    import torch.multiprocessing as mp
+
+    port = _free_port()
+    mp.start_processes(_ep_rank, args=(world, port, str(tmp_path)), nprocs=world, start_method="spawn", join=True)
+    wl, orc = workload(), oracle()
+    lay, x_bits = wl.config_layer("c0")
+    y_ref, _, _ = orc.moe_layer(orc.port(), lay, wl.bf16_bits_to_f32(x_bits))
+    y_ep = np.concatenate([np.load(tmp_path / f"y{r}.npy") for r in range(world)])
+    assert np.array_equal(y_ep.view(np.uint32), y_ref.view(np.uint32))

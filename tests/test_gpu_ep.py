@@ -1,0 +1,98 @@
+"""Expert parallelism on 2 GPUs (one process per GPU, NCCL point-to-point
+exchange inside the library) against one GPU holding every expert: the layer
+outputs and routes must be identical bit for bit.  Skipped on fewer than two
+GPUs."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+from helpers import REPO, nfm, workload
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tokens(case: str, world: int):
+    """(layer, token bits of every rank)."""
+    wl = workload()
+    if case == "c1":
+        lay, x = wl.config_layer("c1")
+        return lay, np.array_split(x, world)
+    if case == "uneven":  # all tokens on rank 0, none on rank 1
+        lay, x = wl.config_layer("c1")
+        return lay, [x] + [x[:0]] * (world - 1)
+    # skewed: Zipf log-prior on the bias sends most picks to the first experts (rank 0)
+    cfg = dict(wl.CONFIGS["c1"])
+    lay = wl.make_layer(cfg, seed=7)
+    lay.bias = (lay.bias + np.log((np.arange(lay.experts) + 1.0) ** -1.1)).astype(np.float32)
+    x = wl.make_tokens(cfg, seed=7, tokens=96 * world)
+    return lay, np.array_split(x, world)
+
+
+def _rank(rank: int, world: int, port: int, out_dir: str, case: str) -> None:
+    sys.path.insert(0, str(REPO / "tests"))
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    m = nfm()
+    gid = [m.ep_group_id() if rank == 0 else None]
+    dist.broadcast_object_list(gid, src=0)
+    lay, parts = _tokens(case, world)
+    cap = max(p.shape[0] for p in parts)
+    layer = m.MoeLayer(lay.hidden, lay.experts, lay.top_k, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                       swiglu_limit=lay.swiglu_limit, max_tokens=max(cap, 1), device=rank, ep=(rank, world, gid[0]))
+    layer.bind_layer(lay)
+    xb = parts[rank]
+    T = xb.shape[0]
+    x = torch.from_numpy(np.ascontiguousarray(xb).view(np.int16)).cuda() if T else torch.zeros((1, lay.hidden), dtype=torch.int16, device="cuda")
+    y = torch.zeros((max(T, 1), lay.hidden), dtype=torch.float32, device="cuda")
+    idx = torch.zeros((max(T, 1), lay.top_k), dtype=torch.int32, device="cuda")
+    w = torch.zeros((max(T, 1), lay.top_k), dtype=torch.float32, device="cuda")
+    for _ in range(2):  # two steps in a row reuse the buffers
+        layer.forward(x, y, T, None, idx, w)
+        layer.sync()
+    np.savez(os.path.join(out_dir, f"r{rank}.npz"), y=y.cpu().numpy()[:T], idx=idx.cpu().numpy()[:T], w=w.cpu().numpy()[:T])
+    layer.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", ["c1", "uneven", "skewed"])
+def test_ep2_matches_one_gpu(tmp_path, case):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    world = 2
+    mp.start_processes(_rank, args=(world, _free_port(), str(tmp_path), case), nprocs=world, start_method="spawn",
+                       join=True)
+    m = nfm()
+    lay, parts = _tokens(case, world)
+    xb = np.concatenate(parts)
+    T = xb.shape[0]
+    layer = m.MoeLayer(lay.hidden, lay.experts, lay.top_k, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                       swiglu_limit=lay.swiglu_limit, max_tokens=T)
+    layer.bind_layer(lay)
+    x = torch.from_numpy(np.ascontiguousarray(xb).view(np.int16)).cuda()
+    y = torch.zeros((T, lay.hidden), dtype=torch.float32, device="cuda")
+    idx = torch.zeros((T, lay.top_k), dtype=torch.int32, device="cuda")
+    w = torch.zeros((T, lay.top_k), dtype=torch.float32, device="cuda")
+    layer.forward(x, y, T, None, idx, w)
+    layer.sync()
+    got = [np.load(tmp_path / f"r{r}.npz") for r in range(world)]
+    y_ep = np.concatenate([g["y"] for g in got])
+    assert np.array_equal(np.concatenate([g["idx"] for g in got]), idx.cpu().numpy())
+    assert np.array_equal(np.concatenate([g["w"] for g in got]).view(np.uint32), w.cpu().numpy().view(np.uint32))
+    assert np.array_equal(y_ep.view(np.uint32), y.cpu().numpy().view(np.uint32))
+    layer.close()
