@@ -14,9 +14,11 @@ dominant kernel (the grouped gate/up GEMM), the end-to-end number through
 the host-buffer C-ABI call, the reference CPU path timed on this host, and a
 secondary prefill measurement (configs[2], 8192 tokens, tensor roofline).
 
-With N > 1 (torchrun), every rank runs the same decode batch on its own GPU
-("replicas": no cross-rank exchange in this build); value sums the tokens of
-all ranks over the max-over-ranks device time.
+With N > 1 (torchrun), the layer is expert-parallel: each rank owns E/N
+experts and brings its own 64-token decode batch (weak scaling: tokens per
+GPU fixed); rows travel to the experts' owners and back over NCCL inside the
+library.  value sums the tokens of all ranks over the max-over-ranks device
+time.
 
 --impl reference times the reference's own CPU implementation (its sources
 compiled under oracle/_ref, else the C restatement) on this host's cores over
@@ -192,9 +194,19 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     fp4_peak = 4 * bf16_peak  # dense FP4 is 4x dense BF16 on this part
 
     lay, x_bits = wl.config_layer("c1")
+    if world > 1:
+        # every rank brings its own decode batch of the same size
+        x_bits = wl.make_tokens(wl.CONFIGS["c1"], seed=1 + rank)
     T, H, K = x_bits.shape[0], lay.hidden, lay.top_k
+    ep = None
+    if world > 1:
+        # expert parallel: this rank owns E / world experts; the group id
+        # comes from rank 0
+        gid = [m.ep_group_id() if rank == 0 else None]
+        dist.broadcast_object_list(gid, src=0)
+        ep = (rank, world, gid[0])
     layer = m.MoeLayer(H, lay.experts, K, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
-                       swiglu_limit=lay.swiglu_limit, max_tokens=T, device=local)
+                       swiglu_limit=lay.swiglu_limit, max_tokens=T, device=local, ep=ep)
     layer.bind_layer(lay)
     x = torch.from_numpy(x_bits.view(np.int16)).cuda()
     y = torch.empty((T, H), dtype=torch.float32, device="cuda")
@@ -203,9 +215,11 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     # The layer runs on its own stream; with graph mode on, the first forward
     # for a token count captures the layer's launches into a CUDA graph and
     # later forwards replay it (one launch per step on the host side).
+    # (An expert-parallel forward synchronises the host once for the row
+    # counts, so it runs without a graph.)
     tstream = torch.cuda.Stream()
     stream = tstream.cuda_stream
-    layer.set_graph_mode(True)
+    layer.set_graph_mode(world == 1)
 
     def step():
         layer.forward(x, y, T, None, idx, w, stream=stream)
@@ -215,11 +229,11 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     layer.sync(stream)
     clocks = ClockSampler(local)
     clocks.start()
-    t_end = time.perf_counter() + 0.6  # settle clocks under the same load before timing
-    while time.perf_counter() < t_end:
-        for _ in range(20):
-            step()
-        tstream.synchronize()
+    # settle clocks under the same load before timing (a fixed step count:
+    # every rank of an expert-parallel group takes the same steps)
+    for _ in range(5000 if world == 1 else 300):
+        step()
+    tstream.synchronize()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -238,11 +252,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     torch.cuda.synchronize()
     stages, nfw = layer.stage_times()
     layer.profile(False)
-    t_end = time.perf_counter() + 0.3
-    while time.perf_counter() < t_end:
-        for _ in range(20):
-            step()
-        tstream.synchronize()
+    for _ in range(2000 if world == 1 else 150):
+        step()
+    tstream.synchronize()
     clk = clocks.stop()
     layer.sync(stream)
     if dist:
@@ -288,7 +300,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "nvfp4 (E2M1 x UE4M3/16, fp32 accumulate); bf16 shared expert", "data": "synthetic",
             "config": {"workload": "c1 decode: H2048 E64 k4 I1536 Is1536 T64 scale2.5 (configs[1])",
-                       "tokens_per_gpu": T, "parallelism": "replicas" if world > 1 else "single",
+                       "tokens_per_gpu": T, "parallelism": f"ep{world}" if world > 1 else "single",
                        "l2": "no flush: the 340 MB of weights streamed per step exceed the 126 MB L2",
                        "active_experts": active},
             "stages_us": {k: 1e3 * v for k, v in stage_ms.items()},
@@ -308,6 +320,10 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         }
     if world == 1 and not args.no_prefill:
         line["prefill"] = run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src)
+    if not args.no_prefill:
+        ep3 = run_ep_c3(args, m, torch, rank, world, local, dist)
+        if rank == 0:
+            line["ep_c3"] = ep3
     if rank == 0 and world == 1:
         rate, info = cpu_reference_rate(lay, x_bits, T)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", **info}
@@ -365,6 +381,54 @@ def run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src) -> dict:
                      "peak_source": f"4 x {peak_src} dense BF16 ({bf16_peak:.0f} TFLOP/s); nominal dense FP4 9000",
                      "down_tflops": (fl["fp4"] - fl["fp4_gate_up"]) / (dn_ms * 1e-3) / 1e12},
     }
+
+
+def run_ep_c3(args, m, torch, rank: int, world: int, local: int, dist) -> dict:
+    """16384 tokens per step split over the ranks (strong scaling),
+    experts sharded evenly, router bias + Zipf(1.1) log-prior (lambda = 1, as
+    the configuration states: nearly every pick lands on the first experts,
+    i.e. on rank 0).  Device time per step, max over ranks."""
+    lay, x_all = wl.config_layer("c3")
+    T_all, H, K = x_all.shape[0], lay.hidden, lay.top_k
+    per = T_all // world
+    xb = x_all[rank * per:(rank + 1) * per]
+    ep = None
+    if world > 1:
+        gid = [m.ep_group_id() if rank == 0 else None]
+        dist.broadcast_object_list(gid, src=0)
+        ep = (rank, world, gid[0])
+    layer = m.MoeLayer(H, lay.experts, K, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                       swiglu_limit=lay.swiglu_limit, max_tokens=per, device=local, ep=ep)
+    layer.bind_layer(lay)
+    x = torch.from_numpy(np.ascontiguousarray(xb).view(np.int16)).cuda()
+    y = torch.empty((per, H), dtype=torch.float32, device="cuda")
+    idx = torch.empty((per, K), dtype=torch.int32, device="cuda")
+    ts = torch.cuda.Stream()
+    steps = max(3, min(args.steps, 10))
+    for _ in range(args.warmup):
+        layer.forward(x, y, per, None, idx, None, stream=ts.cuda_stream)
+    ts.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(ts)
+    for _ in range(steps):
+        layer.forward(x, y, per, None, idx, None, stream=ts.cuda_stream)
+    ev1.record(ts)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    owners = np.bincount(idx.cpu().numpy().ravel() // (lay.experts // world), minlength=world)
+    layer.sync(ts.cuda_stream)
+    layer.close()
+    return {"workload": "c3: c1 shapes, 16384 tokens per step split over the ranks, Zipf(1.1) log-prior lambda = 1 "
+                        "(configs[3])", "tokens_per_s": T_all / (ms * 1e-3), "ms_per_step": ms, "steps": steps,
+            "scaling": "strong", "parallelism": f"ep{world}" if world > 1 else "single",
+            "rank0_picks_by_owner": [int(c) for c in owners]}
 
 
 def run_decode_only(args, m, torch) -> dict:
