@@ -1,0 +1,103 @@
+// moe_demo.cpp -- a C++ host running one MoE layer through nf_host::MoeLayer:
+// reads a tensor file (checkpoint names, the reference's tensor kinds), binds
+// the layer by name, runs TextModel::moe's contract over the token rows `x`
+// and writes y.  It stands where the reference's own host would sit.
+//
+// usage: moe_demo <tensors.nft> <prefix> <out_y.f32> hidden experts top_k inter shared_inter
+//                 routed_scaling [device]
+// tensor file: "NFT1", then records {u32 name_len, name, u8 kind, u32 rank,
+// i64 dims[rank], u64 bytes, data}; `x` is F32 [tokens, hidden].
+#include "nf_moe_layer.hpp"
+
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <iostream>
+#include <map>
+#include <string>
+#include <vector>
+
+namespace {
+
+struct Record {
+    nf_host::TensorView view;
+    std::vector<unsigned char> bytes;
+};
+
+std::map<std::string, Record> read_tensors(const char* path) {
+    std::ifstream in(path, std::ios::binary);
+    if (!in) throw std::runtime_error(std::string("cannot open ") + path);
+    char magic[4];
+    in.read(magic, 4);
+    if (!in || std::memcmp(magic, "NFT1", 4) != 0) throw std::runtime_error("not a tensor file");
+    std::map<std::string, Record> out;
+    for (;;) {
+        uint32_t n = 0;
+        if (!in.read(reinterpret_cast<char*>(&n), 4)) break;
+        std::string name(n, '\0');
+        in.read(&name[0], n);
+        unsigned char kind = 0;
+        uint32_t rank = 0;
+        in.read(reinterpret_cast<char*>(&kind), 1);
+        in.read(reinterpret_cast<char*>(&rank), 4);
+        Record r;
+        r.view.kind = static_cast<char>(kind);
+        r.view.shape.resize(rank);
+        in.read(reinterpret_cast<char*>(r.view.shape.data()), static_cast<std::streamsize>(8 * rank));
+        uint64_t bytes = 0;
+        in.read(reinterpret_cast<char*>(&bytes), 8);
+        r.bytes.resize(bytes);
+        in.read(reinterpret_cast<char*>(r.bytes.data()), static_cast<std::streamsize>(bytes));
+        if (!in) throw std::runtime_error("truncated tensor " + name);
+        out.emplace(name, std::move(r));
+    }
+    for (auto& kv : out) kv.second.view.data = kv.second.bytes.data();
+    return out;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    if (argc < 10) {
+        std::fprintf(stderr, "usage: %s tensors.nft prefix out_y.f32 hidden experts top_k inter shared_inter scaling [device]\n",
+                     argv[0]);
+        return 2;
+    }
+    try {
+        const auto store = read_tensors(argv[1]);
+        const std::string prefix = argv[2];
+        auto lookup = [&](const std::string& name) -> const nf_host::TensorView* {
+            const auto it = store.find(name);
+            return it == store.end() ? nullptr : &it->second.view;
+        };
+        const nf_host::TensorView* x = lookup("x");
+        if (!x || x->kind != 'f' || x->shape.size() != 2) throw std::runtime_error("missing tensor x");
+        nf_moe_desc d{};
+        d.hidden = std::atoi(argv[4]);
+        d.experts = std::atoi(argv[5]);
+        d.top_k = std::atoi(argv[6]);
+        d.inter = std::atoi(argv[7]);
+        d.shared_inter = std::atoi(argv[8]);
+        d.n_group = 1;
+        d.topk_group = 1;
+        d.normalize = 1;
+        d.routed_scaling = static_cast<float>(std::atof(argv[9]));
+        d.swiglu_limit = 10.f;
+        d.expert_kind = NF_EXPERTS_NVFP4;
+        d.max_tokens = static_cast<int>(x->dim(0));
+        const int device = argc > 10 ? std::atoi(argv[10]) : 0;
+        nf_host::MoeLayer layer(d, device);
+        layer.bind_from_store(lookup, prefix);
+        std::vector<float> y(static_cast<size_t>(x->dim(0) * x->dim(1)));
+        layer.moe(static_cast<const float*>(x->data), y.data(), static_cast<int>(x->dim(0)));
+        std::ofstream out(argv[3], std::ios::binary);
+        out.write(reinterpret_cast<const char*>(y.data()), static_cast<std::streamsize>(y.size() * 4));
+        double sum = 0;
+        for (float v : y) sum += v;
+        std::printf("moe_demo: %lld tokens, checksum %.9g\n", static_cast<long long>(x->dim(0)), sum);
+    } catch (const std::exception& e) {
+        std::fprintf(stderr, "moe_demo: %s\n", e.what());
+        return 1;
+    }
+    return 0;
+}

@@ -1,0 +1,113 @@
+// nf_moe_layer.hpp -- C++ host class over the C-ABI of include/nf_moe.h, in the
+// shape of the reference's MoE path: tensors looked up by checkpoint name
+// from a store (Store::get, src/text_forward.cpp:464-470; kinds 'b' BF16,
+// 'f' F32, 'u' U8, '8' F8_E4M3, :408-414), the parameter_schema names of one
+// MoE layer (src/parameter_schema.cpp:72-98), and a forward with
+// TextModel::moe's arguments (prefix, x, y) (src/text_forward.cpp:924).
+// Failures throw std::runtime_error with the library's message, as the
+// reference's fail() does (src/text_forward.cpp:40).  Header-only: link
+// lib/libnf_moe.so.
+#pragma once
+
+#include "nf_moe.h"
+
+#include <cstdint>
+#include <functional>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace nf_host {
+
+// A borrowed tensor: what the reference's Store hands out.
+struct TensorView {
+    const void* data = nullptr;
+    std::vector<int64_t> shape;
+    char kind = '?';  // 'b' BF16, 'f' F32, 'u' U8, '8' F8_E4M3
+    int64_t dim(int axis) const {
+        if (axis < 0 || axis >= static_cast<int>(shape.size())) throw std::runtime_error("tensor rank is short");
+        return shape[static_cast<size_t>(axis)];
+    }
+};
+
+// Name -> tensor; throws "missing tensor <name>" like Store::get.
+using StoreLookup = std::function<const TensorView*(const std::string&)>;
+
+class MoeLayer {
+public:
+    // desc: the layer's shapes (from ModelSpec); max_tokens per forward.
+    MoeLayer(const nf_moe_desc& desc, int device) {
+        if (nf_moe_create(&desc, device, &h_) != NF_OK) throw std::runtime_error(nf_moe_last_error(nullptr));
+        d_ = desc;
+    }
+    MoeLayer(const MoeLayer&) = delete;
+    MoeLayer& operator=(const MoeLayer&) = delete;
+    ~MoeLayer() { nf_moe_destroy(h_); }
+
+    nf_moe* handle() const { return h_; }
+
+    // Binds every tensor of the layer `prefix` (e.g. "model.language_model.layers.3.")
+    // by checkpoint name and finalizes.
+    void bind_from_store(const StoreLookup& store, const std::string& prefix) {
+        auto get = [&](const std::string& name) -> const TensorView& {
+            const TensorView* t = store(name);
+            if (!t) throw std::runtime_error("missing tensor " + name);
+            return *t;
+        };
+        auto bf16 = [&](int which, int expert, const std::string& name) {
+            const TensorView& t = get(name);
+            if (t.kind != 'b' || t.shape.size() != 2) throw std::runtime_error("BF16 linear layout " + name);
+            check(nf_moe_bind_bf16(h_, which, expert, static_cast<const uint16_t*>(t.data), t.dim(0), t.dim(1)));
+        };
+        auto scalar = [&](const std::string& name) {
+            const TensorView& t = get(name);
+            if (t.kind != 'f' || !t.shape.empty()) throw std::runtime_error("expected rank-0 F32 for " + name);
+            return *static_cast<const float*>(t.data);
+        };
+        bf16(NF_BF16_ROUTER, 0, prefix + "mlp.gate.weight");
+        const TensorView& bias = get(prefix + "mlp.gate.e_score_correction_bias");
+        if (bias.kind != 'f' || bias.shape.size() != 1)
+            throw std::runtime_error("vector length mismatch for " + prefix + "mlp.gate.e_score_correction_bias");
+        check(nf_moe_bind_f32(h_, NF_F32_ROUTER_BIAS, static_cast<const float*>(bias.data), bias.dim(0)));
+        if (d_.shared_inter > 0) {
+            bf16(NF_BF16_SHARED_GATE, 0, prefix + "mlp.shared_experts.gate_proj.weight");
+            bf16(NF_BF16_SHARED_UP, 0, prefix + "mlp.shared_experts.up_proj.weight");
+            bf16(NF_BF16_SHARED_DOWN, 0, prefix + "mlp.shared_experts.down_proj.weight");
+        }
+        static const char* proj[3] = {"gate_proj", "up_proj", "down_proj"};
+        for (int e = 0; e < d_.experts; ++e)
+            for (int p = 0; p < 3; ++p) {
+                const std::string base = prefix + "mlp.experts." + std::to_string(e) + "." + proj[p];
+                if (d_.expert_kind == NF_EXPERTS_BF16) {
+                    bf16(NF_BF16_EXPERT_GATE + p, e, base + ".weight");
+                    continue;
+                }
+                const TensorView& w = get(base + ".weight");
+                const TensorView& s = get(base + ".weight_scale");
+                if (w.kind != 'u' || s.kind != '8' || w.shape.size() != 2) throw std::runtime_error("NVFP4 layout " + base);
+                check(nf_moe_bind_nvfp4(h_, e, p, static_cast<const uint8_t*>(w.data), static_cast<const uint8_t*>(s.data),
+                                        scalar(base + ".weight_scale_2"), scalar(base + ".input_scale"), w.dim(0),
+                                        w.dim(1) * 2));
+            }
+        check(nf_moe_finalize(h_));
+    }
+
+    // TextModel::moe's contract over `tokens` rows: x fp32 (BF16-valued) in,
+    // y fp32 out, host memory; synchronous.
+    void moe(const float* x, float* y, int tokens = 1) {
+        check(nf_moe_forward_host(h_, x, nullptr, tokens, y, nullptr, nullptr));
+    }
+    // The same with the routes (indices, weights: tokens x top_k).
+    void moe(const float* x, float* y, int tokens, int32_t* idx, float* w) {
+        check(nf_moe_forward_host(h_, x, nullptr, tokens, y, idx, w));
+    }
+
+private:
+    void check(int status) const {
+        if (status != NF_OK) throw std::runtime_error(nf_moe_last_error(h_));
+    }
+    nf_moe* h_ = nullptr;
+    nf_moe_desc d_{};
+};
+
+}  // namespace nf_host
