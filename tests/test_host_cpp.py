@@ -20,7 +20,7 @@ def write_nft(path, tensors: dict) -> None:
     with open(path, "wb") as f:
         f.write(b"NFT1")
         for name, (kind, arr) in tensors.items():
-            a = np.ascontiguousarray(arr, dtype=KIND[kind])
+            a = np.array(arr, dtype=KIND[kind], order="C")  # keeps rank-0 scalars rank 0
             nb = name.encode()
             f.write(struct.pack("<I", len(nb)) + nb + kind.encode() + struct.pack("<I", a.ndim))
             f.write(struct.pack(f"<{a.ndim}q", *a.shape) if a.ndim else b"")
