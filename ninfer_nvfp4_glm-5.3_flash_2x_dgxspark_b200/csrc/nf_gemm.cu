@@ -10,12 +10,20 @@
 // rows of the same intermediate block, interleaved at bind time, so the
 // epilogue sees gate and up of one output column in one thread).
 // Pipeline: 4 shared-memory stages of 128-byte K slices (256 FP4 or 64 BF16
-// elements) loaded by TMA with 128-byte swizzle; block-scale atoms arrive by
-// 1-D bulk copy and move to TMEM with tcgen05.cp; one elected thread issues
-// the MMAs and commits stage release / accumulator-ready to mbarriers.
-// Warp roles (576 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
+// elements) loaded by TMA with 128-byte swizzle (B from its box-order copy:
+// one contiguous 32 KB box per stage); block-scale atoms arrive by 1-D bulk
+// copy (B's in tile order: one 4 KB copy per stage) and move to TMEM with
+// tcgen05.cp; one elected thread issues the MMAs and commits stage release /
+// accumulator-ready to mbarriers.
+// A thread completes its tcgen05.cp copies one after another (~150 cycles
+// each), and in one thread's stream they also hold up the MMAs behind them:
+// the 12 scale-atom copies of a stage cost about three times the stage's 4
+// MMAs.  So separate scale warps issue them, split between them, one stage
+// ahead of the MMA thread, which waits on a per-stage "scales in TMEM"
+// barrier instead.
+// Warp roles (640 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
 // issuer, warps 2-17 epilogue (TMEM lane quadrant = warp % 4, four column
-// slices per quadrant).
+// slices per quadrant), warps 18-19 scale-factor copies (NVFP4).
 // The persistent grid walks a device-side tile list, so the launch needs no
 // host synchronisation after routing: the producer claims tiles in list
 // order with an atomic counter and publishes each to the MMA and epilogue
@@ -32,9 +40,11 @@ namespace nf {
 
 constexpr int BM = 128, BN = 256, STAGES = 4;
 constexpr int kEpiWarps = 16;
+constexpr int kSfWarps = 2;   // scale-factor copy warps (after the epilogue warps)
+constexpr int kSfWarp0 = 2 + kEpiWarps;
 constexpr int kTileQ = 4;  // depth of the producer -> consumer tile queue
 constexpr int kSmallRows = 32;  // A box height for tiles with few rows (decode)
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kThreads = 64 + 32 * kEpiWarps + 32 * kSfWarps;
 constexpr int A_STAGE_BYTES = BM * 128;
 constexpr int B_STAGE_BYTES = BN * 128;
 constexpr int SFA_STAGE_BYTES = 4 * 512;   // [k-step][512]
@@ -43,7 +53,7 @@ constexpr int TMEM_COLS = 512;
 constexpr int ACC_COLS = 256;
 constexpr int SF_COLS = 48;                // per stage: 16 for A, 32 for B
 constexpr int SMEM_TILES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES + SFA_STAGE_BYTES + SFB_STAGE_BYTES);
-constexpr int SMEM_BYTES = 1024 + SMEM_TILES + 256;
+constexpr int SMEM_BYTES = 1024 + SMEM_TILES + 512;
 
 struct TileInfo {
     int expert, row0, n_block, m_valid;
@@ -88,7 +98,7 @@ __device__ __forceinline__ void set_abort(volatile int* cta_abort, int* dev_err,
 template <int KIND, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tma_small,
-                const GemmArgs args) {
+                const __grid_constant__ CUtensorMap tmb, const GemmArgs args) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -102,7 +112,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* drain = acc_empty + 1;
     uint64_t* tq_full = drain + 1;          // tile queue: slot published
     uint64_t* tq_empty = tq_full + kTileQ;  // tile queue: slot read by every consumer
-    int* tileq = reinterpret_cast<int*>(tq_empty + kTileQ);
+    uint64_t* sf_ready = tq_empty + kTileQ;  // stage's scale atoms are in TMEM
+    uint64_t* sf_drain = sf_ready + STAGES;  // [kSfWarps] teardown after an abort
+    int* tileq = reinterpret_cast<int*>(sf_drain + kSfWarps);
     volatile int* epi_mail = tileq + kTileQ;  // [2 slots][tile, ok]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(epi_mail) + 4);
     volatile int* cta_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -116,8 +128,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int s = 0; s < kTileQ; ++s) {
             mbar_init(&tq_full[s], 1);
-            mbar_init(&tq_empty[s], 2);  // the MMA thread and the epilogue leader
+            // the MMA thread, the epilogue leader and (NVFP4) the scale warps
+            mbar_init(&tq_empty[s], 2 + (KIND == KIND_NVFP4 ? kSfWarps : 0));
         }
+        for (int s = 0; s < STAGES; ++s) mbar_init(&sf_ready[s], kSfWarps);
+        for (int w = 0; w < kSfWarps; ++w) mbar_init(&sf_drain[w], 1);
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, kEpiWarps);
         mbar_init(drain, 1);
@@ -125,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_barrier_init();
         prefetch_tensormap(&tma);
         prefetch_tensormap(&tma_small);
+        prefetch_tensormap(&tmb);
     }
     if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
     tc_fence_before();
@@ -143,11 +159,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------ producer ----------------------------
         // The whole warp runs the loop: lane 0 claims tiles, waits for free
         // stages and sets the expected bytes; the copies of a stage then go
-        // out from separate lanes, because the copies one thread issues are
-        // carried out one after another while those of different threads
-        // overlap.  Lane 0: A (tensor map); lanes 1-4: the four 8 KB quarters
-        // of the stage's B block (stored swizzled: plain bulk copies); lanes
-        // 5-7: the scale-factor atoms of A and of the two B row blocks.
+        // out from separate lanes (a thread keeps only a couple of copies in
+        // flight).  Lane 0: A; lane 1: the stage's 32 KB B box; lane 2: A's
+        // scale atoms; lane 3: the 4 KB group of B's scale atoms.
         int stage = 0;
         uint32_t phase = 0;
         uint32_t issued_parity[STAGES];
@@ -190,7 +204,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             t.row0 = __shfl_sync(0xffffffffu, t.row0, 0);
             t.n_block = __shfl_sync(0xffffffffu, t.n_block, 0);
             t.m_valid = __shfl_sync(0xffffffffu, t.m_valid, 0);
-            const int brow0 = t.expert * args.b_rows_per_expert + t.n_block * BN;
             // tiles with at most 32 rows of the expert load only those rows of A
             const bool small_a = t.m_valid <= kSmallRows;
             for (int kt = 0; kt < k_tiles; ++kt) {
@@ -202,29 +215,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                     } else {
                         uint32_t bytes = (small_a ? kSmallRows * 128 : A_STAGE_BYTES) + B_STAGE_BYTES;
-                        if (KIND == KIND_NVFP4) bytes += static_cast<uint32_t>(steps) * 512u * 3u;
+                        if (KIND == KIND_NVFP4) bytes += static_cast<uint32_t>(steps) * 512u + SFB_STAGE_BYTES;
                         mbar_arrive_expect_tx(&full[stage], bytes);
                     }
                 }
                 ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
                 if (!ok) break;
+                // stage kt of tile (expert, n_block) is box `blk` of B and 4 KB group `blk` of its scales
+                const int blk = (t.expert * args.b_nb + t.n_block) * args.b_kt + kt;
                 if (lane == 0) {
                     const int xc = KIND == KIND_NVFP4 ? kt * 128 : k0;
                     tma_load_2d(sA + stage * A_STAGE_BYTES, small_a ? &tma_small : &tma, &full[stage], xc, t.row0);
-                } else if (lane <= 4) {
-                    // B in box order: stage kt of tile (expert, n_block) is one 32 KB block
-                    const int64_t blk = (static_cast<int64_t>(t.expert) * args.b_nb + t.n_block) * args.b_kt + kt;
-                    constexpr uint32_t kQ = B_STAGE_BYTES / 4;
-                    bulk_load(sB + stage * B_STAGE_BYTES + (lane - 1) * kQ,
-                              args.b + blk * B_STAGE_BYTES + (lane - 1) * kQ, kQ, &full[stage]);
-                } else if (KIND == KIND_NVFP4 && lane == 5) {
+                } else if (lane == 1) {
+                    tma_load_2d(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0, blk * BN);
+                } else if (KIND == KIND_NVFP4 && lane == 2) {
                     const int64_t a_atom = static_cast<int64_t>(t.row0 / 128) * sf_atoms_per_rowblock + kt * 4;
                     bulk_load(sSFA + stage * SFA_STAGE_BYTES, args.sfa + a_atom * 512, steps * 512u, &full[stage]);
-                } else if (KIND == KIND_NVFP4 && lane <= 7) {
-                    const int b = lane - 6;
-                    const int64_t b_atom = static_cast<int64_t>(brow0 / 128 + b) * sf_atoms_per_rowblock + kt * 4;
-                    bulk_load(sSFB + stage * SFB_STAGE_BYTES + b * 2048, args.sfb + b_atom * 512, steps * 512u,
-                              &full[stage]);
+                } else if (KIND == KIND_NVFP4 && lane == 3) {
+                    bulk_load(sSFB + stage * SFB_STAGE_BYTES, args.sfb + static_cast<int64_t>(blk) * SFB_STAGE_BYTES,
+                              SFB_STAGE_BYTES, &full[stage]);
                 }
                 issued[stage] = true;
                 issued_parity[stage] = phase;
@@ -277,6 +286,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
+                    if (KIND == KIND_NVFP4 && !mbar_wait(&sf_ready[stage], phase, cta_abort, dev_err)) {
+                        set_abort(cta_abort, args.err, NF_DEVERR_WAIT_FULL);
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const int k0 = kt * kElemsPerStage;
                     const int steps = min(4, (K - k0) / kMmaK);
@@ -284,15 +298,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
                     const uint32_t sfa_col = ACC_COLS + stage * SF_COLS;
                     const uint32_t sfb_col = sfa_col + 16;
-                    if (KIND == KIND_NVFP4) {
-                        for (int s = 0; s < steps; ++s) {
-                            tmem_cp_sf(tmem + sfa_col + 4 * s, sdesc_sf_atom(smem_u32(sSFA + stage * SFA_STAGE_BYTES + s * 512)));
-                            tmem_cp_sf(tmem + sfb_col + 8 * s,
-                                       sdesc_sf_atom(smem_u32(sSFB + stage * SFB_STAGE_BYTES + s * 512)));
-                            tmem_cp_sf(tmem + sfb_col + 8 * s + 4,
-                                       sdesc_sf_atom(smem_u32(sSFB + stage * SFB_STAGE_BYTES + 2048 + s * 512)));
-                        }
-                    }
                     for (int s = 0; s < steps; ++s) {
                         const uint64_t adesc = sdesc_sw128(a_base + 32 * s);
                         const uint64_t bdesc = sdesc_sw128(b_base + 32 * s);
@@ -321,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else {
+    } else if (warp < kSfWarp0) {
         // ------------------------------ epilogue ----------------------------
         // kEpiWarps warps: a warp may only touch the TMEM lane quadrant
         // warp % 4, and the 4 warps of one quadrant split the tile's columns
@@ -449,6 +454,59 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }  // EPI_STORE_F32 stored while reading the accumulator
         }
+    } else if (KIND == KIND_NVFP4 && lane == 0) {
+        // --------------------------- scale-factor copies -----------------------
+        // Follows the tile queue and the stage ring like the MMA thread: once a
+        // stage has landed, copy this warp's share of its 12 scale atoms (A's
+        // 4, then B's two row halves' 4 each) into the stage's TMEM columns and
+        // commit to sf_ready.  A stage's columns are rewritten only after the
+        // stage was refilled, i.e. after the MMAs that read them completed.
+        const int sw = warp - kSfWarp0;
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        int qslot = 0;
+        uint32_t qphase = 0;
+        while (ok) {
+            if (!mbar_wait(&tq_full[qslot], qphase, cta_abort, dev_err)) {
+                set_abort(cta_abort, args.err, NF_DEVERR_WAIT_ACC);
+                ok = false;
+                break;
+            }
+            const int i = tileq[qslot];
+            mbar_arrive(&tq_empty[qslot]);
+            if (++qslot == kTileQ) qslot = 0, qphase ^= 1u;
+            if (i < 0) break;
+            for (int kt = 0; kt < k_tiles; ++kt) {
+                if (!mbar_wait(&full[stage], phase, cta_abort, dev_err)) {
+                    set_abort(cta_abort, args.err, NF_DEVERR_WAIT_FULL);
+                    ok = false;
+                    break;
+                }
+                const int steps = min(4, (K - kt * kElemsPerStage) / kMmaK);
+                const uint32_t sfa_col = ACC_COLS + stage * SF_COLS;
+                for (int c = sw; c < 12; c += kSfWarps) {
+                    const int s = c & 3, w = c >> 2;  // w 0: A, 1-2: B row halves
+                    if (s >= steps) continue;
+                    const uint8_t* src = w == 0 ? sSFA + stage * SFA_STAGE_BYTES + s * 512
+                                                : sSFB + stage * SFB_STAGE_BYTES + (w - 1) * 2048 + s * 512;
+                    const uint32_t col = w == 0 ? sfa_col + 4 * s : sfa_col + 16 + 8 * s + 4 * (w - 1);
+                    tmem_cp_sf(tmem + col, sdesc_sf_atom(smem_u32(src)));
+                }
+                tc_commit(&sf_ready[stage]);
+                if (++stage == STAGES) stage = 0, phase ^= 1u;
+            }
+        }
+        if (!ok) {
+            tc_commit(&sf_drain[sw]);
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&sf_drain[sw], 0)) {
+                if (globaltimer_ns() - t0 > NF_WAIT_BUDGET_NS) {
+                    atomicCAS(args.err, 0, NF_DEVERR_DRAIN);
+                    break;
+                }
+            }
+        }
     }
 
     tc_fence_before();
@@ -495,6 +553,19 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner_
     return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_blocked(CUtensorMap* map, const void* base, uint64_t bytes) {
+    PfnEncodeTiled fn = encode_fn();
+    if (!fn || bytes % (BN * 128) != 0) return false;
+    cuuint64_t dims[2] = {128, bytes / 128};
+    cuuint64_t strides[1] = {128};
+    cuuint32_t box[2] = {128, BN};
+    cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 int gemm_grid_size(int device) {
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
@@ -502,8 +573,8 @@ int gemm_grid_size(int device) {
 }
 
 template <int KIND, int EPI>
-static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_small, const GemmArgs& args, int grid,
-                              cudaStream_t st) {
+static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
+                              const GemmArgs& args, int grid, cudaStream_t st) {
     // the shared memory limit is an attribute of the kernel in each device's context
     static bool attr[kMaxDevices] = {};
     int dev = 0;
@@ -514,18 +585,18 @@ static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_sma
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
-    gemm_kernel<KIND, EPI><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, args);
+    gemm_kernel<KIND, EPI><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, tmb, args);
     return cudaGetLastError();
 }
 
-cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const GemmArgs& args, int grid,
-                        cudaStream_t st) {
+cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
+                        const GemmArgs& args, int grid, cudaStream_t st) {
     if (args.kind == KIND_NVFP4) {
-        if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT>(tma, tma_small, args, grid, st);
-        if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16>(tma, tma_small, args, grid, st);
+        if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT>(tma, tma_small, tmb, args, grid, st);
+        if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16>(tma, tma_small, tmb, args, grid, st);
     } else {
-        if (args.epi == EPI_SWIGLU_BF16) return launch_one<KIND_BF16, EPI_SWIGLU_BF16>(tma, tma_small, args, grid, st);
-        if (args.epi == EPI_STORE_F32) return launch_one<KIND_BF16, EPI_STORE_F32>(tma, tma_small, args, grid, st);
+        if (args.epi == EPI_SWIGLU_BF16) return launch_one<KIND_BF16, EPI_SWIGLU_BF16>(tma, tma_small, tmb, args, grid, st);
+        if (args.epi == EPI_STORE_F32) return launch_one<KIND_BF16, EPI_STORE_F32>(tma, tma_small, tmb, args, grid, st);
     }
     return cudaErrorInvalidValue;
 }

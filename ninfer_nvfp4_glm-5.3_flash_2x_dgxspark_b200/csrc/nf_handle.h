@@ -39,9 +39,9 @@ struct nf_moe {
     uint16_t* router_wz16 = nullptr;  // and its BF16 chunk-major copy
     float* router_bias = nullptr;   // [E]
     uint8_t* w_gu = nullptr;        // NVFP4 [E * 2I, H/2], 128-row gate/up interleave
-    uint8_t* w_gu_sf = nullptr;     // atoms
+    uint8_t* w_gu_sf = nullptr;     // scale atoms in tile order (GemmArgs::sfb)
     uint8_t* w_dn = nullptr;        // NVFP4 [E * H, I/2]
-    uint8_t* w_dn_sf = nullptr;
+    uint8_t* w_dn_sf = nullptr;     // scale atoms in tile order
     uint16_t* wb_gu = nullptr;      // BF16 experts [E * 2I, H]
     uint16_t* wb_dn = nullptr;      // BF16 experts [E * H, I]
     uint16_t* ws_gu = nullptr;      // shared [2 Is, H]
@@ -97,6 +97,7 @@ struct nf_moe {
     // tensor maps built at finalize
     CUtensorMap tm_a{}, tm_h{}, tm_shh{};
     CUtensorMap tm_a_s{}, tm_h_s{}, tm_shh_s{};  // 32-row boxes of the A operands
+    CUtensorMap tm_b_gu{}, tm_b_dn{}, tm_bs_gu{}, tm_bs_dn{};  // B operands (routed, shared) in box order
     int last_tokens = 0;
 
     // graph mode (nf_moe_set_graph_mode): captured forwards by argument set

@@ -49,16 +49,16 @@ struct GemmArgs {
     int kind;            // GemmKind
     int epi;             // GemmEpi
     int K;               // reduction length in elements
-    int b_rows_per_expert;  // B rows per expert (0 for a dense GEMM; indexes the scale atoms)
     int b_nb;               // B is stored in box order: 256-row blocks per expert ...
     int b_kt;               // ... each split into b_kt blocks of 128 bytes of K
-    const uint8_t* b;       // B in box order (32 KB blocks, rows stored swizzled)
+    const uint8_t* b;       // B in box order (32 KB blocks of 256 rows x 128 bytes); read through `tmb`
     // tile source: grouped (tiles + device tile count) or dense
     const NfTile* tiles;
     const int32_t* num_tiles_dev;
     int dense_rows;      // > 0: dense GEMM over this many A rows
     int n_blocks;        // 256-wide output blocks
-    // NVFP4 scale-factor atoms
+    // NVFP4 scale-factor atoms: sfa [128-row block][K/64 atoms]; sfb in tile
+    // order, one 4 KB group per (expert, n block, K stage): [2 row halves][4 atoms]
     const uint8_t* sfa;
     const uint8_t* sfb;
     // epilogue
@@ -78,9 +78,13 @@ struct GemmArgs {
 // Host helpers (nf_gemm.cu).
 bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner_elems, uint64_t rows,
                   uint32_t box_inner, uint32_t box_rows);
-// tma_small: the same A tensor with a 32-row box, used for tiles with <= 32 rows.
-cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const GemmArgs& args, int grid,
-                        cudaStream_t st);
+// B in box order as a 2-D byte tensor [bytes / 128 rows, 128] with 256-row
+// boxes and 128-byte swizzle: box i is the 32 KB block i.
+bool make_tmap_blocked(CUtensorMap* map, const void* base, uint64_t bytes);
+// tma_small: the same A tensor with a 32-row box, used for tiles with <= 32
+// rows; tmb: B (make_tmap_blocked over args.b).
+cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
+                        const GemmArgs& args, int grid, cudaStream_t st);
 int gemm_grid_size(int device);
 
 // Launchers (nf_kernels.cu).

@@ -63,26 +63,44 @@ bool scales_to_atoms(const uint8_t* scales, int64_t rows, int64_t kgroups, float
     return true;
 }
 
+// Scale atoms in tile order (GemmArgs::sfb): one 4 KB group per 256-row
+// tile and 256-element K stage, [row half][4 atoms][512 B], zero padded
+// past the last atom.  Places one projection's atoms ([128-row block][katoms]
+// from scales_to_atoms) into an expert's groups `out`: a down projection
+// fills both halves (row block rb -> tile rb / 2, half rb % 2), the gate or
+// up projection (half = 0 / 1) the given half of tile rb.
+int64_t sf_tile_bytes(int64_t tiles, int64_t katoms) { return tiles * ((katoms + 3) / 4) * 4096; }
+
+void atoms_to_tiles(const std::vector<uint8_t>& atoms, int64_t rowblocks, int64_t katoms, int half,
+                    std::vector<uint8_t>& out) {
+    const int64_t kts = (katoms + 3) / 4;
+    const int64_t tiles = half < 0 ? rowblocks / 2 : rowblocks;
+    out.assign(static_cast<size_t>(sf_tile_bytes(tiles, katoms)), 0);
+    for (int64_t rb = 0; rb < rowblocks; ++rb) {
+        const int64_t tile = half < 0 ? rb / 2 : rb, b = half < 0 ? rb % 2 : half;
+        for (int64_t a = 0; a < katoms; ++a)
+            std::memcpy(&out[static_cast<size_t>((((tile * kts + a / 4) * 2 + b) * 4 + a % 4) * 512)],
+                        &atoms[static_cast<size_t>((rb * katoms + a) * 512)], 512);
+    }
+}
+
 const char* proj_name(int proj) { return proj == NF_PROJ_GATE ? "gate_proj" : proj == NF_PROJ_UP ? "up_proj" : "down_proj"; }
 
 // Weight matrices that the GEMMs stream (their B operands) are stored in
 // "box order": the matrix is cut into blocks of 256 rows x 128 bytes (one
 // pipeline stage of one tile; 256 FP4 or 64 BF16 K-elements), each block is
 // 32 KB contiguous with 128-byte rows (zero padded past the row end), blocks
-// ordered row-block major, K-block minor.  Inside a block every row is
-// stored in the 128-byte swizzled form the MMA operand descriptors read
-// (16-byte chunk j of row r at chunk j ^ (r % 8)), so a stage is one
-// contiguous 32 KB region that plain bulk copies move into shared memory
-// ready to use, split across several issuing threads.
+// ordered row-block major, K-block minor.  A stage is then one contiguous
+// 32 KB region, which one TMA box (make_tmap_blocked) moves into shared
+// memory in the 128-byte swizzled form the MMA operand descriptors read.
 constexpr int64_t kBlockRows = 256, kBlockRowBytes = 128, kBlockBytes = kBlockRows * kBlockRowBytes;
 
 int64_t k_blocks(int64_t row_bytes) { return (row_bytes + kBlockRowBytes - 1) / kBlockRowBytes; }
 int64_t blocked_bytes(int64_t rows, int64_t row_bytes) { return (rows / kBlockRows) * k_blocks(row_bytes) * kBlockBytes; }
 
-// One row piece (n bytes, a multiple of 16) into row `row` of a block, swizzled.
-void put_row_swizzled(uint8_t* block, int64_t row, const uint8_t* src, int64_t n) {
-    for (int64_t j = 0; j < n / 16; ++j)
-        std::memcpy(block + row * kBlockRowBytes + ((j ^ (row & 7)) * 16), src + j * 16, 16);
+// One row piece (n bytes) into row `row` of a block.
+void put_row(uint8_t* block, int64_t row, const uint8_t* src, int64_t n) {
+    std::memcpy(block + row * kBlockRowBytes, src, static_cast<size_t>(n));
 }
 
 // Copies a row-major [rows, row_bytes] matrix (rows % 256 == 0) into box order.
@@ -92,8 +110,8 @@ cudaError_t upload_blocked(uint8_t* dst, const uint8_t* src, int64_t rows, int64
     for (int64_t r = 0; r < rows; ++r)
         for (int64_t k = 0; k < kt; ++k) {
             const int64_t n = std::min(kBlockRowBytes, row_bytes - k * kBlockRowBytes);
-            put_row_swizzled(&stage[static_cast<size_t>(((r / kBlockRows) * kt + k) * kBlockBytes)], r % kBlockRows,
-                             src + r * row_bytes + k * kBlockRowBytes, n);
+            put_row(&stage[static_cast<size_t>(((r / kBlockRows) * kt + k) * kBlockBytes)], r % kBlockRows,
+                    src + r * row_bytes + k * kBlockRowBytes, n);
         }
     return cudaMemcpy(dst, stage.data(), stage.size(), cudaMemcpyHostToDevice);
 }
@@ -108,9 +126,8 @@ cudaError_t upload_blocked_half(uint8_t* dst, const uint8_t* src, int64_t rows, 
     for (int64_t r = 0; r < rows; ++r)
         for (int64_t k = 0; k < kt; ++k) {
             const int64_t n = std::min(kBlockRowBytes, row_bytes - k * kBlockRowBytes);
-            // the half starts at row 128 * half of the block: (r % 128 + 128 * half) % 8 == r % 8
-            put_row_swizzled(&stage[static_cast<size_t>(((r / 128) * kt + k) * hb)], r % 128,
-                             src + r * row_bytes + k * kBlockRowBytes, n);
+            put_row(&stage[static_cast<size_t>(((r / 128) * kt + k) * hb)], r % 128,
+                    src + r * row_bytes + k * kBlockRowBytes, n);
         }
     return cudaMemcpy2D(dst + half * hb, static_cast<size_t>(kBlockBytes), stage.data(), static_cast<size_t>(hb),
                         static_cast<size_t>(hb), static_cast<size_t>(nb * kt), cudaMemcpyHostToDevice);
@@ -253,8 +270,9 @@ int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::s
     }
     if (routed) {
         if (fp4) {
-            ok = ok && h->alloc(&h->w_gu, E * blocked_bytes(2 * I, H / 2)) && h->alloc(&h->w_gu_sf, E * 2 * I * H / 16) &&
-                 h->alloc(&h->w_dn, E * blocked_bytes(H, I / 2)) && h->alloc(&h->w_dn_sf, E * H * I / 16);
+            ok = ok && h->alloc(&h->w_gu, E * blocked_bytes(2 * I, H / 2)) &&
+                 h->alloc(&h->w_gu_sf, E * sf_tile_bytes(I / 128, H / 64)) &&
+                 h->alloc(&h->w_dn, E * blocked_bytes(H, I / 2)) && h->alloc(&h->w_dn_sf, E * sf_tile_bytes(H / 256, I / 64));
         } else {
             ok = ok && h->alloc(&h->wb_gu, E * blocked_bytes(2 * I, 2 * H) / 2) &&
                  h->alloc(&h->wb_dn, E * blocked_bytes(H, 2 * I) / 2);
@@ -357,21 +375,22 @@ int nf_moe_bind_nvfp4(nf_moe* h, int expert, int proj, const uint8_t* packed, co
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
     cudaError_t e = cudaSuccess;
-    const int64_t kbytes = cols / 2;
-    const int64_t slab = (cols / 64) * 512;  // one 128-row block of atoms
+    const int64_t kbytes = cols / 2, katoms = cols / 64;
+    std::vector<uint8_t> groups;
     if (proj == NF_PROJ_DOWN) {
         e = upload_blocked(h->w_dn + expert * blocked_bytes(H, kbytes), packed, H, kbytes);
+        atoms_to_tiles(atoms, H / 128, katoms, -1, groups);
         if (e == cudaSuccess)
-            e = cudaMemcpy(h->w_dn_sf + expert * H * (cols / 16), atoms.data(), atoms.size(), cudaMemcpyHostToDevice);
+            e = cudaMemcpy(h->w_dn_sf + expert * static_cast<int64_t>(groups.size()), groups.data(), groups.size(),
+                           cudaMemcpyHostToDevice);
     } else {
         // gate rows j -> interleaved row (j / 128) * 256 + j % 128, up rows +128
-        e = upload_blocked_half(h->w_gu + expert * blocked_bytes(2 * I, kbytes), packed, I, kbytes,
-                                proj == NF_PROJ_UP ? 1 : 0);
-        if (e == cudaSuccess) {
-            uint8_t* sbase = h->w_gu_sf + (expert * 2 * I / 128 + (proj == NF_PROJ_UP ? 1 : 0)) * slab;
-            e = cudaMemcpy2D(sbase, static_cast<size_t>(2 * slab), atoms.data(), static_cast<size_t>(slab),
-                             static_cast<size_t>(slab), static_cast<size_t>(I / 128), cudaMemcpyHostToDevice);
-        }
+        const int half = proj == NF_PROJ_UP ? 1 : 0;
+        e = upload_blocked_half(h->w_gu + expert * blocked_bytes(2 * I, kbytes), packed, I, kbytes, half);
+        atoms_to_tiles(atoms, I / 128, katoms, half, groups);
+        if (e == cudaSuccess)
+            e = cudaMemcpy2D(h->w_gu_sf + expert * static_cast<int64_t>(groups.size()) + half * 2048, 4096,
+                             groups.data() + half * 2048, 4096, 2048, groups.size() / 4096, cudaMemcpyHostToDevice);
     }
     cudaSetDevice(prev);
     if (e != cudaSuccess) return h->cuda_fail(e, "bind copy");
@@ -540,17 +559,23 @@ int nf_moe_finalize(nf_moe* h) {
     if (h->ep_outer) {
         // no routed workspace: only the shared expert's maps
     } else if (fp4) {
+        ok = ok && make_tmap_blocked(&h->tm_b_gu, h->w_gu, h->bytes_of(h->w_gu)) &&
+             make_tmap_blocked(&h->tm_b_dn, h->w_dn, h->bytes_of(h->w_dn));
         ok = ok && make_tmap_2d(&h->tm_a, h->pb.a_codes, false, H / 2, R, 128, 128);
         ok = ok && make_tmap_2d(&h->tm_a_s, h->pb.a_codes, false, H / 2, R, 128, 32);
         ok = ok && make_tmap_2d(&h->tm_h_s, h->h_codes, false, I / 2, R, 128, 32);
         ok = ok && make_tmap_2d(&h->tm_h, h->h_codes, false, I / 2, R, 128, 128);
     } else {
+        ok = ok && make_tmap_blocked(&h->tm_b_gu, h->wb_gu, h->bytes_of(h->wb_gu)) &&
+             make_tmap_blocked(&h->tm_b_dn, h->wb_dn, h->bytes_of(h->wb_dn));
         ok = ok && make_tmap_2d(&h->tm_a, h->pb.a_bf16, true, H, R, 64, 128);
         ok = ok && make_tmap_2d(&h->tm_a_s, h->pb.a_bf16, true, H, R, 64, 32);
         ok = ok && make_tmap_2d(&h->tm_h_s, h->h_bf16, true, I, R, 64, 32);
         ok = ok && make_tmap_2d(&h->tm_h, h->h_bf16, true, I, R, 64, 128);
     }
     if (Is > 0) {
+        ok = ok && make_tmap_blocked(&h->tm_bs_gu, h->ws_gu, h->bytes_of(h->ws_gu)) &&
+             make_tmap_blocked(&h->tm_bs_dn, h->ws_dn, h->bytes_of(h->ws_dn));
         ok = ok && make_tmap_2d(&h->tm_shh, h->sh_h, true, Is, Tm, 64, 128);
         ok = ok && make_tmap_2d(&h->tm_shh_s, h->sh_h, true, Is, Tm, 64, 32);
     }
@@ -619,7 +644,7 @@ int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cud
     sg.out = h->sh_h;
     sg.out_ld = Is;
     sg.tile_counter = h->shared_counters;
-    e = launch_gemm(tm_x, tm_x_s, sg, h->grid, h->side);
+    e = launch_gemm(tm_x, tm_x_s, h->tm_bs_gu, sg, h->grid, h->side);
     if (e != cudaSuccess) return h->cuda_fail(e, "shared gate/up GEMM launch");
     sg.epi = EPI_STORE_F32;
     sg.K = Is;
@@ -630,7 +655,7 @@ int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cud
     sg.out = h->sh_out;
     sg.out_ld = H;
     sg.tile_counter = h->shared_counters + 1;
-    e = launch_gemm(h->tm_shh, h->tm_shh_s, sg, h->grid, h->side);
+    e = launch_gemm(h->tm_shh, h->tm_shh_s, h->tm_bs_dn, sg, h->grid, h->side);
     if (e != cudaSuccess) return h->cuda_fail(e, "shared down GEMM launch");
     rec.end(NF_STAGE_SHARED, h->side);
     if ((e = cudaEventRecord(h->ev_join, h->side)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
@@ -660,7 +685,6 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.kind = fp4 ? KIND_NVFP4 : KIND_BF16;
     g.epi = fp4 ? EPI_SWIGLU_QUANT : EPI_SWIGLU_BF16;
     g.K = H;
-    g.b_rows_per_expert = 2 * I;
     g.b_nb = 2 * I / 256;
     g.b = fp4 ? h->w_gu : reinterpret_cast<const uint8_t*>(h->wb_gu);
     g.b_kt = static_cast<int>(k_blocks(fp4 ? H / 2 : 2 * H));
@@ -679,14 +703,13 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.out_sf = h->h_sf;
     g.out_kgroups = I / 16;
     g.tile_counter = h->pb.meta + 4;
-    e = launch_gemm(h->tm_a, h->tm_a_s, g, h->grid, s);
+    e = launch_gemm(h->tm_a, h->tm_a_s, h->tm_b_gu, g, h->grid, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "gate/up GEMM launch");
     rec.end(NF_STAGE_GATE_UP, s);
     rec.begin(NF_STAGE_DOWN, s);
     // down
     g.epi = fp4 ? EPI_STORE_BF16 : EPI_STORE_F32;
     g.K = I;
-    g.b_rows_per_expert = H;
     g.b_nb = H / 256;
     g.b = fp4 ? h->w_dn : reinterpret_cast<const uint8_t*>(h->wb_dn);
     g.b_kt = static_cast<int>(k_blocks(fp4 ? I / 2 : 2 * I));
@@ -699,7 +722,7 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.out = h->down;
     g.out_ld = H;
     g.tile_counter = h->pb.meta + 5;
-    e = launch_gemm(h->tm_h, h->tm_h_s, g, h->grid, s);
+    e = launch_gemm(h->tm_h, h->tm_h_s, h->tm_b_dn, g, h->grid, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "down GEMM launch");
     rec.end(NF_STAGE_DOWN, s);
     return NF_OK;
