@@ -312,6 +312,19 @@ NF_DEV void prefetch_tensormap(const CUtensorMap* map) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with
+// launch_dependent() may start while the kernel before it in the stream is
+// still running: pdl_wait() returns once that kernel has completed and its
+// writes are visible, so every read of its results (and every write it might
+// still read) comes after pdl_wait().  pdl_trigger() lets the next kernel
+// launch; each kernel of the layer calls it only after its own pdl_wait(), so
+// whatever ran two or more launches earlier has completed when a kernel
+// starts.  Both are no-ops for a kernel launched the ordinary way.
+// ---------------------------------------------------------------------------
+NF_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+NF_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // tcgen05: TMEM allocation, MMA, copies, loads
 // ---------------------------------------------------------------------------
 NF_DEV void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {  // whole warp

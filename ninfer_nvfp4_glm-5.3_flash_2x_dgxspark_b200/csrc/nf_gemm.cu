@@ -180,6 +180,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             next = atomicAdd(args.tile_counter, 1);
             if (next < num_tiles) next_t = get_tile(args, next);
         }
+        auto stage_bytes = [&](bool small_a, int steps) {
+            uint32_t bytes = (small_a ? kSmallRows * 128 : A_STAGE_BYTES) + B_STAGE_BYTES;
+            if (KIND == KIND_NVFP4) bytes += static_cast<uint32_t>(steps) * 512u + SFB_STAGE_BYTES;
+            return bytes;
+        };
+        // The kernel may start while the one that writes A is still running
+        // (launch_dependent): the tile list and its counter come from the
+        // permutation, which has completed by then, and B and its scales are
+        // weights, so the first tile's first stages of B go out before
+        // pdl_wait(); A and its scales follow it.
+        int pre = 0;
+        {
+            const int first = __shfl_sync(0xffffffffu, next, 0);
+            const int e0 = __shfl_sync(0xffffffffu, next_t.expert, 0);
+            const int nb0 = __shfl_sync(0xffffffffu, next_t.n_block, 0);
+            const bool small0 = __shfl_sync(0xffffffffu, next_t.m_valid, 0) <= kSmallRows;
+            if (first < num_tiles) {
+                pre = min(STAGES, k_tiles);
+                for (int kt = 0; kt < pre; ++kt) {
+                    if (lane == 0)
+                        mbar_arrive_expect_tx(&full[kt], stage_bytes(small0, min(4, (K - kt * kElemsPerStage) / kMmaK)));
+                    __syncwarp();
+                    const int blk = (e0 * args.b_nb + nb0) * args.b_kt + kt;
+                    if (lane == 1) {
+                        tma_load_2d(sB + kt * B_STAGE_BYTES, &tmb, &full[kt], 0, blk * BN);
+                    } else if (KIND == KIND_NVFP4 && lane == 3) {
+                        bulk_load(sSFB + kt * SFB_STAGE_BYTES, args.sfb + static_cast<int64_t>(blk) * SFB_STAGE_BYTES,
+                                  SFB_STAGE_BYTES, &full[kt]);
+                    }
+                    issued[kt] = true;
+                }
+            }
+        }
+        pdl_wait();
+        if (lane == 0) pdl_trigger();
+        bool first_tile = true;
         while (ok) {
             // publish the claimed tile to the MMA and epilogue warps (-1 ends
             // the CTA's work)
@@ -209,14 +245,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kt = 0; kt < k_tiles; ++kt) {
                 const int k0 = kt * kElemsPerStage;
                 const int steps = min(4, (K - k0) / kMmaK);
-                if (lane == 0) {
+                const bool b_issued = first_tile && kt < pre;  // B of this stage went out before pdl_wait()
+                if (lane == 0 && !b_issued) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, cta_abort, dev_err)) {
                         set_abort(cta_abort, args.err, NF_DEVERR_WAIT_EMPTY);
                         ok = false;
                     } else {
-                        uint32_t bytes = (small_a ? kSmallRows * 128 : A_STAGE_BYTES) + B_STAGE_BYTES;
-                        if (KIND == KIND_NVFP4) bytes += static_cast<uint32_t>(steps) * 512u + SFB_STAGE_BYTES;
-                        mbar_arrive_expect_tx(&full[stage], bytes);
+                        mbar_arrive_expect_tx(&full[stage], stage_bytes(small_a, steps));
                     }
                 }
                 ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -226,12 +261,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) {
                     const int xc = KIND == KIND_NVFP4 ? kt * 128 : k0;
                     tma_load_2d(sA + stage * A_STAGE_BYTES, small_a ? &tma_small : &tma, &full[stage], xc, t.row0);
-                } else if (lane == 1) {
+                } else if (lane == 1 && !b_issued) {
                     tma_load_2d(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0, blk * BN);
                 } else if (KIND == KIND_NVFP4 && lane == 2) {
                     const int64_t a_atom = static_cast<int64_t>(t.row0 / 128) * sf_atoms_per_rowblock + kt * 4;
                     bulk_load(sSFA + stage * SFA_STAGE_BYTES, args.sfa + a_atom * 512, steps * 512u, &full[stage]);
-                } else if (KIND == KIND_NVFP4 && lane == 3) {
+                } else if (KIND == KIND_NVFP4 && lane == 3 && !b_issued) {
                     bulk_load(sSFB + stage * SFB_STAGE_BYTES, args.sfb + static_cast<int64_t>(blk) * SFB_STAGE_BYTES,
                               SFB_STAGE_BYTES, &full[stage]);
                 }
@@ -241,6 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0 && kt == max(0, k_tiles - 3)) next = atomicAdd(args.tile_counter, 1);
                 if (lane == 0 && kt == k_tiles - 1 && next < num_tiles) next_t = get_tile(args, next);
             }
+            first_tile = false;
         }
         if (!ok && lane == 0) {
             // drain: every issued copy lands before the CTA may exit
@@ -585,8 +621,7 @@ static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_sma
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
-    gemm_kernel<KIND, EPI><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, tmb, args);
-    return cudaGetLastError();
+    return launch_dependent(gemm_kernel<KIND, EPI>, dim3(grid), dim3(kThreads), SMEM_BYTES, st, tma, tma_small, tmb, args);
 }
 
 cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,

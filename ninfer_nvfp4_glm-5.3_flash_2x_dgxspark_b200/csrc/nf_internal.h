@@ -75,6 +75,24 @@ struct GemmArgs {
     int* tile_counter;         // tiles claimed so far (zero before the launch)
 };
 
+// Launches `kernel` with programmatic stream serialization: it may begin
+// before the previous kernel in `st` has finished and calls pdl_wait()
+// (nf_common.cuh) before it touches that kernel's results.
+template <typename... P, typename... A>
+cudaError_t launch_dependent(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
+}
+
 // Host helpers (nf_gemm.cu).
 bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner_elems, uint64_t rows,
                   uint32_t box_inner, uint32_t box_rows);

@@ -155,6 +155,8 @@ __global__ void __launch_bounds__(kRtThreads) router_logits_kernel(const uint16_
                                                                    float* __restrict__ scores,
                                                                    float* __restrict__ choices,
                                                                    int* __restrict__ err) {
+    pdl_wait();  // no-op unless launched dependent
+    pdl_trigger();  // let the permutation launch
     extern __shared__ __align__(128) uint8_t rt_smem[];
     __shared__ uint64_t bar;
     const int chunk = min(H, kRtMaxChunk);
@@ -538,6 +540,8 @@ __global__ void __launch_bounds__(kFzCThreads + 32 * PW, 1) router_fused_kernel(
     const uint16_t* __restrict__ x, const void* __restrict__ wz, const float* __restrict__ bias, int T, int H, int E,
     int K, float scaling, int normalize, int n_group, int topk_group, int w_safe, float* __restrict__ logits,
     int32_t* __restrict__ idx_out, float* __restrict__ w_out, int* __restrict__ err) {
+    pdl_wait();  // no-op unless launched dependent
+    pdl_trigger();  // let the permutation launch
     static_assert(!kW16 || (EPT == 1 && TPT == 1), "BF16 staging serves the one-chain form");
     static_assert(!kXRes || (EPT == 1 && TPT == 1), "resident token rows serve small batches");
     static_assert(kXRes || SUB == 1, "streamed token rows come one chunk per stage");
@@ -833,6 +837,8 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __re
                                                              NfTile* __restrict__ tiles_gu,
                                                              NfTile* __restrict__ tiles_down,
                                                              int32_t* __restrict__ meta) {
+    pdl_wait();  // launched dependent on the previous kernel
+    pdl_trigger();
     extern __shared__ int32_t sh[];
     int32_t* s_cnt = sh;
     int32_t* s_off = s_cnt + E;
@@ -868,6 +874,8 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __re
 
 __global__ void permute_hist_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
                                     int32_t* __restrict__ chunk_counts) {
+    pdl_wait();  // launched dependent on the previous kernel
+    pdl_trigger();
     extern __shared__ int32_t cnt[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
@@ -887,6 +895,8 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __res
                                                             NfTile* __restrict__ tiles_gu,
                                                             NfTile* __restrict__ tiles_down,
                                                             int32_t* __restrict__ meta) {
+    pdl_wait();  // launched dependent on the previous kernel
+    pdl_trigger();
     extern __shared__ int32_t sh[];
     int32_t* s_cnt = sh;
     int32_t* s_off = s_cnt + E;
@@ -918,6 +928,8 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const int32_t* __rest
                                                            const int32_t* __restrict__ seg_off,
                                                            int32_t* __restrict__ pair_row,
                                                            int32_t* __restrict__ row_token) {
+    pdl_wait();  // launched dependent on the previous kernel
+    pdl_trigger();
     extern __shared__ uint32_t s_mask[];  // [E][kChunkWords]
     const int t0 = blockIdx.x * kChunkTok;
     const int n = min(kChunkTok, T - t0) * K;
@@ -952,6 +964,8 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
                                 const int32_t* __restrict__ pair_row, const float* __restrict__ gscale, int T, int K,
                                 int H, int bf16_mode, uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
                                 uint16_t* __restrict__ a_bf16) {
+    pdl_wait();  // launched dependent on the previous kernel
+    pdl_trigger();
     const int gq = H / 64;
     const int64_t item = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
     if (item >= static_cast<int64_t>(T) * gq) return;
@@ -1044,6 +1058,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const DownT* __restrict__ 
                                                       const float* __restrict__ topk_w, const float* __restrict__ shared,
                                                       const float* __restrict__ residual, int T, int K, int H,
                                                       float* __restrict__ y) {
+    pdl_wait();  // launched dependent on the previous kernel
+    pdl_trigger();
     const int t = blockIdx.x;
     for (int d0 = threadIdx.x * 8; d0 < H; d0 += blockDim.x * 8) {
         float acc[8];
@@ -1200,22 +1216,29 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
     const size_t small_smem = (3 * E + 2 + T * K + static_cast<size_t>(E) * ((T + 31) / 32)) * sizeof(int32_t);
     if (T * K <= kSmallPairs && small_smem <= 48 * 1024) {
         const size_t smem = small_smem;
-        permute_small_kernel<<<1, 1024, smem, st>>>(idx, T, K, E, nb_gu, nb_down, b.counts, b.seg_off, b.pair_row,
-                                                    b.row_token, b.tiles_gu, b.tiles_down, b.meta);
+        cudaError_t e = launch_dependent(permute_small_kernel, dim3(1), dim3(1024), smem, st, idx, T, K, E, nb_gu,
+                                         nb_down, b.counts, b.seg_off, b.pair_row, b.row_token, b.tiles_gu,
+                                         b.tiles_down, b.meta);
+        if (e != cudaSuccess) return e;
     } else {
         const int nchunks = (T + kChunkTok - 1) / kChunkTok;
-        permute_hist_kernel<<<nchunks, 256, E * sizeof(int32_t), st>>>(idx, T, K, E, b.chunk_counts);
-        permute_scan_kernel<<<1, 1024, (3 * E + 2) * sizeof(int32_t), st>>>(b.chunk_counts, nchunks, E, nb_gu, nb_down,
-                                                                           b.chunk_base, b.counts, b.seg_off,
-                                                                           b.row_token, b.tiles_gu, b.tiles_down,
-                                                                           b.meta);
-        permute_rows_kernel<<<nchunks, 256, static_cast<size_t>(E) * kChunkWords * sizeof(uint32_t), st>>>(
-            idx, T, K, E, b.chunk_base, b.seg_off, b.pair_row, b.row_token);
+        cudaError_t e = launch_dependent(permute_hist_kernel, dim3(nchunks), dim3(256), E * sizeof(int32_t), st, idx, T,
+                                         K, E, b.chunk_counts);
+        if (e == cudaSuccess)
+            e = launch_dependent(permute_scan_kernel, dim3(1), dim3(1024), (3 * E + 2) * sizeof(int32_t), st,
+                                 static_cast<const int32_t*>(b.chunk_counts), nchunks, E, nb_gu, nb_down, b.chunk_base,
+                                 b.counts, b.seg_off, b.row_token, b.tiles_gu, b.tiles_down, b.meta);
+        if (e == cudaSuccess)
+            e = launch_dependent(permute_rows_kernel, dim3(nchunks), dim3(256),
+                                 static_cast<size_t>(E) * kChunkWords * sizeof(uint32_t), st, idx, T, K, E,
+                                 static_cast<const int32_t*>(b.chunk_base), static_cast<const int32_t*>(b.seg_off),
+                                 b.pair_row, b.row_token);
+        if (e != cudaSuccess) return e;
     }
     const int64_t items = static_cast<int64_t>(T) * (H / 64);
-    dispatch_kernel<<<static_cast<unsigned>((items + 127) / 128), 128, 0, st>>>(
-        x, idx, b.pair_row, gscale, T, K, H, bf16_mode, b.a_codes, b.a_sf, b.a_bf16);
-    return cudaGetLastError();
+    return launch_dependent(dispatch_kernel, dim3(static_cast<unsigned>((items + 127) / 128)), dim3(128), 0, st, x, idx,
+                            static_cast<const int32_t*>(b.pair_row), gscale, T, K, H, bf16_mode, b.a_codes, b.a_sf,
+                            b.a_bf16);
 }
 
 cudaError_t launch_format_selfcheck(unsigned long long* mismatches_dev, cudaStream_t st) {
@@ -1228,12 +1251,10 @@ cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair
                            cudaStream_t st) {
     const int threads = min(256, H / 8);
     if (down_bf16)
-        combine_kernel<uint16_t><<<T, threads, 0, st>>>(static_cast<const uint16_t*>(down), pair_row, topk_w, shared,
-                                                        residual, T, K, H, y);
-    else
-        combine_kernel<float><<<T, threads, 0, st>>>(static_cast<const float*>(down), pair_row, topk_w, shared,
-                                                     residual, T, K, H, y);
-    return cudaGetLastError();
+        return launch_dependent(combine_kernel<uint16_t>, dim3(T), dim3(threads), 0, st,
+                                static_cast<const uint16_t*>(down), pair_row, topk_w, shared, residual, T, K, H, y);
+    return launch_dependent(combine_kernel<float>, dim3(T), dim3(threads), 0, st, static_cast<const float*>(down),
+                            pair_row, topk_w, shared, residual, T, K, H, y);
 }
 
 // ---------------------------------------------------------------------------
