@@ -190,6 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // permutation, which has completed by then, and B and its scales are
         // weights, so the first tile's first stages of B go out before
         // pdl_wait(); A and its scales follow it.
+        const uint64_t stream_policy = l2_evict_first();  // B and its scales: read once per step
         int pre = 0;
         {
             const int first = __shfl_sync(0xffffffffu, next, 0);
@@ -204,10 +205,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     const int blk = (e0 * args.b_nb + nb0) * args.b_kt + kt;
                     if (lane == 1) {
-                        tma_load_2d(sB + kt * B_STAGE_BYTES, &tmb, &full[kt], 0, blk * BN);
+                        tma_load_2d_hint(sB + kt * B_STAGE_BYTES, &tmb, &full[kt], 0, blk * BN, stream_policy);
                     } else if (KIND == KIND_NVFP4 && lane == 3) {
-                        bulk_load(sSFB + kt * SFB_STAGE_BYTES, args.sfb + static_cast<int64_t>(blk) * SFB_STAGE_BYTES,
-                                  SFB_STAGE_BYTES, &full[kt]);
+                        bulk_load_hint(sSFB + kt * SFB_STAGE_BYTES,
+                                       args.sfb + static_cast<int64_t>(blk) * SFB_STAGE_BYTES, SFB_STAGE_BYTES,
+                                       &full[kt], stream_policy);
                     }
                     issued[kt] = true;
                 }
@@ -262,13 +264,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int xc = KIND == KIND_NVFP4 ? kt * 128 : k0;
                     tma_load_2d(sA + stage * A_STAGE_BYTES, small_a ? &tma_small : &tma, &full[stage], xc, t.row0);
                 } else if (lane == 1 && !b_issued) {
-                    tma_load_2d(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0, blk * BN);
+                    tma_load_2d_hint(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0, blk * BN, stream_policy);
                 } else if (KIND == KIND_NVFP4 && lane == 2) {
                     const int64_t a_atom = static_cast<int64_t>(t.row0 / 128) * sf_atoms_per_rowblock + kt * 4;
                     bulk_load(sSFA + stage * SFA_STAGE_BYTES, args.sfa + a_atom * 512, steps * 512u, &full[stage]);
                 } else if (KIND == KIND_NVFP4 && lane == 3 && !b_issued) {
-                    bulk_load(sSFB + stage * SFB_STAGE_BYTES, args.sfb + static_cast<int64_t>(blk) * SFB_STAGE_BYTES,
-                              SFB_STAGE_BYTES, &full[stage]);
+                    bulk_load_hint(sSFB + stage * SFB_STAGE_BYTES, args.sfb + static_cast<int64_t>(blk) * SFB_STAGE_BYTES,
+                                   SFB_STAGE_BYTES, &full[stage], stream_policy);
                 }
                 issued[stage] = true;
                 issued_parity[stage] = phase;
