@@ -325,6 +325,122 @@ __device__ __forceinline__ void warp_select(const float* score, const float* cho
     }
 }
 
+// warp_select with the token's scores and choices held in registers (lane l
+// owns experts l + 32 j, j < JN, so E <= 32 JN): each pick is two ballots
+// (the first eligible expert) and one 64-bit max-reduction over keys
+// (order-preserving bits of the choice, then the complement of the expert
+// index: the largest non-NaN choice, lowest index among equals), instead of
+// re-reading shared memory and reducing three values per level.  Lane p
+// keeps pick p (K <= 32), so the weights are normalised by K lanes at once
+// after a sum taken in pick order.  Same results as warp_select.
+__device__ __forceinline__ uint32_t float_order_bits(float c) {
+    const uint32_t u = __float_as_uint(__fadd_rn(c, 0.f));  // -0 -> +0: equal choices get equal keys
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <int JN>
+__device__ __forceinline__ void warp_select_reg(const float* score, const float* choice, int E, int K, float scaling,
+                                                int normalize, int n_group, int topk_group, uint32_t* excl,
+                                                int32_t* __restrict__ idx_row, float* __restrict__ w_row) {
+    const int lane = threadIdx.x & 31;
+    excl[lane] = 0u;
+    __syncwarp();
+    if (n_group > 1 && topk_group < n_group) {
+        if (lane == 0) {
+            const int per = E / n_group;
+            uint32_t keep = 0u;
+            for (int r = 0; r < topk_group; ++r) {
+                int best = -1;
+                float best_score = 0.f;
+                for (int g = 0; g < n_group; ++g) {
+                    if (keep & (1u << g)) continue;
+                    float b1 = -INFINITY, b2 = -INFINITY;
+                    for (int j = 0; j < per; ++j) {
+                        const float c = choice[g * per + j];
+                        if (c > b1) {
+                            b2 = b1;
+                            b1 = c;
+                        } else if (c > b2) {
+                            b2 = c;
+                        }
+                    }
+                    const float s = per >= 2 ? __fadd_rn(b1, b2) : b1;
+                    if (best < 0 || s > best_score) {
+                        best = g;
+                        best_score = s;
+                    }
+                }
+                keep |= 1u << best;
+            }
+            for (int e = 0; e < E; ++e)
+                if (!(keep & (1u << (e / per)))) excl[e >> 5] |= 1u << (e & 31);
+        }
+        __syncwarp();
+    }
+    float ch[JN], sc[JN];
+    uint32_t avail = 0u;  // bit j: expert lane + 32 j exists, is not excluded and not yet taken
+#pragma unroll
+    for (int j = 0; j < JN; ++j) {
+        const int e = lane + 32 * j;
+        ch[j] = 0.f;
+        sc[j] = 0.f;
+        if (e < E) {
+            ch[j] = choice[e];
+            sc[j] = score[e];
+            if (!((excl[e >> 5] >> (e & 31)) & 1u)) avail |= 1u << j;
+        }
+    }
+    int my_pick = 0;
+    float my_w = 0.f;
+    for (int p = 0; p < K; ++p) {
+        int first = -1;
+#pragma unroll
+        for (int j = JN - 1; j >= 0; --j) {
+            const uint32_t b = __ballot_sync(0xffffffffu, (avail >> j) & 1u);
+            if (b) first = 32 * j + __ffs(b) - 1;
+        }
+        uint64_t key = 0;
+#pragma unroll
+        for (int j = 0; j < JN; ++j) {
+            if (((avail >> j) & 1u) && !isnan(ch[j])) {
+                const uint64_t k = (static_cast<uint64_t>(float_order_bits(ch[j])) << 32) |
+                                   (0xffffffffu - static_cast<uint32_t>(lane + 32 * j));
+                key = k > key ? k : key;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const uint64_t o = __shfl_xor_sync(0xffffffffu, key, off);
+            key = o > key ? o : key;
+        }
+        int pick = 0;
+        if (first >= 0) {
+            float cf = ch[0];
+#pragma unroll
+            for (int j = 1; j < JN; ++j)
+                if ((first >> 5) == j) cf = ch[j];
+            cf = __shfl_sync(0xffffffffu, cf, first & 31);
+            pick = (isnan(cf) || key == 0) ? first : static_cast<int>(0xffffffffu - static_cast<uint32_t>(key));
+        }
+        if ((pick & 31) == lane) avail &= ~(1u << (pick >> 5));
+        float w = sc[0];
+#pragma unroll
+        for (int j = 1; j < JN; ++j)
+            if ((pick >> 5) == j) w = sc[j];
+        w = __shfl_sync(0xffffffffu, w, pick & 31);
+        if (lane == p) my_pick = pick, my_w = w;
+    }
+    if (normalize) {
+        float sum = 1e-20f;
+        for (int p = 0; p < K; ++p) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, my_w, p));
+        my_w = __fmul_rn(__fdiv_rn(my_w, sum), scaling);
+    }
+    if (lane < K) {
+        idx_row[lane] = my_pick;
+        w_row[lane] = my_w;
+    }
+}
+
 __global__ void __launch_bounds__(kSelectWarps * 32) router_select_kernel(
     const float* __restrict__ scores, const float* __restrict__ choices, int T, int E, int K, float scaling,
     int normalize, int n_group, int topk_group, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
@@ -730,8 +846,9 @@ __global__ void __launch_bounds__(kFzCThreads + 32 * PW, 1) router_fused_kernel(
         // a few tokens: a warp per token, lanes split the experts
         __shared__ uint32_t s_excl[kThreads / 32][32];
         for (int t = warp; t < nt; t += kThreads / 32)
-            warp_select(s_sc + t * rs, s_ch + t * rs, E, K, scaling, normalize, n_group, topk_group, s_excl[warp],
-                        idx_out + static_cast<int64_t>(t0 + t) * K, w_out + static_cast<int64_t>(t0 + t) * K);
+            warp_select_reg<(kFzMaxE + 31) / 32>(s_sc + t * rs, s_ch + t * rs, E, K, scaling, normalize, n_group,
+                                                 topk_group, s_excl[warp], idx_out + static_cast<int64_t>(t0 + t) * K,
+                                                 w_out + static_cast<int64_t>(t0 + t) * K);
     } else {
         // many tokens: a thread per token
         for (int t = threadIdx.x; t < nt; t += kThreads)
