@@ -612,7 +612,7 @@ int gemm_grid_size(int device) {
 
 template <int KIND, int EPI>
 static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
-                              const GemmArgs& args, int grid, cudaStream_t st) {
+                              const GemmArgs& args, int grid, bool dependent, cudaStream_t st) {
     // the shared memory limit is an attribute of the kernel in each device's context
     static bool attr[kMaxDevices] = {};
     int dev = 0;
@@ -623,17 +623,21 @@ static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_sma
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
-    return launch_dependent(gemm_kernel<KIND, EPI>, dim3(grid), dim3(kThreads), SMEM_BYTES, st, tma, tma_small, tmb, args);
+    if (dependent)
+        return launch_dependent(gemm_kernel<KIND, EPI>, dim3(grid), dim3(kThreads), SMEM_BYTES, st, tma, tma_small, tmb,
+                                args);
+    gemm_kernel<KIND, EPI><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, tmb, args);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
-                        const GemmArgs& args, int grid, cudaStream_t st) {
+                        const GemmArgs& args, int grid, bool dependent, cudaStream_t st) {
     if (args.kind == KIND_NVFP4) {
-        if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT>(tma, tma_small, tmb, args, grid, st);
-        if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16>(tma, tma_small, tmb, args, grid, st);
+        if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT>(tma, tma_small, tmb, args, grid, dependent, st);
+        if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16>(tma, tma_small, tmb, args, grid, dependent, st);
     } else {
-        if (args.epi == EPI_SWIGLU_BF16) return launch_one<KIND_BF16, EPI_SWIGLU_BF16>(tma, tma_small, tmb, args, grid, st);
-        if (args.epi == EPI_STORE_F32) return launch_one<KIND_BF16, EPI_STORE_F32>(tma, tma_small, tmb, args, grid, st);
+        if (args.epi == EPI_SWIGLU_BF16) return launch_one<KIND_BF16, EPI_SWIGLU_BF16>(tma, tma_small, tmb, args, grid, dependent, st);
+        if (args.epi == EPI_STORE_F32) return launch_one<KIND_BF16, EPI_STORE_F32>(tma, tma_small, tmb, args, grid, dependent, st);
     }
     return cudaErrorInvalidValue;
 }

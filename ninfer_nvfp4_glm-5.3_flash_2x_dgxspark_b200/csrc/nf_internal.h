@@ -100,9 +100,11 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner_
 // boxes and 128-byte swizzle: box i is the 32 KB block i.
 bool make_tmap_blocked(CUtensorMap* map, const void* base, uint64_t bytes);
 // tma_small: the same A tensor with a 32-row box, used for tiles with <= 32
-// rows; tmb: B (make_tmap_blocked over args.b).
+// rows; tmb: B (make_tmap_blocked over args.b).  dependent: launch_dependent
+// (the kernel's CTAs may start, and hold their SMs, while the previous
+// kernel in `st` still runs), else an ordinary launch.
 cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
-                        const GemmArgs& args, int grid, cudaStream_t st);
+                        const GemmArgs& args, int grid, bool dependent, cudaStream_t st);
 int gemm_grid_size(int device);
 
 // Launchers (nf_kernels.cu).

@@ -644,7 +644,11 @@ int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cud
     sg.out = h->sh_h;
     sg.out_ld = Is;
     sg.tile_counter = h->shared_counters;
-    e = launch_gemm(tm_x, tm_x_s, h->tm_bs_gu, sg, h->grid, h->side);
+    // Few tiles at decode sizes: a grid of one CTA per tile leaves the other
+    // SMs to the routed path (the down GEMM's CTAs launch early and hold
+    // their SMs while gate/up finishes: few CTAs hold few SMs).
+    const int m_tiles = (T + 127) / 128;
+    e = launch_gemm(tm_x, tm_x_s, h->tm_bs_gu, sg, std::min(h->grid, m_tiles * (Is / 128)), false, h->side);
     if (e != cudaSuccess) return h->cuda_fail(e, "shared gate/up GEMM launch");
     sg.epi = EPI_STORE_F32;
     sg.K = Is;
@@ -655,7 +659,7 @@ int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cud
     sg.out = h->sh_out;
     sg.out_ld = H;
     sg.tile_counter = h->shared_counters + 1;
-    e = launch_gemm(h->tm_shh, h->tm_shh_s, h->tm_bs_dn, sg, h->grid, h->side);
+    e = launch_gemm(h->tm_shh, h->tm_shh_s, h->tm_bs_dn, sg, std::min(h->grid, m_tiles * (H / 256)), true, h->side);
     if (e != cudaSuccess) return h->cuda_fail(e, "shared down GEMM launch");
     rec.end(NF_STAGE_SHARED, h->side);
     if ((e = cudaEventRecord(h->ev_join, h->side)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
@@ -703,7 +707,7 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.out_sf = h->h_sf;
     g.out_kgroups = I / 16;
     g.tile_counter = h->pb.meta + 4;
-    e = launch_gemm(h->tm_a, h->tm_a_s, h->tm_b_gu, g, h->grid, s);
+    e = launch_gemm(h->tm_a, h->tm_a_s, h->tm_b_gu, g, h->grid, true, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "gate/up GEMM launch");
     rec.end(NF_STAGE_GATE_UP, s);
     rec.begin(NF_STAGE_DOWN, s);
@@ -722,7 +726,7 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.out = h->down;
     g.out_ld = H;
     g.tile_counter = h->pb.meta + 5;
-    e = launch_gemm(h->tm_h, h->tm_h_s, h->tm_b_dn, g, h->grid, s);
+    e = launch_gemm(h->tm_h, h->tm_h_s, h->tm_b_dn, g, h->grid, true, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "down GEMM launch");
     rec.end(NF_STAGE_DOWN, s);
     return NF_OK;
