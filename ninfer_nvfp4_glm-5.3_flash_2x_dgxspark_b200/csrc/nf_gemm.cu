@@ -180,8 +180,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             next = atomicAdd(args.tile_counter, 1);
             if (next < num_tiles) next_t = get_tile(args, next);
         }
-        auto stage_bytes = [&](bool small_a, int steps) {
-            uint32_t bytes = (small_a ? kSmallRows * 128 : A_STAGE_BYTES) + B_STAGE_BYTES;
+        // A is always a full 16 KB: tiles with at most 32 rows load their rows four
+        // times, into rows 0-31, 32-63, 64-95 and 96-127 (see the epilogue)
+        auto stage_bytes = [&](int steps) {
+            uint32_t bytes = A_STAGE_BYTES + B_STAGE_BYTES;
             if (KIND == KIND_NVFP4) bytes += static_cast<uint32_t>(steps) * 512u + SFB_STAGE_BYTES;
             return bytes;
         };
@@ -196,12 +198,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int first = __shfl_sync(0xffffffffu, next, 0);
             const int e0 = __shfl_sync(0xffffffffu, next_t.expert, 0);
             const int nb0 = __shfl_sync(0xffffffffu, next_t.n_block, 0);
-            const bool small0 = __shfl_sync(0xffffffffu, next_t.m_valid, 0) <= kSmallRows;
             if (first < num_tiles) {
                 pre = min(STAGES, k_tiles);
                 for (int kt = 0; kt < pre; ++kt) {
                     if (lane == 0)
-                        mbar_arrive_expect_tx(&full[kt], stage_bytes(small0, min(4, (K - kt * kElemsPerStage) / kMmaK)));
+                        mbar_arrive_expect_tx(&full[kt], stage_bytes(min(4, (K - kt * kElemsPerStage) / kMmaK)));
                     __syncwarp();
                     const int blk = (e0 * args.b_nb + nb0) * args.b_kt + kt;
                     if (lane == 1) {
@@ -242,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             t.row0 = __shfl_sync(0xffffffffu, t.row0, 0);
             t.n_block = __shfl_sync(0xffffffffu, t.n_block, 0);
             t.m_valid = __shfl_sync(0xffffffffu, t.m_valid, 0);
-            // tiles with at most 32 rows of the expert load only those rows of A
+            // tiles with at most 32 rows of the expert load only those rows of A (four times)
             const bool small_a = t.m_valid <= kSmallRows;
             for (int kt = 0; kt < k_tiles; ++kt) {
                 const int k0 = kt * kElemsPerStage;
@@ -253,16 +254,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                         set_abort(cta_abort, args.err, NF_DEVERR_WAIT_EMPTY);
                         ok = false;
                     } else {
-                        mbar_arrive_expect_tx(&full[stage], stage_bytes(small_a, steps));
+                        mbar_arrive_expect_tx(&full[stage], stage_bytes(steps));
                     }
                 }
                 ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
                 if (!ok) break;
                 // stage kt of tile (expert, n_block) is box `blk` of B and 4 KB group `blk` of its scales
                 const int blk = (t.expert * args.b_nb + t.n_block) * args.b_kt + kt;
+                const int xc = KIND == KIND_NVFP4 ? kt * 128 : k0;  // A's K coordinate (bytes or BF16 elements)
                 if (lane == 0) {
-                    const int xc = KIND == KIND_NVFP4 ? kt * 128 : k0;
                     tma_load_2d(sA + stage * A_STAGE_BYTES, small_a ? &tma_small : &tma, &full[stage], xc, t.row0);
+                } else if (small_a && lane >= 4 && lane <= 6) {
+                    tma_load_2d(sA + stage * A_STAGE_BYTES + (lane - 3) * kSmallRows * 128, &tma_small, &full[stage], xc,
+                                t.row0);
                 } else if (lane == 1 && !b_issued) {
                     tma_load_2d_hint(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0, blk * BN, stream_policy);
                 } else if (KIND == KIND_NVFP4 && lane == 2) {
@@ -401,11 +405,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok || tile < 0) break;
             const TileInfo t = get_tile(args, tile);
             tc_fence_after();
-            const int row = t.row0 + r;
-            const bool valid = r < t.m_valid;
-            const bool warp_live = q * 32 < t.m_valid;  // some row of this warp belongs to the expert
+            // A tile of at most 32 rows holds them in every TMEM lane quadrant (A was
+            // loaded four times), so for the NVFP4 epilogues all sixteen warps take a
+            // share of its columns instead of quadrant 0's four: SwiGLU-quantise, one
+            // 16-output group per warp (cs < 2); down, 16 columns per warp.
+            const bool rep = KIND == KIND_NVFP4 && t.m_valid <= kSmallRows;
+            const int row = rep ? t.row0 + lane : t.row0 + r;
+            const bool valid = rep ? lane < t.m_valid : r < t.m_valid;
+            // some row of this warp belongs to the expert (and the warp has columns)
+            const bool warp_live = rep ? (EPI != EPI_SWIGLU_QUANT || cs < 2) : q * 32 < t.m_valid;
+            const int rg = 2 * q + cs;      // replicated SwiGLU: output group (16 columns)
+            const int rc = 16 * (4 * q + cs);  // replicated down: first column
             uint32_t v[64];
-            if (warp_live) {
+            if (warp_live && rep) {
+                if (EPI == EPI_SWIGLU_QUANT) {
+                    tmem_ld16(tbase + 16 * rg, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                    tmem_ld16(tbase + 128 + 16 * rg, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
+                } else {
+                    tmem_ld16(tbase + rc, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                }
+                tmem_wait_ld();
+            } else if (warp_live) {
                 if (EPI == EPI_SWIGLU_QUANT || EPI == EPI_SWIGLU_BF16) {
                     // gate columns [32cs, 32cs+32), up columns 128 further
                     tmem_ld16(tbase + 32 * cs, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
@@ -443,8 +463,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float gsd = args.gscale_next[t.expert], L = args.limit;
                 uint32_t cc[2][2];
                 uint32_t sc[2];
+                const int ng = rep ? 1 : 2;
 #pragma unroll
                 for (int g = 0; g < 2; ++g) {
+                    if (g >= ng) break;
                     float h[16];
 #pragma unroll
                     for (int j = 0; j < 16; j += 2) {
@@ -458,7 +480,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     sc[g] = quantize_group16_fast<false>(h, gsd, cc[g]);
                 }
-                if (valid) {
+                if (valid && rep) {
+                    uint8_t* o = static_cast<uint8_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
+                                 t.n_block * 64 + rg * 8;
+                    *reinterpret_cast<uint2*>(o) = make_uint2(cc[0][0], cc[0][1]);
+                    // the down GEMM loads this tile's rows four times too: the scale
+                    // goes to all four lane-quadrant columns of the atom
+                    uint8_t* sfp = args.out_sf + sf_atom_offset(row, t.n_block * 8 + rg, args.out_kgroups);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) sfp[4 * k] = static_cast<uint8_t>(sc[0]);
+                } else if (valid) {
                     uint8_t* o = static_cast<uint8_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
                                  t.n_block * 64 + cs * 16;
                     *reinterpret_cast<uint4*>(o) = make_uint4(cc[0][0], cc[0][1], cc[1][0], cc[1][1]);
@@ -468,6 +499,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else if (EPI == EPI_STORE_BF16) {
                 const float a = args.alpha0[t.expert];
                 uint32_t p[32];
+                if (rep) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        p[j] = bf16x2_hw(__fmul_rn(__uint_as_float(v[2 * j]), a), __fmul_rn(__uint_as_float(v[2 * j + 1]), a));
+                    if (valid) {
+                        uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) +
+                                                            static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + rc);
+                        d[0] = make_uint4(p[0], p[1], p[2], p[3]);
+                        d[1] = make_uint4(p[4], p[5], p[6], p[7]);
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
                     p[j] = bf16x2_hw(__fmul_rn(__uint_as_float(v[2 * j]), a), __fmul_rn(__uint_as_float(v[2 * j + 1]), a));

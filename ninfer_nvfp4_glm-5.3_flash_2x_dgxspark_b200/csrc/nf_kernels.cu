@@ -1078,7 +1078,8 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const int32_t* __rest
 // lanes of a warp write 1 KB of contiguous codes.
 // ---------------------------------------------------------------------------
 __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ idx,
-                                const int32_t* __restrict__ pair_row, const float* __restrict__ gscale, int T, int K,
+                                const int32_t* __restrict__ pair_row, const int32_t* __restrict__ counts,
+                                const int32_t* __restrict__ seg_off, const float* __restrict__ gscale, int T, int K,
                                 int H, int bf16_mode, uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
                                 uint16_t* __restrict__ a_bf16) {
     pdl_wait();  // launched dependent on the previous kernel
@@ -1128,7 +1129,13 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
         uint4* dst = reinterpret_cast<uint4*>(a_codes + static_cast<int64_t>(row) * (H / 2) + q * 32);
         dst[0] = make_uint4(codes[0][0], codes[0][1], codes[1][0], codes[1][1]);
         dst[1] = make_uint4(codes[2][0], codes[2][1], codes[3][0], codes[3][1]);
-        *reinterpret_cast<uint32_t*>(a_sf + sf_atom_offset(row, q * 4, H / 16)) = sfw;
+        // A GEMM tile with at most 32 rows loads them four times (TMEM lane
+        // quadrants 0-3), so its rows' scales go to all four quadrant columns
+        // of the atom: the 16 bytes of this row's slot.
+        const int rank = row - seg_off[e];
+        uint8_t* sfp = a_sf + sf_atom_offset(row, q * 4, H / 16);
+        if (counts[e] - (rank & ~127) <= 32) *reinterpret_cast<uint4*>(sfp) = make_uint4(sfw, sfw, sfw, sfw);
+        else *reinterpret_cast<uint32_t*>(sfp) = sfw;
     }
 }
 
@@ -1354,7 +1361,8 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
     }
     const int64_t items = static_cast<int64_t>(T) * (H / 64);
     return launch_dependent(dispatch_kernel, dim3(static_cast<unsigned>((items + 127) / 128)), dim3(128), 0, st, x, idx,
-                            static_cast<const int32_t*>(b.pair_row), gscale, T, K, H, bf16_mode, b.a_codes, b.a_sf,
+                            static_cast<const int32_t*>(b.pair_row), static_cast<const int32_t*>(b.counts),
+                            static_cast<const int32_t*>(b.seg_off), gscale, T, K, H, bf16_mode, b.a_codes, b.a_sf,
                             b.a_bf16);
 }
 
