@@ -1072,10 +1072,11 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const int32_t* __rest
 // Dispatch: x rows into the permuted activation buffer.  NVFP4 experts: the
 // row of pick (t, p) is x[t] quantised with the gate input_scale of expert
 // idx[t, p] (quant_dequant_nvfp4_activation, src/text_forward.cpp:527-550),
-// stored as E2M1 codes plus E4M3 scales in the tcgen05 atom layout; one
-// quantisation serves every pick whose expert has the same scale.  BF16
-// experts: plain row copies.  One thread per (token, 64 columns): the 32
-// lanes of a warp write 1 KB of contiguous codes.
+// stored as E2M1 codes plus E4M3 scales in the tcgen05 atom layout.  BF16
+// experts: plain row copies.  One thread per (token, pick, 16-element
+// group): a decode step is 64 x 4 x 128 threads, enough to cover the GPU in
+// one wave (one thread per token and 64 columns left it latency-bound on 16
+// CTAs); the threads of one pick write its row's codes contiguously.
 // ---------------------------------------------------------------------------
 __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ idx,
                                 const int32_t* __restrict__ pair_row, const int32_t* __restrict__ counts,
@@ -1084,59 +1085,39 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
                                 uint16_t* __restrict__ a_bf16) {
     pdl_wait();  // launched dependent on the previous kernel
     pdl_trigger();
-    const int gq = H / 64;
+    const int gq = H / 16;
     const int64_t item = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-    if (item >= static_cast<int64_t>(T) * gq) return;
-    const int t = static_cast<int>(item / gq), q = static_cast<int>(item % gq);
-    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * H + q * 64);
-    uint4 raw[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) raw[i] = __ldg(src + i);
+    if (item >= static_cast<int64_t>(T) * K * gq) return;
+    const int64_t pair = item / gq;
+    const int g = static_cast<int>(item - pair * gq);
+    const int t = static_cast<int>(pair / K);
+    const int row = pair_row[pair];
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * H + g * 16);
+    const uint4 r0 = __ldg(src), r1 = __ldg(src + 1);
     if (bf16_mode) {
-        for (int p = 0; p < K; ++p) {
-            const int row = pair_row[static_cast<int64_t>(t) * K + p];
-            uint4* dst = reinterpret_cast<uint4*>(a_bf16 + static_cast<int64_t>(row) * H + q * 64);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) dst[i] = raw[i];
-        }
+        uint4* dst = reinterpret_cast<uint4*>(a_bf16 + static_cast<int64_t>(row) * H + g * 16);
+        dst[0] = r0;
+        dst[1] = r1;
         return;
     }
-    float v[4][16];
+    const int e = idx[pair];
+    const uint32_t u[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+    float v[16];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const uint32_t u[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            v[i >> 1][(i & 1) * 8 + 2 * j] = bf16_lo(u[j]);
-            v[i >> 1][(i & 1) * 8 + 2 * j + 1] = bf16_hi(u[j]);
-        }
+    for (int j = 0; j < 8; ++j) {
+        v[2 * j] = bf16_lo(u[j]);
+        v[2 * j + 1] = bf16_hi(u[j]);
     }
-    float cur_gs = 0.f;
-    bool have = false;
-    uint32_t codes[4][2];
-    uint32_t sfw = 0u;
-    for (int p = 0; p < K; ++p) {
-        const int e = idx[static_cast<int64_t>(t) * K + p];
-        const int row = pair_row[static_cast<int64_t>(t) * K + p];
-        const float gs = gscale[e];
-        if (!have || gs != cur_gs) {
-            sfw = 0u;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) sfw |= quantize_group16_fast<true>(v[j], gs, codes[j]) << (8 * j);
-            cur_gs = gs;
-            have = true;
-        }
-        uint4* dst = reinterpret_cast<uint4*>(a_codes + static_cast<int64_t>(row) * (H / 2) + q * 32);
-        dst[0] = make_uint4(codes[0][0], codes[0][1], codes[1][0], codes[1][1]);
-        dst[1] = make_uint4(codes[2][0], codes[2][1], codes[3][0], codes[3][1]);
-        // A GEMM tile with at most 32 rows loads them four times (TMEM lane
-        // quadrants 0-3), so its rows' scales go to all four quadrant columns
-        // of the atom: the 16 bytes of this row's slot.
-        const int rank = row - seg_off[e];
-        uint8_t* sfp = a_sf + sf_atom_offset(row, q * 4, H / 16);
-        if (counts[e] - (rank & ~127) <= 32) *reinterpret_cast<uint4*>(sfp) = make_uint4(sfw, sfw, sfw, sfw);
-        else *reinterpret_cast<uint32_t*>(sfp) = sfw;
-    }
+    uint32_t codes[2];
+    const uint32_t sf = quantize_group16_fast<true>(v, gscale[e], codes);
+    *reinterpret_cast<uint2*>(a_codes + static_cast<int64_t>(row) * (H / 2) + g * 8) = make_uint2(codes[0], codes[1]);
+    // A GEMM tile with at most 32 rows loads them four times (TMEM lane
+    // quadrants 0-3), so its rows' scales go to all four quadrant columns of
+    // the atom (bytes 4 apart).
+    uint8_t* sfp = a_sf + sf_atom_offset(row, g, H / 16);
+    const int rank = row - seg_off[e];
+    const int copies = counts[e] - (rank & ~127) <= 32 ? 4 : 1;
+    for (int k = 0; k < copies; ++k) sfp[4 * k] = static_cast<uint8_t>(sf);
 }
 
 // ---------------------------------------------------------------------------
@@ -1359,7 +1340,7 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
                                  b.pair_row, b.row_token);
         if (e != cudaSuccess) return e;
     }
-    const int64_t items = static_cast<int64_t>(T) * (H / 64);
+    const int64_t items = static_cast<int64_t>(T) * K * (H / 16);
     return launch_dependent(dispatch_kernel, dim3(static_cast<unsigned>((items + 127) / 128)), dim3(128), 0, st, x, idx,
                             static_cast<const int32_t*>(b.pair_row), static_cast<const int32_t*>(b.counts),
                             static_cast<const int32_t*>(b.seg_off), gscale, T, K, H, bf16_mode, b.a_codes, b.a_sf,
