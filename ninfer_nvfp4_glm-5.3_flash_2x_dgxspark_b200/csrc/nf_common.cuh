@@ -232,6 +232,9 @@ NF_DEV void mbar_init(uint64_t* bar, uint32_t count) {
 }
 NF_DEV void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 NF_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Orders this thread's generic-proxy global accesses with async-proxy (TMA)
+// ones: global data written by st.global in one CTA and read by TMA in another.
+NF_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 NF_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");

@@ -90,6 +90,20 @@ __device__ __forceinline__ float swiglu_fast(float g, float u, float L) {
     return __fmul_rn(__fdividef(cg, 1.f + __expf(-cg)), cu);
 }
 
+// Bounded wait, by every lane of the calling warp, until *counter >= target
+// (acquire); false once the budget runs out or the CTA or kernel gave up.
+__device__ __forceinline__ bool wait_count(const int* counter, int target, volatile int* cta_abort,
+                                           volatile int* dev_err) {
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+        if (v >= target) return true;
+        if (*cta_abort != 0 || *dev_err != 0 || globaltimer_ns() - t0 > NF_WAIT_BUDGET_NS) return false;
+        __nanosleep(64);
+    }
+}
+
 __device__ __forceinline__ void set_abort(volatile int* cta_abort, int* dev_err, int code) {
     *cta_abort = 1;
     atomicCAS(dev_err, 0, code);
@@ -216,7 +230,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-        pdl_wait();
+        // With mt_wait the tiles wait for their own rows of the gate/up GEMM's
+        // output (below) rather than for that whole kernel.
+        if (args.mt_wait == 0) pdl_wait();
         if (lane == 0) pdl_trigger();
         bool first_tile = true;
         while (ok) {
@@ -245,6 +261,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             t.m_valid = __shfl_sync(0xffffffffu, t.m_valid, 0);
             // tiles with at most 32 rows of the expert load only those rows of A (four times)
             const bool small_a = t.m_valid <= kSmallRows;
+            if (args.mt_wait > 0) {
+                // A (and its scales) are the gate/up GEMM's output for these rows:
+                // generic stores in other CTAs, ordered before these TMA reads by
+                // the counter's release/acquire and the proxy fences
+                if (!wait_count(args.mt_done + t.row0 / BM, args.mt_wait, cta_abort, dev_err)) {
+                    if (lane == 0) set_abort(cta_abort, args.err, NF_DEVERR_WAIT_FULL);
+                    ok = false;
+                    break;
+                }
+                fence_proxy_async_global();
+            }
             for (int kt = 0; kt < k_tiles; ++kt) {
                 const int k0 = kt * kElemsPerStage;
                 const int steps = min(4, (K - k0) / kMmaK);
@@ -456,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty);
             acc_phase ^= 1u;
-            if (!warp_live) continue;
+            if (warp_live) {
 
             if (EPI == EPI_SWIGLU_QUANT) {
                 const float ag = args.alpha0[t.expert], au = args.alpha1[t.expert];
@@ -534,6 +561,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 4; ++j) d[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
                 }
             }  // EPI_STORE_F32 stored while reading the accumulator
+            }
+            if (EPI == EPI_SWIGLU_QUANT || EPI == EPI_SWIGLU_BF16) {
+                if (args.mt_signal) {
+                    // count the tile for the down GEMM once every warp's stores are out
+                    named_bar_sync(2, 32 * kEpiWarps);
+                    if (leader) {
+                        __threadfence();
+                        fence_proxy_async_global();
+                        atomicAdd(args.mt_done + t.row0 / BM, 1);
+                    }
+                }
+            }
         }
     } else if (KIND == KIND_NVFP4 && lane == 0) {
         // --------------------------- scale-factor copies -----------------------

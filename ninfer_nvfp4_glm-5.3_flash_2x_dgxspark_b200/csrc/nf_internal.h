@@ -29,6 +29,7 @@ struct PermuteBuffers {
     NfTile* tiles_down;     // down tile list
     int32_t* meta;          // [0] rows in use, [1] gate/up tiles, [2] down tiles, [3] m-tiles,
                             // [4] / [5] gate/up / down tile counters (reset here)
+    int32_t* mt_done;       // [rows_cap / 128] gate/up tiles finished per m-tile (GemmArgs::mt_done; reset here)
     uint8_t* a_codes;       // NVFP4 dispatch: [rows_cap, H/2]
     uint8_t* a_sf;          //                 scale atoms
     uint16_t* a_bf16;       // BF16 dispatch:  [rows_cap, H]
@@ -73,6 +74,11 @@ struct GemmArgs {
     int out_kgroups;           // EPI_SWIGLU_QUANT: 16-groups per output row
     int* err;                  // device error word
     int* tile_counter;         // tiles claimed so far (zero before the launch)
+    // Row-block hand-off between the gate/up and the down GEMM (both grouped):
+    int* mt_done;              // per 128-row m-tile: gate/up tiles finished (zeroed by the permutation)
+    int mt_signal;             // gate/up: count each finished tile in mt_done[row0 / 128]
+    int mt_wait;               // down: > 0 loads a tile's A only once mt_done[row0 / 128] >= mt_wait,
+                               // instead of waiting for the whole previous kernel (pdl_wait)
 };
 
 // Launches `kernel` with programmatic stream serialization: it may begin

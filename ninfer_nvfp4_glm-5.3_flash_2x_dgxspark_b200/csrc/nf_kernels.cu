@@ -874,7 +874,8 @@ constexpr int kSmallPairs = 2048;
 __device__ void build_segments(const int32_t* s_cnt, int32_t* s_off, int32_t* s_mt, int E, int nb_gu, int nb_down,
                                int32_t* __restrict__ counts, int32_t* __restrict__ seg_off,
                                int32_t* __restrict__ row_token, NfTile* __restrict__ tiles_gu,
-                               NfTile* __restrict__ tiles_down, int32_t* __restrict__ meta) {
+                               NfTile* __restrict__ tiles_down, int32_t* __restrict__ meta,
+                               int32_t* __restrict__ mt_done) {
     // exclusive scans of padded rows and m-tiles (warp 0, 32 experts a pass)
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
@@ -920,6 +921,7 @@ __device__ void build_segments(const int32_t* s_cnt, int32_t* s_off, int32_t* s_
     // tile lists, ordered (expert, n_block, m_tile): CTAs that run at the same
     // time share the weight block through L2
     const int32_t mt_total = s_mt[E];
+    for (int32_t i = threadIdx.x; i < mt_total; i += blockDim.x) mt_done[i] = 0;
     for (int pass = 0; pass < 2; ++pass) {
         const int nb = pass == 0 ? nb_gu : nb_down;
         NfTile* tiles = pass == 0 ? tiles_gu : tiles_down;
@@ -953,7 +955,8 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __re
                                                              int32_t* __restrict__ row_token,
                                                              NfTile* __restrict__ tiles_gu,
                                                              NfTile* __restrict__ tiles_down,
-                                                             int32_t* __restrict__ meta) {
+                                                             int32_t* __restrict__ meta,
+                                                             int32_t* __restrict__ mt_done) {
     pdl_wait();  // launched dependent on the previous kernel
     pdl_trigger();
     extern __shared__ int32_t sh[];
@@ -977,7 +980,8 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __re
         atomicOr(&s_mask[e * words + (t >> 5)], 1u << (t & 31));
     }
     __syncthreads();
-    build_segments(s_cnt, s_off, s_mt, E, nb_gu, nb_down, counts, seg_off, row_token, tiles_gu, tiles_down, meta);
+    build_segments(s_cnt, s_off, s_mt, E, nb_gu, nb_down, counts, seg_off, row_token, tiles_gu, tiles_down, meta,
+                   mt_done);
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int e = s_idx[i], t = i / K;
         const uint32_t* m = s_mask + e * words;
@@ -1011,7 +1015,8 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __res
                                                             int32_t* __restrict__ row_token,
                                                             NfTile* __restrict__ tiles_gu,
                                                             NfTile* __restrict__ tiles_down,
-                                                            int32_t* __restrict__ meta) {
+                                                            int32_t* __restrict__ meta,
+                                                            int32_t* __restrict__ mt_done) {
     pdl_wait();  // launched dependent on the previous kernel
     pdl_trigger();
     extern __shared__ int32_t sh[];
@@ -1030,7 +1035,8 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __res
         s_cnt[e] = run;
     }
     __syncthreads();
-    build_segments(s_cnt, s_off, s_mt, E, nb_gu, nb_down, counts, seg_off, row_token, tiles_gu, tiles_down, meta);
+    build_segments(s_cnt, s_off, s_mt, E, nb_gu, nb_down, counts, seg_off, row_token, tiles_gu, tiles_down, meta,
+                   mt_done);
 }
 
 // Rows of a chunk of kChunkTok tokens.  A token's picks are distinct experts,
@@ -1323,7 +1329,7 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
         const size_t smem = small_smem;
         cudaError_t e = launch_dependent(permute_small_kernel, dim3(1), dim3(1024), smem, st, idx, T, K, E, nb_gu,
                                          nb_down, b.counts, b.seg_off, b.pair_row, b.row_token, b.tiles_gu,
-                                         b.tiles_down, b.meta);
+                                         b.tiles_down, b.meta, b.mt_done);
         if (e != cudaSuccess) return e;
     } else {
         const int nchunks = (T + kChunkTok - 1) / kChunkTok;
@@ -1332,7 +1338,7 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
         if (e == cudaSuccess)
             e = launch_dependent(permute_scan_kernel, dim3(1), dim3(1024), (3 * E + 2) * sizeof(int32_t), st,
                                  static_cast<const int32_t*>(b.chunk_counts), nchunks, E, nb_gu, nb_down, b.chunk_base,
-                                 b.counts, b.seg_off, b.row_token, b.tiles_gu, b.tiles_down, b.meta);
+                                 b.counts, b.seg_off, b.row_token, b.tiles_gu, b.tiles_down, b.meta, b.mt_done);
         if (e == cudaSuccess)
             e = launch_dependent(permute_rows_kernel, dim3(nchunks), dim3(256),
                                  static_cast<size_t>(E) * kChunkWords * sizeof(uint32_t), st, idx, T, K, E,

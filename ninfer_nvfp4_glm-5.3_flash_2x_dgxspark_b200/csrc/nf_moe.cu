@@ -288,7 +288,8 @@ int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::s
              h->alloc(&b.chunk_base, static_cast<int64_t>(h->nchunks_cap) * E) && h->alloc(&b.counts, E) &&
              h->alloc(&b.seg_off, E + 1) && h->alloc(&b.pair_row, pairs) && h->alloc(&b.row_token, R) &&
              h->alloc(&b.tiles_gu, static_cast<int64_t>(h->mtiles_cap) * (I / 128)) &&
-             h->alloc(&b.tiles_down, static_cast<int64_t>(h->mtiles_cap) * (H / 256)) && h->alloc(&b.meta, 8);
+             h->alloc(&b.tiles_down, static_cast<int64_t>(h->mtiles_cap) * (H / 256)) && h->alloc(&b.meta, 8) &&
+             h->alloc(&b.mt_done, h->mtiles_cap);
     }
     ok = ok && h->alloc(&h->shared_counters, 2);
     ok = ok && cudaStreamCreateWithFlags(&h->side, cudaStreamNonBlocking) == cudaSuccess &&
@@ -707,6 +708,13 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.out_sf = h->h_sf;
     g.out_kgroups = I / 16;
     g.tile_counter = h->pb.meta + 4;
+    // Unprofiled forwards hand rows over block by block: the down GEMM's
+    // tiles start as soon as the gate/up tiles of their 128 rows are done (so
+    // its CTAs work through the gate/up GEMM's tail instead of waiting for the
+    // whole kernel); profiled forwards keep the kernels apart to time them.
+    const bool handoff = rec.ev == nullptr;
+    g.mt_done = h->pb.mt_done;
+    g.mt_signal = handoff ? 1 : 0;
     e = launch_gemm(h->tm_a, h->tm_a_s, h->tm_b_gu, g, h->grid, true, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "gate/up GEMM launch");
     rec.end(NF_STAGE_GATE_UP, s);
@@ -726,6 +734,8 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.out = h->down;
     g.out_ld = H;
     g.tile_counter = h->pb.meta + 5;
+    g.mt_signal = 0;
+    g.mt_wait = handoff ? I / 128 : 0;
     e = launch_gemm(h->tm_h, h->tm_h_s, h->tm_b_dn, g, h->grid, true, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "down GEMM launch");
     rec.end(NF_STAGE_DOWN, s);
