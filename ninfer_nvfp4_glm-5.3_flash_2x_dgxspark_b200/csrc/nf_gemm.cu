@@ -162,7 +162,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    const int num_tiles = args.dense_rows > 0 ? ((args.dense_rows + BM - 1) / BM) * args.n_blocks : *args.num_tiles_dev;
     const int K = args.K;
     constexpr int kElemsPerStage = KIND == KIND_NVFP4 ? 256 : 64;
     constexpr int kMmaK = KIND == KIND_NVFP4 ? 64 : 16;
@@ -188,12 +187,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         // last and its descriptor read at the last, so neither the atomic nor
         // the dependent load sits between two tiles' copies (and a CTA holds
         // no tile long before it can start it).
-        int next = 0;
+        int next = 0, num_tiles = 0;
         TileInfo next_t{};
-        if (lane == 0) {
-            next = atomicAdd(args.tile_counter, 1);
-            if (next < num_tiles) next_t = get_tile(args, next);
-        }
+        auto claim_first = [&]() {
+            num_tiles = args.dense_rows > 0 ? ((args.dense_rows + BM - 1) / BM) * args.n_blocks : *args.num_tiles_dev;
+            if (lane == 0) {
+                next = atomicAdd(args.tile_counter, 1);
+                if (next < num_tiles) next_t = get_tile(args, next);
+            }
+        };
+        if (args.early_claim) claim_first();
         // A is always a full 16 KB: tiles with at most 32 rows load their rows four
         // times, into rows 0-31, 32-63, 64-95 and 96-127 (see the epilogue)
         auto stage_bytes = [&](int steps) {
@@ -202,13 +205,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             return bytes;
         };
         // The kernel may start while the one that writes A is still running
-        // (launch_dependent): the tile list and its counter come from the
-        // permutation, which has completed by then, and B and its scales are
-        // weights, so the first tile's first stages of B go out before
+        // (launch_dependent).  With early_claim the tile list and its counter
+        // come from a kernel that has completed by then, and B and its scales
+        // are weights, so the first tile's first stages of B go out before
         // pdl_wait(); A and its scales follow it.
         const uint64_t stream_policy = l2_evict_first();  // B and its scales: read once per step
         int pre = 0;
-        {
+        if (args.early_claim) {
             const int first = __shfl_sync(0xffffffffu, next, 0);
             const int e0 = __shfl_sync(0xffffffffu, next_t.expert, 0);
             const int nb0 = __shfl_sync(0xffffffffu, next_t.n_block, 0);
@@ -234,6 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // output (below) rather than for that whole kernel.
         if (args.mt_wait == 0) pdl_wait();
         if (lane == 0) pdl_trigger();
+        if (!args.early_claim) claim_first();
         bool first_tile = true;
         while (ok) {
             // publish the claimed tile to the MMA and epilogue warps (-1 ends

@@ -79,6 +79,8 @@ struct GemmArgs {
     int mt_signal;             // gate/up: count each finished tile in mt_done[row0 / 128]
     int mt_wait;               // down: > 0 loads a tile's A only once mt_done[row0 / 128] >= mt_wait,
                                // instead of waiting for the whole previous kernel (pdl_wait)
+    int early_claim;           // the tile list and counter come from two or more launches back: claim
+                               // the first tile and issue its first B stages before pdl_wait()
 };
 
 // Launches `kernel` with programmatic stream serialization: it may begin
@@ -160,8 +162,11 @@ inline void router_chunked_layout16(const uint16_t* w, int E, int H, uint16_t* o
             }
         }
 }
+// one_kernel: set when the permutation and the dispatch ran as one kernel
+// (small batches), so the kernel after it must not read the tile lists before
+// pdl_wait().
 cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
-                           const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st);
+                           const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st, bool* one_kernel);
 cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair_row, const float* topk_w,
                            const float* shared, const float* residual, int T, int K, int H, float* y,
                            cudaStream_t st);

@@ -868,18 +868,14 @@ __global__ void __launch_bounds__(kFzCThreads + 32 * PW, 1) router_fused_kernel(
 constexpr int kChunkTok = 128;
 constexpr int kSmallPairs = 2048;
 
-// Segment offsets, padding rows, GEMM tile lists and meta from per-expert
-// counts in shared memory (s_cnt [E]); s_off and s_mt get [E + 1] entries.
-// Whole CTA; ends with the CTA synchronised.
-__device__ void build_segments(const int32_t* s_cnt, int32_t* s_off, int32_t* s_mt, int E, int nb_gu, int nb_down,
-                               int32_t* __restrict__ counts, int32_t* __restrict__ seg_off,
-                               int32_t* __restrict__ row_token, NfTile* __restrict__ tiles_gu,
-                               NfTile* __restrict__ tiles_down, int32_t* __restrict__ meta,
-                               int32_t* __restrict__ mt_done) {
-    // exclusive scans of padded rows and m-tiles (warp 0, 32 experts a pass)
+// Segment offsets of the permuted rows (each expert's segment padded to a
+// multiple of 128) and m-tile offsets from per-expert counts in shared memory
+// (s_cnt [E]); s_off and s_mt get [E + 1] entries.  Warp 0 scans; ends with
+// the CTA synchronised.
+__device__ void segment_scan(const int32_t* s_cnt, int32_t* s_off, int32_t* s_mt, int E) {
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
-        int32_t base_off = 0, base_mt = 0;
+        int32_t base_mt = 0;
         for (int e0 = 0; e0 < E; e0 += 32) {
             const int e = e0 + lane;
             const int32_t m = e < E ? (s_cnt[e] + 127) / 128 : 0;
@@ -895,37 +891,51 @@ __device__ void build_segments(const int32_t* s_cnt, int32_t* s_off, int32_t* s_
             }
             base_mt += __shfl_sync(0xffffffffu, inc, 31);
         }
-        base_off = base_mt * 128;
         if (lane == 0) {
             s_mt[E] = base_mt;
-            s_off[E] = base_off;
-            meta[0] = base_off;
-            meta[1] = base_mt * nb_gu;
-            meta[2] = base_mt * nb_down;
-            meta[3] = base_mt;
-            meta[4] = 0;  // tile counters of the two grouped GEMMs
-            meta[5] = 0;
+            s_off[E] = base_mt * 128;
         }
     }
     __syncthreads();
-    for (int e = threadIdx.x; e <= E; e += blockDim.x) {
+}
+
+// The permutation's global outputs that follow from the scan: meta, segment
+// offsets and counts, padding rows (-1 in row_token), the two GEMM tile lists
+// and the zeroed per-m-tile counters.  Work item i of each list is done by
+// thread (i mod stride) of part i / blockDim.x mod parts: one CTA (part 0 of
+// 1) or every CTA of a grid (blockIdx.x of gridDim.x) sharing the lists.
+__device__ void segment_outputs(const int32_t* s_cnt, const int32_t* s_off, const int32_t* s_mt, int E, int nb_gu,
+                                int nb_down, int part, int parts, int32_t* __restrict__ counts,
+                                int32_t* __restrict__ seg_off, int32_t* __restrict__ row_token,
+                                NfTile* __restrict__ tiles_gu, NfTile* __restrict__ tiles_down,
+                                int32_t* __restrict__ meta, int32_t* __restrict__ mt_done) {
+    const int32_t mt_total = s_mt[E];
+    const int first = part * blockDim.x + threadIdx.x, stride = parts * blockDim.x;
+    if (part == 0 && threadIdx.x == 0) {
+        meta[0] = s_off[E];
+        meta[1] = mt_total * nb_gu;
+        meta[2] = mt_total * nb_down;
+        meta[3] = mt_total;
+        meta[4] = 0;  // tile counters of the two grouped GEMMs
+        meta[5] = 0;
+    }
+    for (int e = first; e <= E; e += stride) {
         seg_off[e] = s_off[e];
         if (e < E) counts[e] = s_cnt[e];
     }
     // padding rows (at most 127 per expert)
-    for (int i = threadIdx.x; i < E * 128; i += blockDim.x) {
+    for (int i = first; i < E * 128; i += stride) {
         const int e = i >> 7, j = i & 127;
         const int32_t r = s_off[e] + s_cnt[e] + j;
         if (r < s_off[e + 1]) row_token[r] = -1;
     }
+    for (int32_t i = first; i < mt_total; i += stride) mt_done[i] = 0;
     // tile lists, ordered (expert, n_block, m_tile): CTAs that run at the same
     // time share the weight block through L2
-    const int32_t mt_total = s_mt[E];
-    for (int32_t i = threadIdx.x; i < mt_total; i += blockDim.x) mt_done[i] = 0;
     for (int pass = 0; pass < 2; ++pass) {
         const int nb = pass == 0 ? nb_gu : nb_down;
         NfTile* tiles = pass == 0 ? tiles_gu : tiles_down;
-        for (int32_t i = threadIdx.x; i < mt_total * nb; i += blockDim.x) {
+        for (int32_t i = first; i < mt_total * nb; i += stride) {
             const int32_t mi = i / nb;  // any tile of m-tile group mi's expert
             int lo = 0, hi = E - 1;     // expert e with s_mt[e] <= mi < s_mt[e + 1]
             while (lo < hi) {
@@ -945,52 +955,18 @@ __device__ void build_segments(const int32_t* s_cnt, int32_t* s_off, int32_t* s_
             tiles[i] = t;
         }
     }
-    __syncthreads();
 }
 
-__global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
-                                                             int nb_gu, int nb_down, int32_t* __restrict__ counts,
-                                                             int32_t* __restrict__ seg_off,
-                                                             int32_t* __restrict__ pair_row,
-                                                             int32_t* __restrict__ row_token,
-                                                             NfTile* __restrict__ tiles_gu,
-                                                             NfTile* __restrict__ tiles_down,
-                                                             int32_t* __restrict__ meta,
-                                                             int32_t* __restrict__ mt_done) {
-    pdl_wait();  // launched dependent on the previous kernel
-    pdl_trigger();
-    extern __shared__ int32_t sh[];
-    int32_t* s_cnt = sh;
-    int32_t* s_off = s_cnt + E;
-    int32_t* s_mt = s_off + E + 1;
-    int32_t* s_idx = s_mt + E + 1;  // [T * K]
-    // per expert, a bit per token that picked it (the picks of a token are
-    // distinct experts): the rank of pick (t, e) in expert e's segment is the
-    // popcount of e's bits below t
-    const int words = (T + 31) / 32;
-    uint32_t* s_mask = reinterpret_cast<uint32_t*>(s_idx + T * K);  // [E][words]
-    const int n = T * K;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
-    for (int i = threadIdx.x; i < E * words; i += blockDim.x) s_mask[i] = 0u;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s_idx[i] = idx[i];
+// Scan and every global output in one CTA; ends with the CTA synchronised.
+__device__ void build_segments(const int32_t* s_cnt, int32_t* s_off, int32_t* s_mt, int E, int nb_gu, int nb_down,
+                               int32_t* __restrict__ counts, int32_t* __restrict__ seg_off,
+                               int32_t* __restrict__ row_token, NfTile* __restrict__ tiles_gu,
+                               NfTile* __restrict__ tiles_down, int32_t* __restrict__ meta,
+                               int32_t* __restrict__ mt_done) {
+    segment_scan(s_cnt, s_off, s_mt, E);
+    segment_outputs(s_cnt, s_off, s_mt, E, nb_gu, nb_down, 0, 1, counts, seg_off, row_token, tiles_gu, tiles_down,
+                    meta, mt_done);
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int e = s_idx[i], t = i / K;
-        atomicAdd(&s_cnt[e], 1);
-        atomicOr(&s_mask[e * words + (t >> 5)], 1u << (t & 31));
-    }
-    __syncthreads();
-    build_segments(s_cnt, s_off, s_mt, E, nb_gu, nb_down, counts, seg_off, row_token, tiles_gu, tiles_down, meta,
-                   mt_done);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int e = s_idx[i], t = i / K;
-        const uint32_t* m = s_mask + e * words;
-        int rank = __popc(m[t >> 5] & ((1u << (t & 31)) - 1u));
-        for (int wd = 0; wd < (t >> 5); ++wd) rank += __popc(m[wd]);
-        const int32_t row = s_off[e] + rank;
-        pair_row[i] = row;
-        row_token[row] = t;
-    }
 }
 
 __global__ void permute_hist_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
@@ -1084,20 +1060,12 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const int32_t* __rest
 // one wave (one thread per token and 64 columns left it latency-bound on 16
 // CTAs); the threads of one pick write its row's codes contiguously.
 // ---------------------------------------------------------------------------
-__global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ idx,
-                                const int32_t* __restrict__ pair_row, const int32_t* __restrict__ counts,
-                                const int32_t* __restrict__ seg_off, const float* __restrict__ gscale, int T, int K,
-                                int H, int bf16_mode, uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
-                                uint16_t* __restrict__ a_bf16) {
-    pdl_wait();  // launched dependent on the previous kernel
-    pdl_trigger();
-    const int gq = H / 16;
-    const int64_t item = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-    if (item >= static_cast<int64_t>(T) * K * gq) return;
-    const int64_t pair = item / gq;
-    const int g = static_cast<int>(item - pair * gq);
-    const int t = static_cast<int>(pair / K);
-    const int row = pair_row[pair];
+// One dispatch item: elements [16 g, 16 g + 16) of token t's row, pick to
+// permuted row `row` of expert e whose segment holds `count` rows from `base`.
+__device__ __forceinline__ void dispatch_item(const uint16_t* __restrict__ x, int t, int g, int row, int e, int count,
+                                              int base, const float* __restrict__ gscale, int H, int bf16_mode,
+                                              uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
+                                              uint16_t* __restrict__ a_bf16) {
     const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * H + g * 16);
     const uint4 r0 = __ldg(src), r1 = __ldg(src + 1);
     if (bf16_mode) {
@@ -1106,7 +1074,6 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
         dst[1] = r1;
         return;
     }
-    const int e = idx[pair];
     const uint32_t u[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
     float v[16];
 #pragma unroll
@@ -1121,9 +1088,79 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
     // quadrants 0-3), so its rows' scales go to all four quadrant columns of
     // the atom (bytes 4 apart).
     uint8_t* sfp = a_sf + sf_atom_offset(row, g, H / 16);
-    const int rank = row - seg_off[e];
-    const int copies = counts[e] - (rank & ~127) <= 32 ? 4 : 1;
+    const int copies = count - ((row - base) & ~127) <= 32 ? 4 : 1;
     for (int k = 0; k < copies; ++k) sfp[4 * k] = static_cast<uint8_t>(sf);
+}
+
+__global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ idx,
+                                const int32_t* __restrict__ pair_row, const int32_t* __restrict__ counts,
+                                const int32_t* __restrict__ seg_off, const float* __restrict__ gscale, int T, int K,
+                                int H, int bf16_mode, uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
+                                uint16_t* __restrict__ a_bf16) {
+    pdl_wait();  // launched dependent on the previous kernel
+    pdl_trigger();
+    const int gq = H / 16;
+    const int64_t item = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (item >= static_cast<int64_t>(T) * K * gq) return;
+    const int64_t pair = item / gq;
+    const int g = static_cast<int>(item - pair * gq);
+    const int e = bf16_mode ? 0 : idx[pair];
+    dispatch_item(x, static_cast<int>(pair / K), g, pair_row[pair], e, bf16_mode ? 0 : counts[e],
+                  bf16_mode ? 0 : seg_off[e], gscale, H, bf16_mode, a_codes, a_sf, a_bf16);
+}
+
+// Permutation and dispatch of a small batch (T * K <= kSmallPairs) in one
+// launch: every CTA rebuilds the permutation in shared memory from idx (a
+// few hundred picks: cheaper than a kernel boundary), writes its share of the
+// permutation's global outputs (segment_outputs over the grid, pair rows by
+// pick) and quantises its share of the dispatch items.
+__global__ void __launch_bounds__(256) permute_dispatch_kernel(
+    const int32_t* __restrict__ idx, const uint16_t* __restrict__ x, int T, int K, int E, int H, int nb_gu, int nb_down,
+    const float* __restrict__ gscale, int bf16_mode, int32_t* __restrict__ counts, int32_t* __restrict__ seg_off,
+    int32_t* __restrict__ pair_row, int32_t* __restrict__ row_token, NfTile* __restrict__ tiles_gu,
+    NfTile* __restrict__ tiles_down, int32_t* __restrict__ meta, int32_t* __restrict__ mt_done,
+    uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf, uint16_t* __restrict__ a_bf16) {
+    pdl_wait();  // launched dependent on the previous kernel
+    pdl_trigger();
+    extern __shared__ int32_t sh[];
+    const int n = T * K, words = (T + 31) / 32;
+    int32_t* s_cnt = sh;
+    int32_t* s_off = s_cnt + E;
+    int32_t* s_mt = s_off + E + 1;
+    int32_t* s_idx = s_mt + E + 1;   // [n]
+    int32_t* s_row = s_idx + n;      // [n] permuted row of each pick
+    uint32_t* s_mask = reinterpret_cast<uint32_t*>(s_row + n);  // [E][words]: tokens that picked e
+    for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+    for (int i = threadIdx.x; i < E * words; i += blockDim.x) s_mask[i] = 0u;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s_idx[i] = idx[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = s_idx[i], t = i / K;
+        atomicAdd(&s_cnt[e], 1);
+        atomicOr(&s_mask[e * words + (t >> 5)], 1u << (t & 31));
+    }
+    __syncthreads();
+    segment_scan(s_cnt, s_off, s_mt, E);
+    // the rank of pick (t, e) in expert e's segment: e's tokens below t
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = s_idx[i], t = i / K;
+        const uint32_t* m = s_mask + e * words;
+        int rank = __popc(m[t >> 5] & ((1u << (t & 31)) - 1u));
+        for (int wd = 0; wd < (t >> 5); ++wd) rank += __popc(m[wd]);
+        s_row[i] = s_off[e] + rank;
+    }
+    __syncthreads();
+    segment_outputs(s_cnt, s_off, s_mt, E, nb_gu, nb_down, blockIdx.x, gridDim.x, counts, seg_off, row_token, tiles_gu,
+                    tiles_down, meta, mt_done);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        pair_row[i] = s_row[i];
+        row_token[s_row[i]] = i / K;
+    }
+    const int gq = H / 16;
+    for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < n * gq; item += gridDim.x * blockDim.x) {
+        const int pair = item / gq, g = item - pair * gq, e = s_idx[pair];
+        dispatch_item(x, pair / K, g, s_row[pair], e, s_cnt[e], s_off[e], gscale, H, bf16_mode, a_codes, a_sf, a_bf16);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1323,15 +1360,17 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* w_c
 }
 
 cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
-                           const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st) {
-    const size_t small_smem = (3 * E + 2 + T * K + static_cast<size_t>(E) * ((T + 31) / 32)) * sizeof(int32_t);
+                           const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st, bool* one_kernel) {
+    const size_t small_smem = (3 * E + 2 + 2 * T * K + static_cast<size_t>(E) * ((T + 31) / 32)) * sizeof(int32_t);
     if (T * K <= kSmallPairs && small_smem <= 48 * 1024) {
-        const size_t smem = small_smem;
-        cudaError_t e = launch_dependent(permute_small_kernel, dim3(1), dim3(1024), smem, st, idx, T, K, E, nb_gu,
-                                         nb_down, b.counts, b.seg_off, b.pair_row, b.row_token, b.tiles_gu,
-                                         b.tiles_down, b.meta, b.mt_done);
-        if (e != cudaSuccess) return e;
+        const int64_t items = static_cast<int64_t>(T) * K * (H / 16);
+        const int blocks = static_cast<int>(std::min<int64_t>(256, (items + 255) / 256));
+        *one_kernel = true;
+        return launch_dependent(permute_dispatch_kernel, dim3(blocks), dim3(256), small_smem, st, idx, x, T, K, E, H,
+                                nb_gu, nb_down, gscale, bf16_mode, b.counts, b.seg_off, b.pair_row, b.row_token,
+                                b.tiles_gu, b.tiles_down, b.meta, b.mt_done, b.a_codes, b.a_sf, b.a_bf16);
     } else {
+        *one_kernel = false;
         const int nchunks = (T + kChunkTok - 1) / kChunkTok;
         cudaError_t e = launch_dependent(permute_hist_kernel, dim3(nchunks), dim3(256), E * sizeof(int32_t), st, idx, T,
                                          K, E, b.chunk_counts);

@@ -645,6 +645,7 @@ int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cud
     sg.out = h->sh_h;
     sg.out_ld = Is;
     sg.tile_counter = h->shared_counters;
+    sg.early_claim = 1;  // dense tiles; the counters were zeroed before the first GEMM
     // Few tiles at decode sizes: a grid of one CTA per tile leaves the other
     // SMs to the routed path (the down GEMM's CTAs launch early and hold
     // their SMs while gate/up finishes: few CTAs hold few SMs).
@@ -679,7 +680,8 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
     cudaError_t e = cudaSuccess;
     rec.begin(NF_STAGE_PERMUTE, s);
-    e = launch_permute(idx, x, T, K, E, H, I / 128, H / 256, h->gs_g, fp4 ? 0 : 1, h->pb, s);
+    bool one_kernel = false;
+    e = launch_permute(idx, x, T, K, E, H, I / 128, H / 256, h->gs_g, fp4 ? 0 : 1, h->pb, s, &one_kernel);
     if (e != cudaSuccess) return h->cuda_fail(e, "permute launch");
     rec.end(NF_STAGE_PERMUTE, s);
     rec.begin(NF_STAGE_GATE_UP, s);
@@ -715,6 +717,7 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     const bool handoff = rec.ev == nullptr;
     g.mt_done = h->pb.mt_done;
     g.mt_signal = handoff ? 1 : 0;
+    g.early_claim = one_kernel ? 0 : 1;  // the tile list is written by the kernel right before
     e = launch_gemm(h->tm_a, h->tm_a_s, h->tm_b_gu, g, h->grid, true, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "gate/up GEMM launch");
     rec.end(NF_STAGE_GATE_UP, s);
@@ -736,6 +739,7 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.tile_counter = h->pb.meta + 5;
     g.mt_signal = 0;
     g.mt_wait = handoff ? I / 128 : 0;
+    g.early_claim = 1;
     e = launch_gemm(h->tm_h, h->tm_h_s, h->tm_b_dn, g, h->grid, true, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "down GEMM launch");
     rec.end(NF_STAGE_DOWN, s);
