@@ -320,6 +320,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         }
     if world == 1 and not args.no_prefill:
         line["prefill"] = run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src)
+        line["dense"] = run_dense(args, m, torch, hbm_peak, fp4_peak, peak_src)
     if not args.no_prefill:
         ep3 = run_ep_c3(args, m, torch, rank, world, local, dist)
         if rank == 0:
@@ -431,6 +432,67 @@ def run_ep_c3(args, m, torch, rank: int, world: int, local: int, dist) -> dict:
             "rank0_picks_by_owner": [int(c) for c in owners]}
 
 
+def run_dense(args, m, torch, hbm_peak, fp4_peak, peak_src) -> dict:
+    """configs[4]'s dense NVFP4 MLP (layers 0-2: H2048, I10240) at the decode
+    batch (64 tokens; HBM roofline: every weight byte once per step) and at a
+    prefill batch (8192 tokens; FP4 tensor roofline).  Decode steps replay a
+    CUDA graph on a dedicated stream; the 35 MB of weights fit in L2, so each
+    timed decode step is preceded by an L2 flush (a 256 MB write, outside the
+    per-step events)."""
+    cfg = wl.DENSE_CONFIGS["c4_dense"]
+    H, I = cfg["hidden"], cfg["inter"]
+    lay = wl.make_dense_layer(H, I, seed=4)
+    out = {"workload": "c4 dense NVFP4 MLP (layers 0-2): H2048 I10240, swiglu_clamp_bf16 (configs[4])"}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for T in (64, 8192):
+        mlp = m.DenseMlp(H, I, swiglu_limit=lay.swiglu_limit, max_tokens=T)
+        mlp.bind_layer(lay)
+        x = torch.from_numpy(wl.make_tokens(dict(hidden=H, tokens=T), 4).view(np.int16)).cuda()
+        y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+        ts = torch.cuda.Stream()
+        mlp.set_graph_mode(True)
+        for _ in range(args.warmup):
+            mlp.forward(x, y, T, stream=ts.cuda_stream)
+        ts.synchronize()
+        steps = max(3, min(args.steps, 20))
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for e0, e1 in evs:
+            with torch.cuda.stream(ts):
+                flush.fill_(1)
+            e0.record(ts)
+            mlp.forward(x, y, T, stream=ts.cuda_stream)
+            e1.record(ts)
+        ts.synchronize()
+        ms = float(np.mean([e0.elapsed_time(e1) for e0, e1 in evs]))
+        mlp.profile(True)
+        for _ in range(steps):
+            with torch.cuda.stream(ts):
+                flush.fill_(1)
+            mlp.forward(x, y, T, stream=ts.cuda_stream)
+        ts.synchronize()
+        stages, nfw = mlp.stage_times()
+        mlp.profile(False)
+        mlp.sync(ts.cuda_stream)
+        mlp.close()
+        st_us = {k: 1e3 * v / max(nfw, 1) for k in ("permute", "gate_up", "down", "combine") for v in [stages[k]]}
+        if T == 64:
+            nbytes = lay.weight_bytes() + T * H * 2 + T * H * 4
+            gb = nbytes / (ms * 1e-3) / 1e9
+            out["decode"] = {"tokens": T, "us_per_layer": 1e3 * ms, "tokens_per_s": T / (ms * 1e-3),
+                             "stages_us": st_us, "algorithmic_bytes": nbytes, "achieved_gbs": gb,
+                             "hbm_frac": gb / hbm_peak, "peak_source": peak_src}
+        else:
+            flops = T * 3 * 2 * H * I
+            tf = flops / (ms * 1e-3) / 1e12
+            gu_tf = T * 2 * H * 2 * I / (st_us["gate_up"] * 1e-6) / 1e12
+            out["prefill"] = {"tokens": T, "us_per_layer": 1e3 * ms, "tokens_per_s": T / (ms * 1e-3),
+                              "stages_us": st_us, "fp4_tflops": tf, "fp4_frac": tf / fp4_peak,
+                              "gate_up_fp4_frac": gu_tf / fp4_peak,
+                              "peak_source": f"4 x {peak_src} dense BF16"}
+    del flush
+    return out
+
+
 def run_decode_only(args, m, torch) -> dict:
     """The decode batch alone: warm-up, `steps` timed forwards, stage times."""
     lay, x_bits = wl.config_layer("c1")
@@ -467,7 +529,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true", help="skip the secondary prefill measurement")
-    ap.add_argument("--only", choices=["decode", "prefill"],
+    ap.add_argument("--only", choices=["decode", "prefill", "dense"],
                     help="time one workload alone (no e2e, CPU baseline or clock sampling); for profilers")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -479,6 +541,9 @@ def main():
         torch.cuda.set_device(local)
         if args.only == "decode":
             out = run_decode_only(args, m, torch)
+        elif args.only == "dense":
+            hbm_peak, bf16_peak, peak_src = peaks()
+            out = run_dense(args, m, torch, hbm_peak, 4 * bf16_peak, peak_src)
         else:
             _, bf16_peak, peak_src = peaks()
             out = run_prefill(args, m, torch, 4 * bf16_peak, bf16_peak, peak_src)

@@ -227,6 +227,26 @@ NF_API int nf_sigmoid_ref(const float* x_dev, int64_t n, float* y_dev, void* str
  * counts (all 0 on a correct build).  Synchronous. */
 NF_API int nf_format_selfcheck(int64_t* e2m1_mismatches, int64_t* e4m3_mismatches, int64_t* bf16_mismatches);
 
+/* ---- dense NVFP4 MLP (layers 0-2) ------------------------------------------
+ * Creates a handle for the dense feed-forward of the first layers,
+ * TextModel::dense_mlp (src/text_forward.cpp:909-915), selected by feed()
+ * for FfnKind::kDense (src/text_forward.cpp:903): NVFP4 gate and up linears
+ * (linear_nvfp4 :832-856, outputs rounded to BF16), swiglu_clamp_bf16
+ * (:99-106: BF16 after the clamps, after SiLU and after the product), NVFP4
+ * down linear.  Limits: hidden % 256 == 0, inter % 128 == 0.
+ * The handle is an nf_moe handle with one expert and no router:
+ *   - bind with nf_moe_bind_nvfp4(handle, 0, NF_PROJ_GATE / UP / DOWN, ...)
+ *     the checkpoint's mlp.gate_proj / up_proj / down_proj tensors
+ *     (parameter_schema's dense layers, src/parameter_schema.cpp:187-191);
+ *     gate is [inter, hidden], down [hidden, inter]; messages name
+ *     "mlp.<proj>";
+ *   - nf_moe_finalize, nf_moe_forward / nf_moe_forward_host (topk pointers
+ *     must be NULL), nf_moe_set_graph_mode, nf_moe_profile and
+ *     nf_moe_destroy work as for a MoE layer; y = down + residual (or down
+ *     alone when residual is NULL), the hc = 1 form of mhc_combine (:906). */
+NF_API int nf_moe_create_dense(int32_t hidden, int32_t inter, float swiglu_limit, int32_t max_tokens, int device,
+                               nf_moe** out);
+
 /* ---- expert parallelism ----------------------------------------------------
  * The layer sharded by experts over `world` GPUs of one node (1 <= world <= 8,
  * experts % world == 0), one handle per rank and GPU; the reference runs one

@@ -57,13 +57,27 @@ constexpr int SMEM_BYTES = 1024 + SMEM_TILES + 512;
 
 struct TileInfo {
     int expert, row0, n_block, m_valid;
+    int ks, kt0, kt1;  // K slice and its stages [kt0, kt1)
 };
 
-__device__ __forceinline__ TileInfo get_tile(const GemmArgs& a, int i) {
+// Dense tiles are numbered (n block, K slice, m tile) with m fastest.
+__device__ __forceinline__ void dense_split(const GemmArgs& a, int i, int k_tiles, int* m, int* n, int* ks, int* kt0,
+                                            int* kt1) {
+    const int m_tiles = (a.dense_rows + BM - 1) / BM;
+    const int per_n = m_tiles * max(1, a.k_split);
+    *n = i / per_n;
+    const int r = i - *n * per_n;
+    *ks = r / m_tiles;
+    *m = r - *ks * m_tiles;
+    *kt0 = a.k_split > 1 ? *ks * a.kt_per : 0;
+    *kt1 = a.k_split > 1 ? min(k_tiles, *kt0 + a.kt_per) : k_tiles;
+}
+
+__device__ __forceinline__ TileInfo get_tile(const GemmArgs& a, int i, int k_tiles) {
     TileInfo t;
     if (a.dense_rows > 0) {
-        const int m_tiles = (a.dense_rows + BM - 1) / BM;
-        const int n = i / m_tiles, m = i % m_tiles;
+        int m, n;
+        dense_split(a, i, k_tiles, &m, &n, &t.ks, &t.kt0, &t.kt1);
         t.expert = 0;
         t.row0 = m * BM;
         t.n_block = n;
@@ -74,8 +88,22 @@ __device__ __forceinline__ TileInfo get_tile(const GemmArgs& a, int i) {
         t.row0 = x.row0;
         t.n_block = x.n_block;
         t.m_valid = x.m_valid;
+        t.ks = 0;
+        t.kt0 = 0;
+        t.kt1 = k_tiles;
     }
     return t;
+}
+
+// The K stages of tile i, without reading the tile list (grouped tiles run all of K).
+__device__ __forceinline__ void tile_krange(const GemmArgs& a, int i, int k_tiles, int* kt0, int* kt1) {
+    if (a.dense_rows > 0 && a.k_split > 1) {
+        int m, n, ks;
+        dense_split(a, i, k_tiles, &m, &n, &ks, kt0, kt1);
+    } else {
+        *kt0 = 0;
+        *kt1 = k_tiles;
+    }
 }
 
 // swiglu_clamp element (src/text_forward.cpp:1439-1445): min(g, L) into SiLU,
@@ -88,6 +116,17 @@ __device__ __forceinline__ float swiglu_fast(float g, float u, float L) {
     const float lo = (-L < u) ? u : -L;
     const float cu = (lo < L) ? lo : L;
     return __fmul_rn(__fdividef(cg, 1.f + __expf(-cg)), cu);
+}
+
+// swiglu_clamp_bf16 element (src/text_forward.cpp:99-106), the dense layers'
+// form: the capped gate, the clamped up, SiLU of the capped gate and the
+// product are each rounded to BF16 (the same clamps and SiLU as swiglu_fast).
+__device__ __forceinline__ float swiglu_bf16_fast(float g, float u, float L) {
+    const float cg = bf16_round_hw((L < g) ? L : g);
+    const float lo = (-L < u) ? u : -L;
+    const float cu = bf16_round_hw((lo < L) ? lo : L);
+    const float act = bf16_round_hw(__fdividef(cg, 1.f + __expf(-cg)));
+    return bf16_round_hw(__fmul_rn(act, cu));
 }
 
 // Bounded wait, by every lane of the calling warp, until *counter >= target
@@ -190,10 +229,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         int next = 0, num_tiles = 0;
         TileInfo next_t{};
         auto claim_first = [&]() {
-            num_tiles = args.dense_rows > 0 ? ((args.dense_rows + BM - 1) / BM) * args.n_blocks : *args.num_tiles_dev;
+            num_tiles = args.dense_rows > 0 ? ((args.dense_rows + BM - 1) / BM) * args.n_blocks * max(1, args.k_split)
+                                            : *args.num_tiles_dev;
             if (lane == 0) {
                 next = atomicAdd(args.tile_counter, 1);
-                if (next < num_tiles) next_t = get_tile(args, next);
+                if (next < num_tiles) next_t = get_tile(args, next, k_tiles);
             }
         };
         if (args.early_claim) claim_first();
@@ -215,21 +255,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int first = __shfl_sync(0xffffffffu, next, 0);
             const int e0 = __shfl_sync(0xffffffffu, next_t.expert, 0);
             const int nb0 = __shfl_sync(0xffffffffu, next_t.n_block, 0);
+            const int k00 = __shfl_sync(0xffffffffu, next_t.kt0, 0);
+            const int k01 = __shfl_sync(0xffffffffu, next_t.kt1, 0);
             if (first < num_tiles) {
-                pre = min(STAGES, k_tiles);
-                for (int kt = 0; kt < pre; ++kt) {
+                // stage j holds K stage k00 + j of the first tile
+                pre = min(STAGES, k01 - k00);
+                for (int j = 0; j < pre; ++j) {
+                    const int kt = k00 + j;
                     if (lane == 0)
-                        mbar_arrive_expect_tx(&full[kt], stage_bytes(min(4, (K - kt * kElemsPerStage) / kMmaK)));
+                        mbar_arrive_expect_tx(&full[j], stage_bytes(min(4, (K - kt * kElemsPerStage) / kMmaK)));
                     __syncwarp();
                     const int blk = (e0 * args.b_nb + nb0) * args.b_kt + kt;
                     if (lane == 1) {
-                        tma_load_2d_hint(sB + kt * B_STAGE_BYTES, &tmb, &full[kt], 0, blk * BN, stream_policy);
+                        tma_load_2d_hint(sB + j * B_STAGE_BYTES, &tmb, &full[j], 0, blk * BN, stream_policy);
                     } else if (KIND == KIND_NVFP4 && lane == 3) {
-                        bulk_load_hint(sSFB + kt * SFB_STAGE_BYTES,
+                        bulk_load_hint(sSFB + j * SFB_STAGE_BYTES,
                                        args.sfb + static_cast<int64_t>(blk) * SFB_STAGE_BYTES, SFB_STAGE_BYTES,
-                                       &full[kt], stream_policy);
+                                       &full[j], stream_policy);
                     }
-                    issued[kt] = true;
+                    issued[j] = true;
                 }
             }
         }
@@ -263,6 +307,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             t.row0 = __shfl_sync(0xffffffffu, t.row0, 0);
             t.n_block = __shfl_sync(0xffffffffu, t.n_block, 0);
             t.m_valid = __shfl_sync(0xffffffffu, t.m_valid, 0);
+            t.kt0 = __shfl_sync(0xffffffffu, t.kt0, 0);
+            t.kt1 = __shfl_sync(0xffffffffu, t.kt1, 0);
             // tiles with at most 32 rows of the expert load only those rows of A (four times)
             const bool small_a = t.m_valid <= kSmallRows;
             if (args.mt_wait > 0) {
@@ -276,10 +322,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 fence_proxy_async_global();
             }
-            for (int kt = 0; kt < k_tiles; ++kt) {
+            for (int kt = t.kt0; kt < t.kt1; ++kt) {
                 const int k0 = kt * kElemsPerStage;
                 const int steps = min(4, (K - k0) / kMmaK);
-                const bool b_issued = first_tile && kt < pre;  // B of this stage went out before pdl_wait()
+                const bool b_issued = first_tile && kt - t.kt0 < pre;  // B of this stage went out before pdl_wait()
                 if (lane == 0 && !b_issued) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, cta_abort, dev_err)) {
                         set_abort(cta_abort, args.err, NF_DEVERR_WAIT_EMPTY);
@@ -310,8 +356,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 issued[stage] = true;
                 issued_parity[stage] = phase;
                 if (++stage == STAGES) stage = 0, phase ^= 1u;
-                if (lane == 0 && kt == max(0, k_tiles - 3)) next = atomicAdd(args.tile_counter, 1);
-                if (lane == 0 && kt == k_tiles - 1 && next < num_tiles) next_t = get_tile(args, next);
+                if (lane == 0 && kt == max(t.kt0, t.kt1 - 3)) next = atomicAdd(args.tile_counter, 1);
+                if (lane == 0 && kt == t.kt1 - 1 && next < num_tiles) next_t = get_tile(args, next, k_tiles);
             }
             first_tile = false;
         }
@@ -353,7 +399,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                for (int kt = 0; kt < k_tiles; ++kt) {
+                int kt0, kt1;
+                tile_krange(args, i, k_tiles, &kt0, &kt1);
+                for (int kt = kt0; kt < kt1; ++kt) {
                     if (!mbar_wait(&full[stage], phase, cta_abort, dev_err)) {
                         set_abort(cta_abort, args.err, NF_DEVERR_WAIT_FULL);
                         ok = false;
@@ -374,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int s = 0; s < steps; ++s) {
                         const uint64_t adesc = sdesc_sw128(a_base + 32 * s);
                         const uint64_t bdesc = sdesc_sw128(b_base + 32 * s);
-                        const uint32_t acc = (kt > 0 || s > 0) ? 1u : 0u;
+                        const uint32_t acc = (kt > kt0 || s > 0) ? 1u : 0u;
                         if (KIND == KIND_NVFP4)
                             mma_nvfp4(tmem, adesc, bdesc, idesc, tmem + sfa_col + 4 * s, tmem + sfb_col + 8 * s, acc);
                         else
@@ -434,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int ok = epi_mail[2 * (iter & 1) + 1];
             if (++qslot == kTileQ) qslot = 0, qphase ^= 1u;
             if (!ok || tile < 0) break;
-            const TileInfo t = get_tile(args, tile);
+            const TileInfo t = get_tile(args, tile, k_tiles);
             tc_fence_after();
             // A tile of at most 32 rows holds them in every TMEM lane quadrant (A was
             // loaded four times), so for the NVFP4 epilogues all sixteen warps take a
@@ -465,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld16(tbase + 128 + 32 * cs + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
                 } else if (EPI == EPI_STORE_F32) {
                     // no math: stream 16 columns at a time straight to memory
-                    uint4* d = reinterpret_cast<uint4*>(static_cast<float*>(args.out) +
+                    uint4* d = reinterpret_cast<uint4*>(static_cast<float*>(args.out) + t.ks * args.out_split_stride +
                                                         static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + 64 * cs);
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
@@ -492,6 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (EPI == EPI_SWIGLU_QUANT) {
                 const float ag = args.alpha0[t.expert], au = args.alpha1[t.expert];
                 const float gsd = args.gscale_next[t.expert], L = args.limit;
+                const bool sbf = args.swiglu_bf16 != 0;
                 uint32_t cc[2][2];
                 uint32_t sc[2];
                 const int ng = rep ? 1 : 2;
@@ -506,8 +555,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                       __fmul_rn(__uint_as_float(v[16 * g + j + 1]), ag));
                         const uint32_t u2 = bf16x2_hw(__fmul_rn(__uint_as_float(v[32 + 16 * g + j]), au),
                                                       __fmul_rn(__uint_as_float(v[32 + 16 * g + j + 1]), au));
-                        h[j] = swiglu_fast(__uint_as_float(g2 << 16), __uint_as_float(u2 << 16), L);
-                        h[j + 1] = swiglu_fast(__uint_as_float(g2 & 0xffff0000u), __uint_as_float(u2 & 0xffff0000u), L);
+                        const float g0 = __uint_as_float(g2 << 16), g1 = __uint_as_float(g2 & 0xffff0000u);
+                        const float u0 = __uint_as_float(u2 << 16), u1 = __uint_as_float(u2 & 0xffff0000u);
+                        h[j] = sbf ? swiglu_bf16_fast(g0, u0, L) : swiglu_fast(g0, u0, L);
+                        h[j + 1] = sbf ? swiglu_bf16_fast(g1, u1, L) : swiglu_fast(g1, u1, L);
                     }
                     sc[g] = quantize_group16_fast<false>(h, gsd, cc[g]);
                 }
@@ -564,7 +615,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 4; ++j) d[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
                 }
-            }  // EPI_STORE_F32 stored while reading the accumulator
+            } else if (EPI == EPI_STORE_F32 && rep) {
+                // (tiles of at most 32 rows; larger tiles stored while reading the accumulator)
+                if (valid) {
+                    uint4* d = reinterpret_cast<uint4*>(static_cast<float*>(args.out) + t.ks * args.out_split_stride +
+                                                        static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + rc);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) d[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                }
+            }
             }
             if (EPI == EPI_SWIGLU_QUANT || EPI == EPI_SWIGLU_BF16) {
                 if (args.mt_signal) {
@@ -601,7 +660,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(&tq_empty[qslot]);
             if (++qslot == kTileQ) qslot = 0, qphase ^= 1u;
             if (i < 0) break;
-            for (int kt = 0; kt < k_tiles; ++kt) {
+            int kt0, kt1;
+            tile_krange(args, i, k_tiles, &kt0, &kt1);
+            for (int kt = kt0; kt < kt1; ++kt) {
                 if (!mbar_wait(&full[stage], phase, cta_abort, dev_err)) {
                     set_abort(cta_abort, args.err, NF_DEVERR_WAIT_FULL);
                     ok = false;
@@ -721,6 +782,7 @@ cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, co
     if (args.kind == KIND_NVFP4) {
         if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT>(tma, tma_small, tmb, args, grid, dependent, st);
         if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16>(tma, tma_small, tmb, args, grid, dependent, st);
+        if (args.epi == EPI_STORE_F32) return launch_one<KIND_NVFP4, EPI_STORE_F32>(tma, tma_small, tmb, args, grid, dependent, st);
     } else {
         if (args.epi == EPI_SWIGLU_BF16) return launch_one<KIND_BF16, EPI_SWIGLU_BF16>(tma, tma_small, tmb, args, grid, dependent, st);
         if (args.epi == EPI_STORE_F32) return launch_one<KIND_BF16, EPI_STORE_F32>(tma, tma_small, tmb, args, grid, dependent, st);

@@ -80,6 +80,13 @@ struct nf_moe {
     // experts-only handle over this rank's experts
     bool ep_outer = false;
     bool experts_only = false;
+    // dense MLP (nf_moe_create_dense): an experts-only handle with one expert
+    // that every token takes with weight 1, and the swiglu_clamp_bf16 epilogue
+    bool dense = false;
+    int32_t* dense_idx = nullptr;    // [Tm] zeros: every token's pick is expert 0
+    float* dense_w = nullptr;        // [Tm] ones: the pick's combine weight
+    float* dense_part = nullptr;     // split-K partial sums of the down projection (small batches)
+    int64_t dense_part_elems = 0;
     int ep_rank = 0, ep_world = 1, ep_base = 0, ep_local = 0;
     nf_moe* inner = nullptr;
     void* nccl = nullptr;            // ncclComm_t of the group
@@ -179,9 +186,9 @@ struct nf_moe {
     }
 };
 
-// Handle roles: a full layer, the experts-only engine of an EP rank, or the
-// outer handle of an EP rank.
-enum HandleRole { kRoleFull = 0, kRoleExperts = 1, kRoleEpOuter = 2 };
+// Handle roles: a full layer, the experts-only engine of an EP rank, the
+// outer handle of an EP rank, or a dense MLP.
+enum HandleRole { kRoleFull = 0, kRoleExperts = 1, kRoleEpOuter = 2, kRoleDense = 3 };
 
 // Stage timing of one forward (events recorded when profiling is on).
 struct StageRec {
@@ -203,8 +210,10 @@ int validate_desc(const nf_moe_desc& d, std::string* err);
 std::string& create_error();
 int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::string* err);
 int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cudaStream_t s);
+// down_split > 1 (dense handles): the down GEMM runs as a dense split-K GEMM
+// into h->dense_part (down_split K slices) instead of writing h->down.
 int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int T, int K, StageRec& rec,
-                          cudaStream_t s);
+                          cudaStream_t s, int down_split = 1);
 // nf_ep.cu
 int ep_forward(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx, float* w,
                cudaStream_t s);

@@ -58,6 +58,13 @@ struct GemmArgs {
     const int32_t* num_tiles_dev;
     int dense_rows;      // > 0: dense GEMM over this many A rows
     int n_blocks;        // 256-wide output blocks
+    // Split K (dense GEMMs only): every (m, n) output tile is computed as
+    // k_split partial sums over slices of kt_per K stages; slice s stores its
+    // raw fp32 accumulator (EPI_STORE_F32) at out + s * out_split_stride, and
+    // a reduction kernel sums the slices.  k_split = 1: no split.
+    int k_split;
+    int kt_per;
+    int64_t out_split_stride;  // elements
     // NVFP4 scale-factor atoms: sfa [128-row block][K/64 atoms]; sfb in tile
     // order, one 4 KB group per (expert, n block, K stage): [2 row halves][4 atoms]
     const uint8_t* sfa;
@@ -67,6 +74,8 @@ struct GemmArgs {
     const float* alpha1;       // [E] up alpha (SwiGLU)
     const float* gscale_next;  // [E] 1 / input_scale of the down projection
     float limit;               // swiglu_limit
+    int swiglu_bf16;           // EPI_SWIGLU_QUANT: swiglu_clamp_bf16 (dense layers: BF16 after the clamps,
+                               // SiLU and product) instead of swiglu_clamp
     const int32_t* row_token;  // permuted row -> token (-1 = padding), NULL for dense
     void* out;                 // output rows
     int64_t out_ld;            // output row stride in elements of the output type
@@ -170,6 +179,10 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
 cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair_row, const float* topk_w,
                            const float* shared, const float* residual, int T, int K, int H, float* y,
                            cudaStream_t st);
+// y [T, H] = bf16(alpha[0] * sum of S fp32 slices part + s * stride) (+ residual):
+// the split-K form of a dense down projection and its residual.
+cudaError_t launch_splitk_store(const float* part, int S, int64_t stride, int T, int H, const float* alpha,
+                                const float* residual, float* y, int grid_cap, cudaStream_t st);
 // Expert parallelism (up to kEpMaxRanks ranks): the (destination, token,
 // pick) layout of the picks, and a row gather.
 constexpr int kEpMaxRanks = 8;

@@ -1409,6 +1409,50 @@ cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair
 }
 
 // ---------------------------------------------------------------------------
+// Split-K reduction of a dense down projection: linear_nvfp4's output
+// (src/text_forward.cpp:852-855: accumulator x alpha, rounded to BF16) from
+// the fp32 partial accumulators of S K slices, summed in slice order, then
+// the hc = 1 residual (src/text_forward.cpp:906).  Four columns per thread.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) splitk_store_kernel(const float* __restrict__ part, int S, int64_t stride, int T,
+                                                           int H, const float* __restrict__ alpha,
+                                                           const float* __restrict__ residual, float* __restrict__ y) {
+    pdl_wait();  // launched dependent on the GEMM that writes the slices
+    pdl_trigger();
+    const int64_t n4 = static_cast<int64_t>(T) * H / 4;
+    const float a = alpha[0];
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float4 acc = reinterpret_cast<const float4*>(part)[i];
+        for (int s = 1; s < S; ++s) {
+            const float4 v = reinterpret_cast<const float4*>(part + s * stride)[i];
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        float4 o = make_float4(bf16_round_hw(__fmul_rn(acc.x, a)), bf16_round_hw(__fmul_rn(acc.y, a)),
+                               bf16_round_hw(__fmul_rn(acc.z, a)), bf16_round_hw(__fmul_rn(acc.w, a)));
+        if (residual) {
+            const float4 r = reinterpret_cast<const float4*>(residual)[i];
+            o.x = __fadd_rn(o.x, r.x);
+            o.y = __fadd_rn(o.y, r.y);
+            o.z = __fadd_rn(o.z, r.z);
+            o.w = __fadd_rn(o.w, r.w);
+        }
+        reinterpret_cast<float4*>(y)[i] = o;
+    }
+}
+
+cudaError_t launch_splitk_store(const float* part, int S, int64_t stride, int T, int H, const float* alpha,
+                                const float* residual, float* y, int grid_cap, cudaStream_t st) {
+    const int64_t n4 = static_cast<int64_t>(T) * H / 4;
+    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid_cap, (n4 + 255) / 256)));
+    return launch_dependent(splitk_store_kernel, dim3(blocks), dim3(256), 0, st, part, S, stride, T, H, alpha, residual,
+                            y);
+}
+
+// ---------------------------------------------------------------------------
 // Expert parallelism.  Pick (t, p) goes to rank d = idx[t, p] / e_per_rank.
 // ep_pack lays the picks out in (destination, token, pick) order -- the
 // order the exchange sends them in, fully deterministic -- and writes, per

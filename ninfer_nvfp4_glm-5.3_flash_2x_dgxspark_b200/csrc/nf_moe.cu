@@ -6,6 +6,7 @@
 
 #include "nf_common.cuh"
 
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 #include <cstdarg>
@@ -85,6 +86,27 @@ void atoms_to_tiles(const std::vector<uint8_t>& atoms, int64_t rowblocks, int64_
 }
 
 const char* proj_name(int proj) { return proj == NF_PROJ_GATE ? "gate_proj" : proj == NF_PROJ_UP ? "up_proj" : "down_proj"; }
+
+// Checkpoint name of a projection in messages: mlp.experts.<e>.<proj> for a
+// routed expert, mlp.<proj> for the dense MLP (src/parameter_schema.cpp:187-191).
+// K slices of a dense down projection over T tokens: when its (m, n) tiles
+// would occupy fewer than half the SMs (small batches), K is split so that
+// the slices fill the grid, at least 2 stages of 256 K-elements per slice
+// and no empty slice.  Returns 1 for no split; *kt_per gets the stages per slice.
+int dense_down_split(int T, int H, int I, int grid, int* kt_per) {
+    const int m_tiles = (T + 127) / 128, n_blocks = H / 256, k_tiles = (I + 255) / 256;
+    const int base = m_tiles * n_blocks;
+    *kt_per = k_tiles;
+    if (2 * base > grid || k_tiles < 4) return 1;
+    const int want = std::max(1, grid / base);
+    *kt_per = std::max(2, (k_tiles + want - 1) / want);
+    return (k_tiles + *kt_per - 1) / *kt_per;
+}
+
+std::string proj_label(const nf_moe* h, long long expert, int proj) {
+    if (h->dense) return std::string("mlp.") + proj_name(proj);
+    return "mlp.experts." + std::to_string(expert) + "." + proj_name(proj);
+}
 
 // Weight matrices that the GEMMs stream (their B operands) are stored in
 // "box order": the matrix is cut into blocks of 256 rows x 128 bytes (one
@@ -218,6 +240,36 @@ int nf_moe_create(const nf_moe_desc* desc, int device, nf_moe** out) {
     return create_impl(d, device, kRoleFull, out, &g_create_error);
 }
 
+// TextModel::dense_mlp (src/text_forward.cpp:909-915) as a one-expert,
+// router-less handle: every token takes expert 0 with weight 1, so the
+// permutation is the identity (rows padded to 128), the grouped GEMMs run
+// one segment, and the combine adds 1 * down to the residual exactly.
+int nf_moe_create_dense(int32_t hidden, int32_t inter, float swiglu_limit, int32_t max_tokens, int device,
+                        nf_moe** out) {
+    g_create_error.clear();
+    if (!out) {
+        g_create_error = "null output";
+        return NF_ERR_INVALID;
+    }
+    *out = nullptr;
+    nf_moe_desc d{};
+    d.hidden = hidden;
+    d.experts = 1;
+    d.top_k = 1;
+    d.inter = inter;
+    d.shared_inter = 0;
+    d.n_group = 1;
+    d.topk_group = 1;
+    d.normalize = 1;
+    d.routed_scaling = 1.f;
+    d.swiglu_limit = swiglu_limit;
+    d.expert_kind = NF_EXPERTS_NVFP4;
+    d.max_tokens = max_tokens;
+    const int st = validate_desc(d, &g_create_error);
+    if (st != NF_OK) return st;
+    return create_impl(d, device, kRoleDense, out, &g_create_error);
+}
+
 }  // extern "C"
 
 // Allocates a handle for a validated descriptor.  kRoleExperts (the experts
@@ -250,9 +302,10 @@ int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::s
     h->d = d;
     h->device = device;
     h->grid = gemm_grid_size(device);
-    h->experts_only = role == kRoleExperts;
+    h->experts_only = role == kRoleExperts || role == kRoleDense;
+    h->dense = role == kRoleDense;
     h->ep_outer = role == kRoleEpOuter;
-    const bool routed = role != kRoleEpOuter, router = role != kRoleExperts;
+    const bool routed = role != kRoleEpOuter, router = !h->experts_only;
     const int64_t H = d.hidden, E = d.experts, K = d.top_k, I = d.inter, Is = d.shared_inter, Tm = d.max_tokens;
     const int64_t pairs = Tm * K;
     h->rows_cap = static_cast<int>(round_up(pairs + 127 * E, 128));
@@ -310,6 +363,18 @@ int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::s
     if (Is > 0) ok = ok && h->alloc(&h->sh_h, Tm * Is) && h->alloc(&h->sh_out, Tm * H);
     ok = ok && h->alloc(&h->x_f32, Tm * H) && h->alloc(&h->x_bf16, Tm * H) && h->alloc(&h->res_f32, Tm * H) &&
          h->alloc(&h->y_f32, Tm * H) && h->alloc(&h->dev_err, 1);
+    if (h->dense) {
+        ok = ok && h->alloc(&h->dense_idx, Tm) && h->alloc(&h->dense_w, Tm);
+        // the largest split-K partial buffer over every batch size up to Tm
+        int64_t part = 0;
+        for (int64_t mt = 1; mt <= (Tm + 127) / 128; ++mt) {
+            int kt_per = 0;
+            const int S = dense_down_split(static_cast<int>(mt * 128), static_cast<int>(H), static_cast<int>(I), h->grid, &kt_per);
+            if (S > 1) part = std::max(part, S * mt * 128 * H);
+        }
+        h->dense_part_elems = part;
+        if (part > 0) ok = ok && h->alloc(&h->dense_part, part);
+    }
     if (!ok) {
         cudaGetLastError();
         nf_moe_destroy(h);
@@ -318,6 +383,15 @@ int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::s
     }
     cudaMemset(h->dev_err, 0, sizeof(int));
     if (routed) cudaMemset(b.row_token, 0xff, R * sizeof(int32_t));
+    if (h->dense) {
+        const std::vector<float> ones(static_cast<size_t>(Tm), 1.f);
+        if (cudaMemset(h->dense_idx, 0, Tm * sizeof(int32_t)) != cudaSuccess ||
+            cudaMemcpy(h->dense_w, ones.data(), Tm * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+            nf_moe_destroy(h);
+            cudaSetDevice(prev);
+            return reject(NF_ERR_CUDA, "dense MLP set-up copy failed");
+        }
+    }
     h->bound.assign(static_cast<size_t>(E * 3), 0);
     h->h_alpha_g.assign(E, 0.f);
     h->h_alpha_u.assign(E, 0.f);
@@ -361,11 +435,11 @@ int nf_moe_bind_nvfp4(nf_moe* h, int expert, int proj, const uint8_t* packed, co
         if (expert < h->ep_base || expert >= h->ep_base + h->ep_local) return NF_OK;
         return ep_relay(h, nf_moe_bind_nvfp4(h->inner, expert - h->ep_base, proj, packed, scales, ws2, in_scale, rows, cols));
     }
-    if (!packed || !scales) return h->fail(NF_ERR_LAYOUT, "NVFP4 layout mlp.experts.%d.%s", expert, proj_name(proj));
+    if (!packed || !scales) return h->fail(NF_ERR_LAYOUT, "NVFP4 layout %s", proj_label(h, expert, proj).c_str());
     const int64_t H = d.hidden, I = d.inter;
     const int64_t want_rows = proj == NF_PROJ_DOWN ? H : I, want_cols = proj == NF_PROJ_DOWN ? I : H;
     if (rows != want_rows || cols != want_cols || cols % 16 != 0)
-        return h->fail(NF_ERR_SHAPE, "NVFP4 shape mlp.experts.%d.%s", expert, proj_name(proj));
+        return h->fail(NF_ERR_SHAPE, "NVFP4 shape %s", proj_label(h, expert, proj).c_str());
     if (!(in_scale > 0.f) || !std::isfinite(in_scale)) return h->fail(NF_ERR_SCALE, "NVFP4 input scale");
     if (!std::isfinite(ws2) || ws2 < FLT_MIN)
         return h->fail(NF_ERR_SCALE, "NVFP4 global scale must be finite and at least the minimum normal float");
@@ -427,7 +501,8 @@ int nf_moe_bind_bf16(nf_moe* h, int which, int expert, const uint16_t* data, int
         if (expert < h->ep_base || expert >= h->ep_base + h->ep_local) return NF_OK;
         return ep_relay(h, nf_moe_bind_bf16(h->inner, which, expert - h->ep_base, data, rows, cols));
     }
-    if (!is_expert && h->experts_only) return h->fail(NF_ERR_STATE, "an experts-only handle holds no %s", name);
+    if (!is_expert && h->experts_only)
+        return h->fail(NF_ERR_STATE, "%s handle holds no %s", h->dense ? "a dense MLP" : "an experts-only", name);
     if ((which >= NF_BF16_SHARED_GATE && which <= NF_BF16_SHARED_DOWN) && Is == 0)
         return h->fail(NF_ERR_STATE, "descriptor has no shared expert");
     if (!data || rows != wr || cols != wc) return h->fail(NF_ERR_SHAPE, "BF16 linear layout %s", name);
@@ -496,6 +571,9 @@ int nf_moe_bind_f32(nf_moe* h, int which, const float* data, int64_t n) {
     if (!h) return NF_ERR_INVALID;
     if (h->finalized) return h->fail(NF_ERR_STATE, "weights are already finalized");
     if (which != NF_F32_ROUTER_BIAS) return h->fail(NF_ERR_INVALID, "bad F32 tensor id %d", which);
+    if (h->experts_only)
+        return h->fail(NF_ERR_STATE, "%s handle holds no mlp.gate.e_score_correction_bias",
+                       h->dense ? "a dense MLP" : "an experts-only");
     if (!data || n != h->d.experts) return h->fail(NF_ERR_SHAPE, "vector length mismatch for mlp.gate.e_score_correction_bias");
     int prev = 0;
     cudaGetDevice(&prev);
@@ -531,7 +609,7 @@ int nf_moe_finalize(nf_moe* h) {
         for (int64_t e = 0; e < E; ++e)
             for (int p = 0; p < 3; ++p)
                 if (!h->bound[static_cast<size_t>(e * 3 + p)])
-                    return h->fail(NF_ERR_STATE, "missing tensor mlp.experts.%lld.%s", static_cast<long long>(e), proj_name(p));
+                    return h->fail(NF_ERR_STATE, "missing tensor %s", proj_label(h, e, p).c_str());
     }
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
     std::vector<float> gs_g(E, 1.f), gs_d(E, 1.f);
@@ -539,8 +617,8 @@ int nf_moe_finalize(nf_moe* h) {
         for (int64_t e = 0; e < E; ++e) {
             if (h->h_in_g[e] != h->h_in_u[e])
                 return h->fail(NF_ERR_UNSUPPORTED,
-                               "mlp.experts.%lld gate_proj and up_proj input_scale differ; this build needs one gate/up input scale",
-                               static_cast<long long>(e));
+                               "%s gate_proj and up_proj input_scale differ; this build needs one gate/up input scale",
+                               h->dense ? "mlp" : ("mlp.experts." + std::to_string(e)).c_str());
             gs_g[e] = 1.f / h->h_in_g[e];  // quant_dequant_nvfp4_activation: global_scale = 1 / input_scale
             gs_d[e] = 1.f / h->h_in_d[e];
         }
@@ -599,6 +677,7 @@ static int check_forward_args(nf_moe* h, const void* x, int tokens, bool device_
 int nf_moe_route(nf_moe* h, const uint16_t* x, int tokens, float* logits, int32_t* idx, float* w, void* stream) {
     int st = check_forward_args(h, x, tokens);
     if (st != NF_OK) return st;
+    if (h->experts_only) return h->fail(NF_ERR_STATE, "handle has no router");
     if (tokens == 0) return NF_OK;
     const nf_moe_desc& d = h->d;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -674,7 +753,7 @@ int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cud
 // The down rows land in h->down in permuted order (h->pb.pair_row maps a
 // pick to its row).
 int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int T, int K, StageRec& rec,
-                          cudaStream_t s) {
+                          cudaStream_t s, int down_split) {
     const nf_moe_desc& d = h->d;
     const int H = d.hidden, E = d.experts, I = d.inter;
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
@@ -688,6 +767,7 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     GemmArgs g{};
     g.err = h->dev_err;
     g.limit = d.swiglu_limit;
+    g.swiglu_bf16 = h->dense ? 1 : 0;  // dense_mlp uses swiglu_clamp_bf16 (src/text_forward.cpp:913)
     // gate/up
     g.kind = fp4 ? KIND_NVFP4 : KIND_BF16;
     g.epi = fp4 ? EPI_SWIGLU_QUANT : EPI_SWIGLU_BF16;
@@ -737,18 +817,59 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.out = h->down;
     g.out_ld = H;
     g.tile_counter = h->pb.meta + 5;
+    g.swiglu_bf16 = 0;
     g.mt_signal = 0;
     g.mt_wait = handoff ? I / 128 : 0;
     g.early_claim = 1;
+    if (down_split > 1) {
+        // dense split-K: tiles (n block, K slice, m tile) over the T rows of h
+        // (one segment at row 0), raw fp32 slices into dense_part
+        int kt_per = 0;
+        const int S = dense_down_split(T, H, I, h->grid, &kt_per);
+        const int64_t stride = static_cast<int64_t>((T + 127) / 128) * 128 * H;
+        if (S != down_split || S * stride > h->dense_part_elems) return h->fail(NF_ERR_STATE, "split-K workspace");
+        g.epi = EPI_STORE_F32;
+        g.dense_rows = T;
+        g.tiles = nullptr;
+        g.num_tiles_dev = nullptr;
+        g.k_split = S;
+        g.kt_per = kt_per;
+        g.out = h->dense_part;
+        g.out_ld = H;
+        g.out_split_stride = stride;
+    }
     e = launch_gemm(h->tm_h, h->tm_h_s, h->tm_b_dn, g, h->grid, true, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "down GEMM launch");
     rec.end(NF_STAGE_DOWN, s);
     return NF_OK;
 }
 
+// TextModel::dense_mlp (src/text_forward.cpp:909-915) + the hc = 1 residual:
+// the routed chain with every token on expert 0, then y = 1 * down (+ residual).
+static int dense_forward(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, cudaStream_t s) {
+    h->last_tokens = T;
+    StageRec rec;
+    rec.h = h;
+    rec.ev = h->prof_begin(&rec.set);
+    const int H = h->d.hidden;
+    int kt_per = 0;
+    const int S = dense_down_split(T, H, h->d.inter, h->grid, &kt_per);
+    int st = launch_routed_experts(h, x, h->dense_idx, T, 1, rec, s, S);
+    if (st != NF_OK) return st;
+    rec.begin(NF_STAGE_COMBINE, s);
+    const cudaError_t e =
+        S > 1 ? launch_splitk_store(h->dense_part, S, static_cast<int64_t>((T + 127) / 128) * 128 * H, T, H, h->alpha_d,
+                                    residual, y, 4 * h->grid, s)
+              : launch_combine(h->down, true, h->pb.pair_row, h->dense_w, nullptr, residual, T, 1, H, y, s);
+    if (e != cudaSuccess) return h->cuda_fail(e, "combine launch");
+    rec.end(NF_STAGE_COMBINE, s);
+    return NF_OK;
+}
+
 static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx_user,
                         float* w_user, cudaStream_t s) {
     if (h->ep_outer) return ep_forward(h, x, residual, T, y, idx_user, w_user, s);
+    if (h->dense) return dense_forward(h, x, residual, T, y, s);
     const nf_moe_desc& d = h->d;
     const int H = d.hidden, E = d.experts, K = d.top_k, Is = d.shared_inter;
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
@@ -855,6 +976,7 @@ int nf_moe_forward(nf_moe* h, const uint16_t* x, const float* residual, int toke
     if (!y) return h->fail(NF_ERR_INVALID, "null output");
     if ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(residual)) % 16 != 0)
         return h->fail(NF_ERR_LAYOUT, "y and residual must be 16-byte aligned");
+    if (h->dense && (idx || w)) return h->fail(NF_ERR_INVALID, "a dense MLP has no routes: pass NULL top-k pointers");
     if (tokens == 0 && !h->ep_outer) return NF_OK;  // an EP rank still takes part in the exchanges
     int prev = 0;
     cudaGetDevice(&prev);
@@ -901,6 +1023,7 @@ int nf_moe_forward_host(nf_moe* h, const float* x_host, const float* res_host, i
     int st = check_forward_args(h, x_host, tokens, false);
     if (st != NF_OK) return st;
     if (!y_host) return h->fail(NF_ERR_INVALID, "null output");
+    if (h->dense && (idx_host || w_host)) return h->fail(NF_ERR_INVALID, "a dense MLP has no routes: pass NULL top-k pointers");
     if (tokens == 0 && !h->ep_outer) return NF_OK;  // an EP rank still takes part in the exchanges
     const int64_t n = static_cast<int64_t>(tokens) * h->d.hidden;
     const int64_t nk = static_cast<int64_t>(tokens) * h->d.top_k;

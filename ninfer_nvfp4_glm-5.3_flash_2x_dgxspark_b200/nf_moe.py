@@ -39,7 +39,7 @@ EXPORTED = [
     "nf_moe_bind_bf16", "nf_moe_bind_f32", "nf_moe_finalize", "nf_moe_forward", "nf_moe_forward_host",
     "nf_moe_sync", "nf_moe_route", "nf_moe_debug_tensor", "nf_moe_debug_read", "nf_nvfp4_dequantize", "nf_nvfp4_quantize",
     "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck", "nf_moe_set_graph_mode",
-    "nf_router_topk_noalloc", "nf_ep_unique_id", "nf_moe_create_ep",
+    "nf_router_topk_noalloc", "nf_ep_unique_id", "nf_moe_create_ep", "nf_moe_create_dense",
 ]
 STAGES = ["router", "permute", "gate_up", "down", "shared", "combine"]
 
@@ -91,6 +91,7 @@ def load() -> ctypes.CDLL:
                                    I32),
         "nf_ep_unique_id": ([ctypes.c_char_p, I32], I32),
         "nf_moe_create_ep": ([ctypes.POINTER(Desc), I32, I32, I32, ctypes.c_char_p, I32, ctypes.POINTER(P)], I32),
+        "nf_moe_create_dense": ([I32, I32, F, I32, I32, ctypes.POINTER(P)], I32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -222,13 +223,18 @@ class MoeLayer:
                 if self.desc.expert_kind == EXPERTS_BF16:
                     self.bind_bf16(BF16_EXPERT_GATE + proj, get(base + name + ".weight"), e)
                 else:
-                    ws2 = get(base + name + ".weight_scale_2")
-                    ins = get(base + name + ".input_scale")
-                    if ws2.ndim != 0 or ins.ndim != 0:
-                        raise NfError(3, f"expected rank-0 F32 for {base + name}.weight_scale_2")
-                    self.bind_nvfp4(e, proj, get(base + name + ".weight"), get(base + name + ".weight_scale"),
-                                    float(ws2), float(ins))
+                    self._bind_nvfp4_named(get, base + name, e, proj)
         self.finalize()
+
+    def _bind_nvfp4_named(self, get, name: str, expert: int, proj: int) -> None:
+        """One NVFP4 linear by checkpoint name: <name>.weight, .weight_scale and
+        the rank-0 F32 .weight_scale_2 / .input_scale (linear_nvfp4's lookups,
+        src/text_forward.cpp:833-836)."""
+        ws2 = get(name + ".weight_scale_2")
+        ins = get(name + ".input_scale")
+        if ws2.ndim != 0 or ins.ndim != 0:
+            raise NfError(3, f"expected rank-0 F32 for {name}.weight_scale_2")
+        self.bind_nvfp4(expert, proj, get(name + ".weight"), get(name + ".weight_scale"), float(ws2), float(ins))
 
     # ---- execution ---------------------------------------------------------
     def forward(self, x_dev, y_dev, tokens: int, residual_dev=None, idx_dev=None, w_dev=None, stream=0) -> None:
@@ -280,6 +286,50 @@ class MoeLayer:
         out = np.empty(count, dtype)
         self._check(self.lib.nf_moe_debug_read(self.h, DBG[which], _ptr(out), out.nbytes))
         return out
+
+
+class DenseMlp(MoeLayer):
+    """The dense NVFP4 MLP of the first layers (TextModel::dense_mlp,
+    src/text_forward.cpp:909-915) resident on one GPU: a one-expert handle
+    without a router (nf_moe_create_dense) whose gate/up epilogue applies
+    swiglu_clamp_bf16.  forward() / forward_host() take no route buffers."""
+
+    def __init__(self, hidden: int, inter: int, *, swiglu_limit: float = 10.0, max_tokens: int = 64,
+                 device: int = 0):
+        self.lib = load()
+        h = ctypes.c_void_p()
+        st = self.lib.nf_moe_create_dense(hidden, inter, swiglu_limit, max_tokens, device, ctypes.byref(h))
+        if st != NF_OK:
+            raise NfError(st, self.lib.nf_moe_last_error(None).decode())
+        self.desc = Desc(hidden, 1, 1, inter, 0, 1, 1, 1, 1.0, swiglu_limit, EXPERTS_NVFP4, max_tokens)
+        self.h = h
+        self.device = device
+        self.ep = None
+
+    def bind_layer(self, lay) -> None:
+        """Binds a workload.DenseLayer and finalizes."""
+        self.bind_nvfp4(0, PROJ_GATE, lay.gate_packed, lay.gate_scales, lay.gate_ws2, lay.gate_in)
+        self.bind_nvfp4(0, PROJ_UP, lay.up_packed, lay.up_scales, lay.up_ws2, lay.up_in)
+        self.bind_nvfp4(0, PROJ_DOWN, lay.down_packed, lay.down_scales, lay.down_ws2, lay.down_in)
+        self.finalize()
+
+    def bind_from_store(self, store: Mapping[str, np.ndarray], prefix: str) -> None:
+        """Binds <prefix>mlp.{gate,up,down}_proj by checkpoint name (the dense
+        layers' names, src/parameter_schema.cpp:187-191) and finalizes."""
+
+        def get(name: str) -> np.ndarray:
+            if name not in store:
+                raise NfError(5, f"missing tensor {name}")
+            return np.asarray(store[name])
+
+        for proj, name in ((PROJ_GATE, "gate_proj"), (PROJ_UP, "up_proj"), (PROJ_DOWN, "down_proj")):
+            self._bind_nvfp4_named(get, f"{prefix}mlp.{name}", 0, proj)
+        self.finalize()
+
+    def forward(self, x_dev, y_dev, tokens: int, residual_dev=None, idx_dev=None, w_dev=None, stream=0) -> None:
+        if idx_dev is not None or w_dev is not None:
+            raise NfError(1, "a dense MLP has no routes")
+        super().forward(x_dev, y_dev, tokens, residual_dev, None, None, stream)
 
 
 def dequantize(packed_dev, scales_dev, global_scale: float, rows: int, cols: int, out_dev, stream=0) -> int:

@@ -14,6 +14,8 @@ Configurations (the benchmark's configs list):
   c1 decode   H2048 E64 k4 I1536 Is1536 T64   scale 2.5
   c2 prefill  c1 with T8192 and the bias tuned so every expert gets 512 +- 10%
   c3 EP       c1 with T16384 and a Zipf(1.1) log-prior added to the bias
+  c4 dense    configs[4]'s dense NVFP4 MLP (layers 0-2): H2048 I10240, decode
+              batches of 1/16/64/256 tokens (the stack's batch sizes)
 
 Arrays are numpy; BF16 is carried as uint16 bit patterns.
 """
@@ -192,3 +194,48 @@ def config_layer(name: str, seed: int | None = None, bf16_experts: bool = False)
     elif name == "c3":
         lay.bias = zipf_bias(lay)
     return lay, x
+
+
+DENSE_CONFIGS = {
+    "c4_dense": dict(hidden=2048, inter=10240, tokens=64),
+}
+
+
+@dataclasses.dataclass
+class DenseLayer:
+    """The dense NVFP4 MLP of one of the first layers (mlp.{gate,up,down}_proj)."""
+    hidden: int
+    inter: int
+    swiglu_limit: float
+    gate_packed: np.ndarray   # [I, H/2]
+    gate_scales: np.ndarray   # [I, H/16]
+    up_packed: np.ndarray
+    up_scales: np.ndarray
+    down_packed: np.ndarray   # [H, I/2]
+    down_scales: np.ndarray   # [H, I/16]
+    gate_ws2: float = 1.0 / 448.0
+    gate_in: float = 1.0 / 6.0
+    up_ws2: float = 1.0 / 448.0
+    up_in: float = 1.0 / 6.0
+    down_ws2: float = 1.0 / 448.0
+    down_in: float = 1.0 / 6.0
+
+    def weight_bytes(self) -> int:
+        """Bytes a forward streams: E2M1 codes plus E4M3 block scales."""
+        n = 3 * self.inter * self.hidden
+        return n // 2 + n // 16
+
+
+def make_dense_layer(hidden: int, inter: int, seed: int) -> DenseLayer:
+    """NVFP4 weights with the same distributions as the routed experts."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    H, I = hidden, inter
+    f32 = lambda v: float(np.float32(v))  # noqa: E731
+    return DenseLayer(
+        hidden=H, inter=I, swiglu_limit=SWIGLU_LIMIT,
+        gate_packed=rng.integers(0, 256, (I, H // 2), dtype=np.uint8), gate_scales=_scales(rng, (I, H // 16)),
+        up_packed=rng.integers(0, 256, (I, H // 2), dtype=np.uint8), up_scales=_scales(rng, (I, H // 16)),
+        down_packed=rng.integers(0, 256, (H, I // 2), dtype=np.uint8), down_scales=_scales(rng, (H, I // 16)),
+        gate_ws2=f32(np.float32(1) / np.float32(448)), gate_in=f32(np.float32(1) / np.float32(6)),
+        up_ws2=f32(np.float32(1) / np.float32(448)), up_in=f32(np.float32(1) / np.float32(6)),
+        down_ws2=f32(np.float32(1) / np.float32(448)), down_in=f32(np.float32(1) / np.float32(6)))

@@ -482,6 +482,43 @@ int or_moe_layer(const or_moe_weights* w, int tokens, const float* x, const floa
     return rc ? -1 : 0;
 }
 
+/* src/text_forward.cpp:909-915 for one token, then the residual (:906). */
+static int dense_token(const or_dense_weights* w, const float* x, const float* residual, float* y, float* h_tap) {
+    const int H = w->hidden, I = w->inter;
+    float* g = (float*)malloc(sizeof(float) * (size_t)I);
+    float* u = (float*)malloc(sizeof(float) * (size_t)I);
+    float* h = (float*)malloc(sizeof(float) * (size_t)I);
+    int rc = 0;
+    rc |= or_linear_nvfp4(w->gate_packed, w->gate_scales, w->gate_ws2, w->gate_in, x, H, g, I);
+    rc |= or_linear_nvfp4(w->up_packed, w->up_scales, w->up_ws2, w->up_in, x, H, u, I);
+    or_swiglu_clamp_bf16(g, u, I, w->swiglu_limit, h);
+    rc |= or_linear_nvfp4(w->down_packed, w->down_scales, w->down_ws2, w->down_in, h, I, y, H);
+    if (h_tap) memcpy(h_tap, h, sizeof(float) * (size_t)I);
+    if (residual) {
+        const float one = 1.f;
+        float* out = (float*)malloc(sizeof(float) * (size_t)H);
+        or_mhc_combine(residual, y, &one, &one, 1, H, out);
+        memcpy(y, out, sizeof(float) * (size_t)H);
+        free(out);
+    }
+    free(g);
+    free(u);
+    free(h);
+    return rc;
+}
+
+int or_dense_mlp(const or_dense_weights* w, int tokens, const float* x, const float* residual, float* y, float* h) {
+    const int H = w->hidden, I = w->inter;
+    int rc = 0;
+    /* tokens are independent; each token's arithmetic is the reference's */
+#pragma omp parallel for schedule(dynamic, 1) reduction(| : rc)
+    for (int t = 0; t < tokens; ++t) {
+        rc |= dense_token(w, x + (size_t)t * H, residual ? residual + (size_t)t * H : NULL, y + (size_t)t * H,
+                          h ? h + (size_t)t * I : NULL);
+    }
+    return rc ? -1 : 0;
+}
+
 void or_route_tokens(const or_moe_weights* w, int tokens, const float* x, float* logits, int* indices,
                      float* weights) {
     const int E = w->experts, K = w->top_k, H = w->hidden;

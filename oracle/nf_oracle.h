@@ -128,6 +128,25 @@ int or_moe_layer(const or_moe_weights* w, int tokens, const float* x, const floa
  * the BF16-rounded down projection of h.  Returns 0 or -1. */
 int or_expert_forward(const or_moe_weights* w, int expert, const float* x, float* h, float* down);
 
+/* ---- the dense NVFP4 MLP (layers 0-2) --------------------------------------
+ * src/text_forward.cpp:909-915 TextModel::dense_mlp for every token: NVFP4
+ * gate and up linears (linear_nvfp4, outputs rounded to BF16),
+ * swiglu_clamp_bf16 (:99-106), NVFP4 down linear; then the hc = 1 residual
+ * form of mhc_combine (src/text_forward.cpp:906, 1646-1657) when residual is
+ * not NULL.  Packed [inter][hidden/2] (gate, up), [hidden][inter/2] (down)
+ * with block scales [rows][cols/16]. */
+typedef struct or_dense_weights {
+    int hidden, inter;
+    float swiglu_limit;
+    const uint8_t *gate_packed, *gate_scales, *up_packed, *up_scales, *down_packed, *down_scales;
+    float gate_ws2, gate_in, up_ws2, up_in, down_ws2, down_in;
+} or_dense_weights;
+
+/* x [T][H] fp32 (BF16-valued), residual nullable [T][H], y [T][H]; h
+ * (nullable, [T][I]) receives swiglu_clamp_bf16's output.  Returns 0 or -1
+ * (bad input scale). */
+int or_dense_mlp(const or_dense_weights* w, int tokens, const float* x, const float* residual, float* y, float* h);
+
 /* Router logits for one token: gemv_bf16 over [E][H] (src/text_forward.cpp:926). */
 void or_router_logits(const or_moe_weights* w, const float* x, float* logits);
 

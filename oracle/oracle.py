@@ -40,6 +40,15 @@ class MoeWeights(ctypes.Structure):
     ]
 
 
+class DenseWeights(ctypes.Structure):
+    _fields_ = [
+        ("hidden", _I), ("inter", _I), ("swiglu_limit", _F),
+        ("gate_packed", _P), ("gate_scales", _P), ("up_packed", _P), ("up_scales", _P),
+        ("down_packed", _P), ("down_scales", _P),
+        ("gate_ws2", _F), ("gate_in", _F), ("up_ws2", _F), ("up_in", _F), ("down_ws2", _F), ("down_in", _F),
+    ]
+
+
 def build() -> None:
     """Builds the checker libraries (the reference one only when its tree exists)."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
@@ -105,6 +114,8 @@ def port() -> ctypes.CDLL:
         lib.or_route_tokens.argtypes = [ctypes.POINTER(MoeWeights), _I, _P, _P, _P, _P]
         lib.or_sigmoid_array.restype = None
         lib.or_sigmoid_array.argtypes = [_P, _I64, _P]
+        lib.or_dense_mlp.restype = _I
+        lib.or_dense_mlp.argtypes = [ctypes.POINTER(DenseWeights), _I, _P, _P, _P, _P]
         _port = lib
     return _port
 
@@ -149,6 +160,8 @@ def ref() -> ctypes.CDLL | None:
         lib.ref_rmsnorm.argtypes = [_P, _P, _F, _I, _P]
         lib.ref_moe_layer.restype = _I
         lib.ref_moe_layer.argtypes = [ctypes.POINTER(MoeWeights), _I, _P, _P, _P, _P, _P]
+        lib.ref_dense_mlp.restype = _I
+        lib.ref_dense_mlp.argtypes = [ctypes.POINTER(DenseWeights), _I, _P, _P, _P]
         _ref = lib
     return _ref
 
@@ -258,3 +271,38 @@ def expert_forward(lay, e: int, x_f32: np.ndarray):
     if rc != 0:
         raise RuntimeError("NVFP4 input scale")
     return h, d
+
+
+def dense_struct(lay) -> tuple[DenseWeights, list]:
+    """DenseWeights over a workload.DenseLayer (keeps the arrays alive in `keep`)."""
+    keep = []
+    w = DenseWeights()
+    w.hidden, w.inter, w.swiglu_limit = lay.hidden, lay.inter, lay.swiglu_limit
+    for name in ("gate_packed", "gate_scales", "up_packed", "up_scales", "down_packed", "down_scales"):
+        a = np.ascontiguousarray(getattr(lay, name), dtype=np.uint8)
+        keep.append(a)
+        setattr(w, name, a.ctypes.data)
+    for name in ("gate_ws2", "gate_in", "up_ws2", "up_in", "down_ws2", "down_in"):
+        setattr(w, name, float(getattr(lay, name)))
+    return w, keep
+
+
+def dense_mlp(lib, lay, x_f32: np.ndarray, residual: np.ndarray | None = None, taps: bool = False):
+    """or_dense_mlp (port) or ref_dense_mlp (reference) on fp32 rows: y, and
+    with taps (port only) also swiglu_clamp_bf16's output h [T, I]."""
+    x = np.ascontiguousarray(x_f32, dtype=np.float32)
+    T = x.shape[0]
+    y = np.zeros_like(x)
+    res = None if residual is None else np.ascontiguousarray(residual, dtype=np.float32)
+    ws, keep = dense_struct(lay)
+    if hasattr(lib, "or_dense_mlp"):
+        h = np.zeros((T, lay.inter), np.float32) if taps else None
+        rc = lib.or_dense_mlp(ctypes.byref(ws), T, p(x), p(res), p(y), p(h))
+        if rc != 0:
+            raise RuntimeError("oracle rejected the dense MLP (NVFP4 input scale)")
+        return (y, h) if taps else y
+    rc = lib.ref_dense_mlp(ctypes.byref(ws), T, p(x), p(res), p(y))
+    del keep
+    if rc != 0:
+        raise RuntimeError(f"reference dense_mlp composition failed ({rc})")
+    return y

@@ -161,4 +161,30 @@ int ref_moe_layer(const or_moe_weights* w, int tokens, const float* x, const flo
     }
 }
 
+// TextModel::dense_mlp (src/text_forward.cpp:909-915) for `tokens` tokens one
+// at a time, then the hc = 1 residual combine (src/text_forward.cpp:906).
+// Returns 0 or -1 on a reference exception.
+int ref_dense_mlp(const or_dense_weights* w, int tokens, const float* x, const float* residual, float* y) {
+    const int H = w->hidden, I = w->inter;
+    try {
+        std::vector<float> g(static_cast<std::size_t>(I)), u(g.size()), h(g.size()), out(static_cast<std::size_t>(H));
+        for (int t = 0; t < tokens; ++t) {
+            const float* xt = x + static_cast<std::size_t>(t) * H;
+            float* yt = y + static_cast<std::size_t>(t) * H;
+            linear_nvfp4(w->gate_packed, w->gate_scales, w->gate_ws2, w->gate_in, xt, H, g.data(), I);
+            linear_nvfp4(w->up_packed, w->up_scales, w->up_ws2, w->up_in, xt, H, u.data(), I);
+            R::swiglu_clamp_bf16(g.data(), u.data(), I, w->swiglu_limit, h.data());
+            linear_nvfp4(w->down_packed, w->down_scales, w->down_ws2, w->down_in, h.data(), I, yt, H);
+            if (residual != nullptr) {
+                const float one = 1.f;
+                R::mhc_combine(residual + static_cast<std::size_t>(t) * H, yt, &one, &one, 1, H, out.data());
+                std::copy(out.begin(), out.end(), yt);
+            }
+        }
+        return 0;
+    } catch (const std::exception&) {
+        return -1;
+    }
+}
+
 }  // extern "C"

@@ -131,3 +131,17 @@ def test_moe_layer_c1_subset_bit_exact():
     yb, ib, wb = orc.moe_layer(REF, lay, x)
     assert np.array_equal(ia, ib) and np.array_equal(wa.view(np.uint32), wb.view(np.uint32))
     assert np.array_equal(ya.view(np.uint32), yb.view(np.uint32))
+
+
+@pytest.mark.parametrize("hidden,inter,tokens", [(256, 512, 9), (2048, 10240, 2)])
+def test_dense_mlp_bit_exact(hidden, inter, tokens):
+    """dense_mlp (src/text_forward.cpp:909-915): the restatement against the
+    reference's own primitives, with and without the residual; the second
+    case has the dense layers' shapes of the benchmark's decoder stack."""
+    lay = wl.make_dense_layer(hidden, inter, seed=40 + tokens)
+    x = wl.bf16_bits_to_f32(wl.make_tokens(dict(hidden=hidden, tokens=tokens), 40 + tokens))
+    res = np.random.Generator(np.random.PCG64(14)).standard_normal(x.shape).astype(np.float32)
+    for residual in (None, res):
+        ya = orc.dense_mlp(PORT, lay, x, residual)
+        yb = orc.dense_mlp(REF, lay, x, residual)
+        assert np.array_equal(ya.view(np.uint32), yb.view(np.uint32))
