@@ -80,7 +80,8 @@ def build(verbose_ptxas: bool = False) -> Path:
     # the C++ host example (host/): header-only class over the C ABI + a demo program
     demo = LIB.parent / "moe_demo"
     host = HERE / "host"
-    if not _newer(demo, [host / "moe_demo.cpp", host / "nf_moe_layer.hpp", REPO / "include" / "nf_moe.h", LIB]):
+    if not _newer(demo, [host / "moe_demo.cpp", host / "nf_moe_layer.hpp", host / "nf_safetensors.hpp",
+                         REPO / "include" / "nf_moe.h", LIB]):
         _run(["g++", "-O2", "-std=c++17", "-I", REPO / "include", "-I", host, host / "moe_demo.cpp", "-o", demo,
               "-L", LIB.parent, "-lnf_moe", "-Wl,-rpath,$ORIGIN"])
     return LIB

@@ -1423,14 +1423,26 @@ __global__ void __launch_bounds__(256) splitk_store_kernel(const float* __restri
     const float a = alpha[0];
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        // slices in order; four loads in flight before their adds
         float4 acc = reinterpret_cast<const float4*>(part)[i];
-        for (int s = 1; s < S; ++s) {
-            const float4 v = reinterpret_cast<const float4*>(part + s * stride)[i];
+        auto add = [&](const float4 v) {
             acc.x = __fadd_rn(acc.x, v.x);
             acc.y = __fadd_rn(acc.y, v.y);
             acc.z = __fadd_rn(acc.z, v.z);
             acc.w = __fadd_rn(acc.w, v.w);
+        };
+        int s = 1;
+        for (; s + 3 < S; s += 4) {
+            const float4 v0 = reinterpret_cast<const float4*>(part + s * stride)[i];
+            const float4 v1 = reinterpret_cast<const float4*>(part + (s + 1) * stride)[i];
+            const float4 v2 = reinterpret_cast<const float4*>(part + (s + 2) * stride)[i];
+            const float4 v3 = reinterpret_cast<const float4*>(part + (s + 3) * stride)[i];
+            add(v0);
+            add(v1);
+            add(v2);
+            add(v3);
         }
+        for (; s < S; ++s) add(reinterpret_cast<const float4*>(part + s * stride)[i]);
         float4 o = make_float4(bf16_round_hw(__fmul_rn(acc.x, a)), bf16_round_hw(__fmul_rn(acc.y, a)),
                                bf16_round_hw(__fmul_rn(acc.z, a)), bf16_round_hw(__fmul_rn(acc.w, a)));
         if (residual) {

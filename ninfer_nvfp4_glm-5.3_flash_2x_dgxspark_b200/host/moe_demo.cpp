@@ -1,13 +1,20 @@
-// moe_demo.cpp -- a C++ host running one MoE layer through nf_host::MoeLayer:
-// reads a tensor file (checkpoint names, the reference's tensor kinds), binds
-// the layer by name, runs TextModel::moe's contract over the token rows `x`
-// and writes y.  It stands where the reference's own host would sit.
+// moe_demo.cpp -- a C++ host running one feed-forward layer through
+// nf_host::MoeLayer (or nf_host::DenseMlp): reads a tensor store (checkpoint
+// names, the reference's tensor kinds), binds the layer by name, runs
+// TextModel::moe's (or dense_mlp's) contract over the token rows `x` and
+// writes y.  It stands where the reference's own host would sit.
 //
-// usage: moe_demo <tensors.nft> <prefix> <out_y.f32> hidden experts top_k inter shared_inter
+// usage: moe_demo <store> <prefix> <out_y.f32> hidden experts top_k inter shared_inter
 //                 routed_scaling [device]
-// tensor file: "NFT1", then records {u32 name_len, name, u8 kind, u32 rank,
-// i64 dims[rank], u64 bytes, data}; `x` is F32 [tokens, hidden].
+// store: a safetensors checkpoint directory (model.safetensors.index.json and
+// its shards, or model.safetensors: nf_host::SafetensorsStore), or a tensor
+// file: "NFT1", then records {u32 name_len, name, u8 kind, u32 rank, i64
+// dims[rank], u64 bytes, data}.  The store holds `x`, F32 [tokens, hidden].
+// experts == 0 runs the dense MLP of the first layers (hidden, inter).
 #include "nf_moe_layer.hpp"
+#include "nf_safetensors.hpp"
+
+#include <sys/stat.h>
 
 #include <cstdio>
 #include <cstring>
@@ -64,12 +71,24 @@ int main(int argc, char** argv) {
         return 2;
     }
     try {
-        const auto store = read_tensors(argv[1]);
+        struct stat st {};
+        const bool is_dir = ::stat(argv[1], &st) == 0 && S_ISDIR(st.st_mode);
+        std::unique_ptr<nf_host::SafetensorsStore> ckpt;
+        std::map<std::string, Record> records;
+        nf_host::StoreLookup lookup;
+        if (is_dir) {
+            ckpt = std::make_unique<nf_host::SafetensorsStore>(argv[1]);
+            lookup = ckpt->lookup();
+            std::printf("moe_demo: %zu tensors in %zu shards, %llu bytes mapped\n", ckpt->tensor_count(),
+                        ckpt->shard_count(), static_cast<unsigned long long>(ckpt->data_bytes()));
+        } else {
+            records = read_tensors(argv[1]);
+            lookup = [&records](const std::string& name) -> const nf_host::TensorView* {
+                const auto it = records.find(name);
+                return it == records.end() ? nullptr : &it->second.view;
+            };
+        }
         const std::string prefix = argv[2];
-        auto lookup = [&](const std::string& name) -> const nf_host::TensorView* {
-            const auto it = store.find(name);
-            return it == store.end() ? nullptr : &it->second.view;
-        };
         const nf_host::TensorView* x = lookup("x");
         if (!x || x->kind != 'f' || x->shape.size() != 2) throw std::runtime_error("missing tensor x");
         nf_moe_desc d{};
@@ -86,10 +105,16 @@ int main(int argc, char** argv) {
         d.expert_kind = NF_EXPERTS_NVFP4;
         d.max_tokens = static_cast<int>(x->dim(0));
         const int device = argc > 10 ? std::atoi(argv[10]) : 0;
-        nf_host::MoeLayer layer(d, device);
-        layer.bind_from_store(lookup, prefix);
         std::vector<float> y(static_cast<size_t>(x->dim(0) * x->dim(1)));
-        layer.moe(static_cast<const float*>(x->data), y.data(), static_cast<int>(x->dim(0)));
+        if (d.experts == 0) {
+            nf_host::DenseMlp mlp(d.hidden, d.inter, d.swiglu_limit, d.max_tokens, device);
+            mlp.bind_from_store(lookup, prefix);
+            mlp.dense_mlp(static_cast<const float*>(x->data), y.data(), static_cast<int>(x->dim(0)));
+        } else {
+            nf_host::MoeLayer layer(d, device);
+            layer.bind_from_store(lookup, prefix);
+            layer.moe(static_cast<const float*>(x->data), y.data(), static_cast<int>(x->dim(0)));
+        }
         std::ofstream out(argv[3], std::ios::binary);
         out.write(reinterpret_cast<const char*>(y.data()), static_cast<std::streamsize>(y.size() * 4));
         double sum = 0;

@@ -33,6 +33,36 @@ struct TensorView {
 // Name -> tensor; throws "missing tensor <name>" like Store::get.
 using StoreLookup = std::function<const TensorView*(const std::string&)>;
 
+namespace detail {
+
+inline const TensorView& get(const StoreLookup& store, const std::string& name) {
+    const TensorView* t = store(name);
+    if (!t) throw std::runtime_error("missing tensor " + name);
+    return *t;
+}
+
+// Store::scalar (src/text_forward.cpp:470-476).
+inline float scalar(const StoreLookup& store, const std::string& name) {
+    const TensorView& t = get(store, name);
+    if (t.kind != 'f' || !t.shape.empty()) throw std::runtime_error("expected rank-0 F32 for " + name);
+    return *static_cast<const float*>(t.data);
+}
+
+// One NVFP4 linear by checkpoint name (linear_nvfp4's lookups,
+// src/text_forward.cpp:833-843): <base>.weight U8 [N, K/2],
+// <base>.weight_scale F8_E4M3 [N, K/16], rank-0 F32 weight_scale_2 and
+// input_scale.  Returns the library's status.
+inline int bind_nvfp4_named(nf_moe* h, int expert, int proj, const StoreLookup& store, const std::string& base) {
+    const TensorView& w = get(store, base + ".weight");
+    const TensorView& s = get(store, base + ".weight_scale");
+    if (w.kind != 'u' || s.kind != '8' || w.shape.size() != 2) throw std::runtime_error("NVFP4 layout " + base);
+    return nf_moe_bind_nvfp4(h, expert, proj, static_cast<const uint8_t*>(w.data), static_cast<const uint8_t*>(s.data),
+                             scalar(store, base + ".weight_scale_2"), scalar(store, base + ".input_scale"), w.dim(0),
+                             w.dim(1) * 2);
+}
+
+}  // namespace detail
+
 class MoeLayer {
 public:
     // desc: the layer's shapes (from ModelSpec); max_tokens per forward.
@@ -59,11 +89,6 @@ public:
             if (t.kind != 'b' || t.shape.size() != 2) throw std::runtime_error("BF16 linear layout " + name);
             check(nf_moe_bind_bf16(h_, which, expert, static_cast<const uint16_t*>(t.data), t.dim(0), t.dim(1)));
         };
-        auto scalar = [&](const std::string& name) {
-            const TensorView& t = get(name);
-            if (t.kind != 'f' || !t.shape.empty()) throw std::runtime_error("expected rank-0 F32 for " + name);
-            return *static_cast<const float*>(t.data);
-        };
         bf16(NF_BF16_ROUTER, 0, prefix + "mlp.gate.weight");
         const TensorView& bias = get(prefix + "mlp.gate.e_score_correction_bias");
         if (bias.kind != 'f' || bias.shape.size() != 1)
@@ -82,12 +107,7 @@ public:
                     bf16(NF_BF16_EXPERT_GATE + p, e, base + ".weight");
                     continue;
                 }
-                const TensorView& w = get(base + ".weight");
-                const TensorView& s = get(base + ".weight_scale");
-                if (w.kind != 'u' || s.kind != '8' || w.shape.size() != 2) throw std::runtime_error("NVFP4 layout " + base);
-                check(nf_moe_bind_nvfp4(h_, e, p, static_cast<const uint8_t*>(w.data), static_cast<const uint8_t*>(s.data),
-                                        scalar(base + ".weight_scale_2"), scalar(base + ".input_scale"), w.dim(0),
-                                        w.dim(1) * 2));
+                check(detail::bind_nvfp4_named(h_, e, p, store, base));
             }
         check(nf_moe_finalize(h_));
     }
@@ -108,6 +128,40 @@ private:
     }
     nf_moe* h_ = nullptr;
     nf_moe_desc d_{};
+};
+
+// The dense NVFP4 MLP of the first layers (TextModel::dense_mlp,
+// src/text_forward.cpp:909-915), bound by the dense layers' names
+// (<prefix>mlp.{gate,up,down}_proj, src/parameter_schema.cpp:187-191).
+class DenseMlp {
+public:
+    DenseMlp(int hidden, int inter, float swiglu_limit, int max_tokens, int device) {
+        if (nf_moe_create_dense(hidden, inter, swiglu_limit, max_tokens, device, &h_) != NF_OK)
+            throw std::runtime_error(nf_moe_last_error(nullptr));
+    }
+    DenseMlp(const DenseMlp&) = delete;
+    DenseMlp& operator=(const DenseMlp&) = delete;
+    ~DenseMlp() { nf_moe_destroy(h_); }
+
+    nf_moe* handle() const { return h_; }
+
+    void bind_from_store(const StoreLookup& store, const std::string& prefix) {
+        static const char* proj[3] = {"gate_proj", "up_proj", "down_proj"};
+        for (int p = 0; p < 3; ++p) check(detail::bind_nvfp4_named(h_, 0, p, store, prefix + "mlp." + proj[p]));
+        check(nf_moe_finalize(h_));
+    }
+
+    // dense_mlp's contract over `tokens` rows: x fp32 (BF16-valued) in, y fp32
+    // out, host memory; synchronous.
+    void dense_mlp(const float* x, float* y, int tokens = 1) {
+        check(nf_moe_forward_host(h_, x, nullptr, tokens, y, nullptr, nullptr));
+    }
+
+private:
+    void check(int status) const {
+        if (status != NF_OK) throw std::runtime_error(nf_moe_last_error(h_));
+    }
+    nf_moe* h_ = nullptr;
 };
 
 }  // namespace nf_host

@@ -332,6 +332,66 @@ class DenseMlp(MoeLayer):
         super().forward(x_dev, y_dev, tokens, residual_dev, None, None, stream)
 
 
+_ST_DTYPES = {"BF16": np.uint16, "F32": np.float32, "U8": np.uint8, "F8_E4M3": np.uint8}
+
+
+def safetensors_store(directory) -> dict:
+    """Name -> read-only memory-mapped array over a safetensors checkpoint
+    directory (model.safetensors.index.json and its shards, or a single
+    model.safetensors), for MoeLayer / DenseMlp.bind_from_store.  The Python
+    twin of host/nf_safetensors.hpp, with the reference Store's messages
+    (src/text_forward.cpp:328-495) and the same range and size checks."""
+    import json
+    from pathlib import Path
+
+    d = Path(directory)
+    index = d / "model.safetensors.index.json"
+    if index.is_file():
+        text = index.read_text()
+        if not text:
+            raise NfError(3, "empty safetensors index")
+        wmap = json.loads(text).get("weight_map")
+        if wmap is None:
+            raise NfError(3, "index has no weight_map")
+        shards = list(dict.fromkeys(wmap.values()))
+    elif (d / "model.safetensors").is_file():
+        shards = ["model.safetensors"]
+    else:
+        raise NfError(3, "missing model.safetensors.index.json")
+    out = {}
+    for shard in shards:
+        path = d / shard
+        if not path.is_file():
+            raise NfError(3, f"cannot open shard {path}")
+        raw = np.memmap(path, dtype=np.uint8, mode="r")
+        if raw.size < 8:
+            raise NfError(3, "short safetensors file")
+        hlen = int(raw[:8].view("<u8")[0])
+        if hlen == 0 or hlen > raw.size - 8:
+            raise NfError(3, "bad safetensors header")
+        try:
+            header = json.loads(bytes(raw[8:8 + hlen]).decode())
+        except ValueError:
+            raise NfError(3, "bad safetensors header") from None
+        data = raw[8 + hlen:]
+        for name, info in header.items():
+            if name == "__metadata__":
+                continue
+            dt = _ST_DTYPES.get(info.get("dtype"))
+            if dt is None:
+                raise NfError(3, f"unsupported dtype {info.get('dtype')} for {name}")
+            shape, offs = info.get("shape"), info.get("data_offsets")
+            if shape is None or offs is None:
+                raise NfError(3, f"incomplete tensor header for {name}")
+            b, e = int(offs[0]), int(offs[1])
+            if b < 0 or e < b or e > data.size:
+                raise NfError(3, f"tensor data out of range for {name}")
+            if int(np.prod(shape, dtype=np.int64)) * np.dtype(dt).itemsize != e - b:
+                raise NfError(3, f"tensor size mismatch for {name}")
+            out[name] = data[b:e].view(dt).reshape(shape)
+    return out
+
+
 def dequantize(packed_dev, scales_dev, global_scale: float, rows: int, cols: int, out_dev, stream=0) -> int:
     return load().nf_nvfp4_dequantize(_ptr(packed_dev), _ptr(scales_dev), global_scale, rows, cols, _ptr(out_dev),
                                       stream or None)

@@ -9,7 +9,7 @@ import subprocess
 import numpy as np
 import pytest
 
-from helpers import MAX_ABS, MIN_COS, PKG, assert_close, nfm, workload
+from helpers import MAX_ABS, MIN_COS, PKG, assert_close, load_module, nfm, workload
 
 DEMO = PKG / "lib" / "moe_demo"
 PREFIX = "model.language_model.layers.3."
@@ -94,3 +94,156 @@ def test_demo_missing_expert_tensor_names_it(tmp_path):
     write_nft(tmp_path / "c0.nft", t)
     r = run_demo(tmp_path / "c0.nft", tmp_path / "y.f32", lay)
     assert r.returncode == 1 and f"missing tensor {PREFIX}mlp.experts.5.up_proj.weight_scale" in r.stderr
+
+
+# ---- safetensors checkpoints (host/nf_safetensors.hpp, nf_moe.safetensors_store)
+ST_DTYPE = {"b": "BF16", "f": "F32", "u": "U8", "8": "F8_E4M3"}
+
+
+def write_safetensors(path, tensors: dict, header_patch=None) -> None:
+    """One safetensors shard: u64 header length, JSON header, packed data."""
+    import json
+
+    header, blobs, off = {"__metadata__": {"format": "pt"}}, [], 0
+    for name, (kind, arr) in tensors.items():
+        a = np.array(arr, dtype=KIND[kind], order="C")
+        header[name] = {"dtype": ST_DTYPE[kind], "shape": list(a.shape), "data_offsets": [off, off + a.nbytes]}
+        blobs.append(a.tobytes())
+        off += a.nbytes
+    if header_patch:
+        header_patch(header)
+    h = json.dumps(header).encode()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)) + h + b"".join(blobs))
+
+
+def write_checkpoint(directory, tensors: dict, shards: int = 2) -> None:
+    """A checkpoint directory: the tensors spread over `shards` files and a
+    model.safetensors.index.json weight map."""
+    import json
+
+    directory.mkdir(parents=True, exist_ok=True)
+    names = list(tensors)
+    parts = [names[i::shards] for i in range(shards)]
+    wmap = {}
+    for i, part in enumerate(parts):
+        fname = f"model-{i + 1:05d}-of-{shards:05d}.safetensors"
+        write_safetensors(directory / fname, {n: tensors[n] for n in part})
+        wmap.update({n: fname for n in part})
+    (directory / "model.safetensors.index.json").write_text(json.dumps({"metadata": {}, "weight_map": wmap}))
+
+
+def dense_tensors(lay, prefix) -> dict:
+    t = {}
+    for name in ("gate", "up", "down"):
+        base = f"{prefix}mlp.{name}_proj."
+        t[base + "weight"] = ("u", getattr(lay, f"{name}_packed"))
+        t[base + "weight_scale"] = ("8", getattr(lay, f"{name}_scales"))
+        t[base + "weight_scale_2"] = ("f", np.float32(getattr(lay, f"{name}_ws2")))
+        t[base + "input_scale"] = ("f", np.float32(getattr(lay, f"{name}_in")))
+    return t
+
+
+def test_safetensors_store_errors(tmp_path):
+    """The checkpoint store's failures, from the C++ demo (before any device
+    work) and from the Python reader, with the reference Store's messages."""
+    m = nfm()
+    lay, _ = workload().config_layer("c0")
+    cases = []
+    empty = tmp_path / "empty"
+    empty.mkdir()
+    cases.append((empty, "missing model.safetensors.index.json"))
+    bad = tmp_path / "bad"
+    bad.mkdir()
+    (bad / "model.safetensors").write_bytes(struct.pack("<Q", 1 << 40) + b"{}")
+    cases.append((bad, "bad safetensors header"))
+    dt = tmp_path / "dtype"
+    dt.mkdir()
+    write_safetensors(dt / "model.safetensors", {"x": ("f", np.zeros((2, 4), np.float32))},
+                      lambda h: h["x"].update(dtype="F16"))
+    cases.append((dt, "unsupported dtype F16 for x"))
+    rng = tmp_path / "range"
+    rng.mkdir()
+    write_safetensors(rng / "model.safetensors", {"x": ("f", np.zeros((2, 4), np.float32))},
+                      lambda h: h["x"].update(data_offsets=[0, 4096]))
+    cases.append((rng, "tensor data out of range for x"))
+    size = tmp_path / "size"
+    size.mkdir()
+    write_safetensors(size / "model.safetensors", {"x": ("f", np.zeros((2, 4), np.float32))},
+                      lambda h: h["x"].update(shape=[2, 3]))
+    cases.append((size, "tensor size mismatch for x"))
+    shard = tmp_path / "shard"
+    write_checkpoint(shard, {"x": ("f", np.zeros((2, 4), np.float32)), "y": ("f", np.zeros(3, np.float32))})
+    (shard / "model-00002-of-00002.safetensors").unlink()
+    cases.append((shard, "cannot open shard"))
+    nox = tmp_path / "nox"
+    write_checkpoint(nox, {"y": ("f", np.zeros(3, np.float32))}, shards=1)
+    for d, msg in cases + [(nox, None)]:
+        if msg is not None:
+            with pytest.raises(m.NfError, match=msg):
+                m.safetensors_store(d)
+        if DEMO.exists():
+            r = run_demo(d, tmp_path / "y.f32", lay)
+            assert r.returncode == 1 and (msg or "missing tensor x") in r.stderr, r.stderr
+
+
+def test_safetensors_store_reads_checkpoint(tmp_path):
+    """Every tensor of a two-shard checkpoint comes back with its name, kind,
+    shape and bytes (rank-0 scalars stay rank 0)."""
+    m = nfm()
+    lay, x_bits = workload().config_layer("c0")
+    t = layer_tensors(lay)
+    write_checkpoint(tmp_path / "ckpt", t)
+    store = m.safetensors_store(tmp_path / "ckpt")
+    assert set(store) == set(t)
+    for name, (kind, arr) in t.items():
+        a = np.asarray(arr, dtype=KIND[kind])
+        assert store[name].dtype == a.dtype and store[name].shape == a.shape
+        assert np.array_equal(store[name], a)
+
+
+@pytest.mark.gpu
+def test_checkpoint_directory_binds_moe_and_dense(tmp_path):
+    """Checkpoint -> device residency: a MoE layer and a dense MLP bound by
+    name from safetensors shards (C++ store in the demo, Python store in
+    MoeLayer / DenseMlp.bind_from_store) give the same bits as binding the
+    arrays directly."""
+    wl, m = workload(), nfm()
+    lay, x_bits = wl.config_layer("c0")
+    x = wl.bf16_bits_to_f32(x_bits)
+    t = layer_tensors(lay)
+    t["x"] = ("f", x)
+    write_checkpoint(tmp_path / "moe", t, shards=3)
+    r = run_demo(tmp_path / "moe", tmp_path / "y.f32", lay)
+    assert r.returncode == 0, r.stderr
+    y_cpp = np.fromfile(tmp_path / "y.f32", dtype=np.float32).reshape(x.shape)
+    layer = m.MoeLayer(lay.hidden, lay.experts, lay.top_k, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                       swiglu_limit=lay.swiglu_limit, max_tokens=x.shape[0])
+    layer.bind_layer(lay)
+    y_ref = layer.forward_host(x)
+    layer.close()
+    layer = m.MoeLayer(lay.hidden, lay.experts, lay.top_k, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                       swiglu_limit=lay.swiglu_limit, max_tokens=x.shape[0])
+    layer.bind_from_store(m.safetensors_store(tmp_path / "moe"), PREFIX)
+    y_py = layer.forward_host(x)
+    layer.close()
+    assert np.array_equal(y_cpp.view(np.uint32), y_ref.view(np.uint32))
+    assert np.array_equal(y_py.view(np.uint32), y_ref.view(np.uint32))
+
+    dl = wl.make_dense_layer(256, 512, 21)
+    dprefix = "model.language_model.layers.0."
+    xd = wl.bf16_bits_to_f32(wl.make_tokens(dict(hidden=256, tokens=12), 21))
+    td = dense_tensors(dl, dprefix)
+    td["x"] = ("f", xd)
+    write_checkpoint(tmp_path / "dense", td)
+    r = subprocess.run([str(DEMO), str(tmp_path / "dense"), dprefix, str(tmp_path / "yd.f32"), "256", "0", "1", "512",
+                        "0", "1.0"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    yd_cpp = np.fromfile(tmp_path / "yd.f32", dtype=np.float32).reshape(xd.shape)
+    mlp = m.DenseMlp(256, 512, max_tokens=12)
+    mlp.bind_layer(dl)
+    yd_ref = mlp.forward_host(xd)
+    mlp.close()
+    assert np.array_equal(yd_cpp.view(np.uint32), yd_ref.view(np.uint32))
+    orc = load_module("nf_oracle_py", PKG.parent / "oracle" / "oracle.py")
+    assert_close(yd_cpp, orc.dense_mlp(orc.port(), dl, xd), MAX_ABS, MIN_COS, "dense from checkpoint vs oracle")
