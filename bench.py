@@ -215,11 +215,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     # The layer runs on its own stream; with graph mode on, the first forward
     # for a token count captures the layer's launches into a CUDA graph and
     # later forwards replay it (one launch per step on the host side).
-    # (An expert-parallel forward synchronises the host once for the row
-    # counts, so it runs without a graph.)
+    # (Expert-parallel forwards over NVLink peer memory run in graph mode
+    # too; over the NCCL fallback they synchronise the host once for the row
+    # counts and the library launches them directly.)
     tstream = torch.cuda.Stream()
     stream = tstream.cuda_stream
-    layer.set_graph_mode(world == 1)
+    layer.set_graph_mode(True)
 
     def step():
         layer.forward(x, y, T, None, idx, w, stream=stream)
@@ -294,6 +295,10 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         # fused router, permutation, dispatch, gate/up GEMM, down GEMM,
         # combine; + shared gate/up and down GEMMs on the side stream
         launches_per_step = 8 if lay.shared_inter > 0 else 6
+        if world > 1:
+            # + pack, send, receive wait, return, return wait (NVLink) or
+            # + pack and two row gathers (NCCL, whose own kernels are not counted)
+            launches_per_step += 4 if layer.ep_transport() == "nvlink" else 3
         line = {
             "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3,
@@ -301,6 +306,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "dtype": "nvfp4 (E2M1 x UE4M3/16, fp32 accumulate); bf16 shared expert", "data": "synthetic",
             "config": {"workload": "c1 decode: H2048 E64 k4 I1536 Is1536 T64 scale2.5 (configs[1])",
                        "tokens_per_gpu": T, "parallelism": f"ep{world}" if world > 1 else "single",
+                       "ep_transport": layer.ep_transport(),
                        "l2": "no flush: the 340 MB of weights streamed per step exceed the 126 MB L2",
                        "active_experts": active},
             "stages_us": {k: 1e3 * v for k, v in stage_ms.items()},

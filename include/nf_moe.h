@@ -260,13 +260,24 @@ NF_API int nf_moe_create_dense(int32_t hidden, int32_t inter, float swiglu_limit
  * rank keeps the ones it owns and skips the others.  Every rank must call
  * nf_moe_forward (or nf_moe_forward_host) for each step, also with tokens ==
  * 0: the forward exchanges rows with the other ranks (NCCL point-to-point,
- * loaded from libnccl.so.2 at the first EP handle) and synchronises the host
- * once for the row counts, so EP forwards are never captured into graphs.
+ * loaded from libnccl.so.2 at the first EP handle, or NVLink peer memory:
+ * see nf_moe_ep_transport).
  * Results are bit-identical to one GPU holding every expert. */
 #define NF_EP_ID_BYTES 128
 NF_API int nf_ep_unique_id(uint8_t* group_id_out, int len);
 NF_API int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, const uint8_t* group_id,
                             int id_len, nf_moe** out);
+/* The exchange an EP handle uses (the choice is made collectively at
+ * create): NF_EP_NVLINK -- every rank maps every other rank's receive
+ * "mailbox" with CUDA IPC and rows and outputs cross NVLink by direct stores
+ * with bounded-wait epoch flags, no host synchronisation, so EP forwards run
+ * in graph mode too; NF_EP_NCCL -- NCCL point-to-point with one host
+ * synchronisation for the row counts.  The environment variable
+ * NF_EP_TRANSPORT=nvlink or =nccl chooses (NCCL when unset); NVLink falls
+ * back to NCCL when some rank cannot map a mailbox.  NF_EP_NONE for a
+ * one-GPU handle. */
+enum { NF_EP_NONE = 0, NF_EP_NCCL = 1, NF_EP_NVLINK = 2 };
+NF_API int nf_moe_ep_transport(const nf_moe* handle);
 
 /* ---- router top-k without device allocation ------------------------------
  * No counterpart in the reference: its router runs inside moe() on host

@@ -18,7 +18,8 @@ enum : int {
     NF_DEVERR_WAIT_FULL = 1,    // consumer waited too long for a TMA stage
     NF_DEVERR_WAIT_EMPTY = 2,   // producer waited too long for a free stage
     NF_DEVERR_WAIT_ACC = 3,     // MMA / epilogue accumulator hand-off timed out
-    NF_DEVERR_DRAIN = 4         // teardown drain after an abort timed out
+    NF_DEVERR_DRAIN = 4,        // teardown drain after an abort timed out
+    NF_DEVERR_EP_WAIT = 5       // an expert-parallel peer's rows or outputs never arrived
 };
 
 // One second of %globaltimer (ns) per wait; the longest kernel here runs

@@ -22,12 +22,24 @@
 // NCCL is loaded with dlopen on the first EP handle: a process that already
 // loaded NCCL (e.g. through PyTorch) shares that copy, and processes that
 // never use EP never load it.
+//
+// Two transports carry steps 4-7.  The peer-memory one maps every rank's "mailbox"
+// allocation into every other rank with CUDA IPC and moves rows and outputs
+// by plain stores over NVLink, each direction closed by an epoch flag with a
+// bounded wait (nf_kernels.cu ep_p2p_*): only the rows that exist cross the
+// link, the forward never synchronises the host, and it can be captured in
+// a CUDA graph.  NF_EP_TRANSPORT=nvlink selects it (kEpNvlinkDefault when
+// unset); when a mailbox cannot be mapped on some rank, or NCCL is chosen,
+// every rank uses NCCL point-to-point, with the host synchronisation for the
+// counts.
 #include "nf_handle.h"
 
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <cstring>
+#include <vector>
 #include <mutex>
 
 using namespace nf;
@@ -75,7 +87,159 @@ NcclApi& nccl() {
 
 const char* nccl_str(ncclResult_t r) { return nccl().error_string ? nccl().error_string(r) : "unknown"; }
 
+int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+
+// The transport an EP group uses when NF_EP_TRANSPORT is not set.
+constexpr bool kEpNvlinkDefault = false;
+
+// Every rank sends `bytes` bytes from src to every rank (its own slot
+// included) and receives every rank's into dst[world][bytes]: a gather of
+// small host records through device buffers, used at set-up only.
+bool ep_allgather_host(nf_moe* h, const void* mine, size_t bytes, void* all) {
+    NcclApi& api = nccl();
+    ncclComm_t comm = static_cast<ncclComm_t>(h->nccl);
+    const int R = h->ep_world;
+    uint8_t* buf = nullptr;
+    if (cudaMalloc(&buf, bytes * (R + 1)) != cudaSuccess) return false;
+    bool ok = cudaMemcpy(buf, mine, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
+    ncclResult_t r = ok ? api.group_start() : ncclInternalError;
+    for (int p = 0; p < R && r == ncclSuccess; ++p) {
+        r = api.send(buf, bytes, ncclUint8, p, comm, h->stream);
+        if (r == ncclSuccess) r = api.recv(buf + bytes * (p + 1), bytes, ncclUint8, p, comm, h->stream);
+    }
+    const ncclResult_t r2 = ok ? api.group_end() : ncclInternalError;
+    ok = ok && r == ncclSuccess && r2 == ncclSuccess && cudaStreamSynchronize(h->stream) == cudaSuccess &&
+         cudaMemcpy(all, buf + bytes, bytes * R, cudaMemcpyDeviceToHost) == cudaSuccess;
+    cudaFree(buf);
+    return ok;
+}
+
+// Peer-memory transport set-up (collective: every rank calls it after the
+// communicator exists).  Leaves h->ep_p2p false, with nothing mapped, unless
+// every rank exported its mailbox and mapped every other rank's.
+int ep_p2p_setup(nf_moe* h, std::string* err) {
+    const nf_moe_desc& d = h->d;
+    const int R = h->ep_world, me = h->ep_rank;
+    const int64_t H = d.hidden, cap = static_cast<int64_t>(d.max_tokens) * d.top_k;
+    const int64_t ob = d.expert_kind == NF_EXPERTS_NVFP4 ? 2 : 4;
+    EpLayout& L = h->ep_lay;
+    L.cap = static_cast<int>(cap);
+    L.flags_recv = 0;
+    L.flags_ret = 64;
+    L.cnt = 128;
+    L.off = 192;
+    L.e = 256;
+    L.rows = align256(L.e + R * cap * 4);
+    L.ret = align256(L.rows + R * cap * H * 2);
+    L.total = align256(L.ret + cap * H * ob);
+    if (!h->alloc(&h->ep_mbox, L.total) || !h->alloc(&h->ep_epoch, 1) || !h->alloc(&h->ep_done, 2 * kEpMaxRanks) ||
+        !h->alloc(&h->ep_seen, kEpMaxRanks)) {
+        cudaGetLastError();
+        *err = "device allocation failed";
+        return NF_ERR_NOMEM;
+    }
+    if (cudaMemset(h->ep_mbox, 0, L.total) != cudaSuccess || cudaMemset(h->ep_epoch, 0, 4) != cudaSuccess ||
+        cudaMemset(h->ep_done, 0, 2 * kEpMaxRanks * 4) != cudaSuccess ||
+        cudaMemset(h->ep_seen, 0, kEpMaxRanks * 4) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        *err = "mailbox initialisation failed";
+        return NF_ERR_CUDA;
+    }
+    struct Rec {
+        cudaIpcMemHandle_t handle;
+        int32_t ok;
+        int32_t pad[15];
+    };
+    static_assert(sizeof(Rec) % 16 == 0, "record size");
+    // NF_EP_TRANSPORT=nvlink | nccl chooses; unset: kEpNvlinkDefault
+    const char* tr = std::getenv("NF_EP_TRANSPORT");
+    const bool want = tr ? std::strcmp(tr, "nvlink") == 0 : kEpNvlinkDefault;
+    Rec mine{};
+    mine.ok = want && cudaIpcGetMemHandle(&mine.handle, h->ep_mbox) == cudaSuccess;
+    cudaGetLastError();
+    std::vector<Rec> all(static_cast<size_t>(R));
+    if (!ep_allgather_host(h, &mine, sizeof(Rec), all.data())) {
+        *err = "mailbox handle exchange failed";
+        return NF_ERR_CUDA;
+    }
+    int opened = 1;
+    for (int p = 0; p < R; ++p) opened &= all[static_cast<size_t>(p)].ok ? 1 : 0;
+    h->ep_peers.mbox[me] = h->ep_mbox;
+    for (int p = 0; p < R && opened; ++p) {
+        if (p == me) continue;
+        void* ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, all[static_cast<size_t>(p)].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            opened = 0;
+            break;
+        }
+        h->ep_peers.mbox[p] = static_cast<uint8_t*>(ptr);
+    }
+    // every rank must have mapped every peer
+    Rec done{};
+    done.ok = opened;
+    if (!ep_allgather_host(h, &done, sizeof(Rec), all.data())) {
+        *err = "mailbox mapping agreement failed";
+        return NF_ERR_CUDA;
+    }
+    int every = 1;
+    for (int p = 0; p < R; ++p) every &= all[static_cast<size_t>(p)].ok ? 1 : 0;
+    if (!every) {
+        for (int p = 0; p < R; ++p)
+            if (p != me && h->ep_peers.mbox[p]) cudaIpcCloseMemHandle(h->ep_peers.mbox[p]);
+        for (int p = 0; p < kEpMaxRanks; ++p) h->ep_peers.mbox[p] = nullptr;
+        return NF_OK;  // NCCL transport
+    }
+    h->ep_p2p = true;
+    return NF_OK;
+}
+
 }  // namespace
+
+// One forward over the peer-memory transport: no host synchronisation.
+static int ep_forward_p2p(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx,
+                          float* w, StageRec& rec, cudaStream_t s) {
+    const nf_moe_desc& d = h->d;
+    const int H = d.hidden, E = d.experts, K = d.top_k, Is = d.shared_inter, R = h->ep_world, me = h->ep_rank;
+    const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
+    const int out_bytes = H * (fp4 ? 2 : 4);
+    const EpLayout& L = h->ep_lay;
+    int st = NF_OK;
+    cudaError_t e = cudaSuccess;
+    if (T > 0 && Is > 0 && (st = launch_shared_expert(h, x, T, rec, s)) != NF_OK) return st;
+    rec.begin(NF_STAGE_ROUTER, s);
+    if (T > 0) {
+        e = launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, T, H, E, K, d.routed_scaling,
+                          d.normalize, d.n_group, d.topk_group, h->router_w_safe, h->logits, h->scores, h->choices, idx,
+                          w, h->dev_err, s);
+        if (e == cudaSuccess)
+            e = launch_ep_pack(idx, T, K, h->ep_local, R, h->ep_slot, h->ep_send_tok, h->ep_send_e, h->ep_cnt, s);
+    } else {
+        e = cudaMemsetAsync(h->ep_cnt, 0, R * sizeof(int32_t), s);
+    }
+    if (e == cudaSuccess)
+        e = launch_ep_p2p_send(x, h->ep_send_tok, h->ep_send_e, h->ep_cnt, H, R, me, h->ep_peers, L, h->ep_epoch,
+                               h->ep_done, s);
+    if (e == cudaSuccess) e = launch_ep_p2p_recv_wait(h->ep_mbox, L, R, h->ep_epoch, h->ep_seen, h->dev_err, s);
+    if (e != cudaSuccess) return h->cuda_fail(e, "route and send");
+    rec.end(NF_STAGE_ROUTER, s);
+    // this rank's experts over the [world][cap] receive slots (empty slots carry expert -1)
+    nf_moe* in = h->inner;
+    if ((st = launch_routed_experts(in, reinterpret_cast<const uint16_t*>(h->ep_mbox + L.rows),
+                                    reinterpret_cast<const int32_t*>(h->ep_mbox + L.e), R * L.cap, 1, rec, s)) != NF_OK)
+        return h->fail(st, "%s", in->err.c_str());
+    rec.begin(NF_STAGE_COMBINE, s);
+    e = launch_ep_p2p_return(in->down, in->pb.pair_row, out_bytes, R, me, h->ep_peers, L, h->ep_mbox, h->ep_seen,
+                             h->ep_epoch, h->ep_done, s);
+    if (e == cudaSuccess) e = launch_ep_p2p_ret_wait(h->ep_mbox, L, R, h->ep_epoch, h->dev_err, s);
+    if (e != cudaSuccess) return h->cuda_fail(e, "output return");
+    if (T > 0) {
+        if (Is > 0 && (e = cudaStreamWaitEvent(s, h->ev_join, 0)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
+        e = launch_combine(h->ep_mbox + L.ret, fp4, h->ep_slot, w, Is > 0 ? h->sh_out : nullptr, residual, T, K, H, y, s);
+        if (e != cudaSuccess) return h->cuda_fail(e, "combine launch");
+    }
+    rec.end(NF_STAGE_COMBINE, s);
+    return NF_OK;
+}
 
 // Rows, expert ids and outputs of one forward cross the group in three
 // grouped exchanges; `rows` are element counts per peer (host side).
@@ -93,6 +257,7 @@ int ep_forward(nf_moe* h, const uint16_t* x, const float* residual, int T, float
     StageRec rec;
     rec.h = h;
     rec.ev = h->prof_begin(&rec.set);
+    if (h->ep_p2p) return ep_forward_p2p(h, x, residual, T, y, idx, w, rec, s);
     int st = NF_OK;
     cudaError_t e = cudaSuccess;
     ncclResult_t r = ncclSuccess;
@@ -177,6 +342,12 @@ int ep_forward(nf_moe* h, const uint16_t* x, const float* residual, int T, float
 }
 
 void ep_release(nf_moe* h) {
+    for (int p = 0; p < kEpMaxRanks; ++p)
+        if (h->ep_peers.mbox[p] && h->ep_peers.mbox[p] != h->ep_mbox) {
+            cudaSetDevice(h->device);
+            cudaIpcCloseMemHandle(h->ep_peers.mbox[p]);
+            h->ep_peers.mbox[p] = nullptr;
+        }
     if (h->nccl) {
         cudaSetDevice(h->device);
         nccl().comm_destroy(static_cast<ncclComm_t>(h->nccl));
@@ -210,6 +381,11 @@ int nf_ep_unique_id(uint8_t* out, int len) {
     }
     std::memcpy(out, &id, sizeof(id));
     return NF_OK;
+}
+
+int nf_moe_ep_transport(const nf_moe* h) {
+    if (!h || !h->ep_outer) return NF_EP_NONE;
+    return h->ep_p2p ? NF_EP_NVLINK : NF_EP_NCCL;
 }
 
 int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, const uint8_t* group_id, int id_len,
@@ -288,6 +464,13 @@ int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, c
         return NF_ERR_CUDA;
     }
     h->nccl = comm;
+    cudaSetDevice(device);
+    st = ep_p2p_setup(h, &err);
+    cudaSetDevice(prev);
+    if (st != NF_OK) {
+        nf_moe_destroy(h);
+        return st;
+    }
     *out = h;
     return NF_OK;
 }

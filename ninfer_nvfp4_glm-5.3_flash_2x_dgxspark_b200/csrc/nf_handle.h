@@ -100,6 +100,15 @@ struct nf_moe {
     void* ep_back = nullptr;         // [world*Tm*K, H] expert outputs in receive order
     void* ep_ret = nullptr;          // [Tm*K, H] outputs returned, in send order
     int32_t* ep_hcnt = nullptr;      // pinned host copy of ep_cnt
+    // NVLink peer-memory transport (the default when every rank can map every
+    // other rank's mailbox with CUDA IPC; NCCL point-to-point otherwise)
+    bool ep_p2p = false;
+    uint8_t* ep_mbox = nullptr;      // this rank's mailbox (nf::EpLayout)
+    nf::EpLayout ep_lay{};
+    nf::EpPeers ep_peers{};          // every rank's mailbox mapped here (own included)
+    uint32_t* ep_epoch = nullptr;    // forwards completed (device counter, equal on every rank)
+    int32_t* ep_done = nullptr;      // [2 * kEpMaxRanks] last-block counters (send, return)
+    int32_t* ep_seen = nullptr;      // [kEpMaxRanks] rows received from each source this forward
 
     // tensor maps built at finalize
     CUtensorMap tm_a{}, tm_h{}, tm_shh{};

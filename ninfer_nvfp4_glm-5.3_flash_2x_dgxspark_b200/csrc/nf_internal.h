@@ -189,6 +189,28 @@ constexpr int kEpMaxRanks = 8;
 cudaError_t launch_ep_pack(const int32_t* idx, int T, int K, int e_per_rank, int world, int32_t* slot,
                            int32_t* send_tok, int32_t* send_e, int32_t* counts, cudaStream_t st);
 cudaError_t launch_gather_rows(const void* src, const int32_t* map, int n, int row_bytes, void* dst, cudaStream_t st);
+// Expert parallelism over NVLink peer memory (CUDA IPC mailboxes).  A rank's
+// mailbox holds, at these byte offsets: per-source receive flags, per-owner
+// return flags (uint32 epochs), per-source row counts and send offsets, the
+// received rows' destination-local experts [world][cap] and BF16 rows
+// [world][cap][H], and the outputs of this rank's own sent rows [cap][row].
+struct EpLayout {
+    int64_t flags_recv, flags_ret, cnt, off, e, rows, ret, total;
+    int cap;  // rows a source can send to one owner: max_tokens * top_k
+};
+struct EpPeers {
+    uint8_t* mbox[kEpMaxRanks];  // every rank's mailbox mapped into this process (own included)
+};
+cudaError_t launch_ep_p2p_send(const uint16_t* x, const int32_t* send_tok, const int32_t* send_e,
+                               const int32_t* counts, int H, int world, int me, const EpPeers& peers,
+                               const EpLayout& lay, const uint32_t* epoch, int32_t* done, cudaStream_t st);
+cudaError_t launch_ep_p2p_recv_wait(uint8_t* mbox, const EpLayout& lay, int world, const uint32_t* epoch,
+                                    int32_t* seen, int* err, cudaStream_t st);
+cudaError_t launch_ep_p2p_return(const void* down, const int32_t* pair_row, int out_bytes, int world, int me,
+                                 const EpPeers& peers, const EpLayout& lay, const uint8_t* mbox, const int32_t* seen,
+                                 const uint32_t* epoch, int32_t* done, cudaStream_t st);
+cudaError_t launch_ep_p2p_ret_wait(const uint8_t* mbox, const EpLayout& lay, int world, uint32_t* epoch, int* err,
+                                   cudaStream_t st);
 cudaError_t launch_dequant(const uint8_t* packed, const uint8_t* scales, float gscale, int64_t rows, int64_t cols,
                            float* out, cudaStream_t st);
 cudaError_t launch_quantize(const float* x, int64_t rows, int64_t cols, float gscale, uint8_t* codes,

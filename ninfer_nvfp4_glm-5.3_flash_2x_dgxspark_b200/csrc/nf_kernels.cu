@@ -978,7 +978,10 @@ __global__ void permute_hist_kernel(const int32_t* __restrict__ idx, int T, int 
     __syncthreads();
     const int t0 = blockIdx.x * kChunkTok;
     const int n = min(kChunkTok, T - t0) * K;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&cnt[idx[static_cast<int64_t>(t0) * K + i]], 1);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = idx[static_cast<int64_t>(t0) * K + i];
+        if (e >= 0) atomicAdd(&cnt[e], 1);  // e < 0: an empty slot (expert-parallel receive buffers)
+    }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_counts[static_cast<int64_t>(blockIdx.x) * E + e] = cnt[e];
 }
@@ -1036,11 +1039,15 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const int32_t* __rest
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int e = idx[static_cast<int64_t>(t0) * K + i], t = i / K;
-        atomicOr(&s_mask[e * kChunkWords + (t >> 5)], 1u << (t & 31));
+        if (e >= 0) atomicOr(&s_mask[e * kChunkWords + (t >> 5)], 1u << (t & 31));
     }
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int e = idx[static_cast<int64_t>(t0) * K + i], t = i / K;
+        if (e < 0) {
+            pair_row[static_cast<int64_t>(t0) * K + i] = -1;
+            continue;
+        }
         const uint32_t* m = s_mask + e * kChunkWords;
         int rank = __popc(m[t >> 5] & ((1u << (t & 31)) - 1u));
         for (int wd = 0; wd < (t >> 5); ++wd) rank += __popc(m[wd]);
@@ -1104,8 +1111,10 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
     if (item >= static_cast<int64_t>(T) * K * gq) return;
     const int64_t pair = item / gq;
     const int g = static_cast<int>(item - pair * gq);
+    const int row = pair_row[pair];
+    if (row < 0) return;  // an empty slot
     const int e = bf16_mode ? 0 : idx[pair];
-    dispatch_item(x, static_cast<int>(pair / K), g, pair_row[pair], e, bf16_mode ? 0 : counts[e],
+    dispatch_item(x, static_cast<int>(pair / K), g, row, e, bf16_mode ? 0 : counts[e],
                   bf16_mode ? 0 : seg_off[e], gscale, H, bf16_mode, a_codes, a_sf, a_bf16);
 }
 
@@ -1136,6 +1145,7 @@ __global__ void __launch_bounds__(256) permute_dispatch_kernel(
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int e = s_idx[i], t = i / K;
+        if (e < 0) continue;  // an empty slot (expert-parallel receive buffers)
         atomicAdd(&s_cnt[e], 1);
         atomicOr(&s_mask[e * words + (t >> 5)], 1u << (t & 31));
     }
@@ -1144,6 +1154,10 @@ __global__ void __launch_bounds__(256) permute_dispatch_kernel(
     // the rank of pick (t, e) in expert e's segment: e's tokens below t
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int e = s_idx[i], t = i / K;
+        if (e < 0) {
+            s_row[i] = -1;
+            continue;
+        }
         const uint32_t* m = s_mask + e * words;
         int rank = __popc(m[t >> 5] & ((1u << (t & 31)) - 1u));
         for (int wd = 0; wd < (t >> 5); ++wd) rank += __popc(m[wd]);
@@ -1154,11 +1168,12 @@ __global__ void __launch_bounds__(256) permute_dispatch_kernel(
                     tiles_down, meta, mt_done);
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         pair_row[i] = s_row[i];
-        row_token[s_row[i]] = i / K;
+        if (s_row[i] >= 0) row_token[s_row[i]] = i / K;
     }
     const int gq = H / 16;
     for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < n * gq; item += gridDim.x * blockDim.x) {
         const int pair = item / gq, g = item - pair * gq, e = s_idx[pair];
+        if (e < 0) continue;
         dispatch_item(x, pair / K, g, s_row[pair], e, s_cnt[e], s_off[e], gscale, H, bf16_mode, a_codes, a_sf, a_bf16);
     }
 }
@@ -1548,6 +1563,177 @@ cudaError_t launch_gather_rows(const void* src, const int32_t* map, int n, int r
     const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
     gather_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint8_t*>(src), map, n, row_bytes,
                                                static_cast<uint8_t*>(dst));
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Expert parallelism over NVLink peer memory.  Every rank exports one
+// "mailbox" allocation (EpLayout) that its peers map with CUDA IPC; rows go
+// to their owners and outputs come back by plain stores into the peer's
+// mailbox, each direction closed by a flag the writer sets to the forward's
+// epoch (st.release.sys after a system-scope fence) and the reader waits for
+// (ld.acquire.sys, bounded by NF_WAIT_BUDGET_NS).  The epoch is a device
+// counter (every rank runs the same forwards, so the counters agree), which
+// keeps the forward free of host synchronisation and capturable in a graph.
+// One buffer per direction is enough: a rank sends epoch e + 1 only after it
+// received every owner's epoch-e outputs, which each owner returns after its
+// GEMMs consumed all of epoch e's rows.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Bounded wait until *flag >= want (epochs only grow); false after the budget.
+__device__ bool ep_wait_flag(const uint32_t* flag, uint32_t want) {
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (static_cast<int32_t>(ld_acquire_sys(flag) - want) >= 0) return true;
+        if (globaltimer_ns() - t0 > NF_WAIT_BUDGET_NS) return false;
+        __nanosleep(100);
+    }
+}
+
+// Rows of this rank's picks (send order: destination-major) from x into
+// their owners' mailboxes: grid (blocks, world), one destination per y.
+// The last block of a destination publishes the count, this rank's send
+// offset for it, and the flag.
+__global__ void __launch_bounds__(256) ep_p2p_send_kernel(const uint16_t* __restrict__ x,
+                                                          const int32_t* __restrict__ send_tok,
+                                                          const int32_t* __restrict__ send_e,
+                                                          const int32_t* __restrict__ counts, int H, int me,
+                                                          EpPeers peers, EpLayout lay,
+                                                          const uint32_t* __restrict__ epoch, int32_t* __restrict__ done) {
+    const int p = blockIdx.y;
+    int soff = 0;
+    for (int q = 0; q < p; ++q) soff += counts[q];
+    const int cnt = counts[p];
+    const uint32_t ep = *epoch + 1u;
+    uint8_t* dst = peers.mbox[p];
+    const int per_row = H / 8;  // 16-byte pieces of a BF16 row
+    uint4* rows = reinterpret_cast<uint4*>(dst + lay.rows) + static_cast<int64_t>(me) * lay.cap * per_row;
+    int32_t* dst_e = reinterpret_cast<int32_t*>(dst + lay.e) + static_cast<int64_t>(me) * lay.cap;
+    for (int r = blockIdx.x; r < cnt; r += gridDim.x) {
+        const int slot = soff + r;
+        const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(send_tok[slot]) * H);
+        for (int c = threadIdx.x; c < per_row; c += blockDim.x) rows[static_cast<int64_t>(r) * per_row + c] = __ldg(src + c);
+        if (threadIdx.x == 0) dst_e[r] = send_e[slot];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        if (atomicAdd(&done[p], 1) == static_cast<int>(gridDim.x) - 1) {
+            reinterpret_cast<int32_t*>(dst + lay.cnt)[me] = cnt;
+            reinterpret_cast<int32_t*>(dst + lay.off)[me] = soff;
+            __threadfence_system();
+            st_release_sys(reinterpret_cast<uint32_t*>(dst + lay.flags_recv) + me, ep);
+            done[p] = 0;  // ready for the next forward (which follows this kernel in stream order)
+        }
+    }
+}
+
+// Waits for every source's rows of this epoch, records the counts it saw in
+// seen[] (0 for a source that never arrived: the wait gave up and set *err)
+// and marks the unused slots of the receive buffer as empty (expert -1).
+__global__ void __launch_bounds__(256) ep_p2p_recv_wait_kernel(uint8_t* __restrict__ mbox, EpLayout lay, int world,
+                                                               const uint32_t* __restrict__ epoch,
+                                                               int32_t* __restrict__ seen, int* __restrict__ err) {
+    __shared__ int s_cnt[kEpMaxRanks];
+    const uint32_t ep = *epoch + 1u;
+    if (threadIdx.x < world) {
+        int c = 0;
+        if (ep_wait_flag(reinterpret_cast<const uint32_t*>(mbox + lay.flags_recv) + threadIdx.x, ep)) {
+            c = reinterpret_cast<volatile int32_t*>(mbox + lay.cnt)[threadIdx.x];
+            c = max(0, min(c, lay.cap));
+        } else {
+            atomicCAS(err, 0, NF_DEVERR_EP_WAIT);
+        }
+        s_cnt[threadIdx.x] = c;
+        if (blockIdx.x == 0) seen[threadIdx.x] = c;
+    }
+    __syncthreads();
+    int32_t* e = reinterpret_cast<int32_t*>(mbox + lay.e);
+    for (int src = 0; src < world; ++src)
+        for (int j = s_cnt[src] + blockIdx.x * blockDim.x + threadIdx.x; j < lay.cap; j += gridDim.x * blockDim.x)
+            e[static_cast<int64_t>(src) * lay.cap + j] = -1;
+}
+
+// Each received row's expert output (down, in the inner handle's permuted
+// order, pair_row over the [world][cap] receive slots) back into its
+// source's mailbox at the source's send position: grid (blocks, world), one
+// source per y.  Every source gets its flag, also with no rows.
+__global__ void __launch_bounds__(256) ep_p2p_return_kernel(const uint8_t* __restrict__ down,
+                                                            const int32_t* __restrict__ pair_row, int out_bytes, int me,
+                                                            EpPeers peers, EpLayout lay,
+                                                            const uint8_t* __restrict__ mbox,
+                                                            const int32_t* __restrict__ seen,
+                                                            const uint32_t* __restrict__ epoch,
+                                                            int32_t* __restrict__ done) {
+    const int src = blockIdx.y;
+    const int cnt = seen[src];
+    const int off = reinterpret_cast<const int32_t*>(mbox + lay.off)[src];
+    const uint32_t ep = *epoch + 1u;
+    uint8_t* dst = peers.mbox[src];
+    const int per_row = out_bytes / 16;
+    uint4* ret = reinterpret_cast<uint4*>(dst + lay.ret);
+    for (int r = blockIdx.x; r < cnt; r += gridDim.x) {
+        const int row = pair_row[static_cast<int64_t>(src) * lay.cap + r];
+        const uint4* from = reinterpret_cast<const uint4*>(down + static_cast<int64_t>(row) * out_bytes);
+        for (int c = threadIdx.x; c < per_row; c += blockDim.x)
+            ret[static_cast<int64_t>(off + r) * per_row + c] = __ldg(from + c);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        if (atomicAdd(&done[kEpMaxRanks + src], 1) == static_cast<int>(gridDim.x) - 1) {
+            __threadfence_system();
+            st_release_sys(reinterpret_cast<uint32_t*>(dst + lay.flags_ret) + me, ep);
+            done[kEpMaxRanks + src] = 0;
+        }
+    }
+}
+
+// Waits for every owner's outputs of this epoch, then advances the epoch.
+__global__ void ep_p2p_ret_wait_kernel(const uint8_t* __restrict__ mbox, EpLayout lay, int world,
+                                       uint32_t* __restrict__ epoch, int* __restrict__ err) {
+    const uint32_t ep = *epoch + 1u;
+    if (threadIdx.x < world &&
+        !ep_wait_flag(reinterpret_cast<const uint32_t*>(mbox + lay.flags_ret) + threadIdx.x, ep))
+        atomicCAS(err, 0, NF_DEVERR_EP_WAIT);
+    __syncthreads();
+    if (threadIdx.x == 0) *epoch = ep;
+}
+
+cudaError_t launch_ep_p2p_send(const uint16_t* x, const int32_t* send_tok, const int32_t* send_e,
+                               const int32_t* counts, int H, int world, int me, const EpPeers& peers,
+                               const EpLayout& lay, const uint32_t* epoch, int32_t* done, cudaStream_t st) {
+    const int blocks = std::max(1, std::min(64, lay.cap));
+    ep_p2p_send_kernel<<<dim3(blocks, world), 256, 0, st>>>(x, send_tok, send_e, counts, H, me, peers, lay, epoch, done);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_p2p_recv_wait(uint8_t* mbox, const EpLayout& lay, int world, const uint32_t* epoch,
+                                    int32_t* seen, int* err, cudaStream_t st) {
+    const int blocks = std::max(1, std::min(32, (lay.cap + 255) / 256));
+    ep_p2p_recv_wait_kernel<<<blocks, 256, 0, st>>>(mbox, lay, world, epoch, seen, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_p2p_return(const void* down, const int32_t* pair_row, int out_bytes, int world, int me,
+                                 const EpPeers& peers, const EpLayout& lay, const uint8_t* mbox, const int32_t* seen,
+                                 const uint32_t* epoch, int32_t* done, cudaStream_t st) {
+    const int blocks = std::max(1, std::min(64, lay.cap));
+    ep_p2p_return_kernel<<<dim3(blocks, world), 256, 0, st>>>(static_cast<const uint8_t*>(down), pair_row, out_bytes,
+                                                              me, peers, lay, mbox, seen, epoch, done);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_p2p_ret_wait(const uint8_t* mbox, const EpLayout& lay, int world, uint32_t* epoch, int* err,
+                                   cudaStream_t st) {
+    ep_p2p_ret_wait_kernel<<<1, 32, 0, st>>>(mbox, lay, world, epoch, err);
     return cudaGetLastError();
 }
 

@@ -985,7 +985,7 @@ int nf_moe_forward(nf_moe* h, const uint16_t* x, const float* residual, int toke
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     // graphs need a capturable stream, no per-stage events, and a caller
     // that is not capturing already
-    const bool graph = h->use_graphs && !h->ep_outer && s != nullptr && !h->profiling &&
+    const bool graph = h->use_graphs && (!h->ep_outer || h->ep_p2p) && s != nullptr && !h->profiling &&
                        cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone;
     st = graph ? forward_graph(h, x, residual, tokens, y, idx, w, s) : forward_impl(h, x, residual, tokens, y, idx, w, s);
     cudaSetDevice(prev);
@@ -1039,7 +1039,7 @@ int nf_moe_forward_host(nf_moe* h, const float* x_host, const float* res_host, i
         return h->cuda_fail(e, "host input copy");
     }
     const float* res = res_host ? h->res_f32 : nullptr;
-    st = (h->use_graphs && !h->ep_outer && !h->profiling) ? forward_graph(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s)
+    st = (h->use_graphs && (!h->ep_outer || h->ep_p2p) && !h->profiling) ? forward_graph(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s)
                                           : forward_impl(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s);
     if (st == NF_OK) {
         e = cudaMemcpyAsync(y_host, h->y_f32, n * 4, cudaMemcpyDeviceToHost, s);

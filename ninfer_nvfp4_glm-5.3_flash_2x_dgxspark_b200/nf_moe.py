@@ -40,6 +40,7 @@ EXPORTED = [
     "nf_moe_sync", "nf_moe_route", "nf_moe_debug_tensor", "nf_moe_debug_read", "nf_nvfp4_dequantize", "nf_nvfp4_quantize",
     "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck", "nf_moe_set_graph_mode",
     "nf_router_topk_noalloc", "nf_ep_unique_id", "nf_moe_create_ep", "nf_moe_create_dense",
+    "nf_moe_ep_transport",
 ]
 STAGES = ["router", "permute", "gate_up", "down", "shared", "combine"]
 
@@ -92,6 +93,7 @@ def load() -> ctypes.CDLL:
         "nf_ep_unique_id": ([ctypes.c_char_p, I32], I32),
         "nf_moe_create_ep": ([ctypes.POINTER(Desc), I32, I32, I32, ctypes.c_char_p, I32, ctypes.POINTER(P)], I32),
         "nf_moe_create_dense": ([I32, I32, F, I32, I32, ctypes.POINTER(P)], I32),
+        "nf_moe_ep_transport": ([P], I32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -256,6 +258,10 @@ class MoeLayer:
     def route(self, x_dev, tokens: int, logits_dev=None, idx_dev=None, w_dev=None, stream=0) -> None:
         self._check(self.lib.nf_moe_route(self.h, _ptr(x_dev), tokens, _ptr(logits_dev), _ptr(idx_dev),
                                           _ptr(w_dev), stream or None))
+
+    def ep_transport(self) -> str:
+        """"none" (one GPU), "nccl" or "nvlink" (the EP exchange in use)."""
+        return {0: "none", 1: "nccl", 2: "nvlink"}[self.lib.nf_moe_ep_transport(self.h)]
 
     def sync(self, stream=0) -> None:
         self._check(self.lib.nf_moe_sync(self.h, stream or None))

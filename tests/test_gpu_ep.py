@@ -1,7 +1,8 @@
-"""Expert parallelism on 2 GPUs (one process per GPU, NCCL point-to-point
-exchange inside the library) against one GPU holding every expert: the layer
-outputs and routes must be identical bit for bit.  Skipped on fewer than two
-GPUs."""
+"""Expert parallelism on 2 GPUs (one process per GPU) against one GPU holding
+every expert: the layer outputs and routes must be identical bit for bit,
+over both exchanges inside the library -- NVLink peer memory (CUDA IPC
+mailboxes, run in graph mode for several steps) and NCCL point-to-point.
+Skipped on fewer than two GPUs."""
 import os
 import socket
 import sys
@@ -38,8 +39,9 @@ def _tokens(case: str, world: int):
     return lay, np.array_split(x, world)
 
 
-def _rank(rank: int, world: int, port: int, out_dir: str, case: str) -> None:
+def _rank(rank: int, world: int, port: int, out_dir: str, case: str, transport: str) -> None:
     sys.path.insert(0, str(REPO / "tests"))
+    os.environ["NF_EP_TRANSPORT"] = transport
     import torch
     import torch.distributed as dist
 
@@ -53,6 +55,7 @@ def _rank(rank: int, world: int, port: int, out_dir: str, case: str) -> None:
     layer = m.MoeLayer(lay.hidden, lay.experts, lay.top_k, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
                        swiglu_limit=lay.swiglu_limit, max_tokens=max(cap, 1), device=rank, ep=(rank, world, gid[0]))
     layer.bind_layer(lay)
+    got_transport = layer.ep_transport()
     xb = parts[rank]
     T = xb.shape[0]
     x = torch.from_numpy(np.ascontiguousarray(xb).view(np.int16)).cuda() if T else torch.zeros((1, lay.hidden), dtype=torch.int16, device="cuda")
@@ -62,21 +65,34 @@ def _rank(rank: int, world: int, port: int, out_dir: str, case: str) -> None:
     for _ in range(2):  # two steps in a row reuse the buffers
         layer.forward(x, y, T, None, idx, w)
         layer.sync()
-    np.savez(os.path.join(out_dir, f"r{rank}.npz"), y=y.cpu().numpy()[:T], idx=idx.cpu().numpy()[:T], w=w.cpu().numpy()[:T])
+    first = y.cpu().numpy()[:T].copy()
+    if got_transport == "nvlink":
+        # graph replay on a dedicated stream: the epoch flags advance on the device
+        layer.set_graph_mode(True)
+        s = torch.cuda.Stream()
+        y.zero_()
+        torch.cuda.synchronize()
+        for _ in range(4):
+            layer.forward(x, y, T, None, idx, w, stream=s.cuda_stream)
+        layer.sync(s.cuda_stream)
+        assert np.array_equal(y.cpu().numpy()[:T].view(np.uint32), first.view(np.uint32))
+    np.savez(os.path.join(out_dir, f"r{rank}.npz"), y=first, idx=idx.cpu().numpy()[:T], w=w.cpu().numpy()[:T],
+             transport=np.array(got_transport))
     layer.close()
     dist.barrier()
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("transport", ["nvlink", "nccl"])
 @pytest.mark.parametrize("case", ["c1", "uneven", "skewed"])
-def test_ep2_matches_one_gpu(tmp_path, case):
+def test_ep2_matches_one_gpu(tmp_path, case, transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
 
     world = 2
-    mp.start_processes(_rank, args=(world, _free_port(), str(tmp_path), case), nprocs=world, start_method="spawn",
-                       join=True)
+    mp.start_processes(_rank, args=(world, _free_port(), str(tmp_path), case, transport), nprocs=world,
+                       start_method="spawn", join=True)
     m = nfm()
     lay, parts = _tokens(case, world)
     xb = np.concatenate(parts)
@@ -91,6 +107,7 @@ def test_ep2_matches_one_gpu(tmp_path, case):
     layer.forward(x, y, T, None, idx, w)
     layer.sync()
     got = [np.load(tmp_path / f"r{r}.npz") for r in range(world)]
+    assert all(str(g["transport"]) == transport for g in got), [str(g["transport"]) for g in got]
     y_ep = np.concatenate([g["y"] for g in got])
     assert np.array_equal(np.concatenate([g["idx"] for g in got]), idx.cpu().numpy())
     assert np.array_equal(np.concatenate([g["w"] for g in got]).view(np.uint32), w.cpu().numpy().view(np.uint32))
