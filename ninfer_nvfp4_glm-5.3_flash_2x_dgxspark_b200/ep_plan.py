@@ -53,3 +53,28 @@ def pack(idx: np.ndarray, experts: int, world: int) -> SendPlan:
 def receive_offsets(recv_counts: np.ndarray) -> np.ndarray:
     """First received row of each source rank (rows arrive in rank order)."""
     return np.concatenate([[0], np.cumsum(np.asarray(recv_counts, dtype=np.int64))])
+
+
+def mailbox_exchange(plans: list, cap: int):
+    """The NVLink peer-memory exchange (ep_p2p_* kernels) restated over the
+    send plans of every rank (plans[r] = pack(...) of rank r): owner p's
+    receive slots [world][cap] hold, for source s, s's rows for p in s's send
+    order followed by empty slots (expert -1), plus s's send offset for p.
+    Returns, per owner, (expert [world, cap], source slot [world, cap] -- the
+    sender's slot of each row, -1 for an empty slot -- and the offsets [world])
+    so that a row at (s, j) returns to slot offsets[s] + j of rank s."""
+    world = len(plans)
+    out = []
+    for p in range(world):
+        expert = np.full((world, cap), -1, np.int64)
+        src_slot = np.full((world, cap), -1, np.int64)
+        offs = np.zeros(world, np.int64)
+        for s, plan in enumerate(plans):
+            lo, n = int(plan.offsets[p]), int(plan.counts[p])
+            if n > cap:
+                raise ValueError("a source sent more rows than the mailbox holds")
+            expert[s, :n] = plan.send_expert[lo:lo + n]
+            src_slot[s, :n] = np.arange(lo, lo + n)
+            offs[s] = lo
+        out.append((expert, src_slot, offs))
+    return out

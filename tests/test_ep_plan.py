@@ -123,3 +123,40 @@ def test_ep_decomposition_matches_single_rank(tmp_path, world):
     y_ref, _, _ = orc.moe_layer(orc.port(), lay, wl.bf16_bits_to_f32(x_bits))
     y_ep = np.concatenate([np.load(tmp_path / f"y{r}.npy") for r in range(world)])
     assert np.array_equal(y_ep.view(np.uint32), y_ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_mailbox_exchange_returns_every_row_to_its_slot(world):
+    """The NVLink exchange's addressing (receive slots with holes, return at
+    the sender's offset): every pick's expert output lands in the sender's
+    return buffer at that pick's send slot, for balanced and one-sided
+    routing, and empty slots carry no expert."""
+    rng = np.random.default_rng(world)
+    E, K, T = 64, 4, 37
+    per = E // world
+    for skew in (False, True):
+        plans, idxs = [], []
+        for r in range(world):
+            if skew:  # every pick on rank 0's experts
+                idx = np.stack([rng.permutation(per)[:K] for _ in range(T)])
+            else:
+                idx = np.stack([rng.permutation(E)[:K] for _ in range(T)])
+            idxs.append(idx)
+            plans.append(plan.pack(idx, E, world))
+        cap = T * K
+        boxes = plan.mailbox_exchange(plans, cap)
+        # owner p "computes" a row as (global expert, source rank, source slot) and returns it
+        ret = [np.full((cap, 3), -1, np.int64) for _ in range(world)]
+        for p, (expert, src_slot, offs) in enumerate(boxes):
+            assert np.all((expert >= 0) == (src_slot >= 0))
+            assert np.all(expert[expert >= 0] < per)
+            for s in range(world):
+                n = int((expert[s] >= 0).sum())
+                assert np.all(expert[s, n:] == -1)  # rows first, then holes
+                for j in range(n):
+                    ret[s][offs[s] + j] = (p * per + expert[s, j], s, src_slot[s, j])
+        for r in range(world):
+            got = ret[r][plans[r].slot.ravel()]
+            assert np.array_equal(got[:, 0], idxs[r].ravel())
+            assert np.all(got[:, 1] == r)
+            assert np.array_equal(got[:, 2], plans[r].slot.ravel())
