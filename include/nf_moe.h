@@ -273,7 +273,7 @@ NF_API int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int w
  * with bounded-wait epoch flags, no host synchronisation, so EP forwards run
  * in graph mode too; NF_EP_NCCL -- NCCL point-to-point with one host
  * synchronisation for the row counts.  The environment variable
- * NF_EP_TRANSPORT=nvlink or =nccl chooses (NCCL when unset); NVLink falls
+ * NF_EP_TRANSPORT=nvlink or =nccl chooses (NVLink when unset); NVLink falls
  * back to NCCL when some rank cannot map a mailbox.  NF_EP_NONE for a
  * one-GPU handle. */
 enum { NF_EP_NONE = 0, NF_EP_NCCL = 1, NF_EP_NVLINK = 2 };

@@ -90,7 +90,7 @@ const char* nccl_str(ncclResult_t r) { return nccl().error_string ? nccl().error
 int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 
 // The transport an EP group uses when NF_EP_TRANSPORT is not set.
-constexpr bool kEpNvlinkDefault = false;
+constexpr bool kEpNvlinkDefault = true;
 
 // Every rank sends `bytes` bytes from src to every rank (its own slot
 // included) and receives every rank's into dst[world][bytes]: a gather of

@@ -1707,10 +1707,14 @@ __global__ void ep_p2p_ret_wait_kernel(const uint8_t* __restrict__ mbox, EpLayou
     if (threadIdx.x == 0) *epoch = ep;
 }
 
+// Blocks per peer of the row copies: 64 for decode-sized mailboxes, up to
+// 512 (one per 64 rows) for prefill-sized ones.
+static int ep_copy_blocks(int cap) { return std::max(1, std::min(cap, std::max(64, std::min(512, cap / 64)))); }
+
 cudaError_t launch_ep_p2p_send(const uint16_t* x, const int32_t* send_tok, const int32_t* send_e,
                                const int32_t* counts, int H, int world, int me, const EpPeers& peers,
                                const EpLayout& lay, const uint32_t* epoch, int32_t* done, cudaStream_t st) {
-    const int blocks = std::max(1, std::min(64, lay.cap));
+    const int blocks = ep_copy_blocks(lay.cap);
     ep_p2p_send_kernel<<<dim3(blocks, world), 256, 0, st>>>(x, send_tok, send_e, counts, H, me, peers, lay, epoch, done);
     return cudaGetLastError();
 }
@@ -1725,7 +1729,7 @@ cudaError_t launch_ep_p2p_recv_wait(uint8_t* mbox, const EpLayout& lay, int worl
 cudaError_t launch_ep_p2p_return(const void* down, const int32_t* pair_row, int out_bytes, int world, int me,
                                  const EpPeers& peers, const EpLayout& lay, const uint8_t* mbox, const int32_t* seen,
                                  const uint32_t* epoch, int32_t* done, cudaStream_t st) {
-    const int blocks = std::max(1, std::min(64, lay.cap));
+    const int blocks = ep_copy_blocks(lay.cap);
     ep_p2p_return_kernel<<<dim3(blocks, world), 256, 0, st>>>(static_cast<const uint8_t*>(down), pair_row, out_bytes,
                                                               me, peers, lay, mbox, seen, epoch, done);
     return cudaGetLastError();
