@@ -244,13 +244,24 @@ class MoeLayer:
         self._check(self.lib.nf_moe_forward(self.h, _ptr(x_dev), _ptr(residual_dev), tokens, _ptr(y_dev),
                                             _ptr(idx_dev), _ptr(w_dev), stream or None))
 
-    def forward_host(self, x: np.ndarray, residual: np.ndarray | None = None, with_routes: bool = False):
-        """Host fp32 in / fp32 out, the reference's own moe() contract."""
+    def forward_host(self, x: np.ndarray, residual: np.ndarray | None = None, with_routes: bool = False,
+                     out: tuple | None = None):
+        """Host fp32 in / fp32 out, the reference's own moe() contract.  out =
+        (y, idx, w) reuses caller-owned host arrays (page-locked ones make the
+        device-to-host copies direct); idx and w may be None."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         T = x.shape[0]
-        y = np.empty_like(x)
-        idx = np.empty((T, self.desc.top_k), np.int32) if with_routes else None
-        w = np.empty((T, self.desc.top_k), np.float32) if with_routes else None
+        if out is not None:
+            y, idx, w = out
+            for a, shape, dt in ((y, x.shape, np.float32), (idx, (T, self.desc.top_k), np.int32),
+                                 (w, (T, self.desc.top_k), np.float32)):
+                if a is not None and (a.shape != shape or a.dtype != dt or not a.flags["C_CONTIGUOUS"]):
+                    raise ValueError("out arrays must be contiguous with the forward's shapes and dtypes")
+            with_routes = idx is not None or w is not None
+        else:
+            y = np.empty_like(x)
+            idx = np.empty((T, self.desc.top_k), np.int32) if with_routes else None
+            w = np.empty((T, self.desc.top_k), np.float32) if with_routes else None
         res = None if residual is None else np.ascontiguousarray(residual, dtype=np.float32)
         self._check(self.lib.nf_moe_forward_host(self.h, _ptr(x), _ptr(res), T, _ptr(y), _ptr(idx), _ptr(w)))
         return (y, idx, w) if with_routes else y

@@ -115,6 +115,12 @@ def test_forward_host_matches_device_and_is_deterministic():
     yd, _, _ = gpu_forward(layer, x_bits, res)
     assert np.array_equal(ih, i1) and np.array_equal(wh.view(np.uint32), w1.view(np.uint32))
     assert np.array_equal(yh.view(np.uint32), yd.view(np.uint32))
+    # caller-owned (page-locked) output arrays, reused across calls
+    outs = tuple(torch.from_numpy(np.empty_like(a)).pin_memory().numpy() for a in (yh, ih, wh))
+    for _ in range(2):
+        yo, io, wo = layer.forward_host(wl.bf16_bits_to_f32(x_bits), res, out=outs)
+        assert yo is outs[0] and np.array_equal(yo.view(np.uint32), yh.view(np.uint32))
+        assert np.array_equal(io, ih) and np.array_equal(wo.view(np.uint32), wh.view(np.uint32))
     layer.close()
 
 
