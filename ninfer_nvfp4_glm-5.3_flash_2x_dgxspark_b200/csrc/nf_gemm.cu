@@ -45,15 +45,29 @@ constexpr int kSfWarp0 = 2 + kEpiWarps;
 constexpr int kTileQ = 4;  // depth of the producer -> consumer tile queue
 constexpr int kSmallRows = 32;  // A box height for tiles with few rows (decode)
 constexpr int kThreads = 64 + 32 * kEpiWarps + 32 * kSfWarps;
-constexpr int A_STAGE_BYTES = BM * 128;
 constexpr int B_STAGE_BYTES = BN * 128;
 constexpr int SFA_STAGE_BYTES = 4 * 512;   // [k-step][512]
 constexpr int SFB_STAGE_BYTES = 8 * 512;   // [b-block][k-step][512]
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COLS = 256;
 constexpr int SF_COLS = 48;                // per stage: 16 for A, 32 for B
-constexpr int SMEM_TILES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES + SFA_STAGE_BYTES + SFB_STAGE_BYTES);
-constexpr int SMEM_BYTES = 1024 + SMEM_TILES + 512;
+
+// Geometry of one instantiation.  MT = 2 (BF16 only): a CTA tile is two
+// 128-row halves of A sharing each B stage, with the two accumulators in
+// TMEM columns 0-255 and 256-511 (all of TMEM: BF16 needs no scale-factor
+// columns), so a stage moves 64 KB for twice the MMAs of a 48 KB stage;
+// three stages fit in shared memory.
+template <int KIND, int MT>
+struct Geo {
+    static constexpr int kStages = MT == 2 ? 3 : STAGES;
+    static constexpr int kTileM = BM * MT;
+    static constexpr int kAStage = kTileM * 128;
+    static constexpr int kSfaStage = KIND == KIND_NVFP4 ? SFA_STAGE_BYTES : 0;
+    static constexpr int kSfbStage = KIND == KIND_NVFP4 ? SFB_STAGE_BYTES : 0;
+    static constexpr int kSmem = 1024 + kStages * (kAStage + B_STAGE_BYTES + kSfaStage + kSfbStage) + 512;
+    static_assert(MT == 1 || KIND == KIND_BF16, "paired row tiles are BF16 only");
+    static_assert(kSmem <= 227 * 1024, "shared memory");
+};
 
 struct TileInfo {
     int expert, row0, n_block, m_valid;
@@ -62,8 +76,8 @@ struct TileInfo {
 
 // Dense tiles are numbered (n block, K slice, m tile) with m fastest.
 __device__ __forceinline__ void dense_split(const GemmArgs& a, int i, int k_tiles, int* m, int* n, int* ks, int* kt0,
-                                            int* kt1) {
-    const int m_tiles = (a.dense_rows + BM - 1) / BM;
+                                            int* kt1, int tile_m) {
+    const int m_tiles = (a.dense_rows + tile_m - 1) / tile_m;
     const int per_n = m_tiles * max(1, a.k_split);
     *n = i / per_n;
     const int r = i - *n * per_n;
@@ -73,15 +87,15 @@ __device__ __forceinline__ void dense_split(const GemmArgs& a, int i, int k_tile
     *kt1 = a.k_split > 1 ? min(k_tiles, *kt0 + a.kt_per) : k_tiles;
 }
 
-__device__ __forceinline__ TileInfo get_tile(const GemmArgs& a, int i, int k_tiles) {
+__device__ __forceinline__ TileInfo get_tile(const GemmArgs& a, int i, int k_tiles, int tile_m = BM) {
     TileInfo t;
     if (a.dense_rows > 0) {
         int m, n;
-        dense_split(a, i, k_tiles, &m, &n, &t.ks, &t.kt0, &t.kt1);
+        dense_split(a, i, k_tiles, &m, &n, &t.ks, &t.kt0, &t.kt1, tile_m);
         t.expert = 0;
-        t.row0 = m * BM;
+        t.row0 = m * tile_m;
         t.n_block = n;
-        t.m_valid = min(BM, a.dense_rows - m * BM);
+        t.m_valid = min(tile_m, a.dense_rows - m * tile_m);
     } else {
         const NfTile x = a.tiles[i];
         t.expert = x.expert;
@@ -96,10 +110,10 @@ __device__ __forceinline__ TileInfo get_tile(const GemmArgs& a, int i, int k_til
 }
 
 // The K stages of tile i, without reading the tile list (grouped tiles run all of K).
-__device__ __forceinline__ void tile_krange(const GemmArgs& a, int i, int k_tiles, int* kt0, int* kt1) {
+__device__ __forceinline__ void tile_krange(const GemmArgs& a, int i, int k_tiles, int* kt0, int* kt1, int tile_m = BM) {
     if (a.dense_rows > 0 && a.k_split > 1) {
         int m, n, ks;
-        dense_split(a, i, k_tiles, &m, &n, &ks, kt0, kt1);
+        dense_split(a, i, k_tiles, &m, &n, &ks, kt0, kt1, tile_m);
     } else {
         *kt0 = 0;
         *kt1 = k_tiles;
@@ -148,10 +162,16 @@ __device__ __forceinline__ void set_abort(volatile int* cta_abort, int* dev_err,
     atomicCAS(dev_err, 0, code);
 }
 
-template <int KIND, int EPI>
+template <int KIND, int EPI, int MT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tma_small,
                 const __grid_constant__ CUtensorMap tmb, const GemmArgs args) {
+    using G = Geo<KIND, MT>;
+    constexpr int STAGES = G::kStages;  // (shadows the file-wide stage count)
+    constexpr int A_STAGE_BYTES = G::kAStage;
+    constexpr int SFA_STAGE_BYTES = G::kSfaStage;
+    constexpr int SFB_STAGE_BYTES = G::kSfbStage;
+    constexpr int TM = G::kTileM;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -229,11 +249,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         int next = 0, num_tiles = 0;
         TileInfo next_t{};
         auto claim_first = [&]() {
-            num_tiles = args.dense_rows > 0 ? ((args.dense_rows + BM - 1) / BM) * args.n_blocks * max(1, args.k_split)
+            num_tiles = args.dense_rows > 0 ? ((args.dense_rows + TM - 1) / TM) * args.n_blocks * max(1, args.k_split)
                                             : *args.num_tiles_dev;
             if (lane == 0) {
                 next = atomicAdd(args.tile_counter, 1);
-                if (next < num_tiles) next_t = get_tile(args, next, k_tiles);
+                if (next < num_tiles) next_t = get_tile(args, next, k_tiles, TM);
             }
         };
         if (args.early_claim) claim_first();
@@ -310,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             t.kt0 = __shfl_sync(0xffffffffu, t.kt0, 0);
             t.kt1 = __shfl_sync(0xffffffffu, t.kt1, 0);
             // tiles with at most 32 rows of the expert load only those rows of A (four times)
-            const bool small_a = t.m_valid <= kSmallRows;
+            const bool small_a = MT == 1 && t.m_valid <= kSmallRows;
             if (args.mt_wait > 0) {
                 // A (and its scales) are the gate/up GEMM's output for these rows:
                 // generic stores in other CTAs, ordered before these TMA reads by
@@ -341,6 +361,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int xc = KIND == KIND_NVFP4 ? kt * 128 : k0;  // A's K coordinate (bytes or BF16 elements)
                 if (lane == 0) {
                     tma_load_2d(sA + stage * A_STAGE_BYTES, small_a ? &tma_small : &tma, &full[stage], xc, t.row0);
+                } else if (MT == 2 && lane == 4) {
+                    // the tile's second 128 rows (zero-filled past the tensor)
+                    tma_load_2d(sA + stage * A_STAGE_BYTES + BM * 128, &tma, &full[stage], xc, t.row0 + BM);
                 } else if (small_a && lane >= 4 && lane <= 6) {
                     tma_load_2d(sA + stage * A_STAGE_BYTES + (lane - 3) * kSmallRows * 128, &tma_small, &full[stage], xc,
                                 t.row0);
@@ -357,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 issued_parity[stage] = phase;
                 if (++stage == STAGES) stage = 0, phase ^= 1u;
                 if (lane == 0 && kt == max(t.kt0, t.kt1 - 3)) next = atomicAdd(args.tile_counter, 1);
-                if (lane == 0 && kt == t.kt1 - 1 && next < num_tiles) next_t = get_tile(args, next, k_tiles);
+                if (lane == 0 && kt == t.kt1 - 1 && next < num_tiles) next_t = get_tile(args, next, k_tiles, TM);
             }
             first_tile = false;
         }
@@ -400,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 int kt0, kt1;
-                tile_krange(args, i, k_tiles, &kt0, &kt1);
+                tile_krange(args, i, k_tiles, &kt0, &kt1, TM);
                 for (int kt = kt0; kt < kt1; ++kt) {
                     if (!mbar_wait(&full[stage], phase, cta_abort, dev_err)) {
                         set_abort(cta_abort, args.err, NF_DEVERR_WAIT_FULL);
@@ -427,6 +450,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             mma_nvfp4(tmem, adesc, bdesc, idesc, tmem + sfa_col + 4 * s, tmem + sfb_col + 8 * s, acc);
                         else
                             mma_bf16(tmem, adesc, bdesc, idesc, acc);
+                        if (MT == 2)  // the second 128 rows into the second accumulator
+                            mma_bf16(tmem + ACC_COLS, sdesc_sw128(a_base + BM * 128 + 32 * s), bdesc, idesc, acc);
                     }
                     tc_commit(&empty[stage]);
                     if (++stage == STAGES) stage = 0, phase ^= 1u;
@@ -482,8 +507,72 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int ok = epi_mail[2 * (iter & 1) + 1];
             if (++qslot == kTileQ) qslot = 0, qphase ^= 1u;
             if (!ok || tile < 0) break;
-            const TileInfo t = get_tile(args, tile, k_tiles);
+            const TileInfo t = get_tile(args, tile, k_tiles, TM);
             tc_fence_after();
+            if constexpr (MT == 2) {
+                // Two 128-row accumulators (TMEM columns 0-255, 256-511); every
+                // warp hands the accumulator back once its share of the second
+                // one is in registers.
+#pragma unroll 1
+                for (int mt = 0; mt < 2; ++mt) {
+                    const uint32_t tb = tbase + mt * ACC_COLS;
+                    const int row = t.row0 + mt * BM + r;
+                    const bool valid = mt * BM + r < t.m_valid;
+                    const bool live = mt * BM + q * 32 < t.m_valid;
+                    uint32_t v[64];
+                    if (EPI == EPI_SWIGLU_BF16) {
+                        if (live) {
+                            tmem_ld16(tb + 32 * cs, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                            tmem_ld16(tb + 32 * cs + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+                            tmem_ld16(tb + 128 + 32 * cs, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
+                            tmem_ld16(tb + 128 + 32 * cs + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
+                            tmem_wait_ld();
+                        }
+                        if (mt == 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(acc_empty);
+                        }
+                        if (live) {
+                            const float L = args.limit;
+                            uint32_t p[16];
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                p[j] = bf16x2_hw(swiglu_fast(__uint_as_float(v[2 * j]), __uint_as_float(v[32 + 2 * j]), L),
+                                                 swiglu_fast(__uint_as_float(v[2 * j + 1]), __uint_as_float(v[32 + 2 * j + 1]), L));
+                            if (valid) {
+                                uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) +
+                                                                    static_cast<int64_t>(row) * args.out_ld +
+                                                                    t.n_block * 128 + 32 * cs);
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) d[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                            }
+                        }
+                    } else {  // EPI_STORE_F32: 16 columns at a time straight to memory
+                        if (live) {
+                            uint4* d = reinterpret_cast<uint4*>(static_cast<float*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
+                                                                t.n_block * BN + 64 * cs);
+#pragma unroll 1
+                            for (int c = 0; c < 4; ++c) {
+                                tmem_ld16(tb + 64 * cs + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                                tmem_wait_ld();
+                                if (valid) {
+#pragma unroll
+                                    for (int j = 0; j < 4; ++j)
+                                        d[4 * c + j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                                }
+                            }
+                        }
+                        if (mt == 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(acc_empty);
+                        }
+                    }
+                }
+                acc_phase ^= 1u;
+                continue;
+            }
             // A tile of at most 32 rows holds them in every TMEM lane quadrant (A was
             // loaded four times), so for the NVFP4 epilogues all sixteen warps take a
             // share of its columns instead of quadrant 0's four: SwiGLU-quantise, one
@@ -757,23 +846,24 @@ int gemm_grid_size(int device) {
     return sms > 0 ? sms : 148;
 }
 
-template <int KIND, int EPI>
+template <int KIND, int EPI, int MT = 1>
 static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
                               const GemmArgs& args, int grid, bool dependent, cudaStream_t st) {
+    constexpr int SMEM_BYTES = Geo<KIND, MT>::kSmem;
     // the shared memory limit is an attribute of the kernel in each device's context
     static bool attr[kMaxDevices] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     if (!attr[dev]) {
         const cudaError_t e =
-            cudaFuncSetAttribute(gemm_kernel<KIND, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+            cudaFuncSetAttribute(gemm_kernel<KIND, EPI, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
     if (dependent)
-        return launch_dependent(gemm_kernel<KIND, EPI>, dim3(grid), dim3(kThreads), SMEM_BYTES, st, tma, tma_small, tmb,
+        return launch_dependent(gemm_kernel<KIND, EPI, MT>, dim3(grid), dim3(kThreads), SMEM_BYTES, st, tma, tma_small, tmb,
                                 args);
-    gemm_kernel<KIND, EPI><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, tmb, args);
+    gemm_kernel<KIND, EPI, MT><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, tmb, args);
     return cudaGetLastError();
 }
 
@@ -784,6 +874,11 @@ cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, co
         if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16>(tma, tma_small, tmb, args, grid, dependent, st);
         if (args.epi == EPI_STORE_F32) return launch_one<KIND_NVFP4, EPI_STORE_F32>(tma, tma_small, tmb, args, grid, dependent, st);
     } else {
+        if (args.m_pair && args.dense_rows > 0) {
+            if (args.epi == EPI_SWIGLU_BF16) return launch_one<KIND_BF16, EPI_SWIGLU_BF16, 2>(tma, tma_small, tmb, args, grid, dependent, st);
+            if (args.epi == EPI_STORE_F32) return launch_one<KIND_BF16, EPI_STORE_F32, 2>(tma, tma_small, tmb, args, grid, dependent, st);
+            return cudaErrorInvalidValue;
+        }
         if (args.epi == EPI_SWIGLU_BF16) return launch_one<KIND_BF16, EPI_SWIGLU_BF16>(tma, tma_small, tmb, args, grid, dependent, st);
         if (args.epi == EPI_STORE_F32) return launch_one<KIND_BF16, EPI_STORE_F32>(tma, tma_small, tmb, args, grid, dependent, st);
     }

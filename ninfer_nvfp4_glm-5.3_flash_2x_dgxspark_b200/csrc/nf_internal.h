@@ -64,6 +64,7 @@ struct GemmArgs {
     // a reduction kernel sums the slices.  k_split = 1: no split.
     int k_split;
     int kt_per;
+    int m_pair;                // dense BF16 only: 256-row tiles (two 128-row accumulators)
     int64_t out_split_stride;  // elements
     // NVFP4 scale-factor atoms: sfa [128-row block][K/64 atoms]; sfb in tile
     // order, one 4 KB group per (expert, n block, K stage): [2 row halves][4 atoms]

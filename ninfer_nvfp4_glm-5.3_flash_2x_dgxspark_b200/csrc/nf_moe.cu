@@ -30,6 +30,9 @@ namespace {
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
+// Batches from which the shared expert's GEMMs use 256-row tiles.
+constexpr int kSharedPairTokens = 2048;
+
 float e4m3_host(uint8_t bits) {
     const int exponent = (bits >> 3) & 0xf;
     const int mantissa = bits & 0x7;
@@ -725,10 +728,13 @@ int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cud
     sg.out_ld = Is;
     sg.tile_counter = h->shared_counters;
     sg.early_claim = 1;  // dense tiles; the counters were zeroed before the first GEMM
+    // Large batches: 256-row tiles (two accumulators per B stage, 1.5x fewer
+    // shared-memory bytes per MMA); they still give every SM a few tiles.
+    sg.m_pair = T >= kSharedPairTokens ? 1 : 0;
     // Few tiles at decode sizes: a grid of one CTA per tile leaves the other
     // SMs to the routed path (the down GEMM's CTAs launch early and hold
     // their SMs while gate/up finishes: few CTAs hold few SMs).
-    const int m_tiles = (T + 127) / 128;
+    const int m_tiles = sg.m_pair ? (T + 255) / 256 : (T + 127) / 128;
     e = launch_gemm(tm_x, tm_x_s, h->tm_bs_gu, sg, std::min(h->grid, m_tiles * (Is / 128)), false, h->side);
     if (e != cudaSuccess) return h->cuda_fail(e, "shared gate/up GEMM launch");
     sg.epi = EPI_STORE_F32;

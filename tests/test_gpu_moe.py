@@ -230,3 +230,21 @@ def test_misaligned_buffers_are_rejected_before_any_launch():
         layer.forward(xbuf, ybuf.data_ptr() + 4, T)
     layer.sync()
     layer.close()
+
+
+def test_large_batch_shared_expert_paired_tiles():
+    """From 2,048 tokens the shared expert's BF16 GEMMs use 256-row tiles (two
+    accumulators per B stage): its output and the layer's against the oracle,
+    on a ragged batch whose last tile holds 52 rows."""
+    cfg = dict(wl.CONFIGS["c0"])
+    lay = wl.make_layer(cfg, seed=31)
+    x_bits = wl.make_tokens(cfg, seed=31, tokens=2100)
+    T, H = x_bits.shape
+    layer = make_layer(lay, T)
+    y, idx, w = gpu_forward(layer, x_bits)
+    want_y, want_idx, _, _, shared = orc.moe_layer(orc.port(), lay, wl.bf16_bits_to_f32(x_bits), taps=True)
+    assert np.array_equal(idx, want_idx)
+    sh = fetch(layer, "shared", np.float32, T * H).reshape(T, H)
+    assert_close(sh, shared, what="shared expert, 256-row tiles")
+    assert_close(y, want_y, what="layer, T = 2100")
+    layer.close()
