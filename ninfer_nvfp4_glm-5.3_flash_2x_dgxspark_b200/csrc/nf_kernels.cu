@@ -1062,41 +1062,62 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const int32_t* __rest
 // row of pick (t, p) is x[t] quantised with the gate input_scale of expert
 // idx[t, p] (quant_dequant_nvfp4_activation, src/text_forward.cpp:527-550),
 // stored as E2M1 codes plus E4M3 scales in the tcgen05 atom layout.  BF16
-// experts: plain row copies.  One thread per (token, pick, 16-element
-// group): a decode step is 64 x 4 x 128 threads, enough to cover the GPU in
-// one wave (one thread per token and 64 columns left it latency-bound on 16
-// CTAs); the threads of one pick write its row's codes contiguously.
+// experts: plain row copies.  Large batches: one thread per (token,
+// 16-element group), which quantises the group once and writes it to each
+// pick's row (again only for a pick whose expert has another input scale), so
+// the work is per token, not per pick.  Small batches (permute_dispatch_kernel):
+// one thread per (pick, group), so a decode step still covers the GPU.
 // ---------------------------------------------------------------------------
-// One dispatch item: elements [16 g, 16 g + 16) of token t's row, pick to
-// permuted row `row` of expert e whose segment holds `count` rows from `base`.
-__device__ __forceinline__ void dispatch_item(const uint16_t* __restrict__ x, int t, int g, int row, int e, int count,
-                                              int base, const float* __restrict__ gscale, int H, int bf16_mode,
-                                              uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
-                                              uint16_t* __restrict__ a_bf16) {
+// Elements [16 g, 16 g + 16) of token t's row into the permuted row of each of
+// its K picks (pair_row[t K + p], -1 = an empty slot), quantised once with
+// the gate input scale of the first pick and again only for a pick whose
+// expert has another scale (each row's codes are those of its own expert).
+__device__ __forceinline__ void dispatch_token_group(const uint16_t* __restrict__ x, int t, int g, int K,
+                                                     const int32_t* __restrict__ pick_e,
+                                                     const int32_t* __restrict__ pick_row,
+                                                     const int32_t* __restrict__ counts,
+                                                     const int32_t* __restrict__ seg_off,
+                                                     const float* __restrict__ gscale, int H, int bf16_mode,
+                                                     uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
+                                                     uint16_t* __restrict__ a_bf16) {
     const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * H + g * 16);
     const uint4 r0 = __ldg(src), r1 = __ldg(src + 1);
-    if (bf16_mode) {
-        uint4* dst = reinterpret_cast<uint4*>(a_bf16 + static_cast<int64_t>(row) * H + g * 16);
-        dst[0] = r0;
-        dst[1] = r1;
-        return;
-    }
-    const uint32_t u[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
     float v[16];
+    if (!bf16_mode) {
+        const uint32_t u[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        v[2 * j] = bf16_lo(u[j]);
-        v[2 * j + 1] = bf16_hi(u[j]);
+        for (int j = 0; j < 8; ++j) {
+            v[2 * j] = bf16_lo(u[j]);
+            v[2 * j + 1] = bf16_hi(u[j]);
+        }
     }
-    uint32_t codes[2];
-    const uint32_t sf = quantize_group16_fast<true>(v, gscale[e], codes);
-    *reinterpret_cast<uint2*>(a_codes + static_cast<int64_t>(row) * (H / 2) + g * 8) = make_uint2(codes[0], codes[1]);
-    // A GEMM tile with at most 32 rows loads them four times (TMEM lane
-    // quadrants 0-3), so its rows' scales go to all four quadrant columns of
-    // the atom (bytes 4 apart).
-    uint8_t* sfp = a_sf + sf_atom_offset(row, g, H / 16);
-    const int copies = count - ((row - base) & ~127) <= 32 ? 4 : 1;
-    for (int k = 0; k < copies; ++k) sfp[4 * k] = static_cast<uint8_t>(sf);
+    uint32_t codes[2] = {0u, 0u}, sf = 0u;
+    float have = 0.f;  // the scale the held codes were made with (0: none yet)
+    for (int p = 0; p < K; ++p) {
+        const int row = pick_row[p];
+        if (row < 0) continue;
+        if (bf16_mode) {
+            uint4* dst = reinterpret_cast<uint4*>(a_bf16 + static_cast<int64_t>(row) * H + g * 16);
+            dst[0] = r0;
+            dst[1] = r1;
+            continue;
+        }
+        const int e = pick_e[p];
+        const float gs = gscale[e];
+        if (!(have == gs)) {
+            float w[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) w[j] = v[j];
+            sf = quantize_group16_fast<true>(w, gs, codes);
+            have = gs;
+        }
+        *reinterpret_cast<uint2*>(a_codes + static_cast<int64_t>(row) * (H / 2) + g * 8) = make_uint2(codes[0], codes[1]);
+        // a GEMM tile with at most 32 rows loads them four times (TMEM lane
+        // quadrants 0-3), so its rows' scales go to all four quadrant columns
+        uint8_t* sfp = a_sf + sf_atom_offset(row, g, H / 16);
+        const int copies = counts[e] - ((row - seg_off[e]) & ~127) <= 32 ? 4 : 1;
+        for (int k = 0; k < copies; ++k) sfp[4 * k] = static_cast<uint8_t>(sf);
+    }
 }
 
 __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ idx,
@@ -1108,14 +1129,11 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
     pdl_trigger();
     const int gq = H / 16;
     const int64_t item = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-    if (item >= static_cast<int64_t>(T) * K * gq) return;
-    const int64_t pair = item / gq;
-    const int g = static_cast<int>(item - pair * gq);
-    const int row = pair_row[pair];
-    if (row < 0) return;  // an empty slot
-    const int e = bf16_mode ? 0 : idx[pair];
-    dispatch_item(x, static_cast<int>(pair / K), g, row, e, bf16_mode ? 0 : counts[e],
-                  bf16_mode ? 0 : seg_off[e], gscale, H, bf16_mode, a_codes, a_sf, a_bf16);
+    if (item >= static_cast<int64_t>(T) * gq) return;
+    const int64_t t = item / gq;
+    const int g = static_cast<int>(item - t * gq);
+    dispatch_token_group(x, static_cast<int>(t), g, K, idx + t * K, pair_row + t * K, counts, seg_off, gscale, H,
+                         bf16_mode, a_codes, a_sf, a_bf16);
 }
 
 // Permutation and dispatch of a small batch (T * K <= kSmallPairs) in one
@@ -1170,11 +1188,13 @@ __global__ void __launch_bounds__(256) permute_dispatch_kernel(
         pair_row[i] = s_row[i];
         if (s_row[i] >= 0) row_token[s_row[i]] = i / K;
     }
+    // small batches: one thread per (pick, group), so a decode step still
+    // covers the GPU (a group shared by a token's picks is quantised per pick)
     const int gq = H / 16;
     for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < n * gq; item += gridDim.x * blockDim.x) {
-        const int pair = item / gq, g = item - pair * gq, e = s_idx[pair];
-        if (e < 0) continue;
-        dispatch_item(x, pair / K, g, s_row[pair], e, s_cnt[e], s_off[e], gscale, H, bf16_mode, a_codes, a_sf, a_bf16);
+        const int pair = item / gq, g = item - pair * gq;
+        dispatch_token_group(x, pair / K, g, 1, s_idx + pair, s_row + pair, s_cnt, s_off, gscale, H, bf16_mode,
+                             a_codes, a_sf, a_bf16);
     }
 }
 
@@ -1400,7 +1420,7 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
                                  b.pair_row, b.row_token);
         if (e != cudaSuccess) return e;
     }
-    const int64_t items = static_cast<int64_t>(T) * K * (H / 16);
+    const int64_t items = static_cast<int64_t>(T) * (H / 16);
     return launch_dependent(dispatch_kernel, dim3(static_cast<unsigned>((items + 127) / 128)), dim3(128), 0, st, x, idx,
                             static_cast<const int32_t*>(b.pair_row), static_cast<const int32_t*>(b.counts),
                             static_cast<const int32_t*>(b.seg_off), gscale, T, K, H, bf16_mode, b.a_codes, b.a_sf,
