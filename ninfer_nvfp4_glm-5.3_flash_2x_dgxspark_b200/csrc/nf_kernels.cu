@@ -867,6 +867,7 @@ __global__ void __launch_bounds__(kFzCThreads + 32 * PW, 1) router_fused_kernel(
 // ---------------------------------------------------------------------------
 constexpr int kChunkTok = 128;
 constexpr int kSmallPairs = 2048;
+constexpr int kScanCtas = 16;  // CTAs of the large-batch scan (each writes a share of its outputs)
 
 // Segment offsets of the permuted rows (each expert's segment padded to a
 // multiple of 128) and m-tile offsets from per-expert counts in shared memory
@@ -957,18 +958,6 @@ __device__ void segment_outputs(const int32_t* s_cnt, const int32_t* s_off, cons
     }
 }
 
-// Scan and every global output in one CTA; ends with the CTA synchronised.
-__device__ void build_segments(const int32_t* s_cnt, int32_t* s_off, int32_t* s_mt, int E, int nb_gu, int nb_down,
-                               int32_t* __restrict__ counts, int32_t* __restrict__ seg_off,
-                               int32_t* __restrict__ row_token, NfTile* __restrict__ tiles_gu,
-                               NfTile* __restrict__ tiles_down, int32_t* __restrict__ meta,
-                               int32_t* __restrict__ mt_done) {
-    segment_scan(s_cnt, s_off, s_mt, E);
-    segment_outputs(s_cnt, s_off, s_mt, E, nb_gu, nb_down, 0, 1, counts, seg_off, row_token, tiles_gu, tiles_down,
-                    meta, mt_done);
-    __syncthreads();
-}
-
 __global__ void permute_hist_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
                                     int32_t* __restrict__ chunk_counts) {
     pdl_wait();  // launched dependent on the previous kernel
@@ -1002,20 +991,25 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __res
     int32_t* s_cnt = sh;
     int32_t* s_off = s_cnt + E;
     int32_t* s_mt = s_off + E + 1;
+    // Every CTA scans all the counts (a few thousand integers) and writes its
+    // share of the outputs: the chunk bases of chunks c = blockIdx.x mod
+    // gridDim.x, and a part of the segment outputs and tile lists.
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         // the loads are independent: unrolled, eight are in flight at a time
         int32_t run = 0;
 #pragma unroll 8
         for (int c = 0; c < nchunks; ++c) {
             const int32_t n = chunk_counts[static_cast<int64_t>(c) * E + e];
-            chunk_base[static_cast<int64_t>(c) * E + e] = run;
+            if (c % static_cast<int>(gridDim.x) == static_cast<int>(blockIdx.x))
+                chunk_base[static_cast<int64_t>(c) * E + e] = run;
             run += n;
         }
         s_cnt[e] = run;
     }
     __syncthreads();
-    build_segments(s_cnt, s_off, s_mt, E, nb_gu, nb_down, counts, seg_off, row_token, tiles_gu, tiles_down, meta,
-                   mt_done);
+    segment_scan(s_cnt, s_off, s_mt, E);
+    segment_outputs(s_cnt, s_off, s_mt, E, nb_gu, nb_down, blockIdx.x, gridDim.x, counts, seg_off, row_token, tiles_gu,
+                    tiles_down, meta, mt_done);
 }
 
 // Rows of a chunk of kChunkTok tokens.  A token's picks are distinct experts,
@@ -1410,7 +1404,7 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
         cudaError_t e = launch_dependent(permute_hist_kernel, dim3(nchunks), dim3(256), E * sizeof(int32_t), st, idx, T,
                                          K, E, b.chunk_counts);
         if (e == cudaSuccess)
-            e = launch_dependent(permute_scan_kernel, dim3(1), dim3(1024), (3 * E + 2) * sizeof(int32_t), st,
+            e = launch_dependent(permute_scan_kernel, dim3(kScanCtas), dim3(1024), (3 * E + 2) * sizeof(int32_t), st,
                                  static_cast<const int32_t*>(b.chunk_counts), nchunks, E, nb_gu, nb_down, b.chunk_base,
                                  b.counts, b.seg_off, b.row_token, b.tiles_gu, b.tiles_down, b.meta, b.mt_done);
         if (e == cudaSuccess)
