@@ -862,8 +862,10 @@ __global__ void __launch_bounds__(kFzCThreads + 32 * PW, 1) router_fused_kernel(
 // contiguous segment of permuted rows that starts on a multiple of 128 (the
 // GEMM tile height and the scale-factor atom height); inside a segment rows
 // follow token order.  The order is fully deterministic.
-// Small batches (T * K <= kSmallPairs) run in one CTA; large batches use
-// per-chunk histograms, a scan and a per-chunk scatter.
+// Small batches (T * K <= kSmallPairs) run with the dispatch in one kernel
+// whose every CTA rebuilds the permutation; large batches use per-chunk
+// histograms, a scan and a per-chunk scatter.  Picks with expert -1 (empty
+// slots of expert-parallel receive buffers) get no row (pair_row -1).
 // ---------------------------------------------------------------------------
 constexpr int kChunkTok = 128;
 constexpr int kSmallPairs = 2048;
