@@ -272,7 +272,11 @@ private:
         if (end < begin || static_cast<uint64_t>(end) > data_len)
             throw std::runtime_error("tensor data out of range for " + name);
         uint64_t count = 1;
-        for (int64_t d : t.shape) count *= static_cast<uint64_t>(d);
+        for (int64_t d : t.shape) {
+            if (d > 0 && count > (uint64_t{1} << 62) / static_cast<uint64_t>(d))
+                throw std::runtime_error("tensor size mismatch for " + name);  // larger than any shard
+            count *= static_cast<uint64_t>(d);
+        }
         if (count * st_detail::elem_bytes(t.kind) != static_cast<uint64_t>(end - begin))
             throw std::runtime_error("tensor size mismatch for " + name);
         t.data = data + begin;
