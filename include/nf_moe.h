@@ -147,7 +147,9 @@ NF_API int nf_moe_forward(nf_moe* handle, const uint16_t* x_dev, const float* re
  * moe(prefix, x, y) src/text_forward.cpp:924): copies x (BF16-valued F32,
  * rounded to BF16 on the device) and residual to the device, runs the layer
  * on the handle's internal stream, copies y (and the routes when the
- * pointers are not NULL) back and synchronises. */
+ * pointers are not NULL) back and synchronises.  In graph mode, with every
+ * host buffer page-locked, the copies and the layer replay as one graph per
+ * distinct set of buffers. */
 NF_API int nf_moe_forward_host(nf_moe* handle, const float* x_host, const float* residual_host, int tokens, float* y_host,
                         int32_t* topk_idx_host, float* topk_w_host);
 /* Graph mode (off by default): nf_moe_forward captures its launches for each

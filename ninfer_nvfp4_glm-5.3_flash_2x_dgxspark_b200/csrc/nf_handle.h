@@ -126,6 +126,7 @@ struct nf_moe {
         int T;
         cudaStream_t s;
         cudaGraphExec_t exec;
+        bool host;  // a host-buffer forward (copies included; the pointers are host pointers)
     };
     static constexpr size_t kMaxGraphs = 16;
     bool use_graphs = false;

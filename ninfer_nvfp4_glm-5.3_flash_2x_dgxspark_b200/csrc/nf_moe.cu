@@ -948,7 +948,7 @@ int nf_moe_stage_times(nf_moe* h, float* ms_out, int* forwards) {
 static int forward_graph(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx, float* w,
                          cudaStream_t s) {
     for (auto& g : h->graphs)
-        if (g.x == x && g.res == residual && g.y == y && g.idx == idx && g.w == w && g.T == T && g.s == s) {
+        if (!g.host && g.x == x && g.res == residual && g.y == y && g.idx == idx && g.w == w && g.T == T && g.s == s) {
             const cudaError_t e = cudaGraphLaunch(g.exec, s);
             return e == cudaSuccess ? NF_OK : h->cuda_fail(e, "graph launch");
         }
@@ -970,7 +970,7 @@ static int forward_graph(nf_moe* h, const uint16_t* x, const float* residual, in
         cudaGraphExecDestroy(h->graphs.front().exec);
         h->graphs.erase(h->graphs.begin());
     }
-    h->graphs.push_back({x, residual, y, idx, w, T, s, exec});
+    h->graphs.push_back({x, residual, y, idx, w, T, s, exec, false});
     e = cudaGraphLaunch(exec, s);
     return e == cudaSuccess ? NF_OK : h->cuda_fail(e, "graph launch");
 }
@@ -1024,6 +1024,36 @@ int nf_moe_sync(nf_moe* h, void* stream) {
     return NF_OK;
 }
 
+// The host-buffer forward's device work on s: input copies and BF16
+// conversion, the layer (inner_graph: through forward_graph), output copies.
+static int host_forward_enqueue(nf_moe* h, const float* x_host, const float* res_host, int tokens, float* y_host,
+                                int32_t* idx_host, float* w_host, cudaStream_t s, bool inner_graph) {
+    const int64_t n = static_cast<int64_t>(tokens) * h->d.hidden;
+    const int64_t nk = static_cast<int64_t>(tokens) * h->d.top_k;
+    cudaError_t e = cudaMemcpyAsync(h->x_f32, x_host, n * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && res_host) e = cudaMemcpyAsync(h->res_f32, res_host, n * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = launch_f32_to_bf16(h->x_f32, n, h->x_bf16, s);
+    if (e != cudaSuccess) return h->cuda_fail(e, "host input copy");
+    const float* res = res_host ? h->res_f32 : nullptr;
+    int st = inner_graph ? forward_graph(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s)
+                         : forward_impl(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s);
+    if (st != NF_OK) return st;
+    e = cudaMemcpyAsync(y_host, h->y_f32, n * 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && idx_host) e = cudaMemcpyAsync(idx_host, h->topk_idx, nk * 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && w_host) e = cudaMemcpyAsync(w_host, h->topk_w, nk * 4, cudaMemcpyDeviceToHost, s);
+    return e == cudaSuccess ? NF_OK : h->cuda_fail(e, "host output copy");
+}
+
+static bool page_locked(const void* p) {
+    if (!p) return true;
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
 int nf_moe_forward_host(nf_moe* h, const float* x_host, const float* res_host, int tokens, float* y_host,
                         int32_t* idx_host, float* w_host) {
     int st = check_forward_args(h, x_host, tokens, false);
@@ -1031,28 +1061,45 @@ int nf_moe_forward_host(nf_moe* h, const float* x_host, const float* res_host, i
     if (!y_host) return h->fail(NF_ERR_INVALID, "null output");
     if (h->dense && (idx_host || w_host)) return h->fail(NF_ERR_INVALID, "a dense MLP has no routes: pass NULL top-k pointers");
     if (tokens == 0 && !h->ep_outer) return NF_OK;  // an EP rank still takes part in the exchanges
-    const int64_t n = static_cast<int64_t>(tokens) * h->d.hidden;
-    const int64_t nk = static_cast<int64_t>(tokens) * h->d.top_k;
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
     cudaStream_t s = h->stream;
-    cudaError_t e = cudaMemcpyAsync(h->x_f32, x_host, n * 4, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess && res_host) e = cudaMemcpyAsync(h->res_f32, res_host, n * 4, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = launch_f32_to_bf16(h->x_f32, n, h->x_bf16, s);
-    if (e != cudaSuccess) {
+    const bool graphs = h->use_graphs && (!h->ep_outer || h->ep_p2p) && !h->profiling;
+    // With page-locked host buffers the copies join the layer in one graph
+    // (one launch per call); otherwise they are enqueued around it.
+    if (graphs && page_locked(x_host) && page_locked(res_host) && page_locked(y_host) && page_locked(idx_host) &&
+        page_locked(w_host)) {
+        cudaGraphExec_t exec = nullptr;
+        for (auto& g : h->graphs)
+            if (g.host && g.x == x_host && g.res == res_host && g.y == y_host && g.idx == idx_host && g.w == w_host &&
+                g.T == tokens && g.s == s)
+                exec = g.exec;
+        cudaError_t e = cudaSuccess;
+        if (!exec) {
+            e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+            if (e == cudaSuccess) {
+                st = host_forward_enqueue(h, x_host, res_host, tokens, y_host, idx_host, w_host, s, false);
+                cudaGraph_t graph = nullptr;
+                e = cudaStreamEndCapture(s, &graph);
+                if (st == NF_OK && e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+                if (graph) cudaGraphDestroy(graph);
+                if (st == NF_OK && e == cudaSuccess) {
+                    if (h->graphs.size() >= nf_moe::kMaxGraphs) {
+                        cudaGraphExecDestroy(h->graphs.front().exec);
+                        h->graphs.erase(h->graphs.begin());
+                    }
+                    h->graphs.push_back({x_host, res_host, y_host, idx_host, w_host, tokens, s, exec, true});
+                }
+            }
+        }
+        if (st == NF_OK && e == cudaSuccess) e = cudaGraphLaunch(exec, s);
         cudaSetDevice(prev);
-        return h->cuda_fail(e, "host input copy");
+        if (st != NF_OK) return st;
+        if (e != cudaSuccess) return h->cuda_fail(e, "host-buffer graph");
+        return nf_moe_sync(h, s);
     }
-    const float* res = res_host ? h->res_f32 : nullptr;
-    st = (h->use_graphs && (!h->ep_outer || h->ep_p2p) && !h->profiling) ? forward_graph(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s)
-                                          : forward_impl(h, h->x_bf16, res, tokens, h->y_f32, nullptr, nullptr, s);
-    if (st == NF_OK) {
-        e = cudaMemcpyAsync(y_host, h->y_f32, n * 4, cudaMemcpyDeviceToHost, s);
-        if (e == cudaSuccess && idx_host) e = cudaMemcpyAsync(idx_host, h->topk_idx, nk * 4, cudaMemcpyDeviceToHost, s);
-        if (e == cudaSuccess && w_host) e = cudaMemcpyAsync(w_host, h->topk_w, nk * 4, cudaMemcpyDeviceToHost, s);
-        if (e != cudaSuccess) st = h->cuda_fail(e, "host output copy");
-    }
+    st = host_forward_enqueue(h, x_host, res_host, tokens, y_host, idx_host, w_host, s, graphs);
     cudaSetDevice(prev);
     if (st != NF_OK) return st;
     return nf_moe_sync(h, s);

@@ -121,6 +121,16 @@ def test_forward_host_matches_device_and_is_deterministic():
         yo, io, wo = layer.forward_host(wl.bf16_bits_to_f32(x_bits), res, out=outs)
         assert yo is outs[0] and np.array_equal(yo.view(np.uint32), yh.view(np.uint32))
         assert np.array_equal(io, ih) and np.array_equal(wo.view(np.uint32), wh.view(np.uint32))
+    # graph mode with every host buffer page-locked: copies and layer replay as one graph
+    layer.set_graph_mode(True)
+    xp = torch.from_numpy(wl.bf16_bits_to_f32(x_bits)).pin_memory().numpy()
+    rp = torch.from_numpy(res).pin_memory().numpy()
+    for _ in range(3):
+        for a in outs:
+            a.fill(0)
+        yo, io, wo = layer.forward_host(xp, rp, out=outs)
+        assert np.array_equal(yo.view(np.uint32), yh.view(np.uint32))
+        assert np.array_equal(io, ih) and np.array_equal(wo.view(np.uint32), wh.view(np.uint32))
     layer.close()
 
 
