@@ -68,3 +68,19 @@ def test_python_layer_raises_with_message_without_gpu():
     m = nfm()
     with pytest.raises(RuntimeError):
         m.MoeLayer(hidden=100, experts=8, top_k=2, inter=128, shared_inter=128)
+
+
+def test_dense_and_ep_queries_without_gpu():
+    """The dense MLP's create rejects shapes the GEMMs cannot tile before any
+    device call, and the EP transport query answers for a NULL handle."""
+    m = nfm()
+    lib = m.load()
+    h = ctypes.c_void_p()
+    for hidden, inter, max_tokens in ((100, 512, 8), (256, 96, 8), (256, 512, 0)):
+        st = lib.nf_moe_create_dense(hidden, inter, 10.0, max_tokens, 0, ctypes.byref(h))
+        assert st != 0 and not h.value
+        assert lib.nf_moe_last_error(None)
+    assert lib.nf_moe_create_dense(256, 512, 10.0, 8, 0, None) == 1
+    assert lib.nf_moe_ep_transport(None) == 0
+    with pytest.raises(RuntimeError):
+        m.DenseMlp(256, 100)
