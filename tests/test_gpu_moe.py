@@ -258,3 +258,39 @@ def test_large_batch_shared_expert_paired_tiles():
     assert_close(sh, shared, what="shared expert, 256-row tiles")
     assert_close(y, want_y, what="layer, T = 2100")
     layer.close()
+
+
+def test_bf16_experts_c1_against_oracle():
+    """The BF16 routed experts (the layer-45 form, whose oracle is mlp_bf16 per
+    expert) at the decode batch's full shapes: routes bit-exact, layer output
+    and residual form within the tolerance."""
+    lay, x_bits = wl.config_layer("c1", bf16_experts=True)
+    x = wl.bf16_bits_to_f32(x_bits)
+    layer = make_layer(lay, x_bits.shape[0])
+    y, idx, w = gpu_forward(layer, x_bits)
+    want_y, want_idx, want_w = orc.moe_layer(orc.port(), lay, x)
+    assert np.array_equal(idx, want_idx)
+    assert np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
+    assert_close(y, want_y, what="c1 BF16 experts")
+    res = residual_for(x_bits)
+    yr, _, _ = gpu_forward(layer, x_bits, res)
+    want_r, _, _ = orc.moe_layer(orc.port(), lay, x, res)
+    assert_close(yr, want_r, what="c1 BF16 experts + residual")
+    layer.close()
+
+
+def test_group_limited_routing_through_the_layer():
+    """Group-limited top-k (8 groups of 8 experts, 4 kept) through the whole
+    layer: routes bit-exact against the oracle's group-limited selection and
+    the output within the tolerance."""
+    lay, x_bits = wl.config_layer("c1")
+    x = wl.bf16_bits_to_f32(x_bits)
+    layer = make_layer(lay, x_bits.shape[0], n_group=8, topk_group=4)
+    y, idx, w = gpu_forward(layer, x_bits)
+    want_y, want_idx, want_w = orc.moe_layer(orc.port(), lay, x, n_group=8, topk_group=4)
+    assert np.array_equal(idx, want_idx)
+    assert np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
+    # every pick lies in one of the token's 4 kept groups
+    assert np.all(np.array([np.unique(r // 8).size for r in idx]) <= 4)
+    assert_close(y, want_y, what="c1 group-limited")
+    layer.close()
