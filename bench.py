@@ -12,13 +12,15 @@ needed between steps).  `value` is tokens/s of the whole job; the line also
 carries us/layer, the per-stage device times, the HBM roofline of the
 dominant kernel (the grouped gate/up GEMM), the end-to-end number through
 the host-buffer C-ABI call, the reference CPU path timed on this host, and a
-secondary prefill measurement (configs[2], 8192 tokens, tensor roofline).
+secondary prefill measurement (configs[2], 8192 tokens, tensor roofline) and
+the dense NVFP4 MLP of configs[4] (decode and prefill batches).
 
 With N > 1 (torchrun), the layer is expert-parallel: each rank owns E/N
 experts and brings its own 64-token decode batch (weak scaling: tokens per
-GPU fixed); rows travel to the experts' owners and back over NCCL inside the
-library.  value sums the tokens of all ranks over the max-over-ranks device
-time.
+GPU fixed); rows travel to the experts' owners and back inside the library,
+over NVLink peer memory (NCCL point-to-point when the ranks cannot map each
+other's buffers; config.ep_transport says which).  value sums the tokens of
+all ranks over the max-over-ranks device time.
 
 --impl reference times the reference's own CPU implementation (its sources
 compiled under oracle/_ref, else the C restatement) on this host's cores over
