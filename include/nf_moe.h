@@ -277,7 +277,9 @@ NF_API int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int w
  * synchronisation for the row counts.  The environment variable
  * NF_EP_TRANSPORT=nvlink or =nccl chooses (NVLink when unset); NVLink falls
  * back to NCCL when some rank cannot map a mailbox.  NF_EP_NONE for a
- * one-GPU handle. */
+ * one-GPU handle.  Over NVLink a rank writes into its peers' mailboxes, so
+ * destroy the handles of a group only after every rank's last forward has
+ * completed (for example after a host barrier). */
 enum { NF_EP_NONE = 0, NF_EP_NCCL = 1, NF_EP_NVLINK = 2 };
 NF_API int nf_moe_ep_transport(const nf_moe* handle);
 
