@@ -78,6 +78,7 @@ def _rank(rank: int, world: int, port: int, out_dir: str, case: str, transport: 
         assert np.array_equal(y.cpu().numpy()[:T].view(np.uint32), first.view(np.uint32))
     np.savez(os.path.join(out_dir, f"r{rank}.npz"), y=first, idx=idx.cpu().numpy()[:T], w=w.cpu().numpy()[:T],
              transport=np.array(got_transport))
+    dist.barrier()  # every rank's last forward is done before any handle of the group goes
     layer.close()
     dist.barrier()
     dist.destroy_process_group()
