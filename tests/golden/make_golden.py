@@ -1,10 +1,13 @@
-"""Generates tests/golden/c0_reference.npz: the reference's own outputs
-(oracle/_ref, compiled from the reference's sources) on the seeded tiny
-configuration c0, plus SHA-256 pins of the generated inputs.
+"""Generates the golden files from the reference's own outputs (oracle/_ref,
+compiled from the reference's sources), with SHA-256 pins of the generated
+inputs:
+  c0_reference.npz     the MoE layer on the seeded tiny configuration c0
+  dense_reference.npz  the dense NVFP4 MLP (dense_mlp) on a seeded small shape
 
 Run in a container that holds the reference tree:
-    python tests/golden/make_golden.py
-The GPU box has no reference tree; tests compare against this file there.
+    python tests/golden/make_golden.py            # both files
+    python tests/golden/make_golden.py dense      # the dense file only
+The GPU box has no reference tree; tests compare against these files there.
 """
 import hashlib
 import sys
@@ -66,5 +69,38 @@ def main():
     print("wrote", HERE / "c0_reference.npz")
 
 
+DENSE_SHAPE = dict(hidden=256, inter=512, tokens=16, seed=40)
+
+
+def dense_case():
+    """The dense golden case: (layer, token bits, residual)."""
+    wl = workload()
+    c = DENSE_SHAPE
+    lay = wl.make_dense_layer(c["hidden"], c["inter"], c["seed"])
+    x_bits = wl.make_tokens(dict(hidden=c["hidden"], tokens=c["tokens"]), c["seed"])
+    return lay, x_bits, residual_for(x_bits)
+
+
+def dense_digest(lay, x_bits) -> str:
+    return digest(x_bits, lay.gate_packed, lay.gate_scales, lay.up_packed, lay.up_scales, lay.down_packed,
+                  lay.down_scales, np.array([lay.gate_ws2, lay.gate_in, lay.up_ws2, lay.up_in, lay.down_ws2,
+                                             lay.down_in], np.float32))
+
+
+def main_dense():
+    orc, wl = oracle(), workload()
+    ref = orc.ref()
+    if ref is None:
+        raise SystemExit("oracle/_ref/libnf_ref.so is missing: run make -C oracle with the reference tree present")
+    lay, x_bits, res = dense_case()
+    x = wl.bf16_bits_to_f32(x_bits)
+    out = {"inputs_sha256": np.array(dense_digest(lay, x_bits)), "residual_sha256": np.array(digest(res)),
+           "y": orc.dense_mlp(ref, lay, x), "y_residual": orc.dense_mlp(ref, lay, x, res)}
+    np.savez_compressed(HERE / "dense_reference.npz", **out)
+    print("wrote", HERE / "dense_reference.npz")
+
+
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] != ["dense"]:
+        main()
+    main_dense()

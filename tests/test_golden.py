@@ -37,3 +37,18 @@ def test_port_quantiser_matches_reference_golden():
     x = wl.bf16_bits_to_f32(x_bits)
     fake, _, _ = orc.quant_codes(orc.port(), x, float(lay.gate_in[0]))
     assert np.array_equal(fake.view(np.uint32), GOLDEN["quant_fake"].view(np.uint32))
+
+
+def test_dense_inputs_pinned_and_port_matches_reference_golden():
+    """The dense MLP (dense_mlp, src/text_forward.cpp:909-915): the seeded
+    inputs are the ones the golden file was made from, and the restatement
+    gives the reference's bits with and without the residual."""
+    from golden.make_golden import dense_case, dense_digest
+
+    g = np.load(Path(__file__).resolve().parent / "golden" / "dense_reference.npz")
+    lay, x_bits, res = dense_case()
+    assert dense_digest(lay, x_bits) == str(g["inputs_sha256"]), "dense input generator changed"
+    assert digest(res) == str(g["residual_sha256"])
+    x = wl.bf16_bits_to_f32(x_bits)
+    assert np.array_equal(orc.dense_mlp(orc.port(), lay, x).view(np.uint32), g["y"].view(np.uint32))
+    assert np.array_equal(orc.dense_mlp(orc.port(), lay, x, res).view(np.uint32), g["y_residual"].view(np.uint32))

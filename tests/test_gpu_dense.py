@@ -135,3 +135,19 @@ def test_dense_bind_from_store_and_errors():
     fresh.close()
     with pytest.raises(m.NfError):
         m.DenseMlp(256, 100)
+
+
+def test_dense_against_reference_golden():
+    """The GPU dense MLP against the reference's own outputs (committed golden
+    file, no oracle involved), with and without the residual."""
+    from pathlib import Path
+
+    from golden.make_golden import dense_case
+
+    g = np.load(Path(__file__).resolve().parent / "golden" / "dense_reference.npz")
+    lay, x_bits, res = dense_case()
+    mlp = m.DenseMlp(lay.hidden, lay.inter, swiglu_limit=lay.swiglu_limit, max_tokens=x_bits.shape[0])
+    mlp.bind_layer(lay)
+    assert_close(gpu_forward(mlp, x_bits), g["y"], what="dense vs reference golden")
+    assert_close(gpu_forward(mlp, x_bits, res), g["y_residual"], what="dense + residual vs reference golden")
+    mlp.close()
