@@ -187,6 +187,14 @@ int ep_p2p_setup(nf_moe* h, std::string* err) {
         for (int p = 0; p < R; ++p)
             if (p != me && h->ep_peers.mbox[p]) cudaIpcCloseMemHandle(h->ep_peers.mbox[p]);
         for (int p = 0; p < kEpMaxRanks; ++p) h->ep_peers.mbox[p] = nullptr;
+        // every rank falls back together; once all have closed their mappings
+        // (the exchange below is the barrier) the mailbox goes
+        if (!ep_allgather_host(h, &done, sizeof(Rec), all.data())) {
+            *err = "mailbox release agreement failed";
+            return NF_ERR_CUDA;
+        }
+        h->release(h->ep_mbox);
+        h->ep_mbox = nullptr;
         return NF_OK;  // NCCL transport
     }
     h->ep_p2p = true;
@@ -438,14 +446,10 @@ int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, c
     cudaSetDevice(device);
     const int64_t H = d.hidden, pairs = static_cast<int64_t>(d.max_tokens) * d.top_k, cap = world * pairs;
     const int64_t ob = d.expert_kind == NF_EXPERTS_NVFP4 ? 2 : 4;
-    uint8_t* back = nullptr;
-    uint8_t* ret = nullptr;
-    bool ok = h->alloc(&h->ep_send, pairs * H) && h->alloc(&h->ep_send_e, pairs) && h->alloc(&h->ep_send_tok, pairs) &&
-              h->alloc(&h->ep_slot, pairs) && h->alloc(&h->ep_cnt, 2 * world) && h->alloc(&h->ep_recv, cap * H) &&
-              h->alloc(&h->ep_recv_e, cap) && h->alloc(&back, cap * H * ob) && h->alloc(&ret, pairs * H * ob);
-    h->ep_back = back;
-    h->ep_ret = ret;
-    ok = ok && cudaMallocHost(&h->ep_hcnt, 2 * world * sizeof(int32_t)) == cudaSuccess;
+    // the send layout, used by both transports (the NCCL transport's own
+    // buffers follow once the group has chosen it)
+    bool ok = h->alloc(&h->ep_send_e, pairs) && h->alloc(&h->ep_send_tok, pairs) && h->alloc(&h->ep_slot, pairs) &&
+              h->alloc(&h->ep_cnt, 2 * world);
     if (!ok) {
         cudaGetLastError();
         cudaSetDevice(prev);
@@ -466,6 +470,21 @@ int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, c
     h->nccl = comm;
     cudaSetDevice(device);
     st = ep_p2p_setup(h, &err);
+    if (st == NF_OK && !h->ep_p2p) {
+        // NCCL transport: packed rows, receive and return buffers, host counts
+        uint8_t* back = nullptr;
+        uint8_t* ret = nullptr;
+        ok = h->alloc(&h->ep_send, pairs * H) && h->alloc(&h->ep_recv, cap * H) && h->alloc(&h->ep_recv_e, cap) &&
+             h->alloc(&back, cap * H * ob) && h->alloc(&ret, pairs * H * ob) &&
+             cudaMallocHost(&h->ep_hcnt, 2 * world * sizeof(int32_t)) == cudaSuccess;
+        h->ep_back = back;
+        h->ep_ret = ret;
+        if (!ok) {
+            cudaGetLastError();
+            err = "device allocation failed";
+            st = NF_ERR_NOMEM;
+        }
+    }
     cudaSetDevice(prev);
     if (st != NF_OK) {
         nf_moe_destroy(h);

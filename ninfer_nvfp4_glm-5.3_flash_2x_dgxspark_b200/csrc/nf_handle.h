@@ -189,6 +189,15 @@ struct nf_moe {
         *p = static_cast<T*>(q);
         return true;
     }
+    // frees one allocation of the handle before destroy
+    void release(void* p) {
+        for (size_t i = 0; i < allocs.size(); ++i)
+            if (allocs[i].p == p) {
+                cudaFree(p);
+                allocs.erase(allocs.begin() + static_cast<std::ptrdiff_t>(i));
+                return;
+            }
+    }
     size_t bytes_of(const void* p) const {
         for (const auto& a : allocs)
             if (a.p == p) return a.bytes;
