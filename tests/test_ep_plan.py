@@ -65,7 +65,7 @@ def _exchange(dist, send: list, recv_shapes: list, dtype, rank: int, world: int)
     return [o if isinstance(o, np.ndarray) else o.numpy() for o in out]
 
 
-def _ep_rank(rank: int, world: int, port: int, out_dir: str) -> None:
+def _ep_rank(rank: int, world: int, port: int, out_dir: str, transport: str) -> None:
     sys.path.insert(0, str(REPO / "tests"))
     import torch
     import torch.distributed as dist
@@ -83,23 +83,60 @@ def _ep_rank(rank: int, world: int, port: int, out_dir: str) -> None:
     # 2. send rows to the experts' owners in (destination, token, pick) order
     sp = plan.pack(idx, E, world)
     rows = x[sp.send_token]
-    counts = _exchange(dist, [np.array([c], np.int64) for c in sp.counts], [(1,)] * world, torch.int64, rank, world)
-    rc = np.array([int(c[0]) for c in counts])
-    send_rows = [rows[sp.offsets[p]:sp.offsets[p + 1]] for p in range(world)]
-    send_e = [sp.send_expert[sp.offsets[p]:sp.offsets[p + 1]] for p in range(world)]
-    recv_rows = _exchange(dist, send_rows, [(int(c), H) for c in rc], torch.float32, rank, world)
-    recv_e = _exchange(dist, send_e, [(int(c),) for c in rc], torch.int64, rank, world)
-    # 3. the owned experts on the received rows
     base = rank * (E // world)
-    outs = []
-    for p in range(world):
-        o = np.zeros((rc[p], H), np.float32)
-        for i in range(rc[p]):
-            o[i] = orc.expert_forward(lay, base + int(recv_e[p][i]), recv_rows[p][i])[1]
-        outs.append(o)
-    # 4. outputs back to their sources, in send order
-    back = _exchange(dist, outs, [(int(c), H) for c in sp.counts], torch.float32, rank, world)
-    ret = np.concatenate(back) if back else np.zeros((0, H), np.float32)
+    if transport == "nccl":
+        # counts first, then exactly the rows that exist (the NCCL transport)
+        counts = _exchange(dist, [np.array([c], np.int64) for c in sp.counts], [(1,)] * world, torch.int64, rank, world)
+        rc = np.array([int(c[0]) for c in counts])
+        send_rows = [rows[sp.offsets[p]:sp.offsets[p + 1]] for p in range(world)]
+        send_e = [sp.send_expert[sp.offsets[p]:sp.offsets[p + 1]] for p in range(world)]
+        recv_rows = _exchange(dist, send_rows, [(int(c), H) for c in rc], torch.float32, rank, world)
+        recv_e = _exchange(dist, send_e, [(int(c),) for c in rc], torch.int64, rank, world)
+        # 3. the owned experts on the received rows
+        outs = []
+        for p in range(world):
+            o = np.zeros((rc[p], H), np.float32)
+            for i in range(rc[p]):
+                o[i] = orc.expert_forward(lay, base + int(recv_e[p][i]), recv_rows[p][i])[1]
+            outs.append(o)
+        # 4. outputs back to their sources, in send order
+        back = _exchange(dist, outs, [(int(c), H) for c in sp.counts], torch.float32, rank, world)
+        ret = np.concatenate(back) if back else np.zeros((0, H), np.float32)
+    else:
+        # the NVLink mailbox layout: fixed [cap] slots per source, each with its
+        # count and the sender's offset; unused slots carry expert -1
+        cap = per_tok * K
+        boxes = []
+        for p in range(world):
+            lo, n = int(sp.offsets[p]), int(sp.counts[p])
+            blk_rows = np.zeros((cap, H), np.float32)
+            blk_e = np.full(cap + 2, -1, np.int64)  # [experts..., count, offset]
+            blk_rows[:n] = rows[lo:lo + n]
+            blk_e[:n] = sp.send_expert[lo:lo + n]
+            blk_e[cap], blk_e[cap + 1] = n, lo
+            boxes.append((blk_rows, blk_e))
+        mb_rows = _exchange(dist, [b[0] for b in boxes], [(cap, H)] * world, torch.float32, rank, world)
+        mb_e = _exchange(dist, [b[1] for b in boxes], [(cap + 2,)] * world, torch.int64, rank, world)
+        # 3. the owned experts over every slot, empty ones skipped; outputs go
+        #    back to each source at its own send positions
+        outs = []
+        for s in range(world):
+            n, off = int(mb_e[s][cap]), int(mb_e[s][cap + 1])
+            o = np.zeros((cap, H), np.float32)
+            for j in range(cap):
+                e = int(mb_e[s][j])
+                if e < 0:
+                    assert j >= n
+                    continue
+                o[j] = orc.expert_forward(lay, base + e, mb_rows[s][j])[1]
+            head = np.zeros((1, H), np.float32)  # the sender's offset and count travel with the block
+            head[0, 0], head[0, 1] = off, n
+            outs.append(np.concatenate([head, o]))
+        back = _exchange(dist, outs, [(cap + 1, H)] * world, torch.float32, rank, world)
+        ret = np.zeros((cap, H), np.float32)
+        for blk in back:
+            off, n = int(blk[0, 0]), int(blk[0, 1])
+            ret[off:off + n] = blk[1:1 + n]
     # 5. combine in pick order (y = 0; y += w_p * down_p), then the shared expert
     y = np.zeros((per_tok, H), np.float32)
     for t in range(per_tok):
@@ -112,12 +149,18 @@ def _ep_rank(rank: int, world: int, port: int, out_dir: str) -> None:
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("transport", ["nccl", "mailbox"])
 @pytest.mark.parametrize("world", [2])
-def test_ep_decomposition_matches_single_rank(tmp_path, world):
+def test_ep_decomposition_matches_single_rank(tmp_path, world, transport):
+    """The whole EP forward on gloo ranks with the oracle's expert math, over
+    both exchange layouts -- exactly the rows that exist (NCCL) and the fixed
+    [source][cap] mailbox slots with empty slots and return offsets (NVLink) --
+    against the single-rank oracle layer, bit for bit."""
     import torch.multiprocessing as mp
 
     port = _free_port()
-    mp.start_processes(_ep_rank, args=(world, port, str(tmp_path)), nprocs=world, start_method="spawn", join=True)
+    mp.start_processes(_ep_rank, args=(world, port, str(tmp_path), transport), nprocs=world, start_method="spawn",
+                       join=True)
     wl, orc = workload(), oracle()
     lay, x_bits = wl.config_layer("c0")
     y_ref, _, _ = orc.moe_layer(orc.port(), lay, wl.bf16_bits_to_f32(x_bits))
