@@ -1,5 +1,5 @@
 """Expert parallelism on the CPU: the (destination, token, pick) exchange
-layout, and the whole EP decomposition run by two gloo ranks -- route own
+layout, and the whole EP decomposition run by two and four gloo ranks -- route own
 tokens, send rows to the owners of the picked experts, run the experts there
 (the oracle's expert_forward), send the outputs back, combine in pick order --
 against the single-rank oracle layer, bit for bit."""
@@ -150,7 +150,7 @@ def _ep_rank(rank: int, world: int, port: int, out_dir: str, transport: str) -> 
 
 
 @pytest.mark.parametrize("transport", ["nccl", "mailbox"])
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4])
 def test_ep_decomposition_matches_single_rank(tmp_path, world, transport):
     """The whole EP forward on gloo ranks with the oracle's expert math, over
     both exchange layouts -- exactly the rows that exist (NCCL) and the fixed
