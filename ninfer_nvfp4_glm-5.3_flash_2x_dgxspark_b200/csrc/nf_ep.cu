@@ -479,10 +479,23 @@ int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, c
              cudaMallocHost(&h->ep_hcnt, 2 * world * sizeof(int32_t)) == cudaSuccess;
         h->ep_back = back;
         h->ep_ret = ret;
-        if (!ok) {
-            cudaGetLastError();
-            err = "device allocation failed";
-            st = NF_ERR_NOMEM;
+        if (!ok) cudaGetLastError();
+        // the group agrees: a rank that could not allocate must not leave the
+        // others waiting in their first exchange
+        struct Ok {
+            int32_t ok;
+            int32_t pad[3];
+        } mine{ok ? 1 : 0, {}};
+        std::vector<Ok> all(static_cast<size_t>(world));
+        if (!ep_allgather_host(h, &mine, sizeof(Ok), all.data())) {
+            err = "allocation agreement failed";
+            st = NF_ERR_CUDA;
+        } else {
+            for (const Ok& o : all) ok = ok && o.ok;
+            if (!ok) {
+                err = mine.ok ? "device allocation failed on another rank" : "device allocation failed";
+                st = NF_ERR_NOMEM;
+            }
         }
     }
     cudaSetDevice(prev);
