@@ -13,7 +13,9 @@ Configurations (the benchmark's configs list):
   c0 tiny     H256  E8  k2 I128  Is128 T16    scale 1.0
   c1 decode   H2048 E64 k4 I1536 Is1536 T64   scale 2.5
   c2 prefill  c1 with T8192 and the bias tuned so every expert gets 512 +- 10%
-  c3 EP       c1 with T16384 and a Zipf(1.1) log-prior added to the bias
+  c3 EP       c1 with T16384 and a Zipf(1.1) log-prior added to the bias, at
+              the configuration's literal weight lambda = 1 and at a
+              calibrated lambda (C3_LAMBDA_CALIBRATED)
   c4 dense    configs[4]'s dense NVFP4 MLP (layers 0-2): H2048 I10240, decode
               batches of 1/16/64/256 tokens (the stack's batch sizes)
 
@@ -183,8 +185,44 @@ def zipf_bias(lay: Layer, s: float = 1.1, lam: float = 1.0) -> np.ndarray:
     return (lay.bias.astype(np.float64) + lam * np.log(p)).astype(np.float32)
 
 
-def config_layer(name: str, seed: int | None = None, bf16_experts: bool = False) -> tuple[Layer, np.ndarray]:
-    """The layer and the token batch of a named configuration."""
+# The log-prior weight at which c3's pick shares come closest to the Zipf(1.1)
+# distribution itself (calibrate_zipf_lambda over its grid, seed 3).  At the
+# literal lambda = 1 the prior (0 ... -4.6) swamps the sigmoid scores in (0, 1)
+# and 93% of the picks land on experts 0-3, each of which then takes every
+# token (a share of 1/k); at this lambda experts 0-3 take 48% of the picks
+# (Zipf: 50%) and the busiest expert 18%.
+C3_LAMBDA_CALIBRATED = 0.145
+
+
+def calibrate_zipf_lambda(lay: Layer, x_bits: np.ndarray, s: float = 1.1,
+                          grid: np.ndarray | None = None) -> float:
+    """The lambda on `grid` (default 0, 0.005, ..., 1) whose routing puts the
+    share of picks per expert closest, in L1 distance, to p_e proportional to
+    (e + 1)^-s.  `lay.bias` is the bias before the prior; the routing uses the
+    approximate scores of balance_bias (selection only, which is all the
+    shares need)."""
+    grid = np.round(np.arange(0.0, 1.0 + 1e-9, 0.005), 3) if grid is None else grid
+    scores = _approx_choice(lay, x_bits)
+    E, k = lay.experts, lay.top_k
+    e = np.arange(E, dtype=np.float64)
+    p = (e + 1.0) ** (-s)
+    p /= p.sum()
+    base = lay.bias.astype(np.float64)
+    best, best_l1 = float(grid[0]), np.inf
+    for lam in grid:
+        choice = scores + (base + lam * np.log(p))[None, :]
+        top = np.argpartition(-choice, k - 1, axis=1)[:, :k]
+        share = np.bincount(top.ravel(), minlength=E) / top.size
+        l1 = float(np.abs(share - p).sum())
+        if l1 < best_l1:
+            best, best_l1 = float(lam), l1
+    return best
+
+
+def config_layer(name: str, seed: int | None = None, bf16_experts: bool = False,
+                 zipf_lambda: float = 1.0) -> tuple[Layer, np.ndarray]:
+    """The layer and the token batch of a named configuration (`zipf_lambda`
+    weights c3's log-prior)."""
     cfg = CONFIGS[name]
     seed = {"c0": 0, "c1": 1, "c2": 2, "c3": 3}[name] if seed is None else seed
     lay = make_layer(cfg, seed, bf16_experts=bf16_experts)
@@ -192,7 +230,7 @@ def config_layer(name: str, seed: int | None = None, bf16_experts: bool = False)
     if name == "c2":
         lay.bias = balance_bias(lay, x)
     elif name == "c3":
-        lay.bias = zipf_bias(lay)
+        lay.bias = zipf_bias(lay, lam=zipf_lambda)
     return lay, x
 
 

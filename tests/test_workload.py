@@ -39,3 +39,22 @@ def test_zipf_bias_prefers_low_experts():
     lay, _ = wl.config_layer("c0")
     b = wl.zipf_bias(lay)
     assert b[0] > b[-1]
+
+
+def test_c3_calibrated_lambda():
+    """c3's calibrated log-prior weight is the grid point whose pick shares come
+    closest to Zipf(1.1); at the literal lambda = 1 experts 0-3 take nearly every
+    pick."""
+    cfg = wl.CONFIGS["c3"]
+    lay, x = wl.make_layer(cfg, 3), wl.make_tokens(cfg, 3)
+    assert wl.calibrate_zipf_lambda(lay, x) == wl.C3_LAMBDA_CALIBRATED
+    scores = wl._approx_choice(lay, x)
+
+    def share_0_3(lam):
+        top = np.argpartition(-(scores + wl.zipf_bias(lay, lam=lam)[None, :]), 3, axis=1)[:, :4]
+        return np.isin(top, [0, 1, 2, 3]).mean()
+
+    assert share_0_3(1.0) > 0.9
+    assert 0.4 < share_0_3(wl.C3_LAMBDA_CALIBRATED) < 0.55
+    lay1, _ = wl.config_layer("c3")
+    assert np.array_equal(lay1.bias, wl.zipf_bias(lay, lam=1.0))
