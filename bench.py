@@ -444,7 +444,11 @@ def run_ep_c3(args, m, torch, rank: int, world: int, local: int, dist, lam: floa
                         f"lambda = {lam:g} (configs[3])", "tokens_per_s": T_all / (ms * 1e-3), "ms_per_step": ms,
             "steps": steps,
             "scaling": "strong", "parallelism": f"ep{world}" if world > 1 else "single",
-            "rank0_picks_by_owner": [int(c) for c in owners]}
+            "rank0_picks_by_owner": [int(c) for c in owners],
+            # rank 0's (token, pick) rows that cross to another rank: dispatched
+            # as BF16 rows (H * 2 B) and returned as BF16 down rows (H * 2 B)
+            "rank0_remote_bytes": {"dispatch": int(owners.sum() - owners[0]) * H * 2,
+                                   "combine": int(owners.sum() - owners[0]) * H * 2}}
 
 
 def run_dense(args, m, torch, hbm_peak, fp4_peak, peak_src) -> dict:
