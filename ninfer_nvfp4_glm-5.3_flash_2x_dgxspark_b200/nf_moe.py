@@ -120,6 +120,30 @@ class NfError(RuntimeError):
         self.status = status
 
 
+_X_DTYPES = ("torch.int16", "torch.uint16", "torch.bfloat16")
+
+
+def _dev(a, need: int, dtypes: tuple, name: str, device: int) -> int | None:
+    """The device pointer of a buffer the library reads or writes `need`
+    elements of.  A torch tensor must be a contiguous CUDA tensor on the
+    handle's device with one of `dtypes` and at least `need` elements; a host
+    array is refused (the kernels would fault on it).  A raw integer pointer is
+    the caller's responsibility, as in the C ABI."""
+    if a is None or isinstance(a, int):
+        return a
+    if isinstance(a, np.ndarray):
+        raise NfError(1, f"{name} is a host array; the device-buffer calls take CUDA tensors or device pointers")
+    if not getattr(a, "is_cuda", False) or a.device.index != device:
+        raise NfError(1, f"{name} is not on cuda:{device}")
+    if str(a.dtype) not in dtypes:
+        raise NfError(1, f"{name} has dtype {a.dtype}; expected {' or '.join(d[6:] for d in dtypes)}")
+    if not a.is_contiguous():
+        raise NfError(1, f"{name} is not contiguous")
+    if a.numel() < need:
+        raise NfError(1, f"{name} holds {a.numel()} elements; {need} needed")
+    return a.data_ptr()
+
+
 class MoeLayer:
     """One MoE layer resident on one GPU."""
 
@@ -240,9 +264,18 @@ class MoeLayer:
 
     # ---- execution ---------------------------------------------------------
     def forward(self, x_dev, y_dev, tokens: int, residual_dev=None, idx_dev=None, w_dev=None, stream=0) -> None:
-        """Device-buffer forward (asynchronous on `stream`)."""
-        self._check(self.lib.nf_moe_forward(self.h, _ptr(x_dev), _ptr(residual_dev), tokens, _ptr(y_dev),
-                                            _ptr(idx_dev), _ptr(w_dev), stream or None))
+        """Device-buffer forward (asynchronous on `stream`).  Tensors are checked
+        for device, dtype, contiguity and size before the call (x BF16 bits
+        [tokens, H]; residual and y fp32 [tokens, H]; idx int32 and w fp32
+        [tokens, k]); a token count outside 0..max_tokens is the library's to
+        reject."""
+        H, K, d = self.desc.hidden, self.desc.top_k, self.device
+        n = tokens if 0 <= tokens <= self.desc.max_tokens else 0
+        f32, i32 = ("torch.float32",), ("torch.int32",)
+        self._check(self.lib.nf_moe_forward(self.h, _dev(x_dev, n * H, _X_DTYPES, "x", d),
+                                            _dev(residual_dev, n * H, f32, "residual", d), tokens,
+                                            _dev(y_dev, n * H, f32, "y", d), _dev(idx_dev, n * K, i32, "idx", d),
+                                            _dev(w_dev, n * K, f32, "w", d), stream or None))
 
     def forward_host(self, x: np.ndarray, residual: np.ndarray | None = None, with_routes: bool = False,
                      out: tuple | None = None):
@@ -267,8 +300,15 @@ class MoeLayer:
         return (y, idx, w) if with_routes else y
 
     def route(self, x_dev, tokens: int, logits_dev=None, idx_dev=None, w_dev=None, stream=0) -> None:
-        self._check(self.lib.nf_moe_route(self.h, _ptr(x_dev), tokens, _ptr(logits_dev), _ptr(idx_dev),
-                                          _ptr(w_dev), stream or None))
+        """The router alone: logits fp32 [tokens, E], idx int32 and w fp32
+        [tokens, k] (each optional), checked as in forward."""
+        H, E, K, d = self.desc.hidden, self.desc.experts, self.desc.top_k, self.device
+        n = tokens if 0 <= tokens <= self.desc.max_tokens else 0
+        f32, i32 = ("torch.float32",), ("torch.int32",)
+        self._check(self.lib.nf_moe_route(self.h, _dev(x_dev, n * H, _X_DTYPES, "x", d), tokens,
+                                          _dev(logits_dev, n * E, f32, "logits", d),
+                                          _dev(idx_dev, n * K, i32, "idx", d), _dev(w_dev, n * K, f32, "w", d),
+                                          stream or None))
 
     def ep_transport(self) -> str:
         """"none" (one GPU), "nccl" or "nvlink" (the EP exchange in use)."""

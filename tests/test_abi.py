@@ -84,3 +84,46 @@ def test_dense_and_ep_queries_without_gpu():
     assert lib.nf_moe_ep_transport(None) == 0
     with pytest.raises(RuntimeError):
         m.DenseMlp(256, 100)
+
+
+def test_device_buffer_checks_without_gpu():
+    """forward and route take CUDA tensors on the handle's device with the
+    documented dtypes, contiguous and large enough; anything else is refused
+    on the host before a kernel could read or write out of bounds."""
+    import numpy as np
+    import torch
+
+    m = nfm()
+    f32 = ("torch.float32",)
+    with pytest.raises(m.NfError, match="host array"):
+        m._dev(np.zeros(4, np.float32), 4, f32, "y", 0)
+    with pytest.raises(m.NfError, match="not on cuda:0"):
+        m._dev(torch.zeros(4), 4, f32, "y", 0)
+
+    class FakeCuda:
+        """Duck-typed stand-in for a CUDA tensor (no GPU here)."""
+
+        def __init__(self, n, dtype="torch.float32", contiguous=True, index=0):
+            self.is_cuda, self.dtype, self.n, self.c = True, dtype, n, contiguous
+            self.device = type("D", (), {"index": index})()
+
+        def is_contiguous(self):
+            return self.c
+
+        def numel(self):
+            return self.n
+
+        def data_ptr(self):
+            return 4096
+
+    assert m._dev(FakeCuda(8), 8, f32, "y", 0) == 4096
+    assert m._dev(None, 8, f32, "y", 0) is None and m._dev(1024, 8, f32, "y", 0) == 1024
+    with pytest.raises(m.NfError, match="not on cuda:1"):
+        m._dev(FakeCuda(8), 8, f32, "y", 1)
+    with pytest.raises(m.NfError, match="dtype"):
+        m._dev(FakeCuda(8, "torch.float16"), 8, f32, "y", 0)
+    with pytest.raises(m.NfError, match="contiguous"):
+        m._dev(FakeCuda(8, contiguous=False), 8, f32, "y", 0)
+    with pytest.raises(m.NfError, match="7 elements; 8 needed"):
+        m._dev(FakeCuda(7), 8, f32, "y", 0)
+    assert m._dev(FakeCuda(8, "torch.int16"), 8, m._X_DTYPES, "x", 0) == 4096
