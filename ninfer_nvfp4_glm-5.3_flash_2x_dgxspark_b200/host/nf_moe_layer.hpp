@@ -70,6 +70,15 @@ public:
         if (nf_moe_create(&desc, device, &h_) != NF_OK) throw std::runtime_error(nf_moe_last_error(nullptr));
         d_ = desc;
     }
+    // This rank's handle of an expert-parallel group (collective: every rank
+    // of the group constructs its handle with the same group id, from
+    // nf_ep_unique_id on one rank); max_tokens is per rank.  Binding takes
+    // every expert's tensors, as for one GPU, and keeps the rank's own.
+    MoeLayer(const nf_moe_desc& desc, int device, int rank, int world, const uint8_t* group_id, int id_len) {
+        if (nf_moe_create_ep(&desc, device, rank, world, group_id, id_len, &h_) != NF_OK)
+            throw std::runtime_error(nf_moe_last_error(nullptr));
+        d_ = desc;
+    }
     MoeLayer(const MoeLayer&) = delete;
     MoeLayer& operator=(const MoeLayer&) = delete;
     ~MoeLayer() { nf_moe_destroy(h_); }
@@ -120,6 +129,22 @@ public:
     // The same with the routes (indices, weights: tokens x top_k).
     void moe(const float* x, float* y, int tokens, int32_t* idx, float* w) {
         check(nf_moe_forward_host(h_, x, nullptr, tokens, y, idx, w));
+    }
+    // Device buffers, asynchronous on `stream` (a cudaStream_t): x BF16 bits
+    // [tokens, H], residual fp32 or null, y fp32 [tokens, H], routes optional.
+    // Every rank of an expert-parallel group calls it each step, also with
+    // tokens == 0.
+    void forward(const uint16_t* x_dev, const float* residual_dev, int tokens, float* y_dev, void* stream,
+                 int32_t* idx_dev = nullptr, float* w_dev = nullptr) {
+        check(nf_moe_forward(h_, x_dev, residual_dev, tokens, y_dev, idx_dev, w_dev, stream));
+    }
+    // "none", "nccl" or "nvlink": the exchange the group agreed on.
+    const char* ep_transport() const {
+        switch (nf_moe_ep_transport(h_)) {
+            case NF_EP_NCCL: return "nccl";
+            case NF_EP_NVLINK: return "nvlink";
+            default: return "none";
+        }
     }
 
 private:
