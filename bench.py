@@ -22,15 +22,21 @@ over NVLink peer memory (NCCL point-to-point when the ranks cannot map each
 other's buffers; config.ep_transport says which).  value sums the tokens of
 all ranks over the max-over-ranks device time.
 
+Each rank of an expert-parallel run also checks its EP outputs (y, routes)
+bit for bit against a single-GPU handle holding every expert on the same
+tokens and reports the verdict as "ep_parity".
+
 --impl reference times the reference's own CPU implementation (its sources
 compiled under oracle/_ref, else the C restatement) on this host's cores over
-the same workload: each step is a bounded 16-token sample of the decode
-batch.  Under torchrun only rank 0 runs it.
+the same workload: each step is the full 64-token decode batch.  Under
+torchrun only rank 0 runs it.
 """
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
+import math
 import os
 import subprocess
 import sys
@@ -38,16 +44,38 @@ import threading
 import time
 from pathlib import Path
 
-# The CPU legs use every host core; OpenMP reads this when the oracle loads.
-os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
 
-import numpy as np
+def cpu_threads() -> int:
+    """Host threads this process may run on (its CPU affinity set)."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return max(1, os.cpu_count() or 1)
+
+
+# The CPU legs use every host core the process may run on.  torchrun exports
+# OMP_NUM_THREADS=1 to each rank, so this overrides rather than defaults; the
+# oracle's OpenMP runtime reads it when the oracle library loads.
+os.environ["OMP_NUM_THREADS"] = str(cpu_threads())
+
+import numpy as np  # noqa: E402
 
 REPO = Path(__file__).resolve().parent
-sys.path.insert(0, str(REPO / "tests"))
-from helpers import load_module  # noqa: E402  (module loader by path)
-
 PKG = REPO / "ninfer_nvfp4_glm-5.3_flash_2x_dgxspark_b200"
+
+
+def load_module(name: str, path: Path):
+    """Imports a module by file path (the package folder's name is not a
+    Python identifier)."""
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
 wl = load_module("nf_workload", PKG / "workload.py")
 
 METRIC = "MoE layer tokens/s (decode c1, T=64) + % HBM BW; prefill c2 tokens/s + % NVFP4 TC peak"
@@ -89,6 +117,15 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def wait_first(self, timeout_s: float = 5.0) -> None:
+        """Returns once nvidia-smi has printed its first sample (it takes a
+        few hundred ms to start), so the loop that follows is sampled."""
+        t0 = time.monotonic()
+        while self.proc is not None and not self.lines and time.monotonic() - t0 < timeout_s:
+            if self.proc.poll() is not None:
+                break
+            time.sleep(0.02)
+
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
@@ -119,6 +156,55 @@ def dist_env() -> tuple[int, int, int]:
     return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
 
 
+def steps_for(step, stream, seconds: float, dist, torch) -> int:
+    """Steps that take about `seconds` (from 20 timed steps), the same number
+    on every rank: the largest rank's count wins."""
+    n0 = 20
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(n0):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    per_ms = max(ev0.elapsed_time(ev1) / n0, 1e-3)
+    n = int(min(200000, max(100, math.ceil(seconds * 1e3 / per_ms))))
+    if dist:
+        t = torch.tensor([n], device="cuda", dtype=torch.int64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        n = int(t.item())
+    return n
+
+
+def merge_clocks(per_rank: list) -> dict:
+    """Rank 0's clock record plus every rank's median SM clock and the union
+    of the throttle reasons any rank saw."""
+    out = dict(per_rank[0])
+    out["reasons"] = sorted({r for c in per_rank for r in (c.get("reasons") or [])})
+    out["per_rank_sm_mhz"] = [c.get("sm_mhz") for c in per_rank]
+    out["per_rank_samples"] = [c.get("samples") for c in per_rank]
+    return out
+
+
+def ep_parity_check(m, torch, lay, x, T: int, device: int, y_ep, idx_ep, w_ep) -> bool:
+    """True when the expert-parallel outputs of this rank's tokens (y, route
+    indices and weights) equal bit for bit those of a single-GPU handle that
+    holds every expert, run on the same tokens on this rank's GPU."""
+    H, K = lay.hidden, lay.top_k
+    ref = m.MoeLayer(H, lay.experts, K, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                     swiglu_limit=lay.swiglu_limit, max_tokens=max(T, 1), device=device)
+    ref.bind_layer(lay)
+    y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    idx = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    ref.forward(x, y, T, None, idx, w)
+    ref.sync()
+    ok = (np.array_equal(y.cpu().numpy().view(np.uint32), np.asarray(y_ep).view(np.uint32))
+          and np.array_equal(idx.cpu().numpy(), np.asarray(idx_ep))
+          and np.array_equal(w.cpu().numpy().view(np.uint32), np.asarray(w_ep).view(np.uint32)))
+    ref.close()
+    return bool(ok)
+
+
 def decode_bytes(lay, active: int, tokens: int) -> dict:
     """Algorithmic HBM bytes of one decode step and of the gate/up kernel."""
     H, I, Is, E = lay.hidden, lay.inter, lay.shared_inter, lay.experts
@@ -131,6 +217,37 @@ def decode_bytes(lay, active: int, tokens: int) -> dict:
     router = E * H * 2 + E * 4
     io = tokens * H * 2 + tokens * H * 4     # x in, y out
     return {"gate_up": gu_w + act_gu + h_out, "layer": gu_w + dn_w + shared + router + io}
+
+
+def ep_rank_bytes(lay, idx_all: list, rank: int, world: int) -> dict:
+    """Algorithmic HBM bytes one rank of an expert-parallel decode step moves.
+
+    idx_all[r] holds rank r's routes [T_r, k].  Rank `rank` streams the
+    weights of the experts it owns that received at least one row from any
+    rank, the replicated shared expert and router, its own tokens' input and
+    output rows, and the exchanged rows: every row it receives is written
+    into its mailbox and read by the dispatch (BF16, 2H B each way), and
+    every down row it computes is written back to the source and read by the
+    source's combine (BF16, 2H B each way).  The gate/up figure is the same
+    kernel's share as in decode_bytes, over the rows this rank received."""
+    H, I, Is, E, k = lay.hidden, lay.inter, lay.shared_inter, lay.experts, lay.top_k
+    local = E // world
+    lo, hi = rank * local, (rank + 1) * local
+    picks = np.concatenate([np.asarray(a).ravel() for a in idx_all]) if idx_all else np.zeros(0, np.int64)
+    mine = picks[(picks >= lo) & (picks < hi)]
+    active = int(np.unique(mine).size)
+    recv = int(mine.size)
+    T = int(np.asarray(idx_all[rank]).shape[0])
+    gu_w = active * (2 * I * H // 2 + 2 * I * H // 16)
+    dn_w = active * (H * I // 2 + H * I // 16)
+    act_gu = recv * (H // 2 + H // 16)
+    h_out = recv * (I // 2 + I // 16)
+    exchange = recv * H * 2 * 2 + recv * H * 2 * 2
+    # the single-GPU layer figure's terms (weights, shared expert, router, x in
+    # and y out) plus the exchange
+    layer = gu_w + dn_w + 3 * Is * H * 2 + E * H * 2 + E * 4 + T * H * 2 + T * H * 4 + exchange
+    return {"gate_up": gu_w + act_gu + h_out, "layer": layer, "active_owned": active, "rows_received": recv,
+            "tokens": T}
 
 
 def prefill_flops(lay, tokens: int) -> dict:
@@ -157,24 +274,27 @@ def cpu_reference_rate(lay, x_bits, tokens: int) -> tuple[float, dict]:
 
 
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference's CPU path on the same workload as our arm's headline:
+    each step is the whole 64-token decode batch, on every host thread."""
     if rank != 0:
         return
     lay, x_bits = wl.config_layer("c1")
-    sample = 16
-    for i in range(args.warmup):
-        cpu_reference_rate(lay, x_bits[16 * (i % 4):], sample)
-    rates = []
+    T = x_bits.shape[0]
+    for _ in range(args.warmup):
+        cpu_reference_rate(lay, x_bits, T)
+    info = {}
     t0 = time.perf_counter()
-    for i in range(args.steps):
-        r, info = cpu_reference_rate(lay, x_bits[16 * (i % 4):], sample)
-        rates.append(r)
+    for _ in range(args.steps):
+        _, info = cpu_reference_rate(lay, x_bits, T)
     total = time.perf_counter() - t0
-    value = sample * args.steps / total
+    value = T * args.steps / total
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / max(args.steps, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (NVFP4 fake-quant)",
-        "data": "synthetic", "config": {"workload": "c1 decode: H2048 E64 k4 I1536 Is1536 T64 (configs[1])"},
+        "data": "synthetic",
+        "config": {"workload": "c1 decode: H2048 E64 k4 I1536 Is1536 T64 scale2.5 (configs[1])", "tokens_per_step": T,
+                   "omp_num_threads": int(os.environ["OMP_NUM_THREADS"])},
         "cpu_baseline": {"value": value, "unit": "tokens/s", **info},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -232,9 +352,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     layer.sync(stream)
     clocks = ClockSampler(local)
     clocks.start()
-    # settle clocks under the same load before timing (a fixed step count:
-    # every rank of an expert-parallel group takes the same steps)
-    for _ in range(5000 if world == 1 else 300):
+    clocks.wait_first()
+    # settle clocks under the same load before timing, ~1 s; every rank of an
+    # expert-parallel group takes the same number of steps (steps_for agrees
+    # on it), since each forward exchanges rows with every other rank
+    n_settle = steps_for(step, tstream, 1.0, dist, torch)
+    for _ in range(n_settle):
         step()
     tstream.synchronize()
     if dist:
@@ -255,7 +378,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     torch.cuda.synchronize()
     stages, nfw = layer.stage_times()
     layer.profile(False)
-    for _ in range(2000 if world == 1 else 150):
+    for _ in range(max(1, n_settle // 2)):
         step()
     tstream.synchronize()
     clk = clocks.stop()
@@ -264,11 +387,33 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+        per_rank_clk = [None] * world
+        dist.all_gather_object(per_rank_clk, clk)
+        clk = merge_clocks(per_rank_clk)
         dist.barrier()
     stage_ms = {k: v / max(nfw, 1) for k, v in stages.items()}
     idx_h = idx.cpu().numpy()
-    active = int(np.unique(idx_h).size)
-    nbytes = decode_bytes(lay, active, T)
+    y_ep = y.cpu().numpy()
+    w_ep = w.cpu().numpy()
+    if dist:
+        idx_all = [None] * world
+        dist.all_gather_object(idx_all, idx_h)
+        mine = ep_rank_bytes(lay, idx_all, rank, world)
+        all_bytes = [ep_rank_bytes(lay, idx_all, r, world) for r in range(world)]
+        active = int(np.unique(np.concatenate([a.ravel() for a in idx_all])).size)
+        nbytes = {"gate_up": mine["gate_up"], "layer": sum(b["layer"] for b in all_bytes)}
+    else:
+        active = int(np.unique(idx_h).size)
+        nbytes = decode_bytes(lay, active, T)
+        mine = None
+
+    # expert-parallel outputs against one GPU holding every expert, bit for bit
+    ep_ok = None
+    if dist:
+        ep_ok = ep_parity_check(m, torch, lay, x, T, local, y_ep, idx_h, w_ep)
+        flag = torch.tensor([1 if ep_ok else 0], device="cuda", dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ep_ok = bool(flag.item())
 
     # end to end through the host-buffer C-ABI call (pinned host memory)
     xh = torch.from_numpy(wl.bf16_bits_to_f32(x_bits)).pin_memory().numpy()
@@ -277,6 +422,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             torch.empty((T, K), dtype=torch.float32).pin_memory().numpy())
     for _ in range(args.warmup):
         layer.forward_host(xh, out=outs)
+    if dist:
+        dist.barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         layer.forward_host(xh, out=outs)
@@ -293,7 +440,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         # DRAM read + write of one gate/up launch from the committed ncu summary
         traffic = None
         tf = REPO / "profiles" / "gemm_gate_up_c1_decode.md"
-        if tf.exists():
+        if tf.exists() and world == 1:
             for ln in tf.read_text().splitlines():
                 if ln.startswith("traffic_bytes_per_launch:"):
                     traffic = int(ln.split(":")[1])
@@ -304,6 +451,18 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             # + pack, send, receive wait, return, return wait (NVLink) or
             # + pack and two row gathers (NCCL, whose own kernels are not counted)
             launches_per_step += 4 if layer.ep_transport() == "nvlink" else 3
+        layer_gbs = nbytes["layer"] / (ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "grouped NVFP4 gate/up GEMM (SwiGLU + quant fused)",
+                "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                "peak_source": peak_src, "traffic": traffic,
+                "algorithmic_bytes_per_launch": nbytes["gate_up"],
+                "layer_achieved_gbs": layer_gbs, "layer_frac": layer_gbs / (world * hbm_peak),
+                "layer_algorithmic_bytes": nbytes["layer"]}
+        if world > 1:
+            roof["per_rank"] = ("achieved/frac: rank 0's gate/up bytes (its owned experts with rows, the rows it "
+                                "received) over rank 0's gate/up time; layer_frac: every rank's bytes over "
+                                "world x the max-over-ranks step time x peak")
+            roof["rank0"] = mine
         line = {
             "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3,
@@ -317,18 +476,16 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "stages_us": {k: 1e3 * v for k, v in stage_ms.items()},
             "timing": "timed steps replay a CUDA graph on a dedicated stream; stages_us from K more steps "
                       "launched directly with events around each kernel",
-            "roofline": {"bound": "hbm", "kernel": "grouped NVFP4 gate/up GEMM (SwiGLU + quant fused)",
-                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "peak_source": peak_src, "traffic": traffic,
-                         "algorithmic_bytes_per_launch": nbytes["gate_up"],
-                         "layer_achieved_gbs": nbytes["layer"] / (ms * 1e-3) / 1e9,
-                         "layer_frac": nbytes["layer"] / (ms * 1e-3) / 1e9 / hbm_peak,
-                         "layer_algorithmic_bytes": nbytes["layer"]},
+            "roofline": roof,
             "e2e": {"value": world * T / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
                     "d2h_bytes_per_step": T * H * 4 + T * K * 8, "ms_per_step": 1e3 * e2e_s},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
+        if ep_ok is not None:
+            line["ep_parity"] = ep_ok
+            line["ep_parity_check"] = ("every rank's y, routes and route weights equal bit for bit those of a "
+                                       "single-GPU handle holding all experts on the same tokens")
     if world == 1 and not args.no_prefill:
         line["prefill"] = run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src)
         line["dense"] = run_dense(args, m, torch, hbm_peak, fp4_peak, peak_src)
@@ -418,10 +575,11 @@ def run_ep_c3(args, m, torch, rank: int, world: int, local: int, dist, lam: floa
     x = torch.from_numpy(np.ascontiguousarray(xb).view(np.int16)).cuda()
     y = torch.empty((per, H), dtype=torch.float32, device="cuda")
     idx = torch.empty((per, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((per, K), dtype=torch.float32, device="cuda")
     ts = torch.cuda.Stream()
     steps = max(3, min(args.steps, 10))
     for _ in range(args.warmup):
-        layer.forward(x, y, per, None, idx, None, stream=ts.cuda_stream)
+        layer.forward(x, y, per, None, idx, w, stream=ts.cuda_stream)
     ts.synchronize()
     if dist:
         dist.barrier()
@@ -429,26 +587,34 @@ def run_ep_c3(args, m, torch, rank: int, world: int, local: int, dist, lam: floa
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(ts)
     for _ in range(steps):
-        layer.forward(x, y, per, None, idx, None, stream=ts.cuda_stream)
+        layer.forward(x, y, per, None, idx, w, stream=ts.cuda_stream)
     ev1.record(ts)
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / steps
+    layer.sync(ts.cuda_stream)
     if dist:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    owners = np.bincount(idx.cpu().numpy().ravel() // (lay.experts // world), minlength=world)
-    layer.sync(ts.cuda_stream)
+    idx_h = idx.cpu().numpy()
+    owners = np.bincount(idx_h.ravel() // (lay.experts // world), minlength=world)
+    out = {"workload": f"c3: c1 shapes, 16384 tokens per step split over the ranks, Zipf(1.1) log-prior "
+                       f"lambda = {lam:g} (configs[3])", "tokens_per_s": T_all / (ms * 1e-3), "ms_per_step": ms,
+           "steps": steps,
+           "scaling": "strong", "parallelism": f"ep{world}" if world > 1 else "single",
+           "rank0_picks_by_owner": [int(c) for c in owners],
+           # rank 0's (token, pick) rows that cross to another rank: dispatched
+           # as BF16 rows (H * 2 B) and returned as BF16 down rows (H * 2 B)
+           "rank0_remote_bytes": {"dispatch": int(owners.sum() - owners[0]) * H * 2,
+                                  "combine": int(owners.sum() - owners[0]) * H * 2}}
+    if dist:
+        ok = ep_parity_check(m, torch, lay, x, per, local, y.cpu().numpy(), idx_h, w.cpu().numpy())
+        flag = torch.tensor([1 if ok else 0], device="cuda", dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        out["ep_parity"] = bool(flag.item())
+        dist.barrier()  # every rank's last forward is done before any handle of the group goes
     layer.close()
-    return {"workload": f"c3: c1 shapes, 16384 tokens per step split over the ranks, Zipf(1.1) log-prior "
-                        f"lambda = {lam:g} (configs[3])", "tokens_per_s": T_all / (ms * 1e-3), "ms_per_step": ms,
-            "steps": steps,
-            "scaling": "strong", "parallelism": f"ep{world}" if world > 1 else "single",
-            "rank0_picks_by_owner": [int(c) for c in owners],
-            # rank 0's (token, pick) rows that cross to another rank: dispatched
-            # as BF16 rows (H * 2 B) and returned as BF16 down rows (H * 2 B)
-            "rank0_remote_bytes": {"dispatch": int(owners.sum() - owners[0]) * H * 2,
-                                   "combine": int(owners.sum() - owners[0]) * H * 2}}
+    return out
 
 
 def run_dense(args, m, torch, hbm_peak, fp4_peak, peak_src) -> dict:

@@ -37,6 +37,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <vector>
@@ -92,26 +93,35 @@ int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 // The transport an EP group uses when NF_EP_TRANSPORT is not set.
 constexpr bool kEpNvlinkDefault = true;
 
-// Every rank sends `bytes` bytes from src to every rank (its own slot
-// included) and receives every rank's into dst[world][bytes]: a gather of
-// small host records through device buffers, used at set-up only.
+// Bytes of one record of the set-up exchanges (ep_allgather_host).
+constexpr size_t kEpRecBytes = 256;
+
+// Every rank sends `bytes` bytes from `mine` to every rank (its own slot
+// included) and receives every rank's into all[world][bytes]: a gather of
+// small host records through the handle's staging buffer (h->ep_stage,
+// allocated before the communicator exists), used at set-up only.  The
+// sends and receives are posted whatever happened locally, so a rank whose
+// copy failed never leaves the others waiting: its staging slot is cleared
+// first, so the others then receive a zeroed record, whose `ok` word reads
+// as a failure.  Returns false when this rank's copy or the exchange failed.
 bool ep_allgather_host(nf_moe* h, const void* mine, size_t bytes, void* all) {
     NcclApi& api = nccl();
     ncclComm_t comm = static_cast<ncclComm_t>(h->nccl);
     const int R = h->ep_world;
-    uint8_t* buf = nullptr;
-    if (cudaMalloc(&buf, bytes * (R + 1)) != cudaSuccess) return false;
-    bool ok = cudaMemcpy(buf, mine, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
-    ncclResult_t r = ok ? api.group_start() : ncclInternalError;
+    uint8_t* buf = h->ep_stage;
+    if (!buf || bytes > kEpRecBytes) return false;  // the same on every rank: no exchange is posted anywhere
+    const bool local = cudaMemset(buf, 0, bytes) == cudaSuccess &&
+                       cudaMemcpy(buf, mine, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
+    if (!local) cudaGetLastError();
+    ncclResult_t r = api.group_start();
     for (int p = 0; p < R && r == ncclSuccess; ++p) {
         r = api.send(buf, bytes, ncclUint8, p, comm, h->stream);
         if (r == ncclSuccess) r = api.recv(buf + bytes * (p + 1), bytes, ncclUint8, p, comm, h->stream);
     }
-    const ncclResult_t r2 = ok ? api.group_end() : ncclInternalError;
-    ok = ok && r == ncclSuccess && r2 == ncclSuccess && cudaStreamSynchronize(h->stream) == cudaSuccess &&
-         cudaMemcpy(all, buf + bytes, bytes * R, cudaMemcpyDeviceToHost) == cudaSuccess;
-    cudaFree(buf);
-    return ok;
+    const ncclResult_t r2 = api.group_end();
+    const bool ok = r == ncclSuccess && r2 == ncclSuccess && cudaStreamSynchronize(h->stream) == cudaSuccess &&
+                    cudaMemcpy(all, buf + bytes, bytes * R, cudaMemcpyDeviceToHost) == cudaSuccess;
+    return ok && local;
 }
 
 // Peer-memory transport set-up (collective: every rank calls it after the
@@ -132,34 +142,51 @@ int ep_p2p_setup(nf_moe* h, std::string* err) {
     L.rows = align256(L.e + R * cap * 4);
     L.ret = align256(L.rows + R * cap * H * 2);
     L.total = align256(L.ret + cap * H * ob);
+    // A local failure here does not return at once: the other ranks are about
+    // to enter the handle exchange, so this rank joins it too, reporting the
+    // failure, and every rank then fails the create together.
+    int local_fail = 0;  // 0, NF_ERR_NOMEM or NF_ERR_CUDA
     if (!h->alloc(&h->ep_mbox, L.total) || !h->alloc(&h->ep_epoch, 1) || !h->alloc(&h->ep_done, 2 * kEpMaxRanks) ||
         !h->alloc(&h->ep_seen, kEpMaxRanks)) {
         cudaGetLastError();
-        *err = "device allocation failed";
-        return NF_ERR_NOMEM;
-    }
-    if (cudaMemset(h->ep_mbox, 0, L.total) != cudaSuccess || cudaMemset(h->ep_epoch, 0, 4) != cudaSuccess ||
-        cudaMemset(h->ep_done, 0, 2 * kEpMaxRanks * 4) != cudaSuccess ||
-        cudaMemset(h->ep_seen, 0, kEpMaxRanks * 4) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
-        *err = "mailbox initialisation failed";
-        return NF_ERR_CUDA;
+        local_fail = NF_ERR_NOMEM;
+    } else if (cudaMemset(h->ep_mbox, 0, L.total) != cudaSuccess || cudaMemset(h->ep_epoch, 0, 4) != cudaSuccess ||
+               cudaMemset(h->ep_done, 0, 2 * kEpMaxRanks * 4) != cudaSuccess ||
+               cudaMemset(h->ep_seen, 0, kEpMaxRanks * 4) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaGetLastError();
+        local_fail = NF_ERR_CUDA;
     }
     struct Rec {
         cudaIpcMemHandle_t handle;
-        int32_t ok;
-        int32_t pad[15];
+        int32_t ok;      // the mailbox is exported (a zeroed record: not)
+        int32_t sound;   // 1: this rank's set-up succeeded so far (a zeroed record: failed)
+        int32_t status;  // the failure's status when sound == 0
+        int32_t pad[13];
     };
-    static_assert(sizeof(Rec) % 16 == 0, "record size");
+    static_assert(sizeof(Rec) % 16 == 0 && sizeof(Rec) <= kEpRecBytes, "record size");
     // NF_EP_TRANSPORT=nvlink | nccl chooses; unset: kEpNvlinkDefault
     const char* tr = std::getenv("NF_EP_TRANSPORT");
     const bool want = tr ? std::strcmp(tr, "nvlink") == 0 : kEpNvlinkDefault;
     Rec mine{};
-    mine.ok = want && cudaIpcGetMemHandle(&mine.handle, h->ep_mbox) == cudaSuccess;
+    mine.sound = local_fail == 0;
+    mine.status = local_fail;
+    mine.ok = !local_fail && want && cudaIpcGetMemHandle(&mine.handle, h->ep_mbox) == cudaSuccess;
     cudaGetLastError();
     std::vector<Rec> all(static_cast<size_t>(R));
     if (!ep_allgather_host(h, &mine, sizeof(Rec), all.data())) {
         *err = "mailbox handle exchange failed";
         return NF_ERR_CUDA;
+    }
+    // every rank reads the same records, so every rank takes this branch or none
+    for (int p = 0; p < R; ++p) {
+        const Rec& q = all[static_cast<size_t>(p)];
+        if (!q.sound) {
+            char msg[128];
+            std::snprintf(msg, sizeof(msg), "mailbox set-up failed on rank %d (%s)", p,
+                          q.status == NF_ERR_CUDA ? "initialisation" : "device allocation");
+            *err = msg;
+            return q.status == NF_ERR_CUDA ? NF_ERR_CUDA : NF_ERR_NOMEM;
+        }
     }
     int opened = 1;
     for (int p = 0; p < R; ++p) opened &= all[static_cast<size_t>(p)].ok ? 1 : 0;
@@ -448,8 +475,10 @@ int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, c
     const int64_t ob = d.expert_kind == NF_EXPERTS_NVFP4 ? 2 : 4;
     // the send layout, used by both transports (the NCCL transport's own
     // buffers follow once the group has chosen it)
+    // (and the staging buffer of the set-up exchanges: allocated before the
+    // communicator, so that every exchange has a buffer on every rank)
     bool ok = h->alloc(&h->ep_send_e, pairs) && h->alloc(&h->ep_send_tok, pairs) && h->alloc(&h->ep_slot, pairs) &&
-              h->alloc(&h->ep_cnt, 2 * world);
+              h->alloc(&h->ep_cnt, 2 * world) && h->alloc(&h->ep_stage, kEpRecBytes * (world + 1));
     if (!ok) {
         cudaGetLastError();
         cudaSetDevice(prev);

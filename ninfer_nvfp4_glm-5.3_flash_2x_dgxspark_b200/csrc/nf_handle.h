@@ -100,6 +100,7 @@ struct nf_moe {
     void* ep_back = nullptr;         // [world*Tm*K, H] expert outputs in receive order
     void* ep_ret = nullptr;          // [Tm*K, H] outputs returned, in send order
     int32_t* ep_hcnt = nullptr;      // pinned host copy of ep_cnt
+    uint8_t* ep_stage = nullptr;     // staging of the set-up exchanges' host records
     // NVLink peer-memory transport (the default when every rank can map every
     // other rank's mailbox with CUDA IPC; NCCL point-to-point otherwise)
     bool ep_p2p = false;

@@ -78,3 +78,41 @@ def mailbox_exchange(plans: list, cap: int):
             offs[s] = lo
         out.append((expert, src_slot, offs))
     return out
+
+
+NF_OK, NF_ERR_CUDA, NF_ERR_NOMEM = 0, 6, 9
+
+
+def setup_agreement(exchange, local_status: int, want_nvlink: bool, export_ok: bool, map_peers) -> tuple:
+    """The collective steps of an EP group's transport set-up (ep_p2p_setup in
+    csrc/nf_ep.cu), restated so that the protocol can be run by CPU ranks.
+
+    exchange(record) -> every rank's record (an all-gather); local_status is
+    this rank's mailbox allocation / initialisation outcome (NF_OK,
+    NF_ERR_NOMEM or NF_ERR_CUDA); export_ok whether its mailbox could be
+    exported; map_peers() maps every peer's mailbox and returns success.
+
+    A rank whose own set-up failed still joins the first exchange and reports
+    the failure there, so no rank is left waiting in it; every rank reads the
+    same records, so every rank then fails together with the failing rank's
+    status.  Otherwise every rank maps its peers, the group agrees on whether
+    all did (second exchange), and falls back to NCCL together when one did
+    not (a third exchange is the barrier before the mailboxes are released).
+    Returns (status, transport or message, exchanges taken)."""
+    n = 0
+    sound = local_status == NF_OK
+    recs = exchange({"ok": bool(sound and want_nvlink and export_ok), "sound": sound, "status": local_status})
+    n += 1
+    for p, q in enumerate(recs):
+        if not q["sound"]:
+            what = "initialisation" if q["status"] == NF_ERR_CUDA else "device allocation"
+            status = NF_ERR_CUDA if q["status"] == NF_ERR_CUDA else NF_ERR_NOMEM
+            return status, f"mailbox set-up failed on rank {p} ({what})", n
+    opened = all(q["ok"] for q in recs) and bool(map_peers())
+    recs = exchange({"ok": opened})
+    n += 1
+    if not all(q["ok"] for q in recs):
+        exchange({"ok": opened})  # every rank has closed its mappings before the mailboxes go
+        n += 1
+        return NF_OK, "nccl", n
+    return NF_OK, "nvlink", n

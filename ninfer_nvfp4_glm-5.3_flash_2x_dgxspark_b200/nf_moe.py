@@ -134,7 +134,7 @@ def _dev(a, need: int, dtypes: tuple, name: str, device: int) -> int | None:
     if isinstance(a, np.ndarray):
         raise NfError(1, f"{name} is a host array; the device-buffer calls take CUDA tensors or device pointers")
     if not getattr(a, "is_cuda", False) or a.device.index != device:
-        raise NfError(1, f"{name} is not on cuda:{device}")
+        raise NfError(1, f"{name} is not on cuda:{device}" if device >= 0 else f"{name} is not a CUDA tensor")
     if str(a.dtype) not in dtypes:
         raise NfError(1, f"{name} has dtype {a.dtype}; expected {' or '.join(d[6:] for d in dtypes)}")
     if not a.is_contiguous():
@@ -466,16 +466,41 @@ def sigmoid_ref(x_dev, n: int, y_dev, stream=0) -> int:
 NOALLOC_MAX_SCORES = 16384  # tokens x experts of one nf_router_topk_noalloc call
 
 
+def _current_device() -> int:
+    """The CUDA device the library's calls run on (torch's current device)."""
+    import torch
+
+    return torch.cuda.current_device() if torch.cuda.is_available() else 0
+
+
 def router_topk_noalloc(x_dev, router_w_dev, bias_dev, tokens: int, hidden: int, experts: int, top_k: int,
                         idx_dev, w_dev, *, n_group: int = 1, topk_group: int = 1, normalize: bool = True,
                         routed_scaling: float = 1.0, stream=0) -> tuple[int, str]:
     """Router top-k from caller device buffers with no device allocation
     (the library's static scratch; calls must not overlap).  Returns
-    (status, message)."""
+    (status, message).
+
+    Every tensor is checked before the library is called, as in
+    MoeLayer.forward: a CUDA tensor on the current device (the scratch and
+    the launches use that device), contiguous, with the documented dtype and
+    at least the elements the call reads or writes (x BF16 bits [tokens,
+    hidden], router weights BF16 bits [experts, hidden], bias fp32 [experts],
+    idx int32 and w fp32 [tokens, top_k]).  A host array raises NfError: the
+    router's bulk copies would read it as a device address."""
+    d = -1
+    if any(getattr(a, "is_cuda", False) for a in (x_dev, router_w_dev, bias_dev, idx_dev, w_dev)):
+        d = _current_device()
+    n = tokens if tokens >= 0 else 0
+    e = experts if experts >= 0 else 0
+    f32, i32 = ("torch.float32",), ("torch.int32",)
+    ptrs = (_dev(x_dev, n * max(hidden, 0), _X_DTYPES, "x", d),
+            _dev(router_w_dev, e * max(hidden, 0), _X_DTYPES, "router_w", d),
+            _dev(bias_dev, e, f32, "bias", d),
+            _dev(idx_dev, n * max(top_k, 0), i32, "idx", d),
+            _dev(w_dev, n * max(top_k, 0), f32, "w", d))
     buf = ctypes.create_string_buffer(256)
-    st = load().nf_router_topk_noalloc(_ptr(x_dev), _ptr(router_w_dev), _ptr(bias_dev), tokens, hidden, experts,
-                                       top_k, n_group, topk_group, int(normalize), routed_scaling, _ptr(idx_dev),
-                                       _ptr(w_dev), buf, len(buf), stream or None)
+    st = load().nf_router_topk_noalloc(ptrs[0], ptrs[1], ptrs[2], tokens, hidden, experts, top_k, n_group, topk_group,
+                                       int(normalize), routed_scaling, ptrs[3], ptrs[4], buf, len(buf), stream or None)
     return st, buf.value.decode()
 
 

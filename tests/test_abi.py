@@ -127,3 +127,59 @@ def test_device_buffer_checks_without_gpu():
     with pytest.raises(m.NfError, match="7 elements; 8 needed"):
         m._dev(FakeCuda(7), 8, f32, "y", 0)
     assert m._dev(FakeCuda(8, "torch.int16"), 8, m._X_DTYPES, "x", 0) == 4096
+
+
+def test_noalloc_wrapper_checks_buffers_before_the_library():
+    """router_topk_noalloc refuses host arrays, CPU tensors, wrong dtypes and
+    short buffers on the host: the library is never called (a host pointer
+    would reach the router's bulk copies as a device address)."""
+    import numpy as np
+    import torch
+
+    m = nfm()
+    calls = []
+
+    class Spy:
+        def nf_router_topk_noalloc(self, *a):
+            calls.append(a)
+            return 0
+
+    real = m._lib
+    m._lib = Spy()
+    try:
+        T, H, E, K = 4, 256, 8, 2
+        x = np.zeros((T, H), np.uint16)
+        with pytest.raises(m.NfError, match="x is a host array"):
+            m.router_topk_noalloc(x, 4096, 8192, T, H, E, K, 12288, 16384)
+        with pytest.raises(m.NfError, match="bias is a host array"):
+            m.router_topk_noalloc(1024, 4096, np.zeros(E, np.float32), T, H, E, K, 12288, 16384)
+        with pytest.raises(m.NfError, match="w is not a CUDA tensor"):
+            m.router_topk_noalloc(1024, 4096, 8192, T, H, E, K, 12288, torch.zeros((T, K)))
+
+        class FakeCuda:
+            def __init__(self, n, dtype):
+                self.is_cuda, self.dtype, self.n = True, dtype, n
+                self.device = type("D", (), {"index": 0})()
+
+            def is_contiguous(self):
+                return True
+
+            def numel(self):
+                return self.n
+
+            def data_ptr(self):
+                return 1 << 20
+
+        ok = dict(x=FakeCuda(T * H, "torch.int16"), rw=FakeCuda(E * H, "torch.int16"),
+                  b=FakeCuda(E, "torch.float32"), i=FakeCuda(T * K, "torch.int32"), w=FakeCuda(T * K, "torch.float32"))
+        args = lambda **kw: [{**ok, **kw}[k] for k in ("x", "rw", "b")] + [T, H, E, K] + \
+            [{**ok, **kw}[k] for k in ("i", "w")]  # noqa: E731
+        with pytest.raises(m.NfError, match="router_w holds"):
+            m.router_topk_noalloc(*args(rw=FakeCuda(E * H - 1, "torch.int16")))
+        with pytest.raises(m.NfError, match="idx has dtype"):
+            m.router_topk_noalloc(*args(i=FakeCuda(T * K, "torch.int64")))
+        assert not calls
+        st, msg = m.router_topk_noalloc(*args())  # every check passes: the call goes through
+        assert st == 0 and len(calls) == 1
+    finally:
+        m._lib = real

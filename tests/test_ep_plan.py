@@ -203,3 +203,54 @@ def test_mailbox_exchange_returns_every_row_to_its_slot(world):
             assert np.array_equal(got[:, 0], idxs[r].ravel())
             assert np.all(got[:, 1] == r)
             assert np.array_equal(got[:, 2], plans[r].slot.ravel())
+
+
+def _setup_rank(rank: int, world: int, port: int, out_dir: str, case: str) -> None:
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+
+    def exchange(rec):
+        out = [None] * world
+        dist.all_gather_object(out, rec)
+        return out
+
+    local = plan.NF_OK
+    if case == "nomem" and rank == world - 1:
+        local = plan.NF_ERR_NOMEM
+    if case == "memset" and rank == 0:
+        local = plan.NF_ERR_CUDA
+    mapped = not (case == "nomap" and rank == 1)
+    st, what, n = plan.setup_agreement(exchange, local, True, True, lambda: mapped)
+    # a last exchange after set-up: only reachable when every rank took the
+    # same number of set-up exchanges (gloo would otherwise mismatch or hang)
+    tail = exchange({"n": n})
+    assert all(t["n"] == n for t in tail)
+    np.save(os.path.join(out_dir, f"s{rank}.npy"), np.array([st, n], np.int64))
+    with open(os.path.join(out_dir, f"s{rank}.txt"), "w") as f:
+        f.write(what)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case,world", [("ok", 2), ("nomem", 2), ("memset", 4), ("nomap", 4)])
+def test_setup_agreement_every_rank_takes_the_same_exchanges(tmp_path, case, world):
+    """A rank whose mailbox allocation (or initialisation) fails still joins the
+    set-up exchange: every rank then returns that failure together, after the
+    same number of exchanges; a rank that cannot map a peer makes every rank
+    fall back to NCCL together."""
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_setup_rank, args=(world, _free_port(), str(tmp_path), case), nprocs=world,
+                       start_method="spawn", join=True)
+    res = [np.load(tmp_path / f"s{r}.npy") for r in range(world)]
+    msgs = [(tmp_path / f"s{r}.txt").read_text() for r in range(world)]
+    assert len({tuple(r) for r in res}) == 1 and len(set(msgs)) == 1  # every rank agrees
+    st, n = int(res[0][0]), int(res[0][1])
+    if case == "ok":
+        assert (st, msgs[0], n) == (plan.NF_OK, "nvlink", 2)
+    elif case == "nomem":
+        assert st == plan.NF_ERR_NOMEM and f"rank {world - 1}" in msgs[0] and n == 1
+    elif case == "memset":
+        assert st == plan.NF_ERR_CUDA and "rank 0 (initialisation)" in msgs[0] and n == 1
+    else:
+        assert (st, msgs[0], n) == (plan.NF_OK, "nccl", 3)

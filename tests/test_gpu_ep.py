@@ -1,8 +1,8 @@
-"""Expert parallelism on 2 GPUs (one process per GPU) against one GPU holding
-every expert: the layer outputs and routes must be identical bit for bit,
-over both exchanges inside the library -- NVLink peer memory (CUDA IPC
-mailboxes, run in graph mode for several steps) and NCCL point-to-point.
-Skipped on fewer than two GPUs."""
+"""Expert parallelism on 2 GPUs and on every GPU of the box (up to 8; one
+process per GPU) against one GPU holding every expert: the layer outputs and
+routes must be identical bit for bit, over both exchanges inside the library
+-- NVLink peer memory (CUDA IPC mailboxes, run in graph mode for several
+steps) and NCCL point-to-point.  Skipped on fewer than two GPUs."""
 import os
 import socket
 import sys
@@ -86,12 +86,15 @@ def _rank(rank: int, world: int, port: int, out_dir: str, case: str, transport: 
 
 @pytest.mark.parametrize("transport", ["nvlink", "nccl"])
 @pytest.mark.parametrize("case", ["c1", "uneven", "skewed"])
-def test_ep2_matches_one_gpu(tmp_path, case, transport):
-    if torch.cuda.device_count() < 2:
+@pytest.mark.parametrize("ranks", ["two", "all"])
+def test_ep_matches_one_gpu(tmp_path, case, transport, ranks):
+    n = torch.cuda.device_count()
+    if n < 2:
         pytest.skip("needs 2 GPUs")
+    world = 2 if ranks == "two" else min(n, 8)
+    if ranks == "all" and world == 2:
+        pytest.skip("only two GPUs: covered by the two-rank case")
     import torch.multiprocessing as mp
-
-    world = 2
     mp.start_processes(_rank, args=(world, _free_port(), str(tmp_path), case, transport), nprocs=world,
                        start_method="spawn", join=True)
     m = nfm()

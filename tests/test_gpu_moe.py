@@ -294,3 +294,60 @@ def test_group_limited_routing_through_the_layer():
     assert np.all(np.array([np.unique(r // 8).size for r in idx]) <= 4)
     assert_close(y, want_y, what="c1 group-limited")
     layer.close()
+
+
+def test_c2_prefill_layer_at_its_configuration():
+    """configs[2] exactly: 8192 tokens, H2048, the tuned bias, through the
+    large-batch permutation and dispatch path.  All 8192 routes and weights
+    bit-exact against the oracle's router; the E2M1 codes and E4M3 scales of
+    every live dispatched row bit-exact against the oracle's quantiser of its
+    token; the permutation exact; the layer output within the tolerance on a
+    deterministic subset of 135 tokens (tokens are independent, so a subset
+    is a full check of those tokens), with their down rows."""
+    lay, x_bits = wl.config_layer("c2")
+    T, H, K, E = x_bits.shape[0], lay.hidden, lay.top_k, lay.experts
+    x = wl.bf16_bits_to_f32(x_bits)
+    layer = make_layer(lay, T)
+    y, idx, w = gpu_forward(layer, x_bits)
+    _, want_idx, want_w = orc.route_tokens(lay, x)
+    assert np.array_equal(idx, want_idx)
+    assert np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
+    counts = np.bincount(idx.ravel(), minlength=E)
+    assert np.all(np.abs(counts - 512) <= 51), counts
+    # permutation: expert-major, token order inside a segment, 128-aligned segments
+    seg = fetch(layer, "seg_offset", np.int32, E + 1)
+    padded = (counts + 127) // 128 * 128
+    assert np.array_equal(seg, np.concatenate([[0], np.cumsum(padded)]).astype(np.int32))
+    rows_used = int(fetch(layer, "rows", np.int32, 1)[0])
+    assert rows_used == seg[-1]
+    row_token = fetch(layer, "row_token", np.int32, rows_used)
+    pair_row = fetch(layer, "pair_row", np.int32, T * K).reshape(T, K)
+    for e in range(E):
+        toks = np.nonzero((idx == e).any(axis=1))[0]
+        assert np.array_equal(row_token[seg[e]:seg[e] + toks.size], toks)
+        assert np.all(row_token[seg[e] + toks.size:seg[e + 1]] == -1)
+    p_of = np.argmax(idx[:, :, None] == np.arange(E)[None, None, :], axis=1)  # [T, E]: pick of expert e
+    tt, kk = np.meshgrid(np.arange(T), np.arange(K), indexing="ij")
+    assert np.array_equal(row_token[pair_row], tt)
+    assert np.all(p_of[tt, idx] == kk)
+    # dispatched activation codes and scales of every live row
+    codes = fetch(layer, "act_codes", np.uint8, rows_used * H // 2).reshape(rows_used, H // 2)
+    sf = m.sf_from_atoms(fetch(layer, "act_sf", np.uint8, rows_used * H // 16), rows_used, H // 16)
+    _, want_codes, want_sf = orc.quant_codes(orc.port(), x, float(lay.gate_in[0]))
+    live = row_token >= 0
+    assert int(live.sum()) == T * K
+    assert np.array_equal(codes[live], want_codes[row_token[live]])
+    assert np.array_equal(sf[live], want_sf[row_token[live]])
+    # layer output and down rows on a deterministic subset
+    sel = np.arange(0, T, 61)
+    assert sel.size >= 128
+    want_y, sel_idx, _ = orc.moe_layer(orc.port(), lay, x[sel])
+    assert np.array_equal(sel_idx, idx[sel])
+    assert_close(y[sel], want_y, what="c2 y (subset)")
+    down = fetch(layer, "down", np.uint16, rows_used * H).reshape(rows_used, H)
+    for t in sel[::9]:
+        for p in range(K):
+            _, want_d = orc.expert_forward(lay, int(idx[t, p]), x[t])
+            assert_close(wl.bf16_bits_to_f32(down[pair_row[t, p]]), want_d, max_abs=MAX_ABS, min_cos=0.999,
+                         what=f"c2 down t{t} p{p}")
+    layer.close()

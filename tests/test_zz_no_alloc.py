@@ -1,5 +1,7 @@
 """nf_router_topk_noalloc (router top-k with no device allocation, scratch in
-a static device array) against the handle's nf_moe_route on the same inputs.
+a static device array) against the handle's nf_moe_route and against the CPU
+oracle's router (gemv_bf16 + router_select restated, pinned to the
+reference) on the same inputs: indices equal and weights equal bit for bit.
 
 This file sorts last so that it runs both after every other GPU test and,
 when run alone in a fresh process, with its first call doing the one-time
@@ -7,15 +9,20 @@ set-up itself (the first test calls it before any handle exists)."""
 import numpy as np
 import pytest
 
-from helpers import nfm, workload
+from helpers import nfm, oracle, workload
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
-wl, m = workload(), nfm()
+wl, m, orc = workload(), nfm(), oracle()
 
-# Routes are bit-exact in both entry points; the weights are compared with
-# this absolute tolerance (they are expected to agree exactly).
-W_TOL = 1e-6
+
+def assert_same_routes(got, want, what):
+    """Indices equal; weights equal bit for bit (the routes are bit-exact)."""
+    idx, w = got
+    want_idx, want_w = want
+    assert np.array_equal(idx, want_idx), f"{what}: indices differ"
+    assert np.array_equal(np.asarray(w, np.float32).view(np.uint32),
+                          np.asarray(want_w, np.float32).view(np.uint32)), f"{what}: weights differ"
 
 
 def noalloc(lay, x, rw, bias, T, **kw):
@@ -58,10 +65,11 @@ def test_noalloc_matches_route_on_two_calls(cfg, tokens):
     x, rw, bias = device_inputs(lay, x_bits)
     first = noalloc(lay, x, rw, bias, T)   # before any handle: the call sets itself up
     second = noalloc(lay, x, rw, bias, T)  # a second call in a row reuses the scratch
-    want_idx, want_w = handle_route(lay, x, T)
-    for idx, w in (first, second):
-        assert np.array_equal(idx, want_idx)
-        assert float(np.max(np.abs(w - want_w))) <= W_TOL
+    want = handle_route(lay, x, T)
+    _, o_idx, o_w = orc.route_tokens(lay, wl.bf16_bits_to_f32(x_bits))
+    for i, got in enumerate((first, second)):
+        assert_same_routes(got, want, f"call {i} vs nf_moe_route")
+        assert_same_routes(got, (o_idx, o_w), f"call {i} vs oracle")
 
 
 def test_noalloc_group_limited_matches_route():
@@ -69,10 +77,11 @@ def test_noalloc_group_limited_matches_route():
     T = x_bits.shape[0]
     x, rw, bias = device_inputs(lay, x_bits)
     got = [noalloc(lay, x, rw, bias, T, n_group=8, topk_group=4) for _ in range(2)]
-    want_idx, want_w = handle_route(lay, x, T, n_group=8, topk_group=4)
-    for idx, w in got:
-        assert np.array_equal(idx, want_idx)
-        assert float(np.max(np.abs(w - want_w))) <= W_TOL
+    want = handle_route(lay, x, T, n_group=8, topk_group=4)
+    _, o_idx, o_w = orc.route_tokens(lay, wl.bf16_bits_to_f32(x_bits), n_group=8, topk_group=4)
+    for i, g in enumerate(got):
+        assert_same_routes(g, want, f"group-limited call {i} vs nf_moe_route")
+        assert_same_routes(g, (o_idx, o_w), f"group-limited call {i} vs oracle")
 
 
 def test_noalloc_rejects_batches_beyond_the_scratch():
