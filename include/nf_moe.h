@@ -283,6 +283,59 @@ NF_API int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int w
 enum { NF_EP_NONE = 0, NF_EP_NCCL = 1, NF_EP_NVLINK = 2 };
 NF_API int nf_moe_ep_transport(const nf_moe* handle);
 
+/* ---- tensor-parallel BF16 linears ------------------------------------------
+ * The reference splits every BF16 projection by output rows over its two
+ * ranks and swaps the halves over a socket: apply_rows
+ * (src/text_forward.cpp:803-819) runs gemv_bf16 (:497-508) on rank r's rows,
+ * gather_rows (:242-256) gives every rank the whole vector; linear_bf16
+ * (:821-830) and the lm_head (:656-667, lm_head_logits :760-767) use it, at
+ * the ExecutionPlan's collective boundaries (src/execution_plan.cpp:66-70).
+ * A group of `world` GPUs of one node (1-8, one handle per rank and GPU)
+ * replaces both steps: each rank computes its rows
+ * [rank rows / world, (rank + 1) rows / world) -- for world = 2 the
+ * reference's halves -- with gemv_bf16's exact arithmetic and stores them
+ * into every rank's gather buffer over NVLink (CUDA IPC, bounded-wait epoch
+ * flags), or NCCL point-to-point when the ranks cannot map each other's
+ * buffers (NF_TP_TRANSPORT=nccl forces it).  Results are bit-identical to
+ * gemv_bf16 over all rows on one rank, whatever the world size. */
+typedef struct nf_tp nf_tp;
+/* The row block [*row0, *row1) rank `rank` of `world` computes. */
+NF_API int nf_tp_split(int64_t rows, int rank, int world, int64_t* row0, int64_t* row1);
+/* Creates rank `rank`'s handle on `device` (collective for world > 1: every
+ * rank calls it with the same group id from nf_ep_unique_id; world = 1 needs
+ * no id).  The handle holds two gather buffers of max_tokens x max_rows F32. */
+NF_API int nf_tp_create(int device, int rank, int world, const uint8_t* group_id, int id_len, int max_tokens,
+                        int64_t max_rows, nf_tp** out);
+NF_API void nf_tp_destroy(nf_tp* handle);
+/* Message of the handle's last failure; NULL handle: the last failed create
+ * on this thread. */
+NF_API const char* nf_tp_last_error(const nf_tp* handle);
+/* NF_EP_NONE (world 1), NF_EP_NVLINK or NF_EP_NCCL. */
+NF_API int nf_tp_transport(const nf_tp* handle);
+/* linear_bf16 over `tokens` tokens (every rank makes the call, in the same
+ * order, also with tokens == 0):
+ *   w_dev  BF16 [row1 - row0, cols]: this rank's rows of the [rows, cols]
+ *          weight (nf_tp_split), 8-byte aligned, cols % 4 == 0
+ *   x_dev  F32 [tokens, cols], the same on every rank, 16-byte aligned
+ *   y_dev  F32 [tokens, rows] or NULL: the whole output on every rank (it
+ *          also stays in the handle until the next call; nf_tp_argmax reads
+ *          it there).
+ * Enqueued on `stream`; results of a call are valid until the handle's next
+ * call, which must be enqueued on the same stream.  A peer that never takes
+ * part makes the bounded waits give up: nf_tp_sync then reports
+ * NF_ERR_TIMEOUT and the group must be recreated. */
+NF_API int nf_tp_linear_bf16(nf_tp* handle, const uint16_t* w_dev, int64_t rows, int64_t cols, const float* x_dev,
+                             int tokens, float* y_dev, void* stream);
+/* The reference's greedy pick over the last call's output (TextModel::argmax,
+ * src/text_forward.cpp:668-681): per token the lowest row with the greatest
+ * value; NaN never wins, a NaN in row 0 is kept.  idx_dev INT32 [tokens]. */
+NF_API int nf_tp_argmax(nf_tp* handle, int tokens, int64_t rows, int32_t* idx_dev, void* stream);
+/* Device address of the last call's [tokens, rows] output inside the handle
+ * (synchronous: reads the device's call counter). */
+NF_API int nf_tp_result(nf_tp* handle, const float** out_dev);
+/* Waits for `stream` and reports a bounded wait that gave up. */
+NF_API int nf_tp_sync(nf_tp* handle, void* stream);
+
 /* ---- router top-k without device allocation ------------------------------
  * No counterpart in the reference: its router runs inside moe() on host
  * buffers (src/text_forward.cpp:926-931).  This entry point is for callers

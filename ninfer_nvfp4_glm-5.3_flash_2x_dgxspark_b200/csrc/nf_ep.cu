@@ -34,8 +34,7 @@
 // counts.
 #include "nf_handle.h"
 
-#include <dlfcn.h>
-#include <nccl.h>
+#include "nf_nccl.h"
 
 #include <cstdio>
 #include <cstdlib>
@@ -47,47 +46,6 @@ using namespace nf;
 
 namespace {
 
-struct NcclApi {
-    bool ok = false;
-    std::string why;
-    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
-    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
-    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
-    ncclResult_t (*group_start)() = nullptr;
-    ncclResult_t (*group_end)() = nullptr;
-    ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
-    ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
-    const char* (*error_string)(ncclResult_t) = nullptr;
-};
-
-NcclApi& nccl() {
-    static NcclApi api;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-        if (!lib) lib = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
-        if (!lib) {
-            api.why = "libnccl.so.2 not found";
-            return;
-        }
-        auto sym = [&](const char* name) { return dlsym(lib, name); };
-        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
-        api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
-        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
-        api.group_start = reinterpret_cast<decltype(api.group_start)>(sym("ncclGroupStart"));
-        api.group_end = reinterpret_cast<decltype(api.group_end)>(sym("ncclGroupEnd"));
-        api.send = reinterpret_cast<decltype(api.send)>(sym("ncclSend"));
-        api.recv = reinterpret_cast<decltype(api.recv)>(sym("ncclRecv"));
-        api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
-        api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.group_start && api.group_end &&
-                 api.send && api.recv && api.error_string;
-        if (!api.ok) api.why = "libnccl.so.2 lacks the point-to-point API";
-    });
-    return api;
-}
-
-const char* nccl_str(ncclResult_t r) { return nccl().error_string ? nccl().error_string(r) : "unknown"; }
-
 int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 
 // The transport an EP group uses when NF_EP_TRANSPORT is not set.
@@ -96,32 +54,11 @@ constexpr bool kEpNvlinkDefault = true;
 // Bytes of one record of the set-up exchanges (ep_allgather_host).
 constexpr size_t kEpRecBytes = 256;
 
-// Every rank sends `bytes` bytes from `mine` to every rank (its own slot
-// included) and receives every rank's into all[world][bytes]: a gather of
-// small host records through the handle's staging buffer (h->ep_stage,
-// allocated before the communicator exists), used at set-up only.  The
-// sends and receives are posted whatever happened locally, so a rank whose
-// copy failed never leaves the others waiting: its staging slot is cleared
-// first, so the others then receive a zeroed record, whose `ok` word reads
-// as a failure.  Returns false when this rank's copy or the exchange failed.
+// Every rank's copy of a small set-up record (nccl_allgather_records over
+// the handle's staging buffer, h->ep_stage).
 bool ep_allgather_host(nf_moe* h, const void* mine, size_t bytes, void* all) {
-    NcclApi& api = nccl();
-    ncclComm_t comm = static_cast<ncclComm_t>(h->nccl);
-    const int R = h->ep_world;
-    uint8_t* buf = h->ep_stage;
-    if (!buf || bytes > kEpRecBytes) return false;  // the same on every rank: no exchange is posted anywhere
-    const bool local = cudaMemset(buf, 0, bytes) == cudaSuccess &&
-                       cudaMemcpy(buf, mine, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
-    if (!local) cudaGetLastError();
-    ncclResult_t r = api.group_start();
-    for (int p = 0; p < R && r == ncclSuccess; ++p) {
-        r = api.send(buf, bytes, ncclUint8, p, comm, h->stream);
-        if (r == ncclSuccess) r = api.recv(buf + bytes * (p + 1), bytes, ncclUint8, p, comm, h->stream);
-    }
-    const ncclResult_t r2 = api.group_end();
-    const bool ok = r == ncclSuccess && r2 == ncclSuccess && cudaStreamSynchronize(h->stream) == cudaSuccess &&
-                    cudaMemcpy(all, buf + bytes, bytes * R, cudaMemcpyDeviceToHost) == cudaSuccess;
-    return ok && local;
+    if (bytes > kEpRecBytes) return false;  // the same on every rank: no exchange is posted anywhere
+    return nccl_allgather_records(h->nccl, h->ep_stage, h->stream, h->ep_world, mine, bytes, all);
 }
 
 // Peer-memory transport set-up (collective: every rank calls it after the

@@ -40,7 +40,8 @@ EXPORTED = [
     "nf_moe_sync", "nf_moe_route", "nf_moe_debug_tensor", "nf_moe_debug_read", "nf_nvfp4_dequantize", "nf_nvfp4_quantize",
     "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck", "nf_moe_set_graph_mode",
     "nf_router_topk_noalloc", "nf_ep_unique_id", "nf_moe_create_ep", "nf_moe_create_dense",
-    "nf_moe_ep_transport",
+    "nf_moe_ep_transport", "nf_tp_split", "nf_tp_create", "nf_tp_destroy", "nf_tp_last_error", "nf_tp_transport",
+    "nf_tp_linear_bf16", "nf_tp_argmax", "nf_tp_result", "nf_tp_sync",
 ]
 STAGES = ["router", "permute", "gate_up", "down", "shared", "combine"]
 
@@ -94,6 +95,15 @@ def load() -> ctypes.CDLL:
         "nf_moe_create_ep": ([ctypes.POINTER(Desc), I32, I32, I32, ctypes.c_char_p, I32, ctypes.POINTER(P)], I32),
         "nf_moe_create_dense": ([I32, I32, F, I32, I32, ctypes.POINTER(P)], I32),
         "nf_moe_ep_transport": ([P], I32),
+        "nf_tp_split": ([I64, I32, I32, ctypes.POINTER(I64), ctypes.POINTER(I64)], I32),
+        "nf_tp_create": ([I32, I32, I32, ctypes.c_char_p, I32, I32, I64, ctypes.POINTER(P)], I32),
+        "nf_tp_destroy": ([P], None),
+        "nf_tp_last_error": ([P], ctypes.c_char_p),
+        "nf_tp_transport": ([P], I32),
+        "nf_tp_linear_bf16": ([P, P, I64, I64, P, I32, P, P], I32),
+        "nf_tp_argmax": ([P, I32, I64, P, P], I32),
+        "nf_tp_result": ([P, ctypes.POINTER(P)], I32),
+        "nf_tp_sync": ([P, P], I32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -505,6 +515,76 @@ def router_topk_noalloc(x_dev, router_w_dev, bias_dev, tokens: int, hidden: int,
 
 
 EP_ID_BYTES = 128
+
+
+def tp_split(rows: int, rank: int, world: int) -> tuple[int, int]:
+    """Row block [row0, row1) that rank `rank` of `world` computes."""
+    a, b = ctypes.c_int64(), ctypes.c_int64()
+    st = load().nf_tp_split(rows, rank, world, ctypes.byref(a), ctypes.byref(b))
+    if st != NF_OK:
+        raise NfError(st, "bad tensor-parallel split arguments")
+    return a.value, b.value
+
+
+class TpGroup:
+    """This rank's handle of a tensor-parallel group (nf_tp_*): BF16 linears
+    split by output rows over `world` GPUs with the rows gathered on every
+    rank, the GPU form of the reference's apply_rows + gather_rows
+    (src/text_forward.cpp:242-256, 803-830).  group_id from ep_group_id() on
+    one rank, shared by all (not needed for world = 1)."""
+
+    def __init__(self, max_tokens: int, max_rows: int, *, rank: int = 0, world: int = 1,
+                 group_id: bytes | None = None, device: int = 0):
+        self.lib = load()
+        h = ctypes.c_void_p()
+        gid = group_id if group_id is not None else None
+        st = self.lib.nf_tp_create(device, rank, world, gid, len(gid) if gid else 0, max_tokens, max_rows,
+                                   ctypes.byref(h))
+        if st != NF_OK:
+            raise NfError(st, self.lib.nf_tp_last_error(None).decode())
+        self.h, self.rank, self.world, self.device = h, rank, world, device
+        self.max_tokens, self.max_rows = max_tokens, max_rows
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.nf_tp_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, st: int) -> None:
+        if st != NF_OK:
+            raise NfError(st, self.lib.nf_tp_last_error(self.h).decode())
+
+    def split(self, rows: int) -> tuple[int, int]:
+        return tp_split(rows, self.rank, self.world)
+
+    def transport(self) -> str:
+        return {0: "none", 1: "nccl", 2: "nvlink"}[self.lib.nf_tp_transport(self.h)]
+
+    def linear_bf16(self, w_shard, rows: int, cols: int, x, tokens: int, y=None, stream=0) -> None:
+        """linear_bf16 on this rank's rows: w_shard BF16 bits [row1 - row0, cols]
+        (see split), x fp32 [tokens, cols]; y fp32 [tokens, rows] (optional)
+        receives the whole output.  Checked like MoeLayer.forward."""
+        r0, r1 = self.split(rows)
+        d = self.device
+        n = tokens if 0 <= tokens <= self.max_tokens else 0
+        self._check(self.lib.nf_tp_linear_bf16(self.h, _dev(w_shard, (r1 - r0) * cols, _X_DTYPES, "w_shard", d),
+                                               rows, cols, _dev(x, n * cols, ("torch.float32",), "x", d), tokens,
+                                               _dev(y, n * rows, ("torch.float32",), "y", d), stream or None))
+
+    def argmax(self, tokens: int, rows: int, idx, stream=0) -> None:
+        """The reference's greedy pick over the last linear's output: idx int32 [tokens]."""
+        n = tokens if 0 <= tokens <= self.max_tokens else 0
+        self._check(self.lib.nf_tp_argmax(self.h, tokens, rows, _dev(idx, n, ("torch.int32",), "idx", self.device),
+                                          stream or None))
+
+    def sync(self, stream=0) -> None:
+        self._check(self.lib.nf_tp_sync(self.h, stream or None))
 
 
 def ep_group_id() -> bytes:
