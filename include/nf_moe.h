@@ -336,6 +336,84 @@ NF_API int nf_tp_result(nf_tp* handle, const float** out_dev);
 /* Waits for `stream` and reports a bounded wait that gave up. */
 NF_API int nf_tp_sync(nf_tp* handle, void* stream);
 
+/* ---- decoder stack (greedy decode) ------------------------------------------
+ * The reference's token step, TextModel::step + argmax
+ * (src/text_forward.cpp:625-698), over a synthetic decoder of the benchmark's
+ * shape: embedding (embed_row :753), per layer an attention block and the
+ * feed-forward that feed() selects (:892-907: the dense NVFP4 MLP :909-915,
+ * the NVFP4 MoE :924-963, or BF16 routed experts for the last layers), the
+ * final norm (:652-654) and the greedy token over the lm_head (:656-698).
+ * The attention block is BF16 GQA with per-head q/k RMSNorm and RoPE, the
+ * math of the reference's only GQA attention, draft_attention
+ * (:1216-1289): a = rmsnorm(x) (BF16), q/k/v = a . W^T, q and k normed
+ * (eps 1e-5) and rotated at the token's position, softmax(q.k / sqrt(128))
+ * over the sequence's cache, o = mix . Wo^T, h = x + o; the FFN input is
+ * rmsnorm_stash(h) (:267-276) and the layer output h + ffn.  One new token
+ * per sequence per step; the caches are BF16 [seq][kv_head][position][128].
+ * Limits: head_dim 128, q_heads = 8 kv_heads, hidden % 256 == 0. */
+typedef struct nf_stack_desc {
+    int32_t vocab;              /* vocabulary (embedding and lm_head rows) */
+    int32_t hidden;             /* H */
+    int32_t layers;             /* decoder layers */
+    int32_t dense_layers;       /* the first layers: dense NVFP4 MLP */
+    int32_t bf16_expert_layers; /* the last layers: MoE with BF16 routed experts */
+    int32_t dense_inter;        /* dense MLP intermediate size */
+    nf_moe_desc moe;            /* the MoE layers (hidden and max_tokens are taken from the stack) */
+    int32_t q_heads, kv_heads, head_dim;
+    float rope_theta;           /* RoPE base (rope_heads: 10000) */
+    float norm_eps;             /* input / post-attention / final RMSNorm epsilon */
+    int32_t max_batch;          /* sequences per step */
+    int32_t max_context;        /* cache positions per sequence */
+} nf_stack_desc;
+typedef struct nf_stack nf_stack;
+/* Tensor ids of nf_stack_bind_bf16 / _f32 (names of a layer's tensors in the
+ * stack's own checkpoint convention: layers.<l>.self_attn.{q,k,v,o}_proj,
+ * .input_layernorm, .post_attention_layernorm, .self_attn.{q,k}_norm). */
+enum {
+    NF_STACK_EMBED = 0,      /* BF16 [vocab, H] */
+    NF_STACK_LM_HEAD = 1,    /* BF16 [vocab, H] */
+    NF_STACK_Q_PROJ = 2,     /* BF16 [q_heads 128, H]  (per layer) */
+    NF_STACK_K_PROJ = 3,     /* BF16 [kv_heads 128, H] */
+    NF_STACK_V_PROJ = 4,     /* BF16 [kv_heads 128, H] */
+    NF_STACK_O_PROJ = 5,     /* BF16 [H, q_heads 128]  */
+    NF_STACK_ATTN_NORM = 6,  /* F32 [H] input_layernorm */
+    NF_STACK_FFN_NORM = 7,   /* F32 [H] post_attention_layernorm */
+    NF_STACK_Q_NORM = 8,     /* F32 [128] */
+    NF_STACK_K_NORM = 9,     /* F32 [128] */
+    NF_STACK_FINAL_NORM = 10 /* F32 [H] */
+};
+NF_API int nf_stack_create(const nf_stack_desc* desc, int device, nf_stack** out);
+NF_API void nf_stack_destroy(nf_stack* stack);
+NF_API const char* nf_stack_last_error(const nf_stack* stack);
+/* The feed-forward handle of a layer: bind its weights with nf_moe_bind_*
+ * and nf_moe_finalize (a dense handle for the first dense_layers). */
+NF_API nf_moe* nf_stack_layer_ffn(nf_stack* stack, int layer);
+NF_API int nf_stack_bind_bf16(nf_stack* stack, int which, int layer, const uint16_t* data_host, int64_t rows,
+                              int64_t cols);
+NF_API int nf_stack_bind_f32(nf_stack* stack, int which, int layer, const float* data_host, int64_t n);
+NF_API int nf_stack_finalize(nf_stack* stack);
+/* Device pointers of a layer's K and V caches, BF16 [max_batch][kv_heads]
+ * [max_context][128] (post-norm, post-RoPE keys), e.g. to load a history. */
+NF_API int nf_stack_kv_cache(nf_stack* stack, int layer, uint16_t** k_dev, uint16_t** v_dev);
+/* Copies a layer's whole K and V caches from host memory (the layout above,
+ * max_batch x kv_heads x max_context x 128 BF16 each): a loaded history or
+ * prefix.  Synchronous. */
+NF_API int nf_stack_load_kv(nf_stack* stack, int layer, const uint16_t* k_host, const uint16_t* v_host);
+/* Fills every layer's caches on the device with deterministic pseudo-random
+ * BF16 values in (-1, 1) derived from `seed`: a stand-in history for timing
+ * long contexts.  Synchronous. */
+NF_API int nf_stack_fill_kv(nf_stack* stack, uint64_t seed);
+/* One greedy decode step for `batch` sequences: sequence i takes token
+ * tokens_dev[i] at position positions_dev[i] (keys 0 .. position attended;
+ * the new key and value are written at that position), and next_dev[i]
+ * receives its greedy token.  final_dev (F32 [batch, H], optional)
+ * receives the final norm's output.  Asynchronous on `stream`. */
+NF_API int nf_stack_decode(nf_stack* stack, const int32_t* tokens_dev, const int32_t* positions_dev, int batch,
+                           int32_t* next_dev, float* final_dev, void* stream);
+/* Waits for `stream` and reports device-side failures (a token outside the
+ * vocabulary, a position outside the cache, a bounded wait). */
+NF_API int nf_stack_sync(nf_stack* stack, void* stream);
+
 /* ---- router top-k without device allocation ------------------------------
  * No counterpart in the reference: its router runs inside moe() on host
  * buffers (src/text_forward.cpp:926-931).  This entry point is for callers

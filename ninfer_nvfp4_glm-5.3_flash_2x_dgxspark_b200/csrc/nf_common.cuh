@@ -19,7 +19,8 @@ enum : int {
     NF_DEVERR_WAIT_EMPTY = 2,   // producer waited too long for a free stage
     NF_DEVERR_WAIT_ACC = 3,     // MMA / epilogue accumulator hand-off timed out
     NF_DEVERR_DRAIN = 4,        // teardown drain after an abort timed out
-    NF_DEVERR_EP_WAIT = 5       // an expert-parallel peer's rows or outputs never arrived
+    NF_DEVERR_EP_WAIT = 5,      // an expert-parallel peer's rows or outputs never arrived
+    NF_DEVERR_BAD_TOKEN = 6     // a token id outside the vocabulary, or a position outside the cache
 };
 
 // One second of %globaltimer (ns) per wait; the longest kernel here runs

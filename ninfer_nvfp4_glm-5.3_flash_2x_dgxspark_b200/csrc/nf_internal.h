@@ -124,6 +124,12 @@ bool make_tmap_blocked(CUtensorMap* map, const void* base, uint64_t bytes);
 cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
                         const GemmArgs& args, int grid, bool dependent, cudaStream_t st);
 int gemm_grid_size(int device);
+// Weight matrices the GEMMs stream are kept in "box order" (nf_moe.cu): 32 KB
+// blocks of 256 rows x 128 bytes, row-block major, K-block minor.
+int64_t box_order_bytes(int64_t rows, int64_t row_bytes);
+int64_t box_k_blocks(int64_t row_bytes);
+// Host row-major [rows, row_bytes] (rows % 256 == 0) -> device box order.
+cudaError_t upload_box_order(uint8_t* dst, const uint8_t* src, int64_t rows, int64_t row_bytes);
 
 // Launchers (nf_kernels.cu).
 // w_safe: every nonzero router weight has |w| in [2^-67, 2^63) (checked at
@@ -222,6 +228,30 @@ cudaError_t launch_format_selfcheck(unsigned long long* mismatches_dev, cudaStre
 // Builds the per-device lookup index of the router's sigmoid exception table
 // (once per device; the calling thread's current device).
 cudaError_t prepare_device_tables();
+
+// Attention side of a decoder layer (nf_attn.cu; head dimension 128).
+// A split of the context's partial softmax state: running max and sum.
+struct AttnPart {
+    float m, l;
+};
+constexpr int kAttnMaxSplitsHost = 64;  // splits of the context per (sequence, head)
+cudaError_t launch_embed(const uint16_t* table, int64_t vocab, int H, const int32_t* tok, int T, float* x, int* err,
+                         cudaStream_t st);
+// RMSNorm per row; h = a (+ the sum of b's slices), h_out optional; stash:
+// the rmsnorm_stash form.
+cudaError_t launch_rmsnorm(const float* a, const float* b, int b_slices, int64_t b_stride, float* h_out, const float* w,
+                           int rows, int n, float eps, int stash, uint16_t* y_bf16, float* y_f32, cudaStream_t st);
+cudaError_t launch_qk_norm_rope(const float* qkv, int slices, int64_t stride, int T, int nq, int nkv,
+                                const float* q_norm, const float* k_norm, float eps, float theta, const int32_t* pos,
+                                int L_max, float* q_out, uint16_t* kc, uint16_t* vc, int* err, cudaStream_t st);
+// splits of the context for T sequences (the partial buffers hold
+// T * nq * splits pairs of floats and T * nq * splits * 128 floats)
+int attn_splits(int T, int nkv, int L_max, int sms);
+cudaError_t launch_gqa_decode(const float* q, const uint16_t* kc, const uint16_t* vc, const int32_t* pos, int T,
+                              int nq, int nkv, int L_max, int splits, AttnPart* part_ml, float* part_acc,
+                              uint16_t* out, int* err, cudaStream_t st);
+
+cudaError_t launch_fill_bf16_hash(uint16_t* p, int64_t n, uint64_t seed, cudaStream_t st);
 
 constexpr int kChunkTokHost = 128;  // tokens per permutation chunk (nf_kernels.cu kChunkTok)
 // Per-device one-time state (kernel attributes, lookup tables) is kept in

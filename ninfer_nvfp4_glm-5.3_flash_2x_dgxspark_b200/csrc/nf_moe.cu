@@ -160,6 +160,14 @@ cudaError_t upload_blocked_half(uint8_t* dst, const uint8_t* src, int64_t rows, 
 
 }  // namespace
 
+namespace nf {
+int64_t box_order_bytes(int64_t rows, int64_t row_bytes) { return blocked_bytes(rows, row_bytes); }
+int64_t box_k_blocks(int64_t row_bytes) { return k_blocks(row_bytes); }
+cudaError_t upload_box_order(uint8_t* dst, const uint8_t* src, int64_t rows, int64_t row_bytes) {
+    return upload_blocked(dst, src, rows, row_bytes);
+}
+}  // namespace nf
+
 extern "C" {
 
 const char* nf_status_string(int s) {

@@ -41,7 +41,9 @@ EXPORTED = [
     "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck", "nf_moe_set_graph_mode",
     "nf_router_topk_noalloc", "nf_ep_unique_id", "nf_moe_create_ep", "nf_moe_create_dense",
     "nf_moe_ep_transport", "nf_tp_split", "nf_tp_create", "nf_tp_destroy", "nf_tp_last_error", "nf_tp_transport",
-    "nf_tp_linear_bf16", "nf_tp_argmax", "nf_tp_result", "nf_tp_sync",
+    "nf_tp_linear_bf16", "nf_tp_argmax", "nf_tp_result", "nf_tp_sync", "nf_stack_create", "nf_stack_destroy",
+    "nf_stack_last_error", "nf_stack_layer_ffn", "nf_stack_bind_bf16", "nf_stack_bind_f32", "nf_stack_finalize",
+    "nf_stack_kv_cache", "nf_stack_decode", "nf_stack_sync", "nf_stack_load_kv", "nf_stack_fill_kv",
 ]
 STAGES = ["router", "permute", "gate_up", "down", "shared", "combine"]
 
@@ -52,6 +54,16 @@ class Desc(ctypes.Structure):
         ("inter", ctypes.c_int32), ("shared_inter", ctypes.c_int32), ("n_group", ctypes.c_int32),
         ("topk_group", ctypes.c_int32), ("normalize", ctypes.c_int32), ("routed_scaling", ctypes.c_float),
         ("swiglu_limit", ctypes.c_float), ("expert_kind", ctypes.c_int32), ("max_tokens", ctypes.c_int32),
+    ]
+
+
+class StackDesc(ctypes.Structure):
+    _fields_ = [
+        ("vocab", ctypes.c_int32), ("hidden", ctypes.c_int32), ("layers", ctypes.c_int32),
+        ("dense_layers", ctypes.c_int32), ("bf16_expert_layers", ctypes.c_int32), ("dense_inter", ctypes.c_int32),
+        ("moe", Desc), ("q_heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+        ("rope_theta", ctypes.c_float), ("norm_eps", ctypes.c_float), ("max_batch", ctypes.c_int32),
+        ("max_context", ctypes.c_int32),
     ]
 
 
@@ -104,6 +116,18 @@ def load() -> ctypes.CDLL:
         "nf_tp_argmax": ([P, I32, I64, P, P], I32),
         "nf_tp_result": ([P, ctypes.POINTER(P)], I32),
         "nf_tp_sync": ([P, P], I32),
+        "nf_stack_create": ([ctypes.POINTER(StackDesc), I32, ctypes.POINTER(P)], I32),
+        "nf_stack_destroy": ([P], None),
+        "nf_stack_last_error": ([P], ctypes.c_char_p),
+        "nf_stack_layer_ffn": ([P, I32], P),
+        "nf_stack_bind_bf16": ([P, I32, I32, P, I64, I64], I32),
+        "nf_stack_bind_f32": ([P, I32, I32, P, I64], I32),
+        "nf_stack_finalize": ([P], I32),
+        "nf_stack_kv_cache": ([P, I32, ctypes.POINTER(P), ctypes.POINTER(P)], I32),
+        "nf_stack_decode": ([P, P, P, I32, P, P, P], I32),
+        "nf_stack_sync": ([P, P], I32),
+        "nf_stack_load_kv": ([P, I32, P, P], I32),
+        "nf_stack_fill_kv": ([P, ctypes.c_uint64], I32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -180,7 +204,19 @@ class MoeLayer:
         self.device = device
         self.ep = ep
 
+    @classmethod
+    def borrow(cls, handle: int, desc: Desc, device: int) -> "MoeLayer":
+        """A view of a handle another object owns (a decoder stack's layer):
+        binding and forwards work, close() leaves the handle alone."""
+        self = cls.__new__(cls)
+        self.lib, self.desc, self.h, self.device, self.ep = load(), desc, ctypes.c_void_p(handle), device, None
+        self.borrowed = True
+        return self
+
     def close(self) -> None:
+        if getattr(self, "borrowed", False):
+            self.h = None
+            return
         if getattr(self, "h", None):
             self.lib.nf_moe_destroy(self.h)
             self.h = None
@@ -619,3 +655,123 @@ def sf_from_atoms(atoms: np.ndarray, rows: int, kgroups: int) -> np.ndarray:
     r = np.arange(rows)[:, None]
     k = np.arange(kgroups)[None, :]
     return np.asarray(atoms)[sf_atom_offset(r, k, kgroups)]
+
+
+STACK_EMBED, STACK_LM_HEAD, STACK_Q_PROJ, STACK_K_PROJ, STACK_V_PROJ, STACK_O_PROJ = 0, 1, 2, 3, 4, 5
+STACK_ATTN_NORM, STACK_FFN_NORM, STACK_Q_NORM, STACK_K_NORM, STACK_FINAL_NORM = 6, 7, 8, 9, 10
+
+
+class DecoderStack:
+    """A decoder stack for greedy decode on one GPU (nf_stack_*): embedding,
+    per layer GQA attention + the layer's feed-forward (dense NVFP4 MLP,
+    NVFP4 MoE, BF16-expert MoE), final norm, lm_head and greedy pick -- the
+    reference's TextModel::step + argmax (src/text_forward.cpp:625-698)."""
+
+    def __init__(self, *, vocab: int, hidden: int, layers: int, dense_layers: int, bf16_expert_layers: int,
+                 dense_inter: int, experts: int, top_k: int, inter: int, shared_inter: int, routed_scaling: float,
+                 swiglu_limit: float = 10.0, q_heads: int, kv_heads: int, head_dim: int = 128,
+                 rope_theta: float = 10000.0, norm_eps: float = 1e-5, max_batch: int = 1, max_context: int = 2048,
+                 device: int = 0):
+        self.lib = load()
+        moe = Desc(hidden, experts, top_k, inter, shared_inter, 1, 1, 1, routed_scaling, swiglu_limit, EXPERTS_NVFP4,
+                   max_batch)
+        self.desc = StackDesc(vocab, hidden, layers, dense_layers, bf16_expert_layers, dense_inter, moe, q_heads,
+                              kv_heads, head_dim, rope_theta, norm_eps, max_batch, max_context)
+        h = ctypes.c_void_p()
+        st = self.lib.nf_stack_create(ctypes.byref(self.desc), device, ctypes.byref(h))
+        if st != NF_OK:
+            raise NfError(st, self.lib.nf_stack_last_error(None).decode())
+        self.h, self.device = h, device
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.nf_stack_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, st: int) -> None:
+        if st != NF_OK:
+            raise NfError(st, self.lib.nf_stack_last_error(self.h).decode())
+
+    def ffn(self, layer: int):
+        """The layer's feed-forward handle (a borrowed MoeLayer / DenseMlp view)."""
+        d = self.desc
+        ptr = self.lib.nf_stack_layer_ffn(self.h, layer)
+        if not ptr:
+            raise NfError(1, f"layer {layer} out of range")
+        if layer < d.dense_layers:
+            desc = Desc(d.hidden, 1, 1, d.dense_inter, 0, 1, 1, 1, 1.0, d.moe.swiglu_limit, EXPERTS_NVFP4, d.max_batch)
+            return DenseMlp.borrow(ptr, desc, self.device)
+        bf16 = layer >= d.layers - d.bf16_expert_layers
+        m = d.moe
+        desc = Desc(d.hidden, m.experts, m.top_k, m.inter, m.shared_inter, 1, 1, 1, m.routed_scaling, m.swiglu_limit,
+                    EXPERTS_BF16 if bf16 else EXPERTS_NVFP4, d.max_batch)
+        return MoeLayer.borrow(ptr, desc, self.device)
+
+    def bind_bf16(self, which: int, data: np.ndarray, layer: int = 0) -> None:
+        data = np.ascontiguousarray(data, dtype=np.uint16)
+        rows, cols = data.shape
+        self._check(self.lib.nf_stack_bind_bf16(self.h, which, layer, _ptr(data), rows, cols))
+
+    def bind_f32(self, which: int, data: np.ndarray, layer: int = 0) -> None:
+        data = np.ascontiguousarray(data, dtype=np.float32)
+        self._check(self.lib.nf_stack_bind_f32(self.h, which, layer, _ptr(data), data.size))
+
+    def bind_model(self, model) -> None:
+        """Binds a workload.StackModel (every layer's attention, norms and FFN)
+        and finalizes."""
+        self.bind_bf16(STACK_EMBED, model.embed)
+        self.bind_bf16(STACK_LM_HEAD, model.lm_head)
+        self.bind_f32(STACK_FINAL_NORM, model.final_norm)
+        for l, ly in enumerate(model.layers):
+            self.bind_bf16(STACK_Q_PROJ, ly.wq, l)
+            self.bind_bf16(STACK_K_PROJ, ly.wk, l)
+            self.bind_bf16(STACK_V_PROJ, ly.wv, l)
+            self.bind_bf16(STACK_O_PROJ, ly.wo, l)
+            self.bind_f32(STACK_ATTN_NORM, ly.attn_norm, l)
+            self.bind_f32(STACK_FFN_NORM, ly.ffn_norm, l)
+            self.bind_f32(STACK_Q_NORM, ly.q_norm, l)
+            self.bind_f32(STACK_K_NORM, ly.k_norm, l)
+            self.ffn(l).bind_layer(ly.ffn)
+        self._check(self.lib.nf_stack_finalize(self.h))
+
+    def kv_cache(self, layer: int) -> tuple[int, int]:
+        """Device addresses of the layer's K and V caches (BF16 [max_batch]
+        [kv_heads][max_context][128])."""
+        k, v = ctypes.c_void_p(), ctypes.c_void_p()
+        self._check(self.lib.nf_stack_kv_cache(self.h, layer, ctypes.byref(k), ctypes.byref(v)))
+        return k.value, v.value
+
+    def load_kv(self, layer: int, k: np.ndarray, v: np.ndarray) -> None:
+        """Host BF16 bits [max_batch, kv_heads, max_context, 128] into the layer's caches."""
+        d = self.desc
+        shape = (d.max_batch, d.kv_heads, d.max_context, d.head_dim)
+        k = np.ascontiguousarray(k, dtype=np.uint16)
+        v = np.ascontiguousarray(v, dtype=np.uint16)
+        if k.shape != shape or v.shape != shape:
+            raise NfError(2, f"cache arrays must be {shape}")
+        self._check(self.lib.nf_stack_load_kv(self.h, layer, _ptr(k), _ptr(v)))
+
+    def fill_kv(self, seed: int) -> None:
+        """Every layer's caches filled on the device with pseudo-random BF16 values."""
+        self._check(self.lib.nf_stack_fill_kv(self.h, seed))
+
+    def decode(self, tokens_dev, positions_dev, batch: int, next_dev, final_dev=None, stream=0) -> None:
+        """One greedy step: int32 tokens / positions [batch] -> int32 next [batch]
+        (final fp32 [batch, H] optional).  Asynchronous on `stream`."""
+        d, dv = self.desc, self.device
+        n = batch if 0 <= batch <= d.max_batch else 0
+        i32 = ("torch.int32",)
+        self._check(self.lib.nf_stack_decode(self.h, _dev(tokens_dev, n, i32, "tokens", dv),
+                                             _dev(positions_dev, n, i32, "positions", dv), batch,
+                                             _dev(next_dev, n, i32, "next", dv),
+                                             _dev(final_dev, n * d.hidden, ("torch.float32",), "final", dv),
+                                             stream or None))
+
+    def sync(self, stream=0) -> None:
+        self._check(self.lib.nf_stack_sync(self.h, stream or None))

@@ -277,3 +277,84 @@ def make_dense_layer(hidden: int, inter: int, seed: int) -> DenseLayer:
         gate_ws2=f32(np.float32(1) / np.float32(448)), gate_in=f32(np.float32(1) / np.float32(6)),
         up_ws2=f32(np.float32(1) / np.float32(448)), up_in=f32(np.float32(1) / np.float32(6)),
         down_ws2=f32(np.float32(1) / np.float32(448)), down_in=f32(np.float32(1) / np.float32(6)))
+
+
+# ---- the synthetic decoder stack of configs[4] --------------------------------
+STACK_CONFIGS = {
+    # layers 0-2 dense NVFP4 MLPs (H2048, I10240), layers 3-44 NVFP4
+    # MoE layers as in c1, layer 45 BF16 routed experts; BF16 GQA attention
+    # 32 q heads / 4 KV heads / dim 128; vocab 151552; 2048-token context
+    "c4": dict(vocab=151552, hidden=2048, layers=46, dense_layers=3, bf16_expert_layers=1, dense_inter=10240,
+               experts=64, top_k=4, inter=1536, shared_inter=1536, scaling=2.5, q_heads=32, kv_heads=4,
+               context=2048),
+    # a small stack with the same structure, for parity against the CPU oracle
+    "tiny": dict(vocab=1000, hidden=256, layers=4, dense_layers=1, bf16_expert_layers=1, dense_inter=512,
+                 experts=8, top_k=2, inter=128, shared_inter=128, scaling=1.0, q_heads=8, kv_heads=1,
+                 context=1024),
+}
+STACK_BATCHES = (1, 16, 64, 256)  # configs[4]'s greedy-decode batch sizes
+
+
+@dataclasses.dataclass
+class StackLayer:
+    wq: np.ndarray          # BF16 [q_heads 128, H]
+    wk: np.ndarray          # BF16 [kv_heads 128, H]
+    wv: np.ndarray          # BF16 [kv_heads 128, H]
+    wo: np.ndarray          # BF16 [H, q_heads 128]
+    attn_norm: np.ndarray   # F32 [H]
+    ffn_norm: np.ndarray    # F32 [H]
+    q_norm: np.ndarray      # F32 [128]
+    k_norm: np.ndarray      # F32 [128]
+    ffn: object             # DenseLayer or Layer (NVFP4 or BF16 experts)
+
+
+@dataclasses.dataclass
+class StackModel:
+    cfg: dict
+    embed: np.ndarray       # BF16 [vocab, H], ~N(0, 1)
+    lm_head: np.ndarray     # BF16 [vocab, H], ~N(0, 0.02)
+    final_norm: np.ndarray  # F32 [H]
+    layers: list
+
+
+def make_stack(cfg: dict, seed: int, share: bool = False) -> StackModel:
+    """Random-init weights of the stack (BF16 ~N(0, 0.02) projections, NVFP4
+    experts as make_layer, norms 1 + N(0, 0.05)).  share=True generates one
+    attention block, one dense MLP and one MoE layer and lists them for every
+    layer of their kind (each layer still gets its own device copy when
+    bound): the full configuration's 16 GB of weights without generating
+    them 46 times on the host."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    H, V = cfg["hidden"], cfg["vocab"]
+    nq, nkv, D = cfg["q_heads"], cfg["kv_heads"], 128
+
+    def attn(r):
+        return dict(wq=f32_to_bf16_bits(_normal(r, (nq * D, H), 0.02)),
+                    wk=f32_to_bf16_bits(_normal(r, (nkv * D, H), 0.02)),
+                    wv=f32_to_bf16_bits(_normal(r, (nkv * D, H), 0.02)),
+                    wo=f32_to_bf16_bits(_normal(r, (H, nq * D), 0.02)),
+                    attn_norm=(1 + _normal(r, (H,), 0.05)).astype(np.float32),
+                    ffn_norm=(1 + _normal(r, (H,), 0.05)).astype(np.float32),
+                    q_norm=(1 + _normal(r, (D,), 0.05)).astype(np.float32),
+                    k_norm=(1 + _normal(r, (D,), 0.05)).astype(np.float32))
+
+    moe_cfg = dict(hidden=H, experts=cfg["experts"], top_k=cfg["top_k"], inter=cfg["inter"],
+                   shared_inter=cfg["shared_inter"], scaling=cfg["scaling"])
+    L, nd, nb = cfg["layers"], cfg["dense_layers"], cfg["bf16_expert_layers"]
+    shared_attn = attn(rng) if share else None
+    shared_dense = make_dense_layer(H, cfg["dense_inter"], seed + 7) if share and nd else None
+    shared_moe = make_layer(moe_cfg, seed + 11) if share and L - nd - nb > 0 else None
+    layers = []
+    for l in range(L):
+        a = shared_attn if share else attn(rng)
+        if l < nd:
+            f = shared_dense if share else make_dense_layer(H, cfg["dense_inter"], seed + 100 + l)
+        elif l >= L - nb:
+            f = make_layer(moe_cfg, seed + 100 + l, bf16_experts=True)
+        else:
+            f = shared_moe if share else make_layer(moe_cfg, seed + 100 + l)
+        layers.append(StackLayer(ffn=f, **a))
+    embed = f32_to_bf16_bits(rng.standard_normal((V, H), dtype=np.float32))
+    lm_head = f32_to_bf16_bits(_normal(rng, (V, H), 0.02))
+    final_norm = (1 + _normal(rng, (H,), 0.05)).astype(np.float32)
+    return StackModel(cfg=cfg, embed=embed, lm_head=lm_head, final_norm=final_norm, layers=layers)
