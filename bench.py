@@ -489,6 +489,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     if world == 1 and not args.no_prefill:
         line["prefill"] = run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src)
         line["dense"] = run_dense(args, m, torch, hbm_peak, fp4_peak, peak_src)
+        if not args.no_stack:
+            line["stack_c4"] = run_stack(args, m, torch, hbm_peak)
+    if not args.no_prefill:
+        tph = run_tp_head(args, m, torch, rank, world, local, dist, hbm_peak)
+        if rank == 0:
+            line["tp_lm_head"] = tph
     if not args.no_prefill:
         ep3 = run_ep_c3(args, m, torch, rank, world, local, dist)
         ep3c = run_ep_c3(args, m, torch, rank, world, local, dist, lam=wl.C3_LAMBDA_CALIBRATED)
@@ -678,6 +684,114 @@ def run_dense(args, m, torch, hbm_peak, fp4_peak, peak_src) -> dict:
     return out
 
 
+def run_tp_head(args, m, torch, rank: int, world: int, local: int, dist, hbm_peak: float) -> dict:
+    """The lm_head of configs[4] ([151552, 2048] BF16) through the tensor-
+    parallel linear (exact gemv_bf16 rows, gathered on every rank) and the
+    greedy pick, at the stack's batch sizes.  HBM roofline per rank: its
+    row block's weight bytes once per call."""
+    rows, cols = wl.STACK_CONFIGS["c4"]["vocab"], wl.STACK_CONFIGS["c4"]["hidden"]
+    gid = None
+    if world > 1:
+        g = [m.ep_group_id() if rank == 0 else None]
+        dist.broadcast_object_list(g, src=0)
+        gid = g[0]
+    tp = m.TpGroup(max_tokens=max(wl.STACK_BATCHES), max_rows=rows, rank=rank, world=world, group_id=gid,
+                   device=local)
+    r0, r1 = tp.split(rows)
+    rng = np.random.default_rng(40)
+    w = torch.from_numpy(wl.f32_to_bf16_bits(rng.standard_normal((r1 - r0, cols), dtype=np.float32)
+                                             * np.float32(0.02)).view(np.int16)).cuda()
+    ts = torch.cuda.Stream()
+    out = {"workload": "configs[4] lm_head [151552, 2048] BF16: exact row-split GEMV + NVLink gather + greedy pick",
+           "transport": tp.transport(), "per_batch": {}}
+    for T in wl.STACK_BATCHES:
+        x = torch.from_numpy(rng.standard_normal((T, cols), dtype=np.float32)).cuda()
+        idx = torch.empty(T, dtype=torch.int32, device="cuda")
+        for _ in range(args.warmup):
+            tp.linear_bf16(w, rows, cols, x, T, None, stream=ts.cuda_stream)
+            tp.argmax(T, rows, idx, stream=ts.cuda_stream)
+        tp.sync(ts.cuda_stream)
+        steps = max(3, min(args.steps, 20 if T <= 16 else 5))
+        if dist:
+            dist.barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(ts)
+        for _ in range(steps):
+            tp.linear_bf16(w, rows, cols, x, T, None, stream=ts.cuda_stream)
+            tp.argmax(T, rows, idx, stream=ts.cuda_stream)
+        ev1.record(ts)
+        tp.sync(ts.cuda_stream)
+        ms = ev0.elapsed_time(ev1) / steps
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        gbs = (r1 - r0) * cols * 2 / (ms * 1e-3) / 1e9
+        out["per_batch"][str(T)] = {"us": 1e3 * ms, "tokens_per_s": T / (ms * 1e-3), "rank_weight_gbs": gbs,
+                                    "hbm_frac": gbs / hbm_peak}
+    if dist:
+        dist.barrier()  # every rank's last call is done before any handle of the group goes
+    tp.close()
+    return out
+
+
+def run_stack(args, m, torch, hbm_peak: float) -> dict:
+    """the full synthetic decoder stack (46 layers: 3 dense NVFP4
+    MLPs, 42 NVFP4 MoE layers of c1's shapes, 1 BF16-expert MoE layer; BF16
+    GQA 32/4/128 attention; vocab 151552), greedy decode with a 2048-token
+    context (caches filled on the device with a pseudo-random history) at
+    batch 1/16/64/256 on one GPU.  A step is one token for every sequence;
+    timed as CUDA-graph replays of the whole step."""
+    cfg = wl.STACK_CONFIGS["c4"]
+    t0 = time.perf_counter()
+    model = wl.make_stack(cfg, seed=4, share=True)
+    st = m.DecoderStack(vocab=cfg["vocab"], hidden=cfg["hidden"], layers=cfg["layers"],
+                        dense_layers=cfg["dense_layers"], bf16_expert_layers=cfg["bf16_expert_layers"],
+                        dense_inter=cfg["dense_inter"], experts=cfg["experts"], top_k=cfg["top_k"], inter=cfg["inter"],
+                        shared_inter=cfg["shared_inter"], routed_scaling=cfg["scaling"], q_heads=cfg["q_heads"],
+                        kv_heads=cfg["kv_heads"], max_batch=max(wl.STACK_BATCHES), max_context=cfg["context"])
+    st.bind_model(model)
+    st.fill_kv(1)
+    setup_s = time.perf_counter() - t0
+    del model
+    ts = torch.cuda.Stream()
+    out = {"workload": "configs[4] synthetic decoder stack: 46 layers (3 dense NVFP4 MLP H2048 I10240, 42 NVFP4 MoE "
+                       "c1 shapes, 1 BF16-expert MoE), BF16 GQA 32q/4kv/128 + q/k norm + RoPE, vocab 151552, "
+                       "2048-token context, greedy decode, 1 GPU",
+           "weights": "random init of the configuration's shapes; one attention block, dense MLP and NVFP4 MoE layer "
+                      "generated on the host and bound into every layer of its kind (separate device copies)",
+           "setup_s": setup_s, "per_batch": {}}
+    L = cfg["context"]
+    for B in wl.STACK_BATCHES:
+        rng = np.random.default_rng(B)
+        tok = torch.from_numpy(rng.integers(0, cfg["vocab"], B).astype(np.int32)).cuda()
+        pos = torch.full((B,), L - 1, dtype=torch.int32, device="cuda")
+        nxt = torch.empty(B, dtype=torch.int32, device="cuda")
+        for _ in range(2):
+            st.decode(tok, pos, B, nxt, stream=ts.cuda_stream)
+        st.sync(ts.cuda_stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=ts):
+            st.decode(tok, pos, B, nxt, stream=ts.cuda_stream)
+        for _ in range(max(1, args.warmup - 2)):
+            graph.replay()
+        torch.cuda.synchronize()
+        steps = max(3, min(args.steps, 10))
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(ts)
+        with torch.cuda.stream(ts):
+            for _ in range(steps):
+                graph.replay()
+        ev1.record(ts)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / steps
+        st.sync(ts.cuda_stream)
+        out["per_batch"][str(B)] = {"ms_per_step": ms, "tokens_per_s": B / (ms * 1e-3)}
+        del graph
+    st.close()
+    return out
+
+
 def run_decode_only(args, m, torch) -> dict:
     """The decode batch alone: warm-up, `steps` timed forwards, stage times."""
     lay, x_bits = wl.config_layer("c1")
@@ -714,7 +828,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true", help="skip the secondary prefill measurement")
-    ap.add_argument("--only", choices=["decode", "prefill", "dense"],
+    ap.add_argument("--no-stack", action="store_true", help="skip the configs[4] decoder-stack measurement")
+    ap.add_argument("--only", choices=["decode", "prefill", "dense", "stack"],
                     help="time one workload alone (no e2e, CPU baseline or clock sampling); for profilers")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -729,6 +844,8 @@ def main():
         elif args.only == "dense":
             hbm_peak, bf16_peak, peak_src = peaks()
             out = run_dense(args, m, torch, hbm_peak, 4 * bf16_peak, peak_src)
+        elif args.only == "stack":
+            out = run_stack(args, m, torch, peaks()[0])
         else:
             _, bf16_peak, peak_src = peaks()
             out = run_prefill(args, m, torch, 4 * bf16_peak, bf16_peak, peak_src)
