@@ -117,3 +117,85 @@ def test_ep_matches_one_gpu(tmp_path, case, transport, ranks):
     assert np.array_equal(np.concatenate([g["w"] for g in got]).view(np.uint32), w.cpu().numpy().view(np.uint32))
     assert np.array_equal(y_ep.view(np.uint32), y.cpu().numpy().view(np.uint32))
     layer.close()
+
+
+def _skip_rank(rank: int, world: int, port: int, out_dir: str) -> None:
+    """Step 1: both ranks forward.  Step 2: rank 1 skips its forward (decided
+    on the host); rank 0's bounded flag waits run out and its sync reports
+    the timeout.  Then both ranks drop the group and make a new one, whose
+    forward must again equal one GPU's."""
+    sys.path.insert(0, str(REPO / "tests"))
+    os.environ["NF_EP_TRANSPORT"] = "nvlink"
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    m = nfm()
+    lay, parts = _tokens("c1", world)
+    cap = max(p.shape[0] for p in parts)
+
+    def group():
+        gid = [m.ep_group_id() if rank == 0 else None]
+        dist.broadcast_object_list(gid, src=0)
+        layer = m.MoeLayer(lay.hidden, lay.experts, lay.top_k, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                           swiglu_limit=lay.swiglu_limit, max_tokens=cap, device=rank, ep=(rank, world, gid[0]))
+        layer.bind_layer(lay)
+        return layer
+
+    xb = parts[rank]
+    T = xb.shape[0]
+    x = torch.from_numpy(np.ascontiguousarray(xb).view(np.int16)).cuda()
+    y = torch.zeros((T, lay.hidden), dtype=torch.float32, device="cuda")
+    layer = group()
+    assert layer.ep_transport() == "nvlink"
+    layer.forward(x, y, T)
+    layer.sync()
+    dist.barrier()
+    status = "none"
+    if rank == 0:
+        layer.forward(x, y, T)  # rank 1 never sends: the waits give up after their budget
+        try:
+            layer.sync()
+            status = "ok"
+        except m.NfError as e:
+            status = m.NF_ERR.get(e.status, str(e.status))
+    dist.barrier()  # rank 0's forward (with its given-up waits) is complete before the group goes
+    layer.close()
+    dist.barrier()
+    layer = group()
+    y.zero_()
+    layer.forward(x, y, T)
+    layer.sync()
+    np.savez(os.path.join(out_dir, f"s{rank}.npz"), y=y.cpu().numpy(), status=np.array(status))
+    dist.barrier()
+    layer.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ep_rank_that_skips_a_step_times_out_and_the_group_recovers(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"  # no NVLink multicast objects for a test where a rank drops out
+    world = 2
+    mp.start_processes(_skip_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn",
+                       join=True)
+    got = [np.load(tmp_path / f"s{r}.npz") for r in range(world)]
+    assert str(got[0]["status"]) == "TIMEOUT", str(got[0]["status"])
+    m = nfm()
+    lay, parts = _tokens("c1", world)
+    xb = np.concatenate(parts)
+    T = xb.shape[0]
+    layer = m.MoeLayer(lay.hidden, lay.experts, lay.top_k, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                       swiglu_limit=lay.swiglu_limit, max_tokens=T)
+    layer.bind_layer(lay)
+    x = torch.from_numpy(np.ascontiguousarray(xb).view(np.int16)).cuda()
+    y = torch.zeros((T, lay.hidden), dtype=torch.float32, device="cuda")
+    layer.forward(x, y, T)
+    layer.sync()
+    y_ep = np.concatenate([g["y"] for g in got])
+    assert np.array_equal(y_ep.view(np.uint32), y.cpu().numpy().view(np.uint32))
+    layer.close()
