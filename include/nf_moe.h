@@ -182,7 +182,10 @@ enum {
     NF_DBG_H_SF = 7,        /* U8    E4M3 block scales of the down input (atom layout)   */
     NF_DBG_DOWN = 8,        /* BF16 [rows, H] (NVFP4) or F32 (BF16 experts): down output */
     NF_DBG_SHARED = 9,      /* F32   [T, H]       shared expert output                   */
-    NF_DBG_ROWS = 10        /* INT32 [1]          permuted rows in use (incl. padding)   */
+    NF_DBG_ROWS = 10,       /* INT32 [1]          permuted rows in use (incl. padding)   */
+    NF_DBG_LOGITS = 11,     /* F32   [T, E]       router logits: exact (full router), or the tensor-core
+                                                  approximations the screened router bounds */
+    NF_DBG_SCREEN_COUNT = 12 /* INT32 [T]         screened router: exact chains per token, -1 = all E */
 };
 NF_API int nf_moe_debug_tensor(nf_moe* handle, int which, void** dev_ptr, int64_t* bytes);
 /* Copies the first `bytes` bytes of a debug tensor to host memory

@@ -171,7 +171,7 @@ int ep_p2p_setup(nf_moe* h, std::string* err) {
 static int ep_forward_p2p(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx,
                           float* w, StageRec& rec, cudaStream_t s) {
     const nf_moe_desc& d = h->d;
-    const int H = d.hidden, E = d.experts, K = d.top_k, Is = d.shared_inter, R = h->ep_world, me = h->ep_rank;
+    const int H = d.hidden, K = d.top_k, Is = d.shared_inter, R = h->ep_world, me = h->ep_rank;
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
     const int out_bytes = H * (fp4 ? 2 : 4);
     const EpLayout& L = h->ep_lay;
@@ -180,9 +180,7 @@ static int ep_forward_p2p(nf_moe* h, const uint16_t* x, const float* residual, i
     if (T > 0 && Is > 0 && (st = launch_shared_expert(h, x, T, rec, s)) != NF_OK) return st;
     rec.begin(NF_STAGE_ROUTER, s);
     if (T > 0) {
-        e = launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, T, H, E, K, d.routed_scaling,
-                          d.normalize, d.n_group, d.topk_group, h->router_w_safe, h->logits, h->scores, h->choices, idx,
-                          w, h->dev_err, s);
+        e = route_tokens(h, x, T, idx, w, s);
         if (e == cudaSuccess)
             e = launch_ep_pack(idx, T, K, h->ep_local, R, h->ep_slot, h->ep_send_tok, h->ep_send_e, h->ep_cnt, s);
     } else {
@@ -218,7 +216,7 @@ static int ep_forward_p2p(nf_moe* h, const uint16_t* x, const float* residual, i
 int ep_forward(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx_user,
                float* w_user, cudaStream_t s) {
     const nf_moe_desc& d = h->d;
-    const int H = d.hidden, E = d.experts, K = d.top_k, Is = d.shared_inter, R = h->ep_world;
+    const int H = d.hidden, K = d.top_k, Is = d.shared_inter, R = h->ep_world;
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
     const int out_bytes = H * (fp4 ? 2 : 4);  // a down row: BF16 (NVFP4 experts) or F32 (BF16 experts)
     int32_t* idx = idx_user ? idx_user : h->topk_idx;
@@ -237,9 +235,7 @@ int ep_forward(nf_moe* h, const uint16_t* x, const float* residual, int T, float
     // route, lay out, count
     rec.begin(NF_STAGE_ROUTER, s);
     if (T > 0) {
-        e = launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, T, H, E, K, d.routed_scaling,
-                          d.normalize, d.n_group, d.topk_group, h->router_w_safe, h->logits, h->scores, h->choices, idx,
-                          w, h->dev_err, s);
+        e = route_tokens(h, x, T, idx, w, s);
         if (e == cudaSuccess)
             e = launch_ep_pack(idx, T, K, h->ep_local, R, h->ep_slot, h->ep_send_tok, h->ep_send_e, h->ep_cnt, s);
         if (e == cudaSuccess) e = launch_gather_rows(x, h->ep_send_tok, T * K, H * 2, h->ep_send, s);

@@ -55,6 +55,19 @@ struct nf_moe {
     std::vector<uint8_t> bound;     // [E * 3] expert projection bound flags
     bool router_bound = false, bias_bound = false, sg_bound = false, su_bound = false, sd_bound = false;
     int router_w_safe = 0;  // every nonzero router weight has |w| in [2^-67, 2^63)
+    // screened router for large batches (nf_kernels.cu route_screen_kernel):
+    // the router rows padded to 256 in box order for the tensor-core GEMM, the
+    // rows' 2-norms rounded up, the approximate-logit partials and the
+    // candidates of each token
+    bool screen = false;
+    uint8_t* router_box = nullptr;
+    float* router_wnorm = nullptr;
+    float* screen_part = nullptr;     // [kScreenSlices][Tm][256]
+    int32_t* screen_cand = nullptr;   // [Tm][32]
+    int32_t* screen_cnt = nullptr;    // [Tm]: candidates, -1 = every chain
+    int* screen_counter = nullptr;    // GEMM tile counter
+    CUtensorMap tm_router{};
+    int last_screened = 0;            // the last forward's router was screened
 
     // workspace
     float* logits = nullptr;         // router logits, sigmoid scores and choices [Tm, E]
@@ -230,6 +243,9 @@ int validate_desc(const nf_moe_desc& d, std::string* err);
 std::string& create_error();
 int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::string* err);
 int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cudaStream_t s);
+// The router of a forward (no logits out): the screened router for large
+// batches when the handle has one, else the full exact router.
+cudaError_t route_tokens(nf_moe* h, const uint16_t* x, int T, int32_t* idx, float* w, cudaStream_t s);
 // down_split > 1 (dense handles): the down GEMM runs as a dense split-K GEMM
 // into h->dense_part (down_split K slices) instead of writing h->down.
 int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int T, int K, StageRec& rec,

@@ -253,6 +253,18 @@ cudaError_t launch_gqa_decode(const float* q, const uint16_t* kc, const uint16_t
 
 cudaError_t launch_fill_bf16_hash(uint16_t* p, int64_t n, uint64_t seed, cudaStream_t st);
 
+// Screened router (large batches): candidates per token, split-K slices of the
+// approximate-logit GEMM, and the batch size from which forwards use it.
+constexpr int kScreenMaxCandHost = 32;
+constexpr int kScreenSlices = 4;
+constexpr int kScreenMinTokens = 1024;
+cudaError_t launch_route_screen(const float* part, int S, int64_t stride, int ld, const uint16_t* x, int T, int H,
+                                int E, int K, const float* bias, const float* wnorm, float c, int32_t* cand,
+                                int32_t* cnt, float* approx, cudaStream_t st);
+cudaError_t launch_route_exact(const uint16_t* x, const uint16_t* wz16, const float* bias, int T, int H, int E, int K,
+                               float scaling, int normalize, int w_safe, const int32_t* cand, const int32_t* cnt,
+                               int32_t* idx, float* wts, cudaStream_t st);
+
 constexpr int kChunkTokHost = 128;  // tokens per permutation chunk (nf_kernels.cu kChunkTok)
 // Per-device one-time state (kernel attributes, lookup tables) is kept in
 // arrays of this many devices.

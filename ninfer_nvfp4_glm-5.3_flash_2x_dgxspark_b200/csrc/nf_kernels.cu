@@ -1785,4 +1785,288 @@ cudaError_t launch_sigmoid_ref(const float* x, int64_t n, float* y, cudaStream_t
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Screened router for large batches: the reference's exact logit chains
+// (gemv_bf16, src/text_forward.cpp:497-508) only where they can change the
+// selection (router_select :1447-1471).
+//
+// 1. Approximate logits l~[t, e] come from a tensor-core GEMM of the BF16
+//    tokens and router rows (fp32 accumulation in the MMA's order).
+// 2. route_screen_kernel bounds |l~ - l| for the exact chain l:
+//      |l - s| <= gamma_H sum|w x|  (the reference's sequential sum, exact
+//                                     products: one rounding per step)
+//      |l~ - s| <= H 2^-21 sum|w x| (the tensor core's accumulation, taken
+//                                     eight times fp32's unit roundoff per step)
+//    with s the real dot product and sum|w x| <= ||x||_2 ||w_e||_2 (the
+//    norms rounded up).  choice(l) = sigmoid_ref(l) + bias is non-decreasing
+//    in l (each step is a correctly rounded monotone function), so
+//    [choice(l~ - B), choice(l~ + B)] (endpoints rounded outward) encloses the
+//    exact choice.  At least k experts have an exact choice >= the k-th
+//    largest lower end, so an expert whose upper end lies below it can never
+//    be picked: the candidates are the experts whose upper end reaches it.
+//    A token with a non-finite approximate logit, a token value outside
+//    [2^-67, 2^20) in magnitude (products inexact, or sums near overflow), or
+//    more than 32 candidates, is marked for every chain.
+// 3. route_exact_kernel runs the exact chains of the candidates (all E for a
+//    marked token), the exact sigmoid and bias, and the reference's selection
+//    with every other expert's choice set to -inf: such an expert is below k
+//    exact choices, so it is never picked, and -inf is not a NaN, so the
+//    first-unused rule for NaN never reaches it.  Routes and weights are
+//    therefore bit-identical to the full exact router.
+// ---------------------------------------------------------------------------
+constexpr int kScreenMaxCand = kScreenMaxCandHost;
+
+__device__ __forceinline__ bool bf16_screen_unsafe(uint32_t u) {
+    // a nonzero BF16 half outside [2^-67, 2^20) in magnitude, inf or NaN
+    const uint32_t e0 = (u >> 7) & 0xffu, e1 = (u >> 23) & 0xffu;
+    const bool nz0 = (u & 0x7fffu) != 0u, nz1 = (u & 0x7fff0000u) != 0u;
+    return (nz0 && (e0 < 60u || e0 > 146u)) || (nz1 && (e1 < 60u || e1 > 146u));
+}
+
+__global__ void __launch_bounds__(256) route_screen_kernel(const float* __restrict__ part, int S, int64_t stride,
+                                                           int ld, const uint16_t* __restrict__ x, int T, int H,
+                                                           int E, int K, const float* __restrict__ bias,
+                                                           const float* __restrict__ wnorm, float c,
+                                                           int32_t* __restrict__ cand, int32_t* __restrict__ cnt,
+                                                           float* __restrict__ approx) {
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= T) return;
+    const int lane = threadIdx.x & 31;
+    // ||x_t||_2 in double (each square exact), and the range check
+    const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * H);
+    double ss = 0.0;
+    int bad = 0;
+    for (int i = lane; i < H / 8; i += 32) {
+        const uint4 v = __ldg(xr + i);
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            bad |= bf16_screen_unsafe(w4[j]) ? 1 : 0;
+            const double a = bf16_lo(w4[j]), b = bf16_hi(w4[j]);
+            ss += a * a + b * b;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    const float nx = __double2float_ru(sqrt(ss) * (1.0 + 1e-12));
+    const int jn = (E + 31) / 32;  // E <= 128
+    float lo[4], hi[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        lo[j] = -INFINITY;
+        hi[j] = -INFINITY;
+        const int e = lane + 32 * j;
+        if (j >= jn || e >= E) continue;
+        float l = 0.f;
+        for (int s = 0; s < S; ++s) l += part[s * stride + static_cast<int64_t>(t) * ld + e];
+        if (approx) approx[static_cast<int64_t>(t) * E + e] = l;  // (kept for inspection)
+        const float B = __fmul_ru(__fmul_ru(c, nx), wnorm[e]);
+        const float la = __fsub_rd(l, B), ha = __fadd_ru(l, B);
+        if (!isfinite(l) || !isfinite(la) || !isfinite(ha)) {
+            bad = 1;
+            continue;
+        }
+        lo[j] = __fadd_rn(sigmoid_ref(la), bias[e]);
+        hi[j] = __fadd_rn(sigmoid_ref(ha), bias[e]);
+    }
+    bad = __any_sync(0xffffffffu, bad) ? 1 : 0;
+    if (bad) {
+        if (lane == 0) cnt[t] = -1;
+        return;
+    }
+    // the k-th largest lower end: k rounds of a max over keys (order bits,
+    // expert index) with the winner removed
+    uint32_t removed = 0u;
+    float kth = -INFINITY;
+    for (int p = 0; p < K; ++p) {
+        uint64_t key = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = lane + 32 * j;
+            if (j >= jn || e >= E || ((removed >> j) & 1u)) continue;
+            const uint64_t k = (static_cast<uint64_t>(float_order_bits(lo[j])) << 32) | static_cast<uint32_t>(e);
+            key = k > key ? k : key;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint64_t ok = __shfl_xor_sync(0xffffffffu, key, o);
+            key = ok > key ? ok : key;
+        }
+        const int we = static_cast<int>(key & 0xffffffffu);
+        if ((we & 31) == lane) removed |= 1u << (we >> 5);
+        float v = lo[0];
+#pragma unroll
+        for (int j = 1; j < 4; ++j)
+            if ((we >> 5) == j) v = lo[j];
+        kth = __shfl_sync(0xffffffffu, v, we & 31);
+    }
+    int n = 0;
+    int32_t* out = cand + static_cast<int64_t>(t) * kScreenMaxCand;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int e = lane + 32 * j;
+        const bool is_cand = j < jn && e < E && hi[j] >= kth;
+        const uint32_t b = __ballot_sync(0xffffffffu, is_cand);
+        if (is_cand) {
+            const int slot = n + __popc(b & ((1u << lane) - 1u));
+            if (slot < kScreenMaxCand) out[slot] = e;
+        }
+        n += __popc(b);
+    }
+    if (lane == 0) cnt[t] = n <= kScreenMaxCand ? n : -1;
+}
+
+// The exact chains of the screened candidates, 32 tokens per CTA (one warp
+// each); the router rows stream through shared memory in 128-column chunks
+// of the fused router's BF16 chunk-major copy (rows padded to kRouterPitch16,
+// so the rows the lanes of a warp read fall in different banks), double
+// buffered with plain 16-byte loads; a warp's token chunk is widened into
+// its own 128-float slot.  Lane i runs the chains of candidates i and i + 32
+// (all E experts, lane + 32 j, for a marked token), sequentially over the
+// columns, fused multiply-add when the weights passed the bind-time range
+// check (products exact) and the token is in range, else the separately
+// rounded multiply and add.
+constexpr int kExactWarps = 32;
+constexpr int kExactTpb = kExactWarps * 32;
+
+__global__ void __launch_bounds__(kExactTpb, 1) route_exact_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ wz16, const float* __restrict__ bias, int T, int H,
+    int E, int K, float scaling, int normalize, int w_safe, const int32_t* __restrict__ cand,
+    const int32_t* __restrict__ cnt, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
+    extern __shared__ __align__(16) uint8_t rx_smem[];
+    const int wchunk = E * kRouterPitch16;  // BF16 elements of one chunk of every row
+    uint16_t* sw = reinterpret_cast<uint16_t*>(rx_smem);                       // [2][wchunk]
+    float* sx = reinterpret_cast<float*>(rx_smem + 2 * wchunk * 2);            // [kExactWarps][kRouterKc]
+    float* s_sc = sx + kExactWarps * kRouterKc;                                // [kExactWarps][E]
+    float* s_ch = s_sc + kExactWarps * E;                                      // [kExactWarps][E]
+    __shared__ uint32_t s_excl[kExactWarps][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * kExactWarps + warp;
+    const bool live = t < T;
+    const int n = live ? cnt[t] : 0;
+    const bool all = n < 0;
+    // this lane's experts: candidates lane and lane + 32, or every lane + 32 j
+    int ex[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        ex[j] = -1;
+        if (!live) continue;
+        if (all) {
+            if (lane + 32 * j < E) ex[j] = lane + 32 * j;
+        } else if (j < 2 && lane + 32 * j < n) {
+            ex[j] = cand[static_cast<int64_t>(t) * kScreenMaxCand + lane + 32 * j];
+        }
+    }
+    // products exact (fma equals the rounded multiply-add) unless a token value
+    // or a weight is out of range; a marked token may be out of range
+    int xbad = 0;
+    if (live && all)
+        for (int i = lane; i < H / 2; i += 32)
+            xbad |= bf16x2_unsafe(reinterpret_cast<const uint32_t*>(x + static_cast<int64_t>(t) * H)[i]) ? 1 : 0;
+    const bool fma_ok = w_safe && !__any_sync(0xffffffffu, xbad);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int nchunks = H / kRouterKc;
+    auto load_w = [&](int c, int buf) {
+        const uint4* src = reinterpret_cast<const uint4*>(wz16 + static_cast<int64_t>(c) * wchunk);
+        uint4* dst = reinterpret_cast<uint4*>(sw + buf * wchunk);
+        for (int i = threadIdx.x; i < wchunk / 8; i += kExactTpb) dst[i] = __ldg(src + i);
+    };
+    load_w(0, 0);
+    for (int c = 0; c < nchunks; ++c) {
+        const int buf = c & 1;
+        // this warp's token chunk, widened
+        if (live) {
+            const uint2 v = __ldg(reinterpret_cast<const uint2*>(x + static_cast<int64_t>(t) * H + c * kRouterKc) + lane);
+            float* d = sx + warp * kRouterKc + 4 * lane;
+            d[0] = bf16_lo(v.x);
+            d[1] = bf16_hi(v.x);
+            d[2] = bf16_lo(v.y);
+            d[3] = bf16_hi(v.y);
+        }
+        __syncthreads();  // chunk c of the weights and the token chunks are in place
+        if (c + 1 < nchunks) load_w(c + 1, buf ^ 1);
+        const float* xs = sx + warp * kRouterKc;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (ex[j] < 0) continue;
+            const uint16_t* wr = sw + buf * wchunk + ex[j] * kRouterPitch16;
+            float a = acc[j];
+            for (int k = 0; k < kRouterKc; k += 8) {
+                const uint4 wv = *reinterpret_cast<const uint4*>(wr + k);
+                const float4 xa = *reinterpret_cast<const float4*>(xs + k);
+                const float4 xb = *reinterpret_cast<const float4*>(xs + k + 4);
+                if (fma_ok) {
+                    a = fmaf(bf16_lo(wv.x), xa.x, a);
+                    a = fmaf(bf16_hi(wv.x), xa.y, a);
+                    a = fmaf(bf16_lo(wv.y), xa.z, a);
+                    a = fmaf(bf16_hi(wv.y), xa.w, a);
+                    a = fmaf(bf16_lo(wv.z), xb.x, a);
+                    a = fmaf(bf16_hi(wv.z), xb.y, a);
+                    a = fmaf(bf16_lo(wv.w), xb.z, a);
+                    a = fmaf(bf16_hi(wv.w), xb.w, a);
+                } else {
+                    a = __fadd_rn(a, __fmul_rn(bf16_lo(wv.x), xa.x));
+                    a = __fadd_rn(a, __fmul_rn(bf16_hi(wv.x), xa.y));
+                    a = __fadd_rn(a, __fmul_rn(bf16_lo(wv.y), xa.z));
+                    a = __fadd_rn(a, __fmul_rn(bf16_hi(wv.y), xa.w));
+                    a = __fadd_rn(a, __fmul_rn(bf16_lo(wv.z), xb.x));
+                    a = __fadd_rn(a, __fmul_rn(bf16_hi(wv.z), xb.y));
+                    a = __fadd_rn(a, __fmul_rn(bf16_lo(wv.w), xb.z));
+                    a = __fadd_rn(a, __fmul_rn(bf16_hi(wv.w), xb.w));
+                }
+            }
+            acc[j] = a;
+        }
+        __syncthreads();  // every warp is done with chunk c before its buffer is refilled
+    }
+    if (!live) return;
+    float* sc = s_sc + warp * E;
+    float* ch = s_ch + warp * E;
+    for (int e = lane; e < E; e += 32) {
+        sc[e] = 0.f;
+        ch[e] = -INFINITY;  // not a candidate: below k exact choices
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if (ex[j] < 0) continue;
+        const float s = sigmoid_ref(acc[j]);
+        sc[ex[j]] = s;
+        ch[ex[j]] = __fadd_rn(s, bias[ex[j]]);
+    }
+    __syncwarp();
+    warp_select(sc, ch, E, K, scaling, normalize, 1, 1, s_excl[warp], idx_out + static_cast<int64_t>(t) * K,
+                w_out + static_cast<int64_t>(t) * K);
+}
+
+size_t route_exact_smem(int E) {
+    return static_cast<size_t>(2) * E * kRouterPitch16 * 2 + static_cast<size_t>(kExactWarps) * kRouterKc * 4 +
+           static_cast<size_t>(2) * kExactWarps * E * 4;
+}
+
+cudaError_t launch_route_screen(const float* part, int S, int64_t stride, int ld, const uint16_t* x, int T, int H,
+                                int E, int K, const float* bias, const float* wnorm, float c, int32_t* cand,
+                                int32_t* cnt, float* approx, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    route_screen_kernel<<<(T + 7) / 8, 256, 0, st>>>(part, S, stride, ld, x, T, H, E, K, bias, wnorm, c, cand, cnt,
+                                                     approx);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_route_exact(const uint16_t* x, const uint16_t* wz16, const float* bias, int T, int H, int E, int K,
+                               float scaling, int normalize, int w_safe, const int32_t* cand, const int32_t* cnt,
+                               int32_t* idx, float* wts, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    const size_t smem = route_exact_smem(E);
+    static bool attr[kMaxDevices] = {};
+    cudaError_t e = smem_attr_once(route_exact_kernel, static_cast<int>(route_exact_smem(kRouterMaxE)), attr);
+    if (e != cudaSuccess) return e;
+    route_exact_kernel<<<(T + kExactWarps - 1) / kExactWarps, kExactTpb, smem, st>>>(
+        x, wz16, bias, T, H, E, K, scaling, normalize, w_safe, cand, cnt, idx, wts);
+    return cudaGetLastError();
+}
+
 }  // namespace nf

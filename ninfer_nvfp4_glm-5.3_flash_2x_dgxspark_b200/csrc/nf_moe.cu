@@ -331,6 +331,13 @@ int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::s
             ok = ok && h->alloc(&h->router_wz, router_chunked_elems(E, H)) &&
                  h->alloc(&h->router_wz16, router_chunked_elems16(E, H));
         ok = ok && h->alloc(&h->logits, Tm * E) && h->alloc(&h->scores, Tm * E) && h->alloc(&h->choices, Tm * E);
+        // the screened router, for handles that take prefill-sized batches
+        h->screen = E <= kRouterMaxE && H % kRouterKc == 0 && Tm >= kScreenMinTokens;
+        if (h->screen)
+            ok = ok && h->alloc(&h->router_box, blocked_bytes(256, 2 * H)) && h->alloc(&h->router_wnorm, E) &&
+                 h->alloc(&h->screen_part, static_cast<int64_t>(kScreenSlices) * Tm * 256) &&
+                 h->alloc(&h->screen_cand, Tm * kScreenMaxCandHost) && h->alloc(&h->screen_cnt, Tm) &&
+                 h->alloc(&h->screen_counter, 1);
     }
     if (routed) {
         if (fp4) {
@@ -535,6 +542,28 @@ int nf_moe_bind_bf16(nf_moe* h, int which, int expert, const uint16_t* data, int
                     e = cudaMemcpy(h->router_wz16, wz16.data(), wz16.size() * 2, cudaMemcpyHostToDevice);
                 }
             }
+            if (e == cudaSuccess && h->screen) {
+                // the screen's GEMM operand: rows padded with zeros to one 256-row block
+                std::vector<uint16_t> pad(static_cast<size_t>(256) * cols, 0);
+                std::memcpy(pad.data(), data, static_cast<size_t>(rows) * rb);
+                e = upload_blocked(h->router_box, reinterpret_cast<const uint8_t*>(pad.data()), 256, static_cast<int64_t>(rb));
+                // each row's 2-norm, rounded up (a bound on sum |w x| with ||x||_2)
+                std::vector<float> nrm(static_cast<size_t>(rows));
+                for (int64_t r = 0; r < rows; ++r) {
+                    double ss = 0.0;
+                    for (int64_t c = 0; c < cols; ++c) {
+                        uint32_t b = static_cast<uint32_t>(data[r * cols + c]) << 16;
+                        float f;
+                        std::memcpy(&f, &b, 4);
+                        ss += static_cast<double>(f) * f;
+                    }
+                    const double n = std::sqrt(ss) * (1.0 + 1e-12);
+                    float f = static_cast<float>(n);
+                    if (static_cast<double>(f) < n) f = std::nextafter(f, INFINITY);
+                    nrm[static_cast<size_t>(r)] = std::isfinite(f) ? f : INFINITY;
+                }
+                if (e == cudaSuccess) e = cudaMemcpy(h->router_wnorm, nrm.data(), nrm.size() * 4, cudaMemcpyHostToDevice);
+            }
             h->router_bound = e == cudaSuccess;
             // products with BF16 activations stay exact in fp32 when every
             // nonzero weight has a biased exponent in [60, 189]
@@ -669,6 +698,7 @@ int nf_moe_finalize(nf_moe* h) {
         ok = ok && make_tmap_2d(&h->tm_shh, h->sh_h, true, Is, Tm, 64, 128);
         ok = ok && make_tmap_2d(&h->tm_shh_s, h->sh_h, true, Is, Tm, 64, 32);
     }
+    if (h->screen) ok = ok && make_tmap_blocked(&h->tm_router, h->router_box, h->bytes_of(h->router_box));
     if (!ok) return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
     h->finalized = true;
     return NF_OK;
@@ -880,12 +910,64 @@ static int dense_forward(nf_moe* h, const uint16_t* x, const float* residual, in
     return NF_OK;
 }
 
+cudaError_t route_tokens(nf_moe* h, const uint16_t* x, int T, int32_t* idx, float* w, cudaStream_t s) {
+    const nf_moe_desc& d = h->d;
+    const int H = d.hidden, E = d.experts, K = d.top_k;
+    const bool grouped = d.n_group > 1 && d.topk_group < d.n_group;
+    h->last_screened = 0;
+    if (!h->screen || T < kScreenMinTokens || grouped || T > d.max_tokens)
+        return launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, T, H, E, K,
+                             d.routed_scaling, d.normalize, d.n_group, d.topk_group, h->router_w_safe, h->logits,
+                             h->scores, h->choices, idx, w, h->dev_err, s);
+    h->last_screened = 1;
+    // 1. approximate logits [T, 256] on the tensor cores (split K so that the one
+    //    256-wide output block still spreads over the SMs)
+    CUtensorMap tm_x, tm_x_s;
+    if (!make_tmap_2d(&tm_x, x, true, H, T, 64, 128) || !make_tmap_2d(&tm_x_s, x, true, H, T, 64, 32))
+        return cudaErrorInvalidValue;
+    const int m_tiles = (T + 127) / 128, k_tiles = (H + 63) / 64;
+    const int want = std::max(1, std::min(kScreenSlices, (h->grid + m_tiles - 1) / m_tiles));
+    const int kt_per = std::max(2, (k_tiles + want - 1) / want);
+    const int S = (k_tiles + kt_per - 1) / kt_per;
+    cudaError_t e = cudaMemsetAsync(h->screen_counter, 0, sizeof(int), s);
+    if (e != cudaSuccess) return e;
+    GemmArgs g{};
+    g.err = h->dev_err;
+    g.kind = KIND_BF16;
+    g.epi = EPI_STORE_F32;
+    g.K = H;
+    g.dense_rows = T;
+    g.n_blocks = 1;
+    g.b_nb = 1;
+    g.b = h->router_box;
+    g.b_kt = static_cast<int>(k_blocks(2 * static_cast<int64_t>(H)));
+    g.k_split = S;
+    g.kt_per = kt_per;
+    g.out = h->screen_part;
+    g.out_ld = 256;
+    g.out_split_stride = static_cast<int64_t>(T) * 256;
+    g.tile_counter = h->screen_counter;
+    g.early_claim = 1;
+    e = launch_gemm(tm_x, tm_x_s, h->tm_router, g, std::min(h->grid, m_tiles * S), false, s);
+    if (e != cudaSuccess) return e;
+    // 2. bound and candidates: |l~ - l| <= (gamma_H + H 2^-20 + S 2^-24) ||x||_2 ||w_e||_2, with the
+    //    tensor core's accumulation taken as 16 units of fp32 roundoff per step
+    const double u = std::ldexp(1.0, -24);
+    const double c = (H * u / (1.0 - H * u) + H * std::ldexp(1.0, -20) + (S + 1) * u) * 1.01;
+    e = launch_route_screen(h->screen_part, S, static_cast<int64_t>(T) * 256, 256, x, T, H, E, K, h->router_bias,
+                            h->router_wnorm, static_cast<float>(c), h->screen_cand, h->screen_cnt, h->logits, s);
+    if (e != cudaSuccess) return e;
+    // 3. the exact chains of the candidates and the reference's selection
+    return launch_route_exact(x, h->router_wz16, h->router_bias, T, H, E, K, d.routed_scaling, d.normalize,
+                              h->router_w_safe, h->screen_cand, h->screen_cnt, idx, w, s);
+}
+
 static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx_user,
                         float* w_user, cudaStream_t s) {
     if (h->ep_outer) return ep_forward(h, x, residual, T, y, idx_user, w_user, s);
     if (h->dense) return dense_forward(h, x, residual, T, y, s);
     const nf_moe_desc& d = h->d;
-    const int H = d.hidden, E = d.experts, K = d.top_k, Is = d.shared_inter;
+    const int H = d.hidden, K = d.top_k, Is = d.shared_inter;
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
     int32_t* idx = idx_user ? idx_user : h->topk_idx;
     float* w = w_user ? w_user : h->topk_w;
@@ -896,9 +978,7 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     int st = NF_OK;
     if (Is > 0 && (st = launch_shared_expert(h, x, T, rec, s)) != NF_OK) return st;
     rec.begin(NF_STAGE_ROUTER, s);
-    cudaError_t e = launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, T, H, E, K,
-                                  d.routed_scaling, d.normalize, d.n_group, d.topk_group, h->router_w_safe, h->logits,
-                                  h->scores, h->choices, idx, w, h->dev_err, s);
+    cudaError_t e = route_tokens(h, x, T, idx, w, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "router launch");
     rec.end(NF_STAGE_ROUTER, s);
     if ((st = launch_routed_experts(h, x, idx, T, K, rec, s)) != NF_OK) return st;
@@ -1128,6 +1208,8 @@ int nf_moe_debug_tensor(nf_moe* h, int which, void** ptr, int64_t* bytes) {
         case NF_DBG_DOWN: p = h->down; break;
         case NF_DBG_SHARED: p = h->sh_out; break;
         case NF_DBG_ROWS: p = h->pb.meta; break;
+        case NF_DBG_LOGITS: p = h->logits; break;
+        case NF_DBG_SCREEN_COUNT: p = h->screen_cnt; break;
         default: return h->fail(NF_ERR_INVALID, "bad debug tensor id %d", which);
     }
     if (!p) return h->fail(NF_ERR_STATE, "debug tensor %d does not exist for this descriptor", which);

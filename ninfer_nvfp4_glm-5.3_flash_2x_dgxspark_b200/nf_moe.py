@@ -32,7 +32,7 @@ BF16_EXPERT_GATE, BF16_EXPERT_UP, BF16_EXPERT_DOWN = 4, 5, 6
 F32_ROUTER_BIAS = 0
 EXPERTS_NVFP4, EXPERTS_BF16 = 0, 1
 DBG = dict(counts=0, seg_offset=1, pair_row=2, row_token=3, act_codes=4, act_sf=5, h_codes=6, h_sf=7, down=8,
-           shared=9, rows=10)
+           shared=9, rows=10, logits=11, screen_count=12)
 
 EXPORTED = [
     "nf_moe_create", "nf_moe_destroy", "nf_moe_last_error", "nf_status_string", "nf_moe_bind_nvfp4",

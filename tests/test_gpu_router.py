@@ -98,3 +98,71 @@ def test_router_rows_outside_the_exact_product_range():
     assert np.array_equal(lg.view(np.uint32), want_lg.view(np.uint32))
     assert np.array_equal(idx, want_idx)
     assert np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
+
+
+# ---- the screened router of large batches --------------------------------------
+
+def screened_forward(lay, x_bits):
+    """A forward of a batch large enough for the screened router; returns the
+    routes, the tensor-core logits it screened with and the candidate counts."""
+    T = x_bits.shape[0]
+    layer = m.MoeLayer(lay.hidden, lay.experts, lay.top_k, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
+                       swiglu_limit=lay.swiglu_limit, max_tokens=T)
+    layer.bind_layer(lay)
+    x = torch.from_numpy(np.ascontiguousarray(x_bits).view(np.int16)).cuda()
+    y = torch.empty((T, lay.hidden), dtype=torch.float32, device="cuda")
+    idx = torch.empty((T, lay.top_k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, lay.top_k), dtype=torch.float32, device="cuda")
+    layer.forward(x, y, T, None, idx, w)
+    layer.sync()
+    approx = layer.debug_read("logits", np.float32, T * lay.experts).reshape(T, lay.experts)
+    counts = layer.debug_read("screen_count", np.int32, T)
+    out = idx.cpu().numpy(), w.cpu().numpy(), approx, counts
+    layer.close()
+    return out
+
+
+def test_screened_router_prefill_bit_exact_with_bound_slack():
+    """configs[2] through the forward (screened router): every route and weight
+    bit-exact; the tensor cores' logit error, per ||x||_2 ||w_e||_2, stays far
+    below the constant the screen's bound assumes for it; few chains run."""
+    lay, x_bits = wl.config_layer("c2")
+    idx, w, approx, counts = screened_forward(lay, x_bits)
+    x = wl.bf16_bits_to_f32(x_bits)
+    lg, want_idx, want_w = orc.route_tokens(lay, x)
+    assert np.array_equal(idx, want_idx)
+    assert np.array_equal(w.view(np.uint32), want_w.view(np.uint32))
+    wn = np.sqrt((wl.bf16_bits_to_f32(lay.router_w).astype(np.float64) ** 2).sum(1))
+    xn = np.sqrt((x.astype(np.float64) ** 2).sum(1))
+    ratio = np.abs(approx.astype(np.float64) - lg) / (xn[:, None] * wn[None, :])
+    H = lay.hidden
+    assumed_tc = H * 2.0 ** -20  # the screen's allowance for the tensor-core accumulation
+    assert ratio.max() < assumed_tc / 16, ratio.max()
+    assert np.all(counts[counts >= 0] >= lay.top_k) and np.mean(counts < 0) < 0.01
+    assert np.mean(counts[counts > 0]) < 16
+
+
+def test_screened_router_exact_ties_and_special_tokens():
+    """Duplicated router rows give exact ties at the top-k boundary (lowest
+    index wins); NaN, infinite and huge token values take every chain.  Routes
+    bit-exact against the oracle on a 1,536-token batch."""
+    cfg = dict(wl.CONFIGS["c1"])
+    lay = wl.make_layer(cfg, seed=21)
+    for a, b in ((3, 40), (5, 6), (17, 60)):
+        lay.router_w[b] = lay.router_w[a]
+        lay.bias[b] = lay.bias[a]
+    x_bits = wl.make_tokens(cfg, seed=21, tokens=1536).copy()
+    x_bits[7, 100] = 0x7FC0                                                     # NaN
+    x_bits[8, 5] = 0x7F80                                                       # +inf
+    x_bits[9] = (x_bits[9].astype(np.uint32) + (40 << 7)).astype(np.uint16)     # x 2^40
+    x_bits[10, 3] = 0x0001                                                      # BF16 subnormal
+    idx, w, _, counts = screened_forward(lay, x_bits)
+    _, want_idx, want_w = orc.route_tokens(lay, wl.bf16_bits_to_f32(x_bits))
+    assert np.array_equal(idx, want_idx)
+    ok = ~np.isnan(want_w).any(axis=1)
+    assert np.array_equal(w[ok].view(np.uint32), want_w[ok].view(np.uint32))
+    assert np.all(np.isnan(w[~ok]))
+    assert all(counts[t] == -1 for t in (7, 8, 9, 10))
+    # the tied pairs both reach the exact stage whenever one of them is near the boundary
+    picks = set(map(tuple, np.sort(idx, axis=1)))
+    assert any(3 in p for p in picks) and any(5 in p for p in picks)
