@@ -27,10 +27,10 @@ namespace {
 constexpr int kHd = 128;            // head dimension
 constexpr int kAttnTile = 32;        // keys per pipeline stage
 constexpr int kAttnStages = 4;
-constexpr int kAttnWarps = 4;        // consumer warps (8 keys of every stage each)
+constexpr int kAttnWarps = 2;        // consumer warps (16 keys of every stage each)
 constexpr int kAttnThreads = 32 * (kAttnWarps + 1);
-constexpr int kRowBytes = kHd * 2;   // one BF16 key or value row
-constexpr int kStageBytes = 2 * kAttnTile * kRowBytes;  // K tile + V tile
+constexpr int kBoxBytes = kAttnTile * 128;  // one TMA box: 32 keys x 64 dims (128-byte rows, swizzled)
+constexpr int kStageBytes = 4 * kBoxBytes;  // K dims 0-63 | K 64-127 | V 0-63 | V 64-127
 constexpr int kAttnMaxSplits = kAttnMaxSplitsHost;
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -169,28 +169,63 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(const float* __restri
 // ---------------------------------------------------------------------------
 // GQA decode attention, flash-decoding split over the context.
 // grid (T * nkv, splits), kAttnThreads threads: warp kAttnWarps is the
-// producer (bulk copies of 32-key K and V tiles into a 4-stage ring), warps
-// 0..3 consume 8 keys of every stage each.  In a consumer warp lane
-// (h = lane / 4, quarter = lane % 4) owns q head g*G + h's dims
-// [32 quarter, 32 quarter + 32): a key's score is 32 FMAs per lane plus two
-// shuffles, its value row 32 FMAs -- every byte of K and V feeds all G = 8
-// query heads of the KV head.  Softmax runs online per 8-key tile (max,
-// rescale, exp).  The four warps' partial (max, sum, acc) merge in shared
-// memory; with one split the CTA writes the output, else its partial
-// goes to part_* and attn_combine_kernel merges the splits.
+// producer (TMA tiles of 32 keys x 64 dims, 128-byte swizzled, two per K
+// tile and two per V tile, into a 4-stage ring), warps 0..1 consume 16 keys
+// of every stage each.  The two contractions run on the tensor cores as
+// warp-level MMAs (m16n8k16, BF16 in, F32 accumulate): S = Q K^T with the G
+// = 8 query heads of the KV head as rows (rows 8-15 zero) and 8 keys per
+// n-tile, then O += P V with P from S's accumulator fragments.  The kernel
+// is bound by the cache's HBM bytes (8 flops per byte), so the MMAs only
+// remove the ~200 scalar instructions a key cost on the CUDA cores; the
+// swizzled tiles make every ldmatrix conflict-free.  Softmax runs online per
+// 16-key chunk (max over the chunk, rescale, exp).  The warps' partial (max,
+// sum, acc) merge in shared memory; with one split the CTA writes the
+// output, else its partial goes to part_* and attn_combine_kernel merges the
+// splits.  q is rounded to BF16 for the MMA, P too (as flash attention
+// does); scores and sums stay F32.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// d = a (16 x 16, row) * b (16 x 8, col) + d, BF16 in, F32 accumulate
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// shared-memory address of 16-byte chunk `c` (0..7) of row `r` in a 128-byte
+// swizzled box (the box base is 1024-byte aligned)
+__device__ __forceinline__ uint32_t sw128(uint32_t box, int r, int c) {
+    return box + static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
 template <int G>
-__global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const float* __restrict__ q,
-                                                                  const uint16_t* __restrict__ kc,
-                                                                  const uint16_t* __restrict__ vc,
+__global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const __grid_constant__ CUtensorMap tmk,
+                                                                  const __grid_constant__ CUtensorMap tmv,
+                                                                  const float* __restrict__ q,
                                                                   const int32_t* __restrict__ pos, int nkv, int L_max,
                                                                   int chunk, float scale, uint16_t* __restrict__ out,
                                                                   AttnPart* __restrict__ part_ml,
                                                                   float* __restrict__ part_acc, int* __restrict__ err) {
-    static_assert(G == 8, "lane layout: 8 heads x 4 quarters");
+    static_assert(G == 8, "the 8 query heads of a KV head are the MMA's rows 0-7");
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    uint8_t* stages = smem;  // [kAttnStages][K tile | V tile]
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stages = smem;  // [kAttnStages][K dims 0-63 | K dims 64-127 | V dims 0-63 | V dims 64-127]
     // the warps' partials reuse the stage ring once every tile is consumed
     float* s_acc = reinterpret_cast<float*>(stages);                      // [kAttnWarps][G][kHd]
     float* s_ml = s_acc + kAttnWarps * G * kHd;                           // [kAttnWarps][G][2]
@@ -206,7 +241,7 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const float* _
     const int k0 = blockIdx.y * chunk;
     const int k1 = min(len, k0 + chunk);
     const int ntiles = k1 > k0 ? (k1 - k0 + kAttnTile - 1) / kAttnTile : 0;
-    const int64_t cache_base = (static_cast<int64_t>(seq) * nkv + g) * L_max;
+    const int cache_row = (seq * nkv + g) * L_max;  // tensor-map row of key 0
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kAttnStages; ++s) {
@@ -215,6 +250,8 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const float* _
         }
         s_abort = 0;
         fence_barrier_init();
+        prefetch_tensormap(&tmk);
+        prefetch_tensormap(&tmv);
     }
     __syncthreads();
     volatile int* abort_flag = &s_abort;
@@ -231,13 +268,13 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const float* _
                     atomicCAS(err, 0, NF_DEVERR_WAIT_EMPTY);
                     break;
                 }
-                const int kk = k0 + i * kAttnTile;
-                const int n = min(kAttnTile, k1 - kk);
-                const uint32_t bytes = static_cast<uint32_t>(n) * kRowBytes;
-                mbar_arrive_expect_tx(&full[s], 2 * bytes);
+                const int y = cache_row + k0 + i * kAttnTile;
                 uint8_t* st = stages + s * kStageBytes;
-                bulk_load(st, kc + (cache_base + kk) * kHd, bytes, &full[s]);
-                bulk_load(st + kAttnTile * kRowBytes, vc + (cache_base + kk) * kHd, bytes, &full[s]);
+                mbar_arrive_expect_tx(&full[s], kStageBytes);  // whole boxes (zero-filled past the tensor)
+                tma_load_2d(st, &tmk, &full[s], 0, y);
+                tma_load_2d(st + kBoxBytes, &tmk, &full[s], 64, y);
+                tma_load_2d(st + 2 * kBoxBytes, &tmv, &full[s], 0, y);
+                tma_load_2d(st + 3 * kBoxBytes, &tmv, &full[s], 64, y);
                 issued = i + 1;
             }
             if (*abort_flag) {
@@ -250,23 +287,22 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const float* _
             }
         }
     }
-    float acc[32];
-    float m = -INFINITY, l = 0.f;
-    const int h = lane >> 2, qtr = lane & 3;
+    const int grp = lane >> 2, t4 = lane & 3;  // MMA fragment coordinates: row group, thread in group
+    float o[16][4];                            // O fragments: head grp (c0, c1) x dims 8 n + 2 t4 (+1)
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m = -INFINITY, l = 0.f;  // head grp's running max and (this lane's part of the) sum
     if (warp < kAttnWarps) {
         // ------------------------- consumers -------------------------
-        const int head = g * G + h;
-        // qv and acc hold the quarter's 32 dims in the rotated piece order the
-        // reads below use: element 8c + e is dim 32 qtr + 8 ((c + qtr) % 4) + e,
-        // so every register index is a compile-time constant
-        float qv[32];
-        const float* qsrc = q + (static_cast<int64_t>(seq) * nq + head) * kHd + 32 * qtr;
+        // Q fragments (rows 8-15 of the MMA are zero): k-step s holds dims 16 s + 2 t4 (+1) and + 8
+        uint32_t qa[8][2];
+        const float* qrow = q + (static_cast<int64_t>(seq) * nq + g * G + grp) * kHd;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) qv[8 * c + e] = qsrc[8 * ((c + qtr) & 3) + e];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+        for (int s = 0; s < 8; ++s) {
+            qa[s][0] = pack_bf16x2(qrow[16 * s + 2 * t4], qrow[16 * s + 2 * t4 + 1]);
+            qa[s][1] = pack_bf16x2(qrow[16 * s + 2 * t4 + 8], qrow[16 * s + 2 * t4 + 9]);
+        }
+        const int mi = lane >> 3, mr = lane & 7;  // ldmatrix: this lane's matrix and row
         for (int i = 0; i < ntiles; ++i) {
             const int s = i % kAttnStages;
             const uint32_t ph = (i / kAttnStages) & 1u;
@@ -275,79 +311,89 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const float* _
                 atomicCAS(err, 0, NF_DEVERR_WAIT_FULL);
                 break;
             }
-            const uint8_t* kt = stages + s * kStageBytes;
-            const uint8_t* vt = kt + kAttnTile * kRowBytes;
+            const uint32_t st = smem_u32(stages + s * kStageBytes);
             const int kk = k0 + i * kAttnTile;
-            const int nvalid = min(kAttnTile, k1 - kk);
-            float sc[8];
+            const int nv = min(16, max(0, min(kAttnTile, k1 - kk) - 16 * warp));  // valid keys of my 16
+            if (nv > 0) {
+                if (nv < 16) {
+                    // V rows past the sequence hold whatever the cache holds there: zero
+                    // them, so their zero weights cannot meet a NaN in the MMA
+                    for (int r = 16 * warp + nv + (lane >> 3); r < 16 * warp + 16; r += 4)
+                        for (int b = 0; b < 2; ++b)
+                            *reinterpret_cast<uint4*>(stages + s * kStageBytes + (2 + b) * kBoxBytes + r * 128 +
+                                                      (lane & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
+                    __syncwarp();
+                }
+                // S = Q K^T: n-tile j holds keys 16 warp + 8 j .. + 7
+                float sc[2][4];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int key = warp * 8 + j;
-                float d = 0.f;
-                if (key < nvalid) {
-                    const uint8_t* row = kt + key * kRowBytes + qtr * 64;
-                    // 16-byte pieces in a rotated order: the 4 quarters of a
-                    // row then read 4 different bank groups at each step
+                for (int j = 0; j < 2; ++j) {
+                    sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+                    const int key = 16 * warp + 8 * j + mr;
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const int pc = (c + qtr) & 3;
-                        const uint4 kw = *reinterpret_cast<const uint4*>(row + pc * 16);
-                        const uint32_t w4[4] = {kw.x, kw.y, kw.z, kw.w};
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            d = __fmaf_rn(qv[c * 8 + 2 * u], __uint_as_float(w4[u] << 16), d);
-                            d = __fmaf_rn(qv[c * 8 + 2 * u + 1], __uint_as_float(w4[u] & 0xffff0000u), d);
-                        }
+                    for (int s2 = 0; s2 < 8; s2 += 2) {
+                        // matrices: dims 16 s2 + 8 (mi & 1) of k-step s2 + (mi >> 1)
+                        const int dc = 16 * (s2 + (mi >> 1)) + 8 * (mi & 1);
+                        uint32_t b[4];
+                        ldsm_x4(sw128(st + (dc >> 6) * kBoxBytes, key, (dc & 63) >> 3), b);
+                        mma_16816(sc[j], qa[s2][0], 0u, qa[s2][1], 0u, b[0], b[1]);
+                        mma_16816(sc[j], qa[s2 + 1][0], 0u, qa[s2 + 1][1], 0u, b[2], b[3]);
                     }
                 }
-                d += __shfl_xor_sync(0xffffffffu, d, 1);
-                d += __shfl_xor_sync(0xffffffffu, d, 2);
-                sc[j] = key < nvalid ? d * scale : -INFINITY;
-            }
-            float tm = m;
+                // online softmax over this chunk for head grp (rows 8-15, c2 / c3, are padding)
+                float v[4];
+                v[0] = (8 * 0 + 2 * t4 < nv) ? sc[0][0] * scale : -INFINITY;
+                v[1] = (8 * 0 + 2 * t4 + 1 < nv) ? sc[0][1] * scale : -INFINITY;
+                v[2] = (8 * 1 + 2 * t4 < nv) ? sc[1][0] * scale : -INFINITY;
+                v[3] = (8 * 1 + 2 * t4 + 1 < nv) ? sc[1][1] * scale : -INFINITY;
+                float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float mn = fmaxf(m, mx);
+                if (mn != -INFINITY) {
+                    const float corr = __expf(m - mn);  // m = -inf on the first chunk: 0
+                    float p[4];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) tm = fmaxf(tm, sc[j]);
-            if (tm != -INFINITY) {
-                const float corr = __expf(m - tm);  // m = -inf on the first tile: 0
-                l *= corr;
+                    for (int e = 0; e < 4; ++e) p[e] = __expf(v[e] - mn);
+                    l = l * corr + ((p[0] + p[1]) + (p[2] + p[3]));
+                    m = mn;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) acc[j] *= corr;
-                m = tm;
+                    for (int n = 0; n < 16; ++n) {
+                        o[n][0] *= corr;
+                        o[n][1] *= corr;
+                    }
+                    // O += P V: P (row grp) = keys 2 t4 (+1) and 8 + 2 t4 (+1) of my 16
+                    const uint32_t pa0 = pack_bf16x2(p[0], p[1]), pa2 = pack_bf16x2(p[2], p[3]);
+                    const int key = 16 * warp + 8 * (mi & 1) + mr;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int key = warp * 8 + j;
-                    if (key >= nvalid) continue;
-                    const float p = __expf(sc[j] - m);
-                    l += p;
-                    const uint8_t* row = vt + key * kRowBytes + qtr * 64;
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const int pc = (c + qtr) & 3;
-                        const uint4 vw = *reinterpret_cast<const uint4*>(row + pc * 16);
-                        const uint32_t w4[4] = {vw.x, vw.y, vw.z, vw.w};
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            acc[c * 8 + 2 * u] = __fmaf_rn(p, __uint_as_float(w4[u] << 16), acc[c * 8 + 2 * u]);
-                            acc[c * 8 + 2 * u + 1] =
-                                __fmaf_rn(p, __uint_as_float(w4[u] & 0xffff0000u), acc[c * 8 + 2 * u + 1]);
-                        }
+                    for (int n = 0; n < 16; n += 2) {
+                        // matrices: keys 8 (mi & 1) .. + 7 of dims 8 (n + (mi >> 1)) .. + 7, transposed
+                        const int dc = 8 * (n + (mi >> 1));
+                        uint32_t b[4];
+                        ldsm_x4_t(sw128(st + (2 + (dc >> 6)) * kBoxBytes, key, (dc & 63) >> 3), b);
+                        mma_16816(o[n], pa0, 0u, pa2, 0u, b[0], b[1]);
+                        mma_16816(o[n + 1], pa0, 0u, pa2, 0u, b[2], b[3]);
                     }
                 }
+                if (nv < 16) fence_proxy_async();  // the zeroed rows before the next TMA write into the stage
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
     }
     __syncthreads();  // every tile consumed: the ring is free for the partials
     if (warp < kAttnWarps) {
-        float* sa = s_acc + (warp * G + h) * kHd + 32 * qtr;
+        float* sa = s_acc + (warp * G + grp) * kHd;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) sa[8 * ((c + qtr) & 3) + e] = acc[8 * c + e];
-        if (qtr == 0) {
-            s_ml[(warp * G + h) * 2] = m;
-            s_ml[(warp * G + h) * 2 + 1] = l;
+        for (int n = 0; n < 16; ++n) {
+            sa[8 * n + 2 * t4] = o[n][0];
+            sa[8 * n + 2 * t4 + 1] = o[n][1];
+        }
+        if (t4 == 0) {
+            s_ml[(warp * G + grp) * 2] = m;
+            s_ml[(warp * G + grp) * 2 + 1] = l;
         }
     }
     __syncthreads();
@@ -457,10 +503,10 @@ int attn_splits(int T, int nkv, int L_max, int sms) {
     return std::max(1, std::min(want, std::min(max_splits, kAttnMaxSplits)));
 }
 
-size_t attn_smem_bytes() { return 128 + static_cast<size_t>(kAttnStages) * kStageBytes + 2 * kAttnStages * 8; }
+size_t attn_smem_bytes() { return 1024 + static_cast<size_t>(kAttnStages) * kStageBytes + 2 * kAttnStages * 8; }
 
-cudaError_t launch_gqa_decode(const float* q, const uint16_t* kc, const uint16_t* vc, const int32_t* pos, int T,
-                              int nq, int nkv, int L_max, int splits, AttnPart* part_ml, float* part_acc,
+cudaError_t launch_gqa_decode(const CUtensorMap& tmk, const CUtensorMap& tmv, const float* q, const int32_t* pos,
+                              int T, int nq, int nkv, int L_max, int splits, AttnPart* part_ml, float* part_acc,
                               uint16_t* out, int* err, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (nq != 8 * nkv) return cudaErrorInvalidValue;
@@ -477,8 +523,8 @@ cudaError_t launch_gqa_decode(const float* q, const uint16_t* kc, const uint16_t
         attr[dev] = true;
     }
     const float scale = 1.f / sqrtf(static_cast<float>(kHd));
-    gqa_decode_kernel<8><<<dim3(T * nkv, splits), kAttnThreads, smem, st>>>(q, kc, vc, pos, nkv, L_max, chunk, scale, out,
-                                                                          part_ml, part_acc, err);
+    gqa_decode_kernel<8><<<dim3(T * nkv, splits), kAttnThreads, smem, st>>>(tmk, tmv, q, pos, nkv, L_max, chunk, scale,
+                                                                          out, part_ml, part_acc, err);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess && splits > 1) {
         const int pairs = T * nq;

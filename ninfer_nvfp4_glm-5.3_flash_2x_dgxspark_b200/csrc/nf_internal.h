@@ -247,8 +247,10 @@ cudaError_t launch_qk_norm_rope(const float* qkv, int slices, int64_t stride, in
 // splits of the context for T sequences (the partial buffers hold
 // T * nq * splits pairs of floats and T * nq * splits * 128 floats)
 int attn_splits(int T, int nkv, int L_max, int sms);
-cudaError_t launch_gqa_decode(const float* q, const uint16_t* kc, const uint16_t* vc, const int32_t* pos, int T,
-                              int nq, int nkv, int L_max, int splits, AttnPart* part_ml, float* part_acc,
+// tmk / tmv: the layer's K and V caches as 2-D BF16 tensors [seq * nkv * L_max,
+// 128] with 64 x 32 boxes and 128-byte swizzle (make_tmap_2d)
+cudaError_t launch_gqa_decode(const CUtensorMap& tmk, const CUtensorMap& tmv, const float* q, const int32_t* pos,
+                              int T, int nq, int nkv, int L_max, int splits, AttnPart* part_ml, float* part_acc,
                               uint16_t* out, int* err, cudaStream_t st);
 
 cudaError_t launch_fill_bf16_hash(uint16_t* p, int64_t n, uint64_t seed, cudaStream_t st);

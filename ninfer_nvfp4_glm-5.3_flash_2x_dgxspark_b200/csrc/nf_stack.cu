@@ -52,6 +52,7 @@ struct StackLayer {
     uint16_t* kc = nullptr;    // [B][nkv][L][D]
     uint16_t* vc = nullptr;
     CUtensorMap tm_qkv{}, tm_o{};
+    CUtensorMap tm_kc{}, tm_vc{};  // the caches as [B nkv L, 128] tensors for the attention's TMA tiles
     uint16_t bound = 0;        // bit per NF_STACK_* tensor
 };
 
@@ -380,8 +381,11 @@ int nf_stack_finalize(nf_stack* s) {
     for (int l = 0; l < d.layers; ++l) {
         StackLayer& Ly = s->layers[static_cast<size_t>(l)];
         if ((Ly.bound & all) != all) return s->fail(NF_ERR_STATE, "layer %d: missing attention tensors", l);
+        const uint64_t cache_rows = static_cast<uint64_t>(d.max_batch) * d.kv_heads * d.max_context;
         if (!make_tmap_blocked(&Ly.tm_qkv, Ly.w_qkv, static_cast<uint64_t>(box_order_bytes(qkv_rows(d), 2 * H))) ||
-            !make_tmap_blocked(&Ly.tm_o, Ly.w_o, static_cast<uint64_t>(box_order_bytes(H, 2 * NQ))))
+            !make_tmap_blocked(&Ly.tm_o, Ly.w_o, static_cast<uint64_t>(box_order_bytes(H, 2 * NQ))) ||
+            !make_tmap_2d(&Ly.tm_kc, Ly.kc, true, kHeadDim, cache_rows, 64, 32) ||
+            !make_tmap_2d(&Ly.tm_vc, Ly.vc, true, kHeadDim, cache_rows, 64, 32))
             return s->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
     }
     s->qkv_host.clear();
@@ -459,8 +463,8 @@ int nf_stack_decode(nf_stack* s, const int32_t* tokens, const int32_t* positions
             e = launch_qk_norm_rope(s->qkv_part, S1, static_cast<int64_t>(T) * NQKV, T, nq, nkv, Ly.q_norm, Ly.k_norm,
                                     1e-5f, d.rope_theta, positions, L, s->q, Ly.kc, Ly.vc, s->err, st);
         if (e == cudaSuccess)
-            e = launch_gqa_decode(s->q, Ly.kc, Ly.vc, positions, T, nq, nkv, L, splits, s->part_ml, s->part_acc,
-                                  s->att16, s->err, st);
+            e = launch_gqa_decode(Ly.tm_kc, Ly.tm_vc, s->q, positions, T, nq, nkv, L, splits, s->part_ml,
+                                  s->part_acc, s->att16, s->err, st);
         if (e == cudaSuccess)
             e = launch_projection(s, s->tm_att, s->tm_att_s, Ly.tm_o, Ly.w_o, T, H, NQ, s->o_part,
                                   s->counters + 2 * l + 1, &S2, st);
