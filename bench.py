@@ -742,14 +742,19 @@ def run_stack(args, m, torch, hbm_peak: float) -> dict:
     context (caches filled on the device with a pseudo-random history) at
     batch 1/16/64/256 on one GPU.  A step is one token for every sequence;
     timed as CUDA-graph replays of the whole step."""
-    cfg = wl.STACK_CONFIGS["c4"]
+    cfg = dict(wl.STACK_CONFIGS["c4"])
+    layers = getattr(args, "stack_layers", None)
+    if layers and layers != cfg["layers"]:
+        # a shorter stack of the same shapes (profiling): one dense, one BF16-expert layer
+        cfg.update(layers=layers, dense_layers=1, bf16_expert_layers=1)
+    batches = tuple(getattr(args, "stack_batches", None) or wl.STACK_BATCHES)
     t0 = time.perf_counter()
     model = wl.make_stack(cfg, seed=4, share=True)
     st = m.DecoderStack(vocab=cfg["vocab"], hidden=cfg["hidden"], layers=cfg["layers"],
                         dense_layers=cfg["dense_layers"], bf16_expert_layers=cfg["bf16_expert_layers"],
                         dense_inter=cfg["dense_inter"], experts=cfg["experts"], top_k=cfg["top_k"], inter=cfg["inter"],
                         shared_inter=cfg["shared_inter"], routed_scaling=cfg["scaling"], q_heads=cfg["q_heads"],
-                        kv_heads=cfg["kv_heads"], max_batch=max(wl.STACK_BATCHES), max_context=cfg["context"])
+                        kv_heads=cfg["kv_heads"], max_batch=max(batches), max_context=cfg["context"])
     st.bind_model(model)
     st.fill_kv(1)
     setup_s = time.perf_counter() - t0
@@ -762,7 +767,9 @@ def run_stack(args, m, torch, hbm_peak: float) -> dict:
                       "generated on the host and bound into every layer of its kind (separate device copies)",
            "setup_s": setup_s, "per_batch": {}}
     L = cfg["context"]
-    for B in wl.STACK_BATCHES:
+    if cfg["layers"] != wl.STACK_CONFIGS["c4"]["layers"]:
+        out["workload"] += f" [shortened to {cfg['layers']} layers]"
+    for B in batches:
         rng = np.random.default_rng(B)
         tok = torch.from_numpy(rng.integers(0, cfg["vocab"], B).astype(np.int32)).cuda()
         pos = torch.full((B,), L - 1, dtype=torch.int32, device="cuda")
@@ -829,6 +836,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true", help="skip the secondary prefill measurement")
     ap.add_argument("--no-stack", action="store_true", help="skip the configs[4] decoder-stack measurement")
+    ap.add_argument("--stack-layers", type=int, default=None,
+                    help="--only stack: a shorter stack of configs[4]'s shapes (profiling)")
+    ap.add_argument("--stack-batches", type=int, nargs="*", default=None, help="--only stack: batch sizes to run")
     ap.add_argument("--only", choices=["decode", "prefill", "dense", "stack"],
                     help="time one workload alone (no e2e, CPU baseline or clock sampling); for profilers")
     args = ap.parse_args()
