@@ -518,6 +518,7 @@ def run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src) -> dict:
     layer = m.MoeLayer(H, lay.experts, K, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
                        swiglu_limit=lay.swiglu_limit, max_tokens=T)
     layer.bind_layer(lay)
+    layer.set_expert_gemm(args.expert_gemm)
     x = torch.from_numpy(x_bits.view(np.int16)).cuda()
     y = torch.empty((T, H), dtype=torch.float32, device="cuda")
     idx = torch.empty((T, K), dtype=torch.int32, device="cuda")
@@ -527,7 +528,8 @@ def run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src) -> dict:
         layer.forward(x, y, T, None, idx, w, stream=stream)
     torch.cuda.synchronize()
     steps = max(3, min(args.steps, 20))
-    layer.profile(True)
+    # the step time unprofiled (the kernels hand rows over and overlap as in
+    # service); then the per-stage split from as many profiled steps
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(steps):
@@ -535,10 +537,16 @@ def run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src) -> dict:
     ev1.record()
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / steps
+    layer.profile(True)
+    for _ in range(steps):
+        layer.forward(x, y, T, None, idx, w, stream=stream)
+    torch.cuda.synchronize()
     stages, nfw = layer.stage_times()
     layer.profile(False)
     layer.sync(stream)
     counts = np.bincount(idx.cpu().numpy().ravel(), minlength=lay.experts)
+    # the screened router's candidates per token (-1: every chain)
+    cand = layer.debug_read("screen_count", np.int32, T)
     fl = prefill_flops(lay, T)
     gu_ms = stages["gate_up"] / max(nfw, 1)
     dn_ms = stages["down"] / max(nfw, 1)
@@ -548,7 +556,13 @@ def run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src) -> dict:
         "workload": "c2 prefill: c1 shapes, T8192, bias tuned to 512 +- 10% tokens per expert (configs[2])",
         "tokens_per_s": T / (ms * 1e-3), "ms_per_step": ms, "steps": steps,
         "stages_us": {k: 1e3 * v / max(nfw, 1) for k, v in stages.items()},
+        "timing": "ms_per_step over K unprofiled steps (direct launches, stages overlapping as in service); "
+                  "stages_us from K more steps with an event around each kernel (kernels kept apart)",
+        "expert_gemms": {"one_sm": "one SM per 128 x 256 tile, 256-K stages", "wide": "one SM, 512-K stages",
+                         "pair": "CTA pairs (cta_group::2), 256 x 256 tiles, A resident"}[args.expert_gemm],
         "expert_tokens_min_max": [int(counts.min()), int(counts.max())],
+        "router_screen": {"mean_candidates": float(np.mean(np.where(cand < 0, lay.experts, cand))),
+                          "all_chain_tokens": int(np.sum(cand < 0)), "exact_chains": int(np.sum(np.where(cand < 0, lay.experts, cand)))},
         "fp4_tflops_layer": fl["fp4"] / (ms * 1e-3) / 1e12,
         "fp4_frac_layer": fl["fp4"] / (ms * 1e-3) / 1e12 / fp4_peak,
         "mixed_roofline_frac": t_ideal / (ms * 1e-3),
@@ -836,6 +850,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true", help="skip the secondary prefill measurement")
     ap.add_argument("--no-stack", action="store_true", help="skip the configs[4] decoder-stack measurement")
+    ap.add_argument("--expert-gemm", choices=["one_sm", "wide", "pair"], default="one_sm",
+                    help="prefill: the expert GEMM form (nf_moe_set_expert_gemm); the default is the fastest measured")
     ap.add_argument("--stack-layers", type=int, default=None,
                     help="--only stack: a shorter stack of configs[4]'s shapes (profiling)")
     ap.add_argument("--stack-batches", type=int, nargs="*", default=None, help="--only stack: batch sizes to run")

@@ -159,6 +159,15 @@ NF_API int nf_moe_forward_host(nf_moe* handle, const float* x_host, const float*
  * profiling on, on the NULL stream, or issued while the caller is capturing
  * run the kernels directly. */
 NF_API int nf_moe_set_graph_mode(nf_moe* handle, int enable);
+/* The grouped NVFP4 expert GEMMs of batches with at least 256 routed rows per
+ * expert on average (prefill): NF_GEMM_ONE_SM (default) runs 128 x 256 tiles
+ * with 256-K stages on each SM; NF_GEMM_WIDE_STAGES the same tiles with 512-K
+ * stages (half the TMA copies per MMA, two stages deep); NF_GEMM_CTA_PAIR
+ * 256 x 256 tiles on pairs of SMs (tcgen05 cta_group::2) with the activation
+ * rows resident.  Smaller batches always take the first.  The results agree
+ * within the layer tolerance (the same K order per output). */
+enum { NF_GEMM_ONE_SM = 0, NF_GEMM_WIDE_STAGES = 1, NF_GEMM_CTA_PAIR = 2 };
+NF_API int nf_moe_set_expert_gemm(nf_moe* handle, int mode);
 /* Waits for the handle's work on `stream` and reports a device-side error. */
 NF_API int nf_moe_sync(nf_moe* handle, void* stream);
 

@@ -27,9 +27,9 @@ OBJ = HERE / "_build"
 LIB = HERE / "lib" / "libnf_moe.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["nf_kernels.cu", "nf_gemm.cu", "nf_moe.cu", "nf_noalloc.cu", "nf_ep.cu", "nf_tp.cu", "nf_attn.cu",
+CU_SOURCES = ["nf_kernels.cu", "nf_gemm.cu", "nf_gemm2.cu", "nf_moe.cu", "nf_noalloc.cu", "nf_ep.cu", "nf_tp.cu", "nf_attn.cu",
               "nf_stack.cu"]
-HEADERS = ["nf_handle.h", "nf_common.cuh", "nf_internal.h", "nf_nccl.h"]
+HEADERS = ["nf_handle.h", "nf_common.cuh", "nf_internal.h", "nf_nccl.h", "nf_gemm_shared.cuh"]
 
 
 def _newer(out: Path, inputs: list[Path]) -> bool:

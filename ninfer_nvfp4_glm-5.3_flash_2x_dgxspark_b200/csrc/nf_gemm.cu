@@ -32,6 +32,7 @@
 // Every wait is bounded (nf_common.cuh mbar_wait); on a timeout the kernel
 // records an error code, stops every role, drains and frees TMEM.
 #include "nf_common.cuh"
+#include "nf_gemm_shared.cuh"
 #include "nf_internal.h"
 
 #include <mutex>
@@ -57,16 +58,28 @@ constexpr int SF_COLS = 48;                // per stage: 16 for A, 32 for B
 // TMEM columns 0-255 and 256-511 (all of TMEM: BF16 needs no scale-factor
 // columns), so a stage moves 64 KB for twice the MMAs of a 48 KB stage;
 // three stages fit in shared memory.
-template <int KIND, int MT>
+// KS = 2 (grouped NVFP4 at prefill-sized batches): a stage covers 512 of K
+// with the same four copies, each twice as large -- A as one 3-D box of two
+// 16 KB chunks, B as one 3-D box of two consecutive 32 KB box-order blocks,
+// and each scale group as one bulk copy.  A TMA copy costs its SM about 280
+// cycles of fixed overhead (measured: a 16 KB box streams from L2 at 43 B per
+// cycle per SM, a 32 KB box at 69), so the four copies of a 256-K stage
+// (~1,450 cycles) outlast its four MMAs (512 cycles) almost threefold; at 512
+// K per stage the same copies feed eight MMAs.  Two stages fit.
+template <int KIND, int MT, int KS = 1>
 struct Geo {
-    static constexpr int kStages = MT == 2 ? 3 : STAGES;
+    static constexpr int kStages = MT == 2 ? 3 : (KS == 2 ? 2 : STAGES);
     static constexpr int kTileM = BM * MT;
-    static constexpr int kAStage = kTileM * 128;
-    static constexpr int kSfaStage = KIND == KIND_NVFP4 ? SFA_STAGE_BYTES : 0;
-    static constexpr int kSfbStage = KIND == KIND_NVFP4 ? SFB_STAGE_BYTES : 0;
-    static constexpr int kSmem = 1024 + kStages * (kAStage + B_STAGE_BYTES + kSfaStage + kSfbStage) + 512;
+    static constexpr int kAStage = kTileM * 128 * KS;
+    static constexpr int kBStage = B_STAGE_BYTES * KS;
+    static constexpr int kSfaStage = KIND == KIND_NVFP4 ? SFA_STAGE_BYTES * KS : 0;
+    static constexpr int kSfbStage = KIND == KIND_NVFP4 ? SFB_STAGE_BYTES * KS : 0;
+    static constexpr int kSfCols = SF_COLS * KS;
+    static constexpr int kSmem = 1024 + kStages * (kAStage + kBStage + kSfaStage + kSfbStage) + 512;
     static_assert(MT == 1 || KIND == KIND_BF16, "paired row tiles are BF16 only");
+    static_assert(KS == 1 || (KIND == KIND_NVFP4 && MT == 1), "512-K stages are NVFP4 only");
     static_assert(kSmem <= 227 * 1024, "shared memory");
+    static_assert(KIND == KIND_BF16 || ACC_COLS + kStages * kSfCols <= TMEM_COLS, "TMEM columns");
 };
 
 struct TileInfo {
@@ -120,55 +133,14 @@ __device__ __forceinline__ void tile_krange(const GemmArgs& a, int i, int k_tile
     }
 }
 
-// swiglu_clamp element (src/text_forward.cpp:1439-1445): min(g, L) into SiLU,
-// up clamped to [-L, L] with std::min / std::max semantics, with a fast SiLU
-// (x / (1 + e^-x), hardware exp2 and divide).  Used
-// where the result feeds a 4-bit quantiser or a BF16 store, so agreement to
-// a few ulp with the reference's libm SiLU is all that matters.
-__device__ __forceinline__ float swiglu_fast(float g, float u, float L) {
-    const float cg = (L < g) ? L : g;
-    const float lo = (-L < u) ? u : -L;
-    const float cu = (lo < L) ? lo : L;
-    return __fmul_rn(__fdividef(cg, 1.f + __expf(-cg)), cu);
-}
-
-// swiglu_clamp_bf16 element (src/text_forward.cpp:99-106), the dense layers'
-// form: the capped gate, the clamped up, SiLU of the capped gate and the
-// product are each rounded to BF16 (the same clamps and SiLU as swiglu_fast).
-__device__ __forceinline__ float swiglu_bf16_fast(float g, float u, float L) {
-    const float cg = bf16_round_hw((L < g) ? L : g);
-    const float lo = (-L < u) ? u : -L;
-    const float cu = bf16_round_hw((lo < L) ? lo : L);
-    const float act = bf16_round_hw(__fdividef(cg, 1.f + __expf(-cg)));
-    return bf16_round_hw(__fmul_rn(act, cu));
-}
-
-// Bounded wait, by every lane of the calling warp, until *counter >= target
-// (acquire); false once the budget runs out or the CTA or kernel gave up.
-__device__ __forceinline__ bool wait_count(const int* counter, int target, volatile int* cta_abort,
-                                           volatile int* dev_err) {
-    const uint64_t t0 = globaltimer_ns();
-    for (;;) {
-        int v;
-        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
-        if (v >= target) return true;
-        if (*cta_abort != 0 || *dev_err != 0 || globaltimer_ns() - t0 > NF_WAIT_BUDGET_NS) return false;
-        __nanosleep(64);
-    }
-}
-
-__device__ __forceinline__ void set_abort(volatile int* cta_abort, int* dev_err, int code) {
-    *cta_abort = 1;
-    atomicCAS(dev_err, 0, code);
-}
-
-template <int KIND, int EPI, int MT>
+template <int KIND, int EPI, int MT, int KS>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tma_small,
                 const __grid_constant__ CUtensorMap tmb, const GemmArgs args) {
-    using G = Geo<KIND, MT>;
+    using G = Geo<KIND, MT, KS>;
     constexpr int STAGES = G::kStages;  // (shadows the file-wide stage count)
     constexpr int A_STAGE_BYTES = G::kAStage;
+    constexpr int B_STAGE_BYTES = G::kBStage;  // (shadows the file-wide 256-K size)
     constexpr int SFA_STAGE_BYTES = G::kSfaStage;
     constexpr int SFB_STAGE_BYTES = G::kSfbStage;
     constexpr int TM = G::kTileM;
@@ -222,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     const int K = args.K;
-    constexpr int kElemsPerStage = KIND == KIND_NVFP4 ? 256 : 64;
+    constexpr int kElemsPerStage = (KIND == KIND_NVFP4 ? 256 : 64) * KS;
     constexpr int kMmaK = KIND == KIND_NVFP4 ? 64 : 16;
     const int k_tiles = (K + kElemsPerStage - 1) / kElemsPerStage;
     const int sf_atoms_per_rowblock = K / 64;
@@ -259,9 +231,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (args.early_claim) claim_first();
         // A is always a full 16 KB: tiles with at most 32 rows load their rows four
         // times, into rows 0-31, 32-63, 64-95 and 96-127 (see the epilogue)
+        // B's scale groups of the stage's K blocks that hold MMA steps (a last
+        // 512-K stage may cover one 256-K block only)
+        auto sfb_bytes = [&](int steps) { return static_cast<uint32_t>((steps + 3) / 4) * (SFB_STAGE_BYTES / KS); };
         auto stage_bytes = [&](int steps) {
             uint32_t bytes = A_STAGE_BYTES + B_STAGE_BYTES;
-            if (KIND == KIND_NVFP4) bytes += static_cast<uint32_t>(steps) * 512u + SFB_STAGE_BYTES;
+            if (KIND == KIND_NVFP4) bytes += static_cast<uint32_t>(steps) * 512u + sfb_bytes(steps);
             return bytes;
         };
         // The kernel may start while the one that writes A is still running
@@ -282,15 +257,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pre = min(STAGES, k01 - k00);
                 for (int j = 0; j < pre; ++j) {
                     const int kt = k00 + j;
-                    if (lane == 0)
-                        mbar_arrive_expect_tx(&full[j], stage_bytes(min(4, (K - kt * kElemsPerStage) / kMmaK)));
+                    const int steps_j = min(4 * KS, (K - kt * kElemsPerStage) / kMmaK);
+                    if (lane == 0) mbar_arrive_expect_tx(&full[j], stage_bytes(steps_j));
                     __syncwarp();
-                    const int blk = (e0 * args.b_nb + nb0) * args.b_kt + kt;
+                    const int blk = (e0 * args.b_nb + nb0) * args.b_kt + kt * KS;
                     if (lane == 1) {
-                        tma_load_2d_hint(sB + j * B_STAGE_BYTES, &tmb, &full[j], 0, blk * BN, stream_policy);
+                        if (KS == 2) tma_load_3d_hint(sB + j * B_STAGE_BYTES, &tmb, &full[j], 0, 0, blk, stream_policy);
+                        else tma_load_2d_hint(sB + j * B_STAGE_BYTES, &tmb, &full[j], 0, blk * BN, stream_policy);
                     } else if (KIND == KIND_NVFP4 && lane == 3) {
                         bulk_load_hint(sSFB + j * SFB_STAGE_BYTES,
-                                       args.sfb + static_cast<int64_t>(blk) * SFB_STAGE_BYTES, SFB_STAGE_BYTES,
+                                       args.sfb + static_cast<int64_t>(blk) * (SFB_STAGE_BYTES / KS), sfb_bytes(steps_j),
                                        &full[j], stream_policy);
                     }
                     issued[j] = true;
@@ -330,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             t.kt0 = __shfl_sync(0xffffffffu, t.kt0, 0);
             t.kt1 = __shfl_sync(0xffffffffu, t.kt1, 0);
             // tiles with at most 32 rows of the expert load only those rows of A (four times)
-            const bool small_a = MT == 1 && t.m_valid <= kSmallRows;
+            const bool small_a = MT == 1 && KS == 1 && t.m_valid <= kSmallRows;
             if (args.mt_wait > 0) {
                 // A (and its scales) are the gate/up GEMM's output for these rows:
                 // generic stores in other CTAs, ordered before these TMA reads by
@@ -344,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             for (int kt = t.kt0; kt < t.kt1; ++kt) {
                 const int k0 = kt * kElemsPerStage;
-                const int steps = min(4, (K - k0) / kMmaK);
+                const int steps = min(4 * KS, (K - k0) / kMmaK);
                 const bool b_issued = first_tile && kt - t.kt0 < pre;  // B of this stage went out before pdl_wait()
                 if (lane == 0 && !b_issued) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, cta_abort, dev_err)) {
@@ -357,9 +333,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
                 if (!ok) break;
                 // stage kt of tile (expert, n_block) is box `blk` of B and 4 KB group `blk` of its scales
-                const int blk = (t.expert * args.b_nb + t.n_block) * args.b_kt + kt;
+                // (with KS = 2: boxes and groups blk and blk + 1)
+                const int blk = (t.expert * args.b_nb + t.n_block) * args.b_kt + kt * KS;
                 const int xc = KIND == KIND_NVFP4 ? kt * 128 : k0;  // A's K coordinate (bytes or BF16 elements)
-                if (lane == 0) {
+                if (KS == 2 && lane == 0) {
+                    // A's 128 rows x two 256-K chunks: x 0, rows, chunk index
+                    tma_load_3d(sA + stage * A_STAGE_BYTES, &tma, &full[stage], 0, t.row0, kt * KS);
+                } else if (lane == 0) {
                     tma_load_2d(sA + stage * A_STAGE_BYTES, small_a ? &tma_small : &tma, &full[stage], xc, t.row0);
                 } else if (MT == 2 && lane == 4) {
                     // the tile's second 128 rows (zero-filled past the tensor)
@@ -368,13 +348,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tma_load_2d(sA + stage * A_STAGE_BYTES + (lane - 3) * kSmallRows * 128, &tma_small, &full[stage], xc,
                                 t.row0);
                 } else if (lane == 1 && !b_issued) {
-                    tma_load_2d_hint(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0, blk * BN, stream_policy);
+                    if (KS == 2) tma_load_3d_hint(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0, 0, blk, stream_policy);
+                    else tma_load_2d_hint(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0, blk * BN, stream_policy);
                 } else if (KIND == KIND_NVFP4 && lane == 2) {
-                    const int64_t a_atom = static_cast<int64_t>(t.row0 / 128) * sf_atoms_per_rowblock + kt * 4;
+                    const int64_t a_atom = static_cast<int64_t>(t.row0 / 128) * sf_atoms_per_rowblock + kt * 4 * KS;
                     bulk_load(sSFA + stage * SFA_STAGE_BYTES, args.sfa + a_atom * 512, steps * 512u, &full[stage]);
                 } else if (KIND == KIND_NVFP4 && lane == 3 && !b_issued) {
-                    bulk_load_hint(sSFB + stage * SFB_STAGE_BYTES, args.sfb + static_cast<int64_t>(blk) * SFB_STAGE_BYTES,
-                                   SFB_STAGE_BYTES, &full[stage], stream_policy);
+                    bulk_load_hint(sSFB + stage * SFB_STAGE_BYTES,
+                                   args.sfb + static_cast<int64_t>(blk) * (SFB_STAGE_BYTES / KS), sfb_bytes(steps),
+                                   &full[stage], stream_policy);
                 }
                 issued[stage] = true;
                 issued_parity[stage] = phase;
@@ -437,14 +419,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     tc_fence_after();
                     const int k0 = kt * kElemsPerStage;
-                    const int steps = min(4, (K - k0) / kMmaK);
+                    const int steps = min(4 * KS, (K - k0) / kMmaK);
                     const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
                     const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
-                    const uint32_t sfa_col = ACC_COLS + stage * SF_COLS;
-                    const uint32_t sfb_col = sfa_col + 16;
+                    const uint32_t sfa_col = ACC_COLS + stage * G::kSfCols;
+                    const uint32_t sfb_col = sfa_col + 16 * KS;
                     for (int s = 0; s < steps; ++s) {
-                        const uint64_t adesc = sdesc_sw128(a_base + 32 * s);
-                        const uint64_t bdesc = sdesc_sw128(b_base + 32 * s);
+                        // step s: 256-K block s / 4 of the stage (its own 16 KB of A and 32 KB of B)
+                        const int sb = KS == 2 ? (s >> 2) : 0, s4 = KS == 2 ? (s & 3) : s;
+                        const uint64_t adesc = sdesc_sw128(a_base + sb * (BM * 128) + 32 * s4);
+                        const uint64_t bdesc = sdesc_sw128(b_base + sb * (BN * 128) + 32 * s4);
                         const uint32_t acc = (kt > kt0 || s > 0) ? 1u : 0u;
                         if (KIND == KIND_NVFP4)
                             mma_nvfp4(tmem, adesc, bdesc, idesc, tmem + sfa_col + 4 * s, tmem + sfb_col + 8 * s, acc);
@@ -577,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // loaded four times), so for the NVFP4 epilogues all sixteen warps take a
             // share of its columns instead of quadrant 0's four: SwiGLU-quantise, one
             // 16-output group per warp (cs < 2); down, 16 columns per warp.
-            const bool rep = KIND == KIND_NVFP4 && t.m_valid <= kSmallRows;
+            const bool rep = KIND == KIND_NVFP4 && KS == 1 && t.m_valid <= kSmallRows;
             const int row = rep ? t.row0 + lane : t.row0 + r;
             const bool valid = rep ? lane < t.m_valid : r < t.m_valid;
             // some row of this warp belongs to the expert (and the warp has columns)
@@ -757,14 +741,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                const int steps = min(4, (K - kt * kElemsPerStage) / kMmaK);
-                const uint32_t sfa_col = ACC_COLS + stage * SF_COLS;
-                for (int c = sw; c < 12; c += kSfWarps) {
-                    const int s = c & 3, w = c >> 2;  // w 0: A, 1-2: B row halves
+                const int steps = min(4 * KS, (K - kt * kElemsPerStage) / kMmaK);
+                const uint32_t sfa_col = ACC_COLS + stage * G::kSfCols;
+                for (int c = sw; c < 12 * KS; c += kSfWarps) {
+                    // atoms 0 .. 4 KS - 1: A's, one per MMA step; then B's, two row halves per step
+                    const bool is_a = c < 4 * KS;
+                    const int s = is_a ? c : (c - 4 * KS) >> 1, w = is_a ? 0 : ((c - 4 * KS) & 1);
                     if (s >= steps) continue;
-                    const uint8_t* src = w == 0 ? sSFA + stage * SFA_STAGE_BYTES + s * 512
-                                                : sSFB + stage * SFB_STAGE_BYTES + (w - 1) * 2048 + s * 512;
-                    const uint32_t col = w == 0 ? sfa_col + 4 * s : sfa_col + 16 + 8 * s + 4 * (w - 1);
+                    const uint8_t* src = is_a ? sSFA + stage * SFA_STAGE_BYTES + s * 512
+                                              : sSFB + stage * SFB_STAGE_BYTES + (s >> 2) * 4096 + w * 2048 + (s & 3) * 512;
+                    const uint32_t col = is_a ? sfa_col + 4 * s : sfa_col + 16 * KS + 8 * s + 4 * w;
                     tmem_cp_sf(tmem + col, sdesc_sf_atom(smem_u32(src)));
                 }
                 tc_commit(&sf_ready[stage]);
@@ -827,15 +813,56 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner_
     return r == CUDA_SUCCESS;
 }
 
-bool make_tmap_blocked(CUtensorMap* map, const void* base, uint64_t bytes) {
+bool make_tmap_blocked(CUtensorMap* map, const void* base, uint64_t bytes, uint32_t box_rows) {
     PfnEncodeTiled fn = encode_fn();
-    if (!fn || bytes % (BN * 128) != 0) return false;
+    if (!fn || bytes % (BN * 128) != 0 || box_rows == 0 || box_rows > 256) return false;
     cuuint64_t dims[2] = {128, bytes / 128};
     cuuint64_t strides[1] = {128};
-    cuuint32_t box[2] = {128, BN};
+    cuuint32_t box[2] = {128, box_rows};
     cuuint32_t estr[2] = {1, 1};
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+bool make_tmap_a3(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows) {
+    PfnEncodeTiled fn = encode_fn();
+    if (!fn || row_bytes % 256 != 0) return false;
+    // [K / 256 chunks][rows][128 bytes]: x = byte in the chunk, y = row, z = chunk
+    cuuint64_t dims[3] = {128, rows, row_bytes / 128};
+    cuuint64_t strides[2] = {row_bytes, 128};
+    cuuint32_t box[3] = {128, BM, 2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+bool make_tmap_b3(CUtensorMap* map, const void* base, uint64_t bytes) {
+    PfnEncodeTiled fn = encode_fn();
+    if (!fn || bytes % (BN * 128) != 0) return false;
+    // box-order blocks [blocks][256 rows][128 bytes]; a box is two consecutive blocks
+    cuuint64_t dims[3] = {128, BN, bytes / (BN * 128)};
+    cuuint64_t strides[2] = {128, BN * 128};
+    cuuint32_t box[3] = {128, BN, 2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+bool make_tmap_runs(CUtensorMap* map, const void* base, uint64_t bytes, uint32_t box_rows) {
+    PfnEncodeTiled fn = encode_fn();
+    if (!fn || bytes % 256 != 0 || box_rows == 0 || box_rows > 256) return false;
+    cuuint64_t dims[2] = {256, bytes / 256};
+    cuuint64_t strides[1] = {256};
+    cuuint32_t box[2] = {256, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -846,29 +873,36 @@ int gemm_grid_size(int device) {
     return sms > 0 ? sms : 148;
 }
 
-template <int KIND, int EPI, int MT = 1>
+template <int KIND, int EPI, int MT = 1, int KS = 1>
 static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
                               const GemmArgs& args, int grid, bool dependent, cudaStream_t st) {
-    constexpr int SMEM_BYTES = Geo<KIND, MT>::kSmem;
+    constexpr int SMEM_BYTES = Geo<KIND, MT, KS>::kSmem;
     // the shared memory limit is an attribute of the kernel in each device's context
     static bool attr[kMaxDevices] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     if (!attr[dev]) {
         const cudaError_t e =
-            cudaFuncSetAttribute(gemm_kernel<KIND, EPI, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+            cudaFuncSetAttribute(gemm_kernel<KIND, EPI, MT, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
     if (dependent)
-        return launch_dependent(gemm_kernel<KIND, EPI, MT>, dim3(grid), dim3(kThreads), SMEM_BYTES, st, tma, tma_small, tmb,
-                                args);
-    gemm_kernel<KIND, EPI, MT><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, tmb, args);
+        return launch_dependent(gemm_kernel<KIND, EPI, MT, KS>, dim3(grid), dim3(kThreads), SMEM_BYTES, st, tma, tma_small,
+                                tmb, args);
+    gemm_kernel<KIND, EPI, MT, KS><<<grid, kThreads, SMEM_BYTES, st>>>(tma, tma_small, tmb, args);
     return cudaGetLastError();
 }
 
 cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
                         const GemmArgs& args, int grid, bool dependent, cudaStream_t st) {
+    if (args.kind == KIND_NVFP4 && args.wide_stages) {
+        // 512-K stages: tma / tmb are the 3-D maps (make_tmap_a3 / make_tmap_b3); grouped tiles only
+        if (args.dense_rows > 0) return cudaErrorInvalidValue;
+        if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT, 1, 2>(tma, tma_small, tmb, args, grid, dependent, st);
+        if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16, 1, 2>(tma, tma_small, tmb, args, grid, dependent, st);
+        return cudaErrorInvalidValue;
+    }
     if (args.kind == KIND_NVFP4) {
         if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT>(tma, tma_small, tmb, args, grid, dependent, st);
         if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16>(tma, tma_small, tmb, args, grid, dependent, st);

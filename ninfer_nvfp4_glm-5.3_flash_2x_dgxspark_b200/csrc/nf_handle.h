@@ -56,17 +56,11 @@ struct nf_moe {
     bool router_bound = false, bias_bound = false, sg_bound = false, su_bound = false, sd_bound = false;
     int router_w_safe = 0;  // every nonzero router weight has |w| in [2^-67, 2^63)
     // screened router for large batches (nf_kernels.cu route_screen_kernel):
-    // the router rows padded to 256 in box order for the tensor-core GEMM, the
-    // rows' 2-norms rounded up, the approximate-logit partials and the
-    // candidates of each token
+    // the router rows' 2-norms rounded up and the candidates of each token
     bool screen = false;
-    uint8_t* router_box = nullptr;
     float* router_wnorm = nullptr;
-    float* screen_part = nullptr;     // [kScreenSlices][Tm][256]
     int32_t* screen_cand = nullptr;   // [Tm][32]
     int32_t* screen_cnt = nullptr;    // [Tm]: candidates, -1 = every chain
-    int* screen_counter = nullptr;    // GEMM tile counter
-    CUtensorMap tm_router{};
     int last_screened = 0;            // the last forward's router was screened
 
     // workspace
@@ -128,6 +122,14 @@ struct nf_moe {
     CUtensorMap tm_a{}, tm_h{}, tm_shh{};
     CUtensorMap tm_a_s{}, tm_h_s{}, tm_shh_s{};  // 32-row boxes of the A operands
     CUtensorMap tm_b_gu{}, tm_b_dn{}, tm_bs_gu{}, tm_bs_dn{};  // B operands (routed, shared) in box order
+    // CTA-pair GEMMs (nf_gemm2.cu, NVFP4 experts at prefill-sized batches):
+    // B with 128-row boxes, the A operands' and B's scale atoms as runs
+    CUtensorMap tm_b_gu_half{}, tm_b_dn_half{}, tm_sfa_a{}, tm_sfa_h{}, tm_sfb_gu{}, tm_sfb_dn{};
+    int gemm_mode = 0;  // nf_moe_set_expert_gemm (NF_GEMM_*)
+    // 512-K-stage maps of the one-SM grouped NVFP4 GEMMs (prefill-sized batches)
+    CUtensorMap tm_a3{}, tm_h3{}, tm_b_gu3{}, tm_b_dn3{};
+    bool wide_ok = false;
+    int grid2 = 0;          // CTAs of the pair GEMMs (an even number; 0: not available)
     int last_tokens = 0;
 
     // graph mode (nf_moe_set_graph_mode): captured forwards by argument set

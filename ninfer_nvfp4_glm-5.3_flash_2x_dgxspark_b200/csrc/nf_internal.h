@@ -91,6 +91,12 @@ struct GemmArgs {
                                // instead of waiting for the whole previous kernel (pdl_wait)
     int early_claim;           // the tile list and counter come from two or more launches back: claim
                                // the first tile and issue its first B stages before pdl_wait()
+    int wide_stages;           // grouped NVFP4: 512-K stages; tma / tmb are make_tmap_a3 / make_tmap_b3 maps
+    // CTA-pair GEMM (nf_gemm2.cu): the permutation's segments, from which it
+    // derives its 256-row tiles
+    int num_experts;
+    const int32_t* seg_off;    // [E + 1] first permuted row of each expert (multiples of 128)
+    const int32_t* seg_cnt;    // [E] rows of each expert
 };
 
 // Launches `kernel` with programmatic stream serialization: it may begin
@@ -116,7 +122,15 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner_
                   uint32_t box_inner, uint32_t box_rows);
 // B in box order as a 2-D byte tensor [bytes / 128 rows, 128] with 256-row
 // boxes and 128-byte swizzle: box i is the 32 KB block i.
-bool make_tmap_blocked(CUtensorMap* map, const void* base, uint64_t bytes);
+bool make_tmap_blocked(CUtensorMap* map, const void* base, uint64_t bytes, uint32_t box_rows = 256);
+// 3-D maps for 512-K stages: A (FP4 rows of row_bytes) as [K / 256 chunks]
+// [rows][128 B] with 128-row x 2-chunk boxes; B in box order as [blocks]
+// [256 rows][128 B] with 2-block boxes.  128-byte swizzle.
+bool make_tmap_a3(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows);
+bool make_tmap_b3(CUtensorMap* map, const void* base, uint64_t bytes);
+// A byte tensor [bytes / 256 rows, 256] without swizzle and box_rows-row
+// boxes: contiguous runs of box_rows * 256 bytes (the scale-factor atoms).
+bool make_tmap_runs(CUtensorMap* map, const void* base, uint64_t bytes, uint32_t box_rows);
 // tma_small: the same A tensor with a 32-row box, used for tiles with <= 32
 // rows; tmb: B (make_tmap_blocked over args.b).  dependent: launch_dependent
 // (the kernel's CTAs may start, and hold their SMs, while the previous
@@ -124,6 +138,15 @@ bool make_tmap_blocked(CUtensorMap* map, const void* base, uint64_t bytes);
 cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
                         const GemmArgs& args, int grid, bool dependent, cudaStream_t st);
 int gemm_grid_size(int device);
+// The grouped NVFP4 GEMMs on CTA pairs (nf_gemm2.cu), for prefill-sized
+// batches: tma as for launch_gemm (128-row boxes); tmb_half: B in box order
+// with 128-row boxes; tm_sfa / tm_sfb: args.sfa / args.sfb as make_tmap_runs
+// with 8- and 16-row boxes.  Grouped tiles only (args.seg_off / seg_cnt),
+// K % 256 == 0, the SwiGLU-quantise and BF16-store epilogues.
+bool gemm2_supported(const GemmArgs& args);
+int gemm2_grid(int device);
+cudaError_t launch_gemm2(const CUtensorMap& tma, const CUtensorMap& tmb_half, const CUtensorMap& tm_sfa,
+                         const CUtensorMap& tm_sfb, const GemmArgs& args, int grid, bool dependent, cudaStream_t st);
 // Weight matrices the GEMMs stream are kept in "box order" (nf_moe.cu): 32 KB
 // blocks of 256 rows x 128 bytes, row-block major, K-block minor.
 int64_t box_order_bytes(int64_t rows, int64_t row_bytes);
@@ -255,14 +278,14 @@ cudaError_t launch_gqa_decode(const CUtensorMap& tmk, const CUtensorMap& tmv, co
 
 cudaError_t launch_fill_bf16_hash(uint16_t* p, int64_t n, uint64_t seed, cudaStream_t st);
 
-// Screened router (large batches): candidates per token, split-K slices of the
-// approximate-logit GEMM, and the batch size from which forwards use it.
+// Screened router (large batches): candidates per token and the batch size
+// from which forwards use it.  The screen takes the router rows as BF16
+// [E, H] with E % 16 == 0, E <= kRouterMaxE and H % kRouterKc == 0.
 constexpr int kScreenMaxCandHost = 32;
-constexpr int kScreenSlices = 4;
 constexpr int kScreenMinTokens = 1024;
-cudaError_t launch_route_screen(const float* part, int S, int64_t stride, int ld, const uint16_t* x, int T, int H,
-                                int E, int K, const float* bias, const float* wnorm, float c, int32_t* cand,
-                                int32_t* cnt, float* approx, cudaStream_t st);
+cudaError_t launch_route_screen(const uint16_t* x, int T, int H, const uint16_t* w, int E, int K, const float* bias,
+                                const float* wnorm, float c, int32_t* cand, int32_t* cnt, float* approx,
+                                cudaStream_t st);
 cudaError_t launch_route_exact(const uint16_t* x, const uint16_t* wz16, const float* bias, int T, int H, int E, int K,
                                float scaling, int normalize, int w_safe, const int32_t* cand, const int32_t* cnt,
                                int32_t* idx, float* wts, cudaStream_t st);

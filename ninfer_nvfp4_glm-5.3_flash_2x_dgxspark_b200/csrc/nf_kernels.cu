@@ -1823,236 +1823,464 @@ __device__ __forceinline__ bool bf16_screen_unsafe(uint32_t u) {
     return (nz0 && (e0 < 60u || e0 > 146u)) || (nz1 && (e1 < 60u || e1 > 146u));
 }
 
-__global__ void __launch_bounds__(256) route_screen_kernel(const float* __restrict__ part, int S, int64_t stride,
-                                                           int ld, const uint16_t* __restrict__ x, int T, int H,
-                                                           int E, int K, const float* __restrict__ bias,
-                                                           const float* __restrict__ wnorm, float c,
-                                                           int32_t* __restrict__ cand, int32_t* __restrict__ cnt,
-                                                           float* __restrict__ approx) {
-    const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (t >= T) return;
-    const int lane = threadIdx.x & 31;
-    // ||x_t||_2 in double (each square exact), and the range check
-    const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * H);
-    double ss = 0.0;
-    int bad = 0;
-    for (int i = lane; i < H / 8; i += 32) {
-        const uint4 v = __ldg(xr + i);
-        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            bad |= bf16_screen_unsafe(w4[j]) ? 1 : 0;
-            const double a = bf16_lo(w4[j]), b = bf16_hi(w4[j]);
-            ss += a * a + b * b;
+// The exact chains of the screened candidates, packed densely over the
+// threads (a chain's cost is H dependent steps whoever runs it, so a lane
+// must not idle on a token with few candidates).  A CTA takes kExTok tokens
+// and lists their (token, expert) chains in shared memory -- each candidate,
+// or every expert of a marked token -- and thread i runs chains i, i + 256,
+// i + 512, i + 768 of the list at once (further passes for longer lists),
+// each sequential over the columns: fused multiply-add when the weights
+// passed the bind-time range check and the token is in range (products
+// exact), else the separately rounded multiply and add.  The router rows
+// (the fused router's BF16 chunk-major copy, rows padded to kRouterPitch16)
+// and the tokens' BF16 columns stream through shared memory in 128-column
+// chunks, double buffered with cp.async; the padded pitches put the rows
+// that neighbouring lanes read in different banks.  Then one warp per token
+// applies the exact sigmoid and bias and the reference's selection with
+// every non-candidate's choice at -inf.
+constexpr int kExTok = 32;
+constexpr int kExThreads = 256;
+constexpr int kExWarps = kExThreads / 32;
+constexpr int kExSlots = 4;
+constexpr int kExXPitch = kRouterKc + 8;  // BF16 elements per staged token row
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// One 128-column chunk of a chain.  MODE 0: fused multiply-add; 1: the
+// separately rounded multiply and add; 2: per lane, by `fma`.
+template <int MODE>
+__device__ __forceinline__ float exact_chunk(const uint16_t* wr, const uint16_t* xr, float a, bool fma) {
+#pragma unroll 4
+    for (int k = 0; k < kRouterKc; k += 8) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(wr + k);
+        const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
+        if (MODE == 0 || (MODE == 2 && fma)) {
+            a = chain_step2<true>(wv.x, xv.x, a);
+            a = chain_step2<true>(wv.y, xv.y, a);
+            a = chain_step2<true>(wv.z, xv.z, a);
+            a = chain_step2<true>(wv.w, xv.w, a);
+        } else {
+            a = chain_step2<false>(wv.x, xv.x, a);
+            a = chain_step2<false>(wv.y, xv.y, a);
+            a = chain_step2<false>(wv.z, xv.z, a);
+            a = chain_step2<false>(wv.w, xv.w, a);
         }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
-    }
-    const float nx = __double2float_ru(sqrt(ss) * (1.0 + 1e-12));
-    const int jn = (E + 31) / 32;  // E <= 128
-    float lo[4], hi[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        lo[j] = -INFINITY;
-        hi[j] = -INFINITY;
-        const int e = lane + 32 * j;
-        if (j >= jn || e >= E) continue;
-        float l = 0.f;
-        for (int s = 0; s < S; ++s) l += part[s * stride + static_cast<int64_t>(t) * ld + e];
-        if (approx) approx[static_cast<int64_t>(t) * E + e] = l;  // (kept for inspection)
-        const float B = __fmul_ru(__fmul_ru(c, nx), wnorm[e]);
-        const float la = __fsub_rd(l, B), ha = __fadd_ru(l, B);
-        if (!isfinite(l) || !isfinite(la) || !isfinite(ha)) {
-            bad = 1;
-            continue;
-        }
-        lo[j] = __fadd_rn(sigmoid_ref(la), bias[e]);
-        hi[j] = __fadd_rn(sigmoid_ref(ha), bias[e]);
-    }
-    bad = __any_sync(0xffffffffu, bad) ? 1 : 0;
-    if (bad) {
-        if (lane == 0) cnt[t] = -1;
-        return;
-    }
-    // the k-th largest lower end: k rounds of a max over keys (order bits,
-    // expert index) with the winner removed
-    uint32_t removed = 0u;
-    float kth = -INFINITY;
-    for (int p = 0; p < K; ++p) {
-        uint64_t key = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int e = lane + 32 * j;
-            if (j >= jn || e >= E || ((removed >> j) & 1u)) continue;
-            const uint64_t k = (static_cast<uint64_t>(float_order_bits(lo[j])) << 32) | static_cast<uint32_t>(e);
-            key = k > key ? k : key;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const uint64_t ok = __shfl_xor_sync(0xffffffffu, key, o);
-            key = ok > key ? ok : key;
-        }
-        const int we = static_cast<int>(key & 0xffffffffu);
-        if ((we & 31) == lane) removed |= 1u << (we >> 5);
-        float v = lo[0];
-#pragma unroll
-        for (int j = 1; j < 4; ++j)
-            if ((we >> 5) == j) v = lo[j];
-        kth = __shfl_sync(0xffffffffu, v, we & 31);
-    }
-    int n = 0;
-    int32_t* out = cand + static_cast<int64_t>(t) * kScreenMaxCand;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int e = lane + 32 * j;
-        const bool is_cand = j < jn && e < E && hi[j] >= kth;
-        const uint32_t b = __ballot_sync(0xffffffffu, is_cand);
-        if (is_cand) {
-            const int slot = n + __popc(b & ((1u << lane) - 1u));
-            if (slot < kScreenMaxCand) out[slot] = e;
-        }
-        n += __popc(b);
-    }
-    if (lane == 0) cnt[t] = n <= kScreenMaxCand ? n : -1;
+    return a;
 }
 
-// The exact chains of the screened candidates, 32 tokens per CTA (one warp
-// each); the router rows stream through shared memory in 128-column chunks
-// of the fused router's BF16 chunk-major copy (rows padded to kRouterPitch16,
-// so the rows the lanes of a warp read fall in different banks), double
-// buffered with plain 16-byte loads; a warp's token chunk is widened into
-// its own 128-float slot.  Lane i runs the chains of candidates i and i + 32
-// (all E experts, lane + 32 j, for a marked token), sequentially over the
-// columns, fused multiply-add when the weights passed the bind-time range
-// check (products exact) and the token is in range, else the separately
-// rounded multiply and add.
-constexpr int kExactWarps = 32;
-constexpr int kExactTpb = kExactWarps * 32;
+// NS chains at once, each sequential over the chunk's columns (fused
+// multiply-add: every chain of the warp is in range): the chains are
+// independent, so their loads and steps interleave.
+template <int NS>
+__device__ __forceinline__ void exact_chunk_multi(const uint16_t* wb, const uint16_t* xb, const int (&wofs)[kExSlots],
+                                                  const int (&xofs)[kExSlots], float (&acc)[kExSlots]) {
+#pragma unroll 2
+    for (int k = 0; k < kRouterKc; k += 8) {
+        uint4 wv[NS], xv[NS];
+#pragma unroll
+        for (int s = 0; s < NS; ++s) {
+            wv[s] = *reinterpret_cast<const uint4*>(wb + wofs[s] + k);
+            xv[s] = *reinterpret_cast<const uint4*>(xb + xofs[s] + k);
+        }
+#pragma unroll
+        for (int s = 0; s < NS; ++s) {
+            float a = acc[s];
+            a = chain_step2<true>(wv[s].x, xv[s].x, a);
+            a = chain_step2<true>(wv[s].y, xv[s].y, a);
+            a = chain_step2<true>(wv[s].z, xv[s].z, a);
+            a = chain_step2<true>(wv[s].w, xv[s].w, a);
+            acc[s] = a;
+        }
+    }
+}
 
-__global__ void __launch_bounds__(kExactTpb, 1) route_exact_kernel(
+__global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ wz16, const float* __restrict__ bias, int T, int H,
     int E, int K, float scaling, int normalize, int w_safe, const int32_t* __restrict__ cand,
     const int32_t* __restrict__ cnt, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
     extern __shared__ __align__(16) uint8_t rx_smem[];
     const int wchunk = E * kRouterPitch16;  // BF16 elements of one chunk of every row
-    uint16_t* sw = reinterpret_cast<uint16_t*>(rx_smem);                       // [2][wchunk]
-    float* sx = reinterpret_cast<float*>(rx_smem + 2 * wchunk * 2);            // [kExactWarps][kRouterKc]
-    float* s_sc = sx + kExactWarps * kRouterKc;                                // [kExactWarps][E]
-    float* s_ch = s_sc + kExactWarps * E;                                      // [kExactWarps][E]
-    __shared__ uint32_t s_excl[kExactWarps][32];
+    uint16_t* sw = reinterpret_cast<uint16_t*>(rx_smem);                         // [2][wchunk]
+    uint16_t* sx = sw + 2 * wchunk;                                              // [2][kExTok][kExXPitch]
+    int32_t* s_chain = reinterpret_cast<int32_t*>(sx + 2 * kExTok * kExXPitch);  // [kExTok * E] token << 8 | expert
+    float* s_val = reinterpret_cast<float*>(s_chain + kExTok * E);               // [kExTok * E] exact logits
+    float* s_sc = s_val + kExTok * E;                                            // [kExWarps][E]
+    float* s_ch = s_sc + kExWarps * E;                                           // [kExWarps][E]
+    __shared__ int s_base[kExTok + 1];
+    __shared__ int s_marked[kExTok];
+    __shared__ int s_fma[kExTok];
+    __shared__ uint32_t s_excl[kExWarps][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * kExactWarps + warp;
-    const bool live = t < T;
-    const int n = live ? cnt[t] : 0;
-    const bool all = n < 0;
-    // this lane's experts: candidates lane and lane + 32, or every lane + 32 j
-    int ex[4];
+    const int t0 = blockIdx.x * kExTok;
+    const int ntok = min(kExTok, T - t0);
+
+    // the chain list: per-token counts, their prefix, then the entries
+    if (warp == 0) {
+        const int c = lane < ntok ? cnt[t0 + lane] : 0;
+        const int n = c < 0 ? E : c;
+        int incl = n;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        ex[j] = -1;
-        if (!live) continue;
-        if (all) {
-            if (lane + 32 * j < E) ex[j] = lane + 32 * j;
-        } else if (j < 2 && lane + 32 * j < n) {
-            ex[j] = cand[static_cast<int64_t>(t) * kScreenMaxCand + lane + 32 * j];
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
         }
+        if (lane < kExTok) {
+            s_base[lane] = incl - n;
+            s_marked[lane] = c < 0 ? 1 : 0;
+        }
+        if (lane == 31) s_base[kExTok] = incl;
     }
-    // products exact (fma equals the rounded multiply-add) unless a token value
-    // or a weight is out of range; a marked token may be out of range
-    int xbad = 0;
-    if (live && all)
-        for (int i = lane; i < H / 2; i += 32)
-            xbad |= bf16x2_unsafe(reinterpret_cast<const uint32_t*>(x + static_cast<int64_t>(t) * H)[i]) ? 1 : 0;
-    const bool fma_ok = w_safe && !__any_sync(0xffffffffu, xbad);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    __syncthreads();
+    for (int tl = warp; tl < ntok; tl += kExWarps) {
+        const int t = t0 + tl;
+        const int base = s_base[tl], n = s_base[tl + 1] - base;
+        const bool marked = s_marked[tl] != 0;
+        for (int j = lane; j < n; j += 32)
+            s_chain[base + j] = (tl << 8) | (marked ? j : cand[static_cast<int64_t>(t) * kScreenMaxCand + j]);
+        // a token the screen passed is in range; a marked one may not be
+        int xbad = 0;
+        if (marked)
+            for (int i = lane; i < H / 2; i += 32)
+                xbad |= bf16x2_unsafe(reinterpret_cast<const uint32_t*>(x + static_cast<int64_t>(t) * H)[i]) ? 1 : 0;
+        xbad = __any_sync(0xffffffffu, xbad);
+        if (lane == 0) s_fma[tl] = (w_safe && !xbad) ? 1 : 0;
+    }
+    __syncthreads();
+    const int total = s_base[kExTok];
     const int nchunks = H / kRouterKc;
-    auto load_w = [&](int c, int buf) {
-        const uint4* src = reinterpret_cast<const uint4*>(wz16 + static_cast<int64_t>(c) * wchunk);
-        uint4* dst = reinterpret_cast<uint4*>(sw + buf * wchunk);
-        for (int i = threadIdx.x; i < wchunk / 8; i += kExactTpb) dst[i] = __ldg(src + i);
+    auto stage = [&](int c, int buf) {
+        const uint4* ws = reinterpret_cast<const uint4*>(wz16 + static_cast<int64_t>(c) * wchunk);
+        uint4* wd = reinterpret_cast<uint4*>(sw + buf * wchunk);
+        for (int i = threadIdx.x; i < wchunk / 8; i += kExThreads) cp_async16(wd + i, ws + i);
+        uint16_t* xd = sx + buf * kExTok * kExXPitch;
+        for (int i = threadIdx.x; i < ntok * (kRouterKc / 8); i += kExThreads) {
+            const int tl = i / (kRouterKc / 8), q = i % (kRouterKc / 8);
+            cp_async16(xd + tl * kExXPitch + 8 * q, x + static_cast<int64_t>(t0 + tl) * H + c * kRouterKc + 8 * q);
+        }
+        cp_async_commit();
     };
-    load_w(0, 0);
-    for (int c = 0; c < nchunks; ++c) {
-        const int buf = c & 1;
-        // this warp's token chunk, widened
-        if (live) {
-            const uint2 v = __ldg(reinterpret_cast<const uint2*>(x + static_cast<int64_t>(t) * H + c * kRouterKc) + lane);
-            float* d = sx + warp * kRouterKc + 4 * lane;
-            d[0] = bf16_lo(v.x);
-            d[1] = bf16_hi(v.x);
-            d[2] = bf16_lo(v.y);
-            d[3] = bf16_hi(v.y);
-        }
-        __syncthreads();  // chunk c of the weights and the token chunks are in place
-        if (c + 1 < nchunks) load_w(c + 1, buf ^ 1);
-        const float* xs = sx + warp * kRouterKc;
+    for (int p0 = 0; p0 < total; p0 += kExThreads * kExSlots) {
+        int wofs[kExSlots], xofs[kExSlots];
+        bool fm[kExSlots];
+        float acc[kExSlots];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            if (ex[j] < 0) continue;
-            const uint16_t* wr = sw + buf * wchunk + ex[j] * kRouterPitch16;
-            float a = acc[j];
-            for (int k = 0; k < kRouterKc; k += 8) {
-                const uint4 wv = *reinterpret_cast<const uint4*>(wr + k);
-                const float4 xa = *reinterpret_cast<const float4*>(xs + k);
-                const float4 xb = *reinterpret_cast<const float4*>(xs + k + 4);
-                if (fma_ok) {
-                    a = fmaf(bf16_lo(wv.x), xa.x, a);
-                    a = fmaf(bf16_hi(wv.x), xa.y, a);
-                    a = fmaf(bf16_lo(wv.y), xa.z, a);
-                    a = fmaf(bf16_hi(wv.y), xa.w, a);
-                    a = fmaf(bf16_lo(wv.z), xb.x, a);
-                    a = fmaf(bf16_hi(wv.z), xb.y, a);
-                    a = fmaf(bf16_lo(wv.w), xb.z, a);
-                    a = fmaf(bf16_hi(wv.w), xb.w, a);
-                } else {
-                    a = __fadd_rn(a, __fmul_rn(bf16_lo(wv.x), xa.x));
-                    a = __fadd_rn(a, __fmul_rn(bf16_hi(wv.x), xa.y));
-                    a = __fadd_rn(a, __fmul_rn(bf16_lo(wv.y), xa.z));
-                    a = __fadd_rn(a, __fmul_rn(bf16_hi(wv.y), xa.w));
-                    a = __fadd_rn(a, __fmul_rn(bf16_lo(wv.z), xb.x));
-                    a = __fadd_rn(a, __fmul_rn(bf16_hi(wv.z), xb.y));
-                    a = __fadd_rn(a, __fmul_rn(bf16_lo(wv.w), xb.z));
-                    a = __fadd_rn(a, __fmul_rn(bf16_hi(wv.w), xb.w));
-                }
+        for (int j = 0; j < kExSlots; ++j) {
+            const int ci = p0 + j * kExThreads + threadIdx.x;
+            const int ch = ci < total ? s_chain[ci] : 0;  // a lane past the list runs token 0 / expert 0, unused
+            wofs[j] = (ch & 0xff) * kRouterPitch16;
+            xofs[j] = (ch >> 8) * kExXPitch;
+            fm[j] = ci < total ? s_fma[ch >> 8] != 0 : true;
+            acc[j] = 0.f;
+        }
+        // this warp's live slots, and whether all their chains take the fused form
+        int ns = 0;
+        bool all_fma = true;
+#pragma unroll
+        for (int j = 0; j < kExSlots; ++j) {
+            if (p0 + j * kExThreads + warp * 32 < total) {
+                ns = j + 1;
+                all_fma = all_fma && __all_sync(0xffffffffu, fm[j]);
             }
-            acc[j] = a;
         }
-        __syncthreads();  // every warp is done with chunk c before its buffer is refilled
-    }
-    if (!live) return;
-    float* sc = s_sc + warp * E;
-    float* ch = s_ch + warp * E;
-    for (int e = lane; e < E; e += 32) {
-        sc[e] = 0.f;
-        ch[e] = -INFINITY;  // not a candidate: below k exact choices
-    }
-    __syncwarp();
+        stage(0, 0);
+        for (int c = 0; c < nchunks; ++c) {
+            const int buf = c & 1;
+            cp_async_wait_all();
+            __syncthreads();  // chunk c is in place; every thread is done with chunk c - 1
+            if (c + 1 < nchunks) stage(c + 1, buf ^ 1);
+            const uint16_t* wb = sw + buf * wchunk;
+            const uint16_t* xb = sx + buf * kExTok * kExXPitch;
+            if (all_fma) {
+                switch (ns) {
+                    case 1: exact_chunk_multi<1>(wb, xb, wofs, xofs, acc); break;
+                    case 2: exact_chunk_multi<2>(wb, xb, wofs, xofs, acc); break;
+                    case 3: exact_chunk_multi<3>(wb, xb, wofs, xofs, acc); break;
+                    case 4: exact_chunk_multi<4>(wb, xb, wofs, xofs, acc); break;
+                    default: break;
+                }
+                continue;
+            }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        if (ex[j] < 0) continue;
-        const float s = sigmoid_ref(acc[j]);
-        sc[ex[j]] = s;
-        ch[ex[j]] = __fadd_rn(s, bias[ex[j]]);
+            for (int j = 0; j < kExSlots; ++j) {
+                if (p0 + j * kExThreads + warp * 32 >= total) break;  // (warp-uniform) no chain in this slot
+                const bool all_f = __all_sync(0xffffffffu, fm[j]);
+                const bool none_f = __all_sync(0xffffffffu, !fm[j]);
+                if (all_f)
+                    acc[j] = exact_chunk<0>(wb + wofs[j], xb + xofs[j], acc[j], true);
+                else if (none_f)
+                    acc[j] = exact_chunk<1>(wb + wofs[j], xb + xofs[j], acc[j], false);
+                else
+                    acc[j] = exact_chunk<2>(wb + wofs[j], xb + xofs[j], acc[j], fm[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kExSlots; ++j) {
+            const int ci = p0 + j * kExThreads + threadIdx.x;
+            if (ci < total) s_val[ci] = acc[j];
+        }
+        __syncthreads();  // the buffers are restaged by the next pass; s_val complete
     }
-    __syncwarp();
-    warp_select(sc, ch, E, K, scaling, normalize, 1, 1, s_excl[warp], idx_out + static_cast<int64_t>(t) * K,
-                w_out + static_cast<int64_t>(t) * K);
+
+    // selection, one warp per token
+    float* sc = s_sc + warp * E;
+    float* chv = s_ch + warp * E;
+    for (int tl = warp; tl < ntok; tl += kExWarps) {
+        const int t = t0 + tl;
+        for (int e = lane; e < E; e += 32) {
+            sc[e] = 0.f;
+            chv[e] = -INFINITY;  // not a candidate: below k exact choices
+        }
+        __syncwarp();
+        const int base = s_base[tl], n = s_base[tl + 1] - base;
+        for (int j = lane; j < n; j += 32) {
+            const int e = s_chain[base + j] & 0xff;
+            const float s = sigmoid_ref(s_val[base + j]);
+            sc[e] = s;
+            chv[e] = __fadd_rn(s, bias[e]);
+        }
+        __syncwarp();
+        warp_select(sc, chv, E, K, scaling, normalize, 1, 1, s_excl[warp], idx_out + static_cast<int64_t>(t) * K,
+                    w_out + static_cast<int64_t>(t) * K);
+        __syncwarp();
+    }
 }
 
 size_t route_exact_smem(int E) {
-    return static_cast<size_t>(2) * E * kRouterPitch16 * 2 + static_cast<size_t>(kExactWarps) * kRouterKc * 4 +
-           static_cast<size_t>(2) * kExactWarps * E * 4;
+    return static_cast<size_t>(2) * E * kRouterPitch16 * 2 + static_cast<size_t>(2) * kExTok * kExXPitch * 2 +
+           static_cast<size_t>(2) * kExTok * E * 4 + static_cast<size_t>(2) * kExWarps * E * 4;
 }
 
-cudaError_t launch_route_screen(const float* part, int S, int64_t stride, int ld, const uint16_t* x, int T, int H,
-                                int E, int K, const float* bias, const float* wnorm, float c, int32_t* cand,
-                                int32_t* cnt, float* approx, cudaStream_t st) {
+// Fused screen: 32 tokens per CTA, 4 warps.  The token rows and the router
+// rows ([E, H] BF16) stream through shared memory in 128-column chunks
+// (three cp.async stages, rows padded to 272 bytes so that ldmatrix is
+// conflict-free); warp w multiplies tokens 16 (w & 1) .. + 16 by experts
+// (w >> 1) E / 2 .. + E / 2 with mma.sync m16n8k16 (BF16 in, fp32
+// accumulate).  Meanwhile four threads per token sum the token's squares
+// (fused multiply-adds rounded upward, so the sum bounds the exact one from
+// above) and check its range.  Then four threads per token bound the logits
+// and list the candidates, a quarter of the experts each.
+constexpr int kScTok = 32;
+constexpr int kScThreads = 128;
+constexpr int kScStages = 3;
+constexpr int kScPitch = kRouterKc + 8;  // BF16 elements per staged row (272 bytes)
+constexpr int kScMaxK = 8;
+
+// The interval ends use a float sigmoid: expf is within 2 ulp of e^x (CUDA's
+// documented bound) and the divisions are correctly rounded, so
+// |sig_screen(x) - sigma(x)| <= 2^-21; sigmoid_ref, the reference's float
+// evaluation, is within 2^-22 of sigma.  Widening by kSigMargin = 2^-19 and
+// adding the bias with outward rounding therefore keeps
+// [lo, hi] around fadd_rn(sigmoid_ref(l), bias) for every l in [la, ha]
+// (sigmoid_ref and round-to-nearest are non-decreasing).
+__device__ __forceinline__ float sig_screen(float x) {
+    const float z = expf(-fabsf(x));
+    const float d = __fadd_rn(1.f, z);
+    return x >= 0.f ? __fdiv_rn(1.f, d) : __fdiv_rn(z, d);
+}
+constexpr float kSigMargin = 1.9073486328125e-06f;  // 2^-19
+
+__global__ void __launch_bounds__(kScThreads) route_screen_kernel(const uint16_t* __restrict__ x, int T, int H,
+                                                                  const uint16_t* __restrict__ w, int E, int K,
+                                                                  const float* __restrict__ bias,
+                                                                  const float* __restrict__ wnorm, float c,
+                                                                  int32_t* __restrict__ cand,
+                                                                  int32_t* __restrict__ cnt,
+                                                                  float* __restrict__ approx) {
+    extern __shared__ __align__(16) uint8_t sc_smem[];
+    uint16_t* sx = reinterpret_cast<uint16_t*>(sc_smem);                // [stages][kScTok][kScPitch]
+    uint16_t* sw = sx + kScStages * kScTok * kScPitch;                  // [stages][E][kScPitch]
+    float* slog = reinterpret_cast<float*>(sw + kScStages * E * kScPitch);  // [kScTok][E + 1]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.x * kScTok;
+    const int ntok = min(kScTok, T - t0);
+    const int nchunks = H / kRouterKc;
+    auto stage = [&](int ch, int buf) {
+        uint16_t* xd = sx + buf * kScTok * kScPitch;
+        for (int i = threadIdx.x; i < ntok * (kRouterKc / 8); i += kScThreads) {
+            const int r = i / (kRouterKc / 8), q = i % (kRouterKc / 8);
+            cp_async16(xd + r * kScPitch + 8 * q, x + static_cast<int64_t>(t0 + r) * H + ch * kRouterKc + 8 * q);
+        }
+        uint16_t* wd = sw + buf * E * kScPitch;
+        for (int i = threadIdx.x; i < E * (kRouterKc / 8); i += kScThreads) {
+            const int r = i / (kRouterKc / 8), q = i % (kRouterKc / 8);
+            cp_async16(wd + r * kScPitch + 8 * q, w + static_cast<int64_t>(r) * H + ch * kRouterKc + 8 * q);
+        }
+        cp_async_commit();
+    };
+    // warp tile: 16 tokens x E / 2 experts (nt n-tiles of 8)
+    const int tok0 = 16 * (warp & 1);
+    const int ex0 = (warp >> 1) * (E / 2);
+    const int nt = E / 16;  // n-tiles per warp (E % 16 == 0, E <= 128)
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    // thread -> token tid / 4 and quarter tid % 4 (norm: columns 32 q .. + 32 of each chunk)
+    const int tl = threadIdx.x >> 2, tq = threadIdx.x & 3;
+    float ss0 = 0.f, ss1 = 0.f;
+    int bad = 0;
+    stage(0, 0);
+    if (nchunks > 1) stage(1, 1);
+    for (int ch = 0; ch < nchunks; ++ch) {
+        const int buf = ch % kScStages;
+        if (ch + 1 < nchunks) asm volatile("cp.async.wait_group 1;" ::: "memory");
+        else cp_async_wait_all();
+        __syncthreads();  // chunk ch is in place; every thread is done with chunk ch - 1
+        if (ch + 2 < nchunks) stage(ch + 2, (ch + 2) % kScStages);
+        const uint16_t* xb = sx + buf * kScTok * kScPitch;
+        const uint16_t* wb = sw + buf * E * kScPitch;
+        if (tl < ntok) {
+            const uint4* xr = reinterpret_cast<const uint4*>(xb + tl * kScPitch + 32 * tq);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint4 v = xr[i];
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    bad |= bf16_screen_unsafe(w4[j]) ? 1 : 0;
+                    const float a = bf16_lo(w4[j]), b = bf16_hi(w4[j]);
+                    ss0 = __fmaf_ru(a, a, ss0);
+                    ss1 = __fmaf_ru(b, b, ss1);
+                }
+            }
+        }
+        const uint32_t a_addr = smem_u32(xb + (tok0 + (lane & 15)) * kScPitch + 8 * (lane >> 4));
+        const uint32_t b_addr =
+            smem_u32(wb + (ex0 + (lane & 7) + 8 * (lane >> 4)) * kScPitch + 8 * ((lane >> 3) & 1));
+#pragma unroll
+        for (int s = 0; s < kRouterKc / 16; ++s) {
+            uint32_t a[4];
+            ldsm_x4(a_addr + 32 * s, a);
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                if (2 * p >= nt) break;
+                uint32_t b[4];
+                ldsm_x4(b_addr + 16 * p * kScPitch * 2 + 32 * s, b);
+                mma_16816(acc[2 * p], a[0], a[1], a[2], a[3], b[0], b[1]);
+                mma_16816(acc[2 * p + 1], a[0], a[1], a[2], a[3], b[2], b[3]);
+            }
+        }
+    }
+    // logits to shared memory (row g and g + 8 of the warp's tile, columns 2 (lane % 4) + {0, 1})
+    const int g = lane >> 2, q2 = 2 * (lane & 3);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if (i >= nt) break;
+        float* r0 = slog + (tok0 + g) * (E + 1) + ex0 + 8 * i + q2;
+        float* r1 = r0 + 8 * (E + 1);
+        r0[0] = acc[i][0];
+        r0[1] = acc[i][1];
+        r1[0] = acc[i][2];
+        r1[1] = acc[i][3];
+    }
+    // ||x_t||_2 over the four threads of a token, rounded up at every step
+    float ss = __fadd_ru(ss0, ss1);
+    ss = __fadd_ru(ss, __shfl_xor_sync(0xffffffffu, ss, 1));
+    ss = __fadd_ru(ss, __shfl_xor_sync(0xffffffffu, ss, 2));
+    bad |= __shfl_xor_sync(0xffffffffu, bad, 1);
+    bad |= __shfl_xor_sync(0xffffffffu, bad, 2);
+    const float nx = __fsqrt_ru(ss);
+    __syncthreads();
+    // Choice intervals of this thread's quarter of the experts; the K largest
+    // lower ends (with multiplicity) by insertion, merged over the token's four
+    // threads; the upper ends overwrite the logits in shared memory.
+    const int t = t0 + tl;
+    const bool live = tl < ntok;
+    float* lrow = slog + tl * (E + 1);
+    const int per = E / 4;
+    const float cn = __fmul_ru(c, nx);
+    float top[kScMaxK];
+#pragma unroll
+    for (int i = 0; i < kScMaxK; ++i) top[i] = -INFINITY;
+    for (int j = 0; j < per; ++j) {
+        const int e = tq * per + j;
+        const float l = lrow[e];
+        if (live && approx) approx[static_cast<int64_t>(t) * E + e] = l;  // (kept for inspection)
+        const float B = __fmul_ru(cn, wnorm[e]);
+        const float la = __fsub_rd(l, B), ha = __fadd_ru(l, B);
+        if (!isfinite(l) || !isfinite(la) || !isfinite(ha)) {
+            bad = 1;
+            continue;
+        }
+        float v = __fadd_rd(__fsub_rd(sig_screen(la), kSigMargin), bias[e]);
+        lrow[e] = __fadd_ru(__fadd_ru(sig_screen(ha), kSigMargin), bias[e]);
+#pragma unroll
+        for (int i = 0; i < kScMaxK; ++i) {
+            if (i >= K) break;
+            const float a = top[i];
+            const bool gt = v > a;
+            top[i] = gt ? v : a;
+            v = gt ? a : v;
+        }
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        float other[kScMaxK];
+#pragma unroll
+        for (int i = 0; i < kScMaxK; ++i) other[i] = __shfl_xor_sync(0xffffffffu, top[i], o);
+#pragma unroll
+        for (int m = 0; m < kScMaxK; ++m) {
+            if (m >= K) break;
+            float v = other[m];
+#pragma unroll
+            for (int i = 0; i < kScMaxK; ++i) {
+                if (i >= K) break;
+                const float a = top[i];
+                const bool gt = v > a;
+                top[i] = gt ? v : a;
+                v = gt ? a : v;
+            }
+        }
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    float kth = top[0];
+#pragma unroll
+    for (int i = 1; i < kScMaxK; ++i)
+        if (i < K) kth = top[i];
+    // candidates: the experts whose upper end reaches the k-th largest lower end
+    int n = 0;
+    if (!bad)
+        for (int j = 0; j < per; ++j) n += lrow[tq * per + j] >= kth ? 1 : 0;
+    const int base_lane = lane & ~3;
+    int before = 0, total = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int nq = __shfl_sync(0xffffffffu, n, base_lane + q);
+        before += q < tq ? nq : 0;
+        total += nq;
+    }
+    if (!live) return;
+    if (bad) {
+        if (tq == 0) cnt[t] = -1;
+        return;
+    }
+    int32_t* out = cand + static_cast<int64_t>(t) * kScreenMaxCand;
+    int slot = before;
+    for (int j = 0; j < per && slot < kScreenMaxCand; ++j) {
+        const int e = tq * per + j;
+        if (lrow[e] >= kth) out[slot++] = e;
+    }
+    if (tq == 0) cnt[t] = total <= kScreenMaxCand ? total : -1;
+}
+
+size_t route_screen_smem(int E) {
+    return static_cast<size_t>(kScStages) * (kScTok + E) * kScPitch * 2 + static_cast<size_t>(kScTok) * (E + 1) * 4;
+}
+
+cudaError_t launch_route_screen(const uint16_t* x, int T, int H, const uint16_t* w, int E, int K, const float* bias,
+                                const float* wnorm, float c, int32_t* cand, int32_t* cnt, float* approx,
+                                cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    route_screen_kernel<<<(T + 7) / 8, 256, 0, st>>>(part, S, stride, ld, x, T, H, E, K, bias, wnorm, c, cand, cnt,
-                                                     approx);
+    if (E % 16 != 0 || E > kRouterMaxE || H % kRouterKc != 0 || K < 1 || K > kScMaxK) return cudaErrorInvalidValue;
+    static bool attr[kMaxDevices] = {};
+    cudaError_t e = smem_attr_once(route_screen_kernel, static_cast<int>(route_screen_smem(kRouterMaxE)), attr);
+    if (e != cudaSuccess) return e;
+    route_screen_kernel<<<(T + kScTok - 1) / kScTok, kScThreads, route_screen_smem(E), st>>>(x, T, H, w, E, K, bias,
+                                                                                        wnorm, c, cand, cnt, approx);
     return cudaGetLastError();
 }
 
@@ -2064,7 +2292,7 @@ cudaError_t launch_route_exact(const uint16_t* x, const uint16_t* wz16, const fl
     static bool attr[kMaxDevices] = {};
     cudaError_t e = smem_attr_once(route_exact_kernel, static_cast<int>(route_exact_smem(kRouterMaxE)), attr);
     if (e != cudaSuccess) return e;
-    route_exact_kernel<<<(T + kExactWarps - 1) / kExactWarps, kExactTpb, smem, st>>>(
+    route_exact_kernel<<<(T + kExTok - 1) / kExTok, kExThreads, smem, st>>>(
         x, wz16, bias, T, H, E, K, scaling, normalize, w_safe, cand, cnt, idx, wts);
     return cudaGetLastError();
 }

@@ -332,12 +332,10 @@ int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::s
                  h->alloc(&h->router_wz16, router_chunked_elems16(E, H));
         ok = ok && h->alloc(&h->logits, Tm * E) && h->alloc(&h->scores, Tm * E) && h->alloc(&h->choices, Tm * E);
         // the screened router, for handles that take prefill-sized batches
-        h->screen = E <= kRouterMaxE && H % kRouterKc == 0 && Tm >= kScreenMinTokens;
+        h->screen = E <= kRouterMaxE && E % 16 == 0 && H % kRouterKc == 0 && Tm >= kScreenMinTokens;
         if (h->screen)
-            ok = ok && h->alloc(&h->router_box, blocked_bytes(256, 2 * H)) && h->alloc(&h->router_wnorm, E) &&
-                 h->alloc(&h->screen_part, static_cast<int64_t>(kScreenSlices) * Tm * 256) &&
-                 h->alloc(&h->screen_cand, Tm * kScreenMaxCandHost) && h->alloc(&h->screen_cnt, Tm) &&
-                 h->alloc(&h->screen_counter, 1);
+            ok = ok && h->alloc(&h->router_wnorm, E) && h->alloc(&h->screen_cand, Tm * kScreenMaxCandHost) &&
+                 h->alloc(&h->screen_cnt, Tm);
     }
     if (routed) {
         if (fp4) {
@@ -543,10 +541,6 @@ int nf_moe_bind_bf16(nf_moe* h, int which, int expert, const uint16_t* data, int
                 }
             }
             if (e == cudaSuccess && h->screen) {
-                // the screen's GEMM operand: rows padded with zeros to one 256-row block
-                std::vector<uint16_t> pad(static_cast<size_t>(256) * cols, 0);
-                std::memcpy(pad.data(), data, static_cast<size_t>(rows) * rb);
-                e = upload_blocked(h->router_box, reinterpret_cast<const uint8_t*>(pad.data()), 256, static_cast<int64_t>(rb));
                 // each row's 2-norm, rounded up (a bound on sum |w x| with ||x||_2)
                 std::vector<float> nrm(static_cast<size_t>(rows));
                 for (int64_t r = 0; r < rows; ++r) {
@@ -684,6 +678,26 @@ int nf_moe_finalize(nf_moe* h) {
         ok = ok && make_tmap_2d(&h->tm_a_s, h->pb.a_codes, false, H / 2, R, 128, 32);
         ok = ok && make_tmap_2d(&h->tm_h_s, h->h_codes, false, I / 2, R, 128, 32);
         ok = ok && make_tmap_2d(&h->tm_h, h->h_codes, false, I / 2, R, 128, 128);
+        // 512-K-stage maps (without them the handle keeps 256-K stages)
+        h->wide_ok = H % 512 == 0 && I % 256 == 0 && make_tmap_a3(&h->tm_a3, h->pb.a_codes, H / 2, R) &&
+                     make_tmap_a3(&h->tm_h3, h->h_codes, I / 2, R) &&
+                     make_tmap_b3(&h->tm_b_gu3, h->w_gu, h->bytes_of(h->w_gu)) &&
+                     make_tmap_b3(&h->tm_b_dn3, h->w_dn, h->bytes_of(h->w_dn));
+        // the CTA-pair GEMMs' maps (without them the handle keeps the one-SM kernels)
+        bool pair_ok = make_tmap_blocked(&h->tm_b_gu_half, h->w_gu, h->bytes_of(h->w_gu), 128) &&
+                       make_tmap_blocked(&h->tm_b_dn_half, h->w_dn, h->bytes_of(h->w_dn), 128);
+        pair_ok = pair_ok && make_tmap_runs(&h->tm_sfa_a, h->pb.a_sf, h->bytes_of(h->pb.a_sf), 8) &&
+                  make_tmap_runs(&h->tm_sfa_h, h->h_sf, h->bytes_of(h->h_sf), 8);
+        pair_ok = pair_ok && make_tmap_runs(&h->tm_sfb_gu, h->w_gu_sf, h->bytes_of(h->w_gu_sf), 16) &&
+                  make_tmap_runs(&h->tm_sfb_dn, h->w_dn_sf, h->bytes_of(h->w_dn_sf), 16);
+        h->grid2 = 0;
+        if (ok && pair_ok) {
+            int prev_dev = 0;
+            cudaGetDevice(&prev_dev);
+            cudaSetDevice(h->device);
+            h->grid2 = gemm2_grid(h->device);
+            cudaSetDevice(prev_dev);
+        }
     } else {
         ok = ok && make_tmap_blocked(&h->tm_b_gu, h->wb_gu, h->bytes_of(h->wb_gu)) &&
              make_tmap_blocked(&h->tm_b_dn, h->wb_dn, h->bytes_of(h->wb_dn));
@@ -698,7 +712,6 @@ int nf_moe_finalize(nf_moe* h) {
         ok = ok && make_tmap_2d(&h->tm_shh, h->sh_h, true, Is, Tm, 64, 128);
         ok = ok && make_tmap_2d(&h->tm_shh_s, h->sh_h, true, Is, Tm, 64, 32);
     }
-    if (h->screen) ok = ok && make_tmap_blocked(&h->tm_router, h->router_box, h->bytes_of(h->router_box));
     if (!ok) return h->fail(NF_ERR_CUDA, "cuTensorMapEncodeTiled failed");
     h->finalized = true;
     return NF_OK;
@@ -842,7 +855,19 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.mt_done = h->pb.mt_done;
     g.mt_signal = handoff ? 1 : 0;
     g.early_claim = one_kernel ? 0 : 1;  // the tile list is written by the kernel right before
-    e = launch_gemm(h->tm_a, h->tm_a_s, h->tm_b_gu, g, h->grid, true, s);
+    // Prefill-sized batches (on average a pair tile's 256 rows per expert or
+    // more) may take the alternative GEMM forms (nf_moe_set_expert_gemm)
+    g.num_experts = E;
+    g.seg_off = h->pb.seg_off;
+    g.seg_cnt = h->pb.counts;
+    const bool prefill = static_cast<int64_t>(T) * K >= 256LL * E && down_split <= 1;
+    const bool pair = fp4 && h->gemm_mode == NF_GEMM_CTA_PAIR && h->grid2 >= 2 && prefill && H % 256 == 0 &&
+                      I % 256 == 0 && E <= 256;
+    const bool wide = fp4 && h->gemm_mode == NF_GEMM_WIDE_STAGES && prefill && h->wide_ok;
+    g.wide_stages = wide ? 1 : 0;
+    e = pair ? launch_gemm2(h->tm_a, h->tm_b_gu_half, h->tm_sfa_a, h->tm_sfb_gu, g, h->grid2, true, s)
+        : wide ? launch_gemm(h->tm_a3, h->tm_a3, h->tm_b_gu3, g, h->grid, true, s)
+               : launch_gemm(h->tm_a, h->tm_a_s, h->tm_b_gu, g, h->grid, true, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "gate/up GEMM launch");
     rec.end(NF_STAGE_GATE_UP, s);
     rec.begin(NF_STAGE_DOWN, s);
@@ -882,7 +907,9 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
         g.out_ld = H;
         g.out_split_stride = stride;
     }
-    e = launch_gemm(h->tm_h, h->tm_h_s, h->tm_b_dn, g, h->grid, true, s);
+    e = pair ? launch_gemm2(h->tm_h, h->tm_b_dn_half, h->tm_sfa_h, h->tm_sfb_dn, g, h->grid2, true, s)
+        : wide ? launch_gemm(h->tm_h3, h->tm_h3, h->tm_b_dn3, g, h->grid, true, s)
+               : launch_gemm(h->tm_h, h->tm_h_s, h->tm_b_dn, g, h->grid, true, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "down GEMM launch");
     rec.end(NF_STAGE_DOWN, s);
     return NF_OK;
@@ -915,47 +942,19 @@ cudaError_t route_tokens(nf_moe* h, const uint16_t* x, int T, int32_t* idx, floa
     const int H = d.hidden, E = d.experts, K = d.top_k;
     const bool grouped = d.n_group > 1 && d.topk_group < d.n_group;
     h->last_screened = 0;
-    if (!h->screen || T < kScreenMinTokens || grouped || T > d.max_tokens)
+    if (!h->screen || T < kScreenMinTokens || grouped || T > d.max_tokens || K > 8)
         return launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, T, H, E, K,
                              d.routed_scaling, d.normalize, d.n_group, d.topk_group, h->router_w_safe, h->logits,
                              h->scores, h->choices, idx, w, h->dev_err, s);
     h->last_screened = 1;
-    // 1. approximate logits [T, 256] on the tensor cores (split K so that the one
-    //    256-wide output block still spreads over the SMs)
-    CUtensorMap tm_x, tm_x_s;
-    if (!make_tmap_2d(&tm_x, x, true, H, T, 64, 128) || !make_tmap_2d(&tm_x_s, x, true, H, T, 64, 32))
-        return cudaErrorInvalidValue;
-    const int m_tiles = (T + 127) / 128, k_tiles = (H + 63) / 64;
-    const int want = std::max(1, std::min(kScreenSlices, (h->grid + m_tiles - 1) / m_tiles));
-    const int kt_per = std::max(2, (k_tiles + want - 1) / want);
-    const int S = (k_tiles + kt_per - 1) / kt_per;
-    cudaError_t e = cudaMemsetAsync(h->screen_counter, 0, sizeof(int), s);
-    if (e != cudaSuccess) return e;
-    GemmArgs g{};
-    g.err = h->dev_err;
-    g.kind = KIND_BF16;
-    g.epi = EPI_STORE_F32;
-    g.K = H;
-    g.dense_rows = T;
-    g.n_blocks = 1;
-    g.b_nb = 1;
-    g.b = h->router_box;
-    g.b_kt = static_cast<int>(k_blocks(2 * static_cast<int64_t>(H)));
-    g.k_split = S;
-    g.kt_per = kt_per;
-    g.out = h->screen_part;
-    g.out_ld = 256;
-    g.out_split_stride = static_cast<int64_t>(T) * 256;
-    g.tile_counter = h->screen_counter;
-    g.early_claim = 1;
-    e = launch_gemm(tm_x, tm_x_s, h->tm_router, g, std::min(h->grid, m_tiles * S), false, s);
-    if (e != cudaSuccess) return e;
-    // 2. bound and candidates: |l~ - l| <= (gamma_H + H 2^-20 + S 2^-24) ||x||_2 ||w_e||_2, with the
-    //    tensor core's accumulation taken as 16 units of fp32 roundoff per step
+    // 1-2. approximate logits on the tensor cores, the bound
+    //      |l~ - l| <= (gamma_H + H 2^-22 + 2^-24) ||x||_2 ||w_e||_2 (the tensor
+    //      core's accumulation taken as 4 units of fp32 roundoff per product),
+    //      and the candidates
     const double u = std::ldexp(1.0, -24);
-    const double c = (H * u / (1.0 - H * u) + H * std::ldexp(1.0, -20) + (S + 1) * u) * 1.01;
-    e = launch_route_screen(h->screen_part, S, static_cast<int64_t>(T) * 256, 256, x, T, H, E, K, h->router_bias,
-                            h->router_wnorm, static_cast<float>(c), h->screen_cand, h->screen_cnt, h->logits, s);
+    const double c = (H * u / (1.0 - H * u) + H * std::ldexp(1.0, -22) + u) * 1.01;
+    cudaError_t e = launch_route_screen(x, T, H, h->router_w, E, K, h->router_bias, h->router_wnorm,
+                                        static_cast<float>(c), h->screen_cand, h->screen_cnt, h->logits, s);
     if (e != cudaSuccess) return e;
     // 3. the exact chains of the candidates and the reference's selection
     return launch_route_exact(x, h->router_wz16, h->router_bias, T, H, E, K, d.routed_scaling, d.normalize,
@@ -1089,6 +1088,22 @@ int nf_moe_forward(nf_moe* h, const uint16_t* x, const float* residual, int toke
 int nf_moe_set_graph_mode(nf_moe* h, int enable) {
     if (!h) return NF_ERR_INVALID;
     h->use_graphs = enable != 0;
+    return NF_OK;
+}
+
+int nf_moe_set_expert_gemm(nf_moe* h, int mode) {
+    if (!h) return NF_ERR_INVALID;
+    if (mode < NF_GEMM_ONE_SM || mode > NF_GEMM_CTA_PAIR) return h->fail(NF_ERR_INVALID, "unknown expert GEMM mode");
+    if (h->gemm_mode != mode) {
+        // captured forwards hold the other kernels: drop them
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(h->device);
+        for (auto& g : h->graphs) cudaGraphExecDestroy(g.exec);
+        h->graphs.clear();
+        cudaSetDevice(prev);
+    }
+    h->gemm_mode = mode;
     return NF_OK;
 }
 

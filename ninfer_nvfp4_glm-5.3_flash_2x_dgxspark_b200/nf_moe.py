@@ -31,6 +31,7 @@ BF16_ROUTER, BF16_SHARED_GATE, BF16_SHARED_UP, BF16_SHARED_DOWN = 0, 1, 2, 3
 BF16_EXPERT_GATE, BF16_EXPERT_UP, BF16_EXPERT_DOWN = 4, 5, 6
 F32_ROUTER_BIAS = 0
 EXPERTS_NVFP4, EXPERTS_BF16 = 0, 1
+EXPERT_GEMM = dict(one_sm=0, wide=1, pair=2)  # nf_moe_set_expert_gemm (NF_GEMM_*)
 DBG = dict(counts=0, seg_offset=1, pair_row=2, row_token=3, act_codes=4, act_sf=5, h_codes=6, h_sf=7, down=8,
            shared=9, rows=10, logits=11, screen_count=12)
 
@@ -38,7 +39,7 @@ EXPORTED = [
     "nf_moe_create", "nf_moe_destroy", "nf_moe_last_error", "nf_status_string", "nf_moe_bind_nvfp4",
     "nf_moe_bind_bf16", "nf_moe_bind_f32", "nf_moe_finalize", "nf_moe_forward", "nf_moe_forward_host",
     "nf_moe_sync", "nf_moe_route", "nf_moe_debug_tensor", "nf_moe_debug_read", "nf_nvfp4_dequantize", "nf_nvfp4_quantize",
-    "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck", "nf_moe_set_graph_mode",
+    "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck", "nf_moe_set_graph_mode", "nf_moe_set_expert_gemm",
     "nf_router_topk_noalloc", "nf_ep_unique_id", "nf_moe_create_ep", "nf_moe_create_dense",
     "nf_moe_ep_transport", "nf_tp_split", "nf_tp_create", "nf_tp_destroy", "nf_tp_last_error", "nf_tp_transport",
     "nf_tp_linear_bf16", "nf_tp_argmax", "nf_tp_result", "nf_tp_sync", "nf_stack_create", "nf_stack_destroy",
@@ -99,6 +100,7 @@ def load() -> ctypes.CDLL:
         "nf_sigmoid_ref": ([P, I64, P, P], I32),
         "nf_moe_profile": ([P, I32], I32),
         "nf_moe_set_graph_mode": ([P, I32], I32),
+        "nf_moe_set_expert_gemm": ([P, I32], I32),
         "nf_format_selfcheck": ([ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64)], I32),
         "nf_moe_stage_times": ([P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(I32)], I32),
         "nf_router_topk_noalloc": ([P, P, P, I32, I32, I32, I32, I32, I32, I32, F, P, P, ctypes.c_char_p, I32, P],
@@ -372,6 +374,10 @@ class MoeLayer:
     def set_graph_mode(self, enable: bool) -> None:
         """Capture forwards into CUDA graphs and replay them (needs a stream)."""
         self._check(self.lib.nf_moe_set_graph_mode(self.h, int(enable)))
+
+    def set_expert_gemm(self, mode: str) -> None:
+        """The prefill-size expert GEMM form: "one_sm" (default), "wide" or "pair"."""
+        self._check(self.lib.nf_moe_set_expert_gemm(self.h, EXPERT_GEMM[mode]))
 
     def profile(self, enable: bool) -> None:
         """Start (and clear) or stop per-stage CUDA-event timing."""

@@ -151,3 +151,18 @@ def test_dense_against_reference_golden():
     assert_close(gpu_forward(mlp, x_bits), g["y"], what="dense vs reference golden")
     assert_close(gpu_forward(mlp, x_bits, res), g["y_residual"], what="dense + residual vs reference golden")
     mlp.close()
+
+
+def test_dense_large_batch_wide_stages():
+    """5,000 tokens, H 512, I 1280, with 512-K stages: the down projection is
+    not split and both GEMMs take 512-K stages; the down GEMM's K (1280) ends
+    in a half stage.
+    Tokens are independent, so a subset of 97 rows checks them fully."""
+    lay, mlp = make(512, 1280, 5000, seed=13)
+    mlp.set_expert_gemm("wide")
+    x_bits = tokens(512, 5000, seed=13)
+    got = gpu_forward(mlp, x_bits)
+    sel = np.arange(0, 5000, 52)
+    want = orc.dense_mlp(orc.port(), lay, wl.bf16_bits_to_f32(x_bits[sel]), None)
+    assert_close(got[sel], want, what="dense H512 I1280 T5000 (512-K stages)")
+    mlp.close()

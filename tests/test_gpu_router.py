@@ -136,8 +136,8 @@ def test_screened_router_prefill_bit_exact_with_bound_slack():
     xn = np.sqrt((x.astype(np.float64) ** 2).sum(1))
     ratio = np.abs(approx.astype(np.float64) - lg) / (xn[:, None] * wn[None, :])
     H = lay.hidden
-    assumed_tc = H * 2.0 ** -20  # the screen's allowance for the tensor-core accumulation
-    assert ratio.max() < assumed_tc / 16, ratio.max()
+    assumed_tc = H * 2.0 ** -22  # the screen's allowance for the tensor-core accumulation
+    assert ratio.max() < assumed_tc / 4, ratio.max()
     assert np.all(counts[counts >= 0] >= lay.top_k) and np.mean(counts < 0) < 0.01
     assert np.mean(counts[counts > 0]) < 16
 
