@@ -306,6 +306,15 @@ NF_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, i
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
 }
+// One 32-byte global store (a whole sector per thread; `p` 32-byte aligned):
+// the epilogues write each thread's row segment with these rather than with
+// 16-byte stores, which leave every sector half written per instruction.
+NF_DEV void st_global_v8(void* p, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t a4, uint32_t a5,
+                         uint32_t a6, uint32_t a7) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a0), "r"(a1), "r"(a2),
+                 "r"(a3), "r"(a4), "r"(a5), "r"(a6), "r"(a7)
+                 : "memory");
+}
 // A 3-D tiled TMA load (x, y, z) into this CTA's shared memory.
 NF_DEV void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y, int32_t z) {
     asm volatile(

@@ -525,25 +525,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 p[j] = bf16x2_hw(swiglu_fast(__uint_as_float(v[2 * j]), __uint_as_float(v[32 + 2 * j]), L),
                                                  swiglu_fast(__uint_as_float(v[2 * j + 1]), __uint_as_float(v[32 + 2 * j + 1]), L));
                             if (valid) {
-                                uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) +
-                                                                    static_cast<int64_t>(row) * args.out_ld +
-                                                                    t.n_block * 128 + 32 * cs);
-#pragma unroll
-                                for (int j = 0; j < 4; ++j) d[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                                uint16_t* d = static_cast<uint16_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
+                                              t.n_block * 128 + 32 * cs;
+                                st_global_v8(d, p[0], p[1], p[2], p[3], p[4], p[5], p[6], p[7]);
+                                st_global_v8(d + 16, p[8], p[9], p[10], p[11], p[12], p[13], p[14], p[15]);
                             }
                         }
                     } else {  // EPI_STORE_F32: 16 columns at a time straight to memory
                         if (live) {
-                            uint4* d = reinterpret_cast<uint4*>(static_cast<float*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
-                                                                t.n_block * BN + 64 * cs);
+                            float* d = static_cast<float*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
+                                       t.n_block * BN + 64 * cs;
 #pragma unroll 1
                             for (int c = 0; c < 4; ++c) {
                                 tmem_ld16(tb + 64 * cs + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
                                 tmem_wait_ld();
                                 if (valid) {
-#pragma unroll
-                                    for (int j = 0; j < 4; ++j)
-                                        d[4 * c + j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                                    st_global_v8(d + 16 * c, v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7]);
+                                    st_global_v8(d + 16 * c + 8, v[8], v[9], v[10], v[11], v[12], v[13], v[14], v[15]);
                                 }
                             }
                         }
@@ -586,15 +584,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld16(tbase + 128 + 32 * cs + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
                 } else if (EPI == EPI_STORE_F32) {
                     // no math: stream 16 columns at a time straight to memory
-                    uint4* d = reinterpret_cast<uint4*>(static_cast<float*>(args.out) + t.ks * args.out_split_stride +
-                                                        static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + 64 * cs);
+                    float* d = static_cast<float*>(args.out) + t.ks * args.out_split_stride +
+                               static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + 64 * cs;
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
                         tmem_ld16(tbase + 64 * cs + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
                         tmem_wait_ld();
                         if (valid) {
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) d[4 * c + j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                            st_global_v8(d + 16 * c, v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7]);
+                            st_global_v8(d + 16 * c + 8, v[8], v[9], v[10], v[11], v[12], v[13], v[14], v[15]);
                         }
                     }
                 } else {
@@ -614,26 +612,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float ag = args.alpha0[t.expert], au = args.alpha1[t.expert];
                 const float gsd = args.gscale_next[t.expert], L = args.limit;
                 const bool sbf = args.swiglu_bf16 != 0;
+                const float* os_tab = args.os_table ? args.os_table + 256 * t.expert : nullptr;
                 uint32_t cc[2][2];
                 uint32_t sc[2];
                 const int ng = rep ? 1 : 2;
 #pragma unroll
                 for (int g = 0; g < 2; ++g) {
                     if (g >= ng) break;
-                    float h[16];
-#pragma unroll
-                    for (int j = 0; j < 16; j += 2) {
-                        // linear_nvfp4 output: acc * alpha rounded to BF16 (src/text_forward.cpp:852-855)
-                        const uint32_t g2 = bf16x2_hw(__fmul_rn(__uint_as_float(v[16 * g + j]), ag),
-                                                      __fmul_rn(__uint_as_float(v[16 * g + j + 1]), ag));
-                        const uint32_t u2 = bf16x2_hw(__fmul_rn(__uint_as_float(v[32 + 16 * g + j]), au),
-                                                      __fmul_rn(__uint_as_float(v[32 + 16 * g + j + 1]), au));
-                        const float g0 = __uint_as_float(g2 << 16), g1 = __uint_as_float(g2 & 0xffff0000u);
-                        const float u0 = __uint_as_float(u2 << 16), u1 = __uint_as_float(u2 & 0xffff0000u);
-                        h[j] = sbf ? swiglu_bf16_fast(g0, u0, L) : swiglu_fast(g0, u0, L);
-                        h[j + 1] = sbf ? swiglu_bf16_fast(g1, u1, L) : swiglu_fast(g1, u1, L);
-                    }
-                    sc[g] = quantize_group16_fast<false>(h, gsd, cc[g]);
+                    sc[g] = swiglu_quant_group(&v[16 * g], &v[32 + 16 * g], ag, au, gsd, L, sbf, os_tab, cc[g]);
                 }
                 if (valid && rep) {
                     uint8_t* o = static_cast<uint8_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
@@ -670,10 +656,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 32; ++j)
                     p[j] = bf16x2_hw(__fmul_rn(__uint_as_float(v[2 * j]), a), __fmul_rn(__uint_as_float(v[2 * j + 1]), a));
                 if (valid) {
-                    uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) +
-                                                        static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + 64 * cs);
+                    uint16_t* d = static_cast<uint16_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
+                                  t.n_block * BN + 64 * cs;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) d[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                    for (int j = 0; j < 4; ++j)
+                        st_global_v8(d + 16 * j, p[8 * j], p[8 * j + 1], p[8 * j + 2], p[8 * j + 3], p[8 * j + 4],
+                                     p[8 * j + 5], p[8 * j + 6], p[8 * j + 7]);
                 }
             } else if (EPI == EPI_SWIGLU_BF16) {
                 const float L = args.limit;
@@ -683,10 +671,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     p[j] = bf16x2_hw(swiglu_fast(__uint_as_float(v[2 * j]), __uint_as_float(v[32 + 2 * j]), L),
                                      swiglu_fast(__uint_as_float(v[2 * j + 1]), __uint_as_float(v[32 + 2 * j + 1]), L));
                 if (valid) {
-                    uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) +
-                                                        static_cast<int64_t>(row) * args.out_ld + t.n_block * 128 + 32 * cs);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) d[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                    uint16_t* d = static_cast<uint16_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
+                                  t.n_block * 128 + 32 * cs;
+                    st_global_v8(d, p[0], p[1], p[2], p[3], p[4], p[5], p[6], p[7]);
+                    st_global_v8(d + 16, p[8], p[9], p[10], p[11], p[12], p[13], p[14], p[15]);
                 }
             } else if (EPI == EPI_STORE_F32 && rep) {
                 // (tiles of at most 32 rows; larger tiles stored while reading the accumulator)

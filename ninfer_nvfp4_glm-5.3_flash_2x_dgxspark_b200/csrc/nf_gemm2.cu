@@ -414,25 +414,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const float ag = args.alpha0[t.expert], au = args.alpha1[t.expert];
                         const float gsd = args.gscale_next[t.expert], L = args.limit;
                         const bool sbf = args.swiglu_bf16 != 0;
+                        const float* os_tab = args.os_table ? args.os_table + 256 * t.expert : nullptr;
                         uint32_t cc[2][2];
                         uint32_t sc[2];
 #pragma unroll
-                        for (int g = 0; g < 2; ++g) {
-                            float h[16];
-#pragma unroll
-                            for (int j = 0; j < 16; j += 2) {
-                                // linear_nvfp4 output: acc * alpha rounded to BF16 (src/text_forward.cpp:852-855)
-                                const uint32_t g2 = bf16x2_hw(__fmul_rn(__uint_as_float(v[16 * g + j]), ag),
-                                                              __fmul_rn(__uint_as_float(v[16 * g + j + 1]), ag));
-                                const uint32_t u2 = bf16x2_hw(__fmul_rn(__uint_as_float(v[32 + 16 * g + j]), au),
-                                                              __fmul_rn(__uint_as_float(v[32 + 16 * g + j + 1]), au));
-                                const float g0 = __uint_as_float(g2 << 16), g1 = __uint_as_float(g2 & 0xffff0000u);
-                                const float u0 = __uint_as_float(u2 << 16), u1 = __uint_as_float(u2 & 0xffff0000u);
-                                h[j] = sbf ? swiglu_bf16_fast(g0, u0, L) : swiglu_fast(g0, u0, L);
-                                h[j + 1] = sbf ? swiglu_bf16_fast(g1, u1, L) : swiglu_fast(g1, u1, L);
-                            }
-                            sc[g] = quantize_group16_fast<false>(h, gsd, cc[g]);
-                        }
+                        for (int g = 0; g < 2; ++g)
+                            sc[g] = swiglu_quant_group(&v[16 * g], &v[32 + 16 * g], ag, au, gsd, L, sbf, os_tab, cc[g]);
                         if (valid) {
                             uint8_t* o = static_cast<uint8_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
                                          n * 64 + cs * 16;
@@ -449,12 +436,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             pk[j] = bf16x2_hw(__fmul_rn(__uint_as_float(v[2 * j]), a),
                                               __fmul_rn(__uint_as_float(v[2 * j + 1]), a));
                         if (valid) {
-                            uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) +
-                                                                static_cast<int64_t>(row) * args.out_ld + n * 256 +
-                                                                64 * cs);
+                            uint16_t* d = static_cast<uint16_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
+                                          n * 256 + 64 * cs;
 #pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                d[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                            for (int j = 0; j < 4; ++j)
+                                st_global_v8(d + 16 * j, pk[8 * j], pk[8 * j + 1], pk[8 * j + 2], pk[8 * j + 3],
+                                             pk[8 * j + 4], pk[8 * j + 5], pk[8 * j + 6], pk[8 * j + 7]);
                         }
                     }
                 }

@@ -74,6 +74,8 @@ struct GemmArgs {
     const float* alpha0;       // [E] gate alpha (SwiGLU) or down alpha
     const float* alpha1;       // [E] up alpha (SwiGLU)
     const float* gscale_next;  // [E] 1 / input_scale of the down projection
+    const float* os_table;     // [E][256] the down input quantiser's output scale per E4M3 scale code
+                               // (1 / (scale / gscale_next), or NULL: computed per group)
     float limit;               // swiglu_limit
     int swiglu_bf16;           // EPI_SWIGLU_QUANT: swiglu_clamp_bf16 (dense layers: BF16 after the clamps,
                                // SiLU and product) instead of swiglu_clamp

@@ -349,7 +349,7 @@ int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::s
     }
     if (Is > 0) ok = ok && h->alloc(&h->ws_gu, blocked_bytes(2 * Is, 2 * H) / 2) && h->alloc(&h->ws_dn, blocked_bytes(H, 2 * Is) / 2);
     ok = ok && h->alloc(&h->alpha_g, E) && h->alloc(&h->alpha_u, E) && h->alloc(&h->alpha_d, E) &&
-         h->alloc(&h->gs_g, E) && h->alloc(&h->gs_d, E);
+         h->alloc(&h->gs_g, E) && h->alloc(&h->gs_d, E) && h->alloc(&h->os_tab, E * 256);
     ok = ok && h->alloc(&h->topk_idx, Tm * K) && h->alloc(&h->topk_w, Tm * K);
     PermuteBuffers& b = h->pb;
     if (routed) {
@@ -665,6 +665,18 @@ int nf_moe_finalize(nf_moe* h) {
     if (e == cudaSuccess) e = cudaMemcpy(h->alpha_d, h->h_alpha_d.data(), E * 4, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(h->gs_g, gs_g.data(), E * 4, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(h->gs_d, gs_d.data(), E * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        // the down input quantiser's output scale for each E4M3 scale code:
+        // 1 / (scale / global_scale), with quant_dequant_nvfp4_activation's
+        // guard for a zero scale (src/text_forward.cpp:531-549)
+        std::vector<float> os(static_cast<size_t>(E) * 256);
+        for (int64_t x = 0; x < E; ++x)
+            for (int c = 0; c < 256; ++c) {
+                const float reduced = e4m3_host(static_cast<uint8_t>(c)) / gs_d[static_cast<size_t>(x)];
+                os[static_cast<size_t>(x * 256 + c)] = 1.f / (reduced + (reduced == 0.f ? 1.0e8f : 0.f));
+            }
+        e = cudaMemcpy(h->os_tab, os.data(), os.size() * 4, cudaMemcpyHostToDevice);
+    }
     cudaSetDevice(prev);
     if (e != cudaSuccess) return h->cuda_fail(e, "finalize copy");
     const int64_t R = h->rows_cap, Tm = d.max_tokens;
@@ -841,6 +853,7 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.alpha0 = h->alpha_g;
     g.alpha1 = h->alpha_u;
     g.gscale_next = h->gs_d;
+    g.os_table = fp4 ? h->os_tab : nullptr;
     g.row_token = h->pb.row_token;
     g.out = fp4 ? static_cast<void*>(h->h_codes) : static_cast<void*>(h->h_bf16);
     g.out_ld = fp4 ? I / 2 : I;
