@@ -14,7 +14,10 @@
 // one contiguous 32 KB box per stage); block-scale atoms arrive by 1-D bulk
 // copy (B's in tile order: one 4 KB copy per stage) and move to TMEM with
 // tcgen05.cp; one elected thread issues the MMAs and commits stage release /
-// accumulator-ready to mbarriers.
+// accumulator-ready to mbarriers.  A tile with at most 32 rows (decode)
+// loads only those rows of A (a 32-row box); the MMA's other 96 rows are
+// left-over data whose outputs nobody stores.  Each TMA copy costs its SM
+// about 280 cycles of fixed overhead, so a stage is kept to four copies.
 // A thread completes its tcgen05.cp copies one after another (~150 cycles
 // each), and in one thread's stream they also hold up the MMAs behind them:
 // the 12 scale-atom copies of a stage cost about three times the stage's 4
@@ -229,13 +232,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         };
         if (args.early_claim) claim_first();
-        // A is always a full 16 KB: tiles with at most 32 rows load their rows four
-        // times, into rows 0-31, 32-63, 64-95 and 96-127 (see the epilogue)
+        // A: 16 KB, or 4 KB (rows 0-31) for a tile with at most 32 rows
         // B's scale groups of the stage's K blocks that hold MMA steps (a last
         // 512-K stage may cover one 256-K block only)
         auto sfb_bytes = [&](int steps) { return static_cast<uint32_t>((steps + 3) / 4) * (SFB_STAGE_BYTES / KS); };
-        auto stage_bytes = [&](int steps) {
-            uint32_t bytes = A_STAGE_BYTES + B_STAGE_BYTES;
+        auto stage_bytes = [&](int steps, bool small) {
+            uint32_t bytes = (small ? kSmallRows * 128 : A_STAGE_BYTES) + B_STAGE_BYTES;
             if (KIND == KIND_NVFP4) bytes += static_cast<uint32_t>(steps) * 512u + sfb_bytes(steps);
             return bytes;
         };
@@ -252,13 +254,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int nb0 = __shfl_sync(0xffffffffu, next_t.n_block, 0);
             const int k00 = __shfl_sync(0xffffffffu, next_t.kt0, 0);
             const int k01 = __shfl_sync(0xffffffffu, next_t.kt1, 0);
+            const bool small0 = MT == 1 && KS == 1 && __shfl_sync(0xffffffffu, next_t.m_valid, 0) <= kSmallRows;
             if (first < num_tiles) {
                 // stage j holds K stage k00 + j of the first tile
                 pre = min(STAGES, k01 - k00);
                 for (int j = 0; j < pre; ++j) {
                     const int kt = k00 + j;
                     const int steps_j = min(4 * KS, (K - kt * kElemsPerStage) / kMmaK);
-                    if (lane == 0) mbar_arrive_expect_tx(&full[j], stage_bytes(steps_j));
+                    if (lane == 0) mbar_arrive_expect_tx(&full[j], stage_bytes(steps_j, small0));
                     __syncwarp();
                     const int blk = (e0 * args.b_nb + nb0) * args.b_kt + kt * KS;
                     if (lane == 1) {
@@ -305,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             t.m_valid = __shfl_sync(0xffffffffu, t.m_valid, 0);
             t.kt0 = __shfl_sync(0xffffffffu, t.kt0, 0);
             t.kt1 = __shfl_sync(0xffffffffu, t.kt1, 0);
-            // tiles with at most 32 rows of the expert load only those rows of A (four times)
+            // tiles with at most 32 rows of the expert load only those rows of A
             const bool small_a = MT == 1 && KS == 1 && t.m_valid <= kSmallRows;
             if (args.mt_wait > 0) {
                 // A (and its scales) are the gate/up GEMM's output for these rows:
@@ -327,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         set_abort(cta_abort, args.err, NF_DEVERR_WAIT_EMPTY);
                         ok = false;
                     } else {
-                        mbar_arrive_expect_tx(&full[stage], stage_bytes(steps));
+                        mbar_arrive_expect_tx(&full[stage], stage_bytes(steps, small_a));
                     }
                 }
                 ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -344,9 +347,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else if (MT == 2 && lane == 4) {
                     // the tile's second 128 rows (zero-filled past the tensor)
                     tma_load_2d(sA + stage * A_STAGE_BYTES + BM * 128, &tma, &full[stage], xc, t.row0 + BM);
-                } else if (small_a && lane >= 4 && lane <= 6) {
-                    tma_load_2d(sA + stage * A_STAGE_BYTES + (lane - 3) * kSmallRows * 128, &tma_small, &full[stage], xc,
-                                t.row0);
                 } else if (lane == 1 && !b_issued) {
                     if (KS == 2) tma_load_3d_hint(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0, 0, blk, stream_policy);
                     else tma_load_2d_hint(sB + stage * B_STAGE_BYTES, &tmb, &full[stage], 0, blk * BN, stream_policy);
@@ -555,27 +555,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc_phase ^= 1u;
                 continue;
             }
-            // A tile of at most 32 rows holds them in every TMEM lane quadrant (A was
-            // loaded four times), so for the NVFP4 epilogues all sixteen warps take a
-            // share of its columns instead of quadrant 0's four: SwiGLU-quantise, one
-            // 16-output group per warp (cs < 2); down, 16 columns per warp.
-            const bool rep = KIND == KIND_NVFP4 && KS == 1 && t.m_valid <= kSmallRows;
-            const int row = rep ? t.row0 + lane : t.row0 + r;
-            const bool valid = rep ? lane < t.m_valid : r < t.m_valid;
-            // some row of this warp belongs to the expert (and the warp has columns)
-            const bool warp_live = rep ? (EPI != EPI_SWIGLU_QUANT || cs < 2) : q * 32 < t.m_valid;
-            const int rg = 2 * q + cs;      // replicated SwiGLU: output group (16 columns)
-            const int rc = 16 * (4 * q + cs);  // replicated down: first column
+            // (a tile of at most 32 rows has them in TMEM lane quadrant 0 only:
+            // its four warps take the tile's columns, the others idle)
+            const int row = t.row0 + r;
+            const bool valid = r < t.m_valid;
+            const bool warp_live = q * 32 < t.m_valid;  // some row of this warp belongs to the expert
             uint32_t v[64];
-            if (warp_live && rep) {
-                if (EPI == EPI_SWIGLU_QUANT) {
-                    tmem_ld16(tbase + 16 * rg, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-                    tmem_ld16(tbase + 128 + 16 * rg, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
-                } else {
-                    tmem_ld16(tbase + rc, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-                }
-                tmem_wait_ld();
-            } else if (warp_live) {
+            if (warp_live) {
                 if (EPI == EPI_SWIGLU_QUANT || EPI == EPI_SWIGLU_BF16) {
                     // gate columns [32cs, 32cs+32), up columns 128 further
                     tmem_ld16(tbase + 32 * cs, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
@@ -615,22 +601,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float* os_tab = args.os_table ? args.os_table + 256 * t.expert : nullptr;
                 uint32_t cc[2][2];
                 uint32_t sc[2];
-                const int ng = rep ? 1 : 2;
 #pragma unroll
-                for (int g = 0; g < 2; ++g) {
-                    if (g >= ng) break;
+                for (int g = 0; g < 2; ++g)
                     sc[g] = swiglu_quant_group(&v[16 * g], &v[32 + 16 * g], ag, au, gsd, L, sbf, os_tab, cc[g]);
-                }
-                if (valid && rep) {
-                    uint8_t* o = static_cast<uint8_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
-                                 t.n_block * 64 + rg * 8;
-                    *reinterpret_cast<uint2*>(o) = make_uint2(cc[0][0], cc[0][1]);
-                    // the down GEMM loads this tile's rows four times too: the scale
-                    // goes to all four lane-quadrant columns of the atom
-                    uint8_t* sfp = args.out_sf + sf_atom_offset(row, t.n_block * 8 + rg, args.out_kgroups);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) sfp[4 * k] = static_cast<uint8_t>(sc[0]);
-                } else if (valid) {
+                if (valid) {
                     uint8_t* o = static_cast<uint8_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
                                  t.n_block * 64 + cs * 16;
                     *reinterpret_cast<uint4*>(o) = make_uint4(cc[0][0], cc[0][1], cc[1][0], cc[1][1]);
@@ -640,18 +614,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else if (EPI == EPI_STORE_BF16) {
                 const float a = args.alpha0[t.expert];
                 uint32_t p[32];
-                if (rep) {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        p[j] = bf16x2_hw(__fmul_rn(__uint_as_float(v[2 * j]), a), __fmul_rn(__uint_as_float(v[2 * j + 1]), a));
-                    if (valid) {
-                        uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) +
-                                                            static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + rc);
-                        d[0] = make_uint4(p[0], p[1], p[2], p[3]);
-                        d[1] = make_uint4(p[4], p[5], p[6], p[7]);
-                    }
-                    continue;
-                }
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
                     p[j] = bf16x2_hw(__fmul_rn(__uint_as_float(v[2 * j]), a), __fmul_rn(__uint_as_float(v[2 * j + 1]), a));
@@ -675,14 +637,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   t.n_block * 128 + 32 * cs;
                     st_global_v8(d, p[0], p[1], p[2], p[3], p[4], p[5], p[6], p[7]);
                     st_global_v8(d + 16, p[8], p[9], p[10], p[11], p[12], p[13], p[14], p[15]);
-                }
-            } else if (EPI == EPI_STORE_F32 && rep) {
-                // (tiles of at most 32 rows; larger tiles stored while reading the accumulator)
-                if (valid) {
-                    uint4* d = reinterpret_cast<uint4*>(static_cast<float*>(args.out) + t.ks * args.out_split_stride +
-                                                        static_cast<int64_t>(row) * args.out_ld + t.n_block * BN + rc);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) d[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
                 }
             }
             }

@@ -1071,8 +1071,6 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const int32_t* __rest
 __device__ __forceinline__ void dispatch_token_group(const uint16_t* __restrict__ x, int t, int g, int K,
                                                      const int32_t* __restrict__ pick_e,
                                                      const int32_t* __restrict__ pick_row,
-                                                     const int32_t* __restrict__ counts,
-                                                     const int32_t* __restrict__ seg_off,
                                                      const float* __restrict__ gscale, int H, int bf16_mode,
                                                      uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
                                                      uint16_t* __restrict__ a_bf16) {
@@ -1108,17 +1106,12 @@ __device__ __forceinline__ void dispatch_token_group(const uint16_t* __restrict_
             have = gs;
         }
         *reinterpret_cast<uint2*>(a_codes + static_cast<int64_t>(row) * (H / 2) + g * 8) = make_uint2(codes[0], codes[1]);
-        // a GEMM tile with at most 32 rows loads them four times (TMEM lane
-        // quadrants 0-3), so its rows' scales go to all four quadrant columns
-        uint8_t* sfp = a_sf + sf_atom_offset(row, g, H / 16);
-        const int copies = counts[e] - ((row - seg_off[e]) & ~127) <= 32 ? 4 : 1;
-        for (int k = 0; k < copies; ++k) sfp[4 * k] = static_cast<uint8_t>(sf);
+        a_sf[sf_atom_offset(row, g, H / 16)] = static_cast<uint8_t>(sf);
     }
 }
 
 __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ idx,
-                                const int32_t* __restrict__ pair_row, const int32_t* __restrict__ counts,
-                                const int32_t* __restrict__ seg_off, const float* __restrict__ gscale, int T, int K,
+                                const int32_t* __restrict__ pair_row, const float* __restrict__ gscale, int T, int K,
                                 int H, int bf16_mode, uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
                                 uint16_t* __restrict__ a_bf16) {
     pdl_wait();  // launched dependent on the previous kernel
@@ -1128,7 +1121,7 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
     if (item >= static_cast<int64_t>(T) * gq) return;
     const int64_t t = item / gq;
     const int g = static_cast<int>(item - t * gq);
-    dispatch_token_group(x, static_cast<int>(t), g, K, idx + t * K, pair_row + t * K, counts, seg_off, gscale, H,
+    dispatch_token_group(x, static_cast<int>(t), g, K, idx + t * K, pair_row + t * K, gscale, H,
                          bf16_mode, a_codes, a_sf, a_bf16);
 }
 
@@ -1189,7 +1182,7 @@ __global__ void __launch_bounds__(256) permute_dispatch_kernel(
     const int gq = H / 16;
     for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < n * gq; item += gridDim.x * blockDim.x) {
         const int pair = item / gq, g = item - pair * gq;
-        dispatch_token_group(x, pair / K, g, 1, s_idx + pair, s_row + pair, s_cnt, s_off, gscale, H, bf16_mode,
+        dispatch_token_group(x, pair / K, g, 1, s_idx + pair, s_row + pair, gscale, H, bf16_mode,
                              a_codes, a_sf, a_bf16);
     }
 }
@@ -1418,8 +1411,7 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
     }
     const int64_t items = static_cast<int64_t>(T) * (H / 16);
     return launch_dependent(dispatch_kernel, dim3(static_cast<unsigned>((items + 127) / 128)), dim3(128), 0, st, x, idx,
-                            static_cast<const int32_t*>(b.pair_row), static_cast<const int32_t*>(b.counts),
-                            static_cast<const int32_t*>(b.seg_off), gscale, T, K, H, bf16_mode, b.a_codes, b.a_sf,
+                            static_cast<const int32_t*>(b.pair_row), gscale, T, K, H, bf16_mode, b.a_codes, b.a_sf,
                             b.a_bf16);
 }
 
