@@ -15,6 +15,10 @@
 #include "nf_safetensors.hpp"
 
 #include <sys/stat.h>
+#include <unistd.h>
+
+#include <chrono>
+#include <thread>
 
 #include <cstdio>
 #include <cstring>
@@ -64,9 +68,35 @@ std::map<std::string, Record> read_tensors(const char* path) {
 
 }  // namespace
 
+// The group id of an expert-parallel run: rank 0 makes it and publishes it as
+// a file (written then renamed, so a reader sees it whole); the other ranks
+// wait for the file (two minutes at most).
+std::vector<uint8_t> ep_group_id(int rank, const std::string& path) {
+    std::vector<uint8_t> id(NF_EP_ID_BYTES);
+    if (rank == 0) {
+        if (nf_ep_unique_id(id.data(), NF_EP_ID_BYTES) != NF_OK) throw std::runtime_error("nf_ep_unique_id failed");
+        const std::string tmp = path + ".tmp";
+        {
+            std::ofstream f(tmp, std::ios::binary);
+            f.write(reinterpret_cast<const char*>(id.data()), NF_EP_ID_BYTES);
+            if (!f) throw std::runtime_error("cannot write " + tmp);
+        }
+        if (std::rename(tmp.c_str(), path.c_str()) != 0) throw std::runtime_error("cannot publish " + path);
+        return id;
+    }
+    for (int i = 0; i < 2400; ++i) {
+        std::ifstream f(path, std::ios::binary);
+        if (f && f.read(reinterpret_cast<char*>(id.data()), NF_EP_ID_BYTES)) return id;
+        std::this_thread::sleep_for(std::chrono::milliseconds(50));
+    }
+    throw std::runtime_error("no group id at " + path);
+}
+
 int main(int argc, char** argv) {
     if (argc < 10) {
-        std::fprintf(stderr, "usage: %s tensors.nft prefix out_y.f32 hidden experts top_k inter shared_inter scaling [device]\n",
+        std::fprintf(stderr,
+                     "usage: %s tensors.nft prefix out_y.f32 hidden experts top_k inter shared_inter scaling [device "
+                     "[--ep rank world group_id_file]]\n",
                      argv[0]);
         return 2;
     }
@@ -106,6 +136,24 @@ int main(int argc, char** argv) {
         d.max_tokens = static_cast<int>(x->dim(0));
         const int device = argc > 10 ? std::atoi(argv[10]) : 0;
         std::vector<float> y(static_cast<size_t>(x->dim(0) * x->dim(1)));
+        if (argc > 11 && std::strcmp(argv[11], "--ep") == 0) {
+            // expert parallel: this rank's handle, its share of the token rows
+            // (rows [T r / world, T (r + 1) / world)), out_y gets those rows
+            if (argc < 15) throw std::runtime_error("--ep needs rank world group_id_file");
+            const int rank = std::atoi(argv[12]), world = std::atoi(argv[13]);
+            const int64_t T = x->dim(0), H = x->dim(1);
+            const int64_t r0 = T * rank / world, r1 = T * (rank + 1) / world;
+            d.max_tokens = static_cast<int>((T + world - 1) / world);
+            const std::vector<uint8_t> id = ep_group_id(rank, argv[14]);
+            nf_host::MoeLayer layer(d, device, rank, world, id.data(), NF_EP_ID_BYTES);
+            layer.bind_from_store(lookup, prefix);
+            layer.moe(static_cast<const float*>(x->data) + r0 * H, y.data() + r0 * H, static_cast<int>(r1 - r0));
+            std::ofstream out(argv[3], std::ios::binary);
+            out.write(reinterpret_cast<const char*>(y.data() + r0 * H), static_cast<std::streamsize>((r1 - r0) * H * 4));
+            std::printf("moe_demo: rank %d of %d (%s), rows %lld-%lld\n", rank, world, layer.ep_transport(),
+                        static_cast<long long>(r0), static_cast<long long>(r1));
+            return 0;
+        }
         if (d.experts == 0) {
             nf_host::DenseMlp mlp(d.hidden, d.inter, d.swiglu_limit, d.max_tokens, device);
             mlp.bind_from_store(lookup, prefix);

@@ -85,6 +85,43 @@ def test_demo_matches_python_host_path(tmp_path):
 
 
 @pytest.mark.gpu
+def test_demo_expert_parallel_matches_one_gpu(tmp_path):
+    """The C++ host class's expert-parallel constructor and host-buffer
+    forward on two GPUs (two processes, the group id handed over in a file):
+    each rank's share of the rows equals the one-GPU run bit for bit."""
+    import os
+
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    wl = workload()
+    lay, x_bits = wl.config_layer("c0")
+    x = wl.bf16_bits_to_f32(x_bits)
+    t = layer_tensors(lay)
+    t["x"] = ("f", x)
+    write_nft(tmp_path / "c0.nft", t)
+    r = run_demo(tmp_path / "c0.nft", tmp_path / "y1.f32", lay)
+    assert r.returncode == 0, r.stderr
+    y1 = np.fromfile(tmp_path / "y1.f32", dtype=np.float32).reshape(x.shape)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    args = [str(DEMO), str(tmp_path / "c0.nft"), PREFIX, "", str(lay.hidden), str(lay.experts), str(lay.top_k),
+            str(lay.inter), str(lay.shared_inter), repr(float(lay.scaling))]
+    procs = []
+    for rank in range(2):
+        a = list(args)
+        a[3] = str(tmp_path / f"y_rank{rank}.f32")
+        a += [str(rank), "--ep", str(rank), "2", str(tmp_path / "group.id")]
+        procs.append(subprocess.Popen(a, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True, env=env))
+    outs = [p.communicate(timeout=300) for p in procs]
+    for p, (out, err) in zip(procs, outs):
+        assert p.returncode == 0, err
+    T, H = x.shape
+    parts = [np.fromfile(tmp_path / f"y_rank{rank}.f32", dtype=np.float32) for rank in range(2)]
+    y2 = np.concatenate(parts).reshape(T, H)
+    assert np.array_equal(y2.view(np.uint32), y1.view(np.uint32))
+
+
+@pytest.mark.gpu
 def test_demo_missing_expert_tensor_names_it(tmp_path):
     wl = workload()
     lay, x_bits = wl.config_layer("c0")
