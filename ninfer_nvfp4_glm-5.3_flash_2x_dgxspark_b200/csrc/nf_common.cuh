@@ -362,6 +362,10 @@ NF_DEV void bulk_load_hint(void* smem_dst, const void* gmem_src, uint32_t bytes,
         "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned, bytes a multiple of 16).
+NF_DEV void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 NF_DEV void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -839,8 +839,8 @@ static cudaError_t launch_one(const CUtensorMap& tma, const CUtensorMap& tma_sma
 cudaError_t launch_gemm(const CUtensorMap& tma, const CUtensorMap& tma_small, const CUtensorMap& tmb,
                         const GemmArgs& args, int grid, bool dependent, cudaStream_t st) {
     if (args.kind == KIND_NVFP4 && args.wide_stages) {
-        // 512-K stages: tma / tmb are the 3-D maps (make_tmap_a3 / make_tmap_b3); grouped tiles only
-        if (args.dense_rows > 0) return cudaErrorInvalidValue;
+        // 512-K stages: tma / tmb are the 3-D maps (make_tmap_a3 / make_tmap_b3); no split K
+        if (args.dense_rows > 0 && args.k_split > 1) return cudaErrorInvalidValue;
         if (args.epi == EPI_SWIGLU_QUANT) return launch_one<KIND_NVFP4, EPI_SWIGLU_QUANT, 1, 2>(tma, tma_small, tmb, args, grid, dependent, st);
         if (args.epi == EPI_STORE_BF16) return launch_one<KIND_NVFP4, EPI_STORE_BF16, 1, 2>(tma, tma_small, tmb, args, grid, dependent, st);
         return cudaErrorInvalidValue;

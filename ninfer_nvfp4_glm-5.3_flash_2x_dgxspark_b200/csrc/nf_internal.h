@@ -206,6 +206,10 @@ inline void router_chunked_layout16(const uint16_t* w, int E, int H, uint16_t* o
 // one_kernel: set when the permutation and the dispatch ran as one kernel
 // (small batches), so the kernel after it must not read the tile lists before
 // pdl_wait().
+// The dense MLP's dispatch (rows = tokens, no permutation; resets the GEMMs'
+// tile and hand-off counters).
+cudaError_t launch_dense_dispatch(const uint16_t* x, int T, int H, const float* gscale, PermuteBuffers& b,
+                                  cudaStream_t st);
 cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
                            const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st, bool* one_kernel);
 cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair_row, const float* topk_w,
@@ -281,16 +285,21 @@ cudaError_t launch_gqa_decode(const CUtensorMap& tmk, const CUtensorMap& tmv, co
 cudaError_t launch_fill_bf16_hash(uint16_t* p, int64_t n, uint64_t seed, cudaStream_t st);
 
 // Screened router (large batches): candidates per token and the batch size
-// from which forwards use it.  The screen takes the router rows as BF16
-// [E, H] with E % 16 == 0, E <= kRouterMaxE and H % kRouterKc == 0.
+// from which forwards use it.  Both kernels take the router rows as the
+// chunk-major BF16 copy (rows padded to kRouterPitch16) with E % 16 == 0,
+// E <= kRouterMaxE and H % kRouterKc == 0; a stage that never lands sets
+// `err` and the kernel leaves.
 constexpr int kScreenMaxCandHost = 32;
 constexpr int kScreenMinTokens = 1024;
-cudaError_t launch_route_screen(const uint16_t* x, int T, int H, const uint16_t* w, int E, int K, const float* bias,
-                                const float* wnorm, float c, int32_t* cand, int32_t* cnt, float* approx,
-                                cudaStream_t st);
-cudaError_t launch_route_exact(const uint16_t* x, const uint16_t* wz16, const float* bias, int T, int H, int E, int K,
+// `tmx`: the tokens [T, H] BF16 as a 2-D map with 64 x 32 boxes and the
+// 128-byte swizzle (make_tmap_2d(.., x, true, H, T, 64, 32)).
+cudaError_t launch_route_screen(const CUtensorMap& tmx, const uint16_t* x, int T, int H, const uint16_t* wz16, int E,
+                                int K, const float* bias, const float* wnorm, float c, int32_t* cand, int32_t* cnt,
+                                float* approx, int* err, cudaStream_t st);
+cudaError_t launch_route_exact(const CUtensorMap& tmx, const uint16_t* x, const uint16_t* wz16, const float* bias, int T,
+                               int H, int E, int K,
                                float scaling, int normalize, int w_safe, const int32_t* cand, const int32_t* cnt,
-                               int32_t* idx, float* wts, cudaStream_t st);
+                               int32_t* idx, float* wts, int* err, cudaStream_t st);
 
 constexpr int kChunkTokHost = 128;  // tokens per permutation chunk (nf_kernels.cu kChunkTok)
 // Per-device one-time state (kernel attributes, lookup tables) is kept in

@@ -1125,6 +1125,39 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
                          bf16_mode, a_codes, a_sf, a_bf16);
 }
 
+// The dense MLP's dispatch: its rows are the tokens in order (one segment at
+// row 0, no permutation), so it quantises token t into row t with the one
+// gate input scale, writes the identity pick -> row map for the combine, and
+// block 0 zeroes the GEMMs' tile counters (meta[4..5])
+// and the per-128-row hand-off counters the permutation would otherwise reset.
+__global__ void dense_dispatch_kernel(const uint16_t* __restrict__ x, int T, int H, const float* __restrict__ gscale,
+                                      uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
+                                      int32_t* __restrict__ pair_row, int32_t* __restrict__ meta,
+                                      int32_t* __restrict__ mt_done, int m_tiles) {
+    pdl_wait();  // launched dependent on the previous kernel
+    pdl_trigger();
+    if (blockIdx.x == 0) {
+        if (threadIdx.x < 2) meta[4 + threadIdx.x] = 0;
+        for (int i = threadIdx.x; i < m_tiles; i += blockDim.x) mt_done[i] = 0;
+    }
+    const int gq = H / 16;
+    const int64_t item = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (item >= static_cast<int64_t>(T) * gq) return;
+    const int t = static_cast<int>(item / gq), g = static_cast<int>(item - static_cast<int64_t>(t) * gq);
+    const int32_t e0 = 0, row = t;
+    if (g == 0) pair_row[t] = t;  // the combine's pick -> row map
+    dispatch_token_group(x, t, g, 1, &e0, &row, gscale, H, 0, a_codes, a_sf, nullptr);
+}
+
+cudaError_t launch_dense_dispatch(const uint16_t* x, int T, int H, const float* gscale, PermuteBuffers& b,
+                                  cudaStream_t st) {
+    const int64_t items = static_cast<int64_t>(T) * (H / 16);
+    const int m_tiles = (T + 127) / 128;
+    return launch_dependent(dense_dispatch_kernel, dim3(static_cast<unsigned>(std::max<int64_t>(1, (items + 127) / 128))),
+                            dim3(128), 0, st, x, T, H, gscale, b.a_codes, b.a_sf, b.pair_row, b.meta, b.mt_done,
+                            m_tiles);
+}
+
 // Permutation and dispatch of a small batch (T * K <= kSmallPairs) in one
 // launch: every CTA rebuilds the permutation in shared memory from idx (a
 // few hundred picks: cheaper than a kernel boundary), writes its share of the
@@ -1826,15 +1859,27 @@ __device__ __forceinline__ bool bf16_screen_unsafe(uint32_t u) {
 // exact), else the separately rounded multiply and add.  The router rows
 // (the fused router's BF16 chunk-major copy, rows padded to kRouterPitch16)
 // and the tokens' BF16 columns stream through shared memory in 128-column
-// chunks, double buffered with cp.async; the padded pitches put the rows
-// that neighbouring lanes read in different banks.  Then one warp per token
+// chunks, three stages of cp.async; the padded pitches put the rows that
+// neighbouring lanes read in different banks.  The CTA's token rows are
+// prefetched into L2 as one bulk request each before the first chunk, so
+// the chunks' token columns come from L2 rather than from DRAM one chunk
+// ahead.  Then one warp per token
 // applies the exact sigmoid and bias and the reference's selection with
 // every non-candidate's choice at -inf.
+// Token columns of a 128-column chunk staged by TMA as two 64-column boxes
+// of 32 rows with the 128-byte swizzle: row r of box b at b * 4 KB + r * 128
+// bytes, its 16-byte piece q stored at piece q ^ (r & 7) (so that the rows
+// eight lanes read at one column land in different banks).
+constexpr int kRtXStage = 2 * 32 * 64;  // BF16 elements per stage
+__device__ __forceinline__ int rt_xpiece(int tok, int q) {  // element offset of 16-byte piece q (0..15) of row tok
+    return (q >> 3) * 2048 + tok * 64 + (((q & 7) ^ (tok & 7)) << 3);
+}
 constexpr int kExTok = 32;
 constexpr int kExThreads = 256;
 constexpr int kExWarps = kExThreads / 32;
 constexpr int kExSlots = 4;
-constexpr int kExXPitch = kRouterKc + 8;  // BF16 elements per staged token row
+constexpr int kExStages = 3;
+constexpr int kExMaxK = 8;  // picks per token (the screened path serves K <= 8)
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
@@ -1845,11 +1890,11 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // One 128-column chunk of a chain.  MODE 0: fused multiply-add; 1: the
 // separately rounded multiply and add; 2: per lane, by `fma`.
 template <int MODE>
-__device__ __forceinline__ float exact_chunk(const uint16_t* wr, const uint16_t* xr, float a, bool fma) {
+__device__ __forceinline__ float exact_chunk(const uint16_t* wr, const uint16_t* xb, int tok, float a, bool fma) {
 #pragma unroll 4
     for (int k = 0; k < kRouterKc; k += 8) {
         const uint4 wv = *reinterpret_cast<const uint4*>(wr + k);
-        const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
+        const uint4 xv = *reinterpret_cast<const uint4*>(xb + rt_xpiece(tok, k >> 3));
         if (MODE == 0 || (MODE == 2 && fma)) {
             a = chain_step2<true>(wv.x, xv.x, a);
             a = chain_step2<true>(wv.y, xv.y, a);
@@ -1870,14 +1915,14 @@ __device__ __forceinline__ float exact_chunk(const uint16_t* wr, const uint16_t*
 // independent, so their loads and steps interleave.
 template <int NS>
 __device__ __forceinline__ void exact_chunk_multi(const uint16_t* wb, const uint16_t* xb, const int (&wofs)[kExSlots],
-                                                  const int (&xofs)[kExSlots], float (&acc)[kExSlots]) {
+                                                  const int (&xtok)[kExSlots], float (&acc)[kExSlots]) {
 #pragma unroll 2
     for (int k = 0; k < kRouterKc; k += 8) {
         uint4 wv[NS], xv[NS];
 #pragma unroll
         for (int s = 0; s < NS; ++s) {
             wv[s] = *reinterpret_cast<const uint4*>(wb + wofs[s] + k);
-            xv[s] = *reinterpret_cast<const uint4*>(xb + xofs[s] + k);
+            xv[s] = *reinterpret_cast<const uint4*>(xb + rt_xpiece(xtok[s], k >> 3));
         }
 #pragma unroll
         for (int s = 0; s < NS; ++s) {
@@ -1892,14 +1937,16 @@ __device__ __forceinline__ void exact_chunk_multi(const uint16_t* wb, const uint
 }
 
 __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
-    const uint16_t* __restrict__ x, const uint16_t* __restrict__ wz16, const float* __restrict__ bias, int T, int H,
+    const __grid_constant__ CUtensorMap tmx, const uint16_t* __restrict__ x, const uint16_t* __restrict__ wz16,
+    const float* __restrict__ bias, int T, int H,
     int E, int K, float scaling, int normalize, int w_safe, const int32_t* __restrict__ cand,
-    const int32_t* __restrict__ cnt, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
-    extern __shared__ __align__(16) uint8_t rx_smem[];
+    const int32_t* __restrict__ cnt, int32_t* __restrict__ idx_out, float* __restrict__ w_out, int* __restrict__ err) {
+    extern __shared__ uint8_t rx_smem_raw[];
+    uint8_t* rx_smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rx_smem_raw) + 1023) & ~uintptr_t(1023));
     const int wchunk = E * kRouterPitch16;  // BF16 elements of one chunk of every row
-    uint16_t* sw = reinterpret_cast<uint16_t*>(rx_smem);                         // [2][wchunk]
-    uint16_t* sx = sw + 2 * wchunk;                                              // [2][kExTok][kExXPitch]
-    int32_t* s_chain = reinterpret_cast<int32_t*>(sx + 2 * kExTok * kExXPitch);  // [kExTok * E] token << 8 | expert
+    uint16_t* sx = reinterpret_cast<uint16_t*>(rx_smem);                         // [stages][kRtXStage] (swizzled)
+    uint16_t* sw = sx + kExStages * kRtXStage;                                   // [stages][wchunk]
+    int32_t* s_chain = reinterpret_cast<int32_t*>(sw + kExStages * wchunk);      // [kExTok * E] token << 8 | expert
     float* s_val = reinterpret_cast<float*>(s_chain + kExTok * E);               // [kExTok * E] exact logits
     float* s_sc = s_val + kExTok * E;                                            // [kExWarps][E]
     float* s_ch = s_sc + kExWarps * E;                                           // [kExWarps][E]
@@ -1907,9 +1954,18 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
     __shared__ int s_marked[kExTok];
     __shared__ int s_fma[kExTok];
     __shared__ uint32_t s_excl[kExWarps][32];
+    __shared__ uint64_t full[kExStages];  // chunk stage landed (router rows + token columns)
+    __shared__ int s_abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * kExTok;
     const int ntok = min(kExTok, T - t0);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kExStages; ++i) mbar_init(&full[i], 1);
+        s_abort = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&tmx);
+    }
+    if (threadIdx.x < ntok) prefetch_l2_bulk(x + static_cast<int64_t>(t0 + threadIdx.x) * H, static_cast<uint32_t>(H) * 2u);
 
     // the chain list: per-token counts, their prefix, then the entries
     if (warp == 0) {
@@ -1927,37 +1983,58 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
         }
         if (lane == 31) s_base[kExTok] = incl;
     }
-    __syncthreads();
-    for (int tl = warp; tl < ntok; tl += kExWarps) {
-        const int t = t0 + tl;
-        const int base = s_base[tl], n = s_base[tl + 1] - base;
-        const bool marked = s_marked[tl] != 0;
-        for (int j = lane; j < n; j += 32)
-            s_chain[base + j] = (tl << 8) | (marked ? j : cand[static_cast<int64_t>(t) * kScreenMaxCand + j]);
-        // a token the screen passed is in range; a marked one may not be
-        int xbad = 0;
-        if (marked)
-            for (int i = lane; i < H / 2; i += 32)
-                xbad |= bf16x2_unsafe(reinterpret_cast<const uint32_t*>(x + static_cast<int64_t>(t) * H)[i]) ? 1 : 0;
-        xbad = __any_sync(0xffffffffu, xbad);
-        if (lane == 0) s_fma[tl] = (w_safe && !xbad) ? 1 : 0;
+    __syncthreads();  // (also publishes the barrier initialisation)
+    {
+        // a warp's tokens tl = warp + 8 i; their candidate loads go out together
+        constexpr int kPer = kExTok / kExWarps;
+        int cv[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int tl = warp + i * kExWarps;
+            cv[i] = 0;
+            if (tl < ntok && !s_marked[tl] && lane < s_base[tl + 1] - s_base[tl])
+                cv[i] = cand[static_cast<int64_t>(t0 + tl) * kScreenMaxCand + lane];
+        }
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int tl = warp + i * kExWarps;
+            if (tl >= ntok) break;  // (warp-uniform)
+            const int t = t0 + tl;
+            const int base = s_base[tl], n = s_base[tl + 1] - base;
+            const bool marked = s_marked[tl] != 0;
+            if (marked) {
+                for (int j = lane; j < n; j += 32) s_chain[base + j] = (tl << 8) | j;
+            } else if (lane < n) {
+                s_chain[base + lane] = (tl << 8) | cv[i];
+            }
+            // a token the screen passed is in range; a marked one may not be
+            int xbad = 0;
+            if (marked)
+                for (int q = lane; q < H / 2; q += 32)
+                    xbad |= bf16x2_unsafe(reinterpret_cast<const uint32_t*>(x + static_cast<int64_t>(t) * H)[q]) ? 1 : 0;
+            xbad = __any_sync(0xffffffffu, xbad);
+            if (lane == 0) s_fma[tl] = (w_safe && !xbad) ? 1 : 0;
+        }
     }
     __syncthreads();
     const int total = s_base[kExTok];
     const int nchunks = H / kRouterKc;
-    auto stage = [&](int c, int buf) {
-        const uint4* ws = reinterpret_cast<const uint4*>(wz16 + static_cast<int64_t>(c) * wchunk);
-        uint4* wd = reinterpret_cast<uint4*>(sw + buf * wchunk);
-        for (int i = threadIdx.x; i < wchunk / 8; i += kExThreads) cp_async16(wd + i, ws + i);
-        uint16_t* xd = sx + buf * kExTok * kExXPitch;
-        for (int i = threadIdx.x; i < ntok * (kRouterKc / 8); i += kExThreads) {
-            const int tl = i / (kRouterKc / 8), q = i % (kRouterKc / 8);
-            cp_async16(xd + tl * kExXPitch + 8 * q, x + static_cast<int64_t>(t0 + tl) * H + c * kRouterKc + 8 * q);
-        }
-        cp_async_commit();
+    // Chunk g of the staging sequence (all passes) lands in buffer g % stages
+    // with barrier parity (g / stages) & 1: the router rows of the chunk as
+    // one bulk copy (the chunk-major copy keeps a chunk's rows contiguous, in
+    // the staged pitch) and the tokens' columns as two TMA boxes (rows past
+    // the batch read as zeros).  Thread 0 issues.
+    const uint32_t wbytes = static_cast<uint32_t>(wchunk) * 2u;
+    auto issue = [&](int c, int g) {
+        const int buf = g % kExStages;
+        mbar_arrive_expect_tx(&full[buf], wbytes + static_cast<uint32_t>(kRtXStage) * 2u);
+        bulk_load(sw + buf * wchunk, wz16 + static_cast<int64_t>(c) * wchunk, wbytes, &full[buf]);
+        tma_load_2d(sx + buf * kRtXStage, &tmx, &full[buf], c * kRouterKc, t0);
+        tma_load_2d(sx + buf * kRtXStage + kRtXStage / 2, &tmx, &full[buf], c * kRouterKc + 64, t0);
     };
+    int staged = 0;  // chunks staged by earlier passes
     for (int p0 = 0; p0 < total; p0 += kExThreads * kExSlots) {
-        int wofs[kExSlots], xofs[kExSlots];
+        int wofs[kExSlots], xtok[kExSlots];
         bool fm[kExSlots];
         float acc[kExSlots];
 #pragma unroll
@@ -1965,7 +2042,7 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
             const int ci = p0 + j * kExThreads + threadIdx.x;
             const int ch = ci < total ? s_chain[ci] : 0;  // a lane past the list runs token 0 / expert 0, unused
             wofs[j] = (ch & 0xff) * kRouterPitch16;
-            xofs[j] = (ch >> 8) * kExXPitch;
+            xtok[j] = ch >> 8;
             fm[j] = ci < total ? s_fma[ch >> 8] != 0 : true;
             acc[j] = 0.f;
         }
@@ -1979,20 +2056,41 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
                 all_fma = all_fma && __all_sync(0xffffffffu, fm[j]);
             }
         }
-        stage(0, 0);
+        if (threadIdx.x == 0) {
+            issue(0, staged);
+            if (nchunks > 1) issue(1, staged + 1);
+        }
         for (int c = 0; c < nchunks; ++c) {
-            const int buf = c & 1;
-            cp_async_wait_all();
-            __syncthreads();  // chunk c is in place; every thread is done with chunk c - 1
-            if (c + 1 < nchunks) stage(c + 1, buf ^ 1);
+            const int g = staged + c, buf = g % kExStages;
+            const bool landed = mbar_wait(&full[buf], static_cast<uint32_t>((g / kExStages) & 1), &s_abort, err);
+            // chunk c is in place for every thread, and every thread is done with chunk c - 1
+            if (!__syncthreads_and(landed ? 1 : 0)) {
+                // a stage never landed: record it, let every issued copy land, leave
+                if (threadIdx.x == 0) {
+                    atomicCAS(err, 0, NF_DEVERR_WAIT_FULL);
+                    const int issued_end = staged + min(nchunks, c + 2);
+                    for (int q = g; q < issued_end; ++q) {
+                        const uint64_t tw = globaltimer_ns();
+                        while (!mbar_try_wait(&full[q % kExStages], static_cast<uint32_t>((q / kExStages) & 1))) {
+                            if (globaltimer_ns() - tw > NF_WAIT_BUDGET_NS) {
+                                atomicCAS(err, 0, NF_DEVERR_DRAIN);
+                                break;
+                            }
+                        }
+                    }
+                }
+                __syncthreads();
+                return;
+            }
+            if (threadIdx.x == 0 && c + 2 < nchunks) issue(c + 2, g + 2);
             const uint16_t* wb = sw + buf * wchunk;
-            const uint16_t* xb = sx + buf * kExTok * kExXPitch;
+            const uint16_t* xb = sx + buf * kRtXStage;
             if (all_fma) {
                 switch (ns) {
-                    case 1: exact_chunk_multi<1>(wb, xb, wofs, xofs, acc); break;
-                    case 2: exact_chunk_multi<2>(wb, xb, wofs, xofs, acc); break;
-                    case 3: exact_chunk_multi<3>(wb, xb, wofs, xofs, acc); break;
-                    case 4: exact_chunk_multi<4>(wb, xb, wofs, xofs, acc); break;
+                    case 1: exact_chunk_multi<1>(wb, xb, wofs, xtok, acc); break;
+                    case 2: exact_chunk_multi<2>(wb, xb, wofs, xtok, acc); break;
+                    case 3: exact_chunk_multi<3>(wb, xb, wofs, xtok, acc); break;
+                    case 4: exact_chunk_multi<4>(wb, xb, wofs, xtok, acc); break;
                     default: break;
                 }
                 continue;
@@ -2003,13 +2101,14 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
                 const bool all_f = __all_sync(0xffffffffu, fm[j]);
                 const bool none_f = __all_sync(0xffffffffu, !fm[j]);
                 if (all_f)
-                    acc[j] = exact_chunk<0>(wb + wofs[j], xb + xofs[j], acc[j], true);
+                    acc[j] = exact_chunk<0>(wb + wofs[j], xb, xtok[j], acc[j], true);
                 else if (none_f)
-                    acc[j] = exact_chunk<1>(wb + wofs[j], xb + xofs[j], acc[j], false);
+                    acc[j] = exact_chunk<1>(wb + wofs[j], xb, xtok[j], acc[j], false);
                 else
-                    acc[j] = exact_chunk<2>(wb + wofs[j], xb + xofs[j], acc[j], fm[j]);
+                    acc[j] = exact_chunk<2>(wb + wofs[j], xb, xtok[j], acc[j], fm[j]);
             }
         }
+        staged += nchunks;
 #pragma unroll
         for (int j = 0; j < kExSlots; ++j) {
             const int ci = p0 + j * kExThreads + threadIdx.x;
@@ -2018,32 +2117,85 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
         __syncthreads();  // the buffers are restaged by the next pass; s_val complete
     }
 
-    // selection, one warp per token
+    // selection.  Every chain's score and choice (one thread per chain, into
+    // the staging buffers, free now), then one thread per token over its
+    // candidates in expert order: each pick is the largest choice among the
+    // unused candidates, lowest index among equals -- the reference's rule,
+    // since every other expert's choice is -inf and a screened token's
+    // choices are finite.  Tokens that run every chain (possibly NaN
+    // choices) take the warp form of the full rule.
+    float* c_sc = reinterpret_cast<float*>(sw);  // [total]
+    float* c_ch = c_sc + kExTok * E;             // [total]
+    for (int ci = threadIdx.x; ci < total; ci += kExThreads) {
+        const float sg = sigmoid_ref(s_val[ci]);
+        c_sc[ci] = sg;
+        c_ch[ci] = __fadd_rn(sg, bias[s_chain[ci] & 0xff]);
+    }
+    __syncthreads();
+    if (threadIdx.x < ntok && !s_marked[threadIdx.x]) {
+        const int tl = threadIdx.x, t = t0 + tl;
+        const int base = s_base[tl], n = s_base[tl + 1] - base;  // K <= n <= kScreenMaxCand
+        uint32_t used = 0u;
+        int pk[kExMaxK];
+        float wt[kExMaxK];
+#pragma unroll
+        for (int p = 0; p < kExMaxK; ++p) {
+            pk[p] = 0;
+            wt[p] = 0.f;
+            if (p < K) {
+                int best = -1;
+                float bc = 0.f;
+                for (int j = 0; j < n; ++j) {
+                    if ((used >> j) & 1u) continue;
+                    const float cj = c_ch[base + j];
+                    if (best < 0 || cj > bc) {
+                        best = j;
+                        bc = cj;
+                    }
+                }
+                best = max(best, 0);
+                used |= 1u << best;
+                pk[p] = s_chain[base + best] & 0xff;
+                wt[p] = c_sc[base + best];
+            }
+        }
+        if (normalize) {
+            float sum = 1e-20f;
+#pragma unroll
+            for (int p = 0; p < kExMaxK; ++p)
+                if (p < K) sum = __fadd_rn(sum, wt[p]);
+#pragma unroll
+            for (int p = 0; p < kExMaxK; ++p)
+                if (p < K) wt[p] = __fmul_rn(__fdiv_rn(wt[p], sum), scaling);
+        }
+#pragma unroll
+        for (int p = 0; p < kExMaxK; ++p) {
+            if (p < K) {
+                idx_out[static_cast<int64_t>(t) * K + p] = pk[p];
+                w_out[static_cast<int64_t>(t) * K + p] = wt[p];
+            }
+        }
+    }
     float* sc = s_sc + warp * E;
     float* chv = s_ch + warp * E;
     for (int tl = warp; tl < ntok; tl += kExWarps) {
+        if (!s_marked[tl]) continue;  // (warp-uniform)
         const int t = t0 + tl;
+        const int base = s_base[tl];  // every expert, in order
         for (int e = lane; e < E; e += 32) {
-            sc[e] = 0.f;
-            chv[e] = -INFINITY;  // not a candidate: below k exact choices
+            sc[e] = c_sc[base + e];
+            chv[e] = c_ch[base + e];
         }
         __syncwarp();
-        const int base = s_base[tl], n = s_base[tl + 1] - base;
-        for (int j = lane; j < n; j += 32) {
-            const int e = s_chain[base + j] & 0xff;
-            const float s = sigmoid_ref(s_val[base + j]);
-            sc[e] = s;
-            chv[e] = __fadd_rn(s, bias[e]);
-        }
-        __syncwarp();
-        warp_select(sc, chv, E, K, scaling, normalize, 1, 1, s_excl[warp], idx_out + static_cast<int64_t>(t) * K,
-                    w_out + static_cast<int64_t>(t) * K);
+        warp_select_reg<(kRouterMaxE + 31) / 32>(sc, chv, E, K, scaling, normalize, 1, 1, s_excl[warp],
+                                                 idx_out + static_cast<int64_t>(t) * K,
+                                                 w_out + static_cast<int64_t>(t) * K);
         __syncwarp();
     }
 }
 
 size_t route_exact_smem(int E) {
-    return static_cast<size_t>(2) * E * kRouterPitch16 * 2 + static_cast<size_t>(2) * kExTok * kExXPitch * 2 +
+    return 1024 + static_cast<size_t>(kExStages) * E * kRouterPitch16 * 2 + static_cast<size_t>(kExStages) * kRtXStage * 2 +
            static_cast<size_t>(2) * kExTok * E * 4 + static_cast<size_t>(2) * kExWarps * E * 4;
 }
 
@@ -2076,33 +2228,50 @@ __device__ __forceinline__ float sig_screen(float x) {
 }
 constexpr float kSigMargin = 1.9073486328125e-06f;  // 2^-19
 
-__global__ void __launch_bounds__(kScThreads) route_screen_kernel(const uint16_t* __restrict__ x, int T, int H,
-                                                                  const uint16_t* __restrict__ w, int E, int K,
+__global__ void __launch_bounds__(kScThreads) route_screen_kernel(const __grid_constant__ CUtensorMap tmx,
+                                                                  const uint16_t* __restrict__ x, int T, int H,
+                                                                  const uint16_t* __restrict__ wz16, int E, int K,
                                                                   const float* __restrict__ bias,
                                                                   const float* __restrict__ wnorm, float c,
                                                                   int32_t* __restrict__ cand,
                                                                   int32_t* __restrict__ cnt,
-                                                                  float* __restrict__ approx) {
-    extern __shared__ __align__(16) uint8_t sc_smem[];
-    uint16_t* sx = reinterpret_cast<uint16_t*>(sc_smem);                // [stages][kScTok][kScPitch]
-    uint16_t* sw = sx + kScStages * kScTok * kScPitch;                  // [stages][E][kScPitch]
+                                                                  float* __restrict__ approx, int* __restrict__ err) {
+    extern __shared__ uint8_t sc_smem_raw[];
+    uint8_t* sc_smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sc_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint16_t* sx = reinterpret_cast<uint16_t*>(sc_smem);                // [stages][kRtXStage] (swizzled)
+    uint16_t* sw = sx + kScStages * kRtXStage;                          // [stages][E][kScPitch]
     float* slog = reinterpret_cast<float*>(sw + kScStages * E * kScPitch);  // [kScTok][E + 1]
+    __shared__ uint64_t full[kScStages];  // chunk stage landed (token columns + router rows)
+    __shared__ float s_wn[kRouterMaxE], s_bias[kRouterMaxE];
+    __shared__ int s_abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * kScTok;
     const int ntok = min(kScTok, T - t0);
     const int nchunks = H / kRouterKc;
-    auto stage = [&](int ch, int buf) {
-        uint16_t* xd = sx + buf * kScTok * kScPitch;
-        for (int i = threadIdx.x; i < ntok * (kRouterKc / 8); i += kScThreads) {
-            const int r = i / (kRouterKc / 8), q = i % (kRouterKc / 8);
-            cp_async16(xd + r * kScPitch + 8 * q, x + static_cast<int64_t>(t0 + r) * H + ch * kRouterKc + 8 * q);
-        }
-        uint16_t* wd = sw + buf * E * kScPitch;
-        for (int i = threadIdx.x; i < E * (kRouterKc / 8); i += kScThreads) {
-            const int r = i / (kRouterKc / 8), q = i % (kRouterKc / 8);
-            cp_async16(wd + r * kScPitch + 8 * q, w + static_cast<int64_t>(r) * H + ch * kRouterKc + 8 * q);
-        }
-        cp_async_commit();
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kScStages; ++i) mbar_init(&full[i], 1);
+        s_abort = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&tmx);
+    }
+    for (int e = threadIdx.x; e < E; e += kScThreads) {
+        s_wn[e] = wnorm[e];
+        s_bias[e] = bias[e];
+    }
+    __syncthreads();
+    // Chunk ch lands in buffer ch % stages with barrier parity (ch / stages) & 1:
+    // the tokens' columns as two TMA boxes (rows past the batch read as
+    // zeros) and the router rows of the chunk as one bulk copy (the
+    // chunk-major copy keeps them contiguous, in the staged pitch).  Thread 0
+    // issues.
+    const int wchunk = E * kScPitch;
+    const uint32_t wbytes = static_cast<uint32_t>(wchunk) * 2u;
+    auto issue = [&](int ch) {
+        const int buf = ch % kScStages;
+        mbar_arrive_expect_tx(&full[buf], wbytes + static_cast<uint32_t>(kRtXStage) * 2u);
+        tma_load_2d(sx + buf * kRtXStage, &tmx, &full[buf], ch * kRouterKc, t0);
+        tma_load_2d(sx + buf * kRtXStage + kRtXStage / 2, &tmx, &full[buf], ch * kRouterKc + 64, t0);
+        bulk_load(sw + buf * wchunk, wz16 + static_cast<int64_t>(ch) * wchunk, wbytes, &full[buf]);
     };
     // warp tile: 16 tokens x E / 2 experts (nt n-tiles of 8)
     const int tok0 = 16 * (warp & 1);
@@ -2115,21 +2284,39 @@ __global__ void __launch_bounds__(kScThreads) route_screen_kernel(const uint16_t
     const int tl = threadIdx.x >> 2, tq = threadIdx.x & 3;
     float ss0 = 0.f, ss1 = 0.f;
     int bad = 0;
-    stage(0, 0);
-    if (nchunks > 1) stage(1, 1);
+    if (threadIdx.x == 0) {
+        issue(0);
+        if (nchunks > 1) issue(1);
+    }
     for (int ch = 0; ch < nchunks; ++ch) {
         const int buf = ch % kScStages;
-        if (ch + 1 < nchunks) asm volatile("cp.async.wait_group 1;" ::: "memory");
-        else cp_async_wait_all();
-        __syncthreads();  // chunk ch is in place; every thread is done with chunk ch - 1
-        if (ch + 2 < nchunks) stage(ch + 2, (ch + 2) % kScStages);
-        const uint16_t* xb = sx + buf * kScTok * kScPitch;
-        const uint16_t* wb = sw + buf * E * kScPitch;
+        const bool landed = mbar_wait(&full[buf], static_cast<uint32_t>((ch / kScStages) & 1), &s_abort, err);
+        // chunk ch is in place for every thread, and every thread is done with chunk ch - 1
+        if (!__syncthreads_and(landed ? 1 : 0)) {
+            // a stage never landed: record it, let every issued copy land, leave
+            if (threadIdx.x == 0) {
+                atomicCAS(err, 0, NF_DEVERR_WAIT_FULL);
+                for (int q = ch; q < min(nchunks, ch + 2); ++q) {
+                    const uint64_t tw = globaltimer_ns();
+                    while (!mbar_try_wait(&full[q % kScStages], static_cast<uint32_t>((q / kScStages) & 1))) {
+                        if (globaltimer_ns() - tw > NF_WAIT_BUDGET_NS) {
+                            atomicCAS(err, 0, NF_DEVERR_DRAIN);
+                            break;
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            if (threadIdx.x < ntok) cnt[t0 + threadIdx.x] = -1;  // every chain for these tokens
+            return;
+        }
+        if (threadIdx.x == 0 && ch + 2 < nchunks) issue(ch + 2);
+        const uint16_t* xb = sx + buf * kRtXStage;
+        const uint16_t* wb = sw + buf * wchunk;
         if (tl < ntok) {
-            const uint4* xr = reinterpret_cast<const uint4*>(xb + tl * kScPitch + 32 * tq);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const uint4 v = xr[i];
+                const uint4 v = *reinterpret_cast<const uint4*>(xb + rt_xpiece(tl, 4 * tq + i));
                 const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -2140,13 +2327,16 @@ __global__ void __launch_bounds__(kScThreads) route_screen_kernel(const uint16_t
                 }
             }
         }
-        const uint32_t a_addr = smem_u32(xb + (tok0 + (lane & 15)) * kScPitch + 8 * (lane >> 4));
+        // A: lanes 0-15 give rows tok0 + 0..15 at the k-step's first 8 columns,
+        // lanes 16-31 the same rows at its second 8 (pieces 2 s, 2 s + 1)
+        const int arow = tok0 + (lane & 15);
+        const uint32_t xb_u32 = smem_u32(xb);
         const uint32_t b_addr =
             smem_u32(wb + (ex0 + (lane & 7) + 8 * (lane >> 4)) * kScPitch + 8 * ((lane >> 3) & 1));
 #pragma unroll
         for (int s = 0; s < kRouterKc / 16; ++s) {
             uint32_t a[4];
-            ldsm_x4(a_addr + 32 * s, a);
+            ldsm_x4(xb_u32 + 2 * rt_xpiece(arow, 2 * s + (lane >> 4)), a);
 #pragma unroll
             for (int p = 0; p < 4; ++p) {
                 if (2 * p >= nt) break;
@@ -2192,14 +2382,14 @@ __global__ void __launch_bounds__(kScThreads) route_screen_kernel(const uint16_t
         const int e = tq * per + j;
         const float l = lrow[e];
         if (live && approx) approx[static_cast<int64_t>(t) * E + e] = l;  // (kept for inspection)
-        const float B = __fmul_ru(cn, wnorm[e]);
+        const float B = __fmul_ru(cn, s_wn[e]);
         const float la = __fsub_rd(l, B), ha = __fadd_ru(l, B);
         if (!isfinite(l) || !isfinite(la) || !isfinite(ha)) {
             bad = 1;
             continue;
         }
-        float v = __fadd_rd(__fsub_rd(sig_screen(la), kSigMargin), bias[e]);
-        lrow[e] = __fadd_ru(__fadd_ru(sig_screen(ha), kSigMargin), bias[e]);
+        float v = __fadd_rd(__fsub_rd(sig_screen(la), kSigMargin), s_bias[e]);
+        lrow[e] = __fadd_ru(__fadd_ru(sig_screen(ha), kSigMargin), s_bias[e]);
 #pragma unroll
         for (int i = 0; i < kScMaxK; ++i) {
             if (i >= K) break;
@@ -2260,32 +2450,34 @@ __global__ void __launch_bounds__(kScThreads) route_screen_kernel(const uint16_t
 }
 
 size_t route_screen_smem(int E) {
-    return static_cast<size_t>(kScStages) * (kScTok + E) * kScPitch * 2 + static_cast<size_t>(kScTok) * (E + 1) * 4;
+    return 1024 + static_cast<size_t>(kScStages) * (kRtXStage + E * kScPitch) * 2 + static_cast<size_t>(kScTok) * (E + 1) * 4;
 }
 
-cudaError_t launch_route_screen(const uint16_t* x, int T, int H, const uint16_t* w, int E, int K, const float* bias,
-                                const float* wnorm, float c, int32_t* cand, int32_t* cnt, float* approx,
-                                cudaStream_t st) {
+cudaError_t launch_route_screen(const CUtensorMap& tmx, const uint16_t* x, int T, int H, const uint16_t* wz16, int E,
+                                int K, const float* bias, const float* wnorm, float c, int32_t* cand, int32_t* cnt,
+                                float* approx, int* err, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (E % 16 != 0 || E > kRouterMaxE || H % kRouterKc != 0 || K < 1 || K > kScMaxK) return cudaErrorInvalidValue;
     static bool attr[kMaxDevices] = {};
     cudaError_t e = smem_attr_once(route_screen_kernel, static_cast<int>(route_screen_smem(kRouterMaxE)), attr);
     if (e != cudaSuccess) return e;
-    route_screen_kernel<<<(T + kScTok - 1) / kScTok, kScThreads, route_screen_smem(E), st>>>(x, T, H, w, E, K, bias,
-                                                                                        wnorm, c, cand, cnt, approx);
+    route_screen_kernel<<<(T + kScTok - 1) / kScTok, kScThreads, route_screen_smem(E), st>>>(
+        tmx, x, T, H, wz16, E, K, bias, wnorm, c, cand, cnt, approx, err);
     return cudaGetLastError();
 }
 
-cudaError_t launch_route_exact(const uint16_t* x, const uint16_t* wz16, const float* bias, int T, int H, int E, int K,
+cudaError_t launch_route_exact(const CUtensorMap& tmx, const uint16_t* x, const uint16_t* wz16, const float* bias, int T,
+                               int H, int E, int K,
                                float scaling, int normalize, int w_safe, const int32_t* cand, const int32_t* cnt,
-                               int32_t* idx, float* wts, cudaStream_t st) {
+                               int32_t* idx, float* wts, int* err, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
+    if (K < 1 || K > kExMaxK || E > kRouterMaxE) return cudaErrorInvalidValue;
     const size_t smem = route_exact_smem(E);
     static bool attr[kMaxDevices] = {};
     cudaError_t e = smem_attr_once(route_exact_kernel, static_cast<int>(route_exact_smem(kRouterMaxE)), attr);
     if (e != cudaSuccess) return e;
     route_exact_kernel<<<(T + kExTok - 1) / kExTok, kExThreads, smem, st>>>(
-        x, wz16, bias, T, H, E, K, scaling, normalize, w_safe, cand, cnt, idx, wts);
+        tmx, x, wz16, bias, T, H, E, K, scaling, normalize, w_safe, cand, cnt, idx, wts, err);
     return cudaGetLastError();
 }
 

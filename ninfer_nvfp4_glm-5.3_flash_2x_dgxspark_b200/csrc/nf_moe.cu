@@ -829,7 +829,15 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     cudaError_t e = cudaSuccess;
     rec.begin(NF_STAGE_PERMUTE, s);
     bool one_kernel = false;
-    e = launch_permute(idx, x, T, K, E, H, I / 128, H / 256, h->gs_g, fp4 ? 0 : 1, h->pb, s, &one_kernel);
+    // The dense MLP (every token on expert 0) skips the permutation: its rows
+    // are the tokens in order, and both GEMMs run dense tiles over them.
+    const bool dense_rows = h->dense && fp4;
+    if (dense_rows) {
+        e = launch_dense_dispatch(x, T, H, h->gs_g, h->pb, s);
+        one_kernel = true;
+    } else {
+        e = launch_permute(idx, x, T, K, E, H, I / 128, H / 256, h->gs_g, fp4 ? 0 : 1, h->pb, s, &one_kernel);
+    }
     if (e != cudaSuccess) return h->cuda_fail(e, "permute launch");
     rec.end(NF_STAGE_PERMUTE, s);
     rec.begin(NF_STAGE_GATE_UP, s);
@@ -868,13 +876,20 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.mt_done = h->pb.mt_done;
     g.mt_signal = handoff ? 1 : 0;
     g.early_claim = one_kernel ? 0 : 1;  // the tile list is written by the kernel right before
+    if (dense_rows) {
+        g.dense_rows = T;
+        g.tiles = nullptr;
+        g.num_tiles_dev = nullptr;
+        g.k_split = 1;
+        g.row_token = nullptr;
+    }
     // Prefill-sized batches (on average a pair tile's 256 rows per expert or
     // more) may take the alternative GEMM forms (nf_moe_set_expert_gemm)
     g.num_experts = E;
     g.seg_off = h->pb.seg_off;
     g.seg_cnt = h->pb.counts;
     const bool prefill = static_cast<int64_t>(T) * K >= 256LL * E && down_split <= 1;
-    const bool pair = fp4 && h->gemm_mode == NF_GEMM_CTA_PAIR && h->grid2 >= 2 && prefill && H % 256 == 0 &&
+    const bool pair = !dense_rows && fp4 && h->gemm_mode == NF_GEMM_CTA_PAIR && h->grid2 >= 2 && prefill && H % 256 == 0 &&
                       I % 256 == 0 && E <= 256;
     const bool wide = fp4 && h->gemm_mode == NF_GEMM_WIDE_STAGES && prefill && h->wide_ok;
     g.wide_stages = wide ? 1 : 0;
@@ -903,6 +918,11 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.mt_signal = 0;
     g.mt_wait = handoff ? I / 128 : 0;
     g.early_claim = 1;
+    if (dense_rows) {
+        g.dense_rows = T;
+        g.tiles = nullptr;
+        g.num_tiles_dev = nullptr;
+    }
     if (down_split > 1) {
         // dense split-K: tiles (n block, K slice, m tile) over the T rows of h
         // (one segment at row 0), raw fp32 slices into dense_part
@@ -966,12 +986,14 @@ cudaError_t route_tokens(nf_moe* h, const uint16_t* x, int T, int32_t* idx, floa
     //      and the candidates
     const double u = std::ldexp(1.0, -24);
     const double c = (H * u / (1.0 - H * u) + H * std::ldexp(1.0, -22) + u) * 1.01;
-    cudaError_t e = launch_route_screen(x, T, H, h->router_w, E, K, h->router_bias, h->router_wnorm,
-                                        static_cast<float>(c), h->screen_cand, h->screen_cnt, h->logits, s);
+    CUtensorMap tmx;
+    if (!make_tmap_2d(&tmx, x, true, H, T, 64, 32)) return cudaErrorInvalidValue;
+    cudaError_t e = launch_route_screen(tmx, x, T, H, h->router_wz16, E, K, h->router_bias, h->router_wnorm,
+                                        static_cast<float>(c), h->screen_cand, h->screen_cnt, h->logits, h->dev_err, s);
     if (e != cudaSuccess) return e;
     // 3. the exact chains of the candidates and the reference's selection
-    return launch_route_exact(x, h->router_wz16, h->router_bias, T, H, E, K, d.routed_scaling, d.normalize,
-                              h->router_w_safe, h->screen_cand, h->screen_cnt, idx, w, s);
+    return launch_route_exact(tmx, x, h->router_wz16, h->router_bias, T, H, E, K, d.routed_scaling, d.normalize,
+                              h->router_w_safe, h->screen_cand, h->screen_cnt, idx, w, h->dev_err, s);
 }
 
 static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx_user,
