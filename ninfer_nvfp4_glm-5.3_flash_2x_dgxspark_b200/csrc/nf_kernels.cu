@@ -1966,6 +1966,25 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
         prefetch_tensormap(&tmx);
     }
     if (threadIdx.x < ntok) prefetch_l2_bulk(x + static_cast<int64_t>(t0 + threadIdx.x) * H, static_cast<uint32_t>(H) * 2u);
+    const int nchunks = H / kRouterKc;
+    // Chunk g of the staging sequence (all passes) lands in buffer g % stages
+    // with barrier parity (g / stages) & 1: the router rows of the chunk as
+    // one bulk copy (the chunk-major copy keeps a chunk's rows contiguous, in
+    // the staged pitch) and the tokens' columns as two TMA boxes (rows past
+    // the batch read as zeros).  Thread 0 issues.
+    const uint32_t wbytes = static_cast<uint32_t>(wchunk) * 2u;
+    auto issue = [&](int c, int g) {
+        const int buf = g % kExStages;
+        mbar_arrive_expect_tx(&full[buf], wbytes + static_cast<uint32_t>(kRtXStage) * 2u);
+        bulk_load(sw + buf * wchunk, wz16 + static_cast<int64_t>(c) * wchunk, wbytes, &full[buf]);
+        tma_load_2d(sx + buf * kRtXStage, &tmx, &full[buf], c * kRouterKc, t0);
+        tma_load_2d(sx + buf * kRtXStage + kRtXStage / 2, &tmx, &full[buf], c * kRouterKc + 64, t0);
+    };
+    // the first pass's first two chunks go out before the chain list is built
+    if (threadIdx.x == 0) {
+        issue(0, 0);
+        if (nchunks > 1) issue(1, 1);
+    }
 
     // the chain list: per-token counts, their prefix, then the entries
     if (warp == 0) {
@@ -2018,20 +2037,6 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
     }
     __syncthreads();
     const int total = s_base[kExTok];
-    const int nchunks = H / kRouterKc;
-    // Chunk g of the staging sequence (all passes) lands in buffer g % stages
-    // with barrier parity (g / stages) & 1: the router rows of the chunk as
-    // one bulk copy (the chunk-major copy keeps a chunk's rows contiguous, in
-    // the staged pitch) and the tokens' columns as two TMA boxes (rows past
-    // the batch read as zeros).  Thread 0 issues.
-    const uint32_t wbytes = static_cast<uint32_t>(wchunk) * 2u;
-    auto issue = [&](int c, int g) {
-        const int buf = g % kExStages;
-        mbar_arrive_expect_tx(&full[buf], wbytes + static_cast<uint32_t>(kRtXStage) * 2u);
-        bulk_load(sw + buf * wchunk, wz16 + static_cast<int64_t>(c) * wchunk, wbytes, &full[buf]);
-        tma_load_2d(sx + buf * kRtXStage, &tmx, &full[buf], c * kRouterKc, t0);
-        tma_load_2d(sx + buf * kRtXStage + kRtXStage / 2, &tmx, &full[buf], c * kRouterKc + 64, t0);
-    };
     int staged = 0;  // chunks staged by earlier passes
     for (int p0 = 0; p0 < total; p0 += kExThreads * kExSlots) {
         int wofs[kExSlots], xtok[kExSlots];
@@ -2056,7 +2061,7 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
                 all_fma = all_fma && __all_sync(0xffffffffu, fm[j]);
             }
         }
-        if (threadIdx.x == 0) {
+        if (threadIdx.x == 0 && p0 > 0) {
             issue(0, staged);
             if (nchunks > 1) issue(1, staged + 1);
         }
@@ -2199,6 +2204,20 @@ size_t route_exact_smem(int E) {
            static_cast<size_t>(2) * kExTok * E * 4 + static_cast<size_t>(2) * kExWarps * E * 4;
 }
 
+// bf16_screen_unsafe for both halves at once, as flags (bit 15: low half,
+// bit 31: high half) from the magnitudes m (15 bits per 16-bit lane, so no
+// carry crosses lanes): m >= 147 << 7 sets bit 15 of m + 0x3680; 0 < m <
+// 60 << 7 leaves bit 15 of m + 0x6200 clear and sets that of m + 0x7fff.
+__device__ __forceinline__ uint32_t bf16x2_screen_flags(uint32_t u) {
+    const uint32_t m = u & 0x7fff7fffu;
+    return ((m + 0x36803680u) | (~(m + 0x62006200u) & (m + 0x7fff7fffu))) & 0x80008000u;
+}
+// (lo, hi) += (a_lo^2, a_hi^2) per lane, rounded toward +inf (fmaf_ru on each lane)
+__device__ __forceinline__ void sq_acc_ru2(uint64_t& acc, float lo, float hi) {
+    const uint64_t a = (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+    asm("fma.rp.f32x2 %0, %1, %1, %0;" : "+l"(acc) : "l"(a));
+}
+
 // Fused screen: 32 tokens per CTA, 4 warps.  The token rows and the router
 // rows ([E, H] BF16) stream through shared memory in 128-column chunks
 // (three cp.async stages, rows padded to 272 bytes so that ldmatrix is
@@ -2214,17 +2233,19 @@ constexpr int kScStages = 3;
 constexpr int kScPitch = kRouterKc + 8;  // BF16 elements per staged row (272 bytes)
 constexpr int kScMaxK = 8;
 
-// The interval ends use a float sigmoid: expf is within 2 ulp of e^x (CUDA's
-// documented bound) and the divisions are correctly rounded, so
-// |sig_screen(x) - sigma(x)| <= 2^-21; sigmoid_ref, the reference's float
-// evaluation, is within 2^-22 of sigma.  Widening by kSigMargin = 2^-19 and
-// adding the bias with outward rounding therefore keeps
-// [lo, hi] around fadd_rn(sigmoid_ref(l), bias) for every l in [la, ha]
-// (sigmoid_ref and round-to-nearest are non-decreasing).
+// The interval ends use a float sigmoid: expf is within 2 ulp of e^x and
+// __fdividef within 2 ulp of the quotient for a divisor in [1, 2] (CUDA's
+// documented bounds).  With z = e^-|x| <= 1: |z~ - z| <= 2^-22, the rounded
+// 1 + z~ adds 2^-24, and the quotient (at most 1) 2^-23, so
+// |sig_screen(x) - sigma(x)| <= 2^-22 + 2^-24 + 2^-23 < 2^-21; sigmoid_ref,
+// the reference's float evaluation, is within 2^-22 of sigma.  Widening by
+// kSigMargin = 2^-19 and adding the bias with outward rounding therefore
+// keeps [lo, hi] around fadd_rn(sigmoid_ref(l), bias) for every l in
+// [la, ha] (sigmoid_ref and round-to-nearest are non-decreasing).
 __device__ __forceinline__ float sig_screen(float x) {
     const float z = expf(-fabsf(x));
     const float d = __fadd_rn(1.f, z);
-    return x >= 0.f ? __fdiv_rn(1.f, d) : __fdiv_rn(z, d);
+    return __fdividef(x >= 0.f ? 1.f : z, d);
 }
 constexpr float kSigMargin = 1.9073486328125e-06f;  // 2^-19
 
@@ -2282,7 +2303,8 @@ __global__ void __launch_bounds__(kScThreads) route_screen_kernel(const __grid_c
     for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
     // thread -> token tid / 4 and quarter tid % 4 (norm: columns 32 q .. + 32 of each chunk)
     const int tl = threadIdx.x >> 2, tq = threadIdx.x & 3;
-    float ss0 = 0.f, ss1 = 0.f;
+    uint64_t ss2 = 0;  // (sum of the low halves' squares, of the high halves')
+    uint32_t badf = 0u;
     int bad = 0;
     if (threadIdx.x == 0) {
         issue(0);
@@ -2320,10 +2342,8 @@ __global__ void __launch_bounds__(kScThreads) route_screen_kernel(const __grid_c
                 const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    bad |= bf16_screen_unsafe(w4[j]) ? 1 : 0;
-                    const float a = bf16_lo(w4[j]), b = bf16_hi(w4[j]);
-                    ss0 = __fmaf_ru(a, a, ss0);
-                    ss1 = __fmaf_ru(b, b, ss1);
+                    badf |= bf16x2_screen_flags(w4[j]);
+                    sq_acc_ru2(ss2, bf16_lo(w4[j]), bf16_hi(w4[j]));
                 }
             }
         }
@@ -2360,7 +2380,8 @@ __global__ void __launch_bounds__(kScThreads) route_screen_kernel(const __grid_c
         r1[1] = acc[i][3];
     }
     // ||x_t||_2 over the four threads of a token, rounded up at every step
-    float ss = __fadd_ru(ss0, ss1);
+    bad |= badf != 0u ? 1 : 0;
+    float ss = __fadd_ru(__uint_as_float(static_cast<uint32_t>(ss2)), __uint_as_float(static_cast<uint32_t>(ss2 >> 32)));
     ss = __fadd_ru(ss, __shfl_xor_sync(0xffffffffu, ss, 1));
     ss = __fadd_ru(ss, __shfl_xor_sync(0xffffffffu, ss, 2));
     bad |= __shfl_xor_sync(0xffffffffu, bad, 1);
@@ -2378,6 +2399,7 @@ __global__ void __launch_bounds__(kScThreads) route_screen_kernel(const __grid_c
     float top[kScMaxK];
 #pragma unroll
     for (int i = 0; i < kScMaxK; ++i) top[i] = -INFINITY;
+#pragma unroll 4
     for (int j = 0; j < per; ++j) {
         const int e = tq * per + j;
         const float l = lrow[e];

@@ -761,9 +761,10 @@ int nf_moe_route(nf_moe* h, const uint16_t* x, int tokens, float* logits, int32_
 }  // extern "C"
 
 // The shared expert (mlp_bf16, src/text_forward.cpp:917-922) on the side
-// stream: it does not depend on routing, so it is forked from `s` and
-// overlaps the router, the permutation and the routed GEMMs (the GEMMs'
-// dynamic tile scheduler absorbs the SMs it holds).  Joined by ev_join.
+// stream: it does not depend on routing, so it is forked from `s` (before
+// or after the router, see forward_impl) and overlaps the rest of the layer
+// (the GEMMs' dynamic tile scheduler absorbs the SMs it holds).  Joined by
+// ev_join.
 int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cudaStream_t s) {
     const nf_moe_desc& d = h->d;
     const int H = d.hidden, Is = d.shared_inter;
@@ -1010,11 +1011,18 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     rec.h = h;
     rec.ev = h->prof_begin(&rec.set);
     int st = NF_OK;
-    if (Is > 0 && (st = launch_shared_expert(h, x, T, rec, s)) != NF_OK) return st;
+    // The shared expert forks before the router at decode sizes (the router
+    // is a few CTAs of latency-bound work that the shared GEMMs run beside);
+    // at prefill sizes the screened router fills the GPU and the shared
+    // GEMMs' persistent CTAs would hold its SMs, so they fork after it and run
+    // beside the permutation and the routed GEMMs instead.
+    const bool shared_first = !(h->screen && T >= kScreenMinTokens);
+    if (Is > 0 && shared_first && (st = launch_shared_expert(h, x, T, rec, s)) != NF_OK) return st;
     rec.begin(NF_STAGE_ROUTER, s);
     cudaError_t e = route_tokens(h, x, T, idx, w, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "router launch");
     rec.end(NF_STAGE_ROUTER, s);
+    if (Is > 0 && !shared_first && (st = launch_shared_expert(h, x, T, rec, s)) != NF_OK) return st;
     if ((st = launch_routed_experts(h, x, idx, T, K, rec, s)) != NF_OK) return st;
     if (Is > 0 && (e = cudaStreamWaitEvent(s, h->ev_join, 0)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
     rec.begin(NF_STAGE_COMBINE, s);
