@@ -1880,6 +1880,9 @@ constexpr int kExWarps = kExThreads / 32;
 constexpr int kExSlots = 4;
 constexpr int kExStages = 3;
 constexpr int kExMaxK = 8;  // picks per token (the screened path serves K <= 8)
+// The stages are issued by lane 0 of the last warp: chains fill the threads
+// from 0 up, so that warp computes only for long lists.
+constexpr int kExIssuer = kExThreads - 32;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
@@ -1959,19 +1962,13 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * kExTok;
     const int ntok = min(kExTok, T - t0);
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < kExStages; ++i) mbar_init(&full[i], 1);
-        s_abort = 0;
-        fence_barrier_init();
-        prefetch_tensormap(&tmx);
-    }
     if (threadIdx.x < ntok) prefetch_l2_bulk(x + static_cast<int64_t>(t0 + threadIdx.x) * H, static_cast<uint32_t>(H) * 2u);
     const int nchunks = H / kRouterKc;
     // Chunk g of the staging sequence (all passes) lands in buffer g % stages
     // with barrier parity (g / stages) & 1: the router rows of the chunk as
     // one bulk copy (the chunk-major copy keeps a chunk's rows contiguous, in
     // the staged pitch) and the tokens' columns as two TMA boxes (rows past
-    // the batch read as zeros).  Thread 0 issues.
+    // the batch read as zeros).
     const uint32_t wbytes = static_cast<uint32_t>(wchunk) * 2u;
     auto issue = [&](int c, int g) {
         const int buf = g % kExStages;
@@ -1981,7 +1978,13 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
         tma_load_2d(sx + buf * kRtXStage + kRtXStage / 2, &tmx, &full[buf], c * kRouterKc + 64, t0);
     };
     // the first pass's first two chunks go out before the chain list is built
-    if (threadIdx.x == 0) {
+    // (the issuing thread initialises the barriers; the others first touch
+    // them after the __syncthreads below)
+    if (threadIdx.x == kExIssuer) {
+        for (int i = 0; i < kExStages; ++i) mbar_init(&full[i], 1);
+        s_abort = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&tmx);
         issue(0, 0);
         if (nchunks > 1) issue(1, 1);
     }
@@ -2061,7 +2064,7 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
                 all_fma = all_fma && __all_sync(0xffffffffu, fm[j]);
             }
         }
-        if (threadIdx.x == 0 && p0 > 0) {
+        if (threadIdx.x == kExIssuer && p0 > 0) {
             issue(0, staged);
             if (nchunks > 1) issue(1, staged + 1);
         }
@@ -2087,7 +2090,7 @@ __global__ void __launch_bounds__(kExThreads, 2) route_exact_kernel(
                 __syncthreads();
                 return;
             }
-            if (threadIdx.x == 0 && c + 2 < nchunks) issue(c + 2, g + 2);
+            if (threadIdx.x == kExIssuer && c + 2 < nchunks) issue(c + 2, g + 2);
             const uint16_t* wb = sw + buf * wchunk;
             const uint16_t* xb = sx + buf * kRtXStage;
             if (all_fma) {
