@@ -361,7 +361,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 issued[stage] = true;
                 issued_parity[stage] = phase;
                 if (++stage == STAGES) stage = 0, phase ^= 1u;
-                if (lane == 0 && kt == max(t.kt0, t.kt1 - 3)) next = atomicAdd(args.tile_counter, 1);
+                // (with the fused split-K reduction a CTA takes one tile only: its
+                // epilogue waits for the tile's other K slices, which must not sit
+                // behind it in this CTA's own pipeline)
+                if (lane == 0 && kt == max(t.kt0, t.kt1 - 3))
+                    next = args.splitk_fuse ? num_tiles : atomicAdd(args.tile_counter, 1);
                 if (lane == 0 && kt == t.kt1 - 1 && next < num_tiles) next_t = get_tile(args, next, k_tiles, TM);
             }
             first_tile = false;
@@ -557,12 +561,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // (a tile of at most 32 rows has them in TMEM lane quadrant 0 only:
             // its four warps take the tile's columns, the others idle)
-            const int row = t.row0 + r;
-            const bool valid = r < t.m_valid;
-            const bool warp_live = q * 32 < t.m_valid;  // some row of this warp belongs to the expert
+            // rep64 (dense NVFP4 gate/up of 33-64 rows): the tile's rows 64-127
+            // repeat rows 0-63, so quadrants 2 and 3 hold the accumulators of 0
+            // and 1 again; a warp of quadrant q then stores rows (q & 1) * 32 +
+            // lane and takes the 16-column half q >> 1 of its slice, and all
+            // sixteen warps share the epilogue
+            const bool rep = EPI == EPI_SWIGLU_QUANT && args.rep64 != 0;
+            const int rr = rep ? (q & 1) * 32 + lane : r;
+            const int hg = rep ? (q >> 1) : 0;
+            const int row = t.row0 + rr;
+            const bool valid = rr < t.m_valid;
+            const bool warp_live = rr - lane < t.m_valid;  // some row of this warp belongs to the expert
             uint32_t v[64];
             if (warp_live) {
-                if (EPI == EPI_SWIGLU_QUANT || EPI == EPI_SWIGLU_BF16) {
+                if (EPI == EPI_SWIGLU_QUANT && rep) {
+                    // gate columns [32cs + 16hg, +16), up columns 128 further
+                    tmem_ld16(tbase + 32 * cs + 16 * hg, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                    tmem_ld16(tbase + 128 + 32 * cs + 16 * hg, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
+                } else if (EPI == EPI_SWIGLU_QUANT || EPI == EPI_SWIGLU_BF16) {
                     // gate columns [32cs, 32cs+32), up columns 128 further
                     tmem_ld16(tbase + 32 * cs, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
                     tmem_ld16(tbase + 32 * cs + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
@@ -599,6 +615,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float gsd = args.gscale_next[t.expert], L = args.limit;
                 const bool sbf = args.swiglu_bf16 != 0;
                 const float* os_tab = args.os_table ? args.os_table + 256 * t.expert : nullptr;
+                if (rep) {
+                    uint32_t c1[2];
+                    const uint32_t s1 = swiglu_quant_group(&v[0], &v[32], ag, au, gsd, L, sbf, os_tab, c1);
+                    if (valid) {
+                        uint8_t* o = static_cast<uint8_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
+                                     t.n_block * 64 + cs * 16 + 8 * hg;
+                        *reinterpret_cast<uint2*>(o) = make_uint2(c1[0], c1[1]);
+                        args.out_sf[sf_atom_offset(row, t.n_block * 8 + cs * 2 + hg, args.out_kgroups)] =
+                            static_cast<uint8_t>(s1);
+                    }
+                } else {
                 uint32_t cc[2][2];
                 uint32_t sc[2];
 #pragma unroll
@@ -610,6 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<uint4*>(o) = make_uint4(cc[0][0], cc[0][1], cc[1][0], cc[1][1]);
                     *reinterpret_cast<uint16_t*>(args.out_sf + sf_atom_offset(row, t.n_block * 8 + cs * 2, args.out_kgroups)) =
                         static_cast<uint16_t>(sc[0] | (sc[1] << 8));
+                }
                 }
             } else if (EPI == EPI_STORE_BF16) {
                 const float a = args.alpha0[t.expert];
@@ -648,6 +676,51 @@ __global__ void __launch_bounds__(kThreads, 1)
                         __threadfence();
                         fence_proxy_async_global();
                         atomicAdd(args.mt_done + t.row0 / BM, 1);
+                    }
+                }
+            }
+            if (EPI == EPI_STORE_F32 && args.splitk_fuse) {
+                // Fused split-K reduction: count this slice once every warp's
+                // stores are out, wait for the tile's other slices (their CTAs
+                // are all running: one tile per CTA), then sum this slice's share
+                // of the tile's rows over the slices in order.
+                named_bar_sync(2, 32 * kEpiWarps);
+                if (leader) {
+                    int* cnt = args.splitk_cnt + (t.row0 / BM) * args.n_blocks + t.n_block;
+                    __threadfence();
+                    atomicAdd(cnt, 1);
+                    if (!wait_count(cnt, args.k_split, cta_abort, dev_err)) set_abort(cta_abort, args.err, NF_DEVERR_WAIT_FULL);
+                    __threadfence();
+                }
+                named_bar_sync(2, 32 * kEpiWarps);
+                if (*cta_abort == 0) {
+                    const int S = args.k_split;
+                    const int per = (t.m_valid + S - 1) / S;
+                    const int r0 = min(t.m_valid, t.ks * per), r1 = min(t.m_valid, r0 + per);
+                    const float a = args.alpha0[0];
+                    const int nq = (r1 - r0) * (BN / 4);
+                    for (int u = (warp - 2) * 32 + lane; u < nq; u += 32 * kEpiWarps) {
+                        const int64_t off = static_cast<int64_t>(t.row0 + r0 + u / (BN / 4)) * args.out_ld +
+                                            t.n_block * BN + 4 * (u % (BN / 4));
+                        const float* part = static_cast<const float*>(args.out);
+                        float4 acc = *reinterpret_cast<const float4*>(part + off);
+                        for (int s2 = 1; s2 < S; ++s2) {
+                            const float4 v = *reinterpret_cast<const float4*>(part + s2 * args.out_split_stride + off);
+                            acc.x = __fadd_rn(acc.x, v.x);
+                            acc.y = __fadd_rn(acc.y, v.y);
+                            acc.z = __fadd_rn(acc.z, v.z);
+                            acc.w = __fadd_rn(acc.w, v.w);
+                        }
+                        float4 o = make_float4(bf16_round_hw(__fmul_rn(acc.x, a)), bf16_round_hw(__fmul_rn(acc.y, a)),
+                                               bf16_round_hw(__fmul_rn(acc.z, a)), bf16_round_hw(__fmul_rn(acc.w, a)));
+                        if (args.residual) {
+                            const float4 r = *reinterpret_cast<const float4*>(args.residual + off);
+                            o.x = __fadd_rn(o.x, r.x);
+                            o.y = __fadd_rn(o.y, r.y);
+                            o.z = __fadd_rn(o.z, r.z);
+                            o.w = __fadd_rn(o.w, r.w);
+                        }
+                        *reinterpret_cast<float4*>(args.y + off) = o;
                     }
                 }
             }

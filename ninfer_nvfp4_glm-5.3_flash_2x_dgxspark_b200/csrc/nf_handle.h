@@ -95,6 +95,8 @@ struct nf_moe {
     float* dense_w = nullptr;        // [Tm] ones: the pick's combine weight
     float* dense_part = nullptr;     // split-K partial sums of the down projection (small batches)
     int64_t dense_part_elems = 0;
+    int* splitk_cnt = nullptr;       // [m tiles][H / 256] slices stored per down tile (fused reduction)
+    int splitk_cnt_elems = 0;
     int ep_rank = 0, ep_world = 1, ep_base = 0, ep_local = 0;
     nf_moe* inner = nullptr;
     void* nccl = nullptr;            // ncclComm_t of the group
@@ -250,9 +252,13 @@ int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cud
 // batches when the handle has one, else the full exact router.
 cudaError_t route_tokens(nf_moe* h, const uint16_t* x, int T, int32_t* idx, float* w, cudaStream_t s);
 // down_split > 1 (dense handles): the down GEMM runs as a dense split-K GEMM
-// into h->dense_part (down_split K slices) instead of writing h->down.
+// into h->dense_part (down_split K slices) instead of writing h->down; when
+// dense_splitk_fused(), it also reduces the slices into y (+ residual).
 int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int T, int K, StageRec& rec,
-                          cudaStream_t s, int down_split = 1);
+                          cudaStream_t s, int down_split = 1, const float* residual = nullptr, float* y = nullptr);
+// The dense split-K down GEMM reduces its slices itself when every tile gets
+// its own CTA (so all slices of a tile run together).
+bool dense_splitk_fused(const nf_moe* h, int T, int down_split);
 // nf_ep.cu
 int ep_forward(nf_moe* h, const uint16_t* x, const float* residual, int T, float* y, int32_t* idx, float* w,
                cudaStream_t s);

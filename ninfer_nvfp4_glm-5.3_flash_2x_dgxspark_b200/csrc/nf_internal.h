@@ -66,6 +66,19 @@ struct GemmArgs {
     int kt_per;
     int m_pair;                // dense BF16 only: 256-row tiles (two 128-row accumulators)
     int64_t out_split_stride;  // elements
+    // Split K with the reduction fused (every tile on its own CTA, so all of a
+    // tile's slices are in flight together): after storing its slice a CTA
+    // counts it in splitk_cnt[m tile * n_blocks + n block] (zeroed before the
+    // launch), waits until all k_split are stored, then sums its share of the
+    // tile's rows over the slices in order into y: bf16(alpha0[0] * sum) +
+    // residual (residual may be NULL) -- the reduction kernel's arithmetic.
+    int splitk_fuse;
+    int* splitk_cnt;
+    // EPI_SWIGLU_QUANT over dense rows 33-64: A's rows 64-127 repeat rows 0-63
+    // (the dispatch writes each token twice), so every epilogue warp has rows
+    int rep64;
+    const float* residual;
+    float* y;
     // NVFP4 scale-factor atoms: sfa [128-row block][K/64 atoms]; sfb in tile
     // order, one 4 KB group per (expert, n block, K stage): [2 row halves][4 atoms]
     const uint8_t* sfa;
@@ -209,7 +222,7 @@ inline void router_chunked_layout16(const uint16_t* w, int E, int H, uint16_t* o
 // The dense MLP's dispatch (rows = tokens, no permutation; resets the GEMMs'
 // tile and hand-off counters).
 cudaError_t launch_dense_dispatch(const uint16_t* x, int T, int H, const float* gscale, PermuteBuffers& b,
-                                  cudaStream_t st);
+                                  int* splitk_cnt, int n_splitk_cnt, bool rep64, cudaStream_t st);
 cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
                            const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st, bool* one_kernel);
 cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair_row, const float* topk_w,

@@ -1128,34 +1128,40 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
 // The dense MLP's dispatch: its rows are the tokens in order (one segment at
 // row 0, no permutation), so it quantises token t into row t with the one
 // gate input scale, writes the identity pick -> row map for the combine, and
-// block 0 zeroes the GEMMs' tile counters (meta[4..5])
+// block 0 zeroes the GEMMs' tile counters (meta[4..5]), the fused split-K
+// reduction's slice counters; with rep64 (T <= 64) token t is also written to
+// row t + 64
 // and the per-128-row hand-off counters the permutation would otherwise reset.
 __global__ void dense_dispatch_kernel(const uint16_t* __restrict__ x, int T, int H, const float* __restrict__ gscale,
                                       uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
                                       int32_t* __restrict__ pair_row, int32_t* __restrict__ meta,
-                                      int32_t* __restrict__ mt_done, int m_tiles) {
+                                      int32_t* __restrict__ mt_done, int m_tiles, int* __restrict__ splitk_cnt,
+                                      int n_splitk_cnt, int rep64) {
     pdl_wait();  // launched dependent on the previous kernel
     pdl_trigger();
     if (blockIdx.x == 0) {
         if (threadIdx.x < 2) meta[4 + threadIdx.x] = 0;
         for (int i = threadIdx.x; i < m_tiles; i += blockDim.x) mt_done[i] = 0;
+        for (int i = threadIdx.x; i < n_splitk_cnt; i += blockDim.x) splitk_cnt[i] = 0;
     }
     const int gq = H / 16;
     const int64_t item = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
     if (item >= static_cast<int64_t>(T) * gq) return;
     const int t = static_cast<int>(item / gq), g = static_cast<int>(item - static_cast<int64_t>(t) * gq);
-    const int32_t e0 = 0, row = t;
+    const int32_t e0 = 0, row = t, row2 = t + 64;
     if (g == 0) pair_row[t] = t;  // the combine's pick -> row map
     dispatch_token_group(x, t, g, 1, &e0, &row, gscale, H, 0, a_codes, a_sf, nullptr);
+    if (rep64) dispatch_token_group(x, t, g, 1, &e0, &row2, gscale, H, 0, a_codes, a_sf, nullptr);
 }
 
 cudaError_t launch_dense_dispatch(const uint16_t* x, int T, int H, const float* gscale, PermuteBuffers& b,
-                                  cudaStream_t st) {
+                                  int* splitk_cnt, int n_splitk_cnt, bool rep64, cudaStream_t st) {
+    if (rep64 && T > 64) return cudaErrorInvalidValue;
     const int64_t items = static_cast<int64_t>(T) * (H / 16);
     const int m_tiles = (T + 127) / 128;
     return launch_dependent(dense_dispatch_kernel, dim3(static_cast<unsigned>(std::max<int64_t>(1, (items + 127) / 128))),
                             dim3(128), 0, st, x, T, H, gscale, b.a_codes, b.a_sf, b.pair_row, b.meta, b.mt_done,
-                            m_tiles);
+                            m_tiles, splitk_cnt, splitk_cnt ? n_splitk_cnt : 0, rep64 ? 1 : 0);
 }
 
 // Permutation and dispatch of a small batch (T * K <= kSmallPairs) in one

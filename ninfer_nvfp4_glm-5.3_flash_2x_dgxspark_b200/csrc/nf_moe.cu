@@ -390,6 +390,8 @@ int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::s
         }
         h->dense_part_elems = part;
         if (part > 0) ok = ok && h->alloc(&h->dense_part, part);
+        h->splitk_cnt_elems = static_cast<int>((Tm + 127) / 128 * (H / 256));
+        ok = ok && h->alloc(&h->splitk_cnt, h->splitk_cnt_elems);
     }
     if (!ok) {
         cudaGetLastError();
@@ -822,8 +824,14 @@ int launch_shared_expert(nf_moe* h, const uint16_t* x, int T, StageRec& rec, cud
 // GEMM (SwiGLU and the down input's quantisation fused), grouped down GEMM.
 // The down rows land in h->down in permuted order (h->pb.pair_row maps a
 // pick to its row).
+bool dense_splitk_fused(const nf_moe* h, int T, int down_split) {
+    // (NVFP4 dense handles: their dispatch zeroes the slice counters)
+    return down_split > 1 && h->dense && h->d.expert_kind == NF_EXPERTS_NVFP4 &&
+           static_cast<int64_t>((T + 127) / 128) * (h->d.hidden / 256) * down_split <= static_cast<int64_t>(h->grid);
+}
+
 int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int T, int K, StageRec& rec,
-                          cudaStream_t s, int down_split) {
+                          cudaStream_t s, int down_split, const float* residual, float* y) {
     const nf_moe_desc& d = h->d;
     const int H = d.hidden, E = d.experts, I = d.inter;
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
@@ -833,8 +841,11 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     // The dense MLP (every token on expert 0) skips the permutation: its rows
     // are the tokens in order, and both GEMMs run dense tiles over them.
     const bool dense_rows = h->dense && fp4;
+    // 33-64 tokens fill two of the four TMEM lane quadrants of the gate/up
+    // tile: repeat them in the other two so all the epilogue warps work
+    const bool rep64 = dense_rows && T > 32 && T <= 64;
     if (dense_rows) {
-        e = launch_dense_dispatch(x, T, H, h->gs_g, h->pb, s);
+        e = launch_dense_dispatch(x, T, H, h->gs_g, h->pb, h->splitk_cnt, h->splitk_cnt_elems, rep64, s);
         one_kernel = true;
     } else {
         e = launch_permute(idx, x, T, K, E, H, I / 128, H / 256, h->gs_g, fp4 ? 0 : 1, h->pb, s, &one_kernel);
@@ -883,6 +894,7 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
         g.num_tiles_dev = nullptr;
         g.k_split = 1;
         g.row_token = nullptr;
+        g.rep64 = rep64 ? 1 : 0;
     }
     // Prefill-sized batches (on average a pair tile's 256 rows per expert or
     // more) may take the alternative GEMM forms (nf_moe_set_expert_gemm)
@@ -919,6 +931,7 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.mt_signal = 0;
     g.mt_wait = handoff ? I / 128 : 0;
     g.early_claim = 1;
+    g.rep64 = 0;
     if (dense_rows) {
         g.dense_rows = T;
         g.tiles = nullptr;
@@ -940,6 +953,12 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
         g.out = h->dense_part;
         g.out_ld = H;
         g.out_split_stride = stride;
+        if (dense_splitk_fused(h, T, S)) {
+            g.splitk_fuse = 1;
+            g.splitk_cnt = h->splitk_cnt;
+            g.residual = residual;
+            g.y = y;
+        }
     }
     e = pair ? launch_gemm2(h->tm_h, h->tm_b_dn_half, h->tm_sfa_h, h->tm_sfb_dn, g, h->grid2, true, s)
         : wide ? launch_gemm(h->tm_h3, h->tm_h3, h->tm_b_dn3, g, h->grid, true, s)
@@ -959,8 +978,10 @@ static int dense_forward(nf_moe* h, const uint16_t* x, const float* residual, in
     const int H = h->d.hidden;
     int kt_per = 0;
     const int S = dense_down_split(T, H, h->d.inter, h->grid, &kt_per);
-    int st = launch_routed_experts(h, x, h->dense_idx, T, 1, rec, s, S);
+    const bool fused = dense_splitk_fused(h, T, S);
+    int st = launch_routed_experts(h, x, h->dense_idx, T, 1, rec, s, S, residual, y);
     if (st != NF_OK) return st;
+    if (fused) return NF_OK;  // the down GEMM reduced its K slices into y
     rec.begin(NF_STAGE_COMBINE, s);
     const cudaError_t e =
         S > 1 ? launch_splitk_store(h->dense_part, S, static_cast<int64_t>((T + 127) / 128) * 128 * H, T, H, h->alpha_d,

@@ -36,10 +36,13 @@ def gpu_forward(mlp, x_bits, residual=None):
 
 
 # (256, 512): K too short to split; (256, 2048): the down projection split
-# into K slices (tiles of <= 32 rows at T = 16, two ragged row blocks at
-# T = 200); (2048, 10240): the benchmark's dense layers at the decode batch
-# (14 K slices)
-@pytest.mark.parametrize("hidden,inter,T", [(256, 512, 16), (256, 2048, 16), (256, 2048, 200), (2048, 10240, 64)])
+# into K slices and reduced inside the down GEMM (tiles of <= 32 rows at
+# T = 16, two ragged row blocks at T = 200; at T = 48 the gate/up tile's rows
+# repeated in the upper TMEM lane quadrants, rows 48-63 of each copy empty);
+# (2048, 10240): the benchmark's dense layers at the decode batch (14 K
+# slices, 64 rows repeated)
+@pytest.mark.parametrize("hidden,inter,T", [(256, 512, 16), (256, 2048, 16), (256, 2048, 48), (256, 2048, 200),
+                                            (2048, 10240, 64)])
 def test_dense_against_oracle(hidden, inter, T):
     lay, mlp = make(hidden, inter, T)
     x_bits = tokens(hidden, T)
