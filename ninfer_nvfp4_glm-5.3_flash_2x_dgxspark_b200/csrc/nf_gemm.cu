@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             num_tiles = args.dense_rows > 0 ? ((args.dense_rows + TM - 1) / TM) * args.n_blocks * max(1, args.k_split)
                                             : *args.num_tiles_dev;
             if (lane == 0) {
-                next = atomicAdd(args.tile_counter, 1);
+                next = args.static_tiles ? static_cast<int>(blockIdx.x) : atomicAdd(args.tile_counter, 1);
                 if (next < num_tiles) next_t = get_tile(args, next, k_tiles, TM);
             }
         };
@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // epilogue waits for the tile's other K slices, which must not sit
                 // behind it in this CTA's own pipeline)
                 if (lane == 0 && kt == max(t.kt0, t.kt1 - 3))
-                    next = args.splitk_fuse ? num_tiles : atomicAdd(args.tile_counter, 1);
+                    next = (args.splitk_fuse || args.static_tiles) ? num_tiles : atomicAdd(args.tile_counter, 1);
                 if (lane == 0 && kt == t.kt1 - 1 && next < num_tiles) next_t = get_tile(args, next, k_tiles, TM);
             }
             first_tile = false;

@@ -77,6 +77,10 @@ struct GemmArgs {
     // EPI_SWIGLU_QUANT over dense rows 33-64: A's rows 64-127 repeat rows 0-63
     // (the dispatch writes each token twice), so every epilogue warp has rows
     int rep64;
+    // Dense tiles with a CTA each (grid >= tiles): CTA b takes tile b and no
+    // other, without the tile counter, so it may claim it (and issue its
+    // first B stages) before the previous kernel completes
+    int static_tiles;
     const float* residual;
     float* y;
     // NVFP4 scale-factor atoms: sfa [128-row block][K/64 atoms]; sfb in tile

@@ -895,6 +895,12 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
         g.k_split = 1;
         g.row_token = nullptr;
         g.rep64 = rep64 ? 1 : 0;
+        // a CTA per tile: claimed by block index before the dispatch completes,
+        // so the first B stages stream while it runs
+        if (static_cast<int64_t>((T + 127) / 128) * (I / 128) <= h->grid) {
+            g.static_tiles = 1;
+            g.early_claim = 1;
+        }
     }
     // Prefill-sized batches (on average a pair tile's 256 rows per expert or
     // more) may take the alternative GEMM forms (nf_moe_set_expert_gemm)
@@ -932,6 +938,7 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.mt_wait = handoff ? I / 128 : 0;
     g.early_claim = 1;
     g.rep64 = 0;
+    g.static_tiles = 0;
     if (dense_rows) {
         g.dense_rows = T;
         g.tiles = nullptr;
@@ -955,6 +962,7 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
         g.out_split_stride = stride;
         if (dense_splitk_fused(h, T, S)) {
             g.splitk_fuse = 1;
+            g.static_tiles = 1;
             g.splitk_cnt = h->splitk_cnt;
             g.residual = residual;
             g.y = y;
