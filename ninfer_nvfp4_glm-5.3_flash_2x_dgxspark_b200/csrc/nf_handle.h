@@ -52,6 +52,7 @@ struct nf_moe {
     float* gs_g = nullptr;          // [E] 1 / input_scale
     float* gs_d = nullptr;
     float* os_tab = nullptr;  // [E][256] the down input quantiser's output scale per scale code
+    float* os_tab_g = nullptr;  // [E][256] the same for the gate/up input (the dispatch's quantiser)
     std::vector<float> h_alpha_g, h_alpha_u, h_alpha_d, h_in_g, h_in_u, h_in_d;
     std::vector<uint8_t> bound;     // [E * 3] expert projection bound flags
     bool router_bound = false, bias_bound = false, sg_bound = false, su_bound = false, sd_bound = false;

@@ -225,10 +225,13 @@ inline void router_chunked_layout16(const uint16_t* w, int E, int H, uint16_t* o
 // pdl_wait().
 // The dense MLP's dispatch (rows = tokens, no permutation; resets the GEMMs'
 // tile and hand-off counters).
-cudaError_t launch_dense_dispatch(const uint16_t* x, int T, int H, const float* gscale, PermuteBuffers& b,
-                                  int* splitk_cnt, int n_splitk_cnt, bool rep64, cudaStream_t st);
+cudaError_t launch_dense_dispatch(const uint16_t* x, int T, int H, const float* gscale, const float* os_tab_g,
+                                  PermuteBuffers& b, int* splitk_cnt, int n_splitk_cnt, bool rep64, cudaStream_t st);
+// os_tab_g: [E][256] the NVFP4 activation quantiser's output scale per E4M3
+// scale code for each expert's gate input scale (NULL: computed per group).
 cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
-                           const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st, bool* one_kernel);
+                           const float* gscale, const float* os_tab_g, int bf16_mode, PermuteBuffers& b, cudaStream_t st,
+                           bool* one_kernel);
 cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair_row, const float* topk_w,
                            const float* shared, const float* residual, int T, int K, int H, float* y,
                            cudaStream_t st);

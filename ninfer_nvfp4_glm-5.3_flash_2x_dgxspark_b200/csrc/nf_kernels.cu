@@ -6,6 +6,7 @@
 // use plain coalesced loads, shared-memory staging and grids sized from the
 // SM count.  The contractions live in nf_gemm.cu.
 #include "nf_common.cuh"
+#include "nf_gemm_shared.cuh"
 #include "nf_internal.h"
 
 #include "_gen/sigmoid_table.inc"
@@ -1071,7 +1072,8 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const int32_t* __rest
 __device__ __forceinline__ void dispatch_token_group(const uint16_t* __restrict__ x, int t, int g, int K,
                                                      const int32_t* __restrict__ pick_e,
                                                      const int32_t* __restrict__ pick_row,
-                                                     const float* __restrict__ gscale, int H, int bf16_mode,
+                                                     const float* __restrict__ gscale,
+                                                     const float* __restrict__ os_tab_g, int H, int bf16_mode,
                                                      uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
                                                      uint16_t* __restrict__ a_bf16) {
     const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * H + g * 16);
@@ -1102,7 +1104,9 @@ __device__ __forceinline__ void dispatch_token_group(const uint16_t* __restrict_
             float w[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) w[j] = v[j];
-            sf = quantize_group16_fast<true>(w, gs, codes);
+            // (the expert's table of output scales per scale code, when given:
+            // the same values without the three divisions)
+            sf = os_tab_g ? quantize_group16_tab(w, gs, os_tab_g + 256 * e, codes) : quantize_group16_fast<true>(w, gs, codes);
             have = gs;
         }
         *reinterpret_cast<uint2*>(a_codes + static_cast<int64_t>(row) * (H / 2) + g * 8) = make_uint2(codes[0], codes[1]);
@@ -1111,7 +1115,8 @@ __device__ __forceinline__ void dispatch_token_group(const uint16_t* __restrict_
 }
 
 __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ idx,
-                                const int32_t* __restrict__ pair_row, const float* __restrict__ gscale, int T, int K,
+                                const int32_t* __restrict__ pair_row, const float* __restrict__ gscale,
+                                const float* __restrict__ os_tab_g, int T, int K,
                                 int H, int bf16_mode, uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
                                 uint16_t* __restrict__ a_bf16) {
     pdl_wait();  // launched dependent on the previous kernel
@@ -1121,7 +1126,7 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
     if (item >= static_cast<int64_t>(T) * gq) return;
     const int64_t t = item / gq;
     const int g = static_cast<int>(item - t * gq);
-    dispatch_token_group(x, static_cast<int>(t), g, K, idx + t * K, pair_row + t * K, gscale, H,
+    dispatch_token_group(x, static_cast<int>(t), g, K, idx + t * K, pair_row + t * K, gscale, os_tab_g, H,
                          bf16_mode, a_codes, a_sf, a_bf16);
 }
 
@@ -1133,6 +1138,7 @@ __global__ void dispatch_kernel(const uint16_t* __restrict__ x, const int32_t* _
 // row t + 64
 // and the per-128-row hand-off counters the permutation would otherwise reset.
 __global__ void dense_dispatch_kernel(const uint16_t* __restrict__ x, int T, int H, const float* __restrict__ gscale,
+                                      const float* __restrict__ os_tab_g,
                                       uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf,
                                       int32_t* __restrict__ pair_row, int32_t* __restrict__ meta,
                                       int32_t* __restrict__ mt_done, int m_tiles, int* __restrict__ splitk_cnt,
@@ -1150,17 +1156,17 @@ __global__ void dense_dispatch_kernel(const uint16_t* __restrict__ x, int T, int
     const int t = static_cast<int>(item / gq), g = static_cast<int>(item - static_cast<int64_t>(t) * gq);
     const int32_t e0 = 0, row = t, row2 = t + 64;
     if (g == 0) pair_row[t] = t;  // the combine's pick -> row map
-    dispatch_token_group(x, t, g, 1, &e0, &row, gscale, H, 0, a_codes, a_sf, nullptr);
-    if (rep64) dispatch_token_group(x, t, g, 1, &e0, &row2, gscale, H, 0, a_codes, a_sf, nullptr);
+    dispatch_token_group(x, t, g, 1, &e0, &row, gscale, os_tab_g, H, 0, a_codes, a_sf, nullptr);
+    if (rep64) dispatch_token_group(x, t, g, 1, &e0, &row2, gscale, os_tab_g, H, 0, a_codes, a_sf, nullptr);
 }
 
-cudaError_t launch_dense_dispatch(const uint16_t* x, int T, int H, const float* gscale, PermuteBuffers& b,
-                                  int* splitk_cnt, int n_splitk_cnt, bool rep64, cudaStream_t st) {
+cudaError_t launch_dense_dispatch(const uint16_t* x, int T, int H, const float* gscale, const float* os_tab_g,
+                                  PermuteBuffers& b, int* splitk_cnt, int n_splitk_cnt, bool rep64, cudaStream_t st) {
     if (rep64 && T > 64) return cudaErrorInvalidValue;
     const int64_t items = static_cast<int64_t>(T) * (H / 16);
     const int m_tiles = (T + 127) / 128;
     return launch_dependent(dense_dispatch_kernel, dim3(static_cast<unsigned>(std::max<int64_t>(1, (items + 127) / 128))),
-                            dim3(128), 0, st, x, T, H, gscale, b.a_codes, b.a_sf, b.pair_row, b.meta, b.mt_done,
+                            dim3(128), 0, st, x, T, H, gscale, os_tab_g, b.a_codes, b.a_sf, b.pair_row, b.meta, b.mt_done,
                             m_tiles, splitk_cnt, splitk_cnt ? n_splitk_cnt : 0, rep64 ? 1 : 0);
 }
 
@@ -1171,7 +1177,8 @@ cudaError_t launch_dense_dispatch(const uint16_t* x, int T, int H, const float* 
 // pick) and quantises its share of the dispatch items.
 __global__ void __launch_bounds__(256) permute_dispatch_kernel(
     const int32_t* __restrict__ idx, const uint16_t* __restrict__ x, int T, int K, int E, int H, int nb_gu, int nb_down,
-    const float* __restrict__ gscale, int bf16_mode, int32_t* __restrict__ counts, int32_t* __restrict__ seg_off,
+    const float* __restrict__ gscale, const float* __restrict__ os_tab_g, int bf16_mode, int32_t* __restrict__ counts,
+    int32_t* __restrict__ seg_off,
     int32_t* __restrict__ pair_row, int32_t* __restrict__ row_token, NfTile* __restrict__ tiles_gu,
     NfTile* __restrict__ tiles_down, int32_t* __restrict__ meta, int32_t* __restrict__ mt_done,
     uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_sf, uint16_t* __restrict__ a_bf16) {
@@ -1221,7 +1228,7 @@ __global__ void __launch_bounds__(256) permute_dispatch_kernel(
     const int gq = H / 16;
     for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < n * gq; item += gridDim.x * blockDim.x) {
         const int pair = item / gq, g = item - pair * gq;
-        dispatch_token_group(x, pair / K, g, 1, s_idx + pair, s_row + pair, gscale, H, bf16_mode,
+        dispatch_token_group(x, pair / K, g, 1, s_idx + pair, s_row + pair, gscale, os_tab_g, H, bf16_mode,
                              a_codes, a_sf, a_bf16);
     }
 }
@@ -1423,14 +1430,15 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* w, const float* w_c
 }
 
 cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, int E, int H, int nb_gu, int nb_down,
-                           const float* gscale, int bf16_mode, PermuteBuffers& b, cudaStream_t st, bool* one_kernel) {
+                           const float* gscale, const float* os_tab_g, int bf16_mode, PermuteBuffers& b, cudaStream_t st,
+                           bool* one_kernel) {
     const size_t small_smem = (3 * E + 2 + 2 * T * K + static_cast<size_t>(E) * ((T + 31) / 32)) * sizeof(int32_t);
     if (T * K <= kSmallPairs && small_smem <= 48 * 1024) {
         const int64_t items = static_cast<int64_t>(T) * K * (H / 16);
         const int blocks = static_cast<int>(std::min<int64_t>(256, (items + 255) / 256));
         *one_kernel = true;
         return launch_dependent(permute_dispatch_kernel, dim3(blocks), dim3(256), small_smem, st, idx, x, T, K, E, H,
-                                nb_gu, nb_down, gscale, bf16_mode, b.counts, b.seg_off, b.pair_row, b.row_token,
+                                nb_gu, nb_down, gscale, os_tab_g, bf16_mode, b.counts, b.seg_off, b.pair_row, b.row_token,
                                 b.tiles_gu, b.tiles_down, b.meta, b.mt_done, b.a_codes, b.a_sf, b.a_bf16);
     } else {
         *one_kernel = false;
@@ -1450,7 +1458,7 @@ cudaError_t launch_permute(const int32_t* idx, const uint16_t* x, int T, int K, 
     }
     const int64_t items = static_cast<int64_t>(T) * (H / 16);
     return launch_dependent(dispatch_kernel, dim3(static_cast<unsigned>((items + 127) / 128)), dim3(128), 0, st, x, idx,
-                            static_cast<const int32_t*>(b.pair_row), gscale, T, K, H, bf16_mode, b.a_codes, b.a_sf,
+                            static_cast<const int32_t*>(b.pair_row), gscale, os_tab_g, T, K, H, bf16_mode, b.a_codes, b.a_sf,
                             b.a_bf16);
 }
 

@@ -349,7 +349,8 @@ int create_impl(const nf_moe_desc& d, int device, int role, nf_moe** out, std::s
     }
     if (Is > 0) ok = ok && h->alloc(&h->ws_gu, blocked_bytes(2 * Is, 2 * H) / 2) && h->alloc(&h->ws_dn, blocked_bytes(H, 2 * Is) / 2);
     ok = ok && h->alloc(&h->alpha_g, E) && h->alloc(&h->alpha_u, E) && h->alloc(&h->alpha_d, E) &&
-         h->alloc(&h->gs_g, E) && h->alloc(&h->gs_d, E) && h->alloc(&h->os_tab, E * 256);
+         h->alloc(&h->gs_g, E) && h->alloc(&h->gs_d, E) && h->alloc(&h->os_tab, E * 256) &&
+         h->alloc(&h->os_tab_g, E * 256);
     ok = ok && h->alloc(&h->topk_idx, Tm * K) && h->alloc(&h->topk_w, Tm * K);
     PermuteBuffers& b = h->pb;
     if (routed) {
@@ -671,13 +672,17 @@ int nf_moe_finalize(nf_moe* h) {
         // the down input quantiser's output scale for each E4M3 scale code:
         // 1 / (scale / global_scale), with quant_dequant_nvfp4_activation's
         // guard for a zero scale (src/text_forward.cpp:531-549)
-        std::vector<float> os(static_cast<size_t>(E) * 256);
+        // (and the same for the gate/up input, the dispatch's quantiser)
+        std::vector<float> os(static_cast<size_t>(E) * 256), osg(static_cast<size_t>(E) * 256);
         for (int64_t x = 0; x < E; ++x)
             for (int c = 0; c < 256; ++c) {
                 const float reduced = e4m3_host(static_cast<uint8_t>(c)) / gs_d[static_cast<size_t>(x)];
                 os[static_cast<size_t>(x * 256 + c)] = 1.f / (reduced + (reduced == 0.f ? 1.0e8f : 0.f));
+                const float reduced_g = e4m3_host(static_cast<uint8_t>(c)) / gs_g[static_cast<size_t>(x)];
+                osg[static_cast<size_t>(x * 256 + c)] = 1.f / (reduced_g + (reduced_g == 0.f ? 1.0e8f : 0.f));
             }
         e = cudaMemcpy(h->os_tab, os.data(), os.size() * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(h->os_tab_g, osg.data(), osg.size() * 4, cudaMemcpyHostToDevice);
     }
     cudaSetDevice(prev);
     if (e != cudaSuccess) return h->cuda_fail(e, "finalize copy");
@@ -845,10 +850,11 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     // tile: repeat them in the other two so all the epilogue warps work
     const bool rep64 = dense_rows && T > 32 && T <= 64;
     if (dense_rows) {
-        e = launch_dense_dispatch(x, T, H, h->gs_g, h->pb, h->splitk_cnt, h->splitk_cnt_elems, rep64, s);
+        e = launch_dense_dispatch(x, T, H, h->gs_g, h->os_tab_g, h->pb, h->splitk_cnt, h->splitk_cnt_elems, rep64, s);
         one_kernel = true;
     } else {
-        e = launch_permute(idx, x, T, K, E, H, I / 128, H / 256, h->gs_g, fp4 ? 0 : 1, h->pb, s, &one_kernel);
+        e = launch_permute(idx, x, T, K, E, H, I / 128, H / 256, h->gs_g, fp4 ? h->os_tab_g : nullptr, fp4 ? 0 : 1, h->pb,
+                           s, &one_kernel);
     }
     if (e != cudaSuccess) return h->cuda_fail(e, "permute launch");
     rec.end(NF_STAGE_PERMUTE, s);
@@ -1045,13 +1051,22 @@ static int forward_impl(nf_moe* h, const uint16_t* x, const float* residual, int
     // at prefill sizes the screened router fills the GPU and the shared
     // GEMMs' persistent CTAs would hold its SMs, so they fork after it and run
     // beside the permutation and the routed GEMMs instead.
+    // (Profiled forwards join the shared expert at once, so that every stage
+    // time is its kernels alone.)
     const bool shared_first = !(h->screen && T >= kScreenMinTokens);
-    if (Is > 0 && shared_first && (st = launch_shared_expert(h, x, T, rec, s)) != NF_OK) return st;
+    cudaError_t e = cudaSuccess;
+    auto shared = [&]() -> int {
+        int r = launch_shared_expert(h, x, T, rec, s);
+        if (r == NF_OK && rec.ev && (e = cudaStreamWaitEvent(s, h->ev_join, 0)) != cudaSuccess)
+            r = h->cuda_fail(e, "shared expert join");
+        return r;
+    };
+    if (Is > 0 && shared_first && (st = shared()) != NF_OK) return st;
     rec.begin(NF_STAGE_ROUTER, s);
-    cudaError_t e = route_tokens(h, x, T, idx, w, s);
+    e = route_tokens(h, x, T, idx, w, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "router launch");
     rec.end(NF_STAGE_ROUTER, s);
-    if (Is > 0 && !shared_first && (st = launch_shared_expert(h, x, T, rec, s)) != NF_OK) return st;
+    if (Is > 0 && !shared_first && (st = shared()) != NF_OK) return st;
     if ((st = launch_routed_experts(h, x, idx, T, K, rec, s)) != NF_OK) return st;
     if (Is > 0 && (e = cudaStreamWaitEvent(s, h->ev_join, 0)) != cudaSuccess) return h->cuda_fail(e, "shared expert join");
     rec.begin(NF_STAGE_COMBINE, s);
