@@ -362,6 +362,16 @@ NF_DEV void bulk_load_hint(void* smem_dst, const void* gmem_src, uint32_t bytes,
         "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// System-scope release store / acquire load (flags between GPUs of an
+// expert-parallel group, in peer memory).
+NF_DEV void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+NF_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 // Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned, bytes a multiple of 16).
 NF_DEV void prefetch_l2_bulk(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");

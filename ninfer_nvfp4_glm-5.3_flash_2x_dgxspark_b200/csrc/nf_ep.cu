@@ -83,12 +83,14 @@ int ep_p2p_setup(nf_moe* h, std::string* err) {
     // to enter the handle exchange, so this rank joins it too, reporting the
     // failure, and every rank then fails the create together.
     int local_fail = 0;  // 0, NF_ERR_NOMEM or NF_ERR_CUDA
-    if (!h->alloc(&h->ep_mbox, L.total) || !h->alloc(&h->ep_epoch, 1) || !h->alloc(&h->ep_done, 2 * kEpMaxRanks) ||
+    // ep_done: the send's and the return's per-peer block counters, then the
+    // fused return's finished-tile counter
+    if (!h->alloc(&h->ep_mbox, L.total) || !h->alloc(&h->ep_epoch, 1) || !h->alloc(&h->ep_done, 2 * kEpMaxRanks + 1) ||
         !h->alloc(&h->ep_seen, kEpMaxRanks)) {
         cudaGetLastError();
         local_fail = NF_ERR_NOMEM;
     } else if (cudaMemset(h->ep_mbox, 0, L.total) != cudaSuccess || cudaMemset(h->ep_epoch, 0, 4) != cudaSuccess ||
-               cudaMemset(h->ep_done, 0, 2 * kEpMaxRanks * 4) != cudaSuccess ||
+               cudaMemset(h->ep_done, 0, (2 * kEpMaxRanks + 1) * 4) != cudaSuccess ||
                cudaMemset(h->ep_seen, 0, kEpMaxRanks * 4) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
         cudaGetLastError();
         local_fail = NF_ERR_CUDA;
@@ -192,14 +194,29 @@ static int ep_forward_p2p(nf_moe* h, const uint16_t* x, const float* residual, i
     if (e == cudaSuccess) e = launch_ep_p2p_recv_wait(h->ep_mbox, L, R, h->ep_epoch, h->ep_seen, h->dev_err, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "route and send");
     rec.end(NF_STAGE_ROUTER, s);
-    // this rank's experts over the [world][cap] receive slots (empty slots carry expert -1)
+    // this rank's experts over the [world][cap] receive slots (empty slots carry
+    // expert -1).  NVFP4 experts: the down GEMM's epilogue stores each output
+    // row straight into its source's mailbox and its last tile publishes the
+    // flags (the return overlaps the GEMM); BF16 experts: a return kernel after it.
     nf_moe* in = h->inner;
+    GemmArgs epr{};
+    epr.ep_world = R;
+    epr.ep_me = me;
+    epr.ep_cap = L.cap;
+    epr.ep_ret_off = L.ret;
+    epr.ep_flags_ret = L.flags_ret;
+    for (int p = 0; p < kEpMaxRanks; ++p) epr.ep_mbox[p] = h->ep_peers.mbox[p];
+    epr.ep_src_off = reinterpret_cast<const int32_t*>(h->ep_mbox + L.off);
+    epr.ep_epoch = h->ep_epoch;
+    epr.ep_tiles_done = h->ep_done + 2 * kEpMaxRanks;
     if ((st = launch_routed_experts(in, reinterpret_cast<const uint16_t*>(h->ep_mbox + L.rows),
-                                    reinterpret_cast<const int32_t*>(h->ep_mbox + L.e), R * L.cap, 1, rec, s)) != NF_OK)
+                                    reinterpret_cast<const int32_t*>(h->ep_mbox + L.e), R * L.cap, 1, rec, s, 1, nullptr,
+                                    nullptr, fp4 ? &epr : nullptr)) != NF_OK)
         return h->fail(st, "%s", in->err.c_str());
     rec.begin(NF_STAGE_COMBINE, s);
-    e = launch_ep_p2p_return(in->down, in->pb.pair_row, out_bytes, R, me, h->ep_peers, L, h->ep_mbox, h->ep_seen,
-                             h->ep_epoch, h->ep_done, s);
+    if (!fp4)
+        e = launch_ep_p2p_return(in->down, in->pb.pair_row, out_bytes, R, me, h->ep_peers, L, h->ep_mbox, h->ep_seen,
+                                 h->ep_epoch, h->ep_done, s);
     if (e == cudaSuccess) e = launch_ep_p2p_ret_wait(h->ep_mbox, L, R, h->ep_epoch, h->dev_err, s);
     if (e != cudaSuccess) return h->cuda_fail(e, "output return");
     if (T > 0) {

@@ -477,6 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // shared-memory mailbox (a slot is rewritten only after every warp
         // has passed the next barrier, i.e. read it).
         const bool leader = warp == 2 && lane == 0;
+        int ep_tiles = 0;  // tiles of a fused expert-parallel return stored by this CTA
         uint32_t acc_phase = 0;
         int qslot = 0;
         uint32_t qphase = 0;
@@ -494,7 +495,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int tile = epi_mail[2 * (iter & 1)];
             const int ok = epi_mail[2 * (iter & 1) + 1];
             if (++qslot == kTileQ) qslot = 0, qphase ^= 1u;
-            if (!ok || tile < 0) break;
+            if (!ok || tile < 0) {
+                if (EPI == EPI_STORE_BF16 && args.ep_ret && ok) {
+                    // Fused expert-parallel return: once every epilogue warp's
+                    // rows are out, one system-scope fence and the CTA's tile
+                    // count; the CTA that completes the count (CTA 0 when there
+                    // are no tiles) publishes every source's flag.
+                    named_bar_sync(2, 32 * kEpiWarps);
+                    if (leader) {
+                        const int total = *args.num_tiles_dev;
+                        bool last = total == 0 && blockIdx.x == 0;
+                        if (ep_tiles > 0) {
+                            __threadfence_system();
+                            last = atomicAdd(args.ep_tiles_done, ep_tiles) + ep_tiles == total;
+                        }
+                        if (last) {
+                            __threadfence_system();
+                            const uint32_t ep = *args.ep_epoch + 1u;
+                            for (int s2 = 0; s2 < args.ep_world; ++s2)
+                                st_release_sys(reinterpret_cast<uint32_t*>(args.ep_mbox[s2] + args.ep_flags_ret) + args.ep_me,
+                                               ep);
+                            *args.ep_tiles_done = 0;
+                        }
+                    }
+                }
+                break;
+            }
             const TileInfo t = get_tile(args, tile, k_tiles, TM);
             tc_fence_after();
             if constexpr (MT == 2) {
@@ -645,9 +671,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
                     p[j] = bf16x2_hw(__fmul_rn(__uint_as_float(v[2 * j]), a), __fmul_rn(__uint_as_float(v[2 * j + 1]), a));
-                if (valid) {
-                    uint16_t* d = static_cast<uint16_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld +
-                                  t.n_block * BN + 64 * cs;
+                uint16_t* d = nullptr;
+                if (valid && args.ep_ret) {
+                    // the row's source rank and slot: its output goes to that rank's mailbox
+                    const int j = args.row_token[row];
+                    if (j >= 0) {
+                        const int src = j / args.ep_cap, k = j - src * args.ep_cap;
+                        d = reinterpret_cast<uint16_t*>(args.ep_mbox[src] + args.ep_ret_off) +
+                            static_cast<int64_t>(args.ep_src_off[src] + k) * args.out_ld + t.n_block * BN + 64 * cs;
+                    }
+                } else if (valid) {
+                    d = static_cast<uint16_t*>(args.out) + static_cast<int64_t>(row) * args.out_ld + t.n_block * BN +
+                        64 * cs;
+                }
+                if (d) {
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
                         st_global_v8(d + 16 * j, p[8 * j], p[8 * j + 1], p[8 * j + 2], p[8 * j + 3], p[8 * j + 4],
@@ -679,6 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+            if (EPI == EPI_STORE_BF16 && args.ep_ret) ++ep_tiles;  // counted once, at the CTA's end
             if (EPI == EPI_STORE_F32 && args.splitk_fuse) {
                 // Fused split-K reduction: count this slice once every warp's
                 // stores are out, wait for the tile's other slices (their CTAs

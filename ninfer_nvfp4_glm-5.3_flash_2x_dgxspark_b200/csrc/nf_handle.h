@@ -255,8 +255,10 @@ cudaError_t route_tokens(nf_moe* h, const uint16_t* x, int T, int32_t* idx, floa
 // down_split > 1 (dense handles): the down GEMM runs as a dense split-K GEMM
 // into h->dense_part (down_split K slices) instead of writing h->down; when
 // dense_splitk_fused(), it also reduces the slices into y (+ residual).
+// epr: the expert-parallel return fused into the down GEMM (peer memory).
 int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int T, int K, StageRec& rec,
-                          cudaStream_t s, int down_split = 1, const float* residual = nullptr, float* y = nullptr);
+                          cudaStream_t s, int down_split = 1, const float* residual = nullptr, float* y = nullptr,
+                          const nf::GemmArgs* epr = nullptr);
 // The dense split-K down GEMM reduces its slices itself when every tile gets
 // its own CTA (so all slices of a tile run together).
 bool dense_splitk_fused(const nf_moe* h, int T, int down_split);

@@ -45,6 +45,7 @@ enum GemmEpi : int {
 
 // Operand kinds.
 enum GemmKind : int { KIND_NVFP4 = 0, KIND_BF16 = 1 };
+constexpr int kEpMaxRanks = 8;  // expert-parallel group size limit
 
 struct GemmArgs {
     int kind;            // GemmKind
@@ -81,6 +82,20 @@ struct GemmArgs {
     // other, without the tile counter, so it may claim it (and issue its
     // first B stages) before the previous kernel completes
     int static_tiles;
+    // Expert-parallel return fused into the down GEMM (EPI_STORE_BF16 over
+    // the [world][cap] receive slots, peer memory): permuted row `row` holds
+    // receive slot j = row_token[row] = source * ep_cap + k and its output
+    // row goes straight to ep_mbox[source] + ep_ret_off + (ep_src_off[source]
+    // + k) * row bytes; the CTA that finishes the last tile (or CTA 0 when
+    // there is none) publishes flag ep_flags_ret[ep_me] = *ep_epoch + 1 in
+    // every source's mailbox after a system-scope fence.
+    int ep_ret;
+    int ep_world, ep_me, ep_cap;
+    int64_t ep_ret_off, ep_flags_ret;
+    uint8_t* ep_mbox[kEpMaxRanks];
+    const int32_t* ep_src_off;
+    const uint32_t* ep_epoch;
+    int32_t* ep_tiles_done;    // zero before the launch; reset by the CTA that publishes
     const float* residual;
     float* y;
     // NVFP4 scale-factor atoms: sfa [128-row block][K/64 atoms]; sfb in tile
@@ -241,7 +256,6 @@ cudaError_t launch_splitk_store(const float* part, int S, int64_t stride, int T,
                                 const float* residual, float* y, int grid_cap, cudaStream_t st);
 // Expert parallelism (up to kEpMaxRanks ranks): the (destination, token,
 // pick) layout of the picks, and a row gather.
-constexpr int kEpMaxRanks = 8;
 cudaError_t launch_ep_pack(const int32_t* idx, int T, int K, int e_per_rank, int world, int32_t* slot,
                            int32_t* send_tok, int32_t* send_e, int32_t* counts, cudaStream_t st);
 cudaError_t launch_gather_rows(const void* src, const int32_t* map, int n, int row_bytes, void* dst, cudaStream_t st);

@@ -1634,14 +1634,6 @@ cudaError_t launch_gather_rows(const void* src, const int32_t* map, int n, int r
 // received every owner's epoch-e outputs, which each owner returns after its
 // GEMMs consumed all of epoch e's rows.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 // Bounded wait until *flag >= want (epochs only grow); false after the budget.
 __device__ bool ep_wait_flag(const uint32_t* flag, uint32_t want) {
     const uint64_t t0 = globaltimer_ns();

@@ -836,7 +836,7 @@ bool dense_splitk_fused(const nf_moe* h, int T, int down_split) {
 }
 
 int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int T, int K, StageRec& rec,
-                          cudaStream_t s, int down_split, const float* residual, float* y) {
+                          cudaStream_t s, int down_split, const float* residual, float* y, const GemmArgs* epr) {
     const nf_moe_desc& d = h->d;
     const int H = d.hidden, E = d.experts, I = d.inter;
     const bool fp4 = d.expert_kind == NF_EXPERTS_NVFP4;
@@ -914,9 +914,9 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.seg_off = h->pb.seg_off;
     g.seg_cnt = h->pb.counts;
     const bool prefill = static_cast<int64_t>(T) * K >= 256LL * E && down_split <= 1;
-    const bool pair = !dense_rows && fp4 && h->gemm_mode == NF_GEMM_CTA_PAIR && h->grid2 >= 2 && prefill && H % 256 == 0 &&
+    const bool pair = !epr && !dense_rows && fp4 && h->gemm_mode == NF_GEMM_CTA_PAIR && h->grid2 >= 2 && prefill && H % 256 == 0 &&
                       I % 256 == 0 && E <= 256;
-    const bool wide = fp4 && h->gemm_mode == NF_GEMM_WIDE_STAGES && prefill && h->wide_ok;
+    const bool wide = !epr && fp4 && h->gemm_mode == NF_GEMM_WIDE_STAGES && prefill && h->wide_ok;
     g.wide_stages = wide ? 1 : 0;
     e = pair ? launch_gemm2(h->tm_a, h->tm_b_gu_half, h->tm_sfa_a, h->tm_sfb_gu, g, h->grid2, true, s)
         : wide ? launch_gemm(h->tm_a3, h->tm_a3, h->tm_b_gu3, g, h->grid, true, s)
@@ -945,6 +945,19 @@ int launch_routed_experts(nf_moe* h, const uint16_t* x, const int32_t* idx, int 
     g.early_claim = 1;
     g.rep64 = 0;
     g.static_tiles = 0;
+    if (epr && fp4) {
+        // the outputs go to their source ranks' mailboxes from the epilogue
+        g.ep_ret = 1;
+        g.ep_world = epr->ep_world;
+        g.ep_me = epr->ep_me;
+        g.ep_cap = epr->ep_cap;
+        g.ep_ret_off = epr->ep_ret_off;
+        g.ep_flags_ret = epr->ep_flags_ret;
+        for (int i = 0; i < kEpMaxRanks; ++i) g.ep_mbox[i] = epr->ep_mbox[i];
+        g.ep_src_off = epr->ep_src_off;
+        g.ep_epoch = epr->ep_epoch;
+        g.ep_tiles_done = epr->ep_tiles_done;
+    }
     if (dense_rows) {
         g.dense_rows = T;
         g.tiles = nullptr;
