@@ -689,8 +689,9 @@ __global__ void __launch_bounds__(kFzCThreads + 32 * PW, 1) router_fused_kernel(
     }
     __syncthreads();
     if constexpr (kXRes) {
-        // the first router copies go out at once, then every thread widens
-        // the resident token rows (zero past the batch)
+        // the first router copies go out at once from the producer thread,
+        // while the consumer threads widen the resident token rows (zero past
+        // the batch), their loads issued four at a time before the stores
         if (threadIdx.x == kFzCThreads)
             for (int c = 0; c < NS && c < nstages; ++c) {
                 const int bytes = min(SUB, nchunks - c * SUB) * wchunk;
@@ -700,15 +701,27 @@ __global__ void __launch_bounds__(kFzCThreads + 32 * PW, 1) router_fused_kernel(
             }
         int unsafe = 0;
         const int q8 = H / 8;
-        for (int i = threadIdx.x; i < tc * q8; i += kThreads) {
-            const int r = i / q8, q = i - r * q8;
-            uint4 u = make_uint4(0u, 0u, 0u, 0u);
-            if (r < nt) u = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0 + r) * H) + q);
-            unsafe |= bf16x8_unsafe(u);
-            float4* dst = reinterpret_cast<float4*>(xres + r * xres_pitch) + 2 * q;
-            dst[0] = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
-            dst[1] = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
-        }
+        constexpr int kB = 4;
+        if (threadIdx.x < kFzCThreads)
+            for (int i0 = threadIdx.x; i0 < tc * q8; i0 += kB * kFzCThreads) {
+                uint4 u[kB];
+#pragma unroll
+                for (int j = 0; j < kB; ++j) {
+                    const int i = i0 + j * kFzCThreads, r = i / q8, q = i - r * q8;
+                    u[j] = make_uint4(0u, 0u, 0u, 0u);
+                    if (i < tc * q8 && r < nt)
+                        u[j] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0 + r) * H) + q);
+                }
+#pragma unroll
+                for (int j = 0; j < kB; ++j) {
+                    const int i = i0 + j * kFzCThreads, r = i / q8, q = i - r * q8;
+                    if (i >= tc * q8) break;
+                    unsafe |= bf16x8_unsafe(u[j]);
+                    float4* dst = reinterpret_cast<float4*>(xres + r * xres_pitch) + 2 * q;
+                    dst[0] = make_float4(bf16_lo(u[j].x), bf16_hi(u[j].x), bf16_lo(u[j].y), bf16_hi(u[j].y));
+                    dst[1] = make_float4(bf16_lo(u[j].z), bf16_hi(u[j].z), bf16_lo(u[j].w), bf16_hi(u[j].w));
+                }
+            }
         if (__syncthreads_or(unsafe) && threadIdx.x == 0) s_x_unsafe = 1;
         __syncthreads();
     }
