@@ -574,12 +574,69 @@ def run_prefill(args, m, torch, fp4_peak, bf16_peak, peak_src) -> dict:
     }
 
 
+def choose_replicas(counts_src: np.ndarray, e_per_rank: int, max_rep: int = 16) -> list[int]:
+    """Hot experts to replicate on every rank, greedily: counts_src[r, e] are
+    the picks of expert e made by rank r's tokens; with replica set R rank r
+    computes its own picks of R and every rank's picks of the experts it owns
+    outside R.  Adds experts in descending pick count while that lowers the
+    busiest rank's load by 2% or more."""
+    world, E = counts_src.shape
+    tot = counts_src.sum(0)
+
+    def busiest(rs):
+        load = np.zeros(world)
+        for e in range(E):
+            if e in rs:
+                load += counts_src[:, e]
+            else:
+                load[e // e_per_rank] += tot[e]
+        return load.max()
+
+    reps, best = set(), busiest(set())
+    for e in np.argsort(-tot, kind="stable")[:max_rep]:
+        b = busiest(reps | {int(e)})
+        if b < 0.98 * best:
+            reps, best = reps | {int(e)}, b
+    return sorted(reps)
+
+
 def run_ep_c3(args, m, torch, rank: int, world: int, local: int, dist, lam: float = 1.0) -> dict:
     """16384 tokens per step split over the ranks (strong scaling),
     experts sharded evenly, router bias + lam * Zipf(1.1) log-prior (at the
     configuration's literal lam = 1 nearly every pick lands on the first
     experts, i.e. on rank 0; at the calibrated lam the pick shares follow the
-    Zipf distribution most closely).  Device time per step, max over ranks."""
+    Zipf distribution most closely).  Device time per step, max over ranks.
+    With more than one rank the step is timed twice: experts only sharded,
+    then with the hot experts replicated on every rank (choose_replicas over
+    the first run's picks; the product path's number)."""
+    first = _run_ep_c3_once(args, m, torch, rank, world, local, dist, lam, None)
+    if world == 1:
+        return first
+    e_per_rank = first["experts"] // world
+    counts = np.zeros((world, first["experts"]), dtype=np.int64)
+    counts[rank] = np.bincount(first["idx"].ravel(), minlength=first["experts"])
+    t = torch.from_numpy(counts).cuda()
+    dist.all_reduce(t)
+    counts = t.cpu().numpy()
+    reps = choose_replicas(counts, e_per_rank)
+    out = _run_ep_c3_once(args, m, torch, rank, world, local, dist, lam, reps)
+    out["replicas"] = reps
+    out["ms_per_step_experts_sharded_only"] = first["ms_per_step"]
+    out["ep_parity_experts_sharded_only"] = first.get("ep_parity")
+    # picks each rank computes, with and without the replicas
+    tot = counts.sum(0)
+    for key, rs in (("picks_by_computing_rank_sharded_only", set()), ("picks_by_computing_rank", set(reps))):
+        load = np.zeros(world, dtype=np.int64)
+        for e in range(counts.shape[1]):
+            if e in rs:
+                load += counts[:, e]
+            else:
+                load[e // e_per_rank] += tot[e]
+        out[key] = [int(v) for v in load]
+    return out
+
+
+def _run_ep_c3_once(args, m, torch, rank: int, world: int, local: int, dist, lam: float, replicas) -> dict:
     lay, x_all = wl.config_layer("c3", zipf_lambda=lam)
     T_all, H, K = x_all.shape[0], lay.hidden, lay.top_k
     per = T_all // world
@@ -590,7 +647,7 @@ def run_ep_c3(args, m, torch, rank: int, world: int, local: int, dist, lam: floa
         dist.broadcast_object_list(gid, src=0)
         ep = (rank, world, gid[0])
     layer = m.MoeLayer(H, lay.experts, K, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
-                       swiglu_limit=lay.swiglu_limit, max_tokens=per, device=local, ep=ep)
+                       swiglu_limit=lay.swiglu_limit, max_tokens=per, device=local, ep=ep, ep_replicas=replicas)
     layer.bind_layer(lay)
     x = torch.from_numpy(np.ascontiguousarray(xb).view(np.int16)).cuda()
     y = torch.empty((per, H), dtype=torch.float32, device="cuda")
@@ -617,7 +674,12 @@ def run_ep_c3(args, m, torch, rank: int, world: int, local: int, dist, lam: floa
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     idx_h = idx.cpu().numpy()
-    owners = np.bincount(idx_h.ravel() // (lay.experts // world), minlength=world)
+    # where this rank's picks are computed: the expert's owner, or this rank
+    # for a replicated expert
+    dest = idx_h.ravel() // (lay.experts // world)
+    if replicas:
+        dest = np.where(np.isin(idx_h.ravel(), replicas), rank, dest)
+    owners = np.bincount(dest, minlength=world)
     out = {"workload": f"c3: c1 shapes, 16384 tokens per step split over the ranks, Zipf(1.1) log-prior "
                        f"lambda = {lam:g} (configs[3])", "tokens_per_s": T_all / (ms * 1e-3), "ms_per_step": ms,
            "steps": steps,
@@ -634,6 +696,8 @@ def run_ep_c3(args, m, torch, rank: int, world: int, local: int, dist, lam: floa
         out["ep_parity"] = bool(flag.item())
         dist.barrier()  # every rank's last forward is done before any handle of the group goes
     layer.close()
+    if world > 1 and replicas is None:
+        out["idx"], out["experts"] = idx_h, lay.experts
     return out
 
 

@@ -279,6 +279,17 @@ NF_API int nf_moe_create_dense(int32_t hidden, int32_t inter, float swiglu_limit
  * Results are bit-identical to one GPU holding every expert. */
 #define NF_EP_ID_BYTES 128
 NF_API int nf_ep_unique_id(uint8_t* group_id_out, int len);
+/* Expert parallelism with replicated hot experts: every rank also holds
+ * the experts listed in `replicas` (ids in [0, experts), no duplicates; the
+ * same list on every rank), and a pick of a replicated expert is computed on
+ * the rank whose token made it, with no exchange -- the skew of a few hot
+ * experts spreads over the ranks with the tokens.  The outputs stay
+ * identical to one GPU bit for bit (rows are independent).  Binding every
+ * expert on every rank binds the replicas too.  n_replicas = 0 is
+ * nf_moe_create_ep. */
+NF_API int nf_moe_create_ep_replicated(const nf_moe_desc* desc, int device, int rank, int world,
+                                       const uint8_t* group_id, int id_len, const int32_t* replicas, int n_replicas,
+                                       nf_moe** out);
 NF_API int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, const uint8_t* group_id,
                             int id_len, nf_moe** out);
 /* The exchange an EP handle uses (the choice is made collectively at

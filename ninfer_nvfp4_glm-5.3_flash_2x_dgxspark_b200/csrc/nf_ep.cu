@@ -184,7 +184,7 @@ static int ep_forward_p2p(nf_moe* h, const uint16_t* x, const float* residual, i
     if (T > 0) {
         e = route_tokens(h, x, T, idx, w, s);
         if (e == cudaSuccess)
-            e = launch_ep_pack(idx, T, K, h->ep_local, R, h->ep_slot, h->ep_send_tok, h->ep_send_e, h->ep_cnt, s);
+            e = launch_ep_pack(idx, T, K, h->ep_route, d.experts, R, h->ep_slot, h->ep_send_tok, h->ep_send_e, h->ep_cnt, s);
     } else {
         e = cudaMemsetAsync(h->ep_cnt, 0, R * sizeof(int32_t), s);
     }
@@ -254,7 +254,7 @@ int ep_forward(nf_moe* h, const uint16_t* x, const float* residual, int T, float
     if (T > 0) {
         e = route_tokens(h, x, T, idx, w, s);
         if (e == cudaSuccess)
-            e = launch_ep_pack(idx, T, K, h->ep_local, R, h->ep_slot, h->ep_send_tok, h->ep_send_e, h->ep_cnt, s);
+            e = launch_ep_pack(idx, T, K, h->ep_route, d.experts, R, h->ep_slot, h->ep_send_tok, h->ep_send_e, h->ep_cnt, s);
         if (e == cudaSuccess) e = launch_gather_rows(x, h->ep_send_tok, T * K, H * 2, h->ep_send, s);
     } else {
         e = cudaMemsetAsync(h->ep_cnt, 0, R * sizeof(int32_t), s);
@@ -375,10 +375,19 @@ int nf_moe_ep_transport(const nf_moe* h) {
 
 int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, const uint8_t* group_id, int id_len,
                      nf_moe** out) {
+    return nf_moe_create_ep_replicated(desc, device, rank, world, group_id, id_len, nullptr, 0, out);
+}
+
+int nf_moe_create_ep_replicated(const nf_moe_desc* desc, int device, int rank, int world, const uint8_t* group_id,
+                                int id_len, const int32_t* replicas, int n_replicas, nf_moe** out) {
     std::string& err = create_error();
     err.clear();
     if (!desc || !out || !group_id || id_len < NF_EP_ID_BYTES) {
         err = "null descriptor, output or group id";
+        return NF_ERR_INVALID;
+    }
+    if (n_replicas < 0 || (n_replicas > 0 && !replicas)) {
+        err = "bad replica list";
         return NF_ERR_INVALID;
     }
     *out = nullptr;
@@ -393,6 +402,15 @@ int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, c
         err = "the experts must divide evenly over the ranks";
         return NF_ERR_UNSUPPORTED;
     }
+    std::vector<char> seen(static_cast<size_t>(d.experts), 0);
+    for (int j = 0; j < n_replicas; ++j) {
+        const int e = replicas[j];
+        if (e < 0 || e >= d.experts || seen[static_cast<size_t>(e)]) {
+            err = "replicas must be distinct expert ids in [0, experts)";
+            return NF_ERR_INVALID;
+        }
+        seen[static_cast<size_t>(e)] = 1;
+    }
     NcclApi& api = nccl();
     if (!api.ok) {
         err = api.why;
@@ -404,9 +422,12 @@ int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, c
     h->ep_world = world;
     h->ep_local = d.experts / world;
     h->ep_base = rank * h->ep_local;
-    // the rank's experts: top-1 picks over rows received from every rank
+    for (int j = 0; j < n_replicas; ++j)  // the replicas this rank does not own already
+        if (replicas[j] < h->ep_base || replicas[j] >= h->ep_base + h->ep_local) h->ep_rep.push_back(replicas[j]);
+    // the rank's experts (its own, then its replicas): top-1 picks over rows
+    // received from every rank
     nf_moe_desc di = d;
-    di.experts = h->ep_local;
+    di.experts = h->ep_local + static_cast<int>(h->ep_rep.size());
     di.top_k = 1;
     di.shared_inter = 0;
     di.n_group = 1;
@@ -428,7 +449,21 @@ int nf_moe_create_ep(const nf_moe_desc* desc, int device, int rank, int world, c
     // (and the staging buffer of the set-up exchanges: allocated before the
     // communicator, so that every exchange has a buffer on every rank)
     bool ok = h->alloc(&h->ep_send_e, pairs) && h->alloc(&h->ep_send_tok, pairs) && h->alloc(&h->ep_slot, pairs) &&
-              h->alloc(&h->ep_cnt, 2 * world) && h->alloc(&h->ep_stage, kEpRecBytes * (world + 1));
+              h->alloc(&h->ep_cnt, 2 * world) && h->alloc(&h->ep_stage, kEpRecBytes * (world + 1)) &&
+              h->alloc(&h->ep_route, 2 * d.experts);
+    if (ok) {
+        // where each expert's picks go: its owner and its index there, or this
+        // rank's replica slot
+        std::vector<int32_t> route(static_cast<size_t>(2 * d.experts));
+        for (int e = 0; e < d.experts; ++e) {
+            int dest = e / h->ep_local, loc = e % h->ep_local;
+            for (size_t j = 0; j < h->ep_rep.size(); ++j)
+                if (h->ep_rep[j] == e) dest = rank, loc = h->ep_local + static_cast<int>(j);
+            route[static_cast<size_t>(e)] = dest;
+            route[static_cast<size_t>(d.experts + e)] = loc;
+        }
+        ok = cudaMemcpy(h->ep_route, route.data(), route.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+    }
     if (!ok) {
         cudaGetLastError();
         cudaSetDevice(prev);

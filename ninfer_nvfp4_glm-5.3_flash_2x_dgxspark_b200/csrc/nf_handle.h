@@ -99,6 +99,10 @@ struct nf_moe {
     int* splitk_cnt = nullptr;       // [m tiles][H / 256] slices stored per down tile (fused reduction)
     int splitk_cnt_elems = 0;
     int ep_rank = 0, ep_world = 1, ep_base = 0, ep_local = 0;
+    // Replicated experts this rank holds beyond its own (inner handle slots
+    // ep_local + j): their picks from this rank's tokens stay here.
+    std::vector<int> ep_rep;
+    int32_t* ep_route = nullptr;  // [2E]: destination rank of expert e, then its index there
     nf_moe* inner = nullptr;
     void* nccl = nullptr;            // ncclComm_t of the group
     uint16_t* ep_send = nullptr;     // [Tm*K, H] rows in (destination, token, pick) order

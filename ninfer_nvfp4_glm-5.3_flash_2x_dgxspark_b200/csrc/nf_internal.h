@@ -255,8 +255,9 @@ cudaError_t launch_combine(const void* down, bool down_bf16, const int32_t* pair
 cudaError_t launch_splitk_store(const float* part, int S, int64_t stride, int T, int H, const float* alpha,
                                 const float* residual, float* y, int grid_cap, cudaStream_t st);
 // Expert parallelism (up to kEpMaxRanks ranks): the (destination, token,
-// pick) layout of the picks, and a row gather.
-cudaError_t launch_ep_pack(const int32_t* idx, int T, int K, int e_per_rank, int world, int32_t* slot,
+// pick) layout of the picks (route [2 experts]: expert e's destination rank,
+// then its index there), and a row gather.
+cudaError_t launch_ep_pack(const int32_t* idx, int T, int K, const int32_t* route, int experts, int world, int32_t* slot,
                            int32_t* send_tok, int32_t* send_e, int32_t* counts, cudaStream_t st);
 cudaError_t launch_gather_rows(const void* src, const int32_t* map, int n, int row_bytes, void* dst, cudaStream_t st);
 // Expert parallelism over NVLink peer memory (CUDA IPC mailboxes).  A rank's

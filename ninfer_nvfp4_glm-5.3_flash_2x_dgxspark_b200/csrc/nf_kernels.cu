@@ -1557,7 +1557,8 @@ cudaError_t launch_splitk_store(const float* part, int S, int64_t stride, int T,
 // warp ballots its lanes per destination and a scan over the warps gives
 // every pick its rank.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) ep_pack_kernel(const int32_t* __restrict__ idx, int n, int K, int e_per_rank,
+__global__ void __launch_bounds__(1024) ep_pack_kernel(const int32_t* __restrict__ idx, int n, int K,
+                                                       const int32_t* __restrict__ route, int experts,
                                                        int world, int32_t* __restrict__ slot,
                                                        int32_t* __restrict__ send_tok, int32_t* __restrict__ send_e,
                                                        int32_t* __restrict__ counts) {
@@ -1566,7 +1567,7 @@ __global__ void __launch_bounds__(1024) ep_pack_kernel(const int32_t* __restrict
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x < kEpMaxRanks) s_base[threadIdx.x] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&s_base[idx[i] / e_per_rank], 1);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&s_base[route[idx[i]]], 1);
     __syncthreads();
     if (threadIdx.x == 0) {
         int run = 0;
@@ -1580,7 +1581,7 @@ __global__ void __launch_bounds__(1024) ep_pack_kernel(const int32_t* __restrict
     __syncthreads();
     for (int c0 = 0; c0 < n; c0 += blockDim.x) {
         const int i = c0 + threadIdx.x;
-        const int d = i < n ? idx[i] / e_per_rank : -1;
+        const int d = i < n ? route[idx[i]] : -1;
         int in_warp = 0;
         for (int dd = 0; dd < world; ++dd) {
             const uint32_t m = __ballot_sync(0xffffffffu, d == dd);
@@ -1593,7 +1594,7 @@ __global__ void __launch_bounds__(1024) ep_pack_kernel(const int32_t* __restrict
             for (int w = 0; w < warp; ++w) r += s_w[w][d];
             slot[i] = r;
             send_tok[r] = i / K;
-            send_e[r] = idx[i] - d * e_per_rank;
+            send_e[r] = route[experts + idx[i]];
         }
         __syncthreads();
         if (threadIdx.x < world) {
@@ -1618,10 +1619,10 @@ __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, const int32_
     }
 }
 
-cudaError_t launch_ep_pack(const int32_t* idx, int T, int K, int e_per_rank, int world, int32_t* slot,
+cudaError_t launch_ep_pack(const int32_t* idx, int T, int K, const int32_t* route, int experts, int world, int32_t* slot,
                            int32_t* send_tok, int32_t* send_e, int32_t* counts, cudaStream_t st) {
     if (world < 1 || world > kEpMaxRanks) return cudaErrorInvalidValue;
-    ep_pack_kernel<<<1, 1024, 0, st>>>(idx, T * K, K, e_per_rank, world, slot, send_tok, send_e, counts);
+    ep_pack_kernel<<<1, 1024, 0, st>>>(idx, T * K, K, route, experts, world, slot, send_tok, send_e, counts);
     return cudaGetLastError();
 }
 

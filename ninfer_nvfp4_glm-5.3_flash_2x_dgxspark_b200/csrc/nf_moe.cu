@@ -428,6 +428,21 @@ extern "C" {
 // An EP rank binds only the experts it owns (into its inner handle, with
 // local ids); the others belong to other ranks and are skipped.  Inner
 // failures come back with the expert's global id.
+// The global expert id of inner slot `local` (own experts, then replicas).
+static long long ep_global_expert(const nf_moe* h, long long local) {
+    if (local < h->ep_local) return local + h->ep_base;
+    const long long j = local - h->ep_local;
+    return j < static_cast<long long>(h->ep_rep.size()) ? h->ep_rep[static_cast<size_t>(j)] : -1;
+}
+
+// The inner slot of global expert e on this rank, -1 when the rank holds none.
+static int ep_inner_slot(const nf_moe* h, int e) {
+    if (e >= h->ep_base && e < h->ep_base + h->ep_local) return e - h->ep_base;
+    for (size_t j = 0; j < h->ep_rep.size(); ++j)
+        if (h->ep_rep[j] == e) return h->ep_local + static_cast<int>(j);
+    return -1;
+}
+
 static int ep_relay(nf_moe* h, int st) {
     if (st == NF_OK) return NF_OK;
     std::string m = h->inner->err;
@@ -437,7 +452,7 @@ static int ep_relay(nf_moe* h, int st) {
         while (end < m.size() && m[end] >= '0' && m[end] <= '9') ++end;
         if (end > at + 12) {
             const long long local = std::atoll(m.substr(at + 12, end - at - 12).c_str());
-            m = m.substr(0, at + 12) + std::to_string(local + h->ep_base) + m.substr(end);
+            m = m.substr(0, at + 12) + std::to_string(ep_global_expert(h, local)) + m.substr(end);
         }
     }
     return h->fail(st, "%s", m.c_str());
@@ -451,8 +466,9 @@ int nf_moe_bind_nvfp4(nf_moe* h, int expert, int proj, const uint8_t* packed, co
     if (h->finalized) return h->fail(NF_ERR_STATE, "weights are already finalized");
     if (expert < 0 || expert >= d.experts || proj < 0 || proj > 2) return h->fail(NF_ERR_INVALID, "bad expert or projection id");
     if (h->ep_outer) {
-        if (expert < h->ep_base || expert >= h->ep_base + h->ep_local) return NF_OK;
-        return ep_relay(h, nf_moe_bind_nvfp4(h->inner, expert - h->ep_base, proj, packed, scales, ws2, in_scale, rows, cols));
+        const int slot = ep_inner_slot(h, expert);
+        if (slot < 0) return NF_OK;
+        return ep_relay(h, nf_moe_bind_nvfp4(h->inner, slot, proj, packed, scales, ws2, in_scale, rows, cols));
     }
     if (!packed || !scales) return h->fail(NF_ERR_LAYOUT, "NVFP4 layout %s", proj_label(h, expert, proj).c_str());
     const int64_t H = d.hidden, I = d.inter;
@@ -517,8 +533,9 @@ int nf_moe_bind_bf16(nf_moe* h, int which, int expert, const uint16_t* data, int
     if (is_expert && d.expert_kind != NF_EXPERTS_BF16) return h->fail(NF_ERR_STATE, "handle holds NVFP4 experts");
     if (is_expert && (expert < 0 || expert >= E)) return h->fail(NF_ERR_INVALID, "bad expert id");
     if (is_expert && h->ep_outer) {
-        if (expert < h->ep_base || expert >= h->ep_base + h->ep_local) return NF_OK;
-        return ep_relay(h, nf_moe_bind_bf16(h->inner, which, expert - h->ep_base, data, rows, cols));
+        const int slot = ep_inner_slot(h, expert);
+        if (slot < 0) return NF_OK;
+        return ep_relay(h, nf_moe_bind_bf16(h->inner, which, slot, data, rows, cols));
     }
     if (!is_expert && h->experts_only)
         return h->fail(NF_ERR_STATE, "%s handle holds no %s", h->dense ? "a dense MLP" : "an experts-only", name);
@@ -639,7 +656,7 @@ int nf_moe_finalize(nf_moe* h) {
             long long le = -1;
             char proj[32] = {0};
             if (std::sscanf(m, "missing tensor mlp.experts.%lld.%31s", &le, proj) == 2)
-                return h->fail(st, "missing tensor mlp.experts.%lld.%s", le + h->ep_base, proj);
+                return h->fail(st, "missing tensor mlp.experts.%lld.%s", ep_global_expert(h, le), proj);
             return h->fail(st, "%s", m);
         }
     } else {

@@ -40,7 +40,7 @@ EXPORTED = [
     "nf_moe_bind_bf16", "nf_moe_bind_f32", "nf_moe_finalize", "nf_moe_forward", "nf_moe_forward_host",
     "nf_moe_sync", "nf_moe_route", "nf_moe_debug_tensor", "nf_moe_debug_read", "nf_nvfp4_dequantize", "nf_nvfp4_quantize",
     "nf_sigmoid_ref", "nf_moe_profile", "nf_moe_stage_times", "nf_format_selfcheck", "nf_moe_set_graph_mode", "nf_moe_set_expert_gemm",
-    "nf_router_topk_noalloc", "nf_ep_unique_id", "nf_moe_create_ep", "nf_moe_create_dense",
+    "nf_router_topk_noalloc", "nf_ep_unique_id", "nf_moe_create_ep", "nf_moe_create_ep_replicated", "nf_moe_create_dense",
     "nf_moe_ep_transport", "nf_tp_split", "nf_tp_create", "nf_tp_destroy", "nf_tp_last_error", "nf_tp_transport",
     "nf_tp_linear_bf16", "nf_tp_argmax", "nf_tp_result", "nf_tp_sync", "nf_stack_create", "nf_stack_destroy",
     "nf_stack_last_error", "nf_stack_layer_ffn", "nf_stack_bind_bf16", "nf_stack_bind_f32", "nf_stack_finalize",
@@ -107,6 +107,8 @@ def load() -> ctypes.CDLL:
                                    I32),
         "nf_ep_unique_id": ([ctypes.c_char_p, I32], I32),
         "nf_moe_create_ep": ([ctypes.POINTER(Desc), I32, I32, I32, ctypes.c_char_p, I32, ctypes.POINTER(P)], I32),
+        "nf_moe_create_ep_replicated": ([ctypes.POINTER(Desc), I32, I32, I32, ctypes.c_char_p, I32,
+                                         ctypes.POINTER(ctypes.c_int32), I32, ctypes.POINTER(P)], I32),
         "nf_moe_create_dense": ([I32, I32, F, I32, I32, ctypes.POINTER(P)], I32),
         "nf_moe_ep_transport": ([P], I32),
         "nf_tp_split": ([I64, I32, I32, ctypes.POINTER(I64), ctypes.POINTER(I64)], I32),
@@ -186,10 +188,12 @@ class MoeLayer:
     def __init__(self, hidden: int, experts: int, top_k: int, inter: int, shared_inter: int, *,
                  routed_scaling: float = 1.0, swiglu_limit: float = 10.0, n_group: int = 1, topk_group: int = 1,
                  normalize: bool = True, bf16_experts: bool = False, max_tokens: int = 64, device: int = 0,
-                 ep: tuple[int, int, bytes] | None = None):
+                 ep: tuple[int, int, bytes] | None = None, ep_replicas=None):
         """ep = (rank, world, group_id) makes this rank's handle of an expert-
         parallel group (group_id from ep_group_id() on one rank, shared by all);
-        max_tokens is then per rank."""
+        max_tokens is then per rank.  ep_replicas: expert ids every rank also
+        holds (the same list on every rank); picks of them stay on the rank of
+        their token (nf_moe_create_ep_replicated)."""
         self.lib = load()
         self.desc = Desc(hidden, experts, top_k, inter, shared_inter, n_group, topk_group, int(normalize),
                          routed_scaling, swiglu_limit, EXPERTS_BF16 if bf16_experts else EXPERTS_NVFP4, max_tokens)
@@ -198,8 +202,13 @@ class MoeLayer:
             st = self.lib.nf_moe_create(ctypes.byref(self.desc), device, ctypes.byref(h))
         else:
             rank, world, group_id = ep
-            st = self.lib.nf_moe_create_ep(ctypes.byref(self.desc), device, rank, world, group_id, len(group_id),
-                                           ctypes.byref(h))
+            if ep_replicas:
+                reps = (ctypes.c_int32 * len(ep_replicas))(*[int(e) for e in ep_replicas])
+                st = self.lib.nf_moe_create_ep_replicated(ctypes.byref(self.desc), device, rank, world, group_id,
+                                                          len(group_id), reps, len(ep_replicas), ctypes.byref(h))
+            else:
+                st = self.lib.nf_moe_create_ep(ctypes.byref(self.desc), device, rank, world, group_id, len(group_id),
+                                               ctypes.byref(h))
         if st != NF_OK:
             raise NfError(st, self.lib.nf_moe_last_error(None).decode())
         self.h = h

@@ -67,3 +67,32 @@ def test_ep_roofline_counts_per_rank_bytes():
         io = 64 * H * 6
         exch = world * 64 * K * H * 8
         assert sum(p["layer"] for p in per) == w_all + world * (shared_router + io) + exch
+
+
+def test_replica_choice_lowers_the_busiest_rank():
+    """choose_replicas picks hot experts only while replicating them lowers the
+    busiest rank's pick load: a skewed count matrix (expert 0 hot, owned by
+    rank 0) gets expert 0 replicated and a balanced one gets nothing."""
+    import numpy as np
+
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    world, E = 2, 8
+    counts = np.full((world, E), 10, dtype=np.int64)
+    counts[:, 0] = 500  # every rank's tokens pick expert 0 (rank 0 owns 0-3)
+    reps = bench.choose_replicas(counts, E // world)
+    assert 0 in reps
+
+    def busiest(rs):
+        tot = counts.sum(0)
+        load = np.zeros(world)
+        for e in range(E):
+            if e in rs:
+                load += counts[:, e]
+            else:
+                load[e // (E // world)] += tot[e]
+        return load.max()
+
+    assert busiest(set(reps)) < busiest(set())
+    assert bench.choose_replicas(np.full((world, E), 10, dtype=np.int64), E // world) == []

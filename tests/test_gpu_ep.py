@@ -2,7 +2,9 @@
 process per GPU) against one GPU holding every expert: the layer outputs and
 routes must be identical bit for bit, over both exchanges inside the library
 -- NVLink peer memory (CUDA IPC mailboxes, run in graph mode for several
-steps) and NCCL point-to-point.  Skipped on fewer than two GPUs."""
+steps) and NCCL point-to-point, also with the hot experts replicated on
+every rank (their picks computed where the token is).  Skipped on fewer
+than two GPUs."""
 import os
 import socket
 import sys
@@ -31,12 +33,16 @@ def _tokens(case: str, world: int):
     if case == "uneven":  # all tokens on rank 0, none on rank 1
         lay, x = wl.config_layer("c1")
         return lay, [x] + [x[:0]] * (world - 1)
-    # skewed: Zipf log-prior on the bias sends most picks to the first experts (rank 0)
+    # skewed (and skewed_rep, the same routing with experts 0-3 replicated):
+    # Zipf log-prior on the bias sends most picks to the first experts (rank 0)
     cfg = dict(wl.CONFIGS["c1"])
     lay = wl.make_layer(cfg, seed=7)
     lay.bias = (lay.bias + np.log((np.arange(lay.experts) + 1.0) ** -1.1)).astype(np.float32)
     x = wl.make_tokens(cfg, seed=7, tokens=96 * world)
     return lay, np.array_split(x, world)
+
+
+REPLICAS = [0, 1, 2, 3]  # the skewed routing's hottest experts
 
 
 def _rank(rank: int, world: int, port: int, out_dir: str, case: str, transport: str) -> None:
@@ -53,7 +59,8 @@ def _rank(rank: int, world: int, port: int, out_dir: str, case: str, transport: 
     lay, parts = _tokens(case, world)
     cap = max(p.shape[0] for p in parts)
     layer = m.MoeLayer(lay.hidden, lay.experts, lay.top_k, lay.inter, lay.shared_inter, routed_scaling=lay.scaling,
-                       swiglu_limit=lay.swiglu_limit, max_tokens=max(cap, 1), device=rank, ep=(rank, world, gid[0]))
+                       swiglu_limit=lay.swiglu_limit, max_tokens=max(cap, 1), device=rank, ep=(rank, world, gid[0]),
+                       ep_replicas=REPLICAS if case == "skewed_rep" else None)
     layer.bind_layer(lay)
     got_transport = layer.ep_transport()
     xb = parts[rank]
@@ -85,7 +92,7 @@ def _rank(rank: int, world: int, port: int, out_dir: str, case: str, transport: 
 
 
 @pytest.mark.parametrize("transport", ["nvlink", "nccl"])
-@pytest.mark.parametrize("case", ["c1", "uneven", "skewed"])
+@pytest.mark.parametrize("case", ["c1", "uneven", "skewed", "skewed_rep"])
 @pytest.mark.parametrize("ranks", ["two", "all"])
 def test_ep_matches_one_gpu(tmp_path, case, transport, ranks):
     n = torch.cuda.device_count()
