@@ -276,7 +276,14 @@ NF_API int nf_moe_create_dense(int32_t hidden, int32_t inter, float swiglu_limit
  * 0: the forward exchanges rows with the other ranks (NCCL point-to-point,
  * loaded from libnccl.so.2 at the first EP handle, or NVLink peer memory:
  * see nf_moe_ep_transport).
- * Results are bit-identical to one GPU holding every expert. */
+ * Results are bit-identical to one GPU holding every expert.
+ * Create is collective: a rank whose own part fails (an allocation, its
+ * experts handle) still joins the communicator and the first set-up
+ * exchange and reports its status there, so every rank's create returns
+ * that status ("expert-parallel set-up failed on rank p (...)") instead of
+ * waiting for the failed rank.  Only a failure of the rank's router and
+ * shared-expert part, or of the exchanges' small staging buffer, returns
+ * before the communicator exists. */
 #define NF_EP_ID_BYTES 128
 NF_API int nf_ep_unique_id(uint8_t* group_id_out, int len);
 /* Expert parallelism with replicated hot experts: every rank also holds

@@ -61,10 +61,18 @@ bool ep_allgather_host(nf_moe* h, const void* mine, size_t bytes, void* all) {
     return nccl_allgather_records(h->nccl, h->ep_stage, h->stream, h->ep_world, mine, bytes, all);
 }
 
+// The words a set-up record's failure status is reported with.
+const char* setup_failure_what(int status) {
+    return status == NF_ERR_NOMEM ? "device allocation" : status == NF_ERR_CUDA ? "initialisation" : "handle creation";
+}
+
 // Peer-memory transport set-up (collective: every rank calls it after the
 // communicator exists).  Leaves h->ep_p2p false, with nothing mapped, unless
 // every rank exported its mailbox and mapped every other rank's.
-int ep_p2p_setup(nf_moe* h, std::string* err) {
+// prior_fail: a status (not NF_OK) when this rank's create already failed
+// before the communicator existed; the rank then allocates nothing here and
+// reports the failure in the first exchange, so every rank fails together.
+int ep_p2p_setup(nf_moe* h, std::string* err, int prior_fail) {
     const nf_moe_desc& d = h->d;
     const int R = h->ep_world, me = h->ep_rank;
     const int64_t H = d.hidden, cap = static_cast<int64_t>(d.max_tokens) * d.top_k;
@@ -82,11 +90,13 @@ int ep_p2p_setup(nf_moe* h, std::string* err) {
     // A local failure here does not return at once: the other ranks are about
     // to enter the handle exchange, so this rank joins it too, reporting the
     // failure, and every rank then fails the create together.
-    int local_fail = 0;  // 0, NF_ERR_NOMEM or NF_ERR_CUDA
+    int local_fail = prior_fail;  // NF_OK, or the failure's status
     // ep_done: the send's and the return's per-peer block counters, then the
     // fused return's finished-tile counter
-    if (!h->alloc(&h->ep_mbox, L.total) || !h->alloc(&h->ep_epoch, 1) || !h->alloc(&h->ep_done, 2 * kEpMaxRanks + 1) ||
-        !h->alloc(&h->ep_seen, kEpMaxRanks)) {
+    if (local_fail != NF_OK) {
+        // nothing to allocate: the create already failed on this rank
+    } else if (!h->alloc(&h->ep_mbox, L.total) || !h->alloc(&h->ep_epoch, 1) ||
+               !h->alloc(&h->ep_done, 2 * kEpMaxRanks + 1) || !h->alloc(&h->ep_seen, kEpMaxRanks)) {
         cudaGetLastError();
         local_fail = NF_ERR_NOMEM;
     } else if (cudaMemset(h->ep_mbox, 0, L.total) != cudaSuccess || cudaMemset(h->ep_epoch, 0, 4) != cudaSuccess ||
@@ -121,10 +131,10 @@ int ep_p2p_setup(nf_moe* h, std::string* err) {
         const Rec& q = all[static_cast<size_t>(p)];
         if (!q.sound) {
             char msg[128];
-            std::snprintf(msg, sizeof(msg), "mailbox set-up failed on rank %d (%s)", p,
-                          q.status == NF_ERR_CUDA ? "initialisation" : "device allocation");
+            std::snprintf(msg, sizeof(msg), "expert-parallel set-up failed on rank %d (%s)", p,
+                          setup_failure_what(q.status));
             *err = msg;
-            return q.status == NF_ERR_CUDA ? NF_ERR_CUDA : NF_ERR_NOMEM;
+            return q.status != NF_OK ? q.status : NF_ERR_NOMEM;
         }
     }
     int opened = 1;
@@ -435,22 +445,35 @@ int nf_moe_create_ep_replicated(const nf_moe_desc* desc, int device, int rank, i
     di.normalize = 0;
     di.routed_scaling = 1.f;
     di.max_tokens = world * d.max_tokens * d.top_k;
-    if ((st = create_impl(di, device, kRoleExperts, &h->inner, &err)) != NF_OK) {
-        nf_moe_destroy(h);
-        return st;
-    }
     int prev = 0;
     cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    // The staging buffer of the set-up exchanges comes first: with it this
+    // rank can join them whatever fails next.  Without it the rank cannot,
+    // and it returns before the communicator exists (the other ranks' own
+    // communicator initialisation then waits for it).
+    if (!h->alloc(&h->ep_stage, kEpRecBytes * (world + 1))) {
+        cudaGetLastError();
+        cudaSetDevice(prev);
+        nf_moe_destroy(h);
+        err = "device allocation failed";
+        return NF_ERR_NOMEM;
+    }
+    // From here a local failure does not return at once: the other ranks are
+    // about to initialise the communicator and enter the first set-up
+    // exchange, so this rank joins both and reports the failure there
+    // (ep_p2p_setup), and every rank fails the create together.
+    int local_fail = NF_OK;
+    std::string local_err;
+    cudaSetDevice(prev);
+    local_fail = create_impl(di, device, kRoleExperts, &h->inner, &local_err);
     cudaSetDevice(device);
     const int64_t H = d.hidden, pairs = static_cast<int64_t>(d.max_tokens) * d.top_k, cap = world * pairs;
     const int64_t ob = d.expert_kind == NF_EXPERTS_NVFP4 ? 2 : 4;
     // the send layout, used by both transports (the NCCL transport's own
     // buffers follow once the group has chosen it)
-    // (and the staging buffer of the set-up exchanges: allocated before the
-    // communicator, so that every exchange has a buffer on every rank)
-    bool ok = h->alloc(&h->ep_send_e, pairs) && h->alloc(&h->ep_send_tok, pairs) && h->alloc(&h->ep_slot, pairs) &&
-              h->alloc(&h->ep_cnt, 2 * world) && h->alloc(&h->ep_stage, kEpRecBytes * (world + 1)) &&
-              h->alloc(&h->ep_route, 2 * d.experts);
+    bool ok = local_fail == NF_OK && h->alloc(&h->ep_send_e, pairs) && h->alloc(&h->ep_send_tok, pairs) &&
+              h->alloc(&h->ep_slot, pairs) && h->alloc(&h->ep_cnt, 2 * world) && h->alloc(&h->ep_route, 2 * d.experts);
     if (ok) {
         // where each expert's picks go: its owner and its index there, or this
         // rank's replica slot
@@ -464,12 +487,10 @@ int nf_moe_create_ep_replicated(const nf_moe_desc* desc, int device, int rank, i
         }
         ok = cudaMemcpy(h->ep_route, route.data(), route.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess;
     }
-    if (!ok) {
+    if (local_fail == NF_OK && !ok) {
         cudaGetLastError();
-        cudaSetDevice(prev);
-        nf_moe_destroy(h);
-        err = "device allocation failed";
-        return NF_ERR_NOMEM;
+        local_fail = NF_ERR_NOMEM;
+        local_err = "device allocation failed";
     }
     ncclUniqueId id;
     std::memcpy(&id, group_id, sizeof(id));
@@ -483,7 +504,8 @@ int nf_moe_create_ep_replicated(const nf_moe_desc* desc, int device, int rank, i
     }
     h->nccl = comm;
     cudaSetDevice(device);
-    st = ep_p2p_setup(h, &err);
+    st = ep_p2p_setup(h, &err, local_fail);
+    if (local_fail != NF_OK && st == local_fail && !local_err.empty()) err = local_err;  // this rank's own reason
     if (st == NF_OK && !h->ep_p2p) {
         // NCCL transport: packed rows, receive and return buffers, host counts
         uint8_t* back = nullptr;

@@ -80,7 +80,13 @@ def mailbox_exchange(plans: list, cap: int):
     return out
 
 
-NF_OK, NF_ERR_CUDA, NF_ERR_NOMEM = 0, 6, 9
+NF_OK, NF_ERR_CUDA, NF_ERR_UNSUPPORTED, NF_ERR_NOMEM = 0, 6, 8, 9
+
+
+def setup_failure_what(status: int) -> str:
+    """The words a set-up record's failure status is reported with
+    (setup_failure_what in csrc/nf_ep.cu)."""
+    return {NF_ERR_NOMEM: "device allocation", NF_ERR_CUDA: "initialisation"}.get(status, "handle creation")
 
 
 def setup_agreement(exchange, local_status: int, want_nvlink: bool, export_ok: bool, map_peers) -> tuple:
@@ -88,14 +94,17 @@ def setup_agreement(exchange, local_status: int, want_nvlink: bool, export_ok: b
     csrc/nf_ep.cu), restated so that the protocol can be run by CPU ranks.
 
     exchange(record) -> every rank's record (an all-gather); local_status is
-    this rank's mailbox allocation / initialisation outcome (NF_OK,
-    NF_ERR_NOMEM or NF_ERR_CUDA); export_ok whether its mailbox could be
-    exported; map_peers() maps every peer's mailbox and returns success.
+    this rank's set-up outcome so far: NF_OK, or the status of a failure in
+    its handle creation before the communicator existed (the inner experts
+    handle or the send buffers: NF_ERR_NOMEM and the like, nf_moe_create_ep)
+    or in its mailbox allocation / initialisation (NF_ERR_NOMEM,
+    NF_ERR_CUDA); export_ok whether its mailbox could be exported;
+    map_peers() maps every peer's mailbox and returns success.
 
     A rank whose own set-up failed still joins the first exchange and reports
     the failure there, so no rank is left waiting in it; every rank reads the
     same records, so every rank then fails together with the failing rank's
-    status.  Otherwise every rank maps its peers, the group agrees on whether
+    status (the lowest failing rank's, when several fail).  Otherwise every rank maps its peers, the group agrees on whether
     all did (second exchange), and falls back to NCCL together when one did
     not (a third exchange is the barrier before the mailboxes are released).
     Returns (status, transport or message, exchanges taken)."""
@@ -105,9 +114,7 @@ def setup_agreement(exchange, local_status: int, want_nvlink: bool, export_ok: b
     n += 1
     for p, q in enumerate(recs):
         if not q["sound"]:
-            what = "initialisation" if q["status"] == NF_ERR_CUDA else "device allocation"
-            status = NF_ERR_CUDA if q["status"] == NF_ERR_CUDA else NF_ERR_NOMEM
-            return status, f"mailbox set-up failed on rank {p} ({what})", n
+            return q["status"], f"expert-parallel set-up failed on rank {p} ({setup_failure_what(q['status'])})", n
     opened = all(q["ok"] for q in recs) and bool(map_peers())
     recs = exchange({"ok": opened})
     n += 1

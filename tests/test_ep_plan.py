@@ -220,6 +220,10 @@ def _setup_rank(rank: int, world: int, port: int, out_dir: str, case: str) -> No
         local = plan.NF_ERR_NOMEM
     if case == "memset" and rank == 0:
         local = plan.NF_ERR_CUDA
+    if case == "inner" and rank == 1:
+        local = plan.NF_ERR_UNSUPPORTED  # its experts handle was refused before the communicator existed
+    if case == "two" and rank in (1, 2):
+        local = plan.NF_ERR_NOMEM if rank == 1 else plan.NF_ERR_CUDA
     mapped = not (case == "nomap" and rank == 1)
     st, what, n = plan.setup_agreement(exchange, local, True, True, lambda: mapped)
     # a last exchange after set-up: only reachable when every rank took the
@@ -232,12 +236,15 @@ def _setup_rank(rank: int, world: int, port: int, out_dir: str, case: str) -> No
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case,world", [("ok", 2), ("nomem", 2), ("memset", 4), ("nomap", 4)])
+@pytest.mark.parametrize("case,world", [("ok", 2), ("nomem", 2), ("memset", 4), ("nomap", 4), ("inner", 2),
+                                        ("two", 4)])
 def test_setup_agreement_every_rank_takes_the_same_exchanges(tmp_path, case, world):
-    """A rank whose mailbox allocation (or initialisation) fails still joins the
-    set-up exchange: every rank then returns that failure together, after the
-    same number of exchanges; a rank that cannot map a peer makes every rank
-    fall back to NCCL together."""
+    """A rank whose set-up fails -- its handle creation before the
+    communicator existed, or its mailbox allocation or initialisation -- still
+    joins the set-up exchange: every rank then returns that failure together,
+    after the same number of exchanges (with several failing ranks, the lowest
+    one's); a rank that cannot map a peer makes every rank fall back to NCCL
+    together."""
     import torch.multiprocessing as mp
 
     mp.start_processes(_setup_rank, args=(world, _free_port(), str(tmp_path), case), nprocs=world,
@@ -252,5 +259,9 @@ def test_setup_agreement_every_rank_takes_the_same_exchanges(tmp_path, case, wor
         assert st == plan.NF_ERR_NOMEM and f"rank {world - 1}" in msgs[0] and n == 1
     elif case == "memset":
         assert st == plan.NF_ERR_CUDA and "rank 0 (initialisation)" in msgs[0] and n == 1
+    elif case == "inner":
+        assert st == plan.NF_ERR_UNSUPPORTED and "rank 1 (handle creation)" in msgs[0] and n == 1
+    elif case == "two":
+        assert st == plan.NF_ERR_NOMEM and "rank 1 (device allocation)" in msgs[0] and n == 1
     else:
         assert (st, msgs[0], n) == (plan.NF_OK, "nccl", 3)
