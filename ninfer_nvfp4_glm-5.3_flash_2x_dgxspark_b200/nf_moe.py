@@ -27,6 +27,7 @@ NF_OK = 0
 NF_ERR = {1: "INVALID", 2: "SHAPE", 3: "LAYOUT", 4: "SCALE", 5: "STATE", 6: "CUDA", 7: "TIMEOUT",
           8: "UNSUPPORTED", 9: "NOMEM", 10: "CAPACITY"}
 PROJ_GATE, PROJ_UP, PROJ_DOWN = 0, 1, 2
+_PROJ_NAMES = {PROJ_GATE: "gate_proj", PROJ_UP: "up_proj", PROJ_DOWN: "down_proj"}
 BF16_ROUTER, BF16_SHARED_GATE, BF16_SHARED_UP, BF16_SHARED_DOWN = 0, 1, 2, 3
 BF16_EXPERT_GATE, BF16_EXPERT_UP, BF16_EXPERT_DOWN = 4, 5, 6
 F32_ROUTER_BIAS = 0
@@ -243,11 +244,24 @@ class MoeLayer:
             raise NfError(st, self.lib.nf_moe_last_error(self.h).decode())
 
     # ---- binding -----------------------------------------------------------
+    def _proj_label(self, expert: int, proj: int) -> str:
+        """The tensor prefix the library's messages name (proj_label in
+        csrc/nf_moe.cu)."""
+        return f"mlp.experts.{expert}.{_PROJ_NAMES.get(proj, 'proj')}"
+
     def bind_nvfp4(self, expert: int, proj: int, packed: np.ndarray, scales: np.ndarray, weight_scale_2: float,
                    input_scale: float) -> None:
+        """Codes U8 [rows, cols / 2] and E4M3 block scales [rows, cols / 16].
+        The arrays' ranks and the scales' shape are checked here as
+        linear_nvfp4 checks them (src/text_forward.cpp:837-843): the C ABI takes
+        only rows and cols, so a shorter scale array would be read past its end."""
         packed = np.ascontiguousarray(packed, dtype=np.uint8)
         scales = np.ascontiguousarray(scales, dtype=np.uint8)
+        if packed.ndim != 2 or scales.ndim != 2:
+            raise NfError(3, f"NVFP4 layout {self._proj_label(expert, proj)}")
         rows, half = packed.shape
+        if scales.shape != (rows, 2 * half // 16):
+            raise NfError(2, f"NVFP4 shape {self._proj_label(expert, proj)}")
         self._check(self.lib.nf_moe_bind_nvfp4(self.h, expert, proj, _ptr(packed), _ptr(scales),
                                                float(weight_scale_2), float(input_scale), rows, 2 * half))
 
@@ -340,7 +354,13 @@ class MoeLayer:
         (y, idx, w) reuses caller-owned host arrays (page-locked ones make the
         device-to-host copies direct); idx and w may be None."""
         x = np.ascontiguousarray(x, dtype=np.float32)
+        H = self.desc.hidden
+        # the library copies tokens x hidden floats from each host array
+        if x.ndim != 2 or x.shape[1] != H:
+            raise ValueError(f"x must be [tokens, {H}] float32")
         T = x.shape[0]
+        if residual is not None and np.shape(residual) != x.shape:
+            raise ValueError("residual must have x's shape")
         if out is not None:
             y, idx, w = out
             for a, shape, dt in ((y, x.shape, np.float32), (idx, (T, self.desc.top_k), np.int32),
@@ -411,6 +431,9 @@ class DenseMlp(MoeLayer):
     src/text_forward.cpp:909-915) resident on one GPU: a one-expert handle
     without a router (nf_moe_create_dense) whose gate/up epilogue applies
     swiglu_clamp_bf16.  forward() / forward_host() take no route buffers."""
+
+    def _proj_label(self, expert: int, proj: int) -> str:
+        return f"mlp.{_PROJ_NAMES.get(proj, 'proj')}"
 
     def __init__(self, hidden: int, inter: int, *, swiglu_limit: float = 10.0, max_tokens: int = 64,
                  device: int = 0):
@@ -510,18 +533,48 @@ def safetensors_store(directory) -> dict:
     return out
 
 
+_U8, _F32 = ("torch.uint8",), ("torch.float32",)
+
+
+def _dev_all(specs) -> tuple:
+    """_dev over (buffer, elements, dtypes, name) specs on the current device
+    (the one these free functions run on)."""
+    d = _current_device() if any(getattr(a, "is_cuda", False) for a, *_ in specs) else -1
+    return tuple(_dev(a, max(int(n), 0), dt, name, d) for a, n, dt, name in specs)
+
+
+# The format helpers below return the library's status like the C ABI; a
+# buffer refused on the host (a host array, another device, a dtype or size
+# the call cannot use) returns NF_ERR_INVALID without calling the library.
 def dequantize(packed_dev, scales_dev, global_scale: float, rows: int, cols: int, out_dev, stream=0) -> int:
-    return load().nf_nvfp4_dequantize(_ptr(packed_dev), _ptr(scales_dev), global_scale, rows, cols, _ptr(out_dev),
-                                      stream or None)
+    """packed U8 [rows, cols / 2], scales U8 [rows, cols / 16] -> out F32
+    [rows, cols] (device buffers)."""
+    try:
+        p = _dev_all(((packed_dev, rows * cols // 2, _U8, "packed"), (scales_dev, rows * cols // 16, _U8, "scales"),
+                      (out_dev, rows * cols, _F32, "out")))
+    except NfError as e:
+        return e.status
+    return load().nf_nvfp4_dequantize(p[0], p[1], global_scale, rows, cols, p[2], stream or None)
 
 
 def quantize(x_dev, rows: int, cols: int, input_scale: float, codes_dev, scales_dev, fake_dev=None, stream=0) -> int:
-    return load().nf_nvfp4_quantize(_ptr(x_dev), rows, cols, input_scale, _ptr(codes_dev), _ptr(scales_dev),
-                                    _ptr(fake_dev), stream or None)
+    """x F32 [rows, cols] -> codes U8 [rows, cols / 2], scales U8 [rows,
+    cols / 16], optional fake-quant F32 [rows, cols] (device buffers)."""
+    try:
+        p = _dev_all(((x_dev, rows * cols, _F32, "x"), (codes_dev, rows * cols // 2, _U8, "codes"),
+                      (scales_dev, rows * cols // 16, _U8, "scales"), (fake_dev, rows * cols, _F32, "fake")))
+    except NfError as e:
+        return e.status
+    return load().nf_nvfp4_quantize(p[0], rows, cols, input_scale, p[1], p[2], p[3], stream or None)
 
 
 def sigmoid_ref(x_dev, n: int, y_dev, stream=0) -> int:
-    return load().nf_sigmoid_ref(_ptr(x_dev), n, _ptr(y_dev), stream or None)
+    """y = sigmoid(x) over n F32 elements (device buffers)."""
+    try:
+        p = _dev_all(((x_dev, n, _F32, "x"), (y_dev, n, _F32, "y")))
+    except NfError as e:
+        return e.status
+    return load().nf_sigmoid_ref(p[0], n, p[1], stream or None)
 
 
 NOALLOC_MAX_SCORES = 16384  # tokens x experts of one nf_router_topk_noalloc call

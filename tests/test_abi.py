@@ -183,3 +183,86 @@ def test_noalloc_wrapper_checks_buffers_before_the_library():
         assert st == 0 and len(calls) == 1
     finally:
         m._lib = real
+
+
+def test_format_helpers_and_binds_check_arrays_before_the_library():
+    """The NVFP4 format helpers refuse host arrays and short or mistyped
+    device buffers with NF_ERR_INVALID and no library call; bind_nvfp4 refuses
+    code / scale arrays that linear_nvfp4 refuses (src/text_forward.cpp:
+    837-843: "NVFP4 layout" for a rank other than 2, "NVFP4 shape" for scales
+    that are not [rows, cols / 16]), before the library could read past a
+    short scale array; forward_host refuses an x that is not [tokens, hidden]
+    and a residual of another shape."""
+    import numpy as np
+
+    m = nfm()
+    calls = []
+
+    class Spy:
+        def __getattr__(self, name):
+            def call(*a):
+                calls.append(name)
+                return 0
+            return call
+
+    class FakeCuda:
+        def __init__(self, n, dtype):
+            self.is_cuda, self.dtype, self.n = True, dtype, n
+            self.device = type("D", (), {"index": 0})()
+
+        def is_contiguous(self):
+            return True
+
+        def numel(self):
+            return self.n
+
+        def data_ptr(self):
+            return 1 << 20
+
+    real = m._lib
+    m._lib = Spy()
+    real_dev = m._current_device
+    m._current_device = lambda: 0  # no GPU here: the fakes claim cuda:0
+    try:
+        rows, cols = 4, 64
+        u8 = lambda n: FakeCuda(n, "torch.uint8")  # noqa: E731
+        f32 = lambda n: FakeCuda(n, "torch.float32")  # noqa: E731
+        assert m.dequantize(np.zeros(rows * cols // 2, np.uint8), u8(rows * cols // 16), 1.0, rows, cols,
+                            f32(rows * cols)) == 1
+        assert m.dequantize(u8(rows * cols // 2), u8(rows * cols // 16 - 1), 1.0, rows, cols, f32(rows * cols)) == 1
+        assert m.dequantize(u8(rows * cols // 2), u8(rows * cols // 16), 1.0, rows, cols,
+                            FakeCuda(rows * cols, "torch.float16")) == 1
+        assert m.quantize(f32(rows * cols), rows, cols, 1.0, u8(rows * cols // 2), u8(rows * cols // 16),
+                          f32(rows * cols - 1)) == 1
+        assert m.sigmoid_ref(np.zeros(8, np.float32), 8, f32(8)) == 1
+        assert not calls
+        assert m.dequantize(u8(rows * cols // 2), u8(rows * cols // 16), 1.0, rows, cols, f32(rows * cols)) == 0
+        assert m.quantize(f32(rows * cols), rows, cols, 1.0, u8(rows * cols // 2), u8(rows * cols // 16)) == 0
+        assert m.sigmoid_ref(f32(8), 8, f32(8)) == 0
+        assert calls == ["nf_nvfp4_dequantize", "nf_nvfp4_quantize", "nf_sigmoid_ref"]
+        calls.clear()
+
+        H, I = 256, 128
+        layer = m.MoeLayer.borrow(1234, m.Desc(H, 8, 2, I, 0, 1, 1, 1, 1.0, 10.0, m.EXPERTS_NVFP4, 4), 0)
+        layer.lib = Spy()
+        codes = np.zeros((I, H // 2), np.uint8)
+        with pytest.raises(m.NfError, match="NVFP4 shape mlp.experts.3.up_proj") as e:
+            layer.bind_nvfp4(3, m.PROJ_UP, codes, np.zeros((I, H // 16 - 1), np.uint8), 1 / 448, 1 / 6)
+        assert e.value.status == 2
+        with pytest.raises(m.NfError, match="NVFP4 layout mlp.experts.3.down_proj") as e:
+            layer.bind_nvfp4(3, m.PROJ_DOWN, codes, np.zeros(I * H // 16, np.uint8), 1 / 448, 1 / 6)
+        assert e.value.status == 3
+        dense = m.DenseMlp.borrow(1234, m.Desc(H, 1, 1, I, 0, 1, 1, 1, 1.0, 10.0, m.EXPERTS_NVFP4, 4), 0)
+        dense.lib = Spy()
+        with pytest.raises(m.NfError, match="NVFP4 shape mlp.gate_proj"):
+            dense.bind_nvfp4(0, m.PROJ_GATE, codes, np.zeros((I - 1, H // 16), np.uint8), 1 / 448, 1 / 6)
+        with pytest.raises(ValueError, match=r"\[tokens, 256\]"):
+            layer.forward_host(np.zeros((2, H - 16), np.float32))
+        with pytest.raises(ValueError, match="residual"):
+            layer.forward_host(np.zeros((2, H), np.float32), np.zeros((1, H), np.float32))
+        assert not calls
+        layer.bind_nvfp4(3, m.PROJ_UP, codes, np.zeros((I, H // 16), np.uint8), 1 / 448, 1 / 6)
+        assert calls == ["nf_moe_bind_nvfp4"]
+    finally:
+        m._lib = real
+        m._current_device = real_dev
