@@ -51,11 +51,15 @@ inline float scalar(const StoreLookup& store, const std::string& name) {
 // One NVFP4 linear by checkpoint name (linear_nvfp4's lookups,
 // src/text_forward.cpp:833-843): <base>.weight U8 [N, K/2],
 // <base>.weight_scale F8_E4M3 [N, K/16], rank-0 F32 weight_scale_2 and
-// input_scale.  Returns the library's status.
+// input_scale.  Returns the library's status.  Both tensors must be rank 2
+// ("NVFP4 layout") and the scales [N, K/16] for codes [N, K/2] ("NVFP4
+// shape"): the library takes N and K only and reads N K/16 scale bytes.
 inline int bind_nvfp4_named(nf_moe* h, int expert, int proj, const StoreLookup& store, const std::string& base) {
     const TensorView& w = get(store, base + ".weight");
     const TensorView& s = get(store, base + ".weight_scale");
-    if (w.kind != 'u' || s.kind != '8' || w.shape.size() != 2) throw std::runtime_error("NVFP4 layout " + base);
+    if (w.kind != 'u' || s.kind != '8' || w.shape.size() != 2 || s.shape.size() != 2)
+        throw std::runtime_error("NVFP4 layout " + base);
+    if (s.dim(0) != w.dim(0) || s.dim(1) != w.dim(1) * 2 / 16) throw std::runtime_error("NVFP4 shape " + base);
     return nf_moe_bind_nvfp4(h, expert, proj, static_cast<const uint8_t*>(w.data), static_cast<const uint8_t*>(s.data),
                              scalar(store, base + ".weight_scale_2"), scalar(store, base + ".input_scale"), w.dim(0),
                              w.dim(1) * 2);

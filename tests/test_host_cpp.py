@@ -133,6 +133,25 @@ def test_demo_missing_expert_tensor_names_it(tmp_path):
     assert r.returncode == 1 and f"missing tensor {PREFIX}mlp.experts.5.up_proj.weight_scale" in r.stderr
 
 
+@pytest.mark.gpu
+def test_demo_refuses_scales_of_the_wrong_rank_or_shape(tmp_path):
+    """linear_nvfp4's checks (src/text_forward.cpp:837-843) by checkpoint name:
+    a weight_scale that is not rank 2 is "NVFP4 layout <name>", one that is not
+    [N, K/16] for codes [N, K/2] is "NVFP4 shape <name>" (the library would
+    otherwise read N K/16 bytes past a shorter tensor)."""
+    wl = workload()
+    lay, x_bits = wl.config_layer("c0")
+    name = f"{PREFIX}mlp.experts.2.down_proj"
+    for scales, msg in ((lay.down_scales[2].ravel(), "NVFP4 layout"), (lay.down_scales[2][:, :-1], "NVFP4 shape"),
+                        (lay.down_scales[2][:-1], "NVFP4 shape")):
+        t = layer_tensors(lay)
+        t[name + ".weight_scale"] = ("8", scales)
+        t["x"] = ("f", wl.bf16_bits_to_f32(x_bits))
+        write_nft(tmp_path / "c0.nft", t)
+        r = run_demo(tmp_path / "c0.nft", tmp_path / "y.f32", lay)
+        assert r.returncode == 1 and f"{msg} {name}" in r.stderr, r.stderr
+
+
 # ---- safetensors checkpoints (host/nf_safetensors.hpp, nf_moe.safetensors_store)
 ST_DTYPE = {"b": "BF16", "f": "F32", "u": "U8", "8": "F8_E4M3"}
 
