@@ -67,7 +67,15 @@ public:
                 const char e = s_[i_++];
                 if (e == 'u') {  // names are ASCII in practice; keep the code point's low byte
                     if (i_ + 4 > s_.size()) break;
-                    c = static_cast<char>(std::stoul(s_.substr(i_, 4), nullptr, 16) & 0xffu);
+                    unsigned v = 0;
+                    for (int k = 0; k < 4; ++k) {
+                        const char h = s_[i_ + k];
+                        const int digit = h >= '0' && h <= '9' ? h - '0' : h >= 'a' && h <= 'f' ? h - 'a' + 10
+                                          : h >= 'A' && h <= 'F' ? h - 'A' + 10 : -1;
+                        if (digit < 0) throw std::runtime_error("bad safetensors header");
+                        v = v * 16 + static_cast<unsigned>(digit);
+                    }
+                    c = static_cast<char>(v & 0xffu);
                     i_ += 4;
                 } else {
                     c = e == 'n' ? '\n' : e == 't' ? '\t' : e == 'r' ? '\r' : e == 'b' ? '\b' : e == 'f' ? '\f' : e;
@@ -271,9 +279,10 @@ private:
         if (t.kind == '?' || !have_shape || begin < 0) throw std::runtime_error("incomplete tensor header for " + name);
         if (end < begin || static_cast<uint64_t>(end) > data_len)
             throw std::runtime_error("tensor data out of range for " + name);
+        // (below 2^60 elements the byte count cannot wrap: at most 4 bytes each)
         uint64_t count = 1;
         for (int64_t d : t.shape) {
-            if (d > 0 && count > (uint64_t{1} << 62) / static_cast<uint64_t>(d))
+            if (d > 0 && count > (uint64_t{1} << 60) / static_cast<uint64_t>(d))
                 throw std::runtime_error("tensor size mismatch for " + name);  // larger than any shard
             count *= static_cast<uint64_t>(d);
         }

@@ -15,6 +15,7 @@ data_ptr() or integers); torch is only used by callers for device memory.
 from __future__ import annotations
 
 import ctypes
+import math
 import os
 from pathlib import Path
 from typing import Mapping
@@ -524,10 +525,16 @@ def safetensors_store(directory) -> dict:
             shape, offs = info.get("shape"), info.get("data_offsets")
             if shape is None or offs is None:
                 raise NfError(3, f"incomplete tensor header for {name}")
+            if len(shape) > 8:
+                raise NfError(3, f"rank above 8 for {name}")
+            shape = [int(v) for v in shape]
+            if any(v < 0 for v in shape):
+                raise NfError(3, f"negative dimension for {name}")
             b, e = int(offs[0]), int(offs[1])
             if b < 0 or e < b or e > data.size:
                 raise NfError(3, f"tensor data out of range for {name}")
-            if int(np.prod(shape, dtype=np.int64)) * np.dtype(dt).itemsize != e - b:
+            # (Python integers: the element count cannot wrap)
+            if math.prod(shape) * np.dtype(dt).itemsize != e - b:
                 raise NfError(3, f"tensor size mismatch for {name}")
             out[name] = data[b:e].view(dt).reshape(shape)
     return out

@@ -228,6 +228,21 @@ def test_safetensors_store_errors(tmp_path):
     write_safetensors(size / "model.safetensors", {"x": ("f", np.zeros((2, 4), np.float32))},
                       lambda h: h["x"].update(shape=[2, 3]))
     cases.append((size, "tensor size mismatch for x"))
+    # an element count whose byte size wraps a 64-bit product (2^62 F32 in
+    # zero bytes), one past any shard, a negative shape, a bad \u escape
+    for tag, patch, msg in (("wrap", dict(shape=[1 << 31, 1 << 31], data_offsets=[0, 0]), "tensor size mismatch for x"),
+                            ("huge", dict(shape=[1 << 32, 1 << 32], data_offsets=[0, 0]), "tensor size mismatch for x"),
+                            ("neg", dict(shape=[-2, -4]), "negative dimension for x")):
+        d = tmp_path / tag
+        d.mkdir()
+        write_safetensors(d / "model.safetensors", {"x": ("f", np.zeros((2, 4), np.float32))},
+                          lambda h, patch=patch: h["x"].update(**patch))
+        cases.append((d, msg))
+    esc = tmp_path / "escape"
+    esc.mkdir()
+    h = b'{"x\\uZZZZ":{"dtype":"F32","shape":[1],"data_offsets":[0,4]}}'
+    (esc / "model.safetensors").write_bytes(struct.pack("<Q", len(h)) + h + bytes(4))
+    cases.append((esc, "bad safetensors header"))
     shard = tmp_path / "shard"
     write_checkpoint(shard, {"x": ("f", np.zeros((2, 4), np.float32)), "y": ("f", np.zeros(3, np.float32))})
     (shard / "model-00002-of-00002.safetensors").unlink()
