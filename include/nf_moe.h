@@ -139,6 +139,8 @@ NF_API int nf_moe_finalize(nf_moe* handle);
  *   (x_dev, residual_dev and y_dev 16-byte aligned, else NF_ERR_LAYOUT)
  *   topk_idx_dev INT32 [tokens, top_k] or NULL (router_select indices)
  *   topk_w_dev   F32 [tokens, top_k] or NULL (router_select weights)
+ * With tokens == 0 nothing is read or written, so x_dev and y_dev may be
+ * NULL (an expert-parallel rank without tokens still makes the call).
  * Asynchronous: a device-side failure (bounded wait timeout) is reported by
  * the next call that synchronises (nf_moe_sync or nf_moe_forward_host). */
 NF_API int nf_moe_forward(nf_moe* handle, const uint16_t* x_dev, const float* residual_dev, int tokens, float* y_dev,

@@ -753,13 +753,16 @@ int nf_moe_finalize(nf_moe* h) {
     return NF_OK;
 }
 
+// A device x may be NULL with tokens == 0: nothing reads it then (an
+// expert-parallel rank without tokens still calls the forward for the
+// exchanges).  Host-buffer calls always need their arrays.
 static int check_forward_args(nf_moe* h, const void* x, int tokens, bool device_x = true) {
     if (!h) return NF_ERR_INVALID;
     if (!h->finalized) return h->fail(NF_ERR_STATE, "nf_moe_finalize has not run");
-    if (!x) return h->fail(NF_ERR_INVALID, "null input");
+    if (tokens < 0) return h->fail(NF_ERR_INVALID, "negative token count");
+    if (!x && (tokens > 0 || !device_x)) return h->fail(NF_ERR_INVALID, "null input");
     // the router copies and the combine read and write 16-byte pieces of device rows
     if (device_x && reinterpret_cast<uintptr_t>(x) % 16 != 0) return h->fail(NF_ERR_LAYOUT, "x must be 16-byte aligned");
-    if (tokens < 0) return h->fail(NF_ERR_INVALID, "negative token count");
     if (tokens > h->d.max_tokens) return h->fail(NF_ERR_CAPACITY, "tokens %d exceed max_tokens %d", tokens, h->d.max_tokens);
     return NF_OK;
 }
@@ -1183,7 +1186,7 @@ int nf_moe_forward(nf_moe* h, const uint16_t* x, const float* residual, int toke
                    void* stream) {
     int st = check_forward_args(h, x, tokens);
     if (st != NF_OK) return st;
-    if (!y) return h->fail(NF_ERR_INVALID, "null output");
+    if (!y && tokens > 0) return h->fail(NF_ERR_INVALID, "null output");
     if ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(residual)) % 16 != 0)
         return h->fail(NF_ERR_LAYOUT, "y and residual must be 16-byte aligned");
     if (h->dense && (idx || w)) return h->fail(NF_ERR_INVALID, "a dense MLP has no routes: pass NULL top-k pointers");

@@ -144,6 +144,12 @@ def test_one_token_and_empty_and_capacity():
     x = torch.zeros((1, lay.hidden), dtype=torch.int16, device="cuda")
     yz = torch.empty((1, lay.hidden), dtype=torch.float32, device="cuda")
     layer.forward(x, yz, 0)  # zero tokens is a no-op
+    layer.forward(None, None, 0)  # ... that reads and writes nothing, so it takes NULL buffers
+    layer.route(None, 0)
+    with pytest.raises(m.NfError, match="null input"):
+        layer.forward(None, yz, 1)
+    with pytest.raises(m.NfError, match="null output"):
+        layer.forward(x, None, 1)
     with pytest.raises(RuntimeError, match="max_tokens"):
         layer.forward(x, yz, 17)
     layer.close()
