@@ -1044,7 +1044,11 @@ cudaError_t route_tokens(nf_moe* h, const uint16_t* x, int T, int32_t* idx, floa
     const int H = d.hidden, E = d.experts, K = d.top_k;
     const bool grouped = d.n_group > 1 && d.topk_group < d.n_group;
     h->last_screened = 0;
-    if (!h->screen || T < kScreenMinTokens || grouped || T > d.max_tokens || K > 8)
+    // The screen's bound needs exact products, which the bind-time range
+    // check of the router weights guarantees (router_w_safe).  Weights outside
+    // that range can overflow the reference's sequential chain where the
+    // tensor cores' order does not; such a layer runs every exact chain.
+    if (!h->screen || !h->router_w_safe || T < kScreenMinTokens || grouped || T > d.max_tokens || K > 8)
         return launch_router(x, h->router_w, h->router_wz, h->router_wz16, h->router_bias, T, H, E, K,
                              d.routed_scaling, d.normalize, d.n_group, d.topk_group, h->router_w_safe, h->logits,
                              h->scores, h->choices, idx, w, h->dev_err, s);
