@@ -99,6 +99,70 @@ def test_router_select_bit_exact():
         assert np.array_equal(ia, ib) and np.array_equal(wa.view(np.uint32), wb.view(np.uint32))
 
 
+def same_bits(a: np.ndarray, b: np.ndarray) -> bool:
+    """Equal bit for bit, except that a NaN only has to meet a NaN: its payload
+    follows the order of the operands that made it."""
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    nan = np.isnan(a)
+    return bool(np.array_equal(nan, np.isnan(b)) and np.array_equal(a[~nan].view(np.uint32), b[~nan].view(np.uint32)))
+
+
+def test_router_select_special_logits():
+    """Non-finite and huge logits, with and without renormalisation: the
+    reference's selection takes the first unused expert as its start and
+    replaces it only on a strict ">", so a NaN choice at the lowest unused
+    index is kept (no comparison against it succeeds) and ties keep the lower
+    index."""
+    rng = np.random.Generator(np.random.PCG64(15))
+    specials = np.array([np.nan, np.inf, -np.inf, 3e38, -3e38, 1e-40, -0.0, 88.0, -88.0, 104.0], np.float32)
+    for trial in range(2000):
+        E = int(rng.choice([8, 16, 64]))
+        k = int(rng.integers(1, min(E, 8) + 1))
+        logits = rng.standard_normal(E).astype(np.float32)
+        n_sp = int(rng.integers(1, 4))
+        logits[rng.integers(0, E, n_sp)] = rng.choice(specials, n_sp)
+        if trial % 7 == 0:
+            logits[0] = np.nan  # the first expert scanned
+        bias = rng.uniform(-0.1, 0.1, E).astype(np.float32)
+        if trial % 11 == 0:
+            bias[rng.integers(0, E)] = np.float32(np.inf)
+        normalize, scaling = int(trial % 3 != 0), float(rng.choice([1.0, 2.5]))
+        ia, ib = np.zeros(k, np.int32), np.zeros(k, np.int32)
+        wa, wb = np.zeros(k, np.float32), np.zeros(k, np.float32)
+        PORT.or_router_select(P(logits), P(bias), E, k, scaling, normalize, P(ia), P(wa))
+        REF.ref_router_select(P(logits), P(bias), E, k, scaling, normalize, P(ib), P(wb))
+        assert np.array_equal(ia, ib), (trial, logits, ia, ib)
+        assert same_bits(wa, wb), (trial, wa, wb)
+
+
+def test_gemvs_out_of_range_values_bit_exact():
+    """Both GEMVs on values whose products leave fp32's exact range (huge,
+    tiny, subnormal), overflow to infinity, or carry NaN and infinity: the
+    restatement still follows the reference's rounding step by step."""
+    rng = np.random.Generator(np.random.PCG64(16))
+    rows, cols = 64, 256
+    x = rng.standard_normal(cols).astype(np.float32)
+    x[3], x[17], x[40], x[41], x[99] = 2.0 ** 100, 2.0 ** -120, 1e-42, -3e38, np.float32(2.0 ** 60)
+    for special in (None, np.inf, np.nan):
+        xs = x.copy()
+        if special is not None:
+            xs[200] = special
+        w = wl.f32_to_bf16_bits(rng.standard_normal(rows * cols).astype(np.float32))
+        w[::97] = 0x7E80  # ~8.5e37
+        w[5::89] = 0x0001  # BF16 subnormal
+        ya, yb = np.zeros(rows, np.float32), np.zeros(rows, np.float32)
+        PORT.or_gemv_bf16(P(w), P(xs), rows, cols, 0, rows, P(ya))
+        REF.ref_gemv_bf16(P(w), P(xs), rows, cols, 0, rows, P(yb))
+        assert same_bits(ya, yb)
+        packed = rng.integers(0, 256, rows * cols // 2, dtype=np.uint8)
+        scales = wl.e4m3_encode_normal(np.clip(np.abs(rng.standard_normal(rows * cols // 16)), 2 ** -6, 448)
+                                       .astype(np.float32))
+        for in_scale in (1 / 6, 1e-30, 1e30):
+            PORT.or_gemv_nvfp4_rows(P(packed), P(scales), 1 / 448, in_scale, P(xs), rows, cols, 0, rows, P(ya))
+            REF.ref_gemv_nvfp4_rows(P(packed), P(scales), 1 / 448, in_scale, P(xs), rows, cols, 0, rows, P(yb))
+            assert same_bits(ya, yb)
+
+
 def test_swiglu_bit_exact():
     rng = np.random.Generator(np.random.PCG64(12))
     g = (rng.standard_normal(4096) * 8).astype(np.float32)
